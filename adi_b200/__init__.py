@@ -1,0 +1,380 @@
+"""adi_b200: B200 (sm_100a) backend for ADI's packed-weight MoE path.
+
+Python binding of the C ABI in include/adi_cuda.h (libadi_cuda.so, built
+in-tree by ``python -m adi_b200.build``). The operations mirror the
+reference's Backend table (include/adi/backend.hpp:10-23 of the reference):
+
+    mach_expert_matmul / mach_ne_matmul / mach_head_matmul / bf16_matmul
+    moe_forward_batch   (src/executor.cpp:1181-1453)
+
+with the reference's error behaviour: a shape error raises ``ValueError``
+(the reference's std::invalid_argument) with the reference's message; a
+device failure raises ``RuntimeError``. There is no CPU fallback: if the
+CUDA library is missing or no GPU is present, constructing a ``Context``
+fails.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+from typing import Optional
+
+import numpy as np
+
+LIBRARY = Path(__file__).resolve().parent / "libadi_cuda.so"
+
+u8p = C.POINTER(C.c_uint8)
+u16p = C.POINTER(C.c_uint16)
+u32p = C.POINTER(C.c_uint32)
+i8p = C.POINTER(C.c_int8)
+f32p = C.POINTER(C.c_float)
+
+
+class ExpertMatrixDesc(C.Structure):
+    _fields_ = [("rows", C.c_uint32), ("columns", C.c_uint32), ("trellis", u16p), ("su_f16", u16p),
+                ("sv_f16", u16p), ("wave_gamma_f16", u16p), ("tlut", f32p)]
+
+
+class NeMatrixDesc(C.Structure):
+    _fields_ = [("rows", C.c_uint32), ("columns", C.c_uint32), ("trellis", u16p), ("su", i8p),
+                ("sv", i8p), ("weight_scale", C.c_float), ("tlut", f32p)]
+
+
+class HeadChunkDesc(C.Structure):
+    _fields_ = [("rows", C.c_uint32), ("columns", C.c_uint32), ("packed", u8p), ("group_scale_f16", u16p),
+                ("protected_rows", u32p), ("protected_count", C.c_uint32), ("protected_bf16", u16p)]
+
+
+class Bf16MatrixDesc(C.Structure):
+    _fields_ = [("rows", C.c_uint32), ("columns", C.c_uint32), ("values", u16p)]
+
+
+class MoeLayerDesc(C.Structure):
+    _fields_ = [("hidden", C.c_uint32), ("expert_hidden", C.c_uint32), ("experts", C.c_uint32),
+                ("router", Bf16MatrixDesc), ("shared_expert_gate", Bf16MatrixDesc),
+                ("shared_gate", NeMatrixDesc), ("shared_up", NeMatrixDesc), ("shared_down", NeMatrixDesc),
+                ("routed", C.POINTER(ExpertMatrixDesc))]
+
+
+# Every symbol the header declares, with its C signature.
+_ctx = C.c_void_p
+_h = C.c_uint64
+SIGNATURES = {
+    "adi_cuda_init": (C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
+    "adi_cuda_shutdown": (C.c_int, [_ctx]),
+    "adi_cuda_last_error": (C.c_size_t, [C.c_char_p, C.c_size_t]),
+    "adi_cuda_set_stream": (C.c_int, [_ctx, C.c_void_p]),
+    "adi_cuda_synchronize": (C.c_int, [_ctx]),
+    "adi_cuda_set_precision": (C.c_int, [_ctx, C.c_int]),
+    "adi_cuda_launch_count": (C.c_uint64, [_ctx]),
+    "adi_cuda_set_profiling": (C.c_int, [_ctx, C.c_int]),
+    "adi_cuda_profile_stage": (C.c_int, [_ctx, C.c_uint32, C.c_char_p, C.c_size_t, C.POINTER(C.c_double),
+                                         C.POINTER(C.c_uint64)]),
+    "adi_cuda_profile_reset": (C.c_int, [_ctx]),
+    "adi_cuda_upload_expert": (C.c_int, [_ctx, C.POINTER(ExpertMatrixDesc), C.POINTER(_h)]),
+    "adi_cuda_upload_ne": (C.c_int, [_ctx, C.POINTER(NeMatrixDesc), C.POINTER(_h)]),
+    "adi_cuda_upload_head": (C.c_int, [_ctx, C.POINTER(HeadChunkDesc), C.POINTER(_h)]),
+    "adi_cuda_upload_bf16": (C.c_int, [_ctx, C.POINTER(Bf16MatrixDesc), C.POINTER(_h)]),
+    "adi_cuda_upload_moe_layer": (C.c_int, [_ctx, C.POINTER(MoeLayerDesc), C.POINTER(_h)]),
+    "adi_cuda_release": (C.c_int, [_ctx, _h]),
+    "adi_cuda_expert_matmul": (C.c_int, [_ctx, _h, f32p, C.c_uint32, f32p]),
+    "adi_cuda_ne_matmul": (C.c_int, [_ctx, _h, f32p, C.c_uint32, f32p]),
+    "adi_cuda_head_matmul": (C.c_int, [_ctx, _h, f32p, C.c_uint32, f32p]),
+    "adi_cuda_bf16_matmul": (C.c_int, [_ctx, _h, f32p, C.c_uint32, f32p]),
+    "adi_cuda_moe_forward_batch": (C.c_int, [_ctx, _h, f32p, C.c_uint32, f32p, u32p, f32p]),
+    "adi_cuda_expert_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
+    "adi_cuda_ne_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
+    "adi_cuda_head_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
+    "adi_cuda_bf16_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
+    "adi_cuda_moe_forward_batch_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p,
+                                                    C.c_void_p, C.c_void_p]),
+    "adi_cuda_expert_states": (C.c_int, [_ctx, u16p, C.c_uint32, u32p]),
+    "adi_cuda_ne_states": (C.c_int, [_ctx, u16p, C.c_uint32, u32p]),
+    "adi_cuda_expert_state_values": (C.c_int, [_ctx, f32p, f32p]),
+    "adi_cuda_ne_state_values": (C.c_int, [_ctx, f32p, f32p]),
+    "adi_cuda_top_experts": (C.c_int, [_ctx, f32p, C.c_uint32, C.c_uint32, u32p, f32p]),
+    "adi_cuda_hadamard": (C.c_int, [_ctx, f32p, C.c_uint32, C.c_uint32]),
+    "adi_cuda_rms_norm": (C.c_int, [_ctx, f32p, u16p, C.c_uint32, C.c_uint32, C.c_float, C.c_float, f32p]),
+}
+
+INVALID_ARGUMENT = 1
+
+_lib: Optional[C.CDLL] = None
+
+
+def load() -> C.CDLL:
+    """Loads libadi_cuda.so and declares every exported signature. Raises if
+    the library has not been built: there is no fallback path."""
+    global _lib
+    if _lib is None:
+        if not LIBRARY.exists():
+            raise RuntimeError(f"{LIBRARY} is missing; build it with `python -m adi_b200.build`")
+        lib = C.CDLL(str(LIBRARY))
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    lib = load()
+    buf = C.create_string_buffer(1024)
+    lib.adi_cuda_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def _check(status: int, what: str):
+    if status == 0:
+        return
+    message = last_error()
+    if status == INVALID_ARGUMENT:
+        raise ValueError(message)
+    raise RuntimeError(f"{what} failed with status {status}: {message}")
+
+
+def _arr(a, dtype) -> np.ndarray:
+    out = np.ascontiguousarray(a, dtype=dtype)
+    return out
+
+
+def _p(a: np.ndarray, kind):
+    return a.ctypes.data_as(kind)
+
+
+class Handle:
+    """An uploaded matrix or MoE layer; rows/columns describe its matmul."""
+
+    def __init__(self, context: "Context", value: int, kind: str, rows: int, columns: int):
+        self.context, self.value, self.kind, self.rows, self.columns = context, value, kind, rows, columns
+
+    def release(self):
+        if self.value:
+            _check(self.context.lib.adi_cuda_release(self.context.ptr, self.value), "release")
+            self.value = 0
+
+
+class Context:
+    """One device's backend context: stream, codec tables, uploaded weights."""
+
+    def __init__(self, device: int = 0):
+        self.lib = load()
+        ptr = C.c_void_p()
+        _check(self.lib.adi_cuda_init(device, C.byref(ptr)), "adi_cuda_init")
+        self.ptr = ptr
+        self.device = device
+
+    def close(self):
+        if self.ptr:
+            _check(self.lib.adi_cuda_shutdown(self.ptr), "shutdown")
+            self.ptr = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # -- configuration -----------------------------------------------------
+    def set_stream(self, stream_ptr: int):
+        _check(self.lib.adi_cuda_set_stream(self.ptr, C.c_void_p(stream_ptr or None)), "set_stream")
+
+    def set_precision(self, mode: int):
+        _check(self.lib.adi_cuda_set_precision(self.ptr, mode), "set_precision")
+
+    def synchronize(self):
+        _check(self.lib.adi_cuda_synchronize(self.ptr), "synchronize")
+
+    def launch_count(self) -> int:
+        return int(self.lib.adi_cuda_launch_count(self.ptr))
+
+    def set_profiling(self, enable: bool):
+        _check(self.lib.adi_cuda_set_profiling(self.ptr, int(enable)), "set_profiling")
+
+    def reset_profile(self):
+        _check(self.lib.adi_cuda_profile_reset(self.ptr), "profile_reset")
+
+    def profile(self) -> dict:
+        """{stage: (milliseconds, brackets)} accumulated while profiling."""
+        out = {}
+        name = C.create_string_buffer(64)
+        ms = C.c_double()
+        count = C.c_uint64()
+        index = 0
+        while True:
+            status = self.lib.adi_cuda_profile_stage(self.ptr, index, name, len(name), C.byref(ms), C.byref(count))
+            if status == 1:
+                break
+            _check(status, "profile_stage")
+            if count.value:
+                out[name.value.decode()] = (ms.value, count.value)
+            index += 1
+        return out
+
+    # -- uploads -------------------------------------------------------------
+    @staticmethod
+    def expert_desc(m, keep: list) -> ExpertMatrixDesc:
+        arrays = [_arr(m.trellis, np.uint16), _arr(m.su, np.uint16), _arr(m.sv, np.uint16),
+                  _arr(m.gamma, np.uint16), _arr(m.tlut, np.float32)]
+        keep.extend(arrays)
+        t, su, sv, g, tl = arrays
+        return ExpertMatrixDesc(m.rows, m.columns, _p(t, u16p), _p(su, u16p), _p(sv, u16p), _p(g, u16p),
+                                _p(tl, f32p))
+
+    @staticmethod
+    def ne_desc(m, keep: list) -> NeMatrixDesc:
+        arrays = [_arr(m.trellis, np.uint16), _arr(m.su, np.int8), _arr(m.sv, np.int8), _arr(m.tlut, np.float32)]
+        keep.extend(arrays)
+        t, su, sv, tl = arrays
+        return NeMatrixDesc(m.rows, m.columns, _p(t, u16p), _p(su, i8p), _p(sv, i8p), float(m.weight_scale),
+                            _p(tl, f32p))
+
+    def upload_expert(self, m) -> Handle:
+        keep: list = []
+        desc = self.expert_desc(m, keep)
+        h = C.c_uint64()
+        _check(self.lib.adi_cuda_upload_expert(self.ptr, C.byref(desc), C.byref(h)), "upload_expert")
+        return Handle(self, h.value, "expert", m.rows, m.columns)
+
+    def upload_ne(self, m) -> Handle:
+        keep: list = []
+        desc = self.ne_desc(m, keep)
+        h = C.c_uint64()
+        _check(self.lib.adi_cuda_upload_ne(self.ptr, C.byref(desc), C.byref(h)), "upload_ne")
+        return Handle(self, h.value, "ne", m.rows, m.columns)
+
+    def upload_head(self, head) -> Handle:
+        packed = _arr(head.packed, np.uint8)
+        scales = _arr(head.scales, np.uint16)
+        rows = _arr(head.protected_rows, np.uint32)
+        pbf = _arr(head.protected_bf16, np.uint16)
+        desc = HeadChunkDesc(head.rows, head.columns, _p(packed, u8p), _p(scales, u16p), _p(rows, u32p),
+                             len(rows), _p(pbf, u16p))
+        h = C.c_uint64()
+        _check(self.lib.adi_cuda_upload_head(self.ptr, C.byref(desc), C.byref(h)), "upload_head")
+        return Handle(self, h.value, "head", head.rows, head.columns)
+
+    def upload_bf16(self, values) -> Handle:
+        v = _arr(values, np.uint16)
+        desc = Bf16MatrixDesc(v.shape[0], v.shape[1], _p(v, u16p))
+        h = C.c_uint64()
+        _check(self.lib.adi_cuda_upload_bf16(self.ptr, C.byref(desc), C.byref(h)), "upload_bf16")
+        return Handle(self, h.value, "bf16", v.shape[0], v.shape[1])
+
+    def upload_moe_layer(self, layer) -> Handle:
+        """`layer` provides hidden, expert_hidden, experts, router [E][H] and
+        shared_expert_gate [H] (bf16 bits), shared_gate/up/down (NE views) and
+        expert(e, projection) -> expert view, projection 0/1/2 = gate/up/down."""
+        keep: list = []
+        E = layer.experts
+        routed = (ExpertMatrixDesc * (3 * E))()
+        for e in range(E):
+            for p in range(3):
+                routed[3 * e + p] = self.expert_desc(layer.expert(e, p), keep)
+        router = _arr(layer.router, np.uint16)
+        gate = _arr(layer.shared_expert_gate, np.uint16)
+        keep += [router, gate, routed]
+        desc = MoeLayerDesc(layer.hidden, layer.expert_hidden, E,
+                            Bf16MatrixDesc(E, layer.hidden, _p(router, u16p)),
+                            Bf16MatrixDesc(1, layer.hidden, _p(gate, u16p)),
+                            self.ne_desc(layer.shared_gate, keep), self.ne_desc(layer.shared_up, keep),
+                            self.ne_desc(layer.shared_down, keep),
+                            C.cast(routed, C.POINTER(ExpertMatrixDesc)))
+        h = C.c_uint64()
+        _check(self.lib.adi_cuda_upload_moe_layer(self.ptr, C.byref(desc), C.byref(h)), "upload_moe_layer")
+        return Handle(self, h.value, "moe", layer.hidden, layer.hidden)
+
+    # -- the Backend table operations, host arrays ---------------------------
+    def _matmul(self, fn, handle: Handle, inputs, batch=None):
+        x = _arr(inputs, np.float32).reshape(-1, handle.columns)
+        batch = x.shape[0] if batch is None else batch
+        out = np.zeros((batch, handle.rows), np.float32)
+        _check(fn(self.ptr, handle.value, _p(x, f32p), batch, _p(out, f32p)), fn.__name__)
+        return out
+
+    def mach_expert_matmul(self, handle: Handle, inputs, batch=None):
+        return self._matmul(self.lib.adi_cuda_expert_matmul, handle, inputs, batch)
+
+    def mach_ne_matmul(self, handle: Handle, inputs, batch=None):
+        return self._matmul(self.lib.adi_cuda_ne_matmul, handle, inputs, batch)
+
+    def mach_head_matmul(self, handle: Handle, inputs, batch=None):
+        return self._matmul(self.lib.adi_cuda_head_matmul, handle, inputs, batch)
+
+    def bf16_matmul(self, handle: Handle, inputs, batch=None):
+        return self._matmul(self.lib.adi_cuda_bf16_matmul, handle, inputs, batch)
+
+    def moe_forward_batch(self, layer: Handle, inputs):
+        x = _arr(inputs, np.float32).reshape(-1, layer.columns)
+        T = x.shape[0]
+        out = np.zeros_like(x)
+        experts = np.zeros((T, 8), np.uint32)
+        weights = np.zeros((T, 8), np.float32)
+        _check(self.lib.adi_cuda_moe_forward_batch(self.ptr, layer.value, _p(x, f32p), T, _p(out, f32p),
+                                                   _p(experts, u32p), _p(weights, f32p)), "moe_forward_batch")
+        return out, experts, weights
+
+    # -- device pointers (e.g. torch tensors' data_ptr()), asynchronous -------
+    def moe_forward_batch_device(self, layer: Handle, inputs_ptr: int, batch: int, outputs_ptr: int,
+                                 route_experts_ptr: int = 0, route_weights_ptr: int = 0):
+        _check(self.lib.adi_cuda_moe_forward_batch_device(self.ptr, layer.value, inputs_ptr, batch, outputs_ptr,
+                                                          route_experts_ptr or None, route_weights_ptr or None),
+               "moe_forward_batch_device")
+
+    def matmul_device(self, handle: Handle, inputs_ptr: int, batch: int, outputs_ptr: int):
+        fn = {"expert": self.lib.adi_cuda_expert_matmul_device, "ne": self.lib.adi_cuda_ne_matmul_device,
+              "head": self.lib.adi_cuda_head_matmul_device, "bf16": self.lib.adi_cuda_bf16_matmul_device}[handle.kind]
+        _check(fn(self.ptr, handle.value, inputs_ptr, batch, outputs_ptr), fn.__name__)
+
+    # -- codec pieces ----------------------------------------------------------
+    def expert_states(self, words) -> np.ndarray:
+        w = _arr(words, np.uint16).reshape(-1)
+        tiles = w.size // 24
+        out = np.zeros((tiles, 32), np.uint32)
+        _check(self.lib.adi_cuda_expert_states(self.ptr, _p(w, u16p), tiles, _p(out, u32p)), "expert_states")
+        return out
+
+    def ne_states(self, words) -> np.ndarray:
+        w = _arr(words, np.uint16).reshape(-1)
+        tiles = w.size // 64
+        out = np.zeros((tiles, 128), np.uint32)
+        _check(self.lib.adi_cuda_ne_states(self.ptr, _p(w, u16p), tiles, _p(out, u32p)), "ne_states")
+        return out
+
+    def expert_state_values(self, tlut) -> np.ndarray:
+        t = _arr(tlut, np.float32)
+        out = np.zeros(65536 * 8, np.float32)
+        _check(self.lib.adi_cuda_expert_state_values(self.ptr, _p(t, f32p), _p(out, f32p)), "state values")
+        return out
+
+    def ne_state_values(self, tlut) -> np.ndarray:
+        t = _arr(tlut, np.float32)
+        out = np.zeros(65536 * 2, np.float32)
+        _check(self.lib.adi_cuda_ne_state_values(self.ptr, _p(t, f32p), _p(out, f32p)), "state values")
+        return out
+
+    def top_experts(self, logits):
+        l = _arr(logits, np.float32)
+        l2 = l.reshape(-1, l.shape[-1])
+        T, E = l2.shape
+        experts = np.zeros((T, 8), np.uint32)
+        weights = np.zeros((T, 8), np.float32)
+        _check(self.lib.adi_cuda_top_experts(self.ptr, _p(l2, f32p), T, E, _p(experts, u32p), _p(weights, f32p)),
+               "top_experts")
+        return experts, weights
+
+    def hadamard(self, values):
+        v = _arr(values, np.float32).copy()
+        n = v.shape[-1]
+        _check(self.lib.adi_cuda_hadamard(self.ptr, _p(v, f32p), v.size // n, n), "hadamard")
+        return v
+
+    def rms_norm(self, inputs, weight_bf16, weight_offset: float, epsilon: float):
+        x = _arr(inputs, np.float32)
+        n = x.shape[-1]
+        w = _arr(weight_bf16, np.uint16)
+        out = np.zeros_like(x)
+        _check(self.lib.adi_cuda_rms_norm(self.ptr, _p(x, f32p), _p(w, u16p), x.size // n, n, weight_offset,
+                                          epsilon, _p(out, f32p)), "rms_norm")
+        return out

@@ -1,0 +1,1033 @@
+// C-ABI of the B200 packed-MoE backend (declared in include/adi_cuda.h).
+//
+// A context owns one device, one stream, the decoded codec tables (one set
+// per distinct TLUT), the uploaded matrices and a grow-only scratch arena.
+// Uploads copy the packed bytes unchanged; nothing is ever dequantised into
+// HBM. Every entry validates its arguments on the host first, with the
+// reference's own error messages, so shape errors never reach a kernel.
+#include "adi_cuda.h"
+#include "kernels.cuh"
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+using namespace adi_cuda;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct Status : std::runtime_error {
+    int code;
+    Status(int c, const std::string &m) : std::runtime_error(m), code(c) {}
+};
+
+[[noreturn]] void invalid(const std::string &message) { throw Status(ADI_CUDA_INVALID_ARGUMENT, message); }
+
+void check(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return;
+    const int code = e == cudaErrorMemoryAllocation ? ADI_CUDA_OUT_OF_MEMORY : ADI_CUDA_DEVICE_ERROR;
+    throw Status(code, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+template <typename F>
+int guarded(F &&f) {
+    try {
+        f();
+        return ADI_CUDA_OK;
+    } catch (const Status &s) {
+        g_last_error = s.what();
+        return s.code;
+    } catch (const std::bad_alloc &) {
+        g_last_error = "host allocation failed";
+        return ADI_CUDA_OUT_OF_MEMORY;
+    } catch (const std::exception &e) {
+        g_last_error = e.what();
+        return ADI_CUDA_DEVICE_ERROR;
+    }
+}
+
+bool pow2(uint32_t v) { return v != 0 && (v & (v - 1)) == 0; }
+float transform_scale(uint32_t n) { return 1.0f / std::sqrt(static_cast<float>(n)); }
+
+struct DeviceArray {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+    DeviceArray() = default;
+    DeviceArray(const DeviceArray &) = delete;
+    DeviceArray &operator=(const DeviceArray &) = delete;
+    ~DeviceArray() {
+        if (ptr) cudaFree(ptr);
+    }
+    void reserve(size_t need) {
+        if (need <= bytes) return;
+        if (ptr) check(cudaFree(ptr), "cudaFree");
+        ptr = nullptr;
+        bytes = 0;
+        check(cudaMalloc(&ptr, need), "cudaMalloc");
+        bytes = need;
+    }
+    template <typename T>
+    T *as() const { return static_cast<T *>(ptr); }
+};
+
+std::unique_ptr<DeviceArray> upload_bytes(const void *host, size_t bytes, const char *what) {
+    if (bytes && !host) invalid(std::string(what) + " pointer is null");
+    auto a = std::make_unique<DeviceArray>();
+    a->reserve(bytes ? bytes : 16);
+    if (bytes) check(cudaMemcpy(a->ptr, host, bytes, cudaMemcpyHostToDevice), "upload");
+    return a;
+}
+
+// Decoded value tables, one set per distinct TLUT.
+struct ExpertCodec {
+    DeviceArray half_tables;  // uint2 [2][16384]
+};
+struct NeCodec {
+    DeviceArray table;  // float2 [1024]
+};
+
+struct ExpertDev {
+    uint32_t rows, cols;
+    std::unique_ptr<DeviceArray> trellis, su, sv, gamma;
+    ExpertCodec *codec;
+};
+struct NeDev {
+    uint32_t rows, cols;
+    float weight_scale;
+    std::unique_ptr<DeviceArray> trellis, su, sv;
+    NeCodec *codec;
+};
+struct HeadDev {
+    uint32_t rows, cols, protected_count;
+    std::unique_ptr<DeviceArray> packed, scales, protected_rows, protected_bf16;
+};
+struct Bf16Dev {
+    uint32_t rows, cols;
+    std::unique_ptr<DeviceArray> values;
+};
+struct MoeDev {
+    uint32_t hidden, inner, experts;
+    std::unique_ptr<DeviceArray> router;  // [(E+1)][H] bf16: router rows then the shared gate
+    std::unique_ptr<DeviceArray> trellis[3], su[3], sv[3], gamma[3];
+    ExpertCodec *codec;
+    NeDev shared[3];
+};
+
+enum Kind { kExpert = 1, kNe, kHead, kBf16, kMoe };
+
+enum Stage {
+    kStageRouter,
+    kStageTopk,
+    kStageRoute,
+    kStagePrep,
+    kStageExpertGateUp,
+    kStageSwiglu,
+    kStageExpertDown,
+    kStageShared,
+    kStageCombine,
+    kStageExpertMatmul,
+    kStageNeMatmul,
+    kStageHead,
+    kStageBf16,
+    kStageCount
+};
+const char *const kStageNames[kStageCount] = {
+    "router",           "top_experts",      "route",        "expert_prep",  "expert_gemm_gate_up",
+    "swiglu",           "expert_gemm_down", "shared_expert", "combine",     "expert_matmul",
+    "ne_matmul",        "head_matmul",      "bf16_matmul",
+};
+
+// CUDA-event brackets around stages, resolved lazily.
+struct Profiler {
+    bool enabled = false;
+    struct Pending {
+        int stage;
+        cudaEvent_t begin, end;
+    };
+    std::vector<cudaEvent_t> pool;
+    std::vector<Pending> pending;
+    int open_stage = -1;
+    cudaEvent_t open_event = nullptr;
+    double ms[kStageCount] = {};
+    uint64_t count[kStageCount] = {};
+
+    cudaEvent_t take() {
+        if (!pool.empty()) {
+            cudaEvent_t e = pool.back();
+            pool.pop_back();
+            return e;
+        }
+        cudaEvent_t e;
+        check(cudaEventCreate(&e), "cudaEventCreate");
+        return e;
+    }
+    void begin(int stage, cudaStream_t s) {
+        if (!enabled) return;
+        open_stage = stage;
+        open_event = take();
+        check(cudaEventRecord(open_event, s), "cudaEventRecord");
+    }
+    void end(cudaStream_t s) {
+        if (!enabled || open_stage < 0) return;
+        cudaEvent_t e = take();
+        check(cudaEventRecord(e, s), "cudaEventRecord");
+        pending.push_back({open_stage, open_event, e});
+        open_stage = -1;
+        if (pending.size() > 8192) collect();
+    }
+    void collect() {
+        for (auto &p : pending) {
+            check(cudaEventSynchronize(p.end), "cudaEventSynchronize");
+            float t = 0;
+            check(cudaEventElapsedTime(&t, p.begin, p.end), "cudaEventElapsedTime");
+            ms[p.stage] += t;
+            count[p.stage] += 1;
+            pool.push_back(p.begin);
+            pool.push_back(p.end);
+        }
+        pending.clear();
+    }
+    ~Profiler() {
+        for (auto &p : pending) {
+            cudaEventDestroy(p.begin);
+            cudaEventDestroy(p.end);
+        }
+        for (auto e : pool) cudaEventDestroy(e);
+    }
+};
+
+}  // namespace
+
+struct adi_cuda_context {
+    int device = 0;
+    int sms = 148;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    int precision = 0;
+    uint64_t launches = 0;
+    std::mutex lock;
+    std::map<std::vector<uint8_t>, std::unique_ptr<ExpertCodec>> expert_codecs;
+    std::map<std::vector<uint8_t>, std::unique_ptr<NeCodec>> ne_codecs;
+    uint64_t next_handle = 1;
+    std::map<uint64_t, std::unique_ptr<ExpertDev>> experts;
+    std::map<uint64_t, std::unique_ptr<NeDev>> nes;
+    std::map<uint64_t, std::unique_ptr<HeadDev>> heads;
+    std::map<uint64_t, std::unique_ptr<Bf16Dev>> bf16s;
+    std::map<uint64_t, std::unique_ptr<MoeDev>> moes;
+    Profiler profiler;
+    void stage(int st) { profiler.begin(st, stream); }
+    void stage_end() { profiler.end(stream); }
+    // Scratch arena, grown on demand.
+    std::map<std::string, std::unique_ptr<DeviceArray>> scratch;
+
+    template <typename T>
+    T *buffer(const char *name, size_t count) {
+        auto &slot = scratch[name];
+        if (!slot) slot = std::make_unique<DeviceArray>();
+        slot->reserve(sizeof(T) * (count ? count : 1));
+        return slot->as<T>();
+    }
+
+    void after_launch(uint64_t n) {
+        launches += n;
+        check(cudaGetLastError(), "kernel launch");
+    }
+
+    uint64_t new_handle(Kind kind) { return (next_handle++ << 4) | kind; }
+
+    ExpertCodec *expert_codec(const float *tlut) {
+        if (!tlut) invalid("Mach expert codec tensor shape mismatch");
+        std::vector<uint8_t> key(reinterpret_cast<const uint8_t *>(tlut),
+                                 reinterpret_cast<const uint8_t *>(tlut) + 32768 * 8 * sizeof(float));
+        auto &slot = expert_codecs[key];
+        if (!slot) {
+            slot = std::make_unique<ExpertCodec>();
+            auto staged = upload_bytes(tlut, key.size(), "TLUT");
+            slot->half_tables.reserve(2 * 16384 * sizeof(uint2));
+            launch_build_expert_tables(staged->as<float>(), slot->half_tables.as<uint2>(), stream);
+            after_launch(1);
+            check(cudaStreamSynchronize(stream), "build expert tables");
+        }
+        return slot.get();
+    }
+
+    NeCodec *ne_codec(const float *tlut) {
+        if (!tlut) invalid("Mach NE codec tensor shape mismatch");
+        std::vector<uint8_t> key(reinterpret_cast<const uint8_t *>(tlut),
+                                 reinterpret_cast<const uint8_t *>(tlut) + 512 * 2 * sizeof(float));
+        auto &slot = ne_codecs[key];
+        if (!slot) {
+            slot = std::make_unique<NeCodec>();
+            auto staged = upload_bytes(tlut, key.size(), "TLUT");
+            slot->table.reserve(1024 * sizeof(float2));
+            launch_build_ne_table(staged->as<float>(), slot->table.as<float2>(), stream);
+            after_launch(1);
+            check(cudaStreamSynchronize(stream), "build NE table");
+        }
+        return slot.get();
+    }
+};
+
+namespace {
+
+void use_device(adi_cuda_context *c) { check(cudaSetDevice(c->device), "cudaSetDevice"); }
+
+adi_cuda_context *require(adi_cuda_context *c) {
+    if (!c) invalid("context is null");
+    return c;
+}
+
+template <typename Map>
+auto &lookup(Map &map, adi_cuda_handle h, const char *what) {
+    auto it = map.find(h);
+    if (it == map.end()) invalid(std::string("unknown ") + what + " handle");
+    return *it->second;
+}
+
+void validate_expert_shape(uint32_t rows, uint32_t cols) {
+    if (!pow2(rows) || !pow2(cols) || rows % 16 || cols % 16)
+        invalid("Mach expert dimensions must be tiled powers of two");
+}
+
+void validate_ne_shape(uint32_t rows, uint32_t cols) {
+    if (!pow2(rows) || !pow2(cols) || rows % 16 || cols % 16)
+        invalid("Mach NE dimensions must be tiled powers of two");
+}
+
+void fill_expert(adi_cuda_context *c, const adi_expert_matrix &m, ExpertDev &d) {
+    validate_expert_shape(m.rows, m.columns);
+    if (!m.trellis || !m.su_f16 || !m.sv_f16 || !m.wave_gamma_f16 || !m.tlut)
+        invalid("Mach expert codec tensor shape mismatch");
+    const size_t tiles = size_t(m.rows / 16) * (m.columns / 16);
+    d.rows = m.rows;
+    d.cols = m.columns;
+    d.trellis = upload_bytes(m.trellis, tiles * 24 * 2, "trellis");
+    d.su = upload_bytes(m.su_f16, size_t(m.columns) * 2, "su");
+    d.sv = upload_bytes(m.sv_f16, size_t(m.rows) * 2, "sv");
+    d.gamma = upload_bytes(m.wave_gamma_f16, size_t(m.rows / 16 + m.columns / 16) * 2, "wave_gamma");
+    d.codec = c->expert_codec(m.tlut);
+}
+
+void fill_ne(adi_cuda_context *c, const adi_ne_matrix &m, NeDev &d) {
+    validate_ne_shape(m.rows, m.columns);
+    if (!m.trellis || !m.su || !m.sv || !m.tlut) invalid("Mach NE codec tensor shape mismatch");
+    const size_t tiles = size_t(m.rows / 16) * (m.columns / 16);
+    d.rows = m.rows;
+    d.cols = m.columns;
+    d.weight_scale = m.weight_scale;
+    d.trellis = upload_bytes(m.trellis, tiles * 64 * 2, "trellis");
+    d.su = upload_bytes(m.su, m.columns, "su");
+    d.sv = upload_bytes(m.sv, m.rows, "sv");
+    d.codec = c->ne_codec(m.tlut);
+}
+
+int gemm_grid(adi_cuda_context *c, uint64_t items, int per_item) {
+    const uint64_t want = items * per_item;
+    const uint64_t cap = uint64_t(c->sms);
+    int grid = int(want < cap ? want : cap);
+    if (per_item == 2) grid = (grid + 1) & ~1;
+    return grid < per_item ? per_item : grid;
+}
+
+uint32_t row_blocks(uint32_t rows) { return (rows / 16 + kRowTiles - 1) / kRowTiles; }
+
+// ---- standalone matmuls on device pointers -------------------------------
+
+void expert_matmul_dev(adi_cuda_context *c, ExpertDev &m, const float *in, uint32_t batch, float *out) {
+    if (batch == 0) invalid("Mach expert batch shape mismatch");
+    float *xp = c->buffer<float>("x_prep", size_t(batch) * m.cols);
+    float *acc = c->buffer<float>("acc", 2 * size_t(batch) * m.rows);
+    c->stage(kStageExpertMatmul);
+    PrepParams pp{};
+    pp.input = in;
+    pp.su[0] = m.su->ptr;
+    pp.out[0] = xp;
+    pp.cols = m.cols;
+    pp.scale = transform_scale(m.cols);
+    pp.rows = batch;
+    pp.jobs = 1;
+    pp.su_is_f16 = 1;
+    launch_prep(pp, c->stream);
+    ExpertGemmParams gp{};
+    gp.job[0] = ExpertJob{m.trellis->as<uint32_t>(), m.gamma->as<uint16_t>(), xp, acc, m.rows, m.cols, 0, 0,
+                          size_t(batch) * m.rows};
+    gp.job[1] = gp.job[0];
+    gp.work = WorkList{nullptr, nullptr, batch, 1};
+    gp.table = m.codec->half_tables.as<uint2>();
+    const uint64_t items = uint64_t((batch + kMaxTokens - 1) / kMaxTokens) * row_blocks(m.rows);
+    launch_expert_gemm(gp, gemm_grid(c, items, 2), c->stream);
+    launch_finalize(acc, acc + size_t(batch) * m.rows, m.sv->ptr, 1, batch, m.rows, transform_scale(m.rows), out,
+                    c->stream);
+    c->stage_end();
+    c->after_launch(3);
+}
+
+void ne_matmul_dev(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batch, float *out) {
+    if (batch == 0) invalid("Mach NE batch shape mismatch");
+    float *xp = c->buffer<float>("x_prep", size_t(batch) * m.cols);
+    float *acc = c->buffer<float>("acc", size_t(batch) * m.rows);
+    c->stage(kStageNeMatmul);
+    PrepParams pp{};
+    pp.input = in;
+    pp.su[0] = m.su->ptr;
+    pp.out[0] = xp;
+    pp.cols = m.cols;
+    pp.scale = transform_scale(m.cols);
+    pp.rows = batch;
+    pp.jobs = 1;
+    pp.su_is_f16 = 0;
+    launch_prep(pp, c->stream);
+    NeGemmParams gp{};
+    gp.job[0] = NeJob{m.trellis->as<uint32_t>(), xp, acc, m.rows, m.cols, m.weight_scale};
+    gp.job[1] = gp.job[0];
+    gp.work = WorkList{nullptr, nullptr, batch, 1};
+    gp.table = m.codec->table.as<float2>();
+    const uint64_t items = uint64_t((batch + kMaxTokens - 1) / kMaxTokens) * row_blocks(m.rows);
+    launch_ne_gemm(gp, gemm_grid(c, items, 1), c->stream);
+    launch_finalize(acc, nullptr, m.sv->ptr, 0, batch, m.rows, transform_scale(m.rows), out, c->stream);
+    c->stage_end();
+    c->after_launch(3);
+}
+
+void bf16_matmul_dev(adi_cuda_context *c, Bf16Dev &m, const float *in, uint32_t batch, float *out) {
+    if (batch == 0) invalid("BF16 matrix batch shape mismatch");
+    c->stage(kStageBf16);
+    launch_bf16_gemm(m.values->as<uint16_t>(), m.rows, nullptr, 0, in, batch, m.cols, out, m.rows, c->stream);
+    c->stage_end();
+    c->after_launch(1);
+}
+
+void head_matmul_dev(adi_cuda_context *c, HeadDev &h, const float *in, uint32_t batch, float *out) {
+    if (batch == 0) invalid("Mach output head batch shape mismatch");
+    HeadParams p{};
+    p.packed = h.packed->as<uint8_t>();
+    p.scales = h.scales->as<uint16_t>();
+    p.x = in;
+    p.out = out;
+    p.rows = h.rows;
+    p.cols = h.cols;
+    p.batch = batch;
+    p.protected_rows = h.protected_rows->as<uint32_t>();
+    p.protected_bf16 = h.protected_bf16->as<uint16_t>();
+    p.protected_count = h.protected_count;
+    c->stage(kStageHead);
+    launch_head(p, c->stream);
+    c->stage_end();
+    c->after_launch(h.protected_count ? 2 : 1);
+}
+
+// ---- the MoE block --------------------------------------------------------
+
+void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *out,
+                     uint32_t *route_experts_out, float *route_weights_out) {
+    if (T == 0) invalid("MoE batch shape mismatch");
+    const uint32_t H = L.hidden, I = L.inner, E = L.experts;
+    const size_t P = size_t(T) * 8;
+    cudaStream_t s = c->stream;
+
+    float *logits = c->buffer<float>("moe_logits", size_t(T) * (E + 1));
+    uint32_t *re = route_experts_out ? route_experts_out : c->buffer<uint32_t>("moe_re", P);
+    float *rw = route_weights_out ? route_weights_out : c->buffer<float>("moe_rw", P);
+    c->stage(kStageRouter);
+    launch_bf16_gemm(L.router->as<uint16_t>(), E, L.router->as<uint16_t>() + size_t(E) * H, 1, in, T, H, logits,
+                     E + 1, s);
+    c->stage_end();
+    c->stage(kStageTopk);
+    launch_top_experts(logits, E + 1, T, E, re, rw, s);
+    c->stage_end();
+
+    RouteParams rp{};
+    rp.route_experts = re;
+    rp.tokens = T;
+    rp.experts = E;
+    rp.words = (T + 31) / 32;
+    rp.counts = c->buffer<uint32_t>("moe_counts", E);
+    rp.offsets = c->buffer<uint32_t>("moe_offsets", E + 1);
+    rp.bitmap = c->buffer<uint32_t>("moe_bitmap", size_t(E) * rp.words);
+    rp.prefix = c->buffer<uint32_t>("moe_prefix", size_t(E) * rp.words);
+    rp.grouped = c->buffer<uint32_t>("moe_grouped", P);
+    rp.pos_expert = c->buffer<uint32_t>("moe_pos_expert", P);
+    rp.route_to_grouped = c->buffer<uint32_t>("moe_r2g", P);
+    rp.row_blocks_gate_up = row_blocks(I);
+    rp.row_blocks_down = row_blocks(H);
+    const size_t max_chunks = P / kMaxTokens + E;
+    rp.items_gate_up = c->buffer<uint4>("moe_items_gu", max_chunks * 2 * rp.row_blocks_gate_up);
+    rp.items_down = c->buffer<uint4>("moe_items_d", max_chunks * rp.row_blocks_down);
+    uint32_t *counts2 = c->buffer<uint32_t>("moe_item_counts", 2);
+    rp.count_gate_up = counts2;
+    rp.count_down = counts2 + 1;
+    c->stage(kStageRoute);
+    launch_route(rp, s);
+    c->stage_end();
+
+    float *xg = c->buffer<float>("moe_xg", P * H);
+    float *xu = c->buffer<float>("moe_xu", P * H);
+    PrepParams pp{};
+    pp.input = in;
+    pp.grouped = rp.grouped;
+    pp.pos_expert = rp.pos_expert;
+    pp.su[0] = L.su[0]->ptr;
+    pp.su[1] = L.su[1]->ptr;
+    pp.out[0] = xg;
+    pp.out[1] = xu;
+    pp.su_stride = H;
+    pp.cols = H;
+    pp.scale = transform_scale(H);
+    pp.rows = uint32_t(P);
+    pp.jobs = 2;
+    pp.su_is_f16 = 1;
+    c->stage(kStagePrep);
+    launch_prep(pp, s);
+    c->stage_end();
+
+    float *acc_g = c->buffer<float>("moe_acc_g", 2 * P * I);
+    float *acc_u = c->buffer<float>("moe_acc_u", 2 * P * I);
+    const uint32_t tiles_gu = (I / 16) * (H / 16);
+    ExpertGemmParams gp{};
+    gp.job[0] = ExpertJob{L.trellis[0]->as<uint32_t>(), L.gamma[0]->as<uint16_t>(), xg, acc_g, I, H,
+                          tiles_gu * 12, I / 16 + H / 16, P * I};
+    gp.job[1] = ExpertJob{L.trellis[1]->as<uint32_t>(), L.gamma[1]->as<uint16_t>(), xu, acc_u, I, H,
+                          tiles_gu * 12, I / 16 + H / 16, P * I};
+    gp.work = WorkList{rp.items_gate_up, rp.count_gate_up, 0, 0};
+    gp.table = L.codec->half_tables.as<uint2>();
+    c->stage(kStageExpertGateUp);
+    launch_expert_gemm(gp, c->sms, s);
+    c->stage_end();
+
+    float *xd = c->buffer<float>("moe_xd", P * I);
+    MidParams mp{};
+    mp.acc_gate = acc_g;
+    mp.acc_up = acc_u;
+    mp.half_stride = P * I;
+    mp.pos_expert = rp.pos_expert;
+    mp.sv_gate = L.sv[0]->ptr;
+    mp.sv_up = L.sv[1]->ptr;
+    mp.su_down = L.su[2]->ptr;
+    mp.is_f16 = 1;
+    mp.halves = 2;
+    mp.inner = I;
+    mp.scale = transform_scale(I);
+    mp.xd = xd;
+    mp.positions = uint32_t(P);
+    c->stage(kStageSwiglu);
+    launch_mid(mp, s);
+    c->stage_end();
+
+    float *acc_d = c->buffer<float>("moe_acc_d", 2 * P * H);
+    ExpertGemmParams dp{};
+    dp.job[0] = ExpertJob{L.trellis[2]->as<uint32_t>(), L.gamma[2]->as<uint16_t>(), xd, acc_d, H, I,
+                          tiles_gu * 12, I / 16 + H / 16, P * H};
+    dp.job[1] = dp.job[0];
+    dp.work = WorkList{rp.items_down, rp.count_down, 0, 0};
+    dp.table = gp.table;
+    c->stage(kStageExpertDown);
+    launch_expert_gemm(dp, c->sms, s);
+    c->stage_end();
+
+    // Shared NE expert over all T tokens.
+    float *sxg = c->buffer<float>("moe_sxg", size_t(T) * H);
+    float *sxu = c->buffer<float>("moe_sxu", size_t(T) * H);
+    PrepParams sp{};
+    sp.input = in;
+    sp.su[0] = L.shared[0].su->ptr;
+    sp.su[1] = L.shared[1].su->ptr;
+    sp.out[0] = sxg;
+    sp.out[1] = sxu;
+    sp.cols = H;
+    sp.scale = transform_scale(H);
+    sp.rows = T;
+    sp.jobs = 2;
+    sp.su_is_f16 = 0;
+    c->stage(kStageShared);
+    launch_prep(sp, s);
+    float *sacc_g = c->buffer<float>("moe_sacc_g", size_t(T) * I);
+    float *sacc_u = c->buffer<float>("moe_sacc_u", size_t(T) * I);
+    NeGemmParams np{};
+    np.job[0] = NeJob{L.shared[0].trellis->as<uint32_t>(), sxg, sacc_g, I, H, L.shared[0].weight_scale};
+    np.job[1] = NeJob{L.shared[1].trellis->as<uint32_t>(), sxu, sacc_u, I, H, L.shared[1].weight_scale};
+    np.work = WorkList{nullptr, nullptr, T, 2};
+    np.table = L.shared[0].codec->table.as<float2>();
+    const uint64_t ne_items = uint64_t((T + kMaxTokens - 1) / kMaxTokens) * 2 * row_blocks(I);
+    launch_ne_gemm(np, gemm_grid(c, ne_items, 1), s);
+    float *sxd = c->buffer<float>("moe_sxd", size_t(T) * I);
+    MidParams smp{};
+    smp.acc_gate = sacc_g;
+    smp.acc_up = sacc_u;
+    smp.half_stride = 0;
+    smp.pos_expert = nullptr;
+    smp.sv_gate = L.shared[0].sv->ptr;
+    smp.sv_up = L.shared[1].sv->ptr;
+    smp.su_down = L.shared[2].su->ptr;
+    smp.is_f16 = 0;
+    smp.halves = 1;
+    smp.inner = I;
+    smp.scale = transform_scale(I);
+    smp.xd = sxd;
+    smp.positions = T;
+    launch_mid(smp, s);
+    float *sacc_d = c->buffer<float>("moe_sacc_d", size_t(T) * H);
+    NeGemmParams nd{};
+    nd.job[0] = NeJob{L.shared[2].trellis->as<uint32_t>(), sxd, sacc_d, H, I, L.shared[2].weight_scale};
+    nd.job[1] = nd.job[0];
+    nd.work = WorkList{nullptr, nullptr, T, 1};
+    nd.table = np.table;
+    const uint64_t nd_items = uint64_t((T + kMaxTokens - 1) / kMaxTokens) * row_blocks(H);
+    launch_ne_gemm(nd, gemm_grid(c, nd_items, 1), s);
+    c->stage_end();
+
+    CombineParams cp{};
+    cp.acc_down = acc_d;
+    cp.half_stride = P * H;
+    cp.route_experts = re;
+    cp.route_to_grouped = rp.route_to_grouped;
+    cp.route_weights = rw;
+    cp.sv_down = L.sv[2]->as<uint16_t>();
+    cp.shared_acc = sacc_d;
+    cp.shared_sv = L.shared[2].sv->as<int8_t>();
+    cp.gate_logits = logits + E;
+    cp.gate_stride = E + 1;
+    cp.hidden = H;
+    cp.scale = transform_scale(H);
+    cp.out = out;
+    cp.tokens = T;
+    c->stage(kStageCombine);
+    launch_combine(cp, s);
+    c->stage_end();
+    // router, top-k, 2 memsets + 3 routing kernels, prep, gemm, mid, gemm,
+    // shared prep, gemm, mid, gemm, combine
+    c->after_launch(2 + 3 + 1 + 1 + 1 + 1 + 1 + 1 + 1 + 1 + 1);
+}
+
+// Host-pointer wrapper: stage inputs, run on device, read outputs back.
+template <typename F>
+void host_call(adi_cuda_context *c, const float *in, size_t in_count, float *out, size_t out_count, F &&run) {
+    if (!in || !out) invalid("input or output pointer is null");
+    float *din = c->buffer<float>("host_in", in_count);
+    float *dout = c->buffer<float>("host_out", out_count);
+    check(cudaMemcpyAsync(din, in, in_count * sizeof(float), cudaMemcpyHostToDevice, c->stream), "H2D");
+    run(din, dout);
+    check(cudaMemcpyAsync(out, dout, out_count * sizeof(float), cudaMemcpyDeviceToHost, c->stream), "D2H");
+    check(cudaStreamSynchronize(c->stream), "synchronize");
+}
+
+}  // namespace
+
+extern "C" {
+
+int adi_cuda_init(int device, adi_cuda_context **out) {
+    return guarded([&] {
+        if (!out) invalid("context pointer is null");
+        int count = 0;
+        check(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+        if (device < 0 || device >= count) invalid("device index out of range");
+        auto c = std::make_unique<adi_cuda_context>();
+        c->device = device;
+        check(cudaSetDevice(device), "cudaSetDevice");
+        check(cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device), "SM count");
+        check(cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+        c->stream = c->own_stream;
+        *out = c.release();
+    });
+}
+
+int adi_cuda_shutdown(adi_cuda_context *c) {
+    return guarded([&] {
+        if (!c) return;
+        use_device(c);
+        cudaStreamSynchronize(c->stream);
+        cudaStream_t own = c->own_stream;
+        delete c;
+        if (own) cudaStreamDestroy(own);
+    });
+}
+
+size_t adi_cuda_last_error(char *buffer, size_t size) {
+    if (buffer && size) {
+        const size_t n = g_last_error.size() < size - 1 ? g_last_error.size() : size - 1;
+        std::memcpy(buffer, g_last_error.data(), n);
+        buffer[n] = 0;
+    }
+    return g_last_error.size();
+}
+
+int adi_cuda_set_stream(adi_cuda_context *c, void *stream) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own_stream;
+    });
+}
+
+int adi_cuda_synchronize(adi_cuda_context *c) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        check(cudaStreamSynchronize(c->stream), "synchronize");
+    });
+}
+
+int adi_cuda_set_precision(adi_cuda_context *c, int mode) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        if (mode != 0 && mode != 1) invalid("precision mode must be 0 or 1");
+        c->precision = mode;
+    });
+}
+
+uint64_t adi_cuda_launch_count(const adi_cuda_context *c) { return c ? c->launches : 0; }
+
+int adi_cuda_set_profiling(adi_cuda_context *c, int enable) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        c->profiler.enabled = enable != 0;
+    });
+}
+
+int adi_cuda_profile_stage(adi_cuda_context *c, uint32_t index, char *name, size_t name_size, double *ms,
+                           uint64_t *count) {
+    int past_end = 0;
+    const int status = guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        c->profiler.collect();
+        if (index >= kStageCount) {
+            past_end = 1;
+            return;
+        }
+        if (name && name_size) {
+            std::strncpy(name, kStageNames[index], name_size - 1);
+            name[name_size - 1] = 0;
+        }
+        if (ms) *ms = c->profiler.ms[index];
+        if (count) *count = c->profiler.count[index];
+    });
+    return status ? status : past_end;
+}
+
+int adi_cuda_profile_reset(adi_cuda_context *c) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        c->profiler.collect();
+        for (int i = 0; i < kStageCount; ++i) {
+            c->profiler.ms[i] = 0;
+            c->profiler.count[i] = 0;
+        }
+    });
+}
+
+int adi_cuda_upload_expert(adi_cuda_context *c, const adi_expert_matrix *m, adi_cuda_handle *h) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        if (!m || !h) invalid("matrix or handle pointer is null");
+        use_device(c);
+        auto d = std::make_unique<ExpertDev>();
+        fill_expert(c, *m, *d);
+        const uint64_t id = c->new_handle(kExpert);
+        c->experts[id] = std::move(d);
+        *h = id;
+    });
+}
+
+int adi_cuda_upload_ne(adi_cuda_context *c, const adi_ne_matrix *m, adi_cuda_handle *h) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        if (!m || !h) invalid("matrix or handle pointer is null");
+        use_device(c);
+        auto d = std::make_unique<NeDev>();
+        fill_ne(c, *m, *d);
+        const uint64_t id = c->new_handle(kNe);
+        c->nes[id] = std::move(d);
+        *h = id;
+    });
+}
+
+int adi_cuda_upload_head(adi_cuda_context *c, const adi_head_chunk *m, adi_cuda_handle *h) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        if (!m || !h) invalid("head or handle pointer is null");
+        use_device(c);
+        if (m->columns == 0 || m->columns % 64 || m->rows == 0) invalid("Mach output head shape mismatch");
+        if (size_t(m->columns) * 8 * 4 > 227 * 1024) invalid("Mach output head has too many columns");
+        if (!m->packed || !m->group_scale_f16) invalid("Mach output head shape mismatch");
+        if (m->protected_count && (!m->protected_rows || !m->protected_bf16))
+            invalid("Mach protected output row shape mismatch");
+        for (uint32_t i = 0; i < m->protected_count; ++i)
+            if (m->protected_rows[i] >= m->rows) invalid("Mach protected output row is out of range");
+        auto d = std::make_unique<HeadDev>();
+        d->rows = m->rows;
+        d->cols = m->columns;
+        d->protected_count = m->protected_count;
+        d->packed = upload_bytes(m->packed, size_t(m->rows) * m->columns / 8 * 5, "packed");
+        d->scales = upload_bytes(m->group_scale_f16, size_t(m->rows) * (m->columns / 64) * 2, "scales");
+        d->protected_rows = upload_bytes(m->protected_rows, size_t(m->protected_count) * 4, "protected rows");
+        d->protected_bf16 =
+            upload_bytes(m->protected_bf16, size_t(m->protected_count) * m->columns * 2, "protected bf16");
+        const uint64_t id = c->new_handle(kHead);
+        c->heads[id] = std::move(d);
+        *h = id;
+    });
+}
+
+int adi_cuda_upload_bf16(adi_cuda_context *c, const adi_bf16_matrix *m, adi_cuda_handle *h) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        if (!m || !h) invalid("matrix or handle pointer is null");
+        use_device(c);
+        if (m->rows == 0 || m->columns == 0 || !m->values) invalid("BF16 matrix batch shape mismatch");
+        if (size_t(m->columns) * 8 * 4 > 227 * 1024) invalid("BF16 matrix has too many columns");
+        auto d = std::make_unique<Bf16Dev>();
+        d->rows = m->rows;
+        d->cols = m->columns;
+        d->values = upload_bytes(m->values, size_t(m->rows) * m->columns * 2, "bf16 values");
+        const uint64_t id = c->new_handle(kBf16);
+        c->bf16s[id] = std::move(d);
+        *h = id;
+    });
+}
+
+int adi_cuda_upload_moe_layer(adi_cuda_context *c, const adi_moe_layer *l, adi_cuda_handle *h) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        if (!l || !h || !l->routed) invalid("layer or handle pointer is null");
+        use_device(c);
+        const uint32_t H = l->hidden, I = l->expert_hidden, E = l->experts;
+        if (E < 8 || E > 1024) invalid("MoE routing requires between 8 and 1024 experts");
+        validate_expert_shape(I, H);
+        if (H > 8192) invalid("MoE hidden size above 8192 is not supported");
+        if (l->router.rows != E || l->router.columns != H || !l->router.values)
+            invalid("MoE router shape mismatch");
+        if (l->shared_expert_gate.rows != 1 || l->shared_expert_gate.columns != H ||
+            !l->shared_expert_gate.values)
+            invalid("MoE shared expert gate shape mismatch");
+        auto d = std::make_unique<MoeDev>();
+        d->hidden = H;
+        d->inner = I;
+        d->experts = E;
+        std::vector<uint16_t> router(size_t(E + 1) * H);
+        std::memcpy(router.data(), l->router.values, size_t(E) * H * 2);
+        std::memcpy(router.data() + size_t(E) * H, l->shared_expert_gate.values, size_t(H) * 2);
+        d->router = upload_bytes(router.data(), router.size() * 2, "router");
+        const float *tlut = l->routed[0].tlut;
+        const uint32_t tiles = (I / 16) * (H / 16);
+        for (int p = 0; p < 3; ++p) {
+            const uint32_t rows = p == 2 ? H : I, cols = p == 2 ? I : H;
+            const size_t tw = size_t(tiles) * 24, gw = rows / 16 + cols / 16;
+            std::vector<uint16_t> trellis(tw * E), su(size_t(cols) * E), sv(size_t(rows) * E), gamma(gw * E);
+            for (uint32_t e = 0; e < E; ++e) {
+                const adi_expert_matrix &m = l->routed[3 * e + p];
+                if (m.rows != rows || m.columns != cols) invalid("MoE routed expert shape mismatch");
+                if (!m.trellis || !m.su_f16 || !m.sv_f16 || !m.wave_gamma_f16)
+                    invalid("Mach expert codec tensor shape mismatch");
+                if (m.tlut != tlut) invalid("MoE routed experts must share one TLUT");
+                std::memcpy(trellis.data() + e * tw, m.trellis, tw * 2);
+                std::memcpy(su.data() + size_t(e) * cols, m.su_f16, size_t(cols) * 2);
+                std::memcpy(sv.data() + size_t(e) * rows, m.sv_f16, size_t(rows) * 2);
+                std::memcpy(gamma.data() + e * gw, m.wave_gamma_f16, gw * 2);
+            }
+            d->trellis[p] = upload_bytes(trellis.data(), trellis.size() * 2, "trellis");
+            d->su[p] = upload_bytes(su.data(), su.size() * 2, "su");
+            d->sv[p] = upload_bytes(sv.data(), sv.size() * 2, "sv");
+            d->gamma[p] = upload_bytes(gamma.data(), gamma.size() * 2, "gamma");
+        }
+        d->codec = c->expert_codec(tlut);
+        const adi_ne_matrix *shared[3] = {&l->shared_gate, &l->shared_up, &l->shared_down};
+        for (int p = 0; p < 3; ++p) {
+            const uint32_t rows = p == 2 ? H : I, cols = p == 2 ? I : H;
+            if (shared[p]->rows != rows || shared[p]->columns != cols) invalid("MoE shared expert shape mismatch");
+            fill_ne(c, *shared[p], d->shared[p]);
+        }
+        if (d->shared[0].codec != d->shared[1].codec || d->shared[0].codec != d->shared[2].codec)
+            invalid("MoE shared expert matrices must share one TLUT");
+        const uint64_t id = c->new_handle(kMoe);
+        c->moes[id] = std::move(d);
+        *h = id;
+    });
+}
+
+int adi_cuda_release(adi_cuda_context *c, adi_cuda_handle h) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        check(cudaStreamSynchronize(c->stream), "synchronize");
+        const size_t erased = c->experts.erase(h) + c->nes.erase(h) + c->heads.erase(h) + c->bf16s.erase(h) +
+                              c->moes.erase(h);
+        if (!erased) invalid("unknown handle");
+    });
+}
+
+#define ADI_HOST_MATMUL(NAME, MAP, KIND, FN)                                                                 \
+    int NAME(adi_cuda_context *c, adi_cuda_handle h, const float *in, uint32_t batch, float *out) {        \
+        return guarded([&] {                                                                               \
+            std::lock_guard<std::mutex> g(require(c)->lock);                                               \
+            use_device(c);                                                                                 \
+            auto &m = lookup(c->MAP, h, KIND);                                                             \
+            if (batch == 0) FN(c, m, in, 0, out);                                                          \
+            host_call(c, in, size_t(batch) * m.cols, out, size_t(batch) * m.rows,                          \
+                      [&](const float *din, float *dout) { FN(c, m, din, batch, dout); });                  \
+        });                                                                                                \
+    }                                                                                                      \
+    int NAME##_device(adi_cuda_context *c, adi_cuda_handle h, const float *in, uint32_t batch, float *out) { \
+        return guarded([&] {                                                                               \
+            std::lock_guard<std::mutex> g(require(c)->lock);                                               \
+            use_device(c);                                                                                 \
+            if (!in || !out) invalid("input or output pointer is null");                                   \
+            FN(c, lookup(c->MAP, h, KIND), in, batch, out);                                                \
+        });                                                                                                \
+    }
+
+ADI_HOST_MATMUL(adi_cuda_expert_matmul, experts, "expert", expert_matmul_dev)
+ADI_HOST_MATMUL(adi_cuda_ne_matmul, nes, "NE", ne_matmul_dev)
+ADI_HOST_MATMUL(adi_cuda_head_matmul, heads, "head", head_matmul_dev)
+ADI_HOST_MATMUL(adi_cuda_bf16_matmul, bf16s, "bf16", bf16_matmul_dev)
+
+int adi_cuda_moe_forward_batch(adi_cuda_context *c, adi_cuda_handle h, const float *in, uint32_t batch,
+                               float *out, uint32_t *route_experts, float *route_weights) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        auto &L = lookup(c->moes, h, "MoE layer");
+        if (batch == 0) invalid("MoE batch shape mismatch");
+        const size_t n = size_t(batch) * L.hidden;
+        uint32_t *dre = c->buffer<uint32_t>("host_re", size_t(batch) * 8);
+        float *drw = c->buffer<float>("host_rw", size_t(batch) * 8);
+        host_call(c, in, n, out, n, [&](const float *din, float *dout) {
+            moe_forward_dev(c, L, din, batch, dout, dre, drw);
+            if (route_experts)
+                check(cudaMemcpyAsync(route_experts, dre, size_t(batch) * 8 * 4, cudaMemcpyDeviceToHost, c->stream),
+                      "D2H routes");
+            if (route_weights)
+                check(cudaMemcpyAsync(route_weights, drw, size_t(batch) * 8 * 4, cudaMemcpyDeviceToHost, c->stream),
+                      "D2H weights");
+        });
+    });
+}
+
+int adi_cuda_moe_forward_batch_device(adi_cuda_context *c, adi_cuda_handle h, const float *in, uint32_t batch,
+                                      float *out, uint32_t *route_experts, float *route_weights) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!in || !out) invalid("input or output pointer is null");
+        moe_forward_dev(c, lookup(c->moes, h, "MoE layer"), in, batch, out, route_experts, route_weights);
+    });
+}
+
+int adi_cuda_expert_states(adi_cuda_context *c, const uint16_t *words, uint32_t tiles, uint32_t *states) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!words || !states || tiles == 0) invalid("expert state decode arguments are invalid");
+        auto w = upload_bytes(words, size_t(tiles) * 48, "words");
+        uint32_t *d = c->buffer<uint32_t>("states", size_t(tiles) * 32);
+        launch_expert_states(w->as<uint16_t>(), tiles, d, c->stream);
+        c->after_launch(1);
+        check(cudaMemcpyAsync(states, d, size_t(tiles) * 32 * 4, cudaMemcpyDeviceToHost, c->stream), "D2H");
+        check(cudaStreamSynchronize(c->stream), "synchronize");
+    });
+}
+
+int adi_cuda_ne_states(adi_cuda_context *c, const uint16_t *words, uint32_t tiles, uint32_t *states) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!words || !states || tiles == 0) invalid("NE state decode arguments are invalid");
+        auto w = upload_bytes(words, size_t(tiles) * 128, "words");
+        uint32_t *d = c->buffer<uint32_t>("states", size_t(tiles) * 128);
+        launch_ne_states(w->as<uint16_t>(), tiles, d, c->stream);
+        c->after_launch(1);
+        check(cudaMemcpyAsync(states, d, size_t(tiles) * 128 * 4, cudaMemcpyDeviceToHost, c->stream), "D2H");
+        check(cudaStreamSynchronize(c->stream), "synchronize");
+    });
+}
+
+int adi_cuda_expert_state_values(adi_cuda_context *c, const float *tlut, float *values) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!values) invalid("values pointer is null");
+        ExpertCodec *codec = c->expert_codec(tlut);
+        float *d = c->buffer<float>("state_values", 65536 * 8);
+        launch_expert_state_values(codec->half_tables.as<uint2>(), d, c->stream);
+        c->after_launch(1);
+        check(cudaMemcpyAsync(values, d, 65536 * 8 * 4, cudaMemcpyDeviceToHost, c->stream), "D2H");
+        check(cudaStreamSynchronize(c->stream), "synchronize");
+    });
+}
+
+int adi_cuda_ne_state_values(adi_cuda_context *c, const float *tlut, float *values) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!values) invalid("values pointer is null");
+        NeCodec *codec = c->ne_codec(tlut);
+        float *d = c->buffer<float>("state_values", 65536 * 2);
+        launch_ne_state_values(codec->table.as<float2>(), d, c->stream);
+        c->after_launch(1);
+        check(cudaMemcpyAsync(values, d, 65536 * 2 * 4, cudaMemcpyDeviceToHost, c->stream), "D2H");
+        check(cudaStreamSynchronize(c->stream), "synchronize");
+    });
+}
+
+int adi_cuda_top_experts(adi_cuda_context *c, const float *logits, uint32_t tokens, uint32_t experts,
+                         uint32_t *route_experts, float *route_weights) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (experts < 8) invalid("MoE routing requires at least eight experts");
+        if (!logits || !route_experts || !route_weights || tokens == 0) invalid("top-k arguments are invalid");
+        const size_t n = size_t(tokens) * experts;
+        float *dl = c->buffer<float>("topk_logits", n);
+        uint32_t *de = c->buffer<uint32_t>("topk_e", size_t(tokens) * 8);
+        float *dw = c->buffer<float>("topk_w", size_t(tokens) * 8);
+        check(cudaMemcpyAsync(dl, logits, n * 4, cudaMemcpyHostToDevice, c->stream), "H2D");
+        launch_top_experts(dl, experts, tokens, experts, de, dw, c->stream);
+        c->after_launch(1);
+        check(cudaMemcpyAsync(route_experts, de, size_t(tokens) * 32, cudaMemcpyDeviceToHost, c->stream), "D2H");
+        check(cudaMemcpyAsync(route_weights, dw, size_t(tokens) * 32, cudaMemcpyDeviceToHost, c->stream), "D2H");
+        check(cudaStreamSynchronize(c->stream), "synchronize");
+    });
+}
+
+int adi_cuda_hadamard(adi_cuda_context *c, float *values, uint32_t count, uint32_t n) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!values || !pow2(n) || n > 8192) invalid("hadamard length must be a power of two up to 8192");
+        const size_t total = size_t(count) * n;
+        float *d = c->buffer<float>("hadamard", total);
+        check(cudaMemcpyAsync(d, values, total * 4, cudaMemcpyHostToDevice, c->stream), "H2D");
+        launch_hadamard(d, count, n, transform_scale(n), c->stream);
+        c->after_launch(1);
+        check(cudaMemcpyAsync(values, d, total * 4, cudaMemcpyDeviceToHost, c->stream), "D2H");
+        check(cudaStreamSynchronize(c->stream), "synchronize");
+    });
+}
+
+int adi_cuda_rms_norm(adi_cuda_context *c, const float *inputs, const uint16_t *weight_bf16, uint32_t count,
+                      uint32_t n, float weight_offset, float epsilon, float *outputs) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!inputs || !weight_bf16 || !outputs || n == 0) invalid("RMS norm shape mismatch");
+        const size_t total = size_t(count) * n;
+        auto w = upload_bytes(weight_bf16, size_t(n) * 2, "weight");
+        float *d = c->buffer<float>("rms_in", total);
+        float *o = c->buffer<float>("rms_out", total);
+        check(cudaMemcpyAsync(d, inputs, total * 4, cudaMemcpyHostToDevice, c->stream), "H2D");
+        launch_rms_norm(d, w->as<uint16_t>(), count, n, weight_offset, epsilon, o, c->stream);
+        c->after_launch(1);
+        check(cudaMemcpyAsync(outputs, o, total * 4, cudaMemcpyDeviceToHost, c->stream), "D2H");
+        check(cudaStreamSynchronize(c->stream), "synchronize");
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,903 @@
+// CUDA kernels of the packed MoE path for B200 (sm_100a).
+//
+// Layout and roofline notes live beside each kernel. The expert codec is
+// bound by its value gather: every 16-bit state selects 8 f16 values (16
+// bytes) from a 256 KiB table, which does not fit one SM's shared memory.
+// The expert kernels therefore split each value row in two 8-byte halves
+// (components 0-3 and 4-7): a CTA keeps one 128 KiB half in shared memory and
+// produces the partial products of the columns that half covers; the two
+// partials are summed before the output transform.
+#include "codec.cuh"
+#include "kernels.cuh"
+
+#include <cuda_bf16.h>
+
+namespace adi_cuda {
+
+namespace {
+
+__device__ __forceinline__ float f16_bits_to_f32(uint16_t bits) {
+    return __half2float(__ushort_as_half(bits));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Codec tables
+// ---------------------------------------------------------------------------
+
+// half_tables[h][i] = f16(tlut[2i][4h .. 4h+3]) (RNE, as f32_to_f16 of the
+// reference); component 0 is stored unsigned, the sign comes from the state.
+__global__ void build_expert_tables_kernel(const float *tlut, uint2 *half_tables) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= kExpertTableRows) return;
+    const float *row = tlut + (size_t)(2 * i) * 8;
+    for (int h = 0; h < 2; ++h) {
+        const __half2 a = __floats2half2_rn(row[4 * h + 0], row[4 * h + 1]);
+        const __half2 b = __floats2half2_rn(row[4 * h + 2], row[4 * h + 3]);
+        uint2 packed;
+        packed.x = *reinterpret_cast<const uint32_t *>(&a);
+        packed.y = *reinterpret_cast<const uint32_t *>(&b);
+        half_tables[h * kExpertTableRows + i] = packed;
+    }
+}
+
+// table[i] for signed index i = row | negative << 9 (src/codec_cache.cpp:85-115).
+__global__ void build_ne_table_kernel(const float *tlut, float2 *table) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= kNeTableRows) return;
+    const uint32_t row = i & 511u;
+    float v0 = __half2float(__float2half_rn(tlut[row * 2]));
+    const float v1 = __half2float(__float2half_rn(tlut[row * 2 + 1]));
+    if (i >> 9) v0 = -v0;
+    table[i] = make_float2(v0, v1);
+}
+
+void launch_build_expert_tables(const float *tlut, uint2 *half_tables, cudaStream_t s) {
+    build_expert_tables_kernel<<<kExpertTableRows / 256, 256, 0, s>>>(tlut, half_tables);
+}
+
+void launch_build_ne_table(const float *tlut, float2 *table, cudaStream_t s) {
+    build_ne_table_kernel<<<kNeTableRows / 256, 256, 0, s>>>(tlut, table);
+}
+
+// ---------------------------------------------------------------------------
+// Decode checks: states and state values, for bit-exact comparison
+// ---------------------------------------------------------------------------
+
+// One warp per tile; lane i decodes state i from the tile's 12 u32 words,
+// exactly as the GEMM kernels do (shuffle of the two words that hold it).
+__global__ void expert_states_kernel(const uint16_t *words, uint32_t tiles, uint32_t *states) {
+    const uint32_t tile = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const uint32_t lane = threadIdx.x & 31u;
+    if (tile >= tiles) return;
+    const uint32_t *tw = reinterpret_cast<const uint32_t *>(words) + (size_t)tile * kExpertU32PerTile;
+    const uint32_t w = lane < kExpertU32PerTile ? tw[lane] : 0u;
+    const uint32_t q = (lane * 12u) >> 5;
+    const uint32_t q1 = q + 1u == kExpertU32PerTile ? 0u : q + 1u;
+    const uint32_t hi = stream_order(__shfl_sync(0xffffffffu, w, q));
+    const uint32_t lo = stream_order(__shfl_sync(0xffffffffu, w, q1));
+    states[(size_t)tile * 32 + lane] = expert_window(hi, lo, lane);
+}
+
+// One warp per tile; lane L decodes states 4L..4L+3 from u32 words L, L+1.
+__global__ void ne_states_kernel(const uint16_t *words, uint32_t tiles, uint32_t *states) {
+    const uint32_t tile = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const uint32_t lane = threadIdx.x & 31u;
+    if (tile >= tiles) return;
+    const uint32_t *tw = reinterpret_cast<const uint32_t *>(words) + (size_t)tile * kNeU32PerTile;
+    const uint32_t v = tw[lane];
+    const uint32_t v2 = __shfl_sync(0xffffffffu, v, (lane + 1u) & 31u);
+    uint32_t *out = states + (size_t)tile * 128 + lane * 4;
+    out[0] = v & 0xFFFFu;
+    out[1] = __byte_perm(v, 0, 0x4403);
+    out[2] = v >> 16;
+    out[3] = __byte_perm(v, v2, 0x0025) & 0xFFFFu;
+}
+
+// values[s][c] for all 65536 states from the device tables.
+__global__ void expert_state_values_kernel(const uint2 *half_tables, float *values) {
+    const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= 65536u) return;
+    const uint32_t p = state_product(s);
+    const uint32_t idx = expert_table_index(p);
+    for (int h = 0; h < 2; ++h) {
+        uint2 raw = half_tables[h * kExpertTableRows + idx];
+        if (h == 0) raw.x ^= expert_negative(p) << 15;
+        const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+        float4 out = make_float4(a.x, a.y, b.x, b.y);
+        reinterpret_cast<float4 *>(values)[s * 2 + h] = out;
+    }
+}
+
+__global__ void ne_state_values_kernel(const float2 *table, float *values) {
+    const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= 65536u) return;
+    reinterpret_cast<float2 *>(values)[s] = table[ne_table_index(state_product(s))];
+}
+
+void launch_expert_states(const uint16_t *words, uint32_t tiles, uint32_t *states, cudaStream_t s) {
+    expert_states_kernel<<<(tiles + 7) / 8, 256, 0, s>>>(words, tiles, states);
+}
+void launch_ne_states(const uint16_t *words, uint32_t tiles, uint32_t *states, cudaStream_t s) {
+    ne_states_kernel<<<(tiles + 7) / 8, 256, 0, s>>>(words, tiles, states);
+}
+void launch_expert_state_values(const uint2 *half_tables, float *values, cudaStream_t s) {
+    expert_state_values_kernel<<<256, 256, 0, s>>>(half_tables, values);
+}
+void launch_ne_state_values(const float2 *table, float *values, cudaStream_t s) {
+    ne_state_values_kernel<<<256, 256, 0, s>>>(table, values);
+}
+
+// ---------------------------------------------------------------------------
+// Input transform x' = H(x * su) and output transform y = H(acc) * sv
+// ---------------------------------------------------------------------------
+
+// Block per (row, job). Bit-identical to the reference's per-row transform:
+// one rounded multiply per element, then the butterfly network.
+__global__ void prep_kernel(PrepParams p) {
+    extern __shared__ float v[];
+    const uint32_t row = blockIdx.x;
+    const int job = blockIdx.y;
+    const uint32_t token = p.grouped ? p.grouped[row] : row;
+    const uint32_t expert = p.pos_expert ? p.pos_expert[row] : 0u;
+    const float *x = p.input + (size_t)token * p.cols;
+    const void *su_base = job ? p.su[1] : p.su[0];
+    float *out = (job ? p.out[1] : p.out[0]) + (size_t)row * p.cols;
+    if (p.su_is_f16) {
+        const uint16_t *su = static_cast<const uint16_t *>(su_base) + (size_t)expert * p.su_stride;
+        for (uint32_t c = threadIdx.x; c < p.cols; c += blockDim.x)
+            v[c] = __fmul_rn(x[c], f16_bits_to_f32(su[c]));
+    } else {
+        const int8_t *su = static_cast<const int8_t *>(su_base) + (size_t)expert * p.su_stride;
+        for (uint32_t c = threadIdx.x; c < p.cols; c += blockDim.x)
+            v[c] = __fmul_rn(x[c], (float)su[c]);
+    }
+    __syncthreads();
+    block_fwht(v, p.cols, p.scale);
+    for (uint32_t c = threadIdx.x; c < p.cols; c += blockDim.x) out[c] = v[c];
+}
+
+void launch_prep(const PrepParams &p, cudaStream_t s) {
+    if (p.rows == 0) return;
+    dim3 grid(p.rows, p.jobs);
+    prep_kernel<<<grid, 256, p.cols * sizeof(float), s>>>(p);
+}
+
+__global__ void finalize_kernel(const float *acc0, const float *acc1, const void *sv, int sv_is_f16,
+                                uint32_t rows, float scale, float *out) {
+    extern __shared__ float v[];
+    const uint32_t b = blockIdx.x;
+    const float *a0 = acc0 + (size_t)b * rows;
+    const float *a1 = acc1 ? acc1 + (size_t)b * rows : nullptr;
+    for (uint32_t r = threadIdx.x; r < rows; r += blockDim.x) v[r] = a1 ? a0[r] + a1[r] : a0[r];
+    __syncthreads();
+    block_fwht(v, rows, scale);
+    for (uint32_t r = threadIdx.x; r < rows; r += blockDim.x) {
+        const float m = sv_is_f16 ? f16_bits_to_f32(static_cast<const uint16_t *>(sv)[r])
+                                  : (float)static_cast<const int8_t *>(sv)[r];
+        out[(size_t)b * rows + r] = __fmul_rn(v[r], m);
+    }
+}
+
+void launch_finalize(const float *acc0, const float *acc1, const void *sv, int sv_is_f16,
+                     uint32_t batch, uint32_t rows, float scale, float *out, cudaStream_t s) {
+    if (batch == 0) return;
+    finalize_kernel<<<batch, 256, rows * sizeof(float), s>>>(acc0, acc1, sv, sv_is_f16, rows, scale, out);
+}
+
+// ---------------------------------------------------------------------------
+// Work items
+// ---------------------------------------------------------------------------
+
+struct Item {
+    uint32_t expert, job, row_block, pos0, count;
+};
+
+__device__ __forceinline__ uint32_t work_count(const WorkList &w, uint32_t row_blocks) {
+    if (w.items) return *w.item_count;
+    return ((w.dense_tokens + kMaxTokens - 1) / kMaxTokens) * w.dense_jobs * row_blocks;
+}
+
+__device__ __forceinline__ Item work_item(const WorkList &w, uint32_t i, uint32_t row_blocks) {
+    if (w.items) {
+        const uint4 v = w.items[i];
+        return Item{v.x, v.y >> 16, v.y & 0xFFFFu, v.z, v.w};
+    }
+    const uint32_t rb = i % row_blocks;
+    const uint32_t job = (i / row_blocks) % w.dense_jobs;
+    const uint32_t chunk = i / (row_blocks * w.dense_jobs);
+    const uint32_t pos0 = chunk * kMaxTokens;
+    return Item{0u, job, rb, pos0, min((uint32_t)kMaxTokens, w.dense_tokens - pos0)};
+}
+
+// ---------------------------------------------------------------------------
+// Expert streaming GEMM on CUDA cores (fp32 accumulate)
+//
+// Persistent: one CTA per SM, CTA parity selects the value half it owns. A
+// work item is (expert, projection, block of 4 tile rows, up to 8 positions).
+// Warp w walks tile columns w, w+8, ...; inside a tile, lane i owns state i
+// (tile row i>>1, columns (i&1)*8 + 4*half .. +3), so its inputs stay in
+// registers across the item's tile rows. Per tile the warp loads the 48-byte
+// word stream once (12 lanes), shuffles each lane the two words holding its
+// window, gathers one 8-byte value half from shared memory and applies it to
+// every position. Partial sums reduce over lane pairs and warps at the end
+// of the item.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kGemmThreads, 1) expert_gemm_kernel(const ExpertGemmParams p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint2 *table = reinterpret_cast<uint2 *>(smem);
+    float *red = reinterpret_cast<float *>(smem + kExpertTableRows * sizeof(uint2));
+    const uint32_t half = blockIdx.x & 1u;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(p.table + half * kExpertTableRows);
+        uint4 *dst = reinterpret_cast<uint4 *>(table);
+        for (uint32_t i = threadIdx.x; i < kExpertTableRows / 2; i += blockDim.x) dst[i] = src[i];
+    }
+    __syncthreads();
+
+    const uint32_t rb0 = (p.job[0].rows / 16 + kRowTiles - 1) / kRowTiles;
+    const uint32_t n_items = work_count(p.work, rb0);
+    const uint32_t q = (lane * 12u) >> 5;
+    const uint32_t q1 = q + 1u == kExpertU32PerTile ? 0u : q + 1u;
+
+    for (uint32_t item_index = blockIdx.x >> 1; item_index < n_items; item_index += gridDim.x >> 1) {
+        const Item it = work_item(p.work, item_index, rb0);
+        const ExpertJob J = it.job ? p.job[1] : p.job[0];
+        const uint32_t TC = J.cols / 16, TR = J.rows / 16;
+        const uint32_t *tiles = J.trellis + (size_t)it.expert * J.expert_stride32;
+        const uint16_t *gam = J.gamma + (size_t)it.expert * J.gamma_stride;
+        const uint32_t n = it.count;
+
+        float acc[kRowTiles][kMaxTokens];
+#pragma unroll
+        for (int r = 0; r < kRowTiles; ++r)
+#pragma unroll
+            for (int t = 0; t < kMaxTokens; ++t) acc[r][t] = 0.0f;
+
+        for (uint32_t tc = warp; tc < TC; tc += kGemmWarps) {
+            float4 xv[kMaxTokens];
+            const uint32_t col = tc * 16 + (lane & 1u) * 8 + half * 4;
+#pragma unroll
+            for (int t = 0; t < kMaxTokens; ++t)
+                xv[t] = (uint32_t)t < n ? __ldg(reinterpret_cast<const float4 *>(
+                                              J.x + (size_t)(it.pos0 + t) * J.cols + col))
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int r = 0; r < kRowTiles; ++r) {
+                const uint32_t tr = it.row_block * kRowTiles + r;
+                if (tr >= TR) break;
+                const uint32_t *tw = tiles + (size_t)(tr * TC + tc) * kExpertU32PerTile;
+                const uint32_t w = lane < kExpertU32PerTile ? __ldg(tw + lane) : 0u;
+                const uint32_t hi = stream_order(__shfl_sync(0xffffffffu, w, q));
+                const uint32_t lo = stream_order(__shfl_sync(0xffffffffu, w, q1));
+                const uint32_t state = expert_window(hi, lo, lane);
+                const uint32_t prod = state_product(state);
+                uint2 raw = table[expert_table_index(prod)];
+                if (half == 0) raw.x ^= expert_negative(prod) << 15;
+                const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+                const float g = f16_bits_to_f32(__ldg(gam + wave_index(TR, TC, tr + tc)));
+#pragma unroll
+                for (int t = 0; t < kMaxTokens; ++t) {
+                    if ((uint32_t)t < n) {
+                        float part = a.x * xv[t].x;
+                        part = fmaf(a.y, xv[t].y, part);
+                        part = fmaf(b.x, xv[t].z, part);
+                        part = fmaf(b.y, xv[t].w, part);
+                        acc[r][t] = fmaf(part, g, acc[r][t]);
+                    }
+                }
+            }
+        }
+
+#pragma unroll
+        for (int r = 0; r < kRowTiles; ++r)
+#pragma unroll
+            for (int t = 0; t < kMaxTokens; ++t) acc[r][t] += __shfl_xor_sync(0xffffffffu, acc[r][t], 1);
+        if ((lane & 1u) == 0) {
+#pragma unroll
+            for (int r = 0; r < kRowTiles; ++r)
+#pragma unroll
+                for (int t = 0; t < kMaxTokens; ++t)
+                    red[((warp * kRowTiles + r) * 16 + (lane >> 1)) * kMaxTokens + t] = acc[r][t];
+        }
+        __syncthreads();
+        const uint32_t rows_here = min((uint32_t)kRowTiles, TR - it.row_block * kRowTiles) * 16;
+        for (uint32_t idx = threadIdx.x; idx < rows_here * n; idx += blockDim.x) {
+            const uint32_t t = idx / rows_here, row = idx % rows_here;
+            float sum = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kGemmWarps; ++w) sum += red[((w * kRowTiles) * 16 + row) * kMaxTokens + t];
+            J.acc[half * J.half_stride + (size_t)(it.pos0 + t) * J.rows + it.row_block * kRowTiles * 16 + row] = sum;
+        }
+        __syncthreads();
+    }
+}
+
+void launch_expert_gemm(const ExpertGemmParams &p, int grid, cudaStream_t s) {
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(expert_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kExpertGemmSmem);
+        configured = true;
+    }
+    expert_gemm_kernel<<<grid & ~1, kGemmThreads, kExpertGemmSmem, s>>>(p);
+}
+
+// ---------------------------------------------------------------------------
+// NE streaming GEMM on CUDA cores
+//
+// The [1024] signed value-pair table is tiny, so it is replicated 16 times in
+// shared memory, copy c serving lanes c and c+16: a 64-bit gather by a
+// half-warp then touches 16 distinct bank pairs, conflict-free. Lane L owns
+// states 4L..4L+3 of a tile (row L>>1, columns (L&1)*8 .. +7), decoded from
+// u32 words L and L+1 of the tile's 128-byte stream.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kGemmThreads, 1) ne_gemm_kernel(const NeGemmParams p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    float2 *table = reinterpret_cast<float2 *>(smem);
+    float *red = reinterpret_cast<float *>(smem + kNeTableRows * kNeTableCopies * sizeof(float2));
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    for (uint32_t i = threadIdx.x; i < kNeTableRows * kNeTableCopies; i += blockDim.x)
+        table[i] = p.table[i / kNeTableCopies];
+    __syncthreads();
+
+    const uint32_t rb0 = (p.job[0].rows / 16 + kRowTiles - 1) / kRowTiles;
+    const uint32_t n_items = work_count(p.work, rb0);
+    const float2 *my_table = table + (lane & (kNeTableCopies - 1));
+
+    for (uint32_t item_index = blockIdx.x; item_index < n_items; item_index += gridDim.x) {
+        const Item it = work_item(p.work, item_index, rb0);
+        const NeJob J = it.job ? p.job[1] : p.job[0];
+        const uint32_t TC = J.cols / 16, TR = J.rows / 16;
+        const uint32_t n = it.count;
+
+        float acc[kRowTiles][kMaxTokens];
+#pragma unroll
+        for (int r = 0; r < kRowTiles; ++r)
+#pragma unroll
+            for (int t = 0; t < kMaxTokens; ++t) acc[r][t] = 0.0f;
+
+        for (uint32_t tc = warp; tc < TC; tc += kGemmWarps) {
+            float4 x0[kMaxTokens], x1[kMaxTokens];
+            const uint32_t col = tc * 16 + (lane & 1u) * 8;
+#pragma unroll
+            for (int t = 0; t < kMaxTokens; ++t) {
+                if ((uint32_t)t < n) {
+                    const float4 *src = reinterpret_cast<const float4 *>(
+                        J.x + (size_t)(it.pos0 + t) * J.cols + col);
+                    x0[t] = __ldg(src);
+                    x1[t] = __ldg(src + 1);
+                } else {
+                    x0[t] = x1[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kRowTiles; ++r) {
+                const uint32_t tr = it.row_block * kRowTiles + r;
+                if (tr >= TR) break;
+                const uint32_t *tw = J.trellis + (size_t)(tr * TC + tc) * kNeU32PerTile;
+                const uint32_t v = __ldg(tw + lane);
+                const uint32_t v2 = __shfl_sync(0xffffffffu, v, (lane + 1u) & 31u);
+                const uint32_t s0 = v & 0xFFFFu;
+                const uint32_t s1 = __byte_perm(v, 0, 0x4403);
+                const uint32_t s2 = v >> 16;
+                const uint32_t s3 = __byte_perm(v, v2, 0x0025) & 0xFFFFu;
+                const float2 w0 = my_table[ne_table_index(state_product(s0)) * kNeTableCopies];
+                const float2 w1 = my_table[ne_table_index(state_product(s1)) * kNeTableCopies];
+                const float2 w2 = my_table[ne_table_index(state_product(s2)) * kNeTableCopies];
+                const float2 w3 = my_table[ne_table_index(state_product(s3)) * kNeTableCopies];
+#pragma unroll
+                for (int t = 0; t < kMaxTokens; ++t) {
+                    if ((uint32_t)t < n) {
+                        float part = w0.x * x0[t].x;
+                        part = fmaf(w0.y, x0[t].y, part);
+                        part = fmaf(w1.x, x0[t].z, part);
+                        part = fmaf(w1.y, x0[t].w, part);
+                        part = fmaf(w2.x, x1[t].x, part);
+                        part = fmaf(w2.y, x1[t].y, part);
+                        part = fmaf(w3.x, x1[t].z, part);
+                        part = fmaf(w3.y, x1[t].w, part);
+                        acc[r][t] += part;
+                    }
+                }
+            }
+        }
+
+#pragma unroll
+        for (int r = 0; r < kRowTiles; ++r)
+#pragma unroll
+            for (int t = 0; t < kMaxTokens; ++t) acc[r][t] += __shfl_xor_sync(0xffffffffu, acc[r][t], 1);
+        if ((lane & 1u) == 0) {
+#pragma unroll
+            for (int r = 0; r < kRowTiles; ++r)
+#pragma unroll
+                for (int t = 0; t < kMaxTokens; ++t)
+                    red[((warp * kRowTiles + r) * 16 + (lane >> 1)) * kMaxTokens + t] = acc[r][t];
+        }
+        __syncthreads();
+        const uint32_t rows_here = min((uint32_t)kRowTiles, TR - it.row_block * kRowTiles) * 16;
+        for (uint32_t idx = threadIdx.x; idx < rows_here * n; idx += blockDim.x) {
+            const uint32_t t = idx / rows_here, row = idx % rows_here;
+            float sum = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kGemmWarps; ++w) sum += red[((w * kRowTiles) * 16 + row) * kMaxTokens + t];
+            J.acc[(size_t)(it.pos0 + t) * J.rows + it.row_block * kRowTiles * 16 + row] = sum * J.weight_scale;
+        }
+        __syncthreads();
+    }
+}
+
+void launch_ne_gemm(const NeGemmParams &p, int grid, cudaStream_t s) {
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(ne_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kNeGemmSmem);
+        configured = true;
+    }
+    ne_gemm_kernel<<<grid, kGemmThreads, kNeGemmSmem, s>>>(p);
+}
+
+// ---------------------------------------------------------------------------
+// bf16-weight GEMM with fp32 activations and accumulation (router, shared
+// expert gate, bf16_matmul). Block: 8 tokens x 32 rows; warp: 4 rows.
+// ---------------------------------------------------------------------------
+__global__ void bf16_gemm_kernel(const uint16_t *w0, uint32_t rows0, const uint16_t *w1, uint32_t rows1,
+                                 const float *x, uint32_t tokens, uint32_t cols, float *out,
+                                 uint32_t out_stride) {
+    extern __shared__ float xs[];
+    const uint32_t t0 = blockIdx.x * 8;
+    const uint32_t nt = min(8u, tokens - t0);
+    for (uint32_t i = threadIdx.x; i < 8 * cols; i += blockDim.x) {
+        const uint32_t t = i / cols;
+        xs[i] = t < nt ? x[(size_t)(t0 + t) * cols + (i % cols)] : 0.0f;
+    }
+    __syncthreads();
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t rbase = blockIdx.y * 32 + warp * 4;
+    const uint32_t R = rows0 + rows1;
+    const uint16_t *row_ptr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t r = rbase + i;
+        row_ptr[i] = r < rows0 ? w0 + (size_t)r * cols : (r < R ? w1 + (size_t)(r - rows0) * cols : nullptr);
+    }
+    float acc[4][8] = {};
+    for (uint32_t c = lane; c < cols; c += 32) {
+        float xv[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) xv[t] = xs[t * cols + c];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (row_ptr[i]) {
+                const float wv = bf16_bits_to_f32(__ldg(row_ptr[i] + c));
+#pragma unroll
+                for (int t = 0; t < 8; ++t) acc[i][t] = fmaf(wv, xv[t], acc[i][t]);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const float v = warp_sum(acc[i][t]);
+            if (lane == 0 && row_ptr[i] && (uint32_t)t < nt) out[(size_t)(t0 + t) * out_stride + rbase + i] = v;
+        }
+}
+
+void launch_bf16_gemm(const uint16_t *w0, uint32_t rows0, const uint16_t *w1, uint32_t rows1,
+                      const float *x, uint32_t tokens, uint32_t cols, float *out, uint32_t out_stride,
+                      cudaStream_t s) {
+    if (tokens == 0) return;
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(bf16_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        configured = true;
+    }
+    dim3 grid((tokens + 7) / 8, (rows0 + rows1 + 31) / 32);
+    bf16_gemm_kernel<<<grid, 256, 8 * cols * sizeof(float), s>>>(w0, rows0, w1, rows1, x, tokens, cols,
+                                                                  out, out_stride);
+}
+
+// ---------------------------------------------------------------------------
+// top_experts (src/executor.cpp:193-229): warp per token, eight rounds of a
+// warp arg-max on (logit desc, index asc); weights over the selected eight.
+// ---------------------------------------------------------------------------
+__global__ void top_experts_kernel(const float *logits, uint32_t stride, uint32_t tokens, uint32_t experts,
+                                   uint32_t *route_experts, float *route_weights) {
+    const uint32_t token = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const uint32_t lane = threadIdx.x & 31u;
+    if (token >= tokens) return;
+    const float *l = logits + (size_t)token * stride;
+    uint32_t chosen[8];
+    float chosen_value[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        float bv = -INFINITY;
+        uint32_t be = 0xFFFFFFFFu;
+        for (uint32_t e = lane; e < experts; e += 32) {
+            bool taken = false;
+#pragma unroll
+            for (int j = 0; j < k; ++j) taken |= chosen[j] == e;
+            const float v = l[e];
+            if (!taken && (v > bv || (v == bv && e < be))) {
+                bv = v;
+                be = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const uint32_t oe = __shfl_xor_sync(0xffffffffu, be, o);
+            if (ov > bv || (ov == bv && oe < be)) {
+                bv = ov;
+                be = oe;
+            }
+        }
+        if (be == 0xFFFFFFFFu) {
+            // Only NaN logits remain: take the lowest unchosen index, so the
+            // route is always a valid expert.
+            be = 0;
+            for (bool again = true; again;) {
+                again = false;
+#pragma unroll
+                for (int j = 0; j < k; ++j)
+                    if (chosen[j] == be) {
+                        ++be;
+                        again = true;
+                    }
+            }
+            bv = l[be];
+        }
+        chosen[k] = be;
+        chosen_value[k] = bv;
+    }
+    if (lane == 0) {
+        float selected[8], sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            selected[k] = expf(chosen_value[k] - chosen_value[0]);
+            sum += selected[k];
+        }
+        sum = fmaxf(sum, 6.103515625e-5f);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            route_experts[token * 8 + k] = chosen[k];
+            route_weights[token * 8 + k] = selected[k] / sum;
+        }
+    }
+}
+
+void launch_top_experts(const float *logits, uint32_t logit_stride, uint32_t tokens, uint32_t experts,
+                        uint32_t *route_experts, float *route_weights, cudaStream_t s) {
+    if (tokens == 0) return;
+    top_experts_kernel<<<(tokens + 7) / 8, 256, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
+                                                        route_weights);
+}
+
+// ---------------------------------------------------------------------------
+// Routing: counting sort into expert-contiguous positions (the reference's
+// counting sort, src/executor.cpp:1237-1258), deterministic: a position's
+// rank within its expert is the number of earlier tokens routed there,
+// read off a per-expert token bitmap.
+// ---------------------------------------------------------------------------
+__global__ void route_count_kernel(RouteParams p) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= p.tokens * 8) return;
+    const uint32_t t = i >> 3, e = p.route_experts[i];
+    if (e >= p.experts) return;  // top-k never emits one; never index with it
+    atomicAdd(p.counts + e, 1u);
+    atomicOr(p.bitmap + (size_t)e * p.words + (t >> 5), 1u << (t & 31u));
+}
+
+// One block of 1024 threads: offsets, per-expert word prefixes, the position
+// -> expert map and the GEMM work lists (ordered expert-major so that the
+// CTAs working on one expert run together and share its inputs in L2).
+__global__ void route_scan_kernel(RouteParams p) {
+    __shared__ uint32_t scan[1024];
+    __shared__ uint32_t chunk_scan[1024];
+    const uint32_t e = threadIdx.x;
+    const uint32_t count = e < p.experts ? p.counts[e] : 0u;
+    const uint32_t chunks = (count + kMaxTokens - 1) / kMaxTokens;
+    scan[e] = count;
+    chunk_scan[e] = chunks;
+    __syncthreads();
+    for (uint32_t o = 1; o < 1024; o <<= 1) {
+        const uint32_t a = e >= o ? scan[e - o] : 0u;
+        const uint32_t b = e >= o ? chunk_scan[e - o] : 0u;
+        __syncthreads();
+        scan[e] += a;
+        chunk_scan[e] += b;
+        __syncthreads();
+    }
+    const uint32_t offset = scan[e] - count;
+    const uint32_t chunk_offset = chunk_scan[e] - chunks;
+    if (e < p.experts) {
+        p.offsets[e] = offset;
+        for (uint32_t i = 0; i < count; ++i) p.pos_expert[offset + i] = e;
+        for (uint32_t c = 0; c < chunks; ++c) {
+            const uint32_t pos0 = offset + c * kMaxTokens;
+            const uint32_t n = min((uint32_t)kMaxTokens, count - c * kMaxTokens);
+            for (uint32_t j = 0; j < 2; ++j)
+                for (uint32_t rb = 0; rb < p.row_blocks_gate_up; ++rb)
+                    p.items_gate_up[((chunk_offset + c) * 2 + j) * p.row_blocks_gate_up + rb] =
+                        make_uint4(e, (j << 16) | rb, pos0, n);
+            for (uint32_t rb = 0; rb < p.row_blocks_down; ++rb)
+                p.items_down[(chunk_offset + c) * p.row_blocks_down + rb] = make_uint4(e, rb, pos0, n);
+        }
+    }
+    if (e == p.experts - 1) {
+        p.offsets[p.experts] = offset + count;
+        const uint32_t total_chunks = chunk_offset + chunks;
+        *p.count_gate_up = total_chunks * 2 * p.row_blocks_gate_up;
+        *p.count_down = total_chunks * p.row_blocks_down;
+    }
+    // Per-expert exclusive prefix of bitmap popcounts, one warp per expert.
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    for (uint32_t ex = warp; ex < p.experts; ex += 32) {
+        uint32_t running = 0;
+        for (uint32_t w0 = 0; w0 < p.words; w0 += 32) {
+            const uint32_t w = w0 + lane;
+            const uint32_t c = w < p.words ? __popc(p.bitmap[(size_t)ex * p.words + w]) : 0u;
+            uint32_t incl = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= (uint32_t)o) incl += v;
+            }
+            if (w < p.words) p.prefix[(size_t)ex * p.words + w] = running + incl - c;
+            running += __shfl_sync(0xffffffffu, incl, 31);
+        }
+    }
+}
+
+__global__ void route_place_kernel(RouteParams p) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= p.tokens * 8) return;
+    const uint32_t t = i >> 3, e = p.route_experts[i];
+    if (e >= p.experts) return;
+    const size_t w = (size_t)e * p.words + (t >> 5);
+    const uint32_t rank = p.prefix[w] + __popc(p.bitmap[w] & ((1u << (t & 31u)) - 1u));
+    const uint32_t pos = p.offsets[e] + rank;
+    p.grouped[pos] = t;
+    p.route_to_grouped[i] = pos;
+}
+
+void launch_route(const RouteParams &p, cudaStream_t s) {
+    cudaMemsetAsync(p.counts, 0, sizeof(uint32_t) * p.experts, s);
+    cudaMemsetAsync(p.bitmap, 0, sizeof(uint32_t) * (size_t)p.experts * p.words, s);
+    const uint32_t n = p.tokens * 8;
+    route_count_kernel<<<(n + 255) / 256, 256, 0, s>>>(p);
+    route_scan_kernel<<<1, 1024, 0, s>>>(p);
+    route_place_kernel<<<(n + 255) / 256, 256, 0, s>>>(p);
+}
+
+// ---------------------------------------------------------------------------
+// SwiGLU between projections, block per position.
+// ---------------------------------------------------------------------------
+__global__ void mid_kernel(MidParams p) {
+    extern __shared__ float sm[];
+    float *g = sm, *u = sm + p.inner;
+    const uint32_t pos = blockIdx.x;
+    const uint32_t e = p.pos_expert ? p.pos_expert[pos] : 0u;
+    const size_t base = (size_t)pos * p.inner;
+    for (uint32_t i = threadIdx.x; i < p.inner; i += blockDim.x) {
+        float gv = p.acc_gate[base + i], uv = p.acc_up[base + i];
+        if (p.halves == 2) {
+            gv += p.acc_gate[p.half_stride + base + i];
+            uv += p.acc_up[p.half_stride + base + i];
+        }
+        g[i] = gv;
+        u[i] = uv;
+    }
+    __syncthreads();
+    block_fwht(g, p.inner, p.scale);
+    block_fwht(u, p.inner, p.scale);
+    for (uint32_t i = threadIdx.x; i < p.inner; i += blockDim.x) {
+        float svg, svu, sud;
+        if (p.is_f16) {
+            const size_t o = (size_t)e * p.inner + i;
+            svg = f16_bits_to_f32(static_cast<const uint16_t *>(p.sv_gate)[o]);
+            svu = f16_bits_to_f32(static_cast<const uint16_t *>(p.sv_up)[o]);
+            sud = f16_bits_to_f32(static_cast<const uint16_t *>(p.su_down)[o]);
+        } else {
+            svg = (float)static_cast<const int8_t *>(p.sv_gate)[i];
+            svu = (float)static_cast<const int8_t *>(p.sv_up)[i];
+            sud = (float)static_cast<const int8_t *>(p.su_down)[i];
+        }
+        const float gv = __fmul_rn(g[i], svg), uv = __fmul_rn(u[i], svu);
+        g[i] = __fmul_rn(__fmul_rn(silu_f(gv), uv), sud);
+    }
+    __syncthreads();
+    block_fwht(g, p.inner, p.scale);
+    for (uint32_t i = threadIdx.x; i < p.inner; i += blockDim.x) p.xd[base + i] = g[i];
+}
+
+void launch_mid(const MidParams &p, cudaStream_t s) {
+    if (p.positions == 0) return;
+    mid_kernel<<<p.positions, 256, 2 * p.inner * sizeof(float), s>>>(p);
+}
+
+// ---------------------------------------------------------------------------
+// Route-order combine with the shared expert, block per token
+// (src/executor.cpp:1373-1452).
+// ---------------------------------------------------------------------------
+__global__ void combine_kernel(CombineParams p) {
+    extern __shared__ float v[];
+    const uint32_t t = blockIdx.x;
+    const uint32_t H = p.hidden;
+    constexpr int kPer = 8;  // H / blockDim.x for H = 2048; general H loops below
+    float out[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) out[j] = 0.0f;
+    for (int r = 0; r < 8; ++r) {
+        const uint32_t pos = p.route_to_grouped[t * 8 + r];
+        const uint32_t e = p.route_experts[t * 8 + r];
+        const float w = p.route_weights[t * 8 + r];
+        const float *a0 = p.acc_down + (size_t)pos * H;
+        const float *a1 = a0 + p.half_stride;
+        for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) v[i] = a0[i] + a1[i];
+        __syncthreads();
+        block_fwht(v, H, p.scale);
+        const uint16_t *sv = p.sv_down + (size_t)e * H;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const uint32_t i = threadIdx.x + j * blockDim.x;
+            if (i < H) out[j] = fmaf(w, __fmul_rn(v[i], f16_bits_to_f32(sv[i])), out[j]);
+        }
+        __syncthreads();
+    }
+    const float *sa = p.shared_acc + (size_t)t * H;
+    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) v[i] = sa[i];
+    __syncthreads();
+    block_fwht(v, H, p.scale);
+    const float gate = sigmoid_f(p.gate_logits[(size_t)t * p.gate_stride]);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const uint32_t i = threadIdx.x + j * blockDim.x;
+        if (i < H) p.out[(size_t)t * H + i] = fmaf(gate, __fmul_rn(v[i], (float)p.shared_sv[i]), out[j]);
+    }
+}
+
+void launch_combine(const CombineParams &p, cudaStream_t s) {
+    if (p.tokens == 0) return;
+    const uint32_t threads = (p.hidden + 7) / 8;  // kPer elements per thread
+    combine_kernel<<<p.tokens, threads < 32 ? 32 : threads, p.hidden * sizeof(float), s>>>(p);
+}
+
+// ---------------------------------------------------------------------------
+// int5_g64 output head (src/kernels.cpp:847-979): eight 5-bit codes per five
+// little-endian bytes, so a 64-column group is one 320-bit little-endian
+// integer whose k-th 5-bit field is column k. Warp per row, lane per group;
+// up to 8 input rows per pass from shared memory.
+// ---------------------------------------------------------------------------
+__global__ void head_kernel(HeadParams p) {
+    extern __shared__ float xs[];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t groups = p.cols / 64;
+    const uint32_t bytes_per_row = p.cols / 8 * 5;
+    for (uint32_t b0 = 0; b0 < p.batch; b0 += 8) {
+        const uint32_t nb = min(8u, p.batch - b0);
+        __syncthreads();
+        // xs[b][k][g] holds column g*64+k, so lane g reading column k of its
+        // group sits in bank (k*groups + g) mod 32: distinct across the warp.
+        for (uint32_t i = threadIdx.x; i < 8 * p.cols; i += blockDim.x) {
+            const uint32_t b = i / p.cols, c = i % p.cols;
+            xs[b * p.cols + (c % 64) * groups + c / 64] =
+                b < nb ? p.x[(size_t)(b0 + b) * p.cols + c] : 0.0f;
+        }
+        __syncthreads();
+        for (uint32_t row = blockIdx.x * (blockDim.x / 32) + warp; row < p.rows; row += gridDim.x * (blockDim.x / 32)) {
+            float acc[8] = {};
+            for (uint32_t g = lane; g < groups; g += 32) {
+                const uint2 *src = reinterpret_cast<const uint2 *>(p.packed + (size_t)row * bytes_per_row + g * 40);
+                uint32_t w[11];
+#pragma unroll
+                for (int k = 0; k < 5; ++k) {
+                    const uint2 v = __ldg(src + k);
+                    w[2 * k] = v.x;
+                    w[2 * k + 1] = v.y;
+                }
+                w[10] = 0;
+                const float scale = f16_bits_to_f32(__ldg(p.scales + (size_t)row * groups + g));
+                float part[8] = {};
+#pragma unroll
+                for (int k = 0; k < 64; ++k) {
+                    const uint32_t bit = 5 * k;
+                    const uint32_t code = __funnelshift_r(w[bit >> 5], w[(bit >> 5) + 1], bit & 31) & 31u;
+                    const float c = (float)((int)code - 16);
+#pragma unroll
+                    for (int b = 0; b < 8; ++b)
+                        if ((uint32_t)b < nb) part[b] = fmaf(c, xs[b * p.cols + k * groups + g], part[b]);
+                }
+#pragma unroll
+                for (int b = 0; b < 8; ++b) acc[b] = fmaf(part[b], scale, acc[b]);
+            }
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+                const float v = warp_sum(acc[b]);
+                if (lane == 0 && (uint32_t)b < nb) p.out[(size_t)(b0 + b) * p.rows + row] = v;
+            }
+        }
+    }
+}
+
+__global__ void head_protected_kernel(HeadParams p) {
+    const uint32_t pr = blockIdx.x;
+    const uint32_t row = p.protected_rows[pr];
+    const uint16_t *w = p.protected_bf16 + (size_t)pr * p.cols;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    for (uint32_t b = warp; b < p.batch; b += blockDim.x / 32) {
+        float acc = 0.0f;
+        for (uint32_t c = lane; c < p.cols; c += 32)
+            acc = fmaf(bf16_bits_to_f32(w[c]), p.x[(size_t)b * p.cols + c], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) p.out[(size_t)b * p.rows + row] = acc;
+    }
+}
+
+void launch_head(const HeadParams &p, cudaStream_t s) {
+    if (p.batch == 0 || p.rows == 0) return;
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        configured = true;
+    }
+    const uint32_t blocks = min((p.rows + 7) / 8, 148u * 8u);
+    head_kernel<<<blocks, 256, 8 * p.cols * sizeof(float), s>>>(p);
+    if (p.protected_count) head_protected_kernel<<<p.protected_count, 256, 0, s>>>(p);
+}
+
+// ---------------------------------------------------------------------------
+// Standalone transforms
+// ---------------------------------------------------------------------------
+__global__ void hadamard_kernel(float *values, uint32_t n, float scale) {
+    extern __shared__ float v[];
+    float *row = values + (size_t)blockIdx.x * n;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) v[i] = row[i];
+    __syncthreads();
+    block_fwht(v, n, scale);
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) row[i] = v[i];
+}
+
+void launch_hadamard(float *values, uint32_t count, uint32_t n, float scale, cudaStream_t s) {
+    if (count == 0) return;
+    hadamard_kernel<<<count, 256, n * sizeof(float), s>>>(values, n, scale);
+}
+
+__global__ void rms_norm_kernel(const float *x, const uint16_t *w, uint32_t n, float offset, float eps,
+                                float *out) {
+    __shared__ float partial[32];
+    const float *row = x + (size_t)blockIdx.x * n;
+    float sq = 0.0f;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) sq = fmaf(row[i], row[i], sq);
+    sq = warp_sum(sq);
+    if ((threadIdx.x & 31u) == 0) partial[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < blockDim.x / 32 ? partial[threadIdx.x] : 0.0f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) partial[0] = v;
+    }
+    __syncthreads();
+    const float scale = 1.0f / sqrtf(partial[0] / (float)n + eps);
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x)
+        out[(size_t)blockIdx.x * n + i] = row[i] * scale * (offset + bf16_bits_to_f32(w[i]));
+}
+
+void launch_rms_norm(const float *x, const uint16_t *w, uint32_t count, uint32_t n, float offset, float eps,
+                     float *out, cudaStream_t s) {
+    if (count == 0) return;
+    rms_norm_kernel<<<count, 256, 0, s>>>(x, w, n, offset, eps, out);
+}
+
+}  // namespace adi_cuda

@@ -1,0 +1,137 @@
+"""Synthetic packed MoE blocks for benchmarking (no checkpoint exists here).
+
+A block has the configured shapes and distributions: hidden 2048, 256 routed
+experts of intermediate 512 plus one shared expert, top-8; router weights
+bf16 N(0, 0.02); trellis code words uniform; expert scale surfaces (su, sv,
+wave gamma) f16 log-normal(mu=-4, sigma=0.5); shared-expert signs +-1 and
+log-normal weight scales; TLUTs uniform(-1, 1); activations N(0, 1).
+Words come from torch's generator (on the GPU when one is given, which makes
+forty layers' worth a matter of seconds); the arrays are returned on the host
+in the reference's own layouts, ready for upload.
+
+The parity tests build their inputs with the reference test suite's
+splitmix64 instead (tests/fixtures.py); nothing here is used to check
+results.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+
+@dataclass
+class NeView:
+    rows: int
+    columns: int
+    trellis: np.ndarray
+    su: np.ndarray
+    sv: np.ndarray
+    weight_scale: float
+    tlut: np.ndarray
+
+
+@dataclass
+class ExpertView:
+    rows: int
+    columns: int
+    trellis: np.ndarray
+    su: np.ndarray
+    sv: np.ndarray
+    gamma: np.ndarray
+    tlut: np.ndarray
+
+
+@dataclass
+class MoeBlock:
+    hidden: int
+    expert_hidden: int
+    experts: int
+    router: np.ndarray
+    shared_expert_gate: np.ndarray
+    shared_gate: NeView
+    shared_up: NeView
+    shared_down: NeView
+    expert_tlut: np.ndarray
+    ne_tlut: np.ndarray
+    trellis: list = field(default_factory=list)
+    su: list = field(default_factory=list)
+    sv: list = field(default_factory=list)
+    gamma: list = field(default_factory=list)
+
+    def shape(self, projection: int):
+        return (self.hidden, self.expert_hidden) if projection == 2 else (self.expert_hidden, self.hidden)
+
+    def expert(self, e: int, projection: int) -> ExpertView:
+        rows, columns = self.shape(projection)
+        return ExpertView(rows, columns, self.trellis[projection][e], self.su[projection][e],
+                          self.sv[projection][e], self.gamma[projection][e], self.expert_tlut)
+
+    def packed_bytes_per_expert(self) -> int:
+        """Packed weight bytes of one routed expert (three projections:
+        trellis + su + sv + wave gamma), 606,144 at the configured shapes."""
+        total = 0
+        for p in range(3):
+            rows, columns = self.shape(p)
+            total += (rows // 16) * (columns // 16) * 48 + 2 * (rows + columns) + 2 * (rows // 16 + columns // 16)
+        return total
+
+    def shared_bytes(self) -> int:
+        """Router + shared-expert gate (bf16) + shared NE expert bytes."""
+        ne = sum(m.trellis.nbytes + m.su.nbytes + m.sv.nbytes + 4
+                 for m in (self.shared_gate, self.shared_up, self.shared_down))
+        return self.router.nbytes + self.shared_expert_gate.nbytes + ne
+
+
+def _host(t: torch.Tensor, dtype) -> np.ndarray:
+    return t.cpu().numpy().view(dtype)
+
+
+def moe_block(seed: int, hidden: int = 2048, expert_hidden: int = 512, experts: int = 256,
+              scale_mu: float = -4.0, scale_sigma: float = 0.5, device: str = "cuda") -> MoeBlock:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    H, I, E = hidden, expert_hidden, experts
+
+    def words(count):
+        return _host(torch.randint(0, 65536, (count,), generator=g, device=device, dtype=torch.int32)
+                     .to(torch.int16), np.uint16)
+
+    def lognormal_f16(count):
+        v = torch.exp(scale_mu + scale_sigma * torch.randn(count, generator=g, device=device))
+        return _host(v.to(torch.float16).view(torch.int16), np.uint16)
+
+    def uniform(count):
+        return (torch.rand(count, generator=g, device=device) * 2 - 1).cpu().numpy().astype(np.float32)
+
+    def signs(count):
+        return (torch.randint(0, 2, (count,), generator=g, device=device, dtype=torch.int8) * 2 - 1).cpu().numpy()
+
+    router = _host((0.02 * torch.randn(E * H, generator=g, device=device)).to(torch.bfloat16).view(torch.int16),
+                   np.uint16).reshape(E, H)
+    shared_gate_row = _host((0.02 * torch.randn(H, generator=g, device=device)).to(torch.bfloat16)
+                            .view(torch.int16), np.uint16)
+    expert_tlut = uniform(32768 * 8)
+    ne_tlut = uniform(512 * 2)
+    block = MoeBlock(H, I, E, router, shared_gate_row, None, None, None, expert_tlut, ne_tlut)
+    for projection in range(3):
+        rows, columns = block.shape(projection)
+        tiles = (rows // 16) * (columns // 16)
+        block.trellis.append(words(E * tiles * 24).reshape(E, tiles * 24))
+        block.su.append(lognormal_f16(E * columns).reshape(E, columns))
+        block.sv.append(lognormal_f16(E * rows).reshape(E, rows))
+        block.gamma.append(lognormal_f16(E * (rows // 16 + columns // 16)).reshape(E, -1))
+    shared = []
+    for rows, columns in ((I, H), (I, H), (H, I)):
+        tiles = (rows // 16) * (columns // 16)
+        scale = float(torch.exp(scale_mu + scale_sigma * torch.randn(1, generator=g, device=device)).item())
+        shared.append(NeView(rows, columns, words(tiles * 64), signs(columns), signs(rows), scale, ne_tlut))
+    block.shared_gate, block.shared_up, block.shared_down = shared
+    return block
+
+
+def activations(seed: int, tokens: int, hidden: int, device: str = "cuda") -> torch.Tensor:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return torch.randn(tokens, hidden, generator=g, device=device, dtype=torch.float32)

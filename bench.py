@@ -1,0 +1,388 @@
+#!/usr/bin/env python
+"""Benchmark of the packed MoE block on B200: MoE-block tokens/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (one GPU): one Qwen3.5-MoE sparse block -- hidden 2048, 256 routed
+experts of intermediate 512 in the K=1.5 trellis codec, one shared NE expert,
+top-8 -- at prefill ubatch 512 with N(0,1) activations (near-uniform
+routing). A step is one pass of the block over one ubatch. Four distinct
+synthetic blocks (157 MB of packed weights each, more than the 126 MB L2)
+are used in turn, so no step finds its weights in L2.
+
+`value` is device time: K steps bracketed by a barrier and a synchronize,
+CUDA events on the stream the kernels run on, max over ranks, inputs already
+in HBM. `e2e` runs the same steps through the C ABI's host-pointer entry
+(adi_cuda_moe_forward_batch): pinned host inputs copied in, outputs and
+routes copied back, every step. `roofline` is the expert GEMM kernel (the
+dominant one): packed expert bytes it must stream per launch over its
+event-timed duration. `cpu_baseline` is the reference CPU implementation
+(built from its own sources into oracle/_ref) on this host's cores.
+
+With N > 1 under torchrun each rank runs its own block replica on its own
+tokens (weak scaling, no collective); expert parallelism is separate work.
+
+`--impl reference` times the reference CPU implementation on the same
+workload (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+os.environ.setdefault("ADI_THREADS", str(os.cpu_count() or 1))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "MoE-block tokens/s (ubatch 1/128/512) at 1/2/4/8 B200; % HBM/tensor roofline"
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+TRELLIS_BYTES = 4096 * 48  # one expert projection's trellis
+GAMMA_BYTES = 160 * 2
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=512)
+    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--no-baseline", action="store_true", help="skip the CPU baseline leg")
+    return ap.parse_args()
+
+
+def peaks():
+    if PEAKS_FILE.exists():
+        data = json.loads(PEAKS_FILE.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, value in zip(names, parts[5:9]):
+                if value.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "samples": len(sm), "power_w_max": max(power) if power else None, "reasons": sorted(reasons)}
+
+
+def setup_distributed():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        dist.barrier()
+
+
+def reference_forward_seconds(ref, block, x: np.ndarray, budget_s: float, max_calls: int):
+    """Times the reference's MoE block (restated moe_forward_batch glue over
+    its public kernels) on `x`; one untimed call first."""
+    ref.moe_forward(block, x)
+    times = []
+    start = time.perf_counter()
+    while len(times) < max_calls and (time.perf_counter() - start < budget_s or len(times) < 2):
+        t0 = time.perf_counter()
+        ref.moe_forward(block, x)
+        times.append(time.perf_counter() - t0)
+    return times
+
+
+def cpu_baseline(block, tokens: int, seed_input) -> dict:
+    sys.path.insert(0, str(ROOT / "oracle"))
+    from ffi import Reference, reference_available  # noqa: E402
+    if not reference_available():
+        return {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "reference",
+                "sample": "oracle/_ref not built"}
+    ref = Reference()
+    x = seed_input.cpu().numpy()
+    times = reference_forward_seconds(ref, block, x, budget_s=15.0, max_calls=30)
+    per = statistics.median(times)
+    return {"value": tokens / per, "unit": "tokens/s", "cores": int(ref.lib.ref_worker_threads()),
+            "kind": "reference", "isa": ref.isa(),
+            "sample": f"{len(times)} calls of the full {tokens}-token block after one warm call; median "
+                      f"{per * 1e3:.1f} ms/call"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    from adi_b200 import synthetic
+    sys.path.insert(0, str(ROOT / "oracle"))
+    from ffi import Reference, reference_available  # noqa: E402
+    base = {"metric": METRIC, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
+            "higher_is_better": True}
+    if not reference_available():
+        print(json.dumps({**base, "unavailable": "oracle/_ref/libadi_ref.so was not built"}), flush=True)
+        return
+    ref = Reference()
+    block = synthetic.moe_block(seed=0, device="cpu")
+    x = synthetic.activations(1000, args.tokens, block.hidden, device="cpu").numpy()
+    for _ in range(max(0, min(args.warmup, 3))):
+        ref.moe_forward(block, x)
+    # Each step is one full forward of the ubatch; the run stops early once
+    # it has used its time budget, and `steps` says how many were timed.
+    times = []
+    budget = 150.0
+    start = time.perf_counter()
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        ref.moe_forward(block, x)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - start > budget:
+            break
+    total = sum(times)
+    value = len(times) * args.tokens / total
+    cores = int(ref.lib.ref_worker_threads())
+    print(json.dumps({
+        **base, "value": value, "steps": len(times), "warmup": min(args.warmup, 3),
+        "ms_per_step": 1e3 * total / len(times), "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"MoE block, ubatch {args.tokens}, reference CPU path", "tokens_per_step": args.tokens,
+                   "hidden": block.hidden, "experts": block.experts, "top_k": 8},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "reference",
+                         "sample": f"{len(times)} full {args.tokens}-token forwards, ADI_THREADS={cores}, "
+                                   f"ISA {ref.isa()}"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    import adi_b200
+    from adi_b200 import synthetic
+    torch.cuda.set_device(local)
+    ctx = adi_b200.Context(local)
+    stream = torch.cuda.current_stream()
+    ctx.set_stream(stream.cuda_stream)
+    T, L = args.tokens, args.layers
+
+    blocks, handles = [], []
+    for layer in range(L):
+        block = synthetic.moe_block(seed=1000 * rank + layer, device=f"cuda:{local}")
+        handles.append(ctx.upload_moe_layer(block))
+        blocks.append(block if layer == 0 else None)
+        del block
+    H, E = blocks[0].hidden, blocks[0].experts
+    pool = 8
+    inputs = torch.stack([synthetic.activations(7 * rank + i, T, H, device=f"cuda:{local}") for i in range(pool)])
+    out = torch.empty(T, H, device=f"cuda:{local}")
+    re = torch.empty(T, 8, dtype=torch.int32, device=f"cuda:{local}")
+    rw = torch.empty(T, 8, device=f"cuda:{local}")
+
+    def step(k):
+        ctx.moe_forward_batch_device(handles[k % L], inputs[k % pool].data_ptr(), T, out.data_ptr(),
+                                     re.data_ptr(), rw.data_ptr())
+
+    # Experts each input batch touches (for the algorithmic byte count).
+    touched = []
+    for i in range(pool * L):
+        step(i)
+        touched.append(int(torch.unique(re).numel()))
+    torch.cuda.synchronize()
+    touched_per_step = {i: touched[i] for i in range(len(touched))}
+
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize()
+
+    ctx.reset_profile()
+    ctx.set_profiling(True)
+    launches0 = ctx.launch_count()
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    begin.record(stream)
+    for k in range(args.steps):
+        step(k)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clock_info = clocks.stop()
+    ctx.set_profiling(False)
+    launches = ctx.launch_count() - launches0
+    ms = begin.elapsed_time(end)
+    ms_max = max_over_ranks(ms, world)
+    stages = ctx.profile()
+    n_touched = [touched_per_step[k % (pool * L)] if (k % (pool * L)) in touched_per_step else touched[0]
+                 for k in range(args.steps)]
+    # touched[] was measured with step(i) for i in range(pool*L): step k uses
+    # layer k % L and input k % pool, the same pair as step k % (pool * L).
+
+    value = sum_over_ranks(args.steps * T, world) / (ms_max / 1e3)
+
+    # Roofline of the expert GEMM kernel (both of its launches per step).
+    gemm_ms = stages.get("expert_gemm_gate_up", (0, 0))[0] + stages.get("expert_gemm_down", (0, 0))[0]
+    gemm_launches = stages.get("expert_gemm_gate_up", (0, 0))[1] + stages.get("expert_gemm_down", (0, 0))[1]
+    gemm_bytes = sum(n * 3 * (TRELLIS_BYTES + GAMMA_BYTES) for n in n_touched)
+    hbm_peak, peak_kind = peaks()
+    achieved = (gemm_bytes / (gemm_ms / 1e3)) / 1e9 if gemm_ms > 0 else None
+    # Whole-block algorithmic bytes (router + shared + touched experts +
+    # activations in and out), for the block-level fraction.
+    block_bytes = [blocks[0].shared_bytes() + n * blocks[0].packed_bytes_per_expert() + T * H * 4 * 2
+                   for n in n_touched]
+    block_gbs = sum(block_bytes) / (ms / 1e3) / 1e9
+
+    # End to end through the host-pointer C ABI, pinned host buffers.
+    x_host = torch.empty(pool, T, H, dtype=torch.float32, pin_memory=True)
+    x_host.copy_(inputs.cpu())
+    y_host = torch.empty(T, H, dtype=torch.float32, pin_memory=True)
+    re_host = torch.empty(T, 8, dtype=torch.int32, pin_memory=True)
+    rw_host = torch.empty(T, 8, dtype=torch.float32, pin_memory=True)
+    f32p = C.POINTER(C.c_float)
+    u32p = C.POINTER(C.c_uint32)
+
+    def e2e_step(k):
+        status = ctx.lib.adi_cuda_moe_forward_batch(
+            ctx.ptr, handles[k % L].value, C.cast(x_host[k % pool].data_ptr(), f32p), T,
+            C.cast(y_host.data_ptr(), f32p), C.cast(re_host.data_ptr(), u32p), C.cast(rw_host.data_ptr(), f32p))
+        if status:
+            raise RuntimeError(adi_b200.last_error())
+
+    e2e_steps = max(1, min(args.steps, 200))
+    for k in range(min(args.warmup, 5)):
+        e2e_step(k)
+    barrier(world)
+    t0 = time.perf_counter()
+    for k in range(e2e_steps):
+        e2e_step(k)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    e2e_value = sum_over_ranks(e2e_steps * T, world) / e2e_s
+
+    # Smaller ubatches of the same block (decode and the smaller prefill).
+    sweep = {}
+    for tokens in (1, 128):
+        xs = inputs[0, :tokens].contiguous()
+        for _ in range(5):
+            ctx.moe_forward_batch_device(handles[0], xs.data_ptr(), tokens, out.data_ptr(), 0, 0)
+        steps = 200
+        b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b.record(stream)
+        for k in range(steps):
+            ctx.moe_forward_batch_device(handles[k % L], xs.data_ptr(), tokens, out.data_ptr(), 0, 0)
+        e.record(stream)
+        torch.cuda.synchronize()
+        sweep[f"ubatch_{tokens}"] = {"tokens_per_s": steps * tokens / (b.elapsed_time(e) / 1e3),
+                                     "ms_per_step": b.elapsed_time(e) / steps}
+
+    baseline = None
+    if rank == 0 and world == 1 and not args.no_baseline:
+        baseline = cpu_baseline(blocks[0], T, inputs[0])
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"C2: one MoE block, prefill ubatch {T}, "
+                                   + ("1 GPU" if world == 1 else f"{world} GPU replicas"),
+                       "tokens_per_step": T, "hidden": H, "experts": E, "expert_hidden": blocks[0].expert_hidden,
+                       "top_k": 8, "blocks_rotated": L,
+                       "l2": f"inputs larger than L2: {L} distinct blocks of "
+                             f"{(blocks[0].shared_bytes() + E * blocks[0].packed_bytes_per_expert()) / 1e6:.0f} MB rotated",
+                       "parallelism": "dp1" if world == 1 else f"replicas{world}"},
+            "roofline": {"bound": "hbm", "kernel": "expert_gemm_kernel",
+                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": (achieved / hbm_peak) if achieved else None, "peak_kind": peak_kind,
+                         "traffic": None,
+                         "bytes_per_launch": gemm_bytes / max(1, gemm_launches),
+                         "ms_per_launch": gemm_ms / max(1, gemm_launches)},
+            "block_hbm": {"achieved_gbs": block_gbs, "frac": block_gbs / hbm_peak,
+                          "bytes_per_step": sum(block_bytes) / len(block_bytes),
+                          "experts_touched_mean": sum(n_touched) / len(n_touched)},
+            "stages_ms_per_step": {k: v[0] / max(1, v[1]) for k, v in stages.items()},
+            "ubatch_sweep": sweep,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
+                    "d2h_bytes_per_step": T * H * 4 + T * 8 * 8, "steps": e2e_steps},
+            "gpu_launches": launches,
+            "clocks": clock_info,
+        }
+        if baseline is not None:
+            line["cpu_baseline"] = baseline
+        print(json.dumps(line), flush=True)
+    for h in handles:
+        h.release()
+    ctx.close()
+
+
+def main():
+    args = parse()
+    world, rank, local = setup_distributed()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,231 @@
+/* adi_cuda.h - C ABI of the B200 backend for ADI's packed-weight MoE path.
+ *
+ * The reference CPU runtime routes every packed projection through one
+ * function-pointer table, adi::Backend (include/adi/backend.hpp:10-23 of the
+ * reference), whose only instance is cpu_backend() (src/backend.cpp:11-26).
+ * This header is what a CUDA entry of that table calls: plain C, pointers and
+ * sizes only, int status returns. The matrix views mirror the reference's
+ * descriptor structs field for field, with each std::span replaced by a
+ * pointer whose length follows from rows and columns.
+ *
+ * Weights are uploaded once, byte for byte, and evaluated directly from the
+ * packed codes on the device; they are never decoded to a dense copy.
+ *
+ * Status codes: 0 ok; 1 invalid argument (where the reference throws
+ * std::invalid_argument, with the same message text available from
+ * adi_cuda_last_error); 2 CUDA error; 3 a bounded device wait timed out;
+ * 4 out of device memory.
+ *
+ * Threading: the reference calls its kernels concurrently from pool workers
+ * (src/executor.cpp:261-289, :1321-1371). Every call here takes the
+ * context's lock, so concurrent callers are safe and serialised on the
+ * context's stream. Host-pointer calls are synchronous like the reference's
+ * kernels; *_device calls are asynchronous on the context stream.
+ */
+#ifndef ADI_CUDA_H
+#define ADI_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ADI_CUDA_API __attribute__((visibility("default")))
+#else
+#define ADI_CUDA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    ADI_CUDA_OK = 0,
+    ADI_CUDA_INVALID_ARGUMENT = 1,
+    ADI_CUDA_DEVICE_ERROR = 2,
+    ADI_CUDA_TIMEOUT = 3,
+    ADI_CUDA_OUT_OF_MEMORY = 4,
+};
+
+typedef struct adi_cuda_context adi_cuda_context;
+typedef uint64_t adi_cuda_handle;
+
+/* MachExpertMatrix (include/adi/kernels.hpp:9-20): K=1.5 bits/weight expert
+ * trellis, 24 u16 words per 16x16 tile, f16 scale surfaces, f32 TLUT
+ * [32768][8]. The optional state-value / wave caches of the reference are
+ * derived data and are rebuilt on the device. */
+typedef struct {
+    uint32_t rows;
+    uint32_t columns;
+    const uint16_t *trellis;        /* [rows/16 * columns/16][24] */
+    const uint16_t *su_f16;         /* [columns] */
+    const uint16_t *sv_f16;         /* [rows] */
+    const uint16_t *wave_gamma_f16; /* [rows/16 + columns/16] */
+    const float *tlut;              /* [32768][8] */
+} adi_expert_matrix;
+
+/* MachNeMatrix (include/adi/kernels.hpp:42-52): K=4 non-expert trellis, 64
+ * words per tile, +-1 sign vectors, scalar weight scale, f32 TLUT [512][2]. */
+typedef struct {
+    uint32_t rows;
+    uint32_t columns;
+    const uint16_t *trellis; /* [rows/16 * columns/16][64] */
+    const int8_t *su;        /* [columns] */
+    const int8_t *sv;        /* [rows] */
+    float weight_scale;
+    const float *tlut;       /* [512][2] */
+} adi_ne_matrix;
+
+/* MachHeadChunk (include/adi/kernels.hpp:64-71): int5_g64 output head. */
+typedef struct {
+    uint32_t rows;
+    uint32_t columns;
+    const uint8_t *packed;           /* [rows][columns/8*5] */
+    const uint16_t *group_scale_f16; /* [rows][columns/64] */
+    const uint32_t *protected_rows;  /* [protected_count] */
+    uint32_t protected_count;
+    const uint16_t *protected_bf16;  /* [protected_count][columns] */
+} adi_head_chunk;
+
+/* Bf16Matrix (include/adi/kernels.hpp:73-77). */
+typedef struct {
+    uint32_t rows;
+    uint32_t columns;
+    const uint16_t *values; /* [rows][columns] */
+} adi_bf16_matrix;
+
+/* One sparse MoE block, the MoeDescriptor of the reference's LayerDescriptor
+ * (include/adi/model.hpp): router, shared-expert gate vector, shared NE
+ * SwiGLU expert, and experts*3 routed matrices ordered gate, up, down. All
+ * routed matrices must share one expert TLUT and all shared ones one NE TLUT. */
+typedef struct {
+    uint32_t hidden;
+    uint32_t expert_hidden;
+    uint32_t experts;
+    adi_bf16_matrix router;             /* [experts][hidden] */
+    adi_bf16_matrix shared_expert_gate; /* [1][hidden] */
+    adi_ne_matrix shared_gate;          /* [expert_hidden][hidden] */
+    adi_ne_matrix shared_up;            /* [expert_hidden][hidden] */
+    adi_ne_matrix shared_down;          /* [hidden][expert_hidden] */
+    const adi_expert_matrix *routed;    /* [experts * 3] */
+} adi_moe_layer;
+
+/* ---- context -------------------------------------------------------- */
+
+/* Creates a context on `device` (its own stream, scratch and codec tables). */
+ADI_CUDA_API int adi_cuda_init(int device, adi_cuda_context **context);
+ADI_CUDA_API int adi_cuda_shutdown(adi_cuda_context *context);
+/* Copies the calling thread's last error message; returns its full length. */
+ADI_CUDA_API size_t adi_cuda_last_error(char *buffer, size_t size);
+/* Runs the context on a caller's cudaStream_t (NULL: back to its own). */
+ADI_CUDA_API int adi_cuda_set_stream(adi_cuda_context *context, void *stream);
+ADI_CUDA_API int adi_cuda_synchronize(adi_cuda_context *context);
+/* Matmul arithmetic: 0 = CUDA-core fp32 throughout (parity 1e-3 rel L2);
+ * 1 = tensor-core operands where a path has them (parity 1e-2 rel L2). */
+ADI_CUDA_API int adi_cuda_set_precision(adi_cuda_context *context, int mode);
+/* Device kernels this context has launched so far (for launch accounting). */
+ADI_CUDA_API uint64_t adi_cuda_launch_count(const adi_cuda_context *context);
+
+/* Stage timing, the device counterpart of the reference's opt-in kernel
+ * profiling (include/adi/profiling.hpp, src/profiling_internal.hpp:15-48):
+ * while enabled, every stage of a call is bracketed by CUDA events on the
+ * stream it runs on. adi_cuda_profile_stage reads stage `index`'s name,
+ * accumulated milliseconds and bracket count (synchronising first); it
+ * returns 1 once `index` is past the last stage. adi_cuda_profile_reset
+ * clears the totals. */
+ADI_CUDA_API int adi_cuda_set_profiling(adi_cuda_context *context, int enable);
+ADI_CUDA_API int adi_cuda_profile_stage(adi_cuda_context *context, uint32_t index, char *name, size_t name_size,
+                                        double *milliseconds, uint64_t *count);
+ADI_CUDA_API int adi_cuda_profile_reset(adi_cuda_context *context);
+
+/* ---- weight upload (once per matrix, byte for byte) ------------------
+ * Replace the mmap'd views of MachModel::expert / non_expert / head_chunk
+ * (src/model.cpp:267-314, :367-438, :472-533) with device copies. */
+ADI_CUDA_API int adi_cuda_upload_expert(adi_cuda_context *context,
+                           const adi_expert_matrix *matrix,
+                           adi_cuda_handle *handle);
+ADI_CUDA_API int adi_cuda_upload_ne(adi_cuda_context *context, const adi_ne_matrix *matrix,
+                       adi_cuda_handle *handle);
+ADI_CUDA_API int adi_cuda_upload_head(adi_cuda_context *context, const adi_head_chunk *head,
+                         adi_cuda_handle *handle);
+ADI_CUDA_API int adi_cuda_upload_bf16(adi_cuda_context *context,
+                         const adi_bf16_matrix *matrix,
+                         adi_cuda_handle *handle);
+ADI_CUDA_API int adi_cuda_upload_moe_layer(adi_cuda_context *context,
+                              const adi_moe_layer *layer,
+                              adi_cuda_handle *handle);
+ADI_CUDA_API int adi_cuda_release(adi_cuda_context *context, adi_cuda_handle handle);
+
+/* ---- the Backend table entries, host pointers, synchronous ------------
+ * mach_expert_matvec/matmul   src/kernels.cpp:385-593
+ * mach_ne_matvec/matmul       src/kernels.cpp:595-800
+ * mach_head_matvec/matmul     src/kernels.cpp:847-979
+ * bf16_matvec/matmul          src/kernels.cpp:981-1050
+ * Inputs [batch][columns], outputs [batch][rows], row-major fp32. A batch of
+ * 1 is the matvec. */
+ADI_CUDA_API int adi_cuda_expert_matmul(adi_cuda_context *context, adi_cuda_handle matrix,
+                           const float *inputs, uint32_t batch, float *outputs);
+ADI_CUDA_API int adi_cuda_ne_matmul(adi_cuda_context *context, adi_cuda_handle matrix,
+                       const float *inputs, uint32_t batch, float *outputs);
+ADI_CUDA_API int adi_cuda_head_matmul(adi_cuda_context *context, adi_cuda_handle head,
+                         const float *inputs, uint32_t batch, float *outputs);
+ADI_CUDA_API int adi_cuda_bf16_matmul(adi_cuda_context *context, adi_cuda_handle matrix,
+                         const float *inputs, uint32_t batch, float *outputs);
+
+/* The block-level entry: moe_forward_batch (src/executor.cpp:1181-1453),
+ * and moe_forward (:242-330) at batch 1. Routes come back like
+ * MoeBatchScratch::routes: [batch][8] experts and renormalised weights, in
+ * top_experts order. Either route pointer may be NULL. */
+ADI_CUDA_API int adi_cuda_moe_forward_batch(adi_cuda_context *context,
+                               adi_cuda_handle layer, const float *inputs,
+                               uint32_t batch, float *outputs,
+                               uint32_t *route_experts, float *route_weights);
+
+/* ---- device-pointer variants (asynchronous on the context stream) ------ */
+ADI_CUDA_API int adi_cuda_expert_matmul_device(adi_cuda_context *context,
+                                  adi_cuda_handle matrix, const float *inputs,
+                                  uint32_t batch, float *outputs);
+ADI_CUDA_API int adi_cuda_ne_matmul_device(adi_cuda_context *context, adi_cuda_handle matrix,
+                              const float *inputs, uint32_t batch,
+                              float *outputs);
+ADI_CUDA_API int adi_cuda_head_matmul_device(adi_cuda_context *context,
+                                adi_cuda_handle head, const float *inputs,
+                                uint32_t batch, float *outputs);
+ADI_CUDA_API int adi_cuda_bf16_matmul_device(adi_cuda_context *context,
+                                adi_cuda_handle matrix, const float *inputs,
+                                uint32_t batch, float *outputs);
+ADI_CUDA_API int adi_cuda_moe_forward_batch_device(adi_cuda_context *context,
+                                      adi_cuda_handle layer,
+                                      const float *inputs, uint32_t batch,
+                                      float *outputs, uint32_t *route_experts,
+                                      float *route_weights);
+
+/* ---- codec and routing pieces, for bit-exact parity checks -------------
+ * Device decode of expert tiles into their 32 states each
+ * (src/expert_trellis.hpp:51-105), of NE tiles into 128 states
+ * (src/ne_trellis.hpp:28-97), and the state-value tables built on the device
+ * from a TLUT (src/codec_cache.cpp:17-83). Host pointers. */
+ADI_CUDA_API int adi_cuda_expert_states(adi_cuda_context *context, const uint16_t *words,
+                           uint32_t tiles, uint32_t *states);
+ADI_CUDA_API int adi_cuda_ne_states(adi_cuda_context *context, const uint16_t *words,
+                       uint32_t tiles, uint32_t *states);
+ADI_CUDA_API int adi_cuda_expert_state_values(adi_cuda_context *context, const float *tlut,
+                                 float *values);
+ADI_CUDA_API int adi_cuda_ne_state_values(adi_cuda_context *context, const float *tlut,
+                             float *values);
+/* top_experts (src/executor.cpp:193-229) over [tokens][experts] logits. */
+ADI_CUDA_API int adi_cuda_top_experts(adi_cuda_context *context, const float *logits,
+                         uint32_t tokens, uint32_t experts,
+                         uint32_t *route_experts, float *route_weights);
+/* detail::hadamard_transform (src/simd.cpp:48-63) on [count][n] rows. */
+ADI_CUDA_API int adi_cuda_hadamard(adi_cuda_context *context, float *values, uint32_t count,
+                      uint32_t n);
+/* rms_norm (src/kernels.cpp:1052-1073) on [count][n] rows. */
+ADI_CUDA_API int adi_cuda_rms_norm(adi_cuda_context *context, const float *inputs,
+                      const uint16_t *weight_bf16, uint32_t count, uint32_t n,
+                      float weight_offset, float epsilon, float *outputs);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ADI_CUDA_H */

@@ -190,10 +190,11 @@ class MoeLayer:
 
 
 def moe_layer(seed: int = 0, hidden: int = 2048, expert_hidden: int = 512, experts: int = 256,
-              scale_mu: float = -4.0, scale_sigma: float = 0.5) -> MoeLayer:
+              scale_mu: float = -4.0, scale_sigma: float = 0.5, shared_mu=None) -> MoeLayer:
     """The configured block: trellis words from splitmix64(seed); every other
     tensor class from its own stream seeded seed + class, so the words alone
-    match a plain seed-`seed` stream."""
+    match a plain seed-`seed` stream. `shared_mu` overrides the log-normal
+    mean of the shared expert's weight scales (default: `scale_mu`)."""
     words = SplitMix64(seed)
     scales = SplitMix64(seed + 1)
     router_rng = SplitMix64(seed + 2)
@@ -219,7 +220,8 @@ def moe_layer(seed: int = 0, hidden: int = 2048, expert_hidden: int = 512, exper
         trellis = shared.words(tiles * 64)
         su = shared.signs(columns)
         sv = shared.signs(rows)
-        weight_scale = float(np.float32(np.exp(scale_mu + scale_sigma * shared.normals(1)[0])))
+        mu = scale_mu if shared_mu is None else shared_mu
+        weight_scale = float(np.float32(np.exp(mu + scale_sigma * shared.normals(1)[0])))
         ne.append(NeMatrix(rows, columns, trellis, su, sv, weight_scale, ne_tlut))
     layer.shared_gate, layer.shared_up, layer.shared_down = ne
     return layer

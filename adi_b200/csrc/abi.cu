@@ -223,6 +223,7 @@ struct adi_cuda_context {
     std::map<uint64_t, std::unique_ptr<HeadDev>> heads;
     std::map<uint64_t, std::unique_ptr<Bf16Dev>> bf16s;
     std::map<uint64_t, std::unique_ptr<MoeDev>> moes;
+    uint32_t *error_word = nullptr;  // device word kernels flag timeouts in
     Profiler profiler;
     void stage(int st) { profiler.begin(st, stream); }
     void stage_end() { profiler.end(stream); }
@@ -240,6 +241,17 @@ struct adi_cuda_context {
     void after_launch(uint64_t n) {
         launches += n;
         check(cudaGetLastError(), "kernel launch");
+    }
+
+    // Synchronises the stream, then reports (and clears) a kernel timeout.
+    void finish() {
+        check(cudaStreamSynchronize(stream), "synchronize");
+        uint32_t flags = 0;
+        check(cudaMemcpy(&flags, error_word, sizeof flags, cudaMemcpyDeviceToHost), "read error word");
+        if (flags) {
+            check(cudaMemset(error_word, 0, sizeof flags), "clear error word");
+            throw Status(ADI_CUDA_TIMEOUT, "a bounded device wait timed out; results are invalid");
+        }
     }
 
     uint64_t new_handle(Kind kind) { return (next_handle++ << 4) | kind; }
@@ -296,6 +308,9 @@ auto &lookup(Map &map, adi_cuda_handle h, const char *what) {
 void validate_expert_shape(uint32_t rows, uint32_t cols) {
     if (!pow2(rows) || !pow2(cols) || rows % 16 || cols % 16)
         invalid("Mach expert dimensions must be tiled powers of two");
+    // One tile row of words must fit a 24 KiB pipeline slab; the input
+    // transform keeps a row in shared memory.
+    if (cols > 8192 || rows > 8192) invalid("Mach expert dimensions above 8192 are not supported");
 }
 
 void validate_ne_shape(uint32_t rows, uint32_t cols) {
@@ -340,6 +355,14 @@ int gemm_grid(adi_cuda_context *c, uint64_t items, int per_item) {
 
 uint32_t row_blocks(uint32_t rows) { return (rows / 16 + kRowTiles - 1) / kRowTiles; }
 
+// Positions per expert work item: the next power of two of the expected
+// positions per expert, at most 8.
+uint32_t tokens_per_item(uint64_t expected) {
+    uint32_t n = 1;
+    while (n < expected && n < 8) n <<= 1;
+    return n;
+}
+
 // ---- standalone matmuls on device pointers -------------------------------
 
 void expert_matmul_dev(adi_cuda_context *c, ExpertDev &m, const float *in, uint32_t batch, float *out) {
@@ -361,9 +384,13 @@ void expert_matmul_dev(adi_cuda_context *c, ExpertDev &m, const float *in, uint3
     gp.job[0] = ExpertJob{m.trellis->as<uint32_t>(), m.gamma->as<uint16_t>(), xp, acc, m.rows, m.cols, 0, 0,
                           size_t(batch) * m.rows};
     gp.job[1] = gp.job[0];
-    gp.work = WorkList{nullptr, nullptr, batch, 1};
+    gp.tokens_per_item = tokens_per_item(batch);
+    gp.rows_per_item = expert_rows_per_item(m.cols);
+    gp.work = WorkList{nullptr, nullptr, batch, 1, gp.tokens_per_item};
     gp.table = m.codec->half_tables.as<uint2>();
-    const uint64_t items = uint64_t((batch + kMaxTokens - 1) / kMaxTokens) * row_blocks(m.rows);
+    gp.error = c->error_word;
+    const uint64_t items = uint64_t((batch + gp.tokens_per_item - 1) / gp.tokens_per_item) *
+                           ((m.rows / 16 + gp.rows_per_item - 1) / gp.rows_per_item);
     launch_expert_gemm(gp, gemm_grid(c, items, 2), c->stream);
     launch_finalize(acc, acc + size_t(batch) * m.rows, m.sv->ptr, 1, batch, m.rows, transform_scale(m.rows), out,
                     c->stream);
@@ -389,7 +416,7 @@ void ne_matmul_dev(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batc
     NeGemmParams gp{};
     gp.job[0] = NeJob{m.trellis->as<uint32_t>(), xp, acc, m.rows, m.cols, m.weight_scale};
     gp.job[1] = gp.job[0];
-    gp.work = WorkList{nullptr, nullptr, batch, 1};
+    gp.work = WorkList{nullptr, nullptr, batch, 1, kMaxTokens};
     gp.table = m.codec->table.as<float2>();
     const uint64_t items = uint64_t((batch + kMaxTokens - 1) / kMaxTokens) * row_blocks(m.rows);
     launch_ne_gemm(gp, gemm_grid(c, items, 1), c->stream);
@@ -457,9 +484,12 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     rp.grouped = c->buffer<uint32_t>("moe_grouped", P);
     rp.pos_expert = c->buffer<uint32_t>("moe_pos_expert", P);
     rp.route_to_grouped = c->buffer<uint32_t>("moe_r2g", P);
-    rp.row_blocks_gate_up = row_blocks(I);
-    rp.row_blocks_down = row_blocks(H);
-    const size_t max_chunks = P / kMaxTokens + E;
+    const uint32_t nt = tokens_per_item((uint64_t(T) * 8 + E - 1) / E);
+    const uint32_t rb_gate_up = expert_rows_per_item(H), rb_down = expert_rows_per_item(I);
+    rp.chunk = nt;
+    rp.row_blocks_gate_up = (I / 16 + rb_gate_up - 1) / rb_gate_up;
+    rp.row_blocks_down = (H / 16 + rb_down - 1) / rb_down;
+    const size_t max_chunks = P / nt + E;
     rp.items_gate_up = c->buffer<uint4>("moe_items_gu", max_chunks * 2 * rp.row_blocks_gate_up);
     rp.items_down = c->buffer<uint4>("moe_items_d", max_chunks * rp.row_blocks_down);
     uint32_t *counts2 = c->buffer<uint32_t>("moe_item_counts", 2);
@@ -497,8 +527,11 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
                           tiles_gu * 12, I / 16 + H / 16, P * I};
     gp.job[1] = ExpertJob{L.trellis[1]->as<uint32_t>(), L.gamma[1]->as<uint16_t>(), xu, acc_u, I, H,
                           tiles_gu * 12, I / 16 + H / 16, P * I};
-    gp.work = WorkList{rp.items_gate_up, rp.count_gate_up, 0, 0};
+    gp.work = WorkList{rp.items_gate_up, rp.count_gate_up, 0, 0, nt};
     gp.table = L.codec->half_tables.as<uint2>();
+    gp.rows_per_item = rb_gate_up;
+    gp.tokens_per_item = nt;
+    gp.error = c->error_word;
     c->stage(kStageExpertGateUp);
     launch_expert_gemm(gp, c->sms, s);
     c->stage_end();
@@ -527,8 +560,11 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     dp.job[0] = ExpertJob{L.trellis[2]->as<uint32_t>(), L.gamma[2]->as<uint16_t>(), xd, acc_d, H, I,
                           tiles_gu * 12, I / 16 + H / 16, P * H};
     dp.job[1] = dp.job[0];
-    dp.work = WorkList{rp.items_down, rp.count_down, 0, 0};
+    dp.work = WorkList{rp.items_down, rp.count_down, 0, 0, nt};
     dp.table = gp.table;
+    dp.rows_per_item = rb_down;
+    dp.tokens_per_item = nt;
+    dp.error = c->error_word;
     c->stage(kStageExpertDown);
     launch_expert_gemm(dp, c->sms, s);
     c->stage_end();
@@ -554,7 +590,7 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     NeGemmParams np{};
     np.job[0] = NeJob{L.shared[0].trellis->as<uint32_t>(), sxg, sacc_g, I, H, L.shared[0].weight_scale};
     np.job[1] = NeJob{L.shared[1].trellis->as<uint32_t>(), sxu, sacc_u, I, H, L.shared[1].weight_scale};
-    np.work = WorkList{nullptr, nullptr, T, 2};
+    np.work = WorkList{nullptr, nullptr, T, 2, kMaxTokens};
     np.table = L.shared[0].codec->table.as<float2>();
     const uint64_t ne_items = uint64_t((T + kMaxTokens - 1) / kMaxTokens) * 2 * row_blocks(I);
     launch_ne_gemm(np, gemm_grid(c, ne_items, 1), s);
@@ -578,7 +614,7 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     NeGemmParams nd{};
     nd.job[0] = NeJob{L.shared[2].trellis->as<uint32_t>(), sxd, sacc_d, H, I, L.shared[2].weight_scale};
     nd.job[1] = nd.job[0];
-    nd.work = WorkList{nullptr, nullptr, T, 1};
+    nd.work = WorkList{nullptr, nullptr, T, 1, kMaxTokens};
     nd.table = np.table;
     const uint64_t nd_items = uint64_t((T + kMaxTokens - 1) / kMaxTokens) * row_blocks(H);
     launch_ne_gemm(nd, gemm_grid(c, nd_items, 1), s);
@@ -616,7 +652,7 @@ void host_call(adi_cuda_context *c, const float *in, size_t in_count, float *out
     check(cudaMemcpyAsync(din, in, in_count * sizeof(float), cudaMemcpyHostToDevice, c->stream), "H2D");
     run(din, dout);
     check(cudaMemcpyAsync(out, dout, out_count * sizeof(float), cudaMemcpyDeviceToHost, c->stream), "D2H");
-    check(cudaStreamSynchronize(c->stream), "synchronize");
+    c->finish();
 }
 
 }  // namespace
@@ -635,6 +671,8 @@ int adi_cuda_init(int device, adi_cuda_context **out) {
         check(cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device), "SM count");
         check(cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking), "cudaStreamCreate");
         c->stream = c->own_stream;
+        check(cudaMalloc(&c->error_word, sizeof(uint32_t)), "cudaMalloc");
+        check(cudaMemset(c->error_word, 0, sizeof(uint32_t)), "cudaMemset");
         *out = c.release();
     });
 }
@@ -645,7 +683,9 @@ int adi_cuda_shutdown(adi_cuda_context *c) {
         use_device(c);
         cudaStreamSynchronize(c->stream);
         cudaStream_t own = c->own_stream;
+        uint32_t *error_word = c->error_word;
         delete c;
+        if (error_word) cudaFree(error_word);
         if (own) cudaStreamDestroy(own);
     });
 }
@@ -670,7 +710,7 @@ int adi_cuda_synchronize(adi_cuda_context *c) {
     return guarded([&] {
         std::lock_guard<std::mutex> g(require(c)->lock);
         use_device(c);
-        check(cudaStreamSynchronize(c->stream), "synchronize");
+        c->finish();
     });
 }
 

@@ -9,6 +9,7 @@
 // partials are summed before the output transform.
 #include "codec.cuh"
 #include "kernels.cuh"
+#include "pipeline.cuh"
 
 #include <cuda_bf16.h>
 
@@ -203,7 +204,7 @@ struct Item {
 
 __device__ __forceinline__ uint32_t work_count(const WorkList &w, uint32_t row_blocks) {
     if (w.items) return *w.item_count;
-    return ((w.dense_tokens + kMaxTokens - 1) / kMaxTokens) * w.dense_jobs * row_blocks;
+    return ((w.dense_tokens + w.chunk - 1) / w.chunk) * w.dense_jobs * row_blocks;
 }
 
 __device__ __forceinline__ Item work_item(const WorkList &w, uint32_t i, uint32_t row_blocks) {
@@ -214,27 +215,53 @@ __device__ __forceinline__ Item work_item(const WorkList &w, uint32_t i, uint32_
     const uint32_t rb = i % row_blocks;
     const uint32_t job = (i / row_blocks) % w.dense_jobs;
     const uint32_t chunk = i / (row_blocks * w.dense_jobs);
-    const uint32_t pos0 = chunk * kMaxTokens;
-    return Item{0u, job, rb, pos0, min((uint32_t)kMaxTokens, w.dense_tokens - pos0)};
+    const uint32_t pos0 = chunk * w.chunk;
+    return Item{0u, job, rb, pos0, min(w.chunk, w.dense_tokens - pos0)};
 }
 
 // ---------------------------------------------------------------------------
 // Expert streaming GEMM on CUDA cores (fp32 accumulate)
 //
-// Persistent: one CTA per SM, CTA parity selects the value half it owns. A
-// work item is (expert, projection, block of 4 tile rows, up to 8 positions).
-// Warp w walks tile columns w, w+8, ...; inside a tile, lane i owns state i
-// (tile row i>>1, columns (i&1)*8 + 4*half .. +3), so its inputs stay in
-// registers across the item's tile rows. Per tile the warp loads the 48-byte
-// word stream once (12 lanes), shuffles each lane the two words holding its
-// window, gathers one 8-byte value half from shared memory and applies it to
-// every position. Partial sums reduce over lane pairs and warps at the end
-// of the item.
+// Persistent: one CTA per SM; CTA parity selects the value half it keeps in
+// shared memory (128 KiB). A work item is (expert, projection, block of up
+// to 4 tile rows, up to NT positions); both CTAs of a pair take the same
+// items, each producing the partial sum of its half's columns.
+//
+// Warp 0 is the producer: one lane streams each item's trellis slab (its
+// tile rows are contiguous, at most 24 KiB) into a 3-deep shared-memory ring
+// with cp.async.bulk, each slot guarded by a full/empty mbarrier pair. The CW
+// consumer warps decode from shared memory: warp w walks tile columns w,
+// w+CW, ...; inside a tile lane i owns state i (tile row i>>1, columns
+// (i&1)*8 + 4*half .. +3), gathers one 8-byte value half from the table and
+// applies it to every position, its inputs held in registers across the
+// item's tile rows (and the next column's prefetched). Row partials reduce
+// over lane pairs and consumer warps at the end of the item.
+//
+// Waits are bounded (pipeline.cuh). A warp whose wait expires keeps walking
+// the item list without touching data, so named barriers and the empty
+// slots still complete and the launch drains; the host sees the error word.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kGemmThreads, 1) expert_gemm_kernel(const ExpertGemmParams p) {
-    extern __shared__ __align__(16) uint8_t smem[];
+constexpr uint32_t kSlabBytes = 24576;
+constexpr uint32_t kStages = 3;
+
+template <int NT, int CW>
+struct ExpertStreamSmem {
+    static constexpr size_t table = kExpertTableRows * sizeof(uint2);
+    static constexpr size_t ring = size_t(kStages) * kSlabBytes;
+    static constexpr size_t red = size_t(CW) * kRowTiles * 16 * NT * sizeof(float);
+    static constexpr size_t bars = 2 * kStages * sizeof(uint64_t);
+    static constexpr size_t total = table + ring + red + bars;
+};
+
+template <int NT, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32, 1) expert_stream_kernel(const ExpertGemmParams p) {
+    using L = ExpertStreamSmem<NT, CW>;
+    extern __shared__ __align__(128) uint8_t smem[];
     uint2 *table = reinterpret_cast<uint2 *>(smem);
-    float *red = reinterpret_cast<float *>(smem + kExpertTableRows * sizeof(uint2));
+    uint8_t *ring = smem + L::table;
+    float *red = reinterpret_cast<float *>(smem + L::table + L::ring);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::table + L::ring + L::red);
+    uint64_t *empty = full + kStages;
     const uint32_t half = blockIdx.x & 1u;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
 
@@ -243,95 +270,167 @@ __global__ void __launch_bounds__(kGemmThreads, 1) expert_gemm_kernel(const Expe
         uint4 *dst = reinterpret_cast<uint4 *>(table);
         for (uint32_t i = threadIdx.x; i < kExpertTableRows / 2; i += blockDim.x) dst[i] = src[i];
     }
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], CW);
+        }
+        fence_barrier_init();
+    }
     __syncthreads();
 
-    const uint32_t rb0 = (p.job[0].rows / 16 + kRowTiles - 1) / kRowTiles;
+    const uint32_t rb_rows = p.rows_per_item;
+    const uint32_t rb0 = (p.job[0].rows / 16 + rb_rows - 1) / rb_rows;
     const uint32_t n_items = work_count(p.work, rb0);
+    const uint32_t pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t slot = 0, phase = 0, issued = 0;
+            for (uint32_t i = pair; i < n_items; i += pairs) {
+                const Item it = work_item(p.work, i, rb0);
+                const ExpertJob J = it.job ? p.job[1] : p.job[0];
+                const uint32_t TC = J.cols / 16, TR = J.rows / 16;
+                const uint32_t tr0 = it.row_block * rb_rows;
+                const uint32_t rows = min(rb_rows, TR - tr0);
+                const uint32_t *src = J.trellis + (size_t)it.expert * J.expert_stride32 +
+                                      (size_t)tr0 * TC * kExpertU32PerTile;
+                if (!mbar_wait(&empty[slot], phase ^ 1u, p.error)) break;
+                const uint32_t bytes = rows * TC * kExpertWordsPerTile * 2;
+                mbar_arrive_expect_tx(&full[slot], bytes);
+                bulk_load(ring + slot * kSlabBytes, src, bytes, &full[slot]);
+                ++issued;
+                if (++slot == kStages) {
+                    slot = 0;
+                    phase ^= 1u;
+                }
+            }
+            // Leave no copy in flight into this CTA's shared memory: wait for
+            // the last slots issued to land (they complete on their own).
+            for (uint32_t k = 0; k < min(issued, kStages); ++k) {
+                slot = slot == 0 ? kStages - 1 : slot - 1;
+                if (slot == kStages - 1) phase ^= 1u;
+                mbar_wait(&full[slot], phase, p.error);
+            }
+        }
+        return;
+    }
+
+    const uint32_t cw = warp - 1;
     const uint32_t q = (lane * 12u) >> 5;
     const uint32_t q1 = q + 1u == kExpertU32PerTile ? 0u : q + 1u;
-
-    for (uint32_t item_index = blockIdx.x >> 1; item_index < n_items; item_index += gridDim.x >> 1) {
+    uint32_t slot = 0, phase = 0;
+    bool failed = false;
+    for (uint32_t item_index = pair; item_index < n_items; item_index += pairs) {
         const Item it = work_item(p.work, item_index, rb0);
         const ExpertJob J = it.job ? p.job[1] : p.job[0];
         const uint32_t TC = J.cols / 16, TR = J.rows / 16;
-        const uint32_t *tiles = J.trellis + (size_t)it.expert * J.expert_stride32;
+        const uint32_t tr0 = it.row_block * rb_rows;
+        const uint32_t rows = min(rb_rows, TR - tr0);
         const uint16_t *gam = J.gamma + (size_t)it.expert * J.gamma_stride;
         const uint32_t n = it.count;
 
-        float acc[kRowTiles][kMaxTokens];
+        float acc[kRowTiles][NT];
 #pragma unroll
         for (int r = 0; r < kRowTiles; ++r)
 #pragma unroll
-            for (int t = 0; t < kMaxTokens; ++t) acc[r][t] = 0.0f;
+            for (int t = 0; t < NT; ++t) acc[r][t] = 0.0f;
 
-        for (uint32_t tc = warp; tc < TC; tc += kGemmWarps) {
-            float4 xv[kMaxTokens];
-            const uint32_t col = tc * 16 + (lane & 1u) * 8 + half * 4;
+        if (!failed) failed = !mbar_wait(&full[slot], phase, p.error);
+        if (!failed) {
+            const uint32_t *words = reinterpret_cast<const uint32_t *>(ring + slot * kSlabBytes);
+            const float *xrow = J.x + (size_t)it.pos0 * J.cols + (lane & 1u) * 8 + half * 4;
+            float4 xv[NT], xn[NT];
+            uint32_t tc = cw;
 #pragma unroll
-            for (int t = 0; t < kMaxTokens; ++t)
-                xv[t] = (uint32_t)t < n ? __ldg(reinterpret_cast<const float4 *>(
-                                              J.x + (size_t)(it.pos0 + t) * J.cols + col))
-                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int t = 0; t < NT; ++t)
+                xn[t] = ((uint32_t)t < n && tc < TC)
+                            ? __ldg(reinterpret_cast<const float4 *>(xrow + (size_t)t * J.cols + tc * 16))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (; tc < TC; tc += CW) {
 #pragma unroll
-            for (int r = 0; r < kRowTiles; ++r) {
-                const uint32_t tr = it.row_block * kRowTiles + r;
-                if (tr >= TR) break;
-                const uint32_t *tw = tiles + (size_t)(tr * TC + tc) * kExpertU32PerTile;
-                const uint32_t w = lane < kExpertU32PerTile ? __ldg(tw + lane) : 0u;
-                const uint32_t hi = stream_order(__shfl_sync(0xffffffffu, w, q));
-                const uint32_t lo = stream_order(__shfl_sync(0xffffffffu, w, q1));
-                const uint32_t state = expert_window(hi, lo, lane);
-                const uint32_t prod = state_product(state);
-                uint2 raw = table[expert_table_index(prod)];
-                if (half == 0) raw.x ^= expert_negative(prod) << 15;
-                const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
-                const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
-                const float g = f16_bits_to_f32(__ldg(gam + wave_index(TR, TC, tr + tc)));
+                for (int t = 0; t < NT; ++t) xv[t] = xn[t];
+                const uint32_t next = tc + CW;
 #pragma unroll
-                for (int t = 0; t < kMaxTokens; ++t) {
-                    if ((uint32_t)t < n) {
-                        float part = a.x * xv[t].x;
-                        part = fmaf(a.y, xv[t].y, part);
-                        part = fmaf(b.x, xv[t].z, part);
-                        part = fmaf(b.y, xv[t].w, part);
-                        acc[r][t] = fmaf(part, g, acc[r][t]);
+                for (int t = 0; t < NT; ++t)
+                    xn[t] = ((uint32_t)t < n && next < TC)
+                                ? __ldg(reinterpret_cast<const float4 *>(xrow + (size_t)t * J.cols + next * 16))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int r = 0; r < kRowTiles; ++r) {
+                    if ((uint32_t)r >= rows) break;
+                    const uint32_t *tw = words + (r * TC + tc) * kExpertU32PerTile;
+                    const uint32_t w = lane < kExpertU32PerTile ? tw[lane] : 0u;
+                    const uint32_t hi = stream_order(__shfl_sync(0xffffffffu, w, q));
+                    const uint32_t lo = stream_order(__shfl_sync(0xffffffffu, w, q1));
+                    const uint32_t state = expert_window(hi, lo, lane);
+                    const uint32_t prod = state_product(state);
+                    uint2 raw = table[expert_table_index(prod)];
+                    if (half == 0) raw.x ^= expert_negative(prod) << 15;
+                    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+                    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+                    const float g = f16_bits_to_f32(__ldg(gam + wave_index(TR, TC, tr0 + r + tc)));
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) {
+                        if ((uint32_t)t < n) {
+                            float part = a.x * xv[t].x;
+                            part = fmaf(a.y, xv[t].y, part);
+                            part = fmaf(b.x, xv[t].z, part);
+                            part = fmaf(b.y, xv[t].w, part);
+                            acc[r][t] = fmaf(part, g, acc[r][t]);
+                        }
                     }
                 }
             }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (++slot == kStages) {
+            slot = 0;
+            phase ^= 1u;
+        }
 
 #pragma unroll
         for (int r = 0; r < kRowTiles; ++r)
 #pragma unroll
-            for (int t = 0; t < kMaxTokens; ++t) acc[r][t] += __shfl_xor_sync(0xffffffffu, acc[r][t], 1);
+            for (int t = 0; t < NT; ++t) acc[r][t] += __shfl_xor_sync(0xffffffffu, acc[r][t], 1);
         if ((lane & 1u) == 0) {
 #pragma unroll
             for (int r = 0; r < kRowTiles; ++r)
 #pragma unroll
-                for (int t = 0; t < kMaxTokens; ++t)
-                    red[((warp * kRowTiles + r) * 16 + (lane >> 1)) * kMaxTokens + t] = acc[r][t];
+                for (int t = 0; t < NT; ++t) red[((cw * kRowTiles + r) * 16 + (lane >> 1)) * NT + t] = acc[r][t];
         }
-        __syncthreads();
-        const uint32_t rows_here = min((uint32_t)kRowTiles, TR - it.row_block * kRowTiles) * 16;
-        for (uint32_t idx = threadIdx.x; idx < rows_here * n; idx += blockDim.x) {
+        named_sync(1, CW * 32);
+        const uint32_t rows_here = rows * 16;
+        for (uint32_t idx = cw * 32 + lane; idx < rows_here * n; idx += CW * 32) {
             const uint32_t t = idx / rows_here, row = idx % rows_here;
             float sum = 0.0f;
 #pragma unroll
-            for (int w = 0; w < kGemmWarps; ++w) sum += red[((w * kRowTiles) * 16 + row) * kMaxTokens + t];
-            J.acc[half * J.half_stride + (size_t)(it.pos0 + t) * J.rows + it.row_block * kRowTiles * 16 + row] = sum;
+            for (int w = 0; w < CW; ++w) sum += red[((w * kRowTiles) * 16 + row) * NT + t];
+            J.acc[half * J.half_stride + (size_t)(it.pos0 + t) * J.rows + tr0 * 16 + row] = sum;
         }
-        __syncthreads();
+        named_sync(1, CW * 32);
     }
 }
 
-void launch_expert_gemm(const ExpertGemmParams &p, int grid, cudaStream_t s) {
+template <int NT, int CW>
+static void launch_expert_stream(const ExpertGemmParams &p, int grid, cudaStream_t s) {
     static bool configured = false;
+    const size_t bytes = ExpertStreamSmem<NT, CW>::total;
     if (!configured) {
-        cudaFuncSetAttribute(expert_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kExpertGemmSmem);
+        cudaFuncSetAttribute(expert_stream_kernel<NT, CW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
         configured = true;
     }
-    expert_gemm_kernel<<<grid & ~1, kGemmThreads, kExpertGemmSmem, s>>>(p);
+    expert_stream_kernel<NT, CW><<<grid & ~1, (CW + 1) * 32, bytes, s>>>(p);
+}
+
+void launch_expert_gemm(const ExpertGemmParams &p, int grid, cudaStream_t s) {
+    switch (p.tokens_per_item) {
+        case 1: launch_expert_stream<1, 16>(p, grid, s); break;
+        case 2: launch_expert_stream<2, 16>(p, grid, s); break;
+        case 4: launch_expert_stream<4, 16>(p, grid, s); break;
+        default: launch_expert_stream<8, 8>(p, grid, s); break;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -344,7 +443,7 @@ void launch_expert_gemm(const ExpertGemmParams &p, int grid, cudaStream_t s) {
 // u32 words L and L+1 of the tile's 128-byte stream.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kGemmThreads, 1) ne_gemm_kernel(const NeGemmParams p) {
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem[];
     float2 *table = reinterpret_cast<float2 *>(smem);
     float *red = reinterpret_cast<float *>(smem + kNeTableRows * kNeTableCopies * sizeof(float2));
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
@@ -607,7 +706,7 @@ __global__ void route_scan_kernel(RouteParams p) {
     __shared__ uint32_t chunk_scan[1024];
     const uint32_t e = threadIdx.x;
     const uint32_t count = e < p.experts ? p.counts[e] : 0u;
-    const uint32_t chunks = (count + kMaxTokens - 1) / kMaxTokens;
+    const uint32_t chunks = (count + p.chunk - 1) / p.chunk;
     scan[e] = count;
     chunk_scan[e] = chunks;
     __syncthreads();
@@ -625,8 +724,8 @@ __global__ void route_scan_kernel(RouteParams p) {
         p.offsets[e] = offset;
         for (uint32_t i = 0; i < count; ++i) p.pos_expert[offset + i] = e;
         for (uint32_t c = 0; c < chunks; ++c) {
-            const uint32_t pos0 = offset + c * kMaxTokens;
-            const uint32_t n = min((uint32_t)kMaxTokens, count - c * kMaxTokens);
+            const uint32_t pos0 = offset + c * p.chunk;
+            const uint32_t n = min(p.chunk, count - c * p.chunk);
             for (uint32_t j = 0; j < 2; ++j)
                 for (uint32_t rb = 0; rb < p.row_blocks_gate_up; ++rb)
                     p.items_gate_up[((chunk_offset + c) * 2 + j) * p.row_blocks_gate_up + rb] =

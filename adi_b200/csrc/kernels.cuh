@@ -42,13 +42,25 @@ struct WorkList {
     const uint32_t *item_count;
     uint32_t dense_tokens;
     uint32_t dense_jobs;
+    uint32_t chunk;  // positions per dense item
 };
 
 struct ExpertGemmParams {
     ExpertJob job[2];
     WorkList work;
-    const uint2 *table;  // [2][16384] value halves, 4 x f16 each
+    const uint2 *table;       // [2][16384] value halves, 4 x f16 each
+    uint32_t rows_per_item;   // tile rows per work item (1..kRowTiles)
+    uint32_t tokens_per_item; // 1, 2, 4 or 8: selects the kernel instance
+    uint32_t *error;          // device error word (timeouts)
 };
+
+// Tile rows per expert work item: as many as kRowTiles whose words fit the
+// 24 KiB pipeline slab.
+inline uint32_t expert_rows_per_item(uint32_t cols) {
+    const uint32_t per_row = (cols / 16) * 48;
+    uint32_t rows = 24576 / per_row;
+    return rows < 1 ? 1 : (rows > (uint32_t)kRowTiles ? (uint32_t)kRowTiles : rows);
+}
 
 struct NeGemmParams {
     NeJob job[2];
@@ -111,6 +123,7 @@ struct RouteParams {
     uint32_t *grouped;      // [8T] token of each position
     uint32_t *pos_expert;   // [8T]
     uint32_t *route_to_grouped;  // [8T]
+    uint32_t chunk;         // positions per work item (1, 2, 4 or 8)
     uint4 *items_gate_up;   // work list for the gate/up launch
     uint32_t *count_gate_up;
     uint32_t row_blocks_gate_up;

@@ -1,0 +1,90 @@
+// Shared-memory pipeline primitives for sm_100a: mbarriers, bulk async
+// copies global -> shared (cp.async.bulk with complete_tx), and bounded waits.
+//
+// Every wait here is bounded by wall time (%globaltimer): on expiry it sets
+// bit `kErrorTimeout` in the kernel's device error word and returns false, so
+// a kernel can leave instead of hanging; the host reads the word after the
+// stream synchronises and reports ADI_CUDA_TIMEOUT.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace adi_cuda {
+
+constexpr uint32_t kErrorTimeout = 1u;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any legal wait
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Waits for the phase of `bar` with parity `parity` to complete, at most
+// kWaitLimitNs. Returns false (and flags `error`) on expiry, and at once if
+// any wait of the launch has already expired, so a failed launch drains in
+// bounded time instead of paying the limit at every later wait.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *error) {
+    if (mbar_test(bar, parity)) return true;
+    const uint64_t start = global_ns();
+    while (!mbar_test(bar, parity)) {
+        if (*reinterpret_cast<volatile uint32_t *>(error) != 0) return false;
+        if (global_ns() - start > kWaitLimitNs) {
+            atomicOr(error, kErrorTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
+// Makes mbarrier initialisation visible to the async (bulk copy) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
+// global to this CTA's shared memory, completing on `bar`'s transaction count.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Named barrier over `threads` threads (a subset of the block).
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+}  // namespace adi_cuda

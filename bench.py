@@ -218,7 +218,10 @@ def run_ours(args, world, rank, local):
     from adi_b200 import synthetic
     torch.cuda.set_device(local)
     ctx = adi_b200.Context(local)
-    stream = torch.cuda.current_stream()
+    # One explicit stream for everything: the context launches on it and the
+    # timing events are recorded on it.
+    stream = torch.cuda.Stream(device=local)
+    torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
     T, L = args.tokens, args.layers
 

@@ -201,26 +201,32 @@ void ora_hadamard(float *values, uint32_t count) {
 }
 
 /* The state-value tables are pure functions of the TLUT; keep the last one
- * built, as the reference keeps it in ExpertScratch (kernels.cpp:32-52). */
-static const float *expert_cache_key;
+ * built, as the reference keeps it in ExpertScratch (kernels.cpp:32-52).
+ * Keyed by the TLUT's contents, not its address: a caller may free one TLUT
+ * and allocate the next at the same address. */
+static float *expert_cache_tlut;
 static float *expert_cache;
-static const float *ne_cache_key;
+static float *ne_cache_tlut;
 static float *ne_cache;
 
 static const float *expert_values_for(const float *tlut) {
-    if (expert_cache_key != tlut) {
+    const size_t bytes = sizeof(float) * 32768 * 8;
+    if (!expert_cache_tlut || memcmp(expert_cache_tlut, tlut, bytes) != 0) {
         if (!expert_cache) expert_cache = malloc(sizeof(float) * 65536 * 8);
+        if (!expert_cache_tlut) expert_cache_tlut = malloc(bytes);
         ora_expert_state_values(tlut, expert_cache);
-        expert_cache_key = tlut;
+        memcpy(expert_cache_tlut, tlut, bytes);
     }
     return expert_cache;
 }
 
 static const float *ne_values_for(const float *tlut) {
-    if (ne_cache_key != tlut) {
+    const size_t bytes = sizeof(float) * 512 * 2;
+    if (!ne_cache_tlut || memcmp(ne_cache_tlut, tlut, bytes) != 0) {
         if (!ne_cache) ne_cache = malloc(sizeof(float) * 65536 * 2);
+        if (!ne_cache_tlut) ne_cache_tlut = malloc(bytes);
         ora_ne_state_values(tlut, ne_cache);
-        ne_cache_key = tlut;
+        memcpy(ne_cache_tlut, tlut, bytes);
     }
     return ne_cache;
 }

@@ -424,12 +424,17 @@ static void launch_expert_stream(const ExpertGemmParams &p, int grid, cudaStream
     expert_stream_kernel<NT, CW><<<grid & ~1, (CW + 1) * 32, bytes, s>>>(p);
 }
 
+// Every instance has the same consumer warps, so a position's arithmetic --
+// which warp sums which tile columns, in which order -- is the same whatever
+// the batch around it: results are batch-invariant bit for bit.
+constexpr int kConsumerWarps = 8;
+
 void launch_expert_gemm(const ExpertGemmParams &p, int grid, cudaStream_t s) {
     switch (p.tokens_per_item) {
-        case 1: launch_expert_stream<1, 16>(p, grid, s); break;
-        case 2: launch_expert_stream<2, 16>(p, grid, s); break;
-        case 4: launch_expert_stream<4, 16>(p, grid, s); break;
-        default: launch_expert_stream<8, 8>(p, grid, s); break;
+        case 1: launch_expert_stream<1, kConsumerWarps>(p, grid, s); break;
+        case 2: launch_expert_stream<2, kConsumerWarps>(p, grid, s); break;
+        case 4: launch_expert_stream<4, kConsumerWarps>(p, grid, s); break;
+        default: launch_expert_stream<8, kConsumerWarps>(p, grid, s); break;
     }
 }
 

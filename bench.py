@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--tokens", type=int, default=512)
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--no-baseline", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="only the timed region: no e2e, ubatch sweep or CPU baseline (profiling runs)")
     return ap.parse_args()
 
 
@@ -291,6 +293,17 @@ def run_ours(args, world, rank, local):
     block_bytes = [blocks[0].shared_bytes() + n * blocks[0].packed_bytes_per_expert() + T * H * 4 * 2
                    for n in n_touched]
     block_gbs = sum(block_bytes) / (ms / 1e3) / 1e9
+
+    if args.no_extras:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+                              "steps": args.steps, "ms_per_step": ms_max / args.steps, "profiling_run": True,
+                              "stages_ms_per_step": {k: v[0] / max(1, v[1]) for k, v in stages.items()}}),
+                  flush=True)
+        for h in handles:
+            h.release()
+        ctx.close()
+        return
 
     # End to end through the host-pointer C ABI, pinned host buffers.
     x_host = torch.empty(pool, T, H, dtype=torch.float32, pin_memory=True)

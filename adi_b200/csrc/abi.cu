@@ -6,6 +6,7 @@
 // HBM. Every entry validates its arguments on the host first, with the
 // reference's own error messages, so shape errors never reach a kernel.
 #include "adi_cuda.h"
+#include "expert_tc.cuh"
 #include "kernels.cuh"
 
 #include <cuda_runtime.h>
@@ -87,17 +88,61 @@ std::unique_ptr<DeviceArray> upload_bytes(const void *host, size_t bytes, const 
     return a;
 }
 
+// Exact f16 -> f32 on the host (same result as the device conversion).
+float host_f16(uint16_t bits) {
+    const uint32_t sign = uint32_t(bits & 0x8000u) << 16;
+    uint32_t exponent = (bits >> 10) & 0x1Fu, mantissa = bits & 0x3FFu, out;
+    if (exponent == 0) {
+        if (mantissa == 0) {
+            out = sign;
+        } else {
+            int shift = 0;
+            while ((mantissa & 0x400u) == 0) {
+                mantissa <<= 1;
+                ++shift;
+            }
+            out = sign | (uint32_t(113 - shift) << 23) | ((mantissa & 0x3FFu) << 13);
+        }
+    } else if (exponent == 31) {
+        out = sign | 0x7F800000u | (mantissa << 13);
+    } else {
+        out = sign | ((exponent + 112) << 23) | (mantissa << 13);
+    }
+    float f;
+    std::memcpy(&f, &out, 4);
+    return f;
+}
+
+// Power-of-two exponent bringing `max_abs` to at most 2^14, as the device's
+// operand scaling computes it.
+int8_t scale_exponent_host(float max_abs) {
+    if (!(max_abs > 0.0f) || !std::isfinite(max_abs)) return 0;
+    int e;
+    std::frexp(max_abs, &e);
+    int k = 14 - e;
+    return int8_t(k < -120 ? -120 : (k > 120 ? 120 : k));
+}
+
 // Decoded value tables, one set per distinct TLUT.
 struct ExpertCodec {
     DeviceArray half_tables;  // uint2 [2][16384]
+    float max_value = 0;      // largest |f16 value| of the table
 };
+
+// Exponent folded into a matrix's decoded tensor-core operand: keeps
+// |value * gamma| * 2^ka within f16 range for every tile.
+int8_t expert_ka(const uint16_t *gamma, size_t count, float max_value) {
+    float max_gamma = 0.0f;
+    for (size_t i = 0; i < count; ++i) max_gamma = std::fmax(max_gamma, std::fabs(host_f16(gamma[i])));
+    return scale_exponent_host(max_value * max_gamma);
+}
 struct NeCodec {
     DeviceArray table;  // float2 [1024]
 };
 
 struct ExpertDev {
     uint32_t rows, cols;
-    std::unique_ptr<DeviceArray> trellis, su, sv, gamma;
+    std::unique_ptr<DeviceArray> trellis, su, sv, gamma, ka;
     ExpertCodec *codec;
 };
 struct NeDev {
@@ -117,7 +162,7 @@ struct Bf16Dev {
 struct MoeDev {
     uint32_t hidden, inner, experts;
     std::unique_ptr<DeviceArray> router;  // [(E+1)][H] bf16: router rows then the shared gate
-    std::unique_ptr<DeviceArray> trellis[3], su[3], sv[3], gamma[3];
+    std::unique_ptr<DeviceArray> trellis[3], su[3], sv[3], gamma[3], ka[3];
     ExpertCodec *codec;
     NeDev shared[3];
 };
@@ -264,6 +309,10 @@ struct adi_cuda_context {
         if (!slot) {
             slot = std::make_unique<ExpertCodec>();
             auto staged = upload_bytes(tlut, key.size(), "TLUT");
+            for (size_t i = 0; i < size_t(32768) * 8; ++i) {
+                const float v = std::fabs(tlut[i]);
+                if (std::isfinite(v)) slot->max_value = std::fmax(slot->max_value, v);
+            }
             slot->half_tables.reserve(2 * 16384 * sizeof(uint2));
             launch_build_expert_tables(staged->as<float>(), slot->half_tables.as<uint2>(), stream);
             after_launch(1);
@@ -330,6 +379,8 @@ void fill_expert(adi_cuda_context *c, const adi_expert_matrix &m, ExpertDev &d) 
     d.sv = upload_bytes(m.sv_f16, size_t(m.rows) * 2, "sv");
     d.gamma = upload_bytes(m.wave_gamma_f16, size_t(m.rows / 16 + m.columns / 16) * 2, "wave_gamma");
     d.codec = c->expert_codec(m.tlut);
+    const int8_t ka = expert_ka(m.wave_gamma_f16, m.rows / 16 + m.columns / 16, d.codec->max_value);
+    d.ka = upload_bytes(&ka, 1, "ka");
 }
 
 void fill_ne(adi_cuda_context *c, const adi_ne_matrix &m, NeDev &d) {
@@ -365,8 +416,46 @@ uint32_t tokens_per_item(uint64_t expected) {
 
 // ---- standalone matmuls on device pointers -------------------------------
 
+bool tensor_core_shape(uint32_t rows, uint32_t cols) { return rows % 128 == 0 && cols % 128 == 0; }
+
+void expert_matmul_tc(adi_cuda_context *c, ExpertDev &m, const float *in, uint32_t batch, float *out) {
+    __half *xh = c->buffer<__half>("xh_prep", size_t(batch) * m.cols);
+    int8_t *kx = c->buffer<int8_t>("kx_prep", batch);
+    float *acc = c->buffer<float>("acc", 2 * size_t(batch) * m.rows);
+    c->stage(kStageExpertMatmul);
+    PrepF16Params pp{};
+    pp.input = in;
+    pp.su[0] = pp.su[1] = m.su->as<uint16_t>();
+    pp.xh[0] = pp.xh[1] = xh;
+    pp.kx[0] = pp.kx[1] = kx;
+    pp.cols = m.cols;
+    pp.rows = batch;
+    pp.scale = transform_scale(m.cols);
+    pp.jobs = 1;
+    launch_prep_f16(pp, c->stream);
+    CUtensorMap map;
+    if (!make_b_map(&map, xh, batch, m.cols / 2)) throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
+    TcParams tp{};
+    tp.job[0] = TcJob{m.trellis->as<uint16_t>(), 0, m.gamma->as<uint16_t>(), 0, m.ka->as<int8_t>(), kx, acc,
+                      size_t(batch) * m.rows, m.rows, m.cols, batch};
+    tp.job[1] = tp.job[0];
+    tp.dense_positions = batch;
+    tp.table = m.codec->half_tables.as<uint2>();
+    tp.error = c->error_word;
+    const uint64_t units = uint64_t(m.rows / 128) * ((batch + kTcMaxN - 1) / kTcMaxN);
+    launch_expert_tc(map, map, tp, gemm_grid(c, units, 2), c->stream);
+    launch_finalize(acc, acc + size_t(batch) * m.rows, m.sv->ptr, 1, batch, m.rows, transform_scale(m.rows), out,
+                    c->stream);
+    c->stage_end();
+    c->after_launch(3);
+}
+
 void expert_matmul_dev(adi_cuda_context *c, ExpertDev &m, const float *in, uint32_t batch, float *out) {
     if (batch == 0) invalid("Mach expert batch shape mismatch");
+    if (c->precision == 1 && tensor_core_shape(m.rows, m.cols)) {
+        expert_matmul_tc(c, m, in, batch, out);
+        return;
+    }
     float *xp = c->buffer<float>("x_prep", size_t(batch) * m.cols);
     float *acc = c->buffer<float>("acc", 2 * size_t(batch) * m.rows);
     c->stage(kStageExpertMatmul);
@@ -484,11 +573,14 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     rp.grouped = c->buffer<uint32_t>("moe_grouped", P);
     rp.pos_expert = c->buffer<uint32_t>("moe_pos_expert", P);
     rp.route_to_grouped = c->buffer<uint32_t>("moe_r2g", P);
-    const uint32_t nt = tokens_per_item((uint64_t(T) * 8 + E - 1) / E);
+    // Tensor cores once experts see a few positions each on average; below
+    // that the CUDA-core kernel streams the few touched experts faster.
+    const bool tc = c->precision == 1 && tensor_core_shape(I, H) && uint64_t(T) * 8 >= uint64_t(E) * 4;
+    const uint32_t nt = tc ? kTcMaxN : tokens_per_item((uint64_t(T) * 8 + E - 1) / E);
     const uint32_t rb_gate_up = expert_rows_per_item(H), rb_down = expert_rows_per_item(I);
     rp.chunk = nt;
-    rp.row_blocks_gate_up = (I / 16 + rb_gate_up - 1) / rb_gate_up;
-    rp.row_blocks_down = (H / 16 + rb_down - 1) / rb_down;
+    rp.row_blocks_gate_up = tc ? I / 128 : (I / 16 + rb_gate_up - 1) / rb_gate_up;
+    rp.row_blocks_down = tc ? H / 128 : (H / 16 + rb_down - 1) / rb_down;
     const size_t max_chunks = P / nt + E;
     rp.items_gate_up = c->buffer<uint4>("moe_items_gu", max_chunks * 2 * rp.row_blocks_gate_up);
     rp.items_down = c->buffer<uint4>("moe_items_d", max_chunks * rp.row_blocks_down);
@@ -499,75 +591,147 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     launch_route(rp, s);
     c->stage_end();
 
-    float *xg = c->buffer<float>("moe_xg", P * H);
-    float *xu = c->buffer<float>("moe_xu", P * H);
-    PrepParams pp{};
-    pp.input = in;
-    pp.grouped = rp.grouped;
-    pp.pos_expert = rp.pos_expert;
-    pp.su[0] = L.su[0]->ptr;
-    pp.su[1] = L.su[1]->ptr;
-    pp.out[0] = xg;
-    pp.out[1] = xu;
-    pp.su_stride = H;
-    pp.cols = H;
-    pp.scale = transform_scale(H);
-    pp.rows = uint32_t(P);
-    pp.jobs = 2;
-    pp.su_is_f16 = 1;
-    c->stage(kStagePrep);
-    launch_prep(pp, s);
-    c->stage_end();
-
     float *acc_g = c->buffer<float>("moe_acc_g", 2 * P * I);
     float *acc_u = c->buffer<float>("moe_acc_u", 2 * P * I);
-    const uint32_t tiles_gu = (I / 16) * (H / 16);
-    ExpertGemmParams gp{};
-    gp.job[0] = ExpertJob{L.trellis[0]->as<uint32_t>(), L.gamma[0]->as<uint16_t>(), xg, acc_g, I, H,
-                          tiles_gu * 12, I / 16 + H / 16, P * I};
-    gp.job[1] = ExpertJob{L.trellis[1]->as<uint32_t>(), L.gamma[1]->as<uint16_t>(), xu, acc_u, I, H,
-                          tiles_gu * 12, I / 16 + H / 16, P * I};
-    gp.work = WorkList{rp.items_gate_up, rp.count_gate_up, 0, 0, nt};
-    gp.table = L.codec->half_tables.as<uint2>();
-    gp.rows_per_item = rb_gate_up;
-    gp.tokens_per_item = nt;
-    gp.error = c->error_word;
-    c->stage(kStageExpertGateUp);
-    launch_expert_gemm(gp, c->sms, s);
-    c->stage_end();
-
-    float *xd = c->buffer<float>("moe_xd", P * I);
-    MidParams mp{};
-    mp.acc_gate = acc_g;
-    mp.acc_up = acc_u;
-    mp.half_stride = P * I;
-    mp.pos_expert = rp.pos_expert;
-    mp.sv_gate = L.sv[0]->ptr;
-    mp.sv_up = L.sv[1]->ptr;
-    mp.su_down = L.su[2]->ptr;
-    mp.is_f16 = 1;
-    mp.halves = 2;
-    mp.inner = I;
-    mp.scale = transform_scale(I);
-    mp.xd = xd;
-    mp.positions = uint32_t(P);
-    c->stage(kStageSwiglu);
-    launch_mid(mp, s);
-    c->stage_end();
-
     float *acc_d = c->buffer<float>("moe_acc_d", 2 * P * H);
-    ExpertGemmParams dp{};
-    dp.job[0] = ExpertJob{L.trellis[2]->as<uint32_t>(), L.gamma[2]->as<uint16_t>(), xd, acc_d, H, I,
-                          tiles_gu * 12, I / 16 + H / 16, P * H};
-    dp.job[1] = dp.job[0];
-    dp.work = WorkList{rp.items_down, rp.count_down, 0, 0, nt};
-    dp.table = gp.table;
-    dp.rows_per_item = rb_down;
-    dp.tokens_per_item = nt;
-    dp.error = c->error_word;
-    c->stage(kStageExpertDown);
-    launch_expert_gemm(dp, c->sms, s);
-    c->stage_end();
+    const uint32_t tiles_gu = (I / 16) * (H / 16);
+    if (tc) {
+        __half *xh_g = c->buffer<__half>("moe_xh_g", P * H);
+        __half *xh_u = c->buffer<__half>("moe_xh_u", P * H);
+        int8_t *kx_g = c->buffer<int8_t>("moe_kx_g", P);
+        int8_t *kx_u = c->buffer<int8_t>("moe_kx_u", P);
+        PrepF16Params pp{};
+        pp.input = in;
+        pp.grouped = rp.grouped;
+        pp.pos_expert = rp.pos_expert;
+        pp.su[0] = L.su[0]->as<uint16_t>();
+        pp.su[1] = L.su[1]->as<uint16_t>();
+        pp.xh[0] = xh_g;
+        pp.xh[1] = xh_u;
+        pp.kx[0] = kx_g;
+        pp.kx[1] = kx_u;
+        pp.su_stride = H;
+        pp.cols = H;
+        pp.rows = uint32_t(P);
+        pp.scale = transform_scale(H);
+        pp.jobs = 2;
+        c->stage(kStagePrep);
+        launch_prep_f16(pp, s);
+        c->stage_end();
+        CUtensorMap map_g, map_u, map_d;
+        if (!make_b_map(&map_g, xh_g, uint32_t(P), H / 2) || !make_b_map(&map_u, xh_u, uint32_t(P), H / 2))
+            throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
+        TcParams tp{};
+        tp.job[0] = TcJob{L.trellis[0]->as<uint16_t>(), size_t(tiles_gu) * 48, L.gamma[0]->as<uint16_t>(),
+                          I / 16 + H / 16, L.ka[0]->as<int8_t>(), kx_g, acc_g, P * I, I, H, uint32_t(P)};
+        tp.job[1] = TcJob{L.trellis[1]->as<uint16_t>(), size_t(tiles_gu) * 48, L.gamma[1]->as<uint16_t>(),
+                          I / 16 + H / 16, L.ka[1]->as<int8_t>(), kx_u, acc_u, P * I, I, H, uint32_t(P)};
+        tp.units = rp.items_gate_up;
+        tp.unit_count = rp.count_gate_up;
+        tp.table = L.codec->half_tables.as<uint2>();
+        tp.error = c->error_word;
+        c->stage(kStageExpertGateUp);
+        launch_expert_tc(map_g, map_u, tp, c->sms, s);
+        c->stage_end();
+
+        __half *xh_d = c->buffer<__half>("moe_xh_d", P * I);
+        int8_t *kx_d = c->buffer<int8_t>("moe_kx_d", P);
+        MidF16Params mp{};
+        mp.acc_gate = acc_g;
+        mp.acc_up = acc_u;
+        mp.half_stride = P * I;
+        mp.pos_expert = rp.pos_expert;
+        mp.sv_gate = L.sv[0]->as<uint16_t>();
+        mp.sv_up = L.sv[1]->as<uint16_t>();
+        mp.su_down = L.su[2]->as<uint16_t>();
+        mp.inner = I;
+        mp.scale = transform_scale(I);
+        mp.xh = xh_d;
+        mp.kx = kx_d;
+        mp.positions = uint32_t(P);
+        c->stage(kStageSwiglu);
+        launch_mid_f16(mp, s);
+        c->stage_end();
+        if (!make_b_map(&map_d, xh_d, uint32_t(P), I / 2))
+            throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
+        TcParams dp{};
+        dp.job[0] = TcJob{L.trellis[2]->as<uint16_t>(), size_t(tiles_gu) * 48, L.gamma[2]->as<uint16_t>(),
+                          I / 16 + H / 16, L.ka[2]->as<int8_t>(), kx_d, acc_d, P * H, H, I, uint32_t(P)};
+        dp.job[1] = dp.job[0];
+        dp.units = rp.items_down;
+        dp.unit_count = rp.count_down;
+        dp.table = tp.table;
+        dp.error = c->error_word;
+        c->stage(kStageExpertDown);
+        launch_expert_tc(map_d, map_d, dp, c->sms, s);
+        c->stage_end();
+    } else {
+        float *xg = c->buffer<float>("moe_xg", P * H);
+        float *xu = c->buffer<float>("moe_xu", P * H);
+        PrepParams pp{};
+        pp.input = in;
+        pp.grouped = rp.grouped;
+        pp.pos_expert = rp.pos_expert;
+        pp.su[0] = L.su[0]->ptr;
+        pp.su[1] = L.su[1]->ptr;
+        pp.out[0] = xg;
+        pp.out[1] = xu;
+        pp.su_stride = H;
+        pp.cols = H;
+        pp.scale = transform_scale(H);
+        pp.rows = uint32_t(P);
+        pp.jobs = 2;
+        pp.su_is_f16 = 1;
+        c->stage(kStagePrep);
+        launch_prep(pp, s);
+        c->stage_end();
+
+        ExpertGemmParams gp{};
+        gp.job[0] = ExpertJob{L.trellis[0]->as<uint32_t>(), L.gamma[0]->as<uint16_t>(), xg, acc_g, I, H,
+                              tiles_gu * 12, I / 16 + H / 16, P * I};
+        gp.job[1] = ExpertJob{L.trellis[1]->as<uint32_t>(), L.gamma[1]->as<uint16_t>(), xu, acc_u, I, H,
+                              tiles_gu * 12, I / 16 + H / 16, P * I};
+        gp.work = WorkList{rp.items_gate_up, rp.count_gate_up, 0, 0, nt};
+        gp.table = L.codec->half_tables.as<uint2>();
+        gp.rows_per_item = rb_gate_up;
+        gp.tokens_per_item = nt;
+        gp.error = c->error_word;
+        c->stage(kStageExpertGateUp);
+        launch_expert_gemm(gp, c->sms, s);
+        c->stage_end();
+
+        float *xd = c->buffer<float>("moe_xd", P * I);
+        MidParams mp{};
+        mp.acc_gate = acc_g;
+        mp.acc_up = acc_u;
+        mp.half_stride = P * I;
+        mp.pos_expert = rp.pos_expert;
+        mp.sv_gate = L.sv[0]->ptr;
+        mp.sv_up = L.sv[1]->ptr;
+        mp.su_down = L.su[2]->ptr;
+        mp.is_f16 = 1;
+        mp.halves = 2;
+        mp.inner = I;
+        mp.scale = transform_scale(I);
+        mp.xd = xd;
+        mp.positions = uint32_t(P);
+        c->stage(kStageSwiglu);
+        launch_mid(mp, s);
+        c->stage_end();
+
+        ExpertGemmParams dp{};
+        dp.job[0] = ExpertJob{L.trellis[2]->as<uint32_t>(), L.gamma[2]->as<uint16_t>(), xd, acc_d, H, I,
+                              tiles_gu * 12, I / 16 + H / 16, P * H};
+        dp.job[1] = dp.job[0];
+        dp.work = WorkList{rp.items_down, rp.count_down, 0, 0, nt};
+        dp.table = gp.table;
+        dp.rows_per_item = rb_down;
+        dp.tokens_per_item = nt;
+        dp.error = c->error_word;
+        c->stage(kStageExpertDown);
+        launch_expert_gemm(dp, c->sms, s);
+        c->stage_end();
+    }
 
     // Shared NE expert over all T tokens.
     float *sxg = c->buffer<float>("moe_sxg", size_t(T) * H);
@@ -879,6 +1043,14 @@ int adi_cuda_upload_moe_layer(adi_cuda_context *c, const adi_moe_layer *l, adi_c
             d->gamma[p] = upload_bytes(gamma.data(), gamma.size() * 2, "gamma");
         }
         d->codec = c->expert_codec(tlut);
+        for (int p = 0; p < 3; ++p) {
+            const uint32_t rows = p == 2 ? H : I, cols = p == 2 ? I : H;
+            const size_t gw = rows / 16 + cols / 16;
+            std::vector<int8_t> ka(E);
+            for (uint32_t e = 0; e < E; ++e)
+                ka[e] = expert_ka(l->routed[3 * e + p].wave_gamma_f16, gw, d->codec->max_value);
+            d->ka[p] = upload_bytes(ka.data(), ka.size(), "ka");
+        }
         const adi_ne_matrix *shared[3] = {&l->shared_gate, &l->shared_up, &l->shared_down};
         for (int p = 0; p < 3; ++p) {
             const uint32_t rows = p == 2 ? H : I, cols = p == 2 ? I : H;

@@ -310,7 +310,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) expert_stream_kernel(const E
             for (uint32_t k = 0; k < min(issued, kStages); ++k) {
                 slot = slot == 0 ? kStages - 1 : slot - 1;
                 if (slot == kStages - 1) phase ^= 1u;
-                mbar_wait(&full[slot], phase, p.error);
+                mbar_wait_own(&full[slot], phase, p.error);
             }
         }
         return;

@@ -67,6 +67,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
     return true;
 }
 
+// Waits for work this thread started itself (copies, MMAs), which completes
+// on its own: not cut short by another wait's failure, bounded all the same.
+__device__ __forceinline__ bool mbar_wait_own(uint64_t *bar, uint32_t parity, uint32_t *error) {
+    const uint64_t start = global_ns();
+    while (!mbar_test(bar, parity)) {
+        if (global_ns() - start > kWaitLimitNs) {
+            atomicOr(error, kErrorTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
 // Makes mbarrier initialisation visible to the async (bulk copy) proxy.
 __device__ __forceinline__ void fence_barrier_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");

@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=512)
     ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--precision", type=int, default=1, choices=[0, 1],
+                    help="0: CUDA-core fp32 throughout; 1: tcgen05 f16 operands for the expert products")
     ap.add_argument("--no-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-extras", action="store_true",
                     help="only the timed region: no e2e, ubatch sweep or CPU baseline (profiling runs)")
@@ -225,6 +227,7 @@ def run_ours(args, world, rank, local):
     stream = torch.cuda.Stream(device=local)
     torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
+    ctx.set_precision(args.precision)
     T, L = args.tokens, args.layers
 
     blocks, handles = [], []
@@ -355,7 +358,8 @@ def run_ours(args, world, rank, local):
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 operands, f32 accumulate" if args.precision else "f32", "data": "synthetic",
             "config": {"workload": f"C2: one MoE block, prefill ubatch {T}, "
                                    + ("1 GPU" if world == 1 else f"{world} GPU replicas"),
                        "tokens_per_step": T, "hidden": H, "experts": E, "expert_hidden": blocks[0].expert_hidden,

@@ -6,7 +6,7 @@
 // HBM. Every entry validates its arguments on the host first, with the
 // reference's own error messages, so shape errors never reach a kernel.
 #include "adi_cuda.h"
-#include "expert_tc.cuh"
+#include "tc_gemm.cuh"
 #include "kernels.cuh"
 
 #include <cuda_runtime.h>
@@ -137,7 +137,8 @@ int8_t expert_ka(const uint16_t *gamma, size_t count, float max_value) {
     return scale_exponent_host(max_value * max_gamma);
 }
 struct NeCodec {
-    DeviceArray table;  // float2 [1024]
+    DeviceArray table;      // float2 [1024]
+    DeviceArray table_f16;  // f16x2 [1024], the tensor-core path's copy
 };
 
 struct ExpertDev {
@@ -330,8 +331,10 @@ struct adi_cuda_context {
             slot = std::make_unique<NeCodec>();
             auto staged = upload_bytes(tlut, key.size(), "TLUT");
             slot->table.reserve(1024 * sizeof(float2));
+            slot->table_f16.reserve(1024 * sizeof(uint32_t));
             launch_build_ne_table(staged->as<float>(), slot->table.as<float2>(), stream);
-            after_launch(1);
+            launch_build_ne_table_f16(slot->table.as<float2>(), slot->table_f16.as<uint32_t>(), stream);
+            after_launch(2);
             check(cudaStreamSynchronize(stream), "build NE table");
         }
         return slot.get();
@@ -418,6 +421,15 @@ uint32_t tokens_per_item(uint64_t expected) {
 
 bool tensor_core_shape(uint32_t rows, uint32_t cols) { return rows % 128 == 0 && cols % 128 == 0; }
 
+// Below this many inputs an NE projection streams faster on CUDA cores.
+constexpr uint32_t kNeTensorCoreMinBatch = 16;
+
+CUtensorMap b_map(const __half *x, uint32_t rows, uint32_t cols) {
+    CUtensorMap map;
+    if (!make_b_map(&map, x, rows, cols)) throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
+    return map;
+}
+
 void expert_matmul_tc(adi_cuda_context *c, ExpertDev &m, const float *in, uint32_t batch, float *out) {
     __half *xh = c->buffer<__half>("xh_prep", size_t(batch) * m.cols);
     int8_t *kx = c->buffer<int8_t>("kx_prep", batch);
@@ -425,27 +437,62 @@ void expert_matmul_tc(adi_cuda_context *c, ExpertDev &m, const float *in, uint32
     c->stage(kStageExpertMatmul);
     PrepF16Params pp{};
     pp.input = in;
-    pp.su[0] = pp.su[1] = m.su->as<uint16_t>();
+    pp.su[0] = pp.su[1] = m.su->ptr;
     pp.xh[0] = pp.xh[1] = xh;
     pp.kx[0] = pp.kx[1] = kx;
     pp.cols = m.cols;
     pp.rows = batch;
     pp.scale = transform_scale(m.cols);
     pp.jobs = 1;
+    pp.su_is_f16 = 1;
+    pp.split = 1;
     launch_prep_f16(pp, c->stream);
-    CUtensorMap map;
-    if (!make_b_map(&map, xh, batch, m.cols / 2)) throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
+    const CUtensorMap map = b_map(xh, 2 * batch, m.cols / 2);
     TcParams tp{};
-    tp.job[0] = TcJob{m.trellis->as<uint16_t>(), 0, m.gamma->as<uint16_t>(), 0, m.ka->as<int8_t>(), kx, acc,
+    tp.job[0] = TcJob{m.trellis->as<uint16_t>(), 0, m.gamma->as<uint16_t>(), 0, m.ka->as<int8_t>(), 1.0f, kx, acc,
                       size_t(batch) * m.rows, m.rows, m.cols, batch};
     tp.job[1] = tp.job[0];
     tp.dense_positions = batch;
-    tp.table = m.codec->half_tables.as<uint2>();
+    tp.dense_jobs = 1;
+    tp.table = m.codec->half_tables.ptr;
     tp.error = c->error_word;
     const uint64_t units = uint64_t(m.rows / 128) * ((batch + kTcMaxN - 1) / kTcMaxN);
-    launch_expert_tc(map, map, tp, gemm_grid(c, units, 2), c->stream);
+    launch_tc_gemm(TcCodec::kExpert, map, map, tp, gemm_grid(c, units, 2), c->stream);
     launch_finalize(acc, acc + size_t(batch) * m.rows, m.sv->ptr, 1, batch, m.rows, transform_scale(m.rows), out,
                     c->stream);
+    c->stage_end();
+    c->after_launch(3);
+}
+
+void ne_matmul_tc(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batch, float *out) {
+    __half *xh = c->buffer<__half>("xh_prep", size_t(batch) * m.cols);
+    int8_t *kx = c->buffer<int8_t>("kx_prep", batch);
+    float *acc = c->buffer<float>("acc", size_t(batch) * m.rows);
+    c->stage(kStageNeMatmul);
+    PrepF16Params pp{};
+    pp.input = in;
+    pp.su[0] = pp.su[1] = m.su->ptr;
+    pp.xh[0] = pp.xh[1] = xh;
+    pp.kx[0] = pp.kx[1] = kx;
+    pp.cols = m.cols;
+    pp.rows = batch;
+    pp.scale = transform_scale(m.cols);
+    pp.jobs = 1;
+    pp.su_is_f16 = 0;
+    pp.split = 0;
+    launch_prep_f16(pp, c->stream);
+    const CUtensorMap map = b_map(xh, batch, m.cols);
+    TcParams tp{};
+    tp.job[0] = TcJob{m.trellis->as<uint16_t>(), 0, nullptr, 0, nullptr, m.weight_scale, kx, acc,
+                      size_t(batch) * m.rows, m.rows, m.cols, batch};
+    tp.job[1] = tp.job[0];
+    tp.dense_positions = batch;
+    tp.dense_jobs = 1;
+    tp.table = m.codec->table_f16.ptr;
+    tp.error = c->error_word;
+    const uint64_t units = uint64_t(m.rows / 128) * ((batch + kTcMaxN - 1) / kTcMaxN);
+    launch_tc_gemm(TcCodec::kNe, map, map, tp, gemm_grid(c, units, 1), c->stream);
+    launch_finalize(acc, nullptr, m.sv->ptr, 0, batch, m.rows, transform_scale(m.rows), out, c->stream);
     c->stage_end();
     c->after_launch(3);
 }
@@ -489,6 +536,10 @@ void expert_matmul_dev(adi_cuda_context *c, ExpertDev &m, const float *in, uint3
 
 void ne_matmul_dev(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batch, float *out) {
     if (batch == 0) invalid("Mach NE batch shape mismatch");
+    if (c->precision == 1 && tensor_core_shape(m.rows, m.cols) && batch >= kNeTensorCoreMinBatch) {
+        ne_matmul_tc(c, m, in, batch, out);
+        return;
+    }
     float *xp = c->buffer<float>("x_prep", size_t(batch) * m.cols);
     float *acc = c->buffer<float>("acc", size_t(batch) * m.rows);
     c->stage(kStageNeMatmul);
@@ -542,6 +593,77 @@ void head_matmul_dev(adi_cuda_context *c, HeadDev &h, const float *in, uint32_t 
 }
 
 // ---- the MoE block --------------------------------------------------------
+
+// Shared NE SwiGLU expert on tensor cores: gate and up in one launch, the
+// SwiGLU between, down after; sacc = pre-transform down accumulators.
+void shared_expert_tc(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *sacc) {
+    const uint32_t H = L.hidden, I = L.inner;
+    cudaStream_t s = c->stream;
+    __half *xg = c->buffer<__half>("moe_sxh_g", size_t(T) * H);
+    __half *xu = c->buffer<__half>("moe_sxh_u", size_t(T) * H);
+    int8_t *kg = c->buffer<int8_t>("moe_skx_g", T);
+    int8_t *ku = c->buffer<int8_t>("moe_skx_u", T);
+    c->stage(kStageShared);
+    PrepF16Params pp{};
+    pp.input = in;
+    pp.su[0] = L.shared[0].su->ptr;
+    pp.su[1] = L.shared[1].su->ptr;
+    pp.xh[0] = xg;
+    pp.xh[1] = xu;
+    pp.kx[0] = kg;
+    pp.kx[1] = ku;
+    pp.cols = H;
+    pp.rows = T;
+    pp.scale = transform_scale(H);
+    pp.jobs = 2;
+    pp.su_is_f16 = 0;
+    pp.split = 0;
+    launch_prep_f16(pp, s);
+    float *acc_g = c->buffer<float>("moe_sacc_g", size_t(T) * I);
+    float *acc_u = c->buffer<float>("moe_sacc_u", size_t(T) * I);
+    const CUtensorMap map_g = b_map(xg, T, H), map_u = b_map(xu, T, H);
+    TcParams tp{};
+    tp.job[0] = TcJob{L.shared[0].trellis->as<uint16_t>(), 0, nullptr, 0, nullptr, L.shared[0].weight_scale, kg,
+                      acc_g, size_t(T) * I, I, H, T};
+    tp.job[1] = TcJob{L.shared[1].trellis->as<uint16_t>(), 0, nullptr, 0, nullptr, L.shared[1].weight_scale, ku,
+                      acc_u, size_t(T) * I, I, H, T};
+    tp.dense_positions = T;
+    tp.dense_jobs = 2;
+    tp.table = L.shared[0].codec->table_f16.ptr;
+    tp.error = c->error_word;
+    const uint64_t units_gu = uint64_t(I / 128) * 2 * ((T + kTcMaxN - 1) / kTcMaxN);
+    launch_tc_gemm(TcCodec::kNe, map_g, map_u, tp, gemm_grid(c, units_gu, 1), s);
+    __half *xd = c->buffer<__half>("moe_sxh_d", size_t(T) * I);
+    int8_t *kd = c->buffer<int8_t>("moe_skx_d", T);
+    MidF16Params mp{};
+    mp.acc_gate = acc_g;
+    mp.acc_up = acc_u;
+    mp.sv_gate = L.shared[0].sv->ptr;
+    mp.sv_up = L.shared[1].sv->ptr;
+    mp.su_down = L.shared[2].su->ptr;
+    mp.is_f16 = 0;
+    mp.halves = 1;
+    mp.split = 0;
+    mp.inner = I;
+    mp.scale = transform_scale(I);
+    mp.xh = xd;
+    mp.kx = kd;
+    mp.positions = T;
+    launch_mid_f16(mp, s);
+    const CUtensorMap map_d = b_map(xd, T, I);
+    TcParams dp{};
+    dp.job[0] = TcJob{L.shared[2].trellis->as<uint16_t>(), 0, nullptr, 0, nullptr, L.shared[2].weight_scale, kd,
+                      sacc, size_t(T) * H, H, I, T};
+    dp.job[1] = dp.job[0];
+    dp.dense_positions = T;
+    dp.dense_jobs = 1;
+    dp.table = tp.table;
+    dp.error = c->error_word;
+    const uint64_t units_d = uint64_t(H / 128) * ((T + kTcMaxN - 1) / kTcMaxN);
+    launch_tc_gemm(TcCodec::kNe, map_d, map_d, dp, gemm_grid(c, units_d, 1), s);
+    c->stage_end();
+    c->after_launch(4);
+}
 
 void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *out,
                      uint32_t *route_experts_out, float *route_weights_out) {
@@ -604,8 +726,8 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
         pp.input = in;
         pp.grouped = rp.grouped;
         pp.pos_expert = rp.pos_expert;
-        pp.su[0] = L.su[0]->as<uint16_t>();
-        pp.su[1] = L.su[1]->as<uint16_t>();
+        pp.su[0] = L.su[0]->ptr;
+        pp.su[1] = L.su[1]->ptr;
         pp.xh[0] = xh_g;
         pp.xh[1] = xh_u;
         pp.kx[0] = kx_g;
@@ -615,23 +737,23 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
         pp.rows = uint32_t(P);
         pp.scale = transform_scale(H);
         pp.jobs = 2;
+        pp.su_is_f16 = 1;
+        pp.split = 1;
         c->stage(kStagePrep);
         launch_prep_f16(pp, s);
         c->stage_end();
-        CUtensorMap map_g, map_u, map_d;
-        if (!make_b_map(&map_g, xh_g, uint32_t(P), H / 2) || !make_b_map(&map_u, xh_u, uint32_t(P), H / 2))
-            throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
+        const CUtensorMap map_g = b_map(xh_g, uint32_t(2 * P), H / 2), map_u = b_map(xh_u, uint32_t(2 * P), H / 2);
         TcParams tp{};
         tp.job[0] = TcJob{L.trellis[0]->as<uint16_t>(), size_t(tiles_gu) * 48, L.gamma[0]->as<uint16_t>(),
-                          I / 16 + H / 16, L.ka[0]->as<int8_t>(), kx_g, acc_g, P * I, I, H, uint32_t(P)};
+                          I / 16 + H / 16, L.ka[0]->as<int8_t>(), 1.0f, kx_g, acc_g, P * I, I, H, uint32_t(P)};
         tp.job[1] = TcJob{L.trellis[1]->as<uint16_t>(), size_t(tiles_gu) * 48, L.gamma[1]->as<uint16_t>(),
-                          I / 16 + H / 16, L.ka[1]->as<int8_t>(), kx_u, acc_u, P * I, I, H, uint32_t(P)};
+                          I / 16 + H / 16, L.ka[1]->as<int8_t>(), 1.0f, kx_u, acc_u, P * I, I, H, uint32_t(P)};
         tp.units = rp.items_gate_up;
         tp.unit_count = rp.count_gate_up;
-        tp.table = L.codec->half_tables.as<uint2>();
+        tp.table = L.codec->half_tables.ptr;
         tp.error = c->error_word;
         c->stage(kStageExpertGateUp);
-        launch_expert_tc(map_g, map_u, tp, c->sms, s);
+        launch_tc_gemm(TcCodec::kExpert, map_g, map_u, tp, c->sms, s);
         c->stage_end();
 
         __half *xh_d = c->buffer<__half>("moe_xh_d", P * I);
@@ -641,9 +763,12 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
         mp.acc_up = acc_u;
         mp.half_stride = P * I;
         mp.pos_expert = rp.pos_expert;
-        mp.sv_gate = L.sv[0]->as<uint16_t>();
-        mp.sv_up = L.sv[1]->as<uint16_t>();
-        mp.su_down = L.su[2]->as<uint16_t>();
+        mp.sv_gate = L.sv[0]->ptr;
+        mp.sv_up = L.sv[1]->ptr;
+        mp.su_down = L.su[2]->ptr;
+        mp.is_f16 = 1;
+        mp.halves = 2;
+        mp.split = 1;
         mp.inner = I;
         mp.scale = transform_scale(I);
         mp.xh = xh_d;
@@ -652,18 +777,17 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
         c->stage(kStageSwiglu);
         launch_mid_f16(mp, s);
         c->stage_end();
-        if (!make_b_map(&map_d, xh_d, uint32_t(P), I / 2))
-            throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
+        const CUtensorMap map_d = b_map(xh_d, uint32_t(2 * P), I / 2);
         TcParams dp{};
         dp.job[0] = TcJob{L.trellis[2]->as<uint16_t>(), size_t(tiles_gu) * 48, L.gamma[2]->as<uint16_t>(),
-                          I / 16 + H / 16, L.ka[2]->as<int8_t>(), kx_d, acc_d, P * H, H, I, uint32_t(P)};
+                          I / 16 + H / 16, L.ka[2]->as<int8_t>(), 1.0f, kx_d, acc_d, P * H, H, I, uint32_t(P)};
         dp.job[1] = dp.job[0];
         dp.units = rp.items_down;
         dp.unit_count = rp.count_down;
         dp.table = tp.table;
         dp.error = c->error_word;
         c->stage(kStageExpertDown);
-        launch_expert_tc(map_d, map_d, dp, c->sms, s);
+        launch_tc_gemm(TcCodec::kExpert, map_d, map_d, dp, c->sms, s);
         c->stage_end();
     } else {
         float *xg = c->buffer<float>("moe_xg", P * H);
@@ -734,55 +858,59 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     }
 
     // Shared NE expert over all T tokens.
-    float *sxg = c->buffer<float>("moe_sxg", size_t(T) * H);
-    float *sxu = c->buffer<float>("moe_sxu", size_t(T) * H);
-    PrepParams sp{};
-    sp.input = in;
-    sp.su[0] = L.shared[0].su->ptr;
-    sp.su[1] = L.shared[1].su->ptr;
-    sp.out[0] = sxg;
-    sp.out[1] = sxu;
-    sp.cols = H;
-    sp.scale = transform_scale(H);
-    sp.rows = T;
-    sp.jobs = 2;
-    sp.su_is_f16 = 0;
-    c->stage(kStageShared);
-    launch_prep(sp, s);
-    float *sacc_g = c->buffer<float>("moe_sacc_g", size_t(T) * I);
-    float *sacc_u = c->buffer<float>("moe_sacc_u", size_t(T) * I);
-    NeGemmParams np{};
-    np.job[0] = NeJob{L.shared[0].trellis->as<uint32_t>(), sxg, sacc_g, I, H, L.shared[0].weight_scale};
-    np.job[1] = NeJob{L.shared[1].trellis->as<uint32_t>(), sxu, sacc_u, I, H, L.shared[1].weight_scale};
-    np.work = WorkList{nullptr, nullptr, T, 2, kMaxTokens};
-    np.table = L.shared[0].codec->table.as<float2>();
-    const uint64_t ne_items = uint64_t((T + kMaxTokens - 1) / kMaxTokens) * 2 * row_blocks(I);
-    launch_ne_gemm(np, gemm_grid(c, ne_items, 1), s);
-    float *sxd = c->buffer<float>("moe_sxd", size_t(T) * I);
-    MidParams smp{};
-    smp.acc_gate = sacc_g;
-    smp.acc_up = sacc_u;
-    smp.half_stride = 0;
-    smp.pos_expert = nullptr;
-    smp.sv_gate = L.shared[0].sv->ptr;
-    smp.sv_up = L.shared[1].sv->ptr;
-    smp.su_down = L.shared[2].su->ptr;
-    smp.is_f16 = 0;
-    smp.halves = 1;
-    smp.inner = I;
-    smp.scale = transform_scale(I);
-    smp.xd = sxd;
-    smp.positions = T;
-    launch_mid(smp, s);
     float *sacc_d = c->buffer<float>("moe_sacc_d", size_t(T) * H);
-    NeGemmParams nd{};
-    nd.job[0] = NeJob{L.shared[2].trellis->as<uint32_t>(), sxd, sacc_d, H, I, L.shared[2].weight_scale};
-    nd.job[1] = nd.job[0];
-    nd.work = WorkList{nullptr, nullptr, T, 1, kMaxTokens};
-    nd.table = np.table;
-    const uint64_t nd_items = uint64_t((T + kMaxTokens - 1) / kMaxTokens) * row_blocks(H);
-    launch_ne_gemm(nd, gemm_grid(c, nd_items, 1), s);
-    c->stage_end();
+    if (c->precision == 1 && tensor_core_shape(I, H) && T >= kNeTensorCoreMinBatch) {
+        shared_expert_tc(c, L, in, T, sacc_d);
+    } else {
+        float *sxg = c->buffer<float>("moe_sxg", size_t(T) * H);
+        float *sxu = c->buffer<float>("moe_sxu", size_t(T) * H);
+        PrepParams sp{};
+        sp.input = in;
+        sp.su[0] = L.shared[0].su->ptr;
+        sp.su[1] = L.shared[1].su->ptr;
+        sp.out[0] = sxg;
+        sp.out[1] = sxu;
+        sp.cols = H;
+        sp.scale = transform_scale(H);
+        sp.rows = T;
+        sp.jobs = 2;
+        sp.su_is_f16 = 0;
+        c->stage(kStageShared);
+        launch_prep(sp, s);
+        float *sacc_g = c->buffer<float>("moe_sacc_g", size_t(T) * I);
+        float *sacc_u = c->buffer<float>("moe_sacc_u", size_t(T) * I);
+        NeGemmParams np{};
+        np.job[0] = NeJob{L.shared[0].trellis->as<uint32_t>(), sxg, sacc_g, I, H, L.shared[0].weight_scale};
+        np.job[1] = NeJob{L.shared[1].trellis->as<uint32_t>(), sxu, sacc_u, I, H, L.shared[1].weight_scale};
+        np.work = WorkList{nullptr, nullptr, T, 2, kMaxTokens};
+        np.table = L.shared[0].codec->table.as<float2>();
+        const uint64_t ne_items = uint64_t((T + kMaxTokens - 1) / kMaxTokens) * 2 * row_blocks(I);
+        launch_ne_gemm(np, gemm_grid(c, ne_items, 1), s);
+        float *sxd = c->buffer<float>("moe_sxd", size_t(T) * I);
+        MidParams smp{};
+        smp.acc_gate = sacc_g;
+        smp.acc_up = sacc_u;
+        smp.half_stride = 0;
+        smp.pos_expert = nullptr;
+        smp.sv_gate = L.shared[0].sv->ptr;
+        smp.sv_up = L.shared[1].sv->ptr;
+        smp.su_down = L.shared[2].su->ptr;
+        smp.is_f16 = 0;
+        smp.halves = 1;
+        smp.inner = I;
+        smp.scale = transform_scale(I);
+        smp.xd = sxd;
+        smp.positions = T;
+        launch_mid(smp, s);
+        NeGemmParams nd{};
+        nd.job[0] = NeJob{L.shared[2].trellis->as<uint32_t>(), sxd, sacc_d, H, I, L.shared[2].weight_scale};
+        nd.job[1] = nd.job[0];
+        nd.work = WorkList{nullptr, nullptr, T, 1, kMaxTokens};
+        nd.table = np.table;
+        const uint64_t nd_items = uint64_t((T + kMaxTokens - 1) / kMaxTokens) * row_blocks(H);
+        launch_ne_gemm(nd, gemm_grid(c, nd_items, 1), s);
+        c->stage_end();
+    }
 
     CombineParams cp{};
     cp.acc_down = acc_d;

@@ -68,6 +68,19 @@ void launch_build_ne_table(const float *tlut, float2 *table, cudaStream_t s) {
     build_ne_table_kernel<<<kNeTableRows / 256, 256, 0, s>>>(tlut, table);
 }
 
+// The same pairs as f16x2 (component 0 in the low half): exact, since every
+// value is already an f16 rounding.
+__global__ void build_ne_table_f16_kernel(const float2 *table, uint32_t *pairs) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= kNeTableRows) return;
+    const __half2 h = __floats2half2_rn(table[i].x, table[i].y);
+    pairs[i] = *reinterpret_cast<const uint32_t *>(&h);
+}
+
+void launch_build_ne_table_f16(const float2 *table, uint32_t *pairs, cudaStream_t s) {
+    build_ne_table_f16_kernel<<<kNeTableRows / 256, 256, 0, s>>>(table, pairs);
+}
+
 // ---------------------------------------------------------------------------
 // Decode checks: states and state values, for bit-exact comparison
 // ---------------------------------------------------------------------------

@@ -71,6 +71,7 @@ struct NeGemmParams {
 // Codec tables and decode checks.
 void launch_build_expert_tables(const float *tlut, uint2 *half_tables, cudaStream_t s);
 void launch_build_ne_table(const float *tlut, float2 *table, cudaStream_t s);
+void launch_build_ne_table_f16(const float2 *table, uint32_t *pairs, cudaStream_t s);
 void launch_expert_states(const uint16_t *words, uint32_t tiles, uint32_t *states, cudaStream_t s);
 void launch_ne_states(const uint16_t *words, uint32_t tiles, uint32_t *states, cudaStream_t s);
 void launch_expert_state_values(const uint2 *half_tables, float *values, cudaStream_t s);

@@ -1,0 +1,660 @@
+// Packed projections on the 5th-generation tensor cores (tcgen05), sm_100a.
+//
+// D[128 weight rows x N positions] = A[128 x K] . B[K x N] with fp32
+// accumulators in tensor memory. A is the packed matrix decoded from its
+// trellis codes straight into shared memory; B is the transformed input x',
+// loaded by TMA. Both are f16 (kind::f16). Decoded lattice values are exact in
+// f16; the factors that could leave f16's range are exact powers of two taken
+// out and restored in the epilogue:
+//   expert  A = f16(value * gamma_tile * 2^ka)  ka per (expert, projection)
+//   NE      A = value (exact), weight_scale applied in the epilogue
+//   both    B = f16(x' * 2^kx)                  kx per position
+//
+// Expert codec: a CTA keeps one half of every value row (4 of 8 components,
+// 128 KiB) in shared memory and contracts the columns that half covers --
+// packed column k' = 4g + j is matrix column 8g + 4h + j of half h, in A and
+// B alike; the kernels downstream add the halves. NE codec: the [1024] signed
+// pair table, replicated once per bank (128 KiB), so every gather of a warp
+// is conflict-free; a CTA contracts the full K.
+//
+// Warp roles (448 threads, one persistent CTA per SM):
+//   warp 0 lane 0   trellis words of each K-chunk -> 6-deep ring (bulk copies)
+//   warp 0 lane 1   B chunk (64 f16 x 128 rows, 128B-swizzled) -> 2-deep ring (TMA)
+//   warp 1          TMEM allocation; lane 0 issues the MMAs
+//   warps 2..9      decoders: state -> values -> f16 into A's swizzled K-major
+//                   layout, 2-deep ring
+//   warps 10..13    epilogue: tcgen05.ld, scale, fp32 out; 2 accumulators
+//
+// Every wait is bounded (pipeline.cuh). When one expires the launch drains
+// without touching data, the MMA lane waits (bounded) for its own MMAs, the
+// producers for their own copies, and TMEM is released before exit.
+#include "codec.cuh"
+#include "pipeline.cuh"
+#include "tc_gemm.cuh"
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+namespace adi_cuda {
+namespace {
+
+constexpr uint32_t kWordStages = 6;
+constexpr uint32_t kBStages = 2;
+constexpr uint32_t kAStages = 2;
+constexpr uint32_t kChunkK = 64;                     // f16 columns of A and B per chunk
+constexpr uint32_t kATileBytes = 128 * kChunkK * 2;  // 16 KiB
+constexpr uint32_t kBTileBytes = kTcMaxN * kChunkK * 2;
+constexpr uint32_t kWordSlotBytes = 4096;            // expert 3 KiB, NE 4 KiB per chunk
+constexpr uint32_t kDecodeWarps = 8;
+constexpr uint32_t kTcThreads = 14 * 32;
+constexpr uint32_t kTmemColumns = 2 * kTcMaxN;
+
+struct Smem {
+    static constexpr size_t table = 0;
+    static constexpr size_t a = 131072;  // 1024-aligned
+    static constexpr size_t b = a + kAStages * kATileBytes;
+    static constexpr size_t words = b + kBStages * kBTileBytes;
+    static constexpr size_t bars = words + kWordStages * kWordSlotBytes;
+    static constexpr uint32_t kBars = 2 * kWordStages + 2 * kBStages + 2 * kAStages + 4 + 1;
+    static constexpr size_t total = bars + kBars * 8 + 16;
+};
+static_assert(Smem::total <= 232448, "shared memory budget");
+
+template <TcCodec C>
+struct Traits;
+template <>
+struct Traits<TcCodec::kExpert> {
+    static constexpr uint32_t halves = 2;
+    static constexpr uint32_t chunk_cols = 128;          // matrix columns per chunk (64 packed)
+    static constexpr uint32_t tile_bytes = 48;
+    static constexpr uint32_t tiles_per_row = 8;         // per chunk
+    static constexpr uint32_t words_bytes = 8 * 8 * 48;  // 8 tile rows
+};
+template <>
+struct Traits<TcCodec::kNe> {
+    static constexpr uint32_t halves = 1;
+    static constexpr uint32_t chunk_cols = 64;
+    static constexpr uint32_t tile_bytes = 128;
+    static constexpr uint32_t tiles_per_row = 4;
+    static constexpr uint32_t words_bytes = 8 * 4 * 128;
+};
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    // K-major, 128-byte swizzle: 8-row groups 1024 B apart (SBO), LBO unused
+    // (1), descriptor version 1, layout type 2 = SWIZZLE_128B.
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ uint32_t instr_desc_f16(uint32_t n) {
+    // D f32 (bit 4), A and B f16, both K-major, N >> 3 at bit 17, M >> 4 = 8
+    // at bit 24.
+    return (1u << 4) | ((n >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int32_t x, int32_t y,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+struct Unit {
+    uint32_t expert, job, m_block, pos0, count;
+};
+
+__device__ __forceinline__ uint32_t unit_count(const TcParams &p) {
+    if (p.units) return *p.unit_count;
+    return (p.job[0].rows / 128) * p.dense_jobs * ((p.dense_positions + kTcMaxN - 1) / kTcMaxN);
+}
+
+__device__ __forceinline__ Unit unit_at(const TcParams &p, uint32_t i) {
+    if (p.units) {
+        const uint4 v = p.units[i];
+        return Unit{v.x, v.y >> 16, v.y & 0xFFFFu, v.z, v.w};
+    }
+    const uint32_t mbs = p.job[0].rows / 128;
+    const uint32_t mb = i % mbs;
+    const uint32_t job = (i / mbs) % p.dense_jobs;
+    const uint32_t pos0 = (i / (mbs * p.dense_jobs)) * kTcMaxN;
+    return Unit{0u, job, mb, pos0, min(kTcMaxN, p.dense_positions - pos0)};
+}
+
+// Mutable ring position: slot index and the parity of its current use.
+struct Ring {
+    uint32_t slot = 0, phase = 0;
+    __device__ __forceinline__ void advance(uint32_t stages) {
+        if (++slot == stages) {
+            slot = 0;
+            phase ^= 1u;
+        }
+    }
+};
+
+}  // namespace
+
+template <TcCodec C>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1,
+                   const TcParams p) {
+    using T = Traits<C>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t *a_tiles = smem + Smem::a;
+    uint8_t *b_tiles = smem + Smem::b;
+    uint8_t *word_tiles = smem + Smem::words;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Smem::bars);
+    uint64_t *w_full = bars;
+    uint64_t *w_empty = w_full + kWordStages;
+    uint64_t *b_full = w_empty + kWordStages;
+    uint64_t *b_empty = b_full + kBStages;
+    uint64_t *a_ready = b_empty + kBStages;
+    uint64_t *a_empty = a_ready + kAStages;
+    uint64_t *d_full = a_empty + kAStages;
+    uint64_t *d_empty = d_full + 2;
+    uint64_t *mma_done = d_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+
+    const uint32_t half = T::halves == 2 ? (blockIdx.x & 1u) : 0u;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+
+    // Value table into shared memory.
+    if (C == TcCodec::kExpert) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const uint2 *>(p.table) + half * kExpertTableRows);
+        uint4 *dst = reinterpret_cast<uint4 *>(smem);
+        for (uint32_t i = threadIdx.x; i < kExpertTableRows / 2; i += blockDim.x) dst[i] = src[i];
+    } else {
+        const uint32_t *src = static_cast<const uint32_t *>(p.table);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(smem);
+        for (uint32_t i = threadIdx.x; i < kNeTableRows * 32; i += blockDim.x) dst[i] = src[i >> 5];
+    }
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < kWordStages; ++s) {
+            mbar_init(&w_full[s], 1);
+            mbar_init(&w_empty[s], kDecodeWarps);
+        }
+        for (uint32_t s = 0; s < kBStages; ++s) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 1);
+        }
+        for (uint32_t s = 0; s < kAStages; ++s) {
+            mbar_init(&a_ready[s], kDecodeWarps);
+            mbar_init(&a_empty[s], 1);
+        }
+        for (uint32_t s = 0; s < 2; ++s) {
+            mbar_init(&d_full[s], 1);
+            mbar_init(&d_empty[s], 4);
+        }
+        mbar_init(mma_done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemColumns));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const uint32_t n_units = unit_count(p);
+    const uint32_t first = T::halves == 2 ? blockIdx.x >> 1 : blockIdx.x;
+    const uint32_t stride = T::halves == 2 ? gridDim.x >> 1 : gridDim.x;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- trellis words, 6 chunks ahead ----
+            Ring r;
+            uint32_t issued = 0;
+            bool ok = true;
+            for (uint32_t u = first; u < n_units && ok; u += stride) {
+                const Unit un = unit_at(p, u);
+                const TcJob &J = un.job ? p.job[1] : p.job[0];
+                const uint32_t TC = J.cols / 16;
+                const uint32_t chunks = J.cols / T::chunk_cols;
+                const uint8_t *trellis =
+                    reinterpret_cast<const uint8_t *>(J.trellis) + (size_t)un.expert * J.expert_stride_bytes;
+                for (uint32_t kc = 0; kc < chunks; ++kc) {
+                    if (!mbar_wait(&w_empty[r.slot], r.phase ^ 1u, p.error)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&w_full[r.slot], T::words_bytes);
+                    uint8_t *dst = word_tiles + r.slot * kWordSlotBytes;
+                    const uint32_t seg = T::tiles_per_row * T::tile_bytes;
+                    for (uint32_t row = 0; row < 8; ++row) {
+                        const size_t tile = (size_t)(un.m_block * 8 + row) * TC + kc * T::tiles_per_row;
+                        bulk_load(dst + row * seg, trellis + tile * T::tile_bytes, seg, &w_full[r.slot]);
+                    }
+                    ++issued;
+                    r.advance(kWordStages);
+                }
+            }
+            for (uint32_t k = 0; k < min(issued, kWordStages); ++k) {
+                r.slot = r.slot == 0 ? kWordStages - 1 : r.slot - 1;
+                if (r.slot == kWordStages - 1) r.phase ^= 1u;
+                mbar_wait_own(&w_full[r.slot], r.phase, p.error);
+            }
+        } else if (lane == 1) {
+            // ---- B chunks by TMA, 2 ahead ----
+            Ring r;
+            uint32_t issued = 0;
+            bool ok = true;
+            for (uint32_t u = first; u < n_units && ok; u += stride) {
+                const Unit un = unit_at(p, u);
+                const TcJob &J = un.job ? p.job[1] : p.job[0];
+                const CUtensorMap *map = un.job ? &map1 : &map0;
+                const uint32_t chunks = J.cols / T::chunk_cols;
+                for (uint32_t kc = 0; kc < chunks; ++kc) {
+                    if (!mbar_wait(&b_empty[r.slot], r.phase ^ 1u, p.error)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&b_full[r.slot], kBTileBytes);
+                    tma_load_2d(b_tiles + r.slot * kBTileBytes, map, (int32_t)(kc * kChunkK),
+                                (int32_t)(half * J.positions + un.pos0), &b_full[r.slot]);
+                    ++issued;
+                    r.advance(kBStages);
+                }
+            }
+            for (uint32_t k = 0; k < min(issued, kBStages); ++k) {
+                r.slot = r.slot == 0 ? kBStages - 1 : r.slot - 1;
+                if (r.slot == kBStages - 1) r.phase ^= 1u;
+                mbar_wait_own(&b_full[r.slot], r.phase, p.error);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer ----
+            Ring a, b, d;
+            bool ok = true;
+            for (uint32_t u = first; u < n_units && ok; u += stride) {
+                const Unit un = unit_at(p, u);
+                const TcJob &J = un.job ? p.job[1] : p.job[0];
+                const uint32_t chunks = J.cols / T::chunk_cols;
+                const uint32_t idesc = instr_desc_f16((un.count + 15u) & ~15u);
+                if (!mbar_wait(&d_empty[d.slot], d.phase ^ 1u, p.error)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + d.slot * kTcMaxN;
+                for (uint32_t kc = 0; kc < chunks; ++kc) {
+                    if (!mbar_wait(&a_ready[a.slot], a.phase, p.error) ||
+                        !mbar_wait(&b_full[b.slot], b.phase, p.error)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(a_tiles + a.slot * kATileBytes);
+                    const uint32_t b_addr = smem_u32(b_tiles + b.slot * kBTileBytes);
+#pragma unroll
+                    for (uint32_t k = 0; k < kChunkK / 16; ++k)
+                        mma_f16(d_tmem, smem_desc_sw128(a_addr + k * 32), smem_desc_sw128(b_addr + k * 32), idesc,
+                                (kc | k) != 0);
+                    mma_commit(&a_empty[a.slot]);
+                    mma_commit(&b_empty[b.slot]);
+                    a.advance(kAStages);
+                    b.advance(kBStages);
+                }
+                if (!ok) break;
+                mma_commit(&d_full[d.slot]);
+                d.advance(2);
+            }
+            mma_commit(mma_done);
+            mbar_wait_own(mma_done, 0, p.error);
+        }
+    } else if (warp < 2 + kDecodeWarps) {
+        // ---- decoders ----
+        const uint32_t dw = warp - 2;
+        Ring w, a;
+        bool ok = true;
+        if (C == TcCodec::kExpert) {
+            const uint2 *table = reinterpret_cast<const uint2 *>(smem);
+            const uint32_t lr = lane >> 1, step = lane & 1u;
+            const uint32_t q = (lane * 12u) >> 5;
+            const uint32_t q1 = q + 1u == kExpertU32PerTile ? 0u : q + 1u;
+            const uint32_t neg_mask = half == 0 ? 0x8000u : 0u;
+            // Warp dw decodes tile column dw of each chunk, tile rows 0..7; a
+            // lane owns state `lane` (tile row lr, columns step*8 + 4h ..).
+            const uint32_t a_lane = lr * 128 + (((dw ^ (lr & 7u)) << 4) | (step << 3));
+            for (uint32_t u = first; u < n_units; u += stride) {
+                const Unit un = unit_at(p, u);
+                const TcJob &J = un.job ? p.job[1] : p.job[0];
+                const uint32_t TC = J.cols / 16, TR = J.rows / 16;
+                const uint32_t chunks = J.cols / T::chunk_cols;
+                const uint16_t *gam = J.gamma + (size_t)un.expert * J.gamma_stride;
+                const float gscale = exp2f((float)J.ka[un.expert]);
+                for (uint32_t kc = 0; kc < chunks; ++kc) {
+                    if (ok) ok = mbar_wait(&w_full[w.slot], w.phase, p.error);
+                    if (ok) ok = mbar_wait(&a_empty[a.slot], a.phase ^ 1u, p.error);
+                    if (ok) {
+                        // Lane j < 8 fetches tile row j's gamma; shuffled out below.
+                        uint32_t gpack = 0;
+                        if (lane < 8) {
+                            const uint32_t diag = un.m_block * 8 + lane + kc * 8 + dw;
+                            const float g = __half2float(__ushort_as_half(__ldg(gam + wave_index(TR, TC, diag))));
+                            const __half2 g2 = __float2half2_rn(g * gscale);
+                            gpack = *reinterpret_cast<const uint32_t *>(&g2);
+                        }
+                        const uint32_t *tw = reinterpret_cast<const uint32_t *>(word_tiles + w.slot * kWordSlotBytes) +
+                                             dw * kExpertU32PerTile;
+                        uint8_t *a_tile = a_tiles + a.slot * kATileBytes + a_lane;
+#pragma unroll
+                        for (uint32_t j = 0; j < 8; ++j) {
+                            const uint32_t state =
+                                expert_window(stream_order(tw[j * 96 + q]), stream_order(tw[j * 96 + q1]), lane);
+                            const uint32_t prod = state_product(state);
+                            uint2 raw = table[expert_table_index(prod)];
+                            raw.x ^= (prod & 0x8000u) & neg_mask;  // bit 15 of s(s+1) negates component 0
+                            const uint32_t gj = __shfl_sync(0xffffffffu, gpack, j);
+                            const __half2 g2 = *reinterpret_cast<const __half2 *>(&gj);
+                            const __half2 v0 = __hmul2(*reinterpret_cast<const __half2 *>(&raw.x), g2);
+                            const __half2 v1 = __hmul2(*reinterpret_cast<const __half2 *>(&raw.y), g2);
+                            uint2 out;
+                            out.x = *reinterpret_cast<const uint32_t *>(&v0);
+                            out.y = *reinterpret_cast<const uint32_t *>(&v1);
+                            *reinterpret_cast<uint2 *>(a_tile + j * 2048) = out;
+                        }
+                        fence_async_shared();
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&a_ready[a.slot]);
+                        mbar_arrive(&w_empty[w.slot]);
+                    }
+                    w.advance(kWordStages);
+                    a.advance(kAStages);
+                }
+            }
+        } else {
+            const uint32_t *table = reinterpret_cast<const uint32_t *>(smem) + lane;
+            // Lane (r = lane & 15, hf = lane >> 4) owns tile row r's columns
+            // hf*8 .. +7 (states 8r + 4hf .. +3): stream word pair 2r + hf.
+            const uint32_t r = lane & 15u, hf = lane >> 4;
+            const uint32_t src = 2 * r + hf, src1 = (src + 1) & 31u;
+            for (uint32_t u = first; u < n_units; u += stride) {
+                const Unit un = unit_at(p, u);
+                const TcJob &J = un.job ? p.job[1] : p.job[0];
+                const uint32_t chunks = J.cols / T::chunk_cols;
+                for (uint32_t kc = 0; kc < chunks; ++kc) {
+                    if (ok) ok = mbar_wait(&w_full[w.slot], w.phase, p.error);
+                    if (ok) ok = mbar_wait(&a_empty[a.slot], a.phase ^ 1u, p.error);
+                    if (ok) {
+                        // Warp dw decodes tile row dw: its four tiles j = 0..3.
+                        const uint32_t *tw =
+                            reinterpret_cast<const uint32_t *>(word_tiles + w.slot * kWordSlotBytes) + dw * 128;
+                        uint8_t *a_row = a_tiles + a.slot * kATileBytes + dw * 2048 + r * 128;
+#pragma unroll
+                        for (uint32_t j = 0; j < 4; ++j) {
+                            const uint32_t wv = tw[j * 32 + lane];
+                            const uint32_t v = __shfl_sync(0xffffffffu, wv, src);
+                            const uint32_t v2 = __shfl_sync(0xffffffffu, wv, src1);
+                            uint4 out;
+                            out.x = table[ne_table_index(state_product(v & 0xFFFFu)) * 32];
+                            out.y = table[ne_table_index(state_product(__byte_perm(v, 0, 0x4403))) * 32];
+                            out.z = table[ne_table_index(state_product(v >> 16)) * 32];
+                            out.w = table[ne_table_index(state_product(__byte_perm(v, v2, 0x0025) & 0xFFFFu)) * 32];
+                            const uint32_t c = j * 2 + hf;
+                            *reinterpret_cast<uint4 *>(a_row + ((c ^ (r & 7u)) << 4)) = out;
+                        }
+                        fence_async_shared();
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&a_ready[a.slot]);
+                        mbar_arrive(&w_empty[w.slot]);
+                    }
+                    w.advance(kWordStages);
+                    a.advance(kAStages);
+                }
+            }
+        }
+    } else {
+        // ---- epilogue ----
+        const uint32_t quarter = warp & 3u;  // TMEM lanes 32*quarter .. +31
+        const uint32_t row_local = quarter * 32 + lane;
+        Ring d;
+        bool ok = true;
+        for (uint32_t u = first; u < n_units; u += stride) {
+            const Unit un = unit_at(p, u);
+            const TcJob &J = un.job ? p.job[1] : p.job[0];
+            if (ok) ok = mbar_wait(&d_full[d.slot], d.phase, p.error);
+            tc_fence_after();
+            if (ok) {
+                const uint32_t n_pad = (un.count + 15u) & ~15u;
+                const float base_scale =
+                    C == TcCodec::kExpert ? exp2f((float)-J.ka[un.expert]) : J.out_scale;
+                float *out = J.acc + half * J.half_stride + un.m_block * 128 + row_local;
+                for (uint32_t c0 = 0; c0 < n_pad; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(tmem_base + ((quarter * 32) << 16) + d.slot * kTcMaxN + c0, v);
+#pragma unroll
+                    for (uint32_t i = 0; i < 16; ++i) {
+                        const uint32_t n = c0 + i;
+                        if (n < un.count) {
+                            const uint32_t pos = un.pos0 + n;
+                            out[(size_t)pos * J.rows] = v[i] * base_scale * exp2f((float)-J.kx[pos]);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&d_empty[d.slot]);
+            d.advance(2);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemColumns));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+namespace {
+
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(ptr);
+    }
+    return fn;
+}
+
+template <TcCodec C>
+void launch_codec(const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid, cudaStream_t s) {
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(tc_gemm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Smem::total);
+        configured = true;
+    }
+    if (C == TcCodec::kExpert) grid &= ~1;
+    tc_gemm_kernel<C><<<grid, kTcThreads, Smem::total, s>>>(map0, map1, p);
+}
+
+}  // namespace
+
+bool make_b_map(CUtensorMap *map, const __half *x, uint32_t rows, uint32_t cols) {
+    EncodeTiled fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {kChunkK, kTcMaxN};
+    const cuuint32_t elem[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(x), dims, strides, box, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+void launch_tc_gemm(TcCodec codec, const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid,
+                    cudaStream_t s) {
+    if (codec == TcCodec::kExpert)
+        launch_codec<TcCodec::kExpert>(map0, map1, p, grid, s);
+    else
+        launch_codec<TcCodec::kNe>(map0, map1, p, grid, s);
+}
+
+// ---------------------------------------------------------------------------
+// f16 operand producers
+// ---------------------------------------------------------------------------
+namespace {
+
+__device__ __forceinline__ float block_max_abs(const float *v, uint32_t n, float *scratch) {
+    float m = 0.0f;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, fabsf(v[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31u) == 0) scratch[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float w = threadIdx.x < blockDim.x / 32 ? scratch[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, o));
+        if (threadIdx.x == 0) scratch[0] = w;
+    }
+    __syncthreads();
+    const float r = scratch[0];
+    __syncthreads();
+    return r;
+}
+
+// Power-of-two exponent bringing max |v| to at most 2^14 (f16 max 65504).
+__device__ __forceinline__ int scale_exponent(float max_abs) {
+    if (!(max_abs > 0.0f) || !isfinite(max_abs)) return 0;
+    int e;
+    frexpf(max_abs, &e);
+    const int k = 14 - e;
+    return k < -120 ? -120 : (k > 120 ? 120 : k);
+}
+
+// v (n floats in shared memory) as f16 * 2^k: split into value halves
+// (packed column 4g + j of half h = column 8g + 4h + j) or kept whole.
+__device__ __forceinline__ void write_f16(const float *v, uint32_t n, int k, bool split, __half *out,
+                                          size_t half_stride, uint32_t row) {
+    const float s = exp2f((float)k);
+    if (split) {
+        for (uint32_t i = threadIdx.x; i < n / 2; i += blockDim.x) {
+            const uint32_t g = i >> 2, j = i & 3u;
+            out[(size_t)row * (n / 2) + i] = __float2half_rn(v[8 * g + j] * s);
+            out[half_stride + (size_t)row * (n / 2) + i] = __float2half_rn(v[8 * g + 4 + j] * s);
+        }
+    } else {
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) out[(size_t)row * n + i] = __float2half_rn(v[i] * s);
+    }
+}
+
+__device__ __forceinline__ float scale_value(const void *base, int is_f16, size_t index) {
+    return is_f16 ? __half2float(__ushort_as_half(static_cast<const uint16_t *>(base)[index]))
+                  : (float)static_cast<const int8_t *>(base)[index];
+}
+
+__global__ void prep_f16_kernel(PrepF16Params p) {
+    extern __shared__ float v[];
+    __shared__ float scratch[32];
+    const uint32_t row = blockIdx.x;
+    const int job = blockIdx.y;
+    const uint32_t token = p.grouped ? p.grouped[row] : row;
+    const uint32_t expert = p.pos_expert ? p.pos_expert[row] : 0u;
+    const float *x = p.input + (size_t)token * p.cols;
+    const void *su = job ? p.su[1] : p.su[0];
+    const size_t su0 = (size_t)expert * p.su_stride;
+    for (uint32_t c = threadIdx.x; c < p.cols; c += blockDim.x)
+        v[c] = __fmul_rn(x[c], scale_value(su, p.su_is_f16, su0 + c));
+    __syncthreads();
+    block_fwht(v, p.cols, p.scale);
+    const int k = scale_exponent(block_max_abs(v, p.cols, scratch));
+    if (threadIdx.x == 0) (job ? p.kx[1] : p.kx[0])[row] = (int8_t)k;
+    write_f16(v, p.cols, k, p.split != 0, job ? p.xh[1] : p.xh[0], (size_t)p.rows * (p.cols / 2), row);
+}
+
+__global__ void mid_f16_kernel(MidF16Params p) {
+    extern __shared__ float sm[];
+    __shared__ float scratch[32];
+    float *g = sm, *u = sm + p.inner;
+    const uint32_t pos = blockIdx.x;
+    const uint32_t e = p.pos_expert ? p.pos_expert[pos] : 0u;
+    const size_t base = (size_t)pos * p.inner;
+    for (uint32_t i = threadIdx.x; i < p.inner; i += blockDim.x) {
+        float gv = p.acc_gate[base + i], uv = p.acc_up[base + i];
+        if (p.halves == 2) {
+            gv += p.acc_gate[p.half_stride + base + i];
+            uv += p.acc_up[p.half_stride + base + i];
+        }
+        g[i] = gv;
+        u[i] = uv;
+    }
+    __syncthreads();
+    block_fwht(g, p.inner, p.scale);
+    block_fwht(u, p.inner, p.scale);
+    const size_t s0 = p.is_f16 ? (size_t)e * p.inner : 0;
+    for (uint32_t i = threadIdx.x; i < p.inner; i += blockDim.x) {
+        const float gv = __fmul_rn(g[i], scale_value(p.sv_gate, p.is_f16, s0 + i));
+        const float uv = __fmul_rn(u[i], scale_value(p.sv_up, p.is_f16, s0 + i));
+        g[i] = __fmul_rn(__fmul_rn(silu_f(gv), uv), scale_value(p.su_down, p.is_f16, s0 + i));
+    }
+    __syncthreads();
+    block_fwht(g, p.inner, p.scale);
+    const int k = scale_exponent(block_max_abs(g, p.inner, scratch));
+    if (threadIdx.x == 0) p.kx[pos] = (int8_t)k;
+    write_f16(g, p.inner, k, p.split != 0, p.xh, (size_t)p.positions * (p.inner / 2), pos);
+}
+
+}  // namespace
+
+void launch_prep_f16(const PrepF16Params &p, cudaStream_t s) {
+    if (p.rows == 0) return;
+    prep_f16_kernel<<<dim3(p.rows, p.jobs), 256, p.cols * sizeof(float), s>>>(p);
+}
+
+void launch_mid_f16(const MidF16Params &p, cudaStream_t s) {
+    if (p.positions == 0) return;
+    mid_f16_kernel<<<p.positions, 256, 2 * p.inner * sizeof(float), s>>>(p);
+}
+
+}  // namespace adi_cuda

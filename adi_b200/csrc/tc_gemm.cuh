@@ -1,0 +1,81 @@
+// Packed projections on tcgen05 tensor cores: host interface (tc_gemm.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace adi_cuda {
+
+constexpr uint32_t kTcMaxN = 128;  // positions per work unit (MMA N)
+
+enum class TcCodec { kExpert, kNe };
+
+// One projection of a set of matrices (matrix-major, same geometry).
+struct TcJob {
+    const uint16_t *trellis;     // u16 words; matrix e starts at e * expert_stride_bytes
+    size_t expert_stride_bytes;
+    const uint16_t *gamma;       // expert: f16 bits [E][gamma_stride]
+    uint32_t gamma_stride;
+    const int8_t *ka;            // expert: [E] power-of-two exponent folded into A
+    float out_scale;             // NE: weight scale applied in the epilogue
+    const int8_t *kx;            // [positions] exponent folded into B
+    float *acc;                  // expert [2][positions][rows] (value halves); NE [positions][rows]
+    size_t half_stride;          // positions * rows
+    uint32_t rows, cols, positions;
+};
+
+// Units {matrix, job << 16 | m_block, pos0, count} with a device-resident
+// count, or (units == nullptr) dense over `dense_positions` positions of
+// matrix 0 for `dense_jobs` jobs.
+struct TcParams {
+    TcJob job[2];
+    const uint4 *units;
+    const uint32_t *unit_count;
+    uint32_t dense_positions;
+    uint32_t dense_jobs;
+    const void *table;   // expert: uint2 [2][16384] value halves; NE: f16x2 [1024]
+    uint32_t *error;     // device error word
+};
+
+// B operand map over x [rows][cols] f16: boxes of 64 columns x kTcMaxN rows,
+// 128-byte swizzle.
+bool make_b_map(CUtensorMap *map, const __half *x, uint32_t rows, uint32_t cols);
+void launch_tc_gemm(TcCodec codec, const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid,
+                    cudaStream_t s);
+
+// x' = H(x * su) as f16 * 2^kx for the tensor-core path. With `split` the
+// row is stored as value halves, xh[h][row][4g + j] = x'[8g + 4h + j];
+// without, whole.
+struct PrepF16Params {
+    const float *input;
+    const uint32_t *grouped;     // nullable: row r reads input row grouped[r]
+    const uint32_t *pos_expert;  // nullable: su of matrix pos_expert[r]
+    const void *su[2];           // f16 bits [E][cols] or int8 [cols]
+    __half *xh[2];
+    int8_t *kx[2];
+    uint32_t su_stride, cols, rows;
+    float scale;
+    int jobs, su_is_f16, split;
+};
+void launch_prep_f16(const PrepF16Params &p, cudaStream_t s);
+
+// SwiGLU between projections, output for the tensor-core path:
+// xd = H(su_d * silu(H(g) * sv_g) * (H(u) * sv_u)), f16 * 2^kx.
+struct MidF16Params {
+    const float *acc_gate, *acc_up;  // [halves][P][I]
+    size_t half_stride;
+    const uint32_t *pos_expert;      // nullable
+    const void *sv_gate, *sv_up, *su_down;  // f16 [E][I] or int8 [I]
+    int is_f16, halves, split;
+    uint32_t inner;
+    float scale;
+    __half *xh;
+    int8_t *kx;
+    uint32_t positions;
+};
+void launch_mid_f16(const MidF16Params &p, cudaStream_t s);
+
+}  // namespace adi_cuda

@@ -97,3 +97,20 @@ def test_moe_block_tensor_cores_configured_scales(tensor_cores, oracle):
         if np.array_equal(experts[t], want_e[i]):
             assert rel_l2(out[t], want[i]) <= TC_TOL, t
     handle.release()
+
+
+@pytest.mark.parametrize("rows,cols", [(128, 128), (512, 2048), (2048, 512), (4096, 2048)])
+def test_ne_matmul_tensor_cores(tensor_cores, oracle, rows, cols):
+    """NE projections at batches that take the tensor-core path (>= 16)."""
+    ctx = tensor_cores
+    from fixtures import ne_matrix
+    rng = SplitMix64(0x5E + rows + cols)
+    m = ne_matrix(rows, cols, rng)
+    h = ctx.upload_ne(m)
+    for batch in (16, 17, 100, 200):
+        x = rng.floats(batch * cols).reshape(batch, cols)
+        got = ctx.mach_ne_matmul(h, x)
+        want = oracle.ne_matmul(m, x)
+        err = rel_l2(got, want)
+        assert err <= TC_TOL, (rows, cols, batch, err)
+    h.release()

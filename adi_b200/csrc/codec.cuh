@@ -123,3 +123,54 @@ __device__ __forceinline__ void block_fwht(float *v, uint32_t n, float scale) {
 }
 
 }  // namespace adi_cuda
+
+namespace adi_cuda {
+
+// FWHT of n = 256 * R values held R per thread by a 256-thread block: thread
+// t holds v[r] = x[t * R + r]. The same butterfly network as block_fwht, in
+// the same stride order (so bit-identical to the reference's transform):
+// strides 1 .. R/2 inside a thread's registers, R .. 16R across the warp's
+// lanes by shuffles, 32R .. 128R through `sh` (n floats). The 1/sqrt(n)
+// multiply is left to the caller. Contains __syncthreads().
+template <int R>
+__device__ __forceinline__ void fwht_regs(float (&v)[R], float *sh) {
+#pragma unroll
+    for (int s = 1; s < R; s <<= 1)
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            if ((r & s) == 0) {
+                const float a = v[r], b = v[r + s];
+                v[r] = __fadd_rn(a, b);
+                v[r + s] = __fsub_rn(a, b);
+            }
+    const uint32_t lane = threadIdx.x & 31u;
+#pragma unroll
+    for (int s = 0; s < 5; ++s) {
+        const bool upper = (lane >> s) & 1u;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[r], 1u << s);
+            v[r] = upper ? __fsub_rn(o, v[r]) : __fadd_rn(v[r], o);
+        }
+    }
+    const uint32_t n = 256u * R;
+#pragma unroll
+    for (int r = 0; r < R; ++r) sh[threadIdx.x * R + r] = v[r];
+    __syncthreads();
+#pragma unroll
+    for (int s = 0; s < 3; ++s) {
+        const uint32_t stride = (32u * R) << s;
+        for (uint32_t i = threadIdx.x; i < n / 2; i += 256) {
+            const uint32_t j = ((i & ~(stride - 1u)) << 1) | (i & (stride - 1u));
+            const float a = sh[j], b = sh[j + stride];
+            sh[j] = __fadd_rn(a, b);
+            sh[j + stride] = __fsub_rn(a, b);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = sh[threadIdx.x * R + r];
+    __syncthreads();
+}
+
+}  // namespace adi_cuda

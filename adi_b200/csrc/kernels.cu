@@ -27,6 +27,41 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// R consecutive floats (16-byte aligned when R >= 4).
+template <int R>
+__device__ __forceinline__ void load_regs(const float *src, float (&v)[R]) {
+    if constexpr (R % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < R / 4; ++i) {
+            const float4 q = reinterpret_cast<const float4 *>(src)[i];
+            v[4 * i] = q.x;
+            v[4 * i + 1] = q.y;
+            v[4 * i + 2] = q.z;
+            v[4 * i + 3] = q.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < R; ++i) v[i] = src[i];
+    }
+}
+
+template <int R>
+__device__ __forceinline__ void store_regs(float *dst, const float (&v)[R]) {
+    if constexpr (R % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < R / 4; ++i)
+            reinterpret_cast<float4 *>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < R; ++i) dst[i] = v[i];
+    }
+}
+
+__device__ __forceinline__ float scale_of(const void *base, int is_f16, size_t index) {
+    return is_f16 ? __half2float(__ushort_as_half(static_cast<const uint16_t *>(base)[index]))
+                  : (float)static_cast<const int8_t *>(base)[index];
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -179,10 +214,35 @@ __global__ void prep_kernel(PrepParams p) {
     for (uint32_t c = threadIdx.x; c < p.cols; c += blockDim.x) out[c] = v[c];
 }
 
+// Register-resident variant for cols = 256 * R (thread t owns t*R .. +R-1).
+template <int R>
+__global__ void __launch_bounds__(256) prep_regs_kernel(PrepParams p) {
+    __shared__ float sh[256 * R];
+    const uint32_t row = blockIdx.x;
+    const int job = blockIdx.y;
+    const uint32_t token = p.grouped ? p.grouped[row] : row;
+    const uint32_t expert = p.pos_expert ? p.pos_expert[row] : 0u;
+    float v[R];
+    load_regs<R>(p.input + (size_t)token * p.cols + threadIdx.x * R, v);
+    const void *su = job ? p.su[1] : p.su[0];
+    const size_t su0 = (size_t)expert * p.su_stride + threadIdx.x * R;
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = __fmul_rn(v[r], scale_of(su, p.su_is_f16, su0 + r));
+    fwht_regs<R>(v, sh);
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = __fmul_rn(v[r], p.scale);
+    store_regs<R>((job ? p.out[1] : p.out[0]) + (size_t)row * p.cols + threadIdx.x * R, v);
+}
+
 void launch_prep(const PrepParams &p, cudaStream_t s) {
     if (p.rows == 0) return;
     dim3 grid(p.rows, p.jobs);
-    prep_kernel<<<grid, 256, p.cols * sizeof(float), s>>>(p);
+    switch (p.cols) {
+        case 512: prep_regs_kernel<2><<<grid, 256, 0, s>>>(p); return;
+        case 1024: prep_regs_kernel<4><<<grid, 256, 0, s>>>(p); return;
+        case 2048: prep_regs_kernel<8><<<grid, 256, 0, s>>>(p); return;
+        default: prep_kernel<<<grid, 256, p.cols * sizeof(float), s>>>(p);
+    }
 }
 
 __global__ void finalize_kernel(const float *acc0, const float *acc1, const void *sv, int sv_is_f16,
@@ -201,10 +261,35 @@ __global__ void finalize_kernel(const float *acc0, const float *acc1, const void
     }
 }
 
+template <int R>
+__global__ void __launch_bounds__(256) finalize_regs_kernel(const float *acc0, const float *acc1, const void *sv,
+                                                            int sv_is_f16, float scale, float *out) {
+    __shared__ float sh[256 * R];
+    constexpr uint32_t rows = 256u * R;
+    const size_t base = (size_t)blockIdx.x * rows + threadIdx.x * R;
+    float v[R];
+    load_regs<R>(acc0 + base, v);
+    if (acc1) {
+        float w[R];
+        load_regs<R>(acc1 + base, w);
+#pragma unroll
+        for (int r = 0; r < R; ++r) v[r] += w[r];
+    }
+    fwht_regs<R>(v, sh);
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = __fmul_rn(__fmul_rn(v[r], scale), scale_of(sv, sv_is_f16, threadIdx.x * R + r));
+    store_regs<R>(out + base, v);
+}
+
 void launch_finalize(const float *acc0, const float *acc1, const void *sv, int sv_is_f16,
                      uint32_t batch, uint32_t rows, float scale, float *out, cudaStream_t s) {
     if (batch == 0) return;
-    finalize_kernel<<<batch, 256, rows * sizeof(float), s>>>(acc0, acc1, sv, sv_is_f16, rows, scale, out);
+    switch (rows) {
+        case 512: finalize_regs_kernel<2><<<batch, 256, 0, s>>>(acc0, acc1, sv, sv_is_f16, scale, out); return;
+        case 1024: finalize_regs_kernel<4><<<batch, 256, 0, s>>>(acc0, acc1, sv, sv_is_f16, scale, out); return;
+        case 2048: finalize_regs_kernel<8><<<batch, 256, 0, s>>>(acc0, acc1, sv, sv_is_f16, scale, out); return;
+        default: finalize_kernel<<<batch, 256, rows * sizeof(float), s>>>(acc0, acc1, sv, sv_is_f16, rows, scale, out);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -611,10 +696,83 @@ __global__ void bf16_gemm_kernel(const uint16_t *w0, uint32_t rows0, const uint1
         }
 }
 
+// Wide variant for cols % 256 == 0: a lane takes 8 consecutive columns per
+// step -- one 16-byte load of each of its warp's 4 weight rows, two 16-byte
+// shared loads per token -- for 256 FMAs per 20 memory instructions.
+__global__ void __launch_bounds__(256) bf16_gemm_wide_kernel(const uint16_t *w0, uint32_t rows0,
+                                                             const uint16_t *w1, uint32_t rows1, const float *x,
+                                                             uint32_t tokens, uint32_t cols, float *out,
+                                                             uint32_t out_stride) {
+    extern __shared__ float xs[];
+    const uint32_t t0 = blockIdx.x * 8;
+    const uint32_t nt = min(8u, tokens - t0);
+    for (uint32_t i = threadIdx.x; i < 2 * cols; i += blockDim.x) {
+        const uint32_t t = i / (cols / 4);
+        const uint32_t c4 = i % (cols / 4);
+        reinterpret_cast<float4 *>(xs)[i] = t < nt ? reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * cols)[c4]
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __syncthreads();
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t rbase = blockIdx.y * 32 + warp * 4;
+    const uint32_t R = rows0 + rows1;
+    const uint16_t *row_ptr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t r = rbase + i;
+        row_ptr[i] = r < rows0 ? w0 + (size_t)r * cols : (r < R ? w1 + (size_t)(r - rows0) * cols : nullptr);
+    }
+    float acc[4][8] = {};
+    for (uint32_t c = lane * 8; c < cols; c += 256) {
+        float xv[8][8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const float4 a = reinterpret_cast<const float4 *>(xs + t * cols + c)[0];
+            const float4 b = reinterpret_cast<const float4 *>(xs + t * cols + c)[1];
+            xv[t][0] = a.x; xv[t][1] = a.y; xv[t][2] = a.z; xv[t][3] = a.w;
+            xv[t][4] = b.x; xv[t][5] = b.y; xv[t][6] = b.z; xv[t][7] = b.w;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (!row_ptr[i]) continue;
+            const uint4 wq = __ldg(reinterpret_cast<const uint4 *>(row_ptr[i] + c));
+            const uint32_t wp[4] = {wq.x, wq.y, wq.z, wq.w};
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float wv = __uint_as_float((k & 1) ? (wp[k >> 1] & 0xFFFF0000u) : (wp[k >> 1] << 16));
+#pragma unroll
+                for (int t = 0; t < 8; ++t) acc[i][t] = fmaf(wv, xv[t][k], acc[i][t]);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const float v = warp_sum(acc[i][t]);
+            if (lane == 0 && row_ptr[i] && (uint32_t)t < nt) out[(size_t)(t0 + t) * out_stride + rbase + i] = v;
+        }
+}
+
 void launch_bf16_gemm(const uint16_t *w0, uint32_t rows0, const uint16_t *w1, uint32_t rows1,
                       const float *x, uint32_t tokens, uint32_t cols, float *out, uint32_t out_stride,
                       cudaStream_t s) {
     if (tokens == 0) return;
+    // The wide kernel needs 16-byte aligned rows: cols a multiple of 256 and
+    // both weight bases 16-byte aligned (device allocations are).
+    if (cols % 256 == 0 && (reinterpret_cast<uintptr_t>(w0) & 15u) == 0 &&
+        (rows1 == 0 || (reinterpret_cast<uintptr_t>(w1) & 15u) == 0) &&
+        (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+        static bool wide_configured = false;
+        if (!wide_configured) {
+            cudaFuncSetAttribute(bf16_gemm_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+            wide_configured = true;
+        }
+        dim3 grid((tokens + 7) / 8, (rows0 + rows1 + 31) / 32);
+        bf16_gemm_wide_kernel<<<grid, 256, 8 * cols * sizeof(float), s>>>(w0, rows0, w1, rows1, x, tokens, cols,
+                                                                           out, out_stride);
+        return;
+    }
     static bool configured = false;
     if (!configured) {
         cudaFuncSetAttribute(bf16_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -839,9 +997,48 @@ __global__ void mid_kernel(MidParams p) {
     for (uint32_t i = threadIdx.x; i < p.inner; i += blockDim.x) p.xd[base + i] = g[i];
 }
 
+template <int R>
+__global__ void __launch_bounds__(256) mid_regs_kernel(MidParams p) {
+    __shared__ float sh[256 * R];
+    const uint32_t pos = blockIdx.x;
+    const uint32_t e = p.pos_expert ? p.pos_expert[pos] : 0u;
+    const size_t base = (size_t)pos * p.inner + threadIdx.x * R;
+    float g[R], u[R];
+    load_regs<R>(p.acc_gate + base, g);
+    load_regs<R>(p.acc_up + base, u);
+    if (p.halves == 2) {
+        float g1[R], u1[R];
+        load_regs<R>(p.acc_gate + p.half_stride + base, g1);
+        load_regs<R>(p.acc_up + p.half_stride + base, u1);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            g[r] += g1[r];
+            u[r] += u1[r];
+        }
+    }
+    fwht_regs<R>(g, sh);
+    fwht_regs<R>(u, sh);
+    const size_t s0 = (p.is_f16 ? (size_t)e * p.inner : 0) + threadIdx.x * R;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const float gv = __fmul_rn(__fmul_rn(g[r], p.scale), scale_of(p.sv_gate, p.is_f16, s0 + r));
+        const float uv = __fmul_rn(__fmul_rn(u[r], p.scale), scale_of(p.sv_up, p.is_f16, s0 + r));
+        g[r] = __fmul_rn(__fmul_rn(silu_f(gv), uv), scale_of(p.su_down, p.is_f16, s0 + r));
+    }
+    fwht_regs<R>(g, sh);
+#pragma unroll
+    for (int r = 0; r < R; ++r) g[r] = __fmul_rn(g[r], p.scale);
+    store_regs<R>(p.xd + base, g);
+}
+
 void launch_mid(const MidParams &p, cudaStream_t s) {
     if (p.positions == 0) return;
-    mid_kernel<<<p.positions, 256, 2 * p.inner * sizeof(float), s>>>(p);
+    switch (p.inner) {
+        case 512: mid_regs_kernel<2><<<p.positions, 256, 0, s>>>(p); return;
+        case 1024: mid_regs_kernel<4><<<p.positions, 256, 0, s>>>(p); return;
+        case 2048: mid_regs_kernel<8><<<p.positions, 256, 0, s>>>(p); return;
+        default: mid_kernel<<<p.positions, 256, 2 * p.inner * sizeof(float), s>>>(p);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -885,10 +1082,51 @@ __global__ void combine_kernel(CombineParams p) {
     }
 }
 
+template <int R>
+__global__ void __launch_bounds__(256) combine_regs_kernel(CombineParams p) {
+    __shared__ float sh[256 * R];
+    constexpr uint32_t H = 256u * R;
+    const uint32_t t = blockIdx.x;
+    const uint32_t c0 = threadIdx.x * R;
+    float out[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) out[r] = 0.0f;
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t pos = p.route_to_grouped[t * 8 + k];
+        const uint32_t e = p.route_experts[t * 8 + k];
+        const float w = p.route_weights[t * 8 + k];
+        float v[R], v1[R];
+        load_regs<R>(p.acc_down + (size_t)pos * H + c0, v);
+        load_regs<R>(p.acc_down + p.half_stride + (size_t)pos * H + c0, v1);
+#pragma unroll
+        for (int r = 0; r < R; ++r) v[r] += v1[r];
+        fwht_regs<R>(v, sh);
+        const uint16_t *sv = p.sv_down + (size_t)e * H + c0;
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            out[r] = fmaf(w, __fmul_rn(__fmul_rn(v[r], p.scale), f16_bits_to_f32(sv[r])), out[r]);
+    }
+    float v[R];
+    load_regs<R>(p.shared_acc + (size_t)t * H + c0, v);
+    fwht_regs<R>(v, sh);
+    const float gate = sigmoid_f(p.gate_logits[(size_t)t * p.gate_stride]);
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+        out[r] = fmaf(gate, __fmul_rn(__fmul_rn(v[r], p.scale), (float)p.shared_sv[c0 + r]), out[r]);
+    store_regs<R>(p.out + (size_t)t * H + c0, out);
+}
+
 void launch_combine(const CombineParams &p, cudaStream_t s) {
     if (p.tokens == 0) return;
-    const uint32_t threads = (p.hidden + 7) / 8;  // kPer elements per thread
-    combine_kernel<<<p.tokens, threads < 32 ? 32 : threads, p.hidden * sizeof(float), s>>>(p);
+    switch (p.hidden) {
+        case 512: combine_regs_kernel<2><<<p.tokens, 256, 0, s>>>(p); return;
+        case 1024: combine_regs_kernel<4><<<p.tokens, 256, 0, s>>>(p); return;
+        case 2048: combine_regs_kernel<8><<<p.tokens, 256, 0, s>>>(p); return;
+        default: {
+            const uint32_t threads = (p.hidden + 7) / 8;  // kPer elements per thread
+            combine_kernel<<<p.tokens, threads < 32 ? 32 : threads, p.hidden * sizeof(float), s>>>(p);
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -986,9 +1224,25 @@ __global__ void hadamard_kernel(float *values, uint32_t n, float scale) {
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) row[i] = v[i];
 }
 
+template <int R>
+__global__ void __launch_bounds__(256) hadamard_regs_kernel(float *values, float scale) {
+    __shared__ float sh[256 * R];
+    float *row = values + (size_t)blockIdx.x * (256u * R) + threadIdx.x * R;
+    float v[R];
+    load_regs<R>(row, v);
+    fwht_regs<R>(v, sh);
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = __fmul_rn(v[r], scale);
+    store_regs<R>(row, v);
+}
+
 void launch_hadamard(float *values, uint32_t count, uint32_t n, float scale, cudaStream_t s) {
     if (count == 0) return;
-    hadamard_kernel<<<count, 256, n * sizeof(float), s>>>(values, n, scale);
+    switch (n) {
+        case 512: hadamard_regs_kernel<2><<<count, 256, 0, s>>>(values, scale); return;
+        case 2048: hadamard_regs_kernel<8><<<count, 256, 0, s>>>(values, scale); return;
+        default: hadamard_kernel<<<count, 256, n * sizeof(float), s>>>(values, n, scale);
+    }
 }
 
 __global__ void rms_norm_kernel(const float *x, const uint16_t *w, uint32_t n, float offset, float eps,

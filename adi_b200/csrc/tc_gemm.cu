@@ -50,7 +50,6 @@ constexpr uint32_t kTcThreads = 14 * 32;
 constexpr uint32_t kTmemColumns = 2 * kTcMaxN;
 
 struct Smem {
-    static constexpr size_t table = 0;
     static constexpr size_t a = 131072;  // 1024-aligned
     static constexpr size_t b = a + kAStages * kATileBytes;
     static constexpr size_t words = b + kBStages * kBTileBytes;
@@ -645,16 +644,120 @@ __global__ void mid_f16_kernel(MidF16Params p) {
     write_f16(g, p.inner, k, p.split != 0, p.xh, (size_t)p.positions * (p.inner / 2), pos);
 }
 
+// Register-resident versions for lengths 256 * R: thread t owns elements
+// t*R .. t*R+R-1 from the load to the store.
+template <int R>
+__device__ __forceinline__ float block_max_abs_regs(const float (&v)[R], float *scratch) {
+    float m = 0.0f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) m = fmaxf(m, fabsf(v[r]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31u) == 0) scratch[threadIdx.x >> 5] = m;
+    __syncthreads();
+    float w = scratch[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) w = fmaxf(w, scratch[i]);
+    __syncthreads();
+    return w;
+}
+
+template <int R>
+__device__ __forceinline__ void write_f16_regs(const float (&v)[R], int k, bool split, __half *out,
+                                               size_t half_stride, uint32_t row) {
+    constexpr uint32_t n = 256u * R;
+    const float s = exp2f((float)k);
+    if (split) {
+        // element i = t*R + r -> half (i >> 2) & 1, packed column 4(i >> 3) + (i & 3)
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const uint32_t i = threadIdx.x * R + r;
+            const uint32_t h = (i >> 2) & 1u;
+            out[h * half_stride + (size_t)row * (n / 2) + 4 * (i >> 3) + (i & 3u)] = __float2half_rn(v[r] * s);
+        }
+    } else {
+#pragma unroll
+        for (int r = 0; r < R; ++r) out[(size_t)row * n + threadIdx.x * R + r] = __float2half_rn(v[r] * s);
+    }
+}
+
+template <int R>
+__global__ void __launch_bounds__(256) prep_f16_regs_kernel(PrepF16Params p) {
+    __shared__ float sh[256 * R];
+    __shared__ float scratch[32];
+    const uint32_t row = blockIdx.x;
+    const int job = blockIdx.y;
+    const uint32_t token = p.grouped ? p.grouped[row] : row;
+    const uint32_t expert = p.pos_expert ? p.pos_expert[row] : 0u;
+    const float *x = p.input + (size_t)token * p.cols + threadIdx.x * R;
+    const void *su = job ? p.su[1] : p.su[0];
+    const size_t su0 = (size_t)expert * p.su_stride + threadIdx.x * R;
+    float v[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = __fmul_rn(x[r], scale_value(su, p.su_is_f16, su0 + r));
+    fwht_regs<R>(v, sh);
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = __fmul_rn(v[r], p.scale);
+    const int k = scale_exponent(block_max_abs_regs<R>(v, scratch));
+    if (threadIdx.x == 0) (job ? p.kx[1] : p.kx[0])[row] = (int8_t)k;
+    write_f16_regs<R>(v, k, p.split != 0, job ? p.xh[1] : p.xh[0], (size_t)p.rows * (p.cols / 2), row);
+}
+
+template <int R>
+__global__ void __launch_bounds__(256) mid_f16_regs_kernel(MidF16Params p) {
+    __shared__ float sh[256 * R];
+    __shared__ float scratch[32];
+    const uint32_t pos = blockIdx.x;
+    const uint32_t e = p.pos_expert ? p.pos_expert[pos] : 0u;
+    const size_t base = (size_t)pos * p.inner + threadIdx.x * R;
+    float g[R], u[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        g[r] = p.acc_gate[base + r];
+        u[r] = p.acc_up[base + r];
+        if (p.halves == 2) {
+            g[r] += p.acc_gate[p.half_stride + base + r];
+            u[r] += p.acc_up[p.half_stride + base + r];
+        }
+    }
+    fwht_regs<R>(g, sh);
+    fwht_regs<R>(u, sh);
+    const size_t s0 = (p.is_f16 ? (size_t)e * p.inner : 0) + threadIdx.x * R;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const float gv = __fmul_rn(__fmul_rn(g[r], p.scale), scale_value(p.sv_gate, p.is_f16, s0 + r));
+        const float uv = __fmul_rn(__fmul_rn(u[r], p.scale), scale_value(p.sv_up, p.is_f16, s0 + r));
+        g[r] = __fmul_rn(__fmul_rn(silu_f(gv), uv), scale_value(p.su_down, p.is_f16, s0 + r));
+    }
+    fwht_regs<R>(g, sh);
+#pragma unroll
+    for (int r = 0; r < R; ++r) g[r] = __fmul_rn(g[r], p.scale);
+    const int k = scale_exponent(block_max_abs_regs<R>(g, scratch));
+    if (threadIdx.x == 0) p.kx[pos] = (int8_t)k;
+    write_f16_regs<R>(g, k, p.split != 0, p.xh, (size_t)p.positions * (p.inner / 2), pos);
+}
+
 }  // namespace
 
 void launch_prep_f16(const PrepF16Params &p, cudaStream_t s) {
     if (p.rows == 0) return;
-    prep_f16_kernel<<<dim3(p.rows, p.jobs), 256, p.cols * sizeof(float), s>>>(p);
+    const dim3 grid(p.rows, p.jobs);
+    switch (p.cols) {
+        case 512: prep_f16_regs_kernel<2><<<grid, 256, 0, s>>>(p); return;
+        case 1024: prep_f16_regs_kernel<4><<<grid, 256, 0, s>>>(p); return;
+        case 2048: prep_f16_regs_kernel<8><<<grid, 256, 0, s>>>(p); return;
+        default: prep_f16_kernel<<<grid, 256, p.cols * sizeof(float), s>>>(p);
+    }
 }
 
 void launch_mid_f16(const MidF16Params &p, cudaStream_t s) {
     if (p.positions == 0) return;
-    mid_f16_kernel<<<p.positions, 256, 2 * p.inner * sizeof(float), s>>>(p);
+    switch (p.inner) {
+        case 512: mid_f16_regs_kernel<2><<<p.positions, 256, 0, s>>>(p); return;
+        case 1024: mid_f16_regs_kernel<4><<<p.positions, 256, 0, s>>>(p); return;
+        case 2048: mid_f16_regs_kernel<8><<<p.positions, 256, 0, s>>>(p); return;
+        default: mid_f16_kernel<<<p.positions, 256, 2 * p.inner * sizeof(float), s>>>(p);
+    }
 }
 
 }  // namespace adi_cuda

@@ -17,13 +17,13 @@
 // pair table, replicated once per bank (128 KiB), so every gather of a warp
 // is conflict-free; a CTA contracts the full K.
 //
-// Warp roles (448 threads, one persistent CTA per SM):
+// Warp roles (704 threads, one persistent CTA per SM):
 //   warp 0 lane 0   trellis words of each K-chunk -> 6-deep ring (bulk copies)
 //   warp 0 lane 1   B chunk (64 f16 x 128 rows, 128B-swizzled) -> 2-deep ring (TMA)
 //   warp 1          TMEM allocation; lane 0 issues the MMAs
-//   warps 2..9      decoders: state -> values -> f16 into A's swizzled K-major
+//   warps 2..17     decoders: state -> values -> f16 into A's swizzled K-major
 //                   layout, 2-deep ring
-//   warps 10..13    epilogue: tcgen05.ld, scale, fp32 out; 2 accumulators
+//   warps 18..21    epilogue: tcgen05.ld, scale, fp32 out; 2 accumulators
 //
 // Every wait is bounded (pipeline.cuh). When one expires the launch drains
 // without touching data, the MMA lane waits (bounded) for its own MMAs, the
@@ -45,8 +45,9 @@ constexpr uint32_t kChunkK = 64;                     // f16 columns of A and B p
 constexpr uint32_t kATileBytes = 128 * kChunkK * 2;  // 16 KiB
 constexpr uint32_t kBTileBytes = kTcMaxN * kChunkK * 2;
 constexpr uint32_t kWordSlotBytes = 4096;            // expert 3 KiB, NE 4 KiB per chunk
-constexpr uint32_t kDecodeWarps = 8;
-constexpr uint32_t kTcThreads = 14 * 32;
+constexpr uint32_t kDecodeWarps = 16;
+constexpr uint32_t kEpilogueWarp0 = 2 + kDecodeWarps;
+constexpr uint32_t kTcThreads = (kEpilogueWarp0 + 4) * 32;
 constexpr uint32_t kTmemColumns = 2 * kTcMaxN;
 
 struct Smem {
@@ -345,33 +346,39 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t q = (lane * 12u) >> 5;
             const uint32_t q1 = q + 1u == kExpertU32PerTile ? 0u : q + 1u;
             const uint32_t neg_mask = half == 0 ? 0x8000u : 0u;
-            // Warp dw decodes tile column dw of each chunk, tile rows 0..7; a
-            // lane owns state `lane` (tile row lr, columns step*8 + 4h ..).
-            const uint32_t a_lane = lr * 128 + (((dw ^ (lr & 7u)) << 4) | (step << 3));
+            // Warp dw decodes tile column tcl = dw & 7 of each chunk, tile rows
+            // j0 .. j0+3 (j0 = (dw >> 3) * 4); a lane owns state `lane` (tile
+            // row lr, columns step*8 + 4h ..).
+            const uint32_t tcl = dw & 7u, j0 = (dw >> 3) * 4;
+            const uint32_t a_lane = (j0 * 16 + lr) * 128 + (((tcl ^ (lr & 7u)) << 4) | (step << 3));
+            // Lane i < 4 holds the f16x2 gamma of tile row j0 + i; fetched one
+            // chunk ahead so the load's latency hides behind a chunk of work.
+            auto fetch_gamma = [&](const Unit &un, const TcJob &J, uint32_t kc, float gscale) -> uint32_t {
+                if (lane >= 4) return 0u;
+                const uint32_t TC = J.cols / 16, TR = J.rows / 16;
+                const uint32_t diag = un.m_block * 8 + j0 + lane + kc * 8 + tcl;
+                const uint16_t *gam = J.gamma + (size_t)un.expert * J.gamma_stride;
+                const __half2 g2 =
+                    __float2half2_rn(__half2float(__ushort_as_half(__ldg(gam + wave_index(TR, TC, diag)))) * gscale);
+                return *reinterpret_cast<const uint32_t *>(&g2);
+            };
             for (uint32_t u = first; u < n_units; u += stride) {
                 const Unit un = unit_at(p, u);
                 const TcJob &J = un.job ? p.job[1] : p.job[0];
-                const uint32_t TC = J.cols / 16, TR = J.rows / 16;
                 const uint32_t chunks = J.cols / T::chunk_cols;
-                const uint16_t *gam = J.gamma + (size_t)un.expert * J.gamma_stride;
                 const float gscale = exp2f((float)J.ka[un.expert]);
+                uint32_t gnext = fetch_gamma(un, J, 0, gscale);
                 for (uint32_t kc = 0; kc < chunks; ++kc) {
+                    const uint32_t gpack = gnext;
+                    if (kc + 1 < chunks) gnext = fetch_gamma(un, J, kc + 1, gscale);
                     if (ok) ok = mbar_wait(&w_full[w.slot], w.phase, p.error);
                     if (ok) ok = mbar_wait(&a_empty[a.slot], a.phase ^ 1u, p.error);
                     if (ok) {
-                        // Lane j < 8 fetches tile row j's gamma; shuffled out below.
-                        uint32_t gpack = 0;
-                        if (lane < 8) {
-                            const uint32_t diag = un.m_block * 8 + lane + kc * 8 + dw;
-                            const float g = __half2float(__ushort_as_half(__ldg(gam + wave_index(TR, TC, diag))));
-                            const __half2 g2 = __float2half2_rn(g * gscale);
-                            gpack = *reinterpret_cast<const uint32_t *>(&g2);
-                        }
                         const uint32_t *tw = reinterpret_cast<const uint32_t *>(word_tiles + w.slot * kWordSlotBytes) +
-                                             dw * kExpertU32PerTile;
+                                             j0 * 96 + tcl * kExpertU32PerTile;
                         uint8_t *a_tile = a_tiles + a.slot * kATileBytes + a_lane;
 #pragma unroll
-                        for (uint32_t j = 0; j < 8; ++j) {
+                        for (uint32_t j = 0; j < 4; ++j) {
                             const uint32_t state =
                                 expert_window(stream_order(tw[j * 96 + q]), stream_order(tw[j * 96 + q1]), lane);
                             const uint32_t prod = state_product(state);
@@ -411,12 +418,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     if (ok) ok = mbar_wait(&w_full[w.slot], w.phase, p.error);
                     if (ok) ok = mbar_wait(&a_empty[a.slot], a.phase ^ 1u, p.error);
                     if (ok) {
-                        // Warp dw decodes tile row dw: its four tiles j = 0..3.
+                        // Warp dw decodes tile row dw & 7: tiles j = 2 (dw >> 3) and the next.
+                        const uint32_t trl = dw & 7u;
                         const uint32_t *tw =
-                            reinterpret_cast<const uint32_t *>(word_tiles + w.slot * kWordSlotBytes) + dw * 128;
-                        uint8_t *a_row = a_tiles + a.slot * kATileBytes + dw * 2048 + r * 128;
+                            reinterpret_cast<const uint32_t *>(word_tiles + w.slot * kWordSlotBytes) + trl * 128;
+                        uint8_t *a_row = a_tiles + a.slot * kATileBytes + trl * 2048 + r * 128;
 #pragma unroll
-                        for (uint32_t j = 0; j < 4; ++j) {
+                        for (uint32_t j = (dw >> 3) * 2; j < (dw >> 3) * 2 + 2; ++j) {
                             const uint32_t wv = tw[j * 32 + lane];
                             const uint32_t v = __shfl_sync(0xffffffffu, wv, src);
                             const uint32_t v2 = __shfl_sync(0xffffffffu, wv, src1);
@@ -457,15 +465,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     C == TcCodec::kExpert ? exp2f((float)-J.ka[un.expert]) : J.out_scale;
                 float *out = J.acc + half * J.half_stride + un.m_block * 128 + row_local;
                 for (uint32_t c0 = 0; c0 < n_pad; c0 += 16) {
+                    // Lane i < 16 computes column c0 + i's unscale once.
+                    const uint32_t ni = c0 + (lane & 15u);
+                    const float mine = ni < un.count ? base_scale * exp2f((float)-J.kx[un.pos0 + ni]) : 0.0f;
                     float v[16];
                     tmem_ld16(tmem_base + ((quarter * 32) << 16) + d.slot * kTcMaxN + c0, v);
 #pragma unroll
                     for (uint32_t i = 0; i < 16; ++i) {
-                        const uint32_t n = c0 + i;
-                        if (n < un.count) {
-                            const uint32_t pos = un.pos0 + n;
-                            out[(size_t)pos * J.rows] = v[i] * base_scale * exp2f((float)-J.kx[pos]);
-                        }
+                        const float sc = __shfl_sync(0xffffffffu, mine, i);
+                        if (c0 + i < un.count) out[(size_t)(un.pos0 + c0 + i) * J.rows] = v[i] * sc;
                     }
                 }
             }

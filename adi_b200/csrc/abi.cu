@@ -228,7 +228,7 @@ struct Profiler {
         check(cudaEventRecord(e, s), "cudaEventRecord");
         pending.push_back({open_stage, open_event, e});
         open_stage = -1;
-        if (pending.size() > 8192) collect();
+        if (pending.size() > (1u << 20)) collect();
     }
     void collect() {
         for (auto &p : pending) {

@@ -18,11 +18,12 @@
 // is conflict-free; a CTA contracts the full K.
 //
 // Warp roles (704 threads, one persistent CTA per SM):
-//   warp 0 lane 0   trellis words of each K-chunk -> 6-deep ring (bulk copies)
-//   warp 0 lane 1   B chunk (64 f16 x 128 rows, 128B-swizzled) -> 2-deep ring (TMA)
+//   warp 0 lane 0   trellis words of each K-chunk -> 4-deep ring (bulk copies)
+//   warp 0 lane 1   B chunk (64 f16 x the unit's rows in 16-row boxes,
+//                   128B-swizzled) -> 2-deep ring (TMA)
 //   warp 1          TMEM allocation; lane 0 issues the MMAs
 //   warps 2..17     decoders: state -> values -> f16 into A's swizzled K-major
-//                   layout, 2-deep ring
+//                   layout, 3-deep ring
 //   warps 18..21    epilogue: tcgen05.ld, scale, fp32 out; 2 accumulators
 //
 // Every wait is bounded (pipeline.cuh). When one expires the launch drains
@@ -38,9 +39,10 @@
 namespace adi_cuda {
 namespace {
 
-constexpr uint32_t kWordStages = 6;
+constexpr uint32_t kWordStages = 4;
 constexpr uint32_t kBStages = 2;
-constexpr uint32_t kAStages = 2;
+constexpr uint32_t kAStages = 3;
+constexpr uint32_t kBBoxRows = 16;                    // TMA box height: B loads only the unit's rows
 constexpr uint32_t kChunkK = 64;                     // f16 columns of A and B per chunk
 constexpr uint32_t kATileBytes = 128 * kChunkK * 2;  // 16 KiB
 constexpr uint32_t kBTileBytes = kTcMaxN * kChunkK * 2;
@@ -284,9 +286,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&b_full[r.slot], kBTileBytes);
-                    tma_load_2d(b_tiles + r.slot * kBTileBytes, map, (int32_t)(kc * kChunkK),
-                                (int32_t)(half * J.positions + un.pos0), &b_full[r.slot]);
+                    const uint32_t n_pad = (un.count + kBBoxRows - 1) & ~(kBBoxRows - 1);
+                    mbar_arrive_expect_tx(&b_full[r.slot], n_pad * kChunkK * 2);
+                    for (uint32_t r0 = 0; r0 < n_pad; r0 += kBBoxRows)
+                        tma_load_2d(b_tiles + r.slot * kBTileBytes + r0 * kChunkK * 2, map, (int32_t)(kc * kChunkK),
+                                    (int32_t)(half * J.positions + un.pos0 + r0), &b_full[r.slot]);
                     ++issued;
                     r.advance(kBStages);
                 }
@@ -532,7 +536,7 @@ bool make_b_map(CUtensorMap *map, const __half *x, uint32_t rows, uint32_t cols)
     if (!fn) return false;
     const cuuint64_t dims[2] = {cols, rows};
     const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {kChunkK, kTcMaxN};
+    const cuuint32_t box[2] = {kChunkK, kBBoxRows};
     const cuuint32_t elem[2] = {1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(x), dims, strides, box, elem,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -40,7 +40,7 @@ struct TcParams {
     uint32_t *error;     // device error word
 };
 
-// B operand map over x [rows][cols] f16: boxes of 64 columns x kTcMaxN rows,
+// B operand map over x [rows][cols] f16: boxes of 64 columns x 16 rows,
 // 128-byte swizzle.
 bool make_b_map(CUtensorMap *map, const __half *x, uint32_t rows, uint32_t cols);
 void launch_tc_gemm(TcCodec codec, const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid,

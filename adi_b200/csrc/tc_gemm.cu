@@ -20,7 +20,8 @@
 // Warp roles (704 threads, one persistent CTA per SM):
 //   warp 0 lane 0   trellis words of each K-chunk -> 4-deep ring (bulk copies)
 //   warp 0 lane 1   B chunk (64 f16 x the unit's rows in 16-row boxes,
-//                   128B-swizzled) -> 2-deep ring (TMA)
+//                   128B-swizzled) -> 4-deep ring (TMA; deep because a B
+//                   chunk's L2 latency spans more than two chunks of decode)
 //   warp 1          TMEM allocation; lane 0 issues the MMAs
 //   warps 2..17     decoders: state -> values -> f16 into A's swizzled K-major
 //                   layout, 3-deep ring
@@ -40,7 +41,7 @@ namespace adi_cuda {
 namespace {
 
 constexpr uint32_t kWordStages = 4;
-constexpr uint32_t kBStages = 2;
+constexpr uint32_t kBStages = 4;
 constexpr uint32_t kAStages = 3;
 constexpr uint32_t kBBoxRows = 16;                    // TMA box height: B loads only the unit's rows
 constexpr uint32_t kChunkK = 64;                     // f16 columns of A and B per chunk

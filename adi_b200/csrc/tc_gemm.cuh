@@ -9,7 +9,7 @@
 
 namespace adi_cuda {
 
-constexpr uint32_t kTcMaxN = 128;  // positions per work unit (MMA N)
+constexpr uint32_t kTcMaxN = 64;  // positions per work unit (MMA N)
 
 enum class TcCodec { kExpert, kNe };
 

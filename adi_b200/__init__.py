@@ -21,7 +21,10 @@ from typing import Optional
 
 import numpy as np
 
-LIBRARY = Path(__file__).resolve().parent / "libadi_cuda.so"
+import os
+
+# ADI_CUDA_LIBRARY points at another build of the same library (tuning runs).
+LIBRARY = Path(os.environ.get("ADI_CUDA_LIBRARY", Path(__file__).resolve().parent / "libadi_cuda.so"))
 
 u8p = C.POINTER(C.c_uint8)
 u16p = C.POINTER(C.c_uint16)

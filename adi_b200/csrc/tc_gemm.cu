@@ -17,15 +17,15 @@
 // pair table, replicated once per bank (128 KiB), so every gather of a warp
 // is conflict-free; a CTA contracts the full K.
 //
-// Warp roles (704 threads, one persistent CTA per SM):
-//   warp 0 lane 0   trellis words of each K-chunk -> 4-deep ring (bulk copies)
-//   warp 0 lane 1   B chunk (64 f16 x the unit's rows in 16-row boxes,
-//                   128B-swizzled) -> 4-deep ring (TMA; deep because a B
-//                   chunk's L2 latency spans more than two chunks of decode)
+// Warp roles (736 threads, one persistent CTA per SM):
+//   warp 0 lane 0   trellis words of each K-chunk -> word ring (bulk copies)
 //   warp 1          TMEM allocation; lane 0 issues the MMAs
-//   warps 2..17     decoders: state -> values -> f16 into A's swizzled K-major
-//                   layout, 3-deep ring
-//   warps 18..21    epilogue: tcgen05.ld, scale, fp32 out; 2 accumulators
+//   warp 2 lane 0   B chunk (64 f16 x the unit's rows in 16-row boxes,
+//                   128B-swizzled) -> B ring (TMA), in its own warp so that
+//                   neither producer's waits hold up the other's issue
+//   warps 3..18     decoders: state -> values -> f16 into A's swizzled K-major
+//                   layout, A ring
+//   warps 19..22    epilogue: tcgen05.ld, scale, fp32 out; 2 accumulators
 //
 // Every wait is bounded (pipeline.cuh). When one expires the launch drains
 // without touching data, the MMA lane waits (bounded) for its own MMAs, the
@@ -40,16 +40,27 @@
 namespace adi_cuda {
 namespace {
 
-constexpr uint32_t kWordStages = 4;
-constexpr uint32_t kBStages = 4;
-constexpr uint32_t kAStages = 3;
+// Ring depths (overridable at build time for tuning sweeps).
+#ifndef ADI_TC_WORD_STAGES
+#define ADI_TC_WORD_STAGES 5
+#endif
+#ifndef ADI_TC_B_STAGES
+#define ADI_TC_B_STAGES 3
+#endif
+#ifndef ADI_TC_A_STAGES
+#define ADI_TC_A_STAGES 3
+#endif
+constexpr uint32_t kWordStages = ADI_TC_WORD_STAGES;
+constexpr uint32_t kBStages = ADI_TC_B_STAGES;
+constexpr uint32_t kAStages = ADI_TC_A_STAGES;
 constexpr uint32_t kBBoxRows = 16;                    // TMA box height: B loads only the unit's rows
 constexpr uint32_t kChunkK = 64;                     // f16 columns of A and B per chunk
 constexpr uint32_t kATileBytes = 128 * kChunkK * 2;  // 16 KiB
 constexpr uint32_t kBTileBytes = kTcMaxN * kChunkK * 2;
 constexpr uint32_t kWordSlotBytes = 4096;            // expert 3 KiB, NE 4 KiB per chunk
 constexpr uint32_t kDecodeWarps = 16;
-constexpr uint32_t kEpilogueWarp0 = 2 + kDecodeWarps;
+constexpr uint32_t kDecodeWarp0 = 3;
+constexpr uint32_t kEpilogueWarp0 = kDecodeWarp0 + kDecodeWarps;
 constexpr uint32_t kTcThreads = (kEpilogueWarp0 + 4) * 32;
 constexpr uint32_t kTmemColumns = 2 * kTcMaxN;
 
@@ -272,8 +283,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (r.slot == kWordStages - 1) r.phase ^= 1u;
                 mbar_wait_own(&w_full[r.slot], r.phase, p.error);
             }
-        } else if (lane == 1) {
-            // ---- B chunks by TMA, 2 ahead ----
+        }
+    } else if (warp == 2) {
+        if (lane == 0) {
+            // ---- B chunks by TMA ----
             Ring r;
             uint32_t issued = 0;
             bool ok = true;
@@ -340,9 +353,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mma_commit(mma_done);
             mbar_wait_own(mma_done, 0, p.error);
         }
-    } else if (warp < 2 + kDecodeWarps) {
+    } else if (warp < kEpilogueWarp0) {
         // ---- decoders ----
-        const uint32_t dw = warp - 2;
+        const uint32_t dw = warp - kDecodeWarp0;
         Ring w, a;
         bool ok = true;
         if (C == TcCodec::kExpert) {

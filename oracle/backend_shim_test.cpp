@@ -93,8 +93,19 @@ std::vector<float> inputs(std::size_t n) {
 
 } // namespace
 
+int run(double tol);
+
 int main(int argc, char **argv) {
-    const double tol = argc > 1 ? std::atof(argv[1]) : 1e-3;
+    std::setvbuf(stdout, nullptr, _IONBF, 0);
+    try {
+        return run(argc > 1 ? std::atof(argv[1]) : 1e-3);
+    } catch (const std::exception &error) {
+        std::printf("uncaught exception: %s\n", error.what());
+        return 1;
+    }
+}
+
+int run(double tol) {
     const adi::Backend &cpu = adi::cpu_backend();
     const adi::Backend &gpu = adi::cuda_backend();
     if (gpu.name != "cuda-sm100a" || !gpu.expert_matvec || !gpu.expert_matmul || !gpu.ne_matvec || !gpu.ne_matmul ||
@@ -107,6 +118,7 @@ int main(int argc, char **argv) {
 
     for (auto [rows, cols] : {std::pair<std::uint32_t, std::uint32_t>{512, 2048}, {2048, 512}, {64, 32}}) {
         Expert e = make_expert(rows, cols);
+        std::printf("expert %ux%u\n", rows, cols);
         for (std::uint32_t batch : {1u, 5u, 33u}) {
             auto x = inputs(static_cast<std::size_t>(batch) * cols);
             std::vector<float> want(static_cast<std::size_t>(batch) * rows), got(want.size());
@@ -124,6 +136,7 @@ int main(int argc, char **argv) {
     }
     for (auto [rows, cols] : {std::pair<std::uint32_t, std::uint32_t>{512, 2048}, {4096, 2048}, {2048, 512}}) {
         Ne n = make_ne(rows, cols);
+        std::printf("ne %ux%u\n", rows, cols);
         for (std::uint32_t batch : {1u, 7u, 40u}) {
             auto x = inputs(static_cast<std::size_t>(batch) * cols);
             std::vector<float> want(static_cast<std::size_t>(batch) * rows), got(want.size());

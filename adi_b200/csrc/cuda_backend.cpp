@@ -12,6 +12,7 @@
 #include "adi_cuda.h"
 
 #include <cstdlib>
+#include <functional>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -21,10 +22,33 @@
 namespace adi {
 namespace {
 
+// Uploaded matrices are found again by (kind, address, rows, columns). The
+// views MachModel hands out point into its immutable mapping for the life of
+// the process, so a view seen again is the same matrix; the shape in the key
+// means a different matrix at a reused address can never be given another
+// matrix's handle (the handle's shape sizes the device copies).
+struct MatrixKey {
+    int kind;
+    const void *data;
+    std::uint32_t rows, columns;
+    bool operator==(const MatrixKey &o) const {
+        return kind == o.kind && data == o.data && rows == o.rows && columns == o.columns;
+    }
+};
+
+struct MatrixKeyHash {
+    std::size_t operator()(const MatrixKey &k) const {
+        return std::hash<const void *>()(k.data) ^ (std::size_t(k.rows) << 20) ^ (std::size_t(k.columns) << 40) ^
+               std::size_t(k.kind);
+    }
+};
+
+enum MatrixKind { kExpertMatrix, kNeMatrix, kHeadMatrix, kBf16Matrix };
+
 struct Device {
     adi_cuda_context *context = nullptr;
     std::mutex lock;
-    std::unordered_map<const void *, adi_cuda_handle> matrices;
+    std::unordered_map<MatrixKey, adi_cuda_handle, MatrixKeyHash> matrices;
     std::unordered_map<std::uint64_t, adi_cuda_handle> layers;
 };
 
@@ -66,7 +90,8 @@ adi_ne_matrix view(const MachNeMatrix &m) {
 bool is_power_of_two(std::uint32_t v) { return v != 0 && (v & (v - 1)) == 0; }
 
 adi_cuda_handle expert_handle(Device &d, const MachExpertMatrix &m) {
-    auto it = d.matrices.find(m.trellis.data());
+    const MatrixKey key{kExpertMatrix, m.trellis.data(), m.rows, m.columns};
+    auto it = d.matrices.find(key);
     if (it != d.matrices.end()) return it->second;
     const auto tiles = static_cast<std::size_t>(m.rows / 16) * (m.columns / 16);
     if (m.trellis.size() != tiles * 24 || m.wave_gamma_f16.size() != m.rows / 16 + m.columns / 16 ||
@@ -75,12 +100,13 @@ adi_cuda_handle expert_handle(Device &d, const MachExpertMatrix &m) {
     const auto desc = view(m);
     adi_cuda_handle h = 0;
     check(adi_cuda_upload_expert(d.context, &desc, &h), "upload expert");
-    d.matrices.emplace(m.trellis.data(), h);
+    d.matrices.emplace(key, h);
     return h;
 }
 
 adi_cuda_handle ne_handle(Device &d, const MachNeMatrix &m) {
-    auto it = d.matrices.find(m.trellis.data());
+    const MatrixKey key{kNeMatrix, m.trellis.data(), m.rows, m.columns};
+    auto it = d.matrices.find(key);
     if (it != d.matrices.end()) return it->second;
     const auto tiles = static_cast<std::size_t>(m.rows / 16) * (m.columns / 16);
     if (m.trellis.size() != tiles * 64 || m.tlut.size() != 512 * 2)
@@ -88,7 +114,7 @@ adi_cuda_handle ne_handle(Device &d, const MachNeMatrix &m) {
     const auto desc = view(m);
     adi_cuda_handle h = 0;
     check(adi_cuda_upload_ne(d.context, &desc, &h), "upload NE");
-    d.matrices.emplace(m.trellis.data(), h);
+    d.matrices.emplace(key, h);
     return h;
 }
 
@@ -142,7 +168,8 @@ void head_matmul(const MachHeadChunk &head, std::span<const float> inputs, std::
         throw std::invalid_argument("Mach output head batch shape mismatch");
     auto &d = device();
     std::lock_guard<std::mutex> guard(d.lock);
-    auto it = d.matrices.find(head.packed.data());
+    const MatrixKey key{kHeadMatrix, head.packed.data(), head.rows, head.columns};
+    auto it = d.matrices.find(key);
     adi_cuda_handle h = 0;
     if (it == d.matrices.end()) {
         const adi_head_chunk desc{head.rows,
@@ -153,7 +180,7 @@ void head_matmul(const MachHeadChunk &head, std::span<const float> inputs, std::
                                   static_cast<std::uint32_t>(head.protected_rows.size()),
                                   head.protected_bf16.data()};
         check(adi_cuda_upload_head(d.context, &desc, &h), "upload head");
-        d.matrices.emplace(head.packed.data(), h);
+        d.matrices.emplace(key, h);
     } else {
         h = it->second;
     }
@@ -172,12 +199,13 @@ void dense_matmul(const Bf16Matrix &m, std::span<const float> inputs, std::uint3
         throw std::invalid_argument("BF16 matrix batch shape mismatch");
     auto &d = device();
     std::lock_guard<std::mutex> guard(d.lock);
-    auto it = d.matrices.find(m.values.data());
+    const MatrixKey key{kBf16Matrix, m.values.data(), m.rows, m.columns};
+    auto it = d.matrices.find(key);
     adi_cuda_handle h = 0;
     if (it == d.matrices.end()) {
         const adi_bf16_matrix desc{m.rows, m.columns, m.values.data()};
         check(adi_cuda_upload_bf16(d.context, &desc, &h), "upload bf16");
-        d.matrices.emplace(m.values.data(), h);
+        d.matrices.emplace(key, h);
     } else {
         h = it->second;
     }

@@ -115,9 +115,17 @@ int run(double tol) {
         return 1;
     }
     adi::ExpertScratch scratch;
+    // Every matrix stays alive to the end: views are immutable for the life
+    // of the process, as MachModel's are.
+    static std::vector<Expert> experts;
+    static std::vector<Ne> nes;
+    experts.reserve(8);
+    nes.reserve(8);
 
     for (auto [rows, cols] : {std::pair<std::uint32_t, std::uint32_t>{512, 2048}, {2048, 512}, {64, 32}}) {
-        Expert e = make_expert(rows, cols);
+        experts.push_back(make_expert(rows, cols));
+        Expert &e = experts.back();
+        e.view = {rows, cols, e.trellis, e.su, e.sv, e.gamma, e.tlut};
         std::printf("expert %ux%u\n", rows, cols);
         for (std::uint32_t batch : {1u, 5u, 33u}) {
             auto x = inputs(static_cast<std::size_t>(batch) * cols);
@@ -135,7 +143,9 @@ int run(double tol) {
         expect_close("expert_matvec", got, want, tol);
     }
     for (auto [rows, cols] : {std::pair<std::uint32_t, std::uint32_t>{512, 2048}, {4096, 2048}, {2048, 512}}) {
-        Ne n = make_ne(rows, cols);
+        nes.push_back(make_ne(rows, cols));
+        Ne &n = nes.back();
+        n.view = {rows, cols, n.trellis, n.su, n.sv, 0.0234375F, n.tlut};
         std::printf("ne %ux%u\n", rows, cols);
         for (std::uint32_t batch : {1u, 7u, 40u}) {
             auto x = inputs(static_cast<std::size_t>(batch) * cols);
@@ -178,10 +188,21 @@ int run(double tol) {
         gpu.head_matmul(head, x, 3, got);
         expect_close("head_matmul 1000x2048 batch 3", got, want, 1e-4);
     }
+    // A different matrix at a reused address gets its own upload.
+    for (int round = 0; round < 2; ++round) {
+        Expert e = make_expert(round == 0 ? 64u : 32u, round == 0 ? 32u : 128u);
+        auto x = inputs(e.view.columns * 2);
+        std::vector<float> want(e.view.rows * 2), got(want.size());
+        cpu.expert_matmul(e.view, x, 2, want, scratch);
+        gpu.expert_matmul(e.view, x, 2, got, scratch);
+        expect_close(round == 0 ? "reused address, first matrix" : "reused address, second matrix", got, want, tol);
+    }
     // Shape errors surface as the reference's exception type.
     bool threw = false;
     try {
-        Expert e = make_expert(64, 32);
+        experts.push_back(make_expert(64, 32));
+        Expert &e = experts.back();
+        e.view = {64, 32, e.trellis, e.su, e.sv, e.gamma, e.tlut};
         std::vector<float> x(32), y(64);
         gpu.expert_matmul(e.view, x, 0, y, scratch);
     } catch (const std::invalid_argument &) {

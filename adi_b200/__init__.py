@@ -87,6 +87,7 @@ SIGNATURES = {
     "adi_cuda_moe_forward_batch": (C.c_int, [_ctx, _h, f32p, C.c_uint32, f32p, u32p, f32p]),
     "adi_cuda_expert_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_ne_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
+    "adi_cuda_expert_matmul_device_noalloc": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_head_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_bf16_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_moe_forward_batch_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p,

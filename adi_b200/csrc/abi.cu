@@ -22,6 +22,10 @@
 
 using namespace adi_cuda;
 
+// Scratch of adi_cuda_expert_matmul_device_noalloc: part of the device image,
+// so it exists on every device the module is loaded on and no call allocates.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[ADI_CUDA_NOALLOC_SCRATCH_BYTES];
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -531,6 +535,72 @@ void expert_matmul_dev(adi_cuda_context *c, ExpertDev &m, const float *in, uint3
     launch_finalize(acc, acc + size_t(batch) * m.rows, m.sv->ptr, 1, batch, m.rows, transform_scale(m.rows), out,
                     c->stream);
     c->stage_end();
+    c->after_launch(3);
+}
+
+// ---- the allocation-free expert projection --------------------------------
+//
+// For callers that may not allocate device memory during a call (all free HBM
+// already handed to their own pools, or a decode loop that cannot take the
+// device-wide synchronisation of cudaFree): the CUDA-core expert projection
+// with its scratch in a fixed array of the device image instead of the
+// context's grow-on-demand arena. One array per device, shared by every
+// context there, so calls that overlap on the GPU race on it.
+
+size_t round_up_256(size_t bytes) { return (bytes + 255) / 256 * 256; }
+
+std::mutex g_noalloc_lock;
+void *g_noalloc_address[64] = {};
+
+// The array's device address on the current device, looked up on that
+// device's first call (the lookup may load the module there).
+void *noalloc_scratch(int device) {
+    std::lock_guard<std::mutex> g(g_noalloc_lock);
+    if (device < 0 || device >= 64) invalid("device index out of range for the fixed scratch");
+    if (!g_noalloc_address[device]) {
+        void *address = nullptr;
+        check(cudaGetSymbolAddress(&address, g_noalloc_scratch), "cudaGetSymbolAddress");
+        g_noalloc_address[device] = address;
+    }
+    return g_noalloc_address[device];
+}
+
+void expert_matmul_noalloc(adi_cuda_context *c, ExpertDev &m, const float *in, uint32_t batch, float *out) {
+    if (batch == 0) invalid("Mach expert batch shape mismatch");
+    const size_t prep_bytes = round_up_256(size_t(batch) * m.cols * sizeof(float));
+    const size_t acc_bytes = round_up_256(2 * size_t(batch) * m.rows * sizeof(float));
+    if (prep_bytes + acc_bytes > ADI_CUDA_NOALLOC_SCRATCH_BYTES)
+        invalid("allocation-free expert matmul needs " + std::to_string(prep_bytes + acc_bytes) +
+                " scratch bytes for batch " + std::to_string(batch) + " of " + std::to_string(m.rows) + "x" +
+                std::to_string(m.cols) + "; the fixed scratch holds " +
+                std::to_string(size_t(ADI_CUDA_NOALLOC_SCRATCH_BYTES)));
+    uint8_t *scratch = static_cast<uint8_t *>(noalloc_scratch(c->device));
+    float *xp = reinterpret_cast<float *>(scratch);
+    float *acc = reinterpret_cast<float *>(scratch + prep_bytes);
+    PrepParams pp{};
+    pp.input = in;
+    pp.su[0] = m.su->ptr;
+    pp.out[0] = xp;
+    pp.cols = m.cols;
+    pp.scale = transform_scale(m.cols);
+    pp.rows = batch;
+    pp.jobs = 1;
+    pp.su_is_f16 = 1;
+    launch_prep(pp, c->stream);
+    ExpertGemmParams gp{};
+    gp.job[0] = ExpertJob{m.trellis->as<uint32_t>(), m.gamma->as<uint16_t>(), xp, acc, m.rows, m.cols, 0, 0,
+                          size_t(batch) * m.rows};
+    gp.job[1] = gp.job[0];
+    gp.tokens_per_item = tokens_per_item(batch);
+    gp.rows_per_item = expert_rows_per_item(m.cols);
+    gp.work = WorkList{nullptr, nullptr, batch, 1, gp.tokens_per_item};
+    gp.table = m.codec->half_tables.as<uint2>();
+    gp.error = c->error_word;
+    const uint64_t items = uint64_t((batch + gp.tokens_per_item - 1) / gp.tokens_per_item) *
+                           ((m.rows / 16 + gp.rows_per_item - 1) / gp.rows_per_item);
+    launch_expert_gemm(gp, gemm_grid(c, items, 2), c->stream);
+    launch_finalize(acc, acc + size_t(batch) * m.rows, m.sv->ptr, 1, batch, m.rows, transform_scale(m.rows), out,
+                    c->stream);
     c->after_launch(3);
 }
 
@@ -1228,6 +1298,16 @@ ADI_HOST_MATMUL(adi_cuda_expert_matmul, experts, "expert", expert_matmul_dev)
 ADI_HOST_MATMUL(adi_cuda_ne_matmul, nes, "NE", ne_matmul_dev)
 ADI_HOST_MATMUL(adi_cuda_head_matmul, heads, "head", head_matmul_dev)
 ADI_HOST_MATMUL(adi_cuda_bf16_matmul, bf16s, "bf16", bf16_matmul_dev)
+
+int adi_cuda_expert_matmul_device_noalloc(adi_cuda_context *c, adi_cuda_handle h, const float *in, uint32_t batch,
+                                          float *out) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!in || !out) invalid("input or output pointer is null");
+        expert_matmul_noalloc(c, lookup(c->experts, h, "expert"), in, batch, out);
+    });
+}
 
 int adi_cuda_moe_forward_batch(adi_cuda_context *c, adi_cuda_handle h, const float *in, uint32_t batch,
                                float *out, uint32_t *route_experts, float *route_weights) {

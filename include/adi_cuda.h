@@ -199,6 +199,48 @@ ADI_CUDA_API int adi_cuda_moe_forward_batch_device(adi_cuda_context *context,
                                       float *outputs, uint32_t *route_experts,
                                       float *route_weights);
 
+/* ---- allocation-free expert projection --------------------------------- */
+
+/* Bytes of device scratch the allocation-free entry below can use: one
+ * fixed array per device, reserved when the library's module loads. */
+#define ADI_CUDA_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* Scratch bytes a call of adi_cuda_expert_matmul_device_noalloc needs:
+ * batch x columns fp32 transformed inputs plus 2 x batch x rows fp32 partial
+ * sums, each rounded up to 256 bytes. */
+#define ADI_CUDA_NOALLOC_EXPERT_BYTES(batch, rows, columns)                   \
+    ((((size_t)(batch) * (columns) * 4 + 255) / 256 * 256) +                  \
+     (((size_t)(batch) * (rows) * 8 + 255) / 256 * 256))
+
+/* No counterpart in the reference: its CPU kernels take caller-owned
+ * ExpertScratch, and nothing on its side allocates device memory.
+ *
+ * The same product as adi_cuda_expert_matmul_device on the CUDA-core path
+ * (fp32 decode and accumulate, whatever the context's precision), for
+ * callers that must not allocate device memory during the call: an engine
+ * that has handed all free HBM to its own pools (an allocation would fail
+ * or take memory the pools count on), or a decode loop that cannot afford
+ * the device-wide synchronisation cudaFree implies. The other entries grow
+ * a per-context scratch arena with cudaMalloc/cudaFree; this one uses a
+ * fixed array of ADI_CUDA_NOALLOC_SCRATCH_BYTES in the library's device
+ * image and calls no allocating routine.
+ *
+ * A call needing more than ADI_CUDA_NOALLOC_SCRATCH_BYTES
+ * (ADI_CUDA_NOALLOC_EXPERT_BYTES) fails with ADI_CUDA_INVALID_ARGUMENT and
+ * launches nothing. The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress, which may load the library's module on that device);
+ * make that first call before any stream capture begins. Nothing in the
+ * scratch has to start at zero: every element is written before it is read.
+ * There is ONE array per device, shared by every context on it: calls whose
+ * work overlaps on the GPU (different streams or contexts, or threads that
+ * do not serialise their launches) race on it and corrupt each other's
+ * results. Issue them on one stream. Asynchronous on the context stream like
+ * the other device-pointer entries. */
+ADI_CUDA_API int adi_cuda_expert_matmul_device_noalloc(adi_cuda_context *context,
+                                          adi_cuda_handle matrix,
+                                          const float *inputs, uint32_t batch,
+                                          float *outputs);
+
 /* ---- codec and routing pieces, for bit-exact parity checks -------------
  * Device decode of expert tiles into their 32 states each
  * (src/expert_trellis.hpp:51-105), of NE tiles into 128 states

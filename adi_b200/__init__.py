@@ -88,6 +88,12 @@ SIGNATURES = {
     "adi_cuda_expert_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_ne_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_expert_matmul_device_noalloc": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
+    "adi_cuda_upload_moe_shard": (C.c_int, [_ctx, C.POINTER(MoeLayerDesc), C.c_uint32, C.c_uint32, C.POINTER(_h)]),
+    "adi_cuda_ep_dispatch_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p,
+                                              C.c_void_p, C.c_void_p]),
+    "adi_cuda_ep_experts_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32,
+                                             C.c_void_p]),
+    "adi_cuda_ep_combine_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_head_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_bf16_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_moe_forward_batch_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p,
@@ -270,10 +276,18 @@ class Context:
         """`layer` provides hidden, expert_hidden, experts, router [E][H] and
         shared_expert_gate [H] (bf16 bits), shared_gate/up/down (NE views) and
         expert(e, projection) -> expert view, projection 0/1/2 = gate/up/down."""
+        return self._upload_moe(layer, 0, layer.experts)
+
+    def upload_moe_shard(self, layer, first_expert: int, expert_count: int) -> Handle:
+        """Routed experts [first_expert, first_expert + expert_count) of
+        `layer` plus its router and shared expert, for the ep_* phases."""
+        return self._upload_moe(layer, first_expert, expert_count)
+
+    def _upload_moe(self, layer, first: int, count: int) -> Handle:
         keep: list = []
         E = layer.experts
         routed = (ExpertMatrixDesc * (3 * E))()
-        for e in range(E):
+        for e in range(first, min(first + count, E)):
             for p in range(3):
                 routed[3 * e + p] = self.expert_desc(layer.expert(e, p), keep)
         router = _arr(layer.router, np.uint16)
@@ -286,7 +300,11 @@ class Context:
                             self.ne_desc(layer.shared_down, keep),
                             C.cast(routed, C.POINTER(ExpertMatrixDesc)))
         h = C.c_uint64()
-        _check(self.lib.adi_cuda_upload_moe_layer(self.ptr, C.byref(desc), C.byref(h)), "upload_moe_layer")
+        if first == 0 and count == E:
+            _check(self.lib.adi_cuda_upload_moe_layer(self.ptr, C.byref(desc), C.byref(h)), "upload_moe_layer")
+        else:
+            _check(self.lib.adi_cuda_upload_moe_shard(self.ptr, C.byref(desc), first, count, C.byref(h)),
+                   "upload_moe_shard")
         return Handle(self, h.value, "moe", layer.hidden, layer.hidden)
 
     # -- the Backend table operations, host arrays ---------------------------
@@ -325,6 +343,22 @@ class Context:
         _check(self.lib.adi_cuda_moe_forward_batch_device(self.ptr, layer.value, inputs_ptr, batch, outputs_ptr,
                                                           route_experts_ptr or None, route_weights_ptr or None),
                "moe_forward_batch_device")
+
+    # -- expert-parallel phases (device pointers, asynchronous) ---------------
+    def ep_dispatch_device(self, shard: Handle, inputs_ptr: int, tokens: int, send_ptr: int, counts_ptr: int,
+                           route_experts_ptr: int = 0, route_weights_ptr: int = 0):
+        _check(self.lib.adi_cuda_ep_dispatch_device(self.ptr, shard.value, inputs_ptr, tokens, send_ptr, counts_ptr,
+                                                    route_experts_ptr or None, route_weights_ptr or None),
+               "ep_dispatch_device")
+
+    def ep_experts_device(self, shard: Handle, recv_ptr: int, recv_counts_ptr: int, world: int, rows: int,
+                          out_ptr: int):
+        _check(self.lib.adi_cuda_ep_experts_device(self.ptr, shard.value, recv_ptr or None, recv_counts_ptr, world,
+                                                   rows, out_ptr or None), "ep_experts_device")
+
+    def ep_combine_device(self, shard: Handle, returned_ptr: int, tokens: int, out_ptr: int):
+        _check(self.lib.adi_cuda_ep_combine_device(self.ptr, shard.value, returned_ptr, tokens, out_ptr),
+               "ep_combine_device")
 
     def matmul_device(self, handle: Handle, inputs_ptr: int, batch: int, outputs_ptr: int):
         fn = {"expert": self.lib.adi_cuda_expert_matmul_device, "ne": self.lib.adi_cuda_ne_matmul_device,

@@ -8,6 +8,7 @@
 #include "adi_cuda.h"
 #include "tc_gemm.cuh"
 #include "kernels.cuh"
+#include "ep.cuh"
 
 #include <cuda_runtime.h>
 
@@ -166,6 +167,7 @@ struct Bf16Dev {
 };
 struct MoeDev {
     uint32_t hidden, inner, experts;
+    uint32_t first_expert = 0, local_experts = 0;  // routed experts held: [first, first + local)
     std::unique_ptr<DeviceArray> router;  // [(E+1)][H] bf16: router rows then the shared gate
     std::unique_ptr<DeviceArray> trellis[3], su[3], sv[3], gamma[3], ka[3];
     ExpertCodec *codec;
@@ -274,6 +276,10 @@ struct adi_cuda_context {
     std::map<uint64_t, std::unique_ptr<Bf16Dev>> bf16s;
     std::map<uint64_t, std::unique_ptr<MoeDev>> moes;
     uint32_t *error_word = nullptr;  // device word kernels flag timeouts in
+    // The layer and token count of the last expert-parallel dispatch, whose
+    // routes and shared-expert sums the matching combine reads.
+    uint64_t ep_layer = 0;
+    uint32_t ep_tokens = 0;
     Profiler profiler;
     void stage(int st) { profiler.begin(st, stream); }
     void stage_end() { profiler.end(stream); }
@@ -735,54 +741,77 @@ void shared_expert_tc(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t 
     c->after_launch(4);
 }
 
-void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *out,
-                     uint32_t *route_experts_out, float *route_weights_out) {
-    if (T == 0) invalid("MoE batch shape mismatch");
-    const uint32_t H = L.hidden, I = L.inner, E = L.experts;
-    const size_t P = size_t(T) * 8;
+// The shared NE SwiGLU expert over T tokens: sacc_d = the down projection's
+// accumulators [T][H] before its output transform (combine applies it).
+void shared_expert(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *sacc_d) {
+    const uint32_t H = L.hidden, I = L.inner;
     cudaStream_t s = c->stream;
+    if (c->precision == 1 && tensor_core_shape(I, H) && T >= kNeTensorCoreMinBatch) {
+        shared_expert_tc(c, L, in, T, sacc_d);
+    } else {
+        float *sxg = c->buffer<float>("moe_sxg", size_t(T) * H);
+        float *sxu = c->buffer<float>("moe_sxu", size_t(T) * H);
+        PrepParams sp{};
+        sp.input = in;
+        sp.su[0] = L.shared[0].su->ptr;
+        sp.su[1] = L.shared[1].su->ptr;
+        sp.out[0] = sxg;
+        sp.out[1] = sxu;
+        sp.cols = H;
+        sp.scale = transform_scale(H);
+        sp.rows = T;
+        sp.jobs = 2;
+        sp.su_is_f16 = 0;
+        c->stage(kStageShared);
+        launch_prep(sp, s);
+        float *sacc_g = c->buffer<float>("moe_sacc_g", size_t(T) * I);
+        float *sacc_u = c->buffer<float>("moe_sacc_u", size_t(T) * I);
+        NeGemmParams np{};
+        np.job[0] = NeJob{L.shared[0].trellis->as<uint32_t>(), sxg, sacc_g, I, H, L.shared[0].weight_scale};
+        np.job[1] = NeJob{L.shared[1].trellis->as<uint32_t>(), sxu, sacc_u, I, H, L.shared[1].weight_scale};
+        np.work = WorkList{nullptr, nullptr, T, 2, kMaxTokens};
+        np.table = L.shared[0].codec->table.as<float2>();
+        const uint64_t ne_items = uint64_t((T + kMaxTokens - 1) / kMaxTokens) * 2 * row_blocks(I);
+        launch_ne_gemm(np, gemm_grid(c, ne_items, 1), s);
+        float *sxd = c->buffer<float>("moe_sxd", size_t(T) * I);
+        MidParams smp{};
+        smp.acc_gate = sacc_g;
+        smp.acc_up = sacc_u;
+        smp.half_stride = 0;
+        smp.pos_expert = nullptr;
+        smp.sv_gate = L.shared[0].sv->ptr;
+        smp.sv_up = L.shared[1].sv->ptr;
+        smp.su_down = L.shared[2].su->ptr;
+        smp.is_f16 = 0;
+        smp.halves = 1;
+        smp.inner = I;
+        smp.scale = transform_scale(I);
+        smp.xd = sxd;
+        smp.positions = T;
+        launch_mid(smp, s);
+        NeGemmParams nd{};
+        nd.job[0] = NeJob{L.shared[2].trellis->as<uint32_t>(), sxd, sacc_d, H, I, L.shared[2].weight_scale};
+        nd.job[1] = nd.job[0];
+        nd.work = WorkList{nullptr, nullptr, T, 1, kMaxTokens};
+        nd.table = np.table;
+        const uint64_t nd_items = uint64_t((T + kMaxTokens - 1) / kMaxTokens) * row_blocks(H);
+        launch_ne_gemm(nd, gemm_grid(c, nd_items, 1), s);
+        c->stage_end();
+        c->after_launch(4);
+    }
 
-    float *logits = c->buffer<float>("moe_logits", size_t(T) * (E + 1));
-    uint32_t *re = route_experts_out ? route_experts_out : c->buffer<uint32_t>("moe_re", P);
-    float *rw = route_weights_out ? route_weights_out : c->buffer<float>("moe_rw", P);
-    c->stage(kStageRouter);
-    launch_bf16_gemm(L.router->as<uint16_t>(), E, L.router->as<uint16_t>() + size_t(E) * H, 1, in, T, H, logits,
-                     E + 1, s);
-    c->stage_end();
-    c->stage(kStageTopk);
-    launch_top_experts(logits, E + 1, T, E, re, rw, s);
-    c->stage_end();
+}
 
-    RouteParams rp{};
-    rp.route_experts = re;
-    rp.tokens = T;
-    rp.experts = E;
-    rp.words = (T + 31) / 32;
-    rp.counts = c->buffer<uint32_t>("moe_counts", E);
-    rp.offsets = c->buffer<uint32_t>("moe_offsets", E + 1);
-    rp.bitmap = c->buffer<uint32_t>("moe_bitmap", size_t(E) * rp.words);
-    rp.prefix = c->buffer<uint32_t>("moe_prefix", size_t(E) * rp.words);
-    rp.grouped = c->buffer<uint32_t>("moe_grouped", P);
-    rp.pos_expert = c->buffer<uint32_t>("moe_pos_expert", P);
-    rp.route_to_grouped = c->buffer<uint32_t>("moe_r2g", P);
-    // Tensor cores once experts see a few positions each on average; below
-    // that the CUDA-core kernel streams the few touched experts faster.
-    const bool tc = c->precision == 1 && tensor_core_shape(I, H) && uint64_t(T) * 8 >= uint64_t(E) * 4;
-    const uint32_t nt = tc ? kTcMaxN : tokens_per_item((uint64_t(T) * 8 + E - 1) / E);
+// The routed SwiGLU experts over P grouped positions: prep (gather, su,
+// transform), gate/up, SwiGLU, down. `rp` supplies the grouping (position ->
+// input row, position -> expert, 0-based in L's experts) and the work lists
+// in chunks of `nt` positions. Returns the down projection's two partial
+// accumulators, [2][P][H], before its output transform.
+float *routed_experts(adi_cuda_context *c, MoeDev &L, const float *in, size_t P, const RouteParams &rp, uint32_t nt,
+                      bool tc) {
+    const uint32_t H = L.hidden, I = L.inner;
     const uint32_t rb_gate_up = expert_rows_per_item(H), rb_down = expert_rows_per_item(I);
-    rp.chunk = nt;
-    rp.row_blocks_gate_up = tc ? I / 128 : (I / 16 + rb_gate_up - 1) / rb_gate_up;
-    rp.row_blocks_down = tc ? H / 128 : (H / 16 + rb_down - 1) / rb_down;
-    const size_t max_chunks = P / nt + E;
-    rp.items_gate_up = c->buffer<uint4>("moe_items_gu", max_chunks * 2 * rp.row_blocks_gate_up);
-    rp.items_down = c->buffer<uint4>("moe_items_d", max_chunks * rp.row_blocks_down);
-    uint32_t *counts2 = c->buffer<uint32_t>("moe_item_counts", 2);
-    rp.count_gate_up = counts2;
-    rp.count_down = counts2 + 1;
-    c->stage(kStageRoute);
-    launch_route(rp, s);
-    c->stage_end();
-
+    cudaStream_t s = c->stream;
     float *acc_g = c->buffer<float>("moe_acc_g", 2 * P * I);
     float *acc_u = c->buffer<float>("moe_acc_u", 2 * P * I);
     float *acc_d = c->buffer<float>("moe_acc_d", 2 * P * H);
@@ -927,60 +956,65 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
         c->stage_end();
     }
 
+    c->after_launch(4);
+    return acc_d;
+}
+
+void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *out,
+                     uint32_t *route_experts_out, float *route_weights_out) {
+    if (T == 0) invalid("MoE batch shape mismatch");
+    if (L.local_experts != L.experts)
+        invalid("MoE layer handle holds a shard of the routed experts; use the expert-parallel entries");
+    const uint32_t H = L.hidden, I = L.inner, E = L.experts;
+    const size_t P = size_t(T) * 8;
+    cudaStream_t s = c->stream;
+
+    float *logits = c->buffer<float>("moe_logits", size_t(T) * (E + 1));
+    uint32_t *re = route_experts_out ? route_experts_out : c->buffer<uint32_t>("moe_re", P);
+    float *rw = route_weights_out ? route_weights_out : c->buffer<float>("moe_rw", P);
+    c->stage(kStageRouter);
+    launch_bf16_gemm(L.router->as<uint16_t>(), E, L.router->as<uint16_t>() + size_t(E) * H, 1, in, T, H, logits,
+                     E + 1, s);
+    c->stage_end();
+    c->stage(kStageTopk);
+    launch_top_experts(logits, E + 1, T, E, re, rw, s);
+    c->stage_end();
+
+    RouteParams rp{};
+    rp.route_experts = re;
+    rp.tokens = T;
+    rp.experts = E;
+    rp.words = (T + 31) / 32;
+    rp.counts = c->buffer<uint32_t>("moe_counts", E);
+    rp.offsets = c->buffer<uint32_t>("moe_offsets", E + 1);
+    rp.bitmap = c->buffer<uint32_t>("moe_bitmap", size_t(E) * rp.words);
+    rp.prefix = c->buffer<uint32_t>("moe_prefix", size_t(E) * rp.words);
+    rp.grouped = c->buffer<uint32_t>("moe_grouped", P);
+    rp.pos_expert = c->buffer<uint32_t>("moe_pos_expert", P);
+    rp.route_to_grouped = c->buffer<uint32_t>("moe_r2g", P);
+    // Tensor cores once experts see a few positions each on average; below
+    // that the CUDA-core kernel streams the few touched experts faster.
+    const bool tc = c->precision == 1 && tensor_core_shape(I, H) && uint64_t(T) * 8 >= uint64_t(E) * 4;
+    const uint32_t nt = tc ? kTcMaxN : tokens_per_item((uint64_t(T) * 8 + E - 1) / E);
+    const uint32_t rb_gate_up = expert_rows_per_item(H), rb_down = expert_rows_per_item(I);
+    rp.chunk = nt;
+    rp.row_blocks_gate_up = tc ? I / 128 : (I / 16 + rb_gate_up - 1) / rb_gate_up;
+    rp.row_blocks_down = tc ? H / 128 : (H / 16 + rb_down - 1) / rb_down;
+    const size_t max_chunks = P / nt + E;
+    rp.items_gate_up = c->buffer<uint4>("moe_items_gu", max_chunks * 2 * rp.row_blocks_gate_up);
+    rp.items_down = c->buffer<uint4>("moe_items_d", max_chunks * rp.row_blocks_down);
+    uint32_t *counts2 = c->buffer<uint32_t>("moe_item_counts", 2);
+    rp.count_gate_up = counts2;
+    rp.count_down = counts2 + 1;
+    c->stage(kStageRoute);
+    launch_route(rp, s);
+    c->stage_end();
+
+    float *acc_d = routed_experts(c, L, in, P, rp, nt, tc);
+
     // Shared NE expert over all T tokens.
     float *sacc_d = c->buffer<float>("moe_sacc_d", size_t(T) * H);
-    if (c->precision == 1 && tensor_core_shape(I, H) && T >= kNeTensorCoreMinBatch) {
-        shared_expert_tc(c, L, in, T, sacc_d);
-    } else {
-        float *sxg = c->buffer<float>("moe_sxg", size_t(T) * H);
-        float *sxu = c->buffer<float>("moe_sxu", size_t(T) * H);
-        PrepParams sp{};
-        sp.input = in;
-        sp.su[0] = L.shared[0].su->ptr;
-        sp.su[1] = L.shared[1].su->ptr;
-        sp.out[0] = sxg;
-        sp.out[1] = sxu;
-        sp.cols = H;
-        sp.scale = transform_scale(H);
-        sp.rows = T;
-        sp.jobs = 2;
-        sp.su_is_f16 = 0;
-        c->stage(kStageShared);
-        launch_prep(sp, s);
-        float *sacc_g = c->buffer<float>("moe_sacc_g", size_t(T) * I);
-        float *sacc_u = c->buffer<float>("moe_sacc_u", size_t(T) * I);
-        NeGemmParams np{};
-        np.job[0] = NeJob{L.shared[0].trellis->as<uint32_t>(), sxg, sacc_g, I, H, L.shared[0].weight_scale};
-        np.job[1] = NeJob{L.shared[1].trellis->as<uint32_t>(), sxu, sacc_u, I, H, L.shared[1].weight_scale};
-        np.work = WorkList{nullptr, nullptr, T, 2, kMaxTokens};
-        np.table = L.shared[0].codec->table.as<float2>();
-        const uint64_t ne_items = uint64_t((T + kMaxTokens - 1) / kMaxTokens) * 2 * row_blocks(I);
-        launch_ne_gemm(np, gemm_grid(c, ne_items, 1), s);
-        float *sxd = c->buffer<float>("moe_sxd", size_t(T) * I);
-        MidParams smp{};
-        smp.acc_gate = sacc_g;
-        smp.acc_up = sacc_u;
-        smp.half_stride = 0;
-        smp.pos_expert = nullptr;
-        smp.sv_gate = L.shared[0].sv->ptr;
-        smp.sv_up = L.shared[1].sv->ptr;
-        smp.su_down = L.shared[2].su->ptr;
-        smp.is_f16 = 0;
-        smp.halves = 1;
-        smp.inner = I;
-        smp.scale = transform_scale(I);
-        smp.xd = sxd;
-        smp.positions = T;
-        launch_mid(smp, s);
-        NeGemmParams nd{};
-        nd.job[0] = NeJob{L.shared[2].trellis->as<uint32_t>(), sxd, sacc_d, H, I, L.shared[2].weight_scale};
-        nd.job[1] = nd.job[0];
-        nd.work = WorkList{nullptr, nullptr, T, 1, kMaxTokens};
-        nd.table = np.table;
-        const uint64_t nd_items = uint64_t((T + kMaxTokens - 1) / kMaxTokens) * row_blocks(H);
-        launch_ne_gemm(nd, gemm_grid(c, nd_items, 1), s);
-        c->stage_end();
-    }
+    shared_expert(c, L, in, T, sacc_d);
 
     CombineParams cp{};
     cp.acc_down = acc_d;
@@ -1000,9 +1034,9 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     c->stage(kStageCombine);
     launch_combine(cp, s);
     c->stage_end();
-    // router, top-k, 2 memsets + 3 routing kernels, prep, gemm, mid, gemm,
-    // shared prep, gemm, mid, gemm, combine
-    c->after_launch(2 + 3 + 1 + 1 + 1 + 1 + 1 + 1 + 1 + 1 + 1);
+    // router, top-k, 3 routing kernels, combine (the routed and shared
+    // experts count their own four each)
+    c->after_launch(2 + 3 + 1);
 }
 
 // Host-pointer wrapper: stage inputs, run on device, read outputs back.
@@ -1015,6 +1049,216 @@ void host_call(adi_cuda_context *c, const float *in, size_t in_count, float *out
     run(din, dout);
     check(cudaMemcpyAsync(out, dout, out_count * sizeof(float), cudaMemcpyDeviceToHost, c->stream), "D2H");
     c->finish();
+}
+
+// Uploads the router, the shared expert and routed experts [first, first +
+// count) of `l`, expert-major, byte for byte.
+uint64_t upload_moe(adi_cuda_context *c, const adi_moe_layer &layer, uint32_t first, uint32_t count,
+                    const adi_cuda_handle *h) {
+    const adi_moe_layer *l = &layer;
+    if (!h || !l->routed) invalid("layer or handle pointer is null");
+    use_device(c);
+    const uint32_t H = l->hidden, I = l->expert_hidden, E = l->experts;
+    if (E < 8 || E > 1024) invalid("MoE routing requires between 8 and 1024 experts");
+    validate_expert_shape(I, H);
+    if (H > 8192) invalid("MoE hidden size above 8192 is not supported");
+    if (l->router.rows != E || l->router.columns != H || !l->router.values) invalid("MoE router shape mismatch");
+    if (l->shared_expert_gate.rows != 1 || l->shared_expert_gate.columns != H || !l->shared_expert_gate.values)
+        invalid("MoE shared expert gate shape mismatch");
+    auto d = std::make_unique<MoeDev>();
+    d->hidden = H;
+    d->inner = I;
+    d->experts = E;
+    d->first_expert = first;
+    d->local_experts = count;
+    std::vector<uint16_t> router(size_t(E + 1) * H);
+    std::memcpy(router.data(), l->router.values, size_t(E) * H * 2);
+    std::memcpy(router.data() + size_t(E) * H, l->shared_expert_gate.values, size_t(H) * 2);
+    d->router = upload_bytes(router.data(), router.size() * 2, "router");
+    const float *tlut = l->routed[3 * size_t(first)].tlut;
+    const uint32_t tiles = (I / 16) * (H / 16);
+    for (int p = 0; p < 3; ++p) {
+        const uint32_t rows = p == 2 ? H : I, cols = p == 2 ? I : H;
+        const size_t tw = size_t(tiles) * 24, gw = rows / 16 + cols / 16;
+        std::vector<uint16_t> trellis(tw * count), su(size_t(cols) * count), sv(size_t(rows) * count),
+            gamma(gw * count);
+        for (uint32_t i = 0; i < count; ++i) {
+            const adi_expert_matrix &m = l->routed[3 * size_t(first + i) + p];
+            if (m.rows != rows || m.columns != cols) invalid("MoE routed expert shape mismatch");
+            if (!m.trellis || !m.su_f16 || !m.sv_f16 || !m.wave_gamma_f16)
+                invalid("Mach expert codec tensor shape mismatch");
+            if (m.tlut != tlut) invalid("MoE routed experts must share one TLUT");
+            std::memcpy(trellis.data() + i * tw, m.trellis, tw * 2);
+            std::memcpy(su.data() + size_t(i) * cols, m.su_f16, size_t(cols) * 2);
+            std::memcpy(sv.data() + size_t(i) * rows, m.sv_f16, size_t(rows) * 2);
+            std::memcpy(gamma.data() + i * gw, m.wave_gamma_f16, gw * 2);
+        }
+        d->trellis[p] = upload_bytes(trellis.data(), trellis.size() * 2, "trellis");
+        d->su[p] = upload_bytes(su.data(), su.size() * 2, "su");
+        d->sv[p] = upload_bytes(sv.data(), sv.size() * 2, "sv");
+        d->gamma[p] = upload_bytes(gamma.data(), gamma.size() * 2, "gamma");
+    }
+    d->codec = c->expert_codec(tlut);
+    for (int p = 0; p < 3; ++p) {
+        const uint32_t rows = p == 2 ? H : I, cols = p == 2 ? I : H;
+        const size_t gw = rows / 16 + cols / 16;
+        std::vector<int8_t> ka(count);
+        for (uint32_t i = 0; i < count; ++i)
+            ka[i] = expert_ka(l->routed[3 * size_t(first + i) + p].wave_gamma_f16, gw, d->codec->max_value);
+        d->ka[p] = upload_bytes(ka.data(), ka.size(), "ka");
+    }
+    const adi_ne_matrix *shared[3] = {&l->shared_gate, &l->shared_up, &l->shared_down};
+    for (int p = 0; p < 3; ++p) {
+        const uint32_t rows = p == 2 ? H : I, cols = p == 2 ? I : H;
+        if (shared[p]->rows != rows || shared[p]->columns != cols) invalid("MoE shared expert shape mismatch");
+        fill_ne(c, *shared[p], d->shared[p]);
+    }
+    if (d->shared[0].codec != d->shared[1].codec || d->shared[0].codec != d->shared[2].codec)
+        invalid("MoE shared expert matrices must share one TLUT");
+    const uint64_t id = c->new_handle(kMoe);
+    c->moes[id] = std::move(d);
+    return id;
+}
+
+// ---- expert parallelism ----------------------------------------------------
+
+// Router, top-k and the counting sort over all experts; the rows of every
+// route in expert (= destination) order; the shared expert of these tokens.
+// Routes, weights, positions and shared sums stay for ep_combine_dev.
+void ep_dispatch_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const float *in, uint32_t T, float *send,
+                     uint32_t *expert_counts, uint32_t *route_experts_out, float *route_weights_out) {
+    if (T == 0) invalid("MoE batch shape mismatch");
+    const uint32_t H = L.hidden, E = L.experts;
+    const size_t P = size_t(T) * 8;
+    cudaStream_t s = c->stream;
+    float *logits = c->buffer<float>("ep_logits", size_t(T) * (E + 1));
+    uint32_t *re = c->buffer<uint32_t>("ep_re", P);
+    float *rw = c->buffer<float>("ep_rw", P);
+    c->stage(kStageRouter);
+    launch_bf16_gemm(L.router->as<uint16_t>(), E, L.router->as<uint16_t>() + size_t(E) * H, 1, in, T, H, logits,
+                     E + 1, s);
+    c->stage_end();
+    c->stage(kStageTopk);
+    launch_top_experts(logits, E + 1, T, E, re, rw, s);
+    c->stage_end();
+
+    // The counting sort only: no work lists (row_blocks 0), large chunks so
+    // the scan's per-expert loop is short.
+    RouteParams rp{};
+    rp.route_experts = re;
+    rp.tokens = T;
+    rp.experts = E;
+    rp.words = (T + 31) / 32;
+    rp.counts = expert_counts;
+    rp.offsets = c->buffer<uint32_t>("ep_offsets", E + 1);
+    rp.bitmap = c->buffer<uint32_t>("ep_bitmap", size_t(E) * rp.words);
+    rp.prefix = c->buffer<uint32_t>("ep_prefix", size_t(E) * rp.words);
+    rp.grouped = c->buffer<uint32_t>("ep_send_grouped", P);
+    rp.pos_expert = c->buffer<uint32_t>("ep_send_pos_expert", P);
+    rp.route_to_grouped = c->buffer<uint32_t>("ep_r2g", P);
+    rp.chunk = 1u << 16;
+    uint32_t *counts2 = c->buffer<uint32_t>("ep_item_counts", 2);
+    rp.count_gate_up = counts2;
+    rp.count_down = counts2 + 1;
+    c->stage(kStageRoute);
+    launch_route(rp, s);
+    launch_ep_gather(in, rp.grouped, uint32_t(P), H, send, s);
+    c->stage_end();
+    c->after_launch(2 + 3 + 1);
+
+    shared_expert(c, L, in, T, c->buffer<float>("ep_sacc", size_t(T) * H));
+    if (route_experts_out)
+        check(cudaMemcpyAsync(route_experts_out, re, P * 4, cudaMemcpyDeviceToDevice, s), "route copy");
+    if (route_weights_out)
+        check(cudaMemcpyAsync(route_weights_out, rw, P * 4, cudaMemcpyDeviceToDevice, s), "route copy");
+    c->ep_layer = handle;
+    c->ep_tokens = T;
+}
+
+// The shard's routed experts on received rows; one output row per row.
+void ep_experts_dev(adi_cuda_context *c, MoeDev &L, const float *recv, const uint32_t *recv_counts, uint32_t world,
+                    uint32_t rows, float *expert_rows) {
+    const uint32_t H = L.hidden, I = L.inner, local = L.local_experts;
+    if (world == 0 || uint64_t(world) * local > 1024) invalid("expert-parallel world times shard experts must be 1..1024");
+    if (rows == 0) return;
+    cudaStream_t s = c->stream;
+    const size_t P = rows;
+    const bool tc = c->precision == 1 && tensor_core_shape(I, H) && uint64_t(rows) >= uint64_t(local) * 4;
+    const uint32_t nt = tc ? kTcMaxN : tokens_per_item((uint64_t(rows) + local - 1) / local);
+    const uint32_t rb_gate_up = expert_rows_per_item(H), rb_down = expert_rows_per_item(I);
+    RouteParams rp{};
+    rp.grouped = c->buffer<uint32_t>("ep_grouped", P);
+    rp.pos_expert = c->buffer<uint32_t>("ep_pos_expert", P);
+    rp.chunk = nt;
+    rp.row_blocks_gate_up = tc ? I / 128 : (I / 16 + rb_gate_up - 1) / rb_gate_up;
+    rp.row_blocks_down = tc ? H / 128 : (H / 16 + rb_down - 1) / rb_down;
+    const size_t max_chunks = P / nt + local;
+    rp.items_gate_up = c->buffer<uint4>("ep_items_gu", max_chunks * 2 * rp.row_blocks_gate_up);
+    rp.items_down = c->buffer<uint4>("ep_items_d", max_chunks * rp.row_blocks_down);
+    uint32_t *counts3 = c->buffer<uint32_t>("ep_plan_counts", 3);
+    rp.count_gate_up = counts3;
+    rp.count_down = counts3 + 1;
+    EpPlanParams pp{};
+    pp.recv_counts = recv_counts;
+    pp.world = world;
+    pp.local = local;
+    pp.rows = rows;
+    pp.grouped = rp.grouped;
+    pp.pos_expert = rp.pos_expert;
+    pp.placed = counts3 + 2;
+    pp.chunk = nt;
+    pp.items_gate_up = rp.items_gate_up;
+    pp.count_gate_up = rp.count_gate_up;
+    pp.row_blocks_gate_up = rp.row_blocks_gate_up;
+    pp.items_down = rp.items_down;
+    pp.count_down = rp.count_down;
+    pp.row_blocks_down = rp.row_blocks_down;
+    c->stage(kStageRoute);
+    launch_ep_plan(pp, s);
+    c->stage_end();
+    c->after_launch(1);
+    float *acc_d = routed_experts(c, L, recv, P, rp, nt, tc);
+    EpFinalizeParams fp{};
+    fp.acc_down = acc_d;
+    fp.half_stride = P * H;
+    fp.grouped = rp.grouped;
+    fp.pos_expert = rp.pos_expert;
+    fp.placed = pp.placed;
+    fp.sv_down = L.sv[2]->as<uint16_t>();
+    fp.hidden = H;
+    fp.positions = rows;
+    fp.scale = transform_scale(H);
+    fp.expert_rows = expert_rows;
+    c->stage(kStageCombine);
+    launch_ep_finalize(fp, s);
+    c->stage_end();
+    c->after_launch(1);
+}
+
+void ep_combine_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const float *returned, uint32_t T,
+                    float *out) {
+    if (c->ep_layer != handle || c->ep_tokens != T || T == 0)
+        invalid("expert-parallel combine must follow a dispatch of the same layer and token count");
+    const uint32_t H = L.hidden, E = L.experts;
+    const size_t P = size_t(T) * 8;
+    EpCombineParams cp{};
+    cp.returned = returned;
+    cp.route_to_grouped = c->buffer<uint32_t>("ep_r2g", P);
+    cp.route_weights = c->buffer<float>("ep_rw", P);
+    cp.shared_acc = c->buffer<float>("ep_sacc", size_t(T) * H);
+    cp.shared_sv = L.shared[2].sv->as<int8_t>();
+    cp.gate_logits = c->buffer<float>("ep_logits", size_t(T) * (E + 1)) + E;
+    cp.gate_stride = E + 1;
+    cp.hidden = H;
+    cp.tokens = T;
+    cp.scale = transform_scale(H);
+    cp.out = out;
+    c->stage(kStageCombine);
+    launch_ep_combine(cp, c->stream);
+    c->stage_end();
+    c->after_launch(1);
+    c->ep_layer = 0;
+    c->ep_tokens = 0;
 }
 
 }  // namespace
@@ -1199,67 +1443,19 @@ int adi_cuda_upload_bf16(adi_cuda_context *c, const adi_bf16_matrix *m, adi_cuda
 int adi_cuda_upload_moe_layer(adi_cuda_context *c, const adi_moe_layer *l, adi_cuda_handle *h) {
     return guarded([&] {
         std::lock_guard<std::mutex> g(require(c)->lock);
-        if (!l || !h || !l->routed) invalid("layer or handle pointer is null");
-        use_device(c);
-        const uint32_t H = l->hidden, I = l->expert_hidden, E = l->experts;
-        if (E < 8 || E > 1024) invalid("MoE routing requires between 8 and 1024 experts");
-        validate_expert_shape(I, H);
-        if (H > 8192) invalid("MoE hidden size above 8192 is not supported");
-        if (l->router.rows != E || l->router.columns != H || !l->router.values)
-            invalid("MoE router shape mismatch");
-        if (l->shared_expert_gate.rows != 1 || l->shared_expert_gate.columns != H ||
-            !l->shared_expert_gate.values)
-            invalid("MoE shared expert gate shape mismatch");
-        auto d = std::make_unique<MoeDev>();
-        d->hidden = H;
-        d->inner = I;
-        d->experts = E;
-        std::vector<uint16_t> router(size_t(E + 1) * H);
-        std::memcpy(router.data(), l->router.values, size_t(E) * H * 2);
-        std::memcpy(router.data() + size_t(E) * H, l->shared_expert_gate.values, size_t(H) * 2);
-        d->router = upload_bytes(router.data(), router.size() * 2, "router");
-        const float *tlut = l->routed[0].tlut;
-        const uint32_t tiles = (I / 16) * (H / 16);
-        for (int p = 0; p < 3; ++p) {
-            const uint32_t rows = p == 2 ? H : I, cols = p == 2 ? I : H;
-            const size_t tw = size_t(tiles) * 24, gw = rows / 16 + cols / 16;
-            std::vector<uint16_t> trellis(tw * E), su(size_t(cols) * E), sv(size_t(rows) * E), gamma(gw * E);
-            for (uint32_t e = 0; e < E; ++e) {
-                const adi_expert_matrix &m = l->routed[3 * e + p];
-                if (m.rows != rows || m.columns != cols) invalid("MoE routed expert shape mismatch");
-                if (!m.trellis || !m.su_f16 || !m.sv_f16 || !m.wave_gamma_f16)
-                    invalid("Mach expert codec tensor shape mismatch");
-                if (m.tlut != tlut) invalid("MoE routed experts must share one TLUT");
-                std::memcpy(trellis.data() + e * tw, m.trellis, tw * 2);
-                std::memcpy(su.data() + size_t(e) * cols, m.su_f16, size_t(cols) * 2);
-                std::memcpy(sv.data() + size_t(e) * rows, m.sv_f16, size_t(rows) * 2);
-                std::memcpy(gamma.data() + e * gw, m.wave_gamma_f16, gw * 2);
-            }
-            d->trellis[p] = upload_bytes(trellis.data(), trellis.size() * 2, "trellis");
-            d->su[p] = upload_bytes(su.data(), su.size() * 2, "su");
-            d->sv[p] = upload_bytes(sv.data(), sv.size() * 2, "sv");
-            d->gamma[p] = upload_bytes(gamma.data(), gamma.size() * 2, "gamma");
-        }
-        d->codec = c->expert_codec(tlut);
-        for (int p = 0; p < 3; ++p) {
-            const uint32_t rows = p == 2 ? H : I, cols = p == 2 ? I : H;
-            const size_t gw = rows / 16 + cols / 16;
-            std::vector<int8_t> ka(E);
-            for (uint32_t e = 0; e < E; ++e)
-                ka[e] = expert_ka(l->routed[3 * e + p].wave_gamma_f16, gw, d->codec->max_value);
-            d->ka[p] = upload_bytes(ka.data(), ka.size(), "ka");
-        }
-        const adi_ne_matrix *shared[3] = {&l->shared_gate, &l->shared_up, &l->shared_down};
-        for (int p = 0; p < 3; ++p) {
-            const uint32_t rows = p == 2 ? H : I, cols = p == 2 ? I : H;
-            if (shared[p]->rows != rows || shared[p]->columns != cols) invalid("MoE shared expert shape mismatch");
-            fill_ne(c, *shared[p], d->shared[p]);
-        }
-        if (d->shared[0].codec != d->shared[1].codec || d->shared[0].codec != d->shared[2].codec)
-            invalid("MoE shared expert matrices must share one TLUT");
-        const uint64_t id = c->new_handle(kMoe);
-        c->moes[id] = std::move(d);
-        *h = id;
+        if (!l) invalid("layer or handle pointer is null");
+        *h = upload_moe(c, *l, 0, l->experts, h);
+    });
+}
+
+int adi_cuda_upload_moe_shard(adi_cuda_context *c, const adi_moe_layer *l, uint32_t first_expert,
+                              uint32_t expert_count, adi_cuda_handle *h) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        if (!l) invalid("layer or handle pointer is null");
+        if (expert_count == 0 || first_expert >= l->experts || expert_count > l->experts - first_expert)
+            invalid("expert shard is outside the layer's experts");
+        *h = upload_moe(c, *l, first_expert, expert_count, h);
     });
 }
 
@@ -1447,6 +1643,38 @@ int adi_cuda_rms_norm(adi_cuda_context *c, const float *inputs, const uint16_t *
         c->after_launch(1);
         check(cudaMemcpyAsync(outputs, o, total * 4, cudaMemcpyDeviceToHost, c->stream), "D2H");
         check(cudaStreamSynchronize(c->stream), "synchronize");
+    });
+}
+
+int adi_cuda_ep_dispatch_device(adi_cuda_context *c, adi_cuda_handle h, const float *in, uint32_t tokens,
+                                float *send_rows, uint32_t *expert_counts, uint32_t *route_experts,
+                                float *route_weights) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!in || !send_rows || !expert_counts) invalid("input, send or count pointer is null");
+        ep_dispatch_dev(c, h, lookup(c->moes, h, "MoE layer"), in, tokens, send_rows, expert_counts, route_experts,
+                        route_weights);
+    });
+}
+
+int adi_cuda_ep_experts_device(adi_cuda_context *c, adi_cuda_handle h, const float *recv_rows,
+                               const uint32_t *recv_counts, uint32_t world, uint32_t rows, float *expert_rows) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!recv_counts || (rows && (!recv_rows || !expert_rows))) invalid("receive or output pointer is null");
+        ep_experts_dev(c, lookup(c->moes, h, "MoE layer"), recv_rows, recv_counts, world, rows, expert_rows);
+    });
+}
+
+int adi_cuda_ep_combine_device(adi_cuda_context *c, adi_cuda_handle h, const float *returned_rows,
+                               uint32_t tokens, float *outputs) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!returned_rows || !outputs) invalid("returned-row or output pointer is null");
+        ep_combine_dev(c, h, lookup(c->moes, h, "MoE layer"), returned_rows, tokens, outputs);
     });
 }
 

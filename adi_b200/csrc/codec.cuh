@@ -103,6 +103,40 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) {
     return __uint_as_float(bits16 << 16);
 }
 
+__device__ __forceinline__ float f16_bits_to_f32(uint16_t bits) {
+    return __half2float(__ushort_as_half(bits));
+}
+
+// R consecutive floats (16-byte aligned when R >= 4).
+template <int R>
+__device__ __forceinline__ void load_regs(const float *src, float (&v)[R]) {
+    if constexpr (R % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < R / 4; ++i) {
+            const float4 q = reinterpret_cast<const float4 *>(src)[i];
+            v[4 * i] = q.x;
+            v[4 * i + 1] = q.y;
+            v[4 * i + 2] = q.z;
+            v[4 * i + 3] = q.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < R; ++i) v[i] = src[i];
+    }
+}
+
+template <int R>
+__device__ __forceinline__ void store_regs(float *dst, const float (&v)[R]) {
+    if constexpr (R % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < R / 4; ++i)
+            reinterpret_cast<float4 *>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < R; ++i) dst[i] = v[i];
+    }
+}
+
 // In-place Sylvester FWHT of n (power of two) floats in shared memory by the
 // whole block, strides 1, 2, 4, ... as the reference's scalar transform
 // (src/simd.cpp:48-63), then a multiply by `scale` = 1/sqrt(n) computed on

@@ -1,0 +1,235 @@
+// Expert-parallel pieces of the MoE block (declared in ep.cuh).
+//
+// One GPU's moe_forward_batch is route -> experts -> combine on one device.
+// Split across ranks, the rows of each route travel to the rank that owns
+// the route's expert and its output row travels back. The arithmetic of
+// every row is the single-GPU arithmetic: the receiving rank runs the same
+// prep / GEMM / SwiGLU kernels on its received rows, ep_finalize applies the
+// down projection's output transform exactly as combine does per route, and
+// ep_combine sums the returned rows in route order with the same fused
+// multiply-adds, so an expert-parallel block returns what one GPU returns.
+// All of it is HBM-bound row traffic (8 KiB rows, coalesced 16-byte
+// accesses); the routing plan is one block.
+#include "codec.cuh"
+#include "ep.cuh"
+
+namespace adi_cuda {
+namespace {
+
+__global__ void ep_gather_kernel(const float4 *x, const uint32_t *grouped, uint32_t positions, uint32_t quads,
+                                 float4 *send) {
+    const size_t total = (size_t)positions * quads;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t pos = i / quads, q = i - pos * quads;
+        send[i] = x[(size_t)grouped[pos] * quads + q];
+    }
+}
+
+// Inclusive prefix sum of a[0..1023] by a 1024-thread block.
+__device__ void block_scan_1024(uint32_t *a) {
+    const uint32_t t = threadIdx.x;
+    for (uint32_t o = 1; o < 1024; o <<= 1) {
+        const uint32_t add = t >= o ? a[t - o] : 0u;
+        __syncthreads();
+        a[t] += add;
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(1024) ep_plan_kernel(EpPlanParams p) {
+    __shared__ uint32_t cnt[1024], seg[1024], base[1024], scan[1024], chunk_scan[1024];
+    const uint32_t t = threadIdx.x, n = p.world * p.local;
+    const uint32_t c_t = t < n ? p.recv_counts[t] : 0u;
+    cnt[t] = c_t;
+    scan[t] = c_t;
+    __syncthreads();
+    block_scan_1024(scan);
+    seg[t] = scan[t] - c_t;  // receive-buffer row where segment (s, e) = t starts
+    const uint32_t total = scan[1023];
+    __syncthreads();
+    if (total != p.rows) {
+        for (uint32_t i = t; i < p.rows; i += 1024) {
+            p.grouped[i] = 0;
+            p.pos_expert[i] = 0;
+        }
+        if (t == 0) {
+            *p.count_gate_up = 0;
+            *p.count_down = 0;
+            *p.placed = 0;
+        }
+        return;
+    }
+
+    const uint32_t e = t;
+    uint32_t mine = 0;  // rows for local expert e from all senders
+    if (e < p.local)
+        for (uint32_t s = 0; s < p.world; ++s) mine += cnt[s * p.local + e];
+    const uint32_t chunks = (mine + p.chunk - 1) / p.chunk;
+    scan[e] = mine;
+    chunk_scan[e] = chunks;
+    __syncthreads();
+    block_scan_1024(scan);
+    block_scan_1024(chunk_scan);
+    const uint32_t offset = scan[e] - mine, chunk_offset = chunk_scan[e] - chunks;
+    if (e < p.local) {
+        uint32_t running = offset;
+        for (uint32_t s = 0; s < p.world; ++s) {
+            base[s * p.local + e] = running;
+            running += cnt[s * p.local + e];
+        }
+        for (uint32_t c = 0; c < chunks; ++c) {
+            const uint32_t pos0 = offset + c * p.chunk, m = min(p.chunk, mine - c * p.chunk);
+            for (uint32_t j = 0; j < 2; ++j)
+                for (uint32_t rb = 0; rb < p.row_blocks_gate_up; ++rb)
+                    p.items_gate_up[((chunk_offset + c) * 2 + j) * p.row_blocks_gate_up + rb] =
+                        make_uint4(e, (j << 16) | rb, pos0, m);
+            for (uint32_t rb = 0; rb < p.row_blocks_down; ++rb)
+                p.items_down[(chunk_offset + c) * p.row_blocks_down + rb] = make_uint4(e, rb, pos0, m);
+        }
+    }
+    if (e == p.local - 1) {
+        const uint32_t total_chunks = chunk_offset + chunks;
+        *p.count_gate_up = total_chunks * 2 * p.row_blocks_gate_up;
+        *p.count_down = total_chunks * p.row_blocks_down;
+        *p.placed = p.rows;
+    }
+    __syncthreads();
+    // One warp per (sender, expert) segment.
+    const uint32_t warp = t >> 5, lane = t & 31u;
+    for (uint32_t g = warp; g < n; g += 32) {
+        const uint32_t le = g % p.local, count = cnt[g], b = base[g], row0 = seg[g];
+        for (uint32_t i = lane; i < count; i += 32) {
+            p.grouped[b + i] = row0 + i;
+            p.pos_expert[b + i] = le;
+        }
+    }
+}
+
+template <int R>
+__global__ void __launch_bounds__(256) ep_finalize_regs_kernel(EpFinalizeParams p) {
+    __shared__ float sh[256 * R];
+    constexpr uint32_t H = 256u * R;
+    const uint32_t pos = blockIdx.x, c0 = threadIdx.x * R;
+    if (pos >= *p.placed) return;
+    const uint32_t e = p.pos_expert[pos], row = p.grouped[pos];
+    float v[R], v1[R];
+    load_regs<R>(p.acc_down + (size_t)pos * H + c0, v);
+    load_regs<R>(p.acc_down + p.half_stride + (size_t)pos * H + c0, v1);
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] += v1[r];
+    fwht_regs<R>(v, sh);
+    const uint16_t *sv = p.sv_down + (size_t)e * H + c0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = __fmul_rn(__fmul_rn(v[r], p.scale), f16_bits_to_f32(sv[r]));
+    store_regs<R>(p.expert_rows + (size_t)row * H + c0, v);
+}
+
+__global__ void ep_finalize_kernel(EpFinalizeParams p) {
+    extern __shared__ float v[];
+    const uint32_t pos = blockIdx.x, H = p.hidden;
+    if (pos >= *p.placed) return;
+    const uint32_t e = p.pos_expert[pos], row = p.grouped[pos];
+    const float *a0 = p.acc_down + (size_t)pos * H, *a1 = a0 + p.half_stride;
+    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) v[i] = a0[i] + a1[i];
+    __syncthreads();
+    block_fwht(v, H, p.scale);
+    const uint16_t *sv = p.sv_down + (size_t)e * H;
+    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x)
+        p.expert_rows[(size_t)row * H + i] = __fmul_rn(v[i], f16_bits_to_f32(sv[i]));
+}
+
+template <int R>
+__global__ void __launch_bounds__(256) ep_combine_regs_kernel(EpCombineParams p) {
+    __shared__ float sh[256 * R];
+    constexpr uint32_t H = 256u * R;
+    const uint32_t t = blockIdx.x, c0 = threadIdx.x * R;
+    float out[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) out[r] = 0.0f;
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t pos = p.route_to_grouped[t * 8 + k];
+        const float w = p.route_weights[t * 8 + k];
+        float v[R];
+        load_regs<R>(p.returned + (size_t)pos * H + c0, v);
+#pragma unroll
+        for (int r = 0; r < R; ++r) out[r] = fmaf(w, v[r], out[r]);
+    }
+    float v[R];
+    load_regs<R>(p.shared_acc + (size_t)t * H + c0, v);
+    fwht_regs<R>(v, sh);
+    const float gate = sigmoid_f(p.gate_logits[(size_t)t * p.gate_stride]);
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+        out[r] = fmaf(gate, __fmul_rn(__fmul_rn(v[r], p.scale), (float)p.shared_sv[c0 + r]), out[r]);
+    store_regs<R>(p.out + (size_t)t * H + c0, out);
+}
+
+// Generic hidden sizes: blockDim = H / 8, eight columns per thread, the
+// same order of operations as the single-GPU generic combine.
+__global__ void ep_combine_kernel(EpCombineParams p) {
+    extern __shared__ float v[];
+    const uint32_t t = blockIdx.x, H = p.hidden;
+    constexpr int kPer = 8;
+    float out[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) out[j] = 0.0f;
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t pos = p.route_to_grouped[t * 8 + k];
+        const float w = p.route_weights[t * 8 + k];
+        const float *row = p.returned + (size_t)pos * H;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const uint32_t i = threadIdx.x + j * blockDim.x;
+            if (i < H) out[j] = fmaf(w, row[i], out[j]);
+        }
+    }
+    const float *sa = p.shared_acc + (size_t)t * H;
+    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) v[i] = sa[i];
+    __syncthreads();
+    block_fwht(v, H, p.scale);
+    const float gate = sigmoid_f(p.gate_logits[(size_t)t * p.gate_stride]);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const uint32_t i = threadIdx.x + j * blockDim.x;
+        if (i < H) p.out[(size_t)t * H + i] = fmaf(gate, __fmul_rn(v[i], (float)p.shared_sv[i]), out[j]);
+    }
+}
+
+}  // namespace
+
+void launch_ep_gather(const float *x, const uint32_t *grouped, uint32_t positions, uint32_t hidden, float *send,
+                      cudaStream_t s) {
+    if (positions == 0) return;
+    const uint32_t quads = hidden / 4;
+    const size_t total = (size_t)positions * quads;
+    const size_t blocks = (total + 255) / 256;
+    ep_gather_kernel<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, s>>>(
+        reinterpret_cast<const float4 *>(x), grouped, positions, quads, reinterpret_cast<float4 *>(send));
+}
+
+void launch_ep_plan(const EpPlanParams &p, cudaStream_t s) { ep_plan_kernel<<<1, 1024, 0, s>>>(p); }
+
+void launch_ep_finalize(const EpFinalizeParams &p, cudaStream_t s) {
+    if (p.positions == 0) return;
+    switch (p.hidden) {
+        case 512: ep_finalize_regs_kernel<2><<<p.positions, 256, 0, s>>>(p); return;
+        case 1024: ep_finalize_regs_kernel<4><<<p.positions, 256, 0, s>>>(p); return;
+        case 2048: ep_finalize_regs_kernel<8><<<p.positions, 256, 0, s>>>(p); return;
+        default: ep_finalize_kernel<<<p.positions, 256, p.hidden * sizeof(float), s>>>(p);
+    }
+}
+
+void launch_ep_combine(const EpCombineParams &p, cudaStream_t s) {
+    if (p.tokens == 0) return;
+    switch (p.hidden) {
+        case 512: ep_combine_regs_kernel<2><<<p.tokens, 256, 0, s>>>(p); return;
+        case 1024: ep_combine_regs_kernel<4><<<p.tokens, 256, 0, s>>>(p); return;
+        case 2048: ep_combine_regs_kernel<8><<<p.tokens, 256, 0, s>>>(p); return;
+        default: {
+            const uint32_t threads = (p.hidden + 7) / 8;
+            ep_combine_kernel<<<p.tokens, threads < 32 ? 32 : threads, p.hidden * sizeof(float), s>>>(p);
+        }
+    }
+}
+
+}  // namespace adi_cuda

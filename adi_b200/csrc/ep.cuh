@@ -1,0 +1,70 @@
+// Kernels of the expert-parallel split of the MoE block (ep.cu): the rows a
+// rank sends, the receiving rank's expert work lists, its per-row expert
+// outputs and the owner's route-order combine.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace adi_cuda {
+
+// send[pos] = x[grouped[pos]] for the positions of the counting sort: the
+// rows of every route in global expert order, which is destination order.
+void launch_ep_gather(const float *x, const uint32_t *grouped, uint32_t positions, uint32_t hidden, float *send,
+                      cudaStream_t s);
+
+// The receiving rank's routing. recv_counts[s][e]: rows rank s sent for
+// local expert e; they sit in the receive buffer in (s, e) order. Positions
+// are expert-major (then sender, then arrival), so each local expert's rows
+// are contiguous, as the counting sort makes them on one GPU. If the counts
+// do not add up to `rows` the plan holds no work (empty lists, *placed = 0,
+// every index 0), so no launch after it reads or writes out of bounds.
+struct EpPlanParams {
+    const uint32_t *recv_counts;  // [world][local]
+    uint32_t world, local;        // world * local <= 1024
+    uint32_t rows;                // rows in the receive buffer
+    uint32_t *grouped;            // [rows] receive-buffer row of each position
+    uint32_t *pos_expert;         // [rows] local expert of each position
+    uint32_t *placed;             // positions planned: rows, or 0 on a mismatch
+    uint32_t chunk;               // positions per work item
+    uint4 *items_gate_up;
+    uint32_t *count_gate_up;
+    uint32_t row_blocks_gate_up;
+    uint4 *items_down;
+    uint32_t *count_down;
+    uint32_t row_blocks_down;
+};
+void launch_ep_plan(const EpPlanParams &p, cudaStream_t s);
+
+// expert_rows[grouped[pos]] = H(acc0[pos] + acc1[pos]) / sqrt(H) * sv_e: the
+// output transform of the down projection, written in receive order.
+struct EpFinalizeParams {
+    const float *acc_down;     // [2][positions][hidden]
+    size_t half_stride;
+    const uint32_t *grouped, *pos_expert;
+    const uint32_t *placed;    // positions at or past *placed are skipped
+    const uint16_t *sv_down;   // f16 [local][hidden]
+    uint32_t hidden, positions;
+    float scale;
+    float *expert_rows;
+};
+void launch_ep_finalize(const EpFinalizeParams &p, cudaStream_t s);
+
+// out[t] = sum_k w[t][k] * returned[route_to_grouped[t*8+k]] (k = 0..7 in
+// order) + sigmoid(gate) * H(shared_acc[t]) / sqrt(H) * shared_sv.
+struct EpCombineParams {
+    const float *returned;     // [8T][hidden]
+    const uint32_t *route_to_grouped;
+    const float *route_weights;
+    const float *shared_acc;   // [T][hidden]
+    const int8_t *shared_sv;   // [hidden]
+    const float *gate_logits;  // token t's at gate_logits[t * gate_stride]
+    uint32_t gate_stride;
+    uint32_t hidden, tokens;
+    float scale;
+    float *out;
+};
+void launch_ep_combine(const EpCombineParams &p, cudaStream_t s);
+
+}  // namespace adi_cuda

@@ -1,0 +1,108 @@
+"""Expert-parallel MoE block over the GPUs of one node.
+
+The reference runs the whole block in one process (moe_forward_batch,
+src/executor.cpp:1181-1453); here the block's experts are spread over
+`world` ranks, one process per GPU. Rank r holds routed experts
+[r*L, (r+1)*L), L = experts / world, and a copy of the router and the
+shared expert; tokens are data-parallel, each rank feeding its own. One
+layer is three device phases with two exchanges between them:
+
+    dispatch   router, top-8, counting sort over all experts, the row of
+               every route in expert order (which is destination order),
+               the shared expert of this rank's tokens
+    exchange   route counts per expert (all_to_all, E int32), then the
+               rows (all_to_all with per-rank sizes)
+    experts    this rank's SwiGLU experts on the rows it received, one
+               output row per row, in receive order
+    exchange   the output rows back (the reverse all_to_all)
+    combine    route-order weighted sum of the returned rows, plus the
+               gated shared expert
+
+The exchanges are torch.distributed collectives (NCCL over NVLink on the
+GPUs). Every row is computed with the single-GPU kernels, so the output is
+the single-GPU block's output for the same tokens.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+class DevicePhases:
+    """The three device phases of one MoE layer shard, through the C ABI.
+
+    Kernels run on the caller's current torch stream, so they are ordered
+    with the collectives torch issues around them."""
+
+    def __init__(self, ctx, layer, rank: int, world: int):
+        if layer.experts % world:
+            raise ValueError(f"{layer.experts} experts do not split over {world} ranks")
+        self.ctx = ctx
+        self.experts, self.hidden = layer.experts, layer.hidden
+        self.local = layer.experts // world
+        self.handle = ctx.upload_moe_shard(layer, rank * self.local, self.local)
+
+    def _stream(self, device):
+        self.ctx.set_stream(torch.cuda.current_stream(device).cuda_stream)
+
+    def dispatch(self, x: torch.Tensor):
+        tokens = x.shape[0]
+        self._stream(x.device)
+        send = torch.empty(8 * tokens, self.hidden, dtype=torch.float32, device=x.device)
+        counts = torch.empty(self.experts, dtype=torch.int32, device=x.device)
+        self.ctx.ep_dispatch_device(self.handle, x.data_ptr(), tokens, send.data_ptr(), counts.data_ptr())
+        return send, counts
+
+    def experts_forward(self, recv: torch.Tensor, recv_counts: torch.Tensor, world: int) -> torch.Tensor:
+        self._stream(recv_counts.device)
+        rows = recv.shape[0]
+        out = torch.empty(rows, self.hidden, dtype=torch.float32, device=recv_counts.device)
+        self.ctx.ep_experts_device(self.handle, recv.data_ptr() if rows else 0, recv_counts.data_ptr(), world,
+                                   rows, out.data_ptr() if rows else 0)
+        return out
+
+    def combine(self, returned: torch.Tensor, tokens: int) -> torch.Tensor:
+        self._stream(returned.device)
+        out = torch.empty(tokens, self.hidden, dtype=torch.float32, device=returned.device)
+        self.ctx.ep_combine_device(self.handle, returned.data_ptr(), tokens, out.data_ptr())
+        return out
+
+    def release(self):
+        self.handle.release()
+
+
+class ExpertParallelMoe:
+    """One MoE layer across the ranks of `group`; forward(x) takes this
+    rank's tokens [T, H] and returns their block outputs [T, H].
+
+    `phases` does the per-rank compute (DevicePhases on GPUs); the class
+    owns the exchanges, whose sizes come from the routed counts."""
+
+    def __init__(self, phases, group=None):
+        self.phases = phases
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.experts, self.hidden, self.local = phases.experts, phases.hidden, phases.local
+        if self.local * self.world != self.experts:
+            raise ValueError("the shard's experts times the world size must be the layer's experts")
+        self.last_splits: tuple[list[int], list[int]] | None = None  # rows sent to / received from each rank
+        self.last_received = None  # rows received per local expert (host, int64)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        tokens = x.shape[0]
+        send, counts = self.phases.dispatch(x)
+        recv_counts = torch.empty_like(counts)
+        dist.all_to_all_single(recv_counts, counts, group=self.group)
+        host = torch.cat([counts, recv_counts]).cpu()
+        send_splits = host[:self.experts].view(self.world, self.local).sum(1).tolist()
+        recv_splits = host[self.experts:].view(self.world, self.local).sum(1).tolist()
+        self.last_splits = (send_splits, recv_splits)
+        self.last_received = host[self.experts:].view(self.world, self.local).sum(0).long()
+        recv = torch.empty(sum(recv_splits), self.hidden, dtype=send.dtype, device=send.device)
+        dist.all_to_all_single(recv, send, recv_splits, send_splits, group=self.group)
+        expert_rows = self.phases.experts_forward(recv, recv_counts, self.world)
+        returned = torch.empty_like(send)
+        dist.all_to_all_single(returned, expert_rows, send_splits, recv_splits, group=self.group)
+        return self.phases.combine(returned, tokens)
+
+    __call__ = forward

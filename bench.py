@@ -19,8 +19,11 @@ dominant one): packed expert bytes it must stream per launch over its
 event-timed duration. `cpu_baseline` is the reference CPU implementation
 (built from its own sources into oracle/_ref) on this host's cores.
 
-With N > 1 under torchrun each rank runs its own block replica on its own
-tokens (weak scaling, no collective); expert parallelism is separate work.
+With N > 1 under torchrun the block is expert-parallel (C4): every rank
+holds 256/N of each block's routed experts plus the router and shared
+expert, feeds its own 512 tokens (weak scaling: 512 x N tokens per step, so
+4096 at N = 8), and each layer exchanges route counts, token rows and
+expert output rows with NCCL all-to-alls (adi_b200.expert_parallel).
 
 `--impl reference` times the reference CPU implementation on the same
 workload (rank 0 only).
@@ -217,9 +220,132 @@ def run_reference(args, world, rank):
     }), flush=True)
 
 
+def run_ep(args, world, rank, local):
+    """Expert-parallel MoE block over `world` ranks (one process per GPU)."""
+    import adi_b200
+    from adi_b200 import synthetic
+    from adi_b200.expert_parallel import DevicePhases, ExpertParallelMoe
+    torch.cuda.set_device(local)
+    device = f"cuda:{local}"
+    ctx = adi_b200.Context(local)
+    stream = torch.cuda.Stream(device=local)
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    ctx.set_precision(args.precision)
+    T, L = args.tokens, args.layers
+
+    layers, first = [], None
+    for layer in range(L):
+        block = synthetic.moe_block(seed=layer, device=device)  # the same blocks on every rank
+        layers.append(ExpertParallelMoe(DevicePhases(ctx, block, rank, world)))
+        if first is None:
+            first = block
+        del block
+    H, E = first.hidden, first.experts
+    local_experts = E // world
+    pool = 8
+    inputs = torch.stack([synthetic.activations(7 * rank + i, T, H, device=device) for i in range(pool)])
+
+    def step(k):
+        return layers[k % L](inputs[k % pool])
+
+    # Local experts each (layer, input) pair touches, from the rows this
+    # rank receives per expert: the algorithmic bytes of its expert GEMMs.
+    touched = []
+    for i in range(pool * L):
+        step(i)
+        touched.append(int((layers[i % L].last_received > 0).sum()))
+
+    ctx.set_profiling(True)
+    for k in range(max(args.warmup, 1)):
+        step(k)
+    torch.cuda.synchronize()
+    ctx.reset_profile()
+    launches0 = ctx.launch_count()
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    begin.record(stream)
+    for k in range(args.steps):
+        step(k)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clock_info = clocks.stop()
+    ctx.set_profiling(False)
+    launches = ctx.launch_count() - launches0
+    ms = begin.elapsed_time(end)
+    ms_max = max_over_ranks(ms, world)
+    stages = ctx.profile()
+    value = sum_over_ranks(args.steps * T, world) / (ms_max / 1e3)
+    n_touched = [touched[k % (pool * L)] for k in range(args.steps)]
+
+    gemm_ms = stages.get("expert_gemm_gate_up", (0, 0))[0] + stages.get("expert_gemm_down", (0, 0))[0]
+    gemm_launches = stages.get("expert_gemm_gate_up", (0, 0))[1] + stages.get("expert_gemm_down", (0, 0))[1]
+    hbm_peak, peak_kind = peaks()
+    gemm_bytes = sum(n * 3 * (TRELLIS_BYTES + GAMMA_BYTES) for n in n_touched)
+    achieved = (gemm_bytes / (gemm_ms / 1e3)) / 1e9 if gemm_ms > 0 else None
+
+    # End to end through the public API: pinned host tokens in, outputs back.
+    x_host = torch.empty(pool, T, H, dtype=torch.float32, pin_memory=True)
+    x_host.copy_(inputs.cpu())
+    y_host = torch.empty(T, H, dtype=torch.float32, pin_memory=True)
+    x_dev = torch.empty(T, H, device=device)
+    e2e_steps = max(1, min(args.steps, 200))
+
+    def e2e_step(k):
+        x_dev.copy_(x_host[k % pool], non_blocking=True)
+        y_host.copy_(layers[k % L](x_dev), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for k in range(min(args.warmup, 5)):
+        e2e_step(k)
+    barrier(world)
+    t0 = time.perf_counter()
+    for k in range(e2e_steps):
+        e2e_step(k)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    e2e_value = sum_over_ranks(e2e_steps * T, world) / e2e_s
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 operands, f32 accumulate" if args.precision else "f32", "data": "synthetic",
+            "config": {"workload": f"C4: expert-parallel MoE block, {T} tokens per GPU, {T * world} per step",
+                       "tokens_per_step": T * world, "tokens_per_gpu": T, "hidden": H, "experts": E,
+                       "experts_per_gpu": local_experts, "expert_hidden": first.expert_hidden, "top_k": 8,
+                       "blocks_rotated": L, "routing": "N(0,1) inputs, near-uniform",
+                       "l2": f"inputs larger than L2: {L} distinct blocks rotated",
+                       "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single, fp32 rows"},
+            "roofline": {"bound": "hbm", "kernel": "expert_gemm_kernel",
+                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": (achieved / hbm_peak) if achieved else None, "peak_kind": peak_kind,
+                         "traffic": None,
+                         "bytes_per_launch": gemm_bytes / max(1, gemm_launches),
+                         "ms_per_launch": gemm_ms / max(1, gemm_launches)},
+            "local_experts_touched_mean": sum(n_touched) / len(n_touched),
+            "stages_ms_per_step": {k: v[0] / max(1, v[1]) for k, v in stages.items()},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4 * world,
+                    "d2h_bytes_per_step": T * H * 4 * world, "steps": e2e_steps},
+            "gpu_launches": launches,
+            "clocks": clock_info,
+        }
+        print(json.dumps(line), flush=True)
+    barrier(world)
+    for moe in layers:
+        moe.phases.release()
+    ctx.close()
+
+
 def run_ours(args, world, rank, local):
     import adi_b200
     from adi_b200 import synthetic
+    if world > 1:
+        run_ep(args, world, rank, local)
+        return
     torch.cuda.set_device(local)
     ctx = adi_b200.Context(local)
     # One explicit stream for everything: the context launches on it and the

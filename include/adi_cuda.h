@@ -199,6 +199,57 @@ ADI_CUDA_API int adi_cuda_moe_forward_batch_device(adi_cuda_context *context,
                                       float *outputs, uint32_t *route_experts,
                                       float *route_weights);
 
+/* ---- expert parallelism ---------------------------------------------------
+ * No counterpart in the reference, which runs one process on one host (its
+ * only parallelism is CPU tasks, src/executor.cpp:261, :1302-1371). These
+ * split moe_forward_batch (src/executor.cpp:1181-1453) at its two exchange
+ * points so that a caller can run experts on other GPUs:
+ *
+ *   rank r owns routed experts [r*L, (r+1)*L), L = experts / world;
+ *   1. adi_cuda_ep_dispatch_device: router, top_experts, the counting sort
+ *      (:1237-1258) over all experts, the token rows of every route in
+ *      expert order (= destination-rank order) into `send_rows`, the count
+ *      of routes per expert, and the shared expert of the local tokens;
+ *   2. the caller exchanges counts (expert_counts[d*L .. d*L+L) go to rank
+ *      d) and rows (an all-to-all with per-rank sizes), e.g. over NCCL;
+ *   3. adi_cuda_ep_experts_device: the routed SwiGLU experts of this rank on
+ *      the received rows, one output row per received row, in receive order;
+ *   4. the caller sends those rows back (the reverse all-to-all);
+ *   5. adi_cuda_ep_combine_device: the route-order weighted sum of the
+ *      returned rows plus the gated shared expert (:1373-1452).
+ *
+ * Phases 1 and 5 of one layer run on the same context with no other
+ * dispatch between them: 1 leaves the routes, weights and shared-expert
+ * partial sums in the context for 5. All are asynchronous on the context
+ * stream. */
+
+/* Uploads routed experts [first_expert, first_expert + expert_count) of
+ * `layer` plus its router and shared expert (replicated). `layer->routed`
+ * is the full [experts * 3] array; only the shard's entries are read. The
+ * handle serves the ep_* entries; moe_forward_batch rejects a handle that
+ * does not hold every expert. */
+ADI_CUDA_API int adi_cuda_upload_moe_shard(adi_cuda_context *context, const adi_moe_layer *layer,
+                                           uint32_t first_expert, uint32_t expert_count,
+                                           adi_cuda_handle *handle);
+/* inputs [tokens][hidden]; send_rows [8 * tokens][hidden]; expert_counts
+ * [experts]; route_experts / route_weights [tokens][8] or NULL. */
+ADI_CUDA_API int adi_cuda_ep_dispatch_device(adi_cuda_context *context, adi_cuda_handle shard,
+                                             const float *inputs, uint32_t tokens, float *send_rows,
+                                             uint32_t *expert_counts, uint32_t *route_experts,
+                                             float *route_weights);
+/* recv_counts [world][expert_count] (device): rows rank s sent for each of
+ * this shard's experts, i.e. what rank s's expert_counts held for them;
+ * recv_rows [rows][hidden] as the all-to-all delivered them (rank 0's first,
+ * each rank's in expert order); rows = the sum of recv_counts.
+ * expert_rows [rows][hidden] receives each row's expert output. */
+ADI_CUDA_API int adi_cuda_ep_experts_device(adi_cuda_context *context, adi_cuda_handle shard,
+                                            const float *recv_rows, const uint32_t *recv_counts,
+                                            uint32_t world, uint32_t rows, float *expert_rows);
+/* returned_rows [8 * tokens][hidden]: the expert rows of this rank's
+ * routes, in the order send_rows had them. outputs [tokens][hidden]. */
+ADI_CUDA_API int adi_cuda_ep_combine_device(adi_cuda_context *context, adi_cuda_handle shard,
+                                            const float *returned_rows, uint32_t tokens, float *outputs);
+
 /* ---- allocation-free expert projection --------------------------------- */
 
 /* Bytes of device scratch the allocation-free entry below can use: one

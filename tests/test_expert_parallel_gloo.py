@@ -1,0 +1,63 @@
+"""The expert-parallel exchange logic (adi_b200.expert_parallel) on CPU
+ranks over gloo: ExpertParallelMoe with the oracle-composed phases of
+ep_cpu_phases gives each rank the block output of its own tokens, equal to
+the oracle's single-process moe_forward (src/executor.cpp:242-330), for 2
+and 4 ranks with unequal token counts per rank."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from fixtures import activations, moe_layer
+
+TOL = 1e-5  # only the SwiGLU and combine summation order differ
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def tokens_of(rank: int) -> int:
+    return 3 + 4 * rank
+
+
+def worker(rank: int, world: int, port: int):
+    import torch
+    import torch.distributed as dist
+
+    from adi_b200.expert_parallel import ExpertParallelMoe
+    from ep_cpu_phases import CpuPhases
+    from oracle_ffi import Oracle, rel_l2
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        layer = moe_layer(seed=5, hidden=256, expert_hidden=64, experts=16, scale_mu=-1.0, shared_mu=-3.0)
+        x = activations(40 + rank, tokens_of(rank), layer.hidden)
+        phases = CpuPhases(layer, rank, world)
+        moe = ExpertParallelMoe(phases)
+        y = moe(torch.from_numpy(x)).numpy()
+        want, experts, weights = Oracle().moe_forward(layer, x)
+        assert np.array_equal(phases.route_experts, experts)
+        assert np.array_equal(phases.route_weights, weights)
+        err = rel_l2(y, want)
+        assert err <= TOL, (rank, world, err)
+        # Every rank sends all 8 routes of its tokens and receives the routes
+        # of all ranks' tokens that name one of its experts.
+        send_splits, recv_splits = moe.last_splits
+        assert sum(send_splits) == 8 * tokens_of(rank)
+        owners = np.concatenate([Oracle().moe_forward(layer, activations(40 + s, tokens_of(s), layer.hidden))[1]
+                                 .reshape(-1) for s in range(world)]) // (layer.experts // world)
+        assert sum(recv_splits) == int((owners == rank).sum())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_expert_parallel_matches_single_process(world):
+    mp.spawn(worker, args=(world, free_port()), nprocs=world, join=True)

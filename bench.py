@@ -53,6 +53,10 @@ PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM_GBS = 6650.0
 TRELLIS_BYTES = 4096 * 48  # one expert projection's trellis
 GAMMA_BYTES = 160 * 2
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
+# tensor-core expert GEMM, averaged over the gate/up and down launches of one
+# 512-token block, from one ncu capture (profiles/tc_gemm_expert_t512.md).
+EXPERT_GEMM_TRAFFIC_T512 = (134.81216e6 + 20.108288e6 + 54.997248e6 + 21.127424e6) / 2
 
 
 def parse():
@@ -497,7 +501,8 @@ def run_ours(args, world, rank, local):
             "roofline": {"bound": "hbm", "kernel": "expert_gemm_kernel",
                          "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": (achieved / hbm_peak) if achieved else None, "peak_kind": peak_kind,
-                         "traffic": None,
+                         "traffic": EXPERT_GEMM_TRAFFIC_T512 if (T == 512 and args.precision == 1) else None,
+                         "traffic_source": "ncu capture of this workload, bytes per launch",
                          "bytes_per_launch": gemm_bytes / max(1, gemm_launches),
                          "ms_per_launch": gemm_ms / max(1, gemm_launches)},
             "block_hbm": {"achieved_gbs": block_gbs, "frac": block_gbs / hbm_peak,

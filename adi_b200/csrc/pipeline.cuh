@@ -50,37 +50,45 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
     return done != 0;
 }
 
+// Polls between the slow checks of a bounded wait. Each poll is one
+// try_wait (which itself may suspend the thread for a while); the clock and
+// the launch's error word are read only every kPollsPerCheck polls, so a
+// waiting warp neither spends issue slots on them nor wakes up late behind a
+// global load that is still in flight when the phase completes.
+constexpr uint32_t kPollsPerCheck = 64;
+
 // Waits for the phase of `bar` with parity `parity` to complete, at most
-// kWaitLimitNs. Returns false (and flags `error`) on expiry, and at once if
-// any wait of the launch has already expired, so a failed launch drains in
-// bounded time instead of paying the limit at every later wait.
+// kWaitLimitNs. Returns false (and flags `error`) on expiry, and soon after
+// any wait of the launch has expired, so a failed launch drains in bounded
+// time instead of paying the limit at every later wait.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *error) {
     if (mbar_test(bar, parity)) return true;
     const uint64_t start = global_ns();
-    while (!mbar_test(bar, parity)) {
-        if (*reinterpret_cast<volatile uint32_t *>(error) != 0) return false;
-        if (global_ns() - start > kWaitLimitNs) {
-            atomicOr(error, kErrorTimeout);
-            return false;
+    for (uint32_t polls = 1;; ++polls) {
+        if (mbar_test(bar, parity)) return true;
+        if (polls % kPollsPerCheck == 0) {
+            if (*reinterpret_cast<volatile uint32_t *>(error) != 0) return false;
+            if (global_ns() - start > kWaitLimitNs) {
+                atomicOr(error, kErrorTimeout);
+                return false;
+            }
         }
     }
-    return true;
 }
-
-// Waits for work this thread started itself (copies, MMAs), which completes
-// on its own: not cut short by another wait's failure, bounded all the same.
+// The same bound without giving up early on another wait's expiry: for a
+// thread's own copies or MMAs, which must land before the launch exits.
 __device__ __forceinline__ bool mbar_wait_own(uint64_t *bar, uint32_t parity, uint32_t *error) {
+    if (mbar_test(bar, parity)) return true;
     const uint64_t start = global_ns();
-    while (!mbar_test(bar, parity)) {
-        if (global_ns() - start > kWaitLimitNs) {
+    for (uint32_t polls = 1;; ++polls) {
+        if (mbar_test(bar, parity)) return true;
+        if (polls % kPollsPerCheck == 0 && global_ns() - start > kWaitLimitNs) {
             atomicOr(error, kErrorTimeout);
             return false;
         }
     }
-    return true;
 }
 
-// Makes mbarrier initialisation visible to the async (bulk copy) proxy.
 __device__ __forceinline__ void fence_barrier_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }

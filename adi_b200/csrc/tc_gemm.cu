@@ -2,8 +2,10 @@
 //
 // D[128 weight rows x N positions] = A[128 x K] . B[K x N] with fp32
 // accumulators in tensor memory. A is the packed matrix decoded from its
-// trellis codes straight into shared memory; B is the transformed input x',
-// loaded by TMA. Both are f16 (kind::f16). Decoded lattice values are exact in
+// trellis codes: straight into tensor memory for the expert codec (the MMA
+// reads A from TMEM, so the decoded tile never touches shared memory, whose
+// bandwidth the value gather needs), into shared memory for the NE codec. B
+// is the transformed input x', loaded by TMA. Both are f16 (kind::f16). Decoded lattice values are exact in
 // f16; the factors that could leave f16's range are exact powers of two taken
 // out and restored in the epilogue:
 //   expert  A = f16(value * gamma_tile * 2^ka)  ka per (expert, projection)
@@ -23,8 +25,10 @@
 //   warp 2 lane 0   B chunk (64 f16 x the unit's rows in 16-row boxes,
 //                   128B-swizzled) -> B ring (TMA), in its own warp so that
 //                   neither producer's waits hold up the other's issue
-//   warps 3..18     decoders: state -> values -> f16 into A's swizzled K-major
-//                   layout, A ring
+//   warps 3..18     decoders: state -> values -> f16 A. Expert: a lane owns a
+//                   weight row (TMEM lane) and decodes both states of that
+//                   row in two tiles per chunk into TMEM (tcgen05.st); NE:
+//                   A's swizzled K-major layout in shared memory
 //   warps 19..22    epilogue: tcgen05.ld, scale, fp32 out; 2 accumulators
 //
 // Every wait is bounded (pipeline.cuh). When one expires the launch drains
@@ -62,14 +66,21 @@ constexpr uint32_t kDecodeWarps = 16;
 constexpr uint32_t kDecodeWarp0 = 3;
 constexpr uint32_t kEpilogueWarp0 = kDecodeWarp0 + kDecodeWarps;
 constexpr uint32_t kTcThreads = (kEpilogueWarp0 + 4) * 32;
-constexpr uint32_t kTmemColumns = 2 * kTcMaxN;
+// Tensor memory: two accumulator slots of kTcMaxN columns, then (expert
+// codec) kTmemAStages A slots of 32 columns (128 lanes x 64 f16).
+constexpr uint32_t kTmemAStages = 4;
+constexpr uint32_t kTmemAColumn0 = 2 * kTcMaxN;
+constexpr uint32_t kTmemAColumns = kChunkK / 2;
+constexpr uint32_t kTmemColumns = 256;
+static_assert(kTmemAColumn0 + kTmemAStages * kTmemAColumns <= kTmemColumns, "tensor memory budget");
+constexpr uint32_t kMaxAStages = kTmemAStages > kAStages ? kTmemAStages : kAStages;
 
 struct Smem {
     static constexpr size_t a = 131072;  // 1024-aligned
     static constexpr size_t b = a + kAStages * kATileBytes;
     static constexpr size_t words = b + kBStages * kBTileBytes;
     static constexpr size_t bars = words + kWordStages * kWordSlotBytes;
-    static constexpr uint32_t kBars = 2 * kWordStages + 2 * kBStages + 2 * kAStages + 4 + 1;
+    static constexpr uint32_t kBars = 2 * kWordStages + 2 * kBStages + 2 * kMaxAStages + 4 + 1;
     static constexpr size_t total = bars + kBars * 8 + 16;
 };
 static_assert(Smem::total <= 232448, "shared memory budget");
@@ -83,6 +94,10 @@ struct Traits<TcCodec::kExpert> {
     static constexpr uint32_t tile_bytes = 48;
     static constexpr uint32_t tiles_per_row = 8;         // per chunk
     static constexpr uint32_t words_bytes = 8 * 8 * 48;  // 8 tile rows
+    // Word-slot stride per tile row: 432 bytes puts consecutive tile rows 12
+    // banks apart, so the two tile rows one warp reads never share a bank.
+    static constexpr uint32_t row_stride = 432;
+    static constexpr uint32_t a_stages = kTmemAStages;
 };
 template <>
 struct Traits<TcCodec::kNe> {
@@ -91,7 +106,11 @@ struct Traits<TcCodec::kNe> {
     static constexpr uint32_t tile_bytes = 128;
     static constexpr uint32_t tiles_per_row = 4;
     static constexpr uint32_t words_bytes = 8 * 4 * 128;
+    static constexpr uint32_t row_stride = 512;
+    static constexpr uint32_t a_stages = kAStages;
 };
+static_assert(8 * Traits<TcCodec::kExpert>::row_stride <= kWordSlotBytes, "expert word slot");
+static_assert(8 * Traits<TcCodec::kNe>::row_stride <= kWordSlotBytes, "NE word slot");
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
     // K-major, 128-byte swizzle: 8-row groups 1024 B apart (SBO), LBO unused
@@ -122,6 +141,27 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// The same with A read from tensor memory (128 lanes = rows, 8 columns of
+// f16 pairs = 16 K elements at a_tmem).
+__device__ __forceinline__ void mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// Eight consecutive 32-bit TMEM columns of this thread's lane, then waits
+// for the stores to complete.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(v[0]),
+        "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
@@ -196,8 +236,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t *b_full = w_empty + kWordStages;
     uint64_t *b_empty = b_full + kBStages;
     uint64_t *a_ready = b_empty + kBStages;
-    uint64_t *a_empty = a_ready + kAStages;
-    uint64_t *d_full = a_empty + kAStages;
+    uint64_t *a_empty = a_ready + kMaxAStages;
+    uint64_t *d_full = a_empty + kMaxAStages;
     uint64_t *d_empty = d_full + 2;
     uint64_t *mma_done = d_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
@@ -224,7 +264,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&b_full[s], 1);
             mbar_init(&b_empty[s], 1);
         }
-        for (uint32_t s = 0; s < kAStages; ++s) {
+        for (uint32_t s = 0; s < T::a_stages; ++s) {
             mbar_init(&a_ready[s], kDecodeWarps);
             mbar_init(&a_empty[s], 1);
         }
@@ -272,7 +312,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     const uint32_t seg = T::tiles_per_row * T::tile_bytes;
                     for (uint32_t row = 0; row < 8; ++row) {
                         const size_t tile = (size_t)(un.m_block * 8 + row) * TC + kc * T::tiles_per_row;
-                        bulk_load(dst + row * seg, trellis + tile * T::tile_bytes, seg, &w_full[r.slot]);
+                        bulk_load(dst + row * T::row_stride, trellis + tile * T::tile_bytes, seg, &w_full[r.slot]);
                     }
                     ++issued;
                     r.advance(kWordStages);
@@ -335,15 +375,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(a_tiles + a.slot * kATileBytes);
                     const uint32_t b_addr = smem_u32(b_tiles + b.slot * kBTileBytes);
+                    if (C == TcCodec::kExpert) {
+                        const uint32_t a_tmem = tmem_base + kTmemAColumn0 + a.slot * kTmemAColumns;
 #pragma unroll
-                    for (uint32_t k = 0; k < kChunkK / 16; ++k)
-                        mma_f16(d_tmem, smem_desc_sw128(a_addr + k * 32), smem_desc_sw128(b_addr + k * 32), idesc,
-                                (kc | k) != 0);
+                        for (uint32_t k = 0; k < kChunkK / 16; ++k)
+                            mma_f16_tmem_a(d_tmem, a_tmem + k * 8, smem_desc_sw128(b_addr + k * 32), idesc,
+                                           (kc | k) != 0);
+                    } else {
+                        const uint32_t a_addr = smem_u32(a_tiles + a.slot * kATileBytes);
+#pragma unroll
+                        for (uint32_t k = 0; k < kChunkK / 16; ++k)
+                            mma_f16(d_tmem, smem_desc_sw128(a_addr + k * 32), smem_desc_sw128(b_addr + k * 32),
+                                    idesc, (kc | k) != 0);
+                    }
                     mma_commit(&a_empty[a.slot]);
                     mma_commit(&b_empty[b.slot]);
-                    a.advance(kAStages);
+                    a.advance(T::a_stages);
                     b.advance(kBStages);
                 }
                 if (!ok) break;
@@ -360,21 +408,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         bool ok = true;
         if (C == TcCodec::kExpert) {
             const uint2 *table = reinterpret_cast<const uint2 *>(smem);
-            const uint32_t lr = lane >> 1, step = lane & 1u;
-            const uint32_t q = (lane * 12u) >> 5;
-            const uint32_t q1 = q + 1u == kExpertU32PerTile ? 0u : q + 1u;
+            // Lane = weight row of the chunk = TMEM lane: this warp may only
+            // reach lanes 32*(warp % 4) .. +31, i.e. tile rows tr0, tr0 + 1.
+            // The four warps of a lane quarter split the chunk's 8 tile
+            // columns in pairs: warp `pair` decodes tile columns 2*pair and
+            // 2*pair + 1. In a tile, a row is states 2*rl and 2*rl + 1, stream
+            // bits 24*rl .. 24*rl + 28: one funnel shift yields both.
+            const uint32_t quarter = warp & 3u, pair = dw >> 2;
+            const uint32_t tr = 2u * quarter + (lane >> 4), rl = lane & 15u;
+            const uint32_t bit0 = rl * 24u, wq = bit0 >> 5, woff = bit0 & 31u;
+            const uint32_t wq1 = wq + 1u == kExpertU32PerTile ? 0u : wq + 1u;
             const uint32_t neg_mask = half == 0 ? 0x8000u : 0u;
-            // Warp dw decodes tile column tcl = dw & 7 of each chunk, tile rows
-            // j0 .. j0+3 (j0 = (dw >> 3) * 4); a lane owns state `lane` (tile
-            // row lr, columns step*8 + 4h ..).
-            const uint32_t tcl = dw & 7u, j0 = (dw >> 3) * 4;
-            const uint32_t a_lane = (j0 * 16 + lr) * 128 + (((tcl ^ (lr & 7u)) << 4) | (step << 3));
-            // Lane i < 4 holds the f16x2 gamma of tile row j0 + i; fetched one
-            // chunk ahead so the load's latency hides behind a chunk of work.
-            auto fetch_gamma = [&](const Unit &un, const TcJob &J, uint32_t kc, float gscale) -> uint32_t {
-                if (lane >= 4) return 0u;
+            const uint32_t a_lane = tmem_base + ((32u * quarter) << 16) + kTmemAColumn0 + 8u * pair;
+            // The f16x2 gamma (x 2^ka) of this lane's two tiles of chunk kc;
+            // fetched a chunk ahead so the load's latency hides behind a
+            // chunk of work.
+            auto fetch_gamma = [&](const Unit &un, const TcJob &J, uint32_t kc, float gscale, uint32_t t) -> uint32_t {
                 const uint32_t TC = J.cols / 16, TR = J.rows / 16;
-                const uint32_t diag = un.m_block * 8 + j0 + lane + kc * 8 + tcl;
+                const uint32_t diag = un.m_block * 8 + tr + kc * 8 + 2u * pair + t;
                 const uint16_t *gam = J.gamma + (size_t)un.expert * J.gamma_stride;
                 const __half2 g2 =
                     __float2half2_rn(__half2float(__ushort_as_half(__ldg(gam + wave_index(TR, TC, diag)))) * gscale);
@@ -385,33 +436,45 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const TcJob &J = un.job ? p.job[1] : p.job[0];
                 const uint32_t chunks = J.cols / T::chunk_cols;
                 const float gscale = exp2f((float)J.ka[un.expert]);
-                uint32_t gnext = fetch_gamma(un, J, 0, gscale);
+                uint32_t gnext0 = fetch_gamma(un, J, 0, gscale, 0), gnext1 = fetch_gamma(un, J, 0, gscale, 1);
                 for (uint32_t kc = 0; kc < chunks; ++kc) {
-                    const uint32_t gpack = gnext;
-                    if (kc + 1 < chunks) gnext = fetch_gamma(un, J, kc + 1, gscale);
+                    const uint32_t gcur[2] = {gnext0, gnext1};
+                    if (kc + 1 < chunks) {
+                        gnext0 = fetch_gamma(un, J, kc + 1, gscale, 0);
+                        gnext1 = fetch_gamma(un, J, kc + 1, gscale, 1);
+                    }
                     if (ok) ok = mbar_wait(&w_full[w.slot], w.phase, p.error);
                     if (ok) ok = mbar_wait(&a_empty[a.slot], a.phase ^ 1u, p.error);
+                    ok = __all_sync(0xffffffffu, ok);  // tcgen05.st is warp-wide
                     if (ok) {
-                        const uint32_t *tw = reinterpret_cast<const uint32_t *>(word_tiles + w.slot * kWordSlotBytes) +
-                                             j0 * 96 + tcl * kExpertU32PerTile;
-                        uint8_t *a_tile = a_tiles + a.slot * kATileBytes + a_lane;
+                        tc_fence_after();
+                        const uint32_t *tw = reinterpret_cast<const uint32_t *>(word_tiles + w.slot * kWordSlotBytes +
+                                                                                tr * T::row_stride) +
+                                             2u * pair * kExpertU32PerTile;
+                        uint32_t out[8];
 #pragma unroll
-                        for (uint32_t j = 0; j < 4; ++j) {
-                            const uint32_t state =
-                                expert_window(stream_order(tw[j * 96 + q]), stream_order(tw[j * 96 + q1]), lane);
-                            const uint32_t prod = state_product(state);
-                            uint2 raw = table[expert_table_index(prod)];
-                            raw.x ^= (prod & 0x8000u) & neg_mask;  // bit 15 of s(s+1) negates component 0
-                            const uint32_t gj = __shfl_sync(0xffffffffu, gpack, j);
-                            const __half2 g2 = *reinterpret_cast<const __half2 *>(&gj);
-                            const __half2 v0 = __hmul2(*reinterpret_cast<const __half2 *>(&raw.x), g2);
-                            const __half2 v1 = __hmul2(*reinterpret_cast<const __half2 *>(&raw.y), g2);
-                            uint2 out;
-                            out.x = *reinterpret_cast<const uint32_t *>(&v0);
-                            out.y = *reinterpret_cast<const uint32_t *>(&v1);
-                            *reinterpret_cast<uint2 *>(a_tile + j * 2048) = out;
+                        for (uint32_t t = 0; t < 2; ++t) {
+                            const uint32_t *tile = tw + t * kExpertU32PerTile;
+                            const uint32_t window =
+                                __funnelshift_l(stream_order(tile[wq1]), stream_order(tile[wq]), woff);
+                            const uint32_t pa = state_product(window >> 16);
+                            const uint32_t pb = state_product((window >> 4) & 0xFFFFu);
+                            uint2 ra = table[expert_table_index(pa)];
+                            uint2 rb = table[expert_table_index(pb)];
+                            ra.x ^= (pa & 0x8000u) & neg_mask;  // bit 15 of s(s+1) negates component 0
+                            rb.x ^= (pb & 0x8000u) & neg_mask;
+                            const __half2 g2 = *reinterpret_cast<const __half2 *>(&gcur[t]);
+                            const __half2 va0 = __hmul2(*reinterpret_cast<const __half2 *>(&ra.x), g2);
+                            const __half2 va1 = __hmul2(*reinterpret_cast<const __half2 *>(&ra.y), g2);
+                            const __half2 vb0 = __hmul2(*reinterpret_cast<const __half2 *>(&rb.x), g2);
+                            const __half2 vb1 = __hmul2(*reinterpret_cast<const __half2 *>(&rb.y), g2);
+                            out[4 * t + 0] = *reinterpret_cast<const uint32_t *>(&va0);
+                            out[4 * t + 1] = *reinterpret_cast<const uint32_t *>(&va1);
+                            out[4 * t + 2] = *reinterpret_cast<const uint32_t *>(&vb0);
+                            out[4 * t + 3] = *reinterpret_cast<const uint32_t *>(&vb1);
                         }
-                        fence_async_shared();
+                        tmem_st8(a_lane + a.slot * kTmemAColumns, out);
+                        tc_fence_before();
                     }
                     __syncwarp();
                     if (lane == 0) {
@@ -419,7 +482,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         mbar_arrive(&w_empty[w.slot]);
                     }
                     w.advance(kWordStages);
-                    a.advance(kAStages);
+                    a.advance(T::a_stages);
                 }
             }
         } else {
@@ -462,7 +525,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         mbar_arrive(&w_empty[w.slot]);
                     }
                     w.advance(kWordStages);
-                    a.advance(kAStages);
+                    a.advance(T::a_stages);
                 }
             }
         }
@@ -476,6 +539,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const Unit un = unit_at(p, u);
             const TcJob &J = un.job ? p.job[1] : p.job[0];
             if (ok) ok = mbar_wait(&d_full[d.slot], d.phase, p.error);
+            ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-wide
             tc_fence_after();
             if (ok) {
                 const uint32_t n_pad = (un.count + 15u) & ~15u;

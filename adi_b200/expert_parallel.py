@@ -27,6 +27,8 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
+CUDA_STREAM_LEGACY = 0x1  # cudaStreamLegacy
+
 
 class DevicePhases:
     """The three device phases of one MoE layer shard, through the C ABI.
@@ -43,7 +45,12 @@ class DevicePhases:
         self.handle = ctx.upload_moe_shard(layer, rank * self.local, self.local)
 
     def _stream(self, device):
-        self.ctx.set_stream(torch.cuda.current_stream(device).cuda_stream)
+        # torch's default stream is CUDA's legacy stream, whose handle 0 the
+        # context would read as "its own stream"; name it explicitly
+        # (cudaStreamLegacy) so that the kernels stay ordered with torch's
+        # work and collectives on that stream.
+        handle = torch.cuda.current_stream(device).cuda_stream
+        self.ctx.set_stream(handle if handle else CUDA_STREAM_LEGACY)
 
     def dispatch(self, x: torch.Tensor):
         tokens = x.shape[0]

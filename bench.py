@@ -478,8 +478,18 @@ def run_ours(args, world, rank, local):
             ctx.moe_forward_batch_device(handles[k % L], xs.data_ptr(), tokens, out.data_ptr(), 0, 0)
         e.record(stream)
         torch.cuda.synchronize()
+        # The same steps again with stage timing (separately: its events
+        # would add to the timed run).
+        ctx.set_profiling(True)
+        ctx.reset_profile()
+        for k in range(50):
+            ctx.moe_forward_batch_device(handles[k % L], xs.data_ptr(), tokens, out.data_ptr(), 0, 0)
+        torch.cuda.synchronize()
+        sweep_stages = {k: v[0] / max(1, v[1]) for k, v in ctx.profile().items()}
+        ctx.set_profiling(False)
         sweep[f"ubatch_{tokens}"] = {"tokens_per_s": steps * tokens / (b.elapsed_time(e) / 1e3),
-                                     "ms_per_step": b.elapsed_time(e) / steps}
+                                     "ms_per_step": b.elapsed_time(e) / steps,
+                                     "stages_ms_per_step": sweep_stages}
 
     baseline = None
     if rank == 0 and world == 1 and not args.no_baseline:

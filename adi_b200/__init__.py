@@ -89,8 +89,8 @@ SIGNATURES = {
     "adi_cuda_ne_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_expert_matmul_device_noalloc": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_upload_moe_shard": (C.c_int, [_ctx, C.POINTER(MoeLayerDesc), C.c_uint32, C.c_uint32, C.POINTER(_h)]),
-    "adi_cuda_ep_dispatch_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p,
-                                              C.c_void_p, C.c_void_p]),
+    "adi_cuda_ep_dispatch_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p,
+                                              C.c_void_p, C.c_void_p, C.c_void_p]),
     "adi_cuda_ep_experts_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32,
                                              C.c_void_p]),
     "adi_cuda_ep_combine_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
@@ -346,10 +346,10 @@ class Context:
 
     # -- expert-parallel phases (device pointers, asynchronous) ---------------
     def ep_dispatch_device(self, shard: Handle, inputs_ptr: int, tokens: int, send_ptr: int, counts_ptr: int,
-                           route_experts_ptr: int = 0, route_weights_ptr: int = 0):
-        _check(self.lib.adi_cuda_ep_dispatch_device(self.ptr, shard.value, inputs_ptr, tokens, send_ptr, counts_ptr,
-                                                    route_experts_ptr or None, route_weights_ptr or None),
-               "ep_dispatch_device")
+                           route_experts_ptr: int = 0, route_weights_ptr: int = 0, logits_ptr: int = 0):
+        _check(self.lib.adi_cuda_ep_dispatch_device(self.ptr, shard.value, inputs_ptr, logits_ptr or None, tokens,
+                                                    send_ptr, counts_ptr, route_experts_ptr or None,
+                                                    route_weights_ptr or None), "ep_dispatch_device")
 
     def ep_experts_device(self, shard: Handle, recv_ptr: int, recv_counts_ptr: int, world: int, rows: int,
                           out_ptr: int):

@@ -417,7 +417,26 @@ int gemm_grid(adi_cuda_context *c, uint64_t items, int per_item) {
     return grid < per_item ? per_item : grid;
 }
 
-uint32_t row_blocks(uint32_t rows) { return (rows / 16 + kRowTiles - 1) / kRowTiles; }
+uint32_t row_blocks(uint32_t rows, uint32_t row_tiles = kRowTiles) {
+    return (rows / 16 + row_tiles - 1) / row_tiles;
+}
+
+// Tile rows per CUDA-core NE work item: one when the usual four would leave
+// SMs idle (small batches), so that more CTAs stream the matrix at once.
+uint32_t ne_row_tiles(adi_cuda_context *c, uint32_t tokens, uint32_t rows, uint32_t jobs) {
+    const uint64_t items = uint64_t((tokens + kMaxTokens - 1) / kMaxTokens) * jobs * row_blocks(rows);
+    return items < 2 * uint64_t(c->sms) ? 1u : uint32_t(kRowTiles);
+}
+
+// Tokens per CUDA-core NE work item: with one tile row per item, the next
+// power of two of the batch (at most eight), so that a short item carries
+// no idle token slots; otherwise eight.
+uint32_t ne_tokens_per_item(uint32_t row_tiles, uint32_t tokens) {
+    if (row_tiles != 1) return kMaxTokens;
+    uint32_t n = 1;
+    while (n < tokens && n < uint32_t(kMaxTokens)) n <<= 1;
+    return n;
+}
 
 // Positions per expert work item: the next power of two of the expected
 // positions per expert, at most 8.
@@ -430,6 +449,11 @@ uint32_t tokens_per_item(uint64_t expected) {
 // ---- standalone matmuls on device pointers -------------------------------
 
 bool tensor_core_shape(uint32_t rows, uint32_t cols) { return rows % 128 == 0 && cols % 128 == 0; }
+
+// Up to this many tokens the block's combine runs as one block per route,
+// then one per token, instead of one block per token doing all nine
+// transforms.
+constexpr uint32_t kSplitCombineTokens = 64;
 
 // Below this many inputs an NE projection streams faster on CUDA cores.
 constexpr uint32_t kNeTensorCoreMinBatch = 16;
@@ -632,9 +656,11 @@ void ne_matmul_dev(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batc
     NeGemmParams gp{};
     gp.job[0] = NeJob{m.trellis->as<uint32_t>(), xp, acc, m.rows, m.cols, m.weight_scale};
     gp.job[1] = gp.job[0];
-    gp.work = WorkList{nullptr, nullptr, batch, 1, kMaxTokens};
     gp.table = m.codec->table.as<float2>();
-    const uint64_t items = uint64_t((batch + kMaxTokens - 1) / kMaxTokens) * row_blocks(m.rows);
+    gp.row_tiles = ne_row_tiles(c, batch, m.rows, 1);
+    const uint32_t nt = ne_tokens_per_item(gp.row_tiles, batch);
+    gp.work = WorkList{nullptr, nullptr, batch, 1, nt};
+    const uint64_t items = uint64_t((batch + nt - 1) / nt) * row_blocks(m.rows, gp.row_tiles);
     launch_ne_gemm(gp, gemm_grid(c, items, 1), c->stream);
     launch_finalize(acc, nullptr, m.sv->ptr, 0, batch, m.rows, transform_scale(m.rows), out, c->stream);
     c->stage_end();
@@ -769,9 +795,11 @@ void shared_expert(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, 
         NeGemmParams np{};
         np.job[0] = NeJob{L.shared[0].trellis->as<uint32_t>(), sxg, sacc_g, I, H, L.shared[0].weight_scale};
         np.job[1] = NeJob{L.shared[1].trellis->as<uint32_t>(), sxu, sacc_u, I, H, L.shared[1].weight_scale};
-        np.work = WorkList{nullptr, nullptr, T, 2, kMaxTokens};
         np.table = L.shared[0].codec->table.as<float2>();
-        const uint64_t ne_items = uint64_t((T + kMaxTokens - 1) / kMaxTokens) * 2 * row_blocks(I);
+        np.row_tiles = ne_row_tiles(c, T, I, 2);
+        const uint32_t gu_nt = ne_tokens_per_item(np.row_tiles, T);
+        np.work = WorkList{nullptr, nullptr, T, 2, gu_nt};
+        const uint64_t ne_items = uint64_t((T + gu_nt - 1) / gu_nt) * 2 * row_blocks(I, np.row_tiles);
         launch_ne_gemm(np, gemm_grid(c, ne_items, 1), s);
         float *sxd = c->buffer<float>("moe_sxd", size_t(T) * I);
         MidParams smp{};
@@ -792,9 +820,11 @@ void shared_expert(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, 
         NeGemmParams nd{};
         nd.job[0] = NeJob{L.shared[2].trellis->as<uint32_t>(), sxd, sacc_d, H, I, L.shared[2].weight_scale};
         nd.job[1] = nd.job[0];
-        nd.work = WorkList{nullptr, nullptr, T, 1, kMaxTokens};
         nd.table = np.table;
-        const uint64_t nd_items = uint64_t((T + kMaxTokens - 1) / kMaxTokens) * row_blocks(H);
+        nd.row_tiles = ne_row_tiles(c, T, H, 1);
+        const uint32_t d_nt = ne_tokens_per_item(nd.row_tiles, T);
+        nd.work = WorkList{nullptr, nullptr, T, 1, d_nt};
+        const uint64_t nd_items = uint64_t((T + d_nt - 1) / d_nt) * row_blocks(H, nd.row_tiles);
         launch_ne_gemm(nd, gemm_grid(c, nd_items, 1), s);
         c->stage_end();
         c->after_launch(4);
@@ -1007,7 +1037,7 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     rp.count_gate_up = counts2;
     rp.count_down = counts2 + 1;
     c->stage(kStageRoute);
-    launch_route(rp, s);
+    const uint32_t route_launches = launch_route(rp, s);
     c->stage_end();
 
     float *acc_d = routed_experts(c, L, in, P, rp, nt, tc);
@@ -1016,6 +1046,39 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     float *sacc_d = c->buffer<float>("moe_sacc_d", size_t(T) * H);
     shared_expert(c, L, in, T, sacc_d);
 
+    if (T <= kSplitCombineTokens) {
+        // Small batches: one block per route applies the down projection's
+        // output transform (all routes in parallel), then a block per token
+        // sums them; the same arithmetic as the fused combine.
+        float *route_rows = c->buffer<float>("moe_route_rows", P * H);
+        EpFinalizeParams fp{};
+        fp.acc_down = acc_d;
+        fp.half_stride = P * H;
+        fp.pos_expert = rp.pos_expert;
+        fp.sv_down = L.sv[2]->as<uint16_t>();
+        fp.hidden = H;
+        fp.positions = uint32_t(P);
+        fp.scale = transform_scale(H);
+        fp.expert_rows = route_rows;
+        EpCombineParams ecp{};
+        ecp.returned = route_rows;
+        ecp.route_to_grouped = rp.route_to_grouped;
+        ecp.route_weights = rw;
+        ecp.shared_acc = sacc_d;
+        ecp.shared_sv = L.shared[2].sv->as<int8_t>();
+        ecp.gate_logits = logits + E;
+        ecp.gate_stride = E + 1;
+        ecp.hidden = H;
+        ecp.tokens = T;
+        ecp.scale = transform_scale(H);
+        ecp.out = out;
+        c->stage(kStageCombine);
+        launch_ep_finalize(fp, s);
+        launch_ep_combine(ecp, s);
+        c->stage_end();
+        c->after_launch(2 + route_launches + 2);
+        return;
+    }
     CombineParams cp{};
     cp.acc_down = acc_d;
     cp.half_stride = P * H;
@@ -1034,9 +1097,9 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     c->stage(kStageCombine);
     launch_combine(cp, s);
     c->stage_end();
-    // router, top-k, 3 routing kernels, combine (the routed and shared
+    // router, top-k, the routing kernels, combine (the routed and shared
     // experts count their own four each)
-    c->after_launch(2 + 3 + 1);
+    c->after_launch(2 + route_launches + 1);
 }
 
 // Host-pointer wrapper: stage inputs, run on device, read outputs back.
@@ -1125,8 +1188,9 @@ uint64_t upload_moe(adi_cuda_context *c, const adi_moe_layer &layer, uint32_t fi
 // Router, top-k and the counting sort over all experts; the rows of every
 // route in expert (= destination) order; the shared expert of these tokens.
 // Routes, weights, positions and shared sums stay for ep_combine_dev.
-void ep_dispatch_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const float *in, uint32_t T, float *send,
-                     uint32_t *expert_counts, uint32_t *route_experts_out, float *route_weights_out) {
+void ep_dispatch_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const float *in, const float *given_logits,
+                     uint32_t T, float *send, uint32_t *expert_counts, uint32_t *route_experts_out,
+                     float *route_weights_out) {
     if (T == 0) invalid("MoE batch shape mismatch");
     const uint32_t H = L.hidden, E = L.experts;
     const size_t P = size_t(T) * 8;
@@ -1135,8 +1199,14 @@ void ep_dispatch_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const floa
     uint32_t *re = c->buffer<uint32_t>("ep_re", P);
     float *rw = c->buffer<float>("ep_rw", P);
     c->stage(kStageRouter);
-    launch_bf16_gemm(L.router->as<uint16_t>(), E, L.router->as<uint16_t>() + size_t(E) * H, 1, in, T, H, logits,
-                     E + 1, s);
+    if (given_logits) {
+        check(cudaMemcpyAsync(logits, given_logits, size_t(T) * (E + 1) * 4, cudaMemcpyDeviceToDevice, s),
+              "logits copy");
+    } else {
+        launch_bf16_gemm(L.router->as<uint16_t>(), E, L.router->as<uint16_t>() + size_t(E) * H, 1, in, T, H,
+                         logits, E + 1, s);
+        c->after_launch(1);
+    }
     c->stage_end();
     c->stage(kStageTopk);
     launch_top_experts(logits, E + 1, T, E, re, rw, s);
@@ -1161,10 +1231,10 @@ void ep_dispatch_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const floa
     rp.count_gate_up = counts2;
     rp.count_down = counts2 + 1;
     c->stage(kStageRoute);
-    launch_route(rp, s);
+    const uint32_t route_launches = launch_route(rp, s);
     launch_ep_gather(in, rp.grouped, uint32_t(P), H, send, s);
     c->stage_end();
-    c->after_launch(2 + 3 + 1);
+    c->after_launch(1 + route_launches + 1);
 
     shared_expert(c, L, in, T, c->buffer<float>("ep_sacc", size_t(T) * H));
     if (route_experts_out)
@@ -1646,15 +1716,15 @@ int adi_cuda_rms_norm(adi_cuda_context *c, const float *inputs, const uint16_t *
     });
 }
 
-int adi_cuda_ep_dispatch_device(adi_cuda_context *c, adi_cuda_handle h, const float *in, uint32_t tokens,
-                                float *send_rows, uint32_t *expert_counts, uint32_t *route_experts,
-                                float *route_weights) {
+int adi_cuda_ep_dispatch_device(adi_cuda_context *c, adi_cuda_handle h, const float *in,
+                                const float *router_logits, uint32_t tokens, float *send_rows,
+                                uint32_t *expert_counts, uint32_t *route_experts, float *route_weights) {
     return guarded([&] {
         std::lock_guard<std::mutex> g(require(c)->lock);
         use_device(c);
         if (!in || !send_rows || !expert_counts) invalid("input, send or count pointer is null");
-        ep_dispatch_dev(c, h, lookup(c->moes, h, "MoE layer"), in, tokens, send_rows, expert_counts, route_experts,
-                        route_weights);
+        ep_dispatch_dev(c, h, lookup(c->moes, h, "MoE layer"), in, router_logits, tokens, send_rows, expert_counts,
+                        route_experts, route_weights);
     });
 }
 

@@ -110,8 +110,8 @@ __global__ void __launch_bounds__(256) ep_finalize_regs_kernel(EpFinalizeParams 
     __shared__ float sh[256 * R];
     constexpr uint32_t H = 256u * R;
     const uint32_t pos = blockIdx.x, c0 = threadIdx.x * R;
-    if (pos >= *p.placed) return;
-    const uint32_t e = p.pos_expert[pos], row = p.grouped[pos];
+    if (p.placed && pos >= *p.placed) return;
+    const uint32_t e = p.pos_expert[pos], row = p.grouped ? p.grouped[pos] : pos;
     float v[R], v1[R];
     load_regs<R>(p.acc_down + (size_t)pos * H + c0, v);
     load_regs<R>(p.acc_down + p.half_stride + (size_t)pos * H + c0, v1);
@@ -127,8 +127,8 @@ __global__ void __launch_bounds__(256) ep_finalize_regs_kernel(EpFinalizeParams 
 __global__ void ep_finalize_kernel(EpFinalizeParams p) {
     extern __shared__ float v[];
     const uint32_t pos = blockIdx.x, H = p.hidden;
-    if (pos >= *p.placed) return;
-    const uint32_t e = p.pos_expert[pos], row = p.grouped[pos];
+    if (p.placed && pos >= *p.placed) return;
+    const uint32_t e = p.pos_expert[pos], row = p.grouped ? p.grouped[pos] : pos;
     const float *a0 = p.acc_down + (size_t)pos * H, *a1 = a0 + p.half_stride;
     for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) v[i] = a0[i] + a1[i];
     __syncthreads();

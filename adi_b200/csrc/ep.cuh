@@ -38,12 +38,15 @@ struct EpPlanParams {
 void launch_ep_plan(const EpPlanParams &p, cudaStream_t s);
 
 // expert_rows[grouped[pos]] = H(acc0[pos] + acc1[pos]) / sqrt(H) * sv_e: the
-// output transform of the down projection, written in receive order.
+// output transform of the down projection, written in receive order (or in
+// position order: the one-GPU block uses the pair for small batches, where
+// one block per route spreads the transforms over many SMs).
 struct EpFinalizeParams {
     const float *acc_down;     // [2][positions][hidden]
     size_t half_stride;
-    const uint32_t *grouped, *pos_expert;
-    const uint32_t *placed;    // positions at or past *placed are skipped
+    const uint32_t *grouped;   // output row of each position; null: the position itself
+    const uint32_t *pos_expert;
+    const uint32_t *placed;    // positions at or past *placed are skipped; null: none
     const uint16_t *sv_down;   // f16 [local][hidden]
     uint32_t hidden, positions;
     float scale;

@@ -207,6 +207,8 @@ void launch_prep(const PrepParams &p, cudaStream_t s) {
         case 512: prep_regs_kernel<2><<<grid, 256, 0, s>>>(p); return;
         case 1024: prep_regs_kernel<4><<<grid, 256, 0, s>>>(p); return;
         case 2048: prep_regs_kernel<8><<<grid, 256, 0, s>>>(p); return;
+        case 4096: prep_regs_kernel<16><<<grid, 256, 0, s>>>(p); return;
+        case 8192: prep_regs_kernel<32><<<grid, 256, 0, s>>>(p); return;
         default: prep_kernel<<<grid, 256, p.cols * sizeof(float), s>>>(p);
     }
 }
@@ -254,6 +256,8 @@ void launch_finalize(const float *acc0, const float *acc1, const void *sv, int s
         case 512: finalize_regs_kernel<2><<<batch, 256, 0, s>>>(acc0, acc1, sv, sv_is_f16, scale, out); return;
         case 1024: finalize_regs_kernel<4><<<batch, 256, 0, s>>>(acc0, acc1, sv, sv_is_f16, scale, out); return;
         case 2048: finalize_regs_kernel<8><<<batch, 256, 0, s>>>(acc0, acc1, sv, sv_is_f16, scale, out); return;
+        case 4096: finalize_regs_kernel<16><<<batch, 256, 0, s>>>(acc0, acc1, sv, sv_is_f16, scale, out); return;
+        case 8192: finalize_regs_kernel<32><<<batch, 256, 0, s>>>(acc0, acc1, sv, sv_is_f16, scale, out); return;
         default: finalize_kernel<<<batch, 256, rows * sizeof(float), s>>>(acc0, acc1, sv, sv_is_f16, rows, scale, out);
     }
 }
@@ -404,22 +408,34 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) expert_stream_kernel(const E
         if (!failed) {
             const uint32_t *words = reinterpret_cast<const uint32_t *>(ring + slot * kSlabBytes);
             const float *xrow = J.x + (size_t)it.pos0 * J.cols + (lane & 1u) * 8 + half * 4;
-            float4 xv[NT], xn[NT];
-            uint32_t tc = cw;
+            // Inputs are loaded kXAhead tile columns ahead of their use (a
+            // ring of kXAhead x NT float4 in registers), so that a short
+            // iteration of few tokens does not wait on each load.
+            constexpr int kXAhead = NT >= 8 ? 1 : 8 / NT;
+            float4 xr[kXAhead][NT];
 #pragma unroll
-            for (int t = 0; t < NT; ++t)
-                xn[t] = ((uint32_t)t < n && tc < TC)
-                            ? __ldg(reinterpret_cast<const float4 *>(xrow + (size_t)t * J.cols + tc * 16))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-            for (; tc < TC; tc += CW) {
+            for (int d = 0; d < kXAhead; ++d)
 #pragma unroll
-                for (int t = 0; t < NT; ++t) xv[t] = xn[t];
-                const uint32_t next = tc + CW;
+                for (int t = 0; t < NT; ++t) {
+                    const uint32_t tcd = cw + d * CW;
+                    xr[d][t] = ((uint32_t)t < n && tcd < TC)
+                                   ? __ldg(reinterpret_cast<const float4 *>(xrow + (size_t)t * J.cols + tcd * 16))
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            for (uint32_t tc0 = cw; tc0 < TC; tc0 += kXAhead * CW)
+#pragma unroll
+            for (int d = 0; d < kXAhead; ++d) {
+                const uint32_t tc = tc0 + d * CW;
+                if (tc >= TC) break;
+                float4 xv[NT];
+#pragma unroll
+                for (int t = 0; t < NT; ++t) xv[t] = xr[d][t];
+                const uint32_t next = tc + kXAhead * CW;
 #pragma unroll
                 for (int t = 0; t < NT; ++t)
-                    xn[t] = ((uint32_t)t < n && next < TC)
-                                ? __ldg(reinterpret_cast<const float4 *>(xrow + (size_t)t * J.cols + next * 16))
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
+                    xr[d][t] = ((uint32_t)t < n && next < TC)
+                                   ? __ldg(reinterpret_cast<const float4 *>(xrow + (size_t)t * J.cols + next * 16))
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                 for (int r = 0; r < kRowTiles; ++r) {
                     if ((uint32_t)r >= rows) break;
@@ -511,6 +527,7 @@ void launch_expert_gemm(const ExpertGemmParams &p, int grid, cudaStream_t s) {
 // states 4L..4L+3 of a tile (row L>>1, columns (L&1)*8 .. +7), decoded from
 // u32 words L and L+1 of the tile's 128-byte stream.
 // ---------------------------------------------------------------------------
+template <int RT, int NT>
 __global__ void __launch_bounds__(kGemmThreads, 1) ne_gemm_kernel(const NeGemmParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     float2 *table = reinterpret_cast<float2 *>(smem);
@@ -520,7 +537,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) ne_gemm_kernel(const NeGemmPa
         table[i] = p.table[i / kNeTableCopies];
     __syncthreads();
 
-    const uint32_t rb0 = (p.job[0].rows / 16 + kRowTiles - 1) / kRowTiles;
+    const uint32_t rb0 = (p.job[0].rows / 16 + RT - 1) / RT;
     const uint32_t n_items = work_count(p.work, rb0);
     const float2 *my_table = table + (lane & (kNeTableCopies - 1));
 
@@ -530,32 +547,75 @@ __global__ void __launch_bounds__(kGemmThreads, 1) ne_gemm_kernel(const NeGemmPa
         const uint32_t TC = J.cols / 16, TR = J.rows / 16;
         const uint32_t n = it.count;
 
-        float acc[kRowTiles][kMaxTokens];
+        float acc[RT][NT];
 #pragma unroll
-        for (int r = 0; r < kRowTiles; ++r)
+        for (int r = 0; r < RT; ++r)
 #pragma unroll
-            for (int t = 0; t < kMaxTokens; ++t) acc[r][t] = 0.0f;
+            for (int t = 0; t < NT; ++t) acc[r][t] = 0.0f;
 
-        for (uint32_t tc = warp; tc < TC; tc += kGemmWarps) {
-            float4 x0[kMaxTokens], x1[kMaxTokens];
-            const uint32_t col = tc * 16 + (lane & 1u) * 8;
+        // Inputs are loaded kXAhead tile columns ahead of their use (a ring
+        // in registers), so that a short iteration of few tokens does not
+        // wait on each load; each row's partial sums still accumulate in
+        // tile-column order.
+        constexpr int kXAhead = NT >= 8 ? 1 : 8 / NT;
+        const uint32_t col0 = (lane & 1u) * 8;
+        // The tile words ride in the same ring: word `lane` of tile (row r,
+        // column tc), loaded kXAhead columns ahead.
+        auto tile_word = [&](uint32_t r, uint32_t tc) -> uint32_t {
+            const uint32_t tr = it.row_block * RT + r;
+            return (tr < TR && tc < TC) ? __ldg(J.trellis + (size_t)(tr * TC + tc) * kNeU32PerTile + lane) : 0u;
+        };
+        float4 xr0[kXAhead][NT], xr1[kXAhead][NT];
+        uint32_t wr[kXAhead][RT];
 #pragma unroll
-            for (int t = 0; t < kMaxTokens; ++t) {
-                if ((uint32_t)t < n) {
-                    const float4 *src = reinterpret_cast<const float4 *>(
-                        J.x + (size_t)(it.pos0 + t) * J.cols + col);
-                    x0[t] = __ldg(src);
-                    x1[t] = __ldg(src + 1);
+        for (int d = 0; d < kXAhead; ++d) {
+            const uint32_t tcd = warp + d * kGemmWarps;
+#pragma unroll
+            for (int r = 0; r < RT; ++r) wr[d][r] = tile_word(r, tcd);
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                if ((uint32_t)t < n && tcd < TC) {
+                    const float4 *src =
+                        reinterpret_cast<const float4 *>(J.x + (size_t)(it.pos0 + t) * J.cols + tcd * 16 + col0);
+                    xr0[d][t] = __ldg(src);
+                    xr1[d][t] = __ldg(src + 1);
                 } else {
-                    x0[t] = x1[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    xr0[d][t] = xr1[d][t] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+        }
+        for (uint32_t tc0 = warp; tc0 < TC; tc0 += kXAhead * kGemmWarps)
+#pragma unroll
+        for (int d = 0; d < kXAhead; ++d) {
+            const uint32_t tc = tc0 + d * kGemmWarps;
+            if (tc >= TC) break;
+            float4 x0[NT], x1[NT];
+            uint32_t words[RT];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                x0[t] = xr0[d][t];
+                x1[t] = xr1[d][t];
+            }
+            const uint32_t next = tc + kXAhead * kGemmWarps;
+#pragma unroll
+            for (int r = 0; r < RT; ++r) {
+                words[r] = wr[d][r];
+                wr[d][r] = tile_word(r, next);
+            }
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                if ((uint32_t)t < n && next < TC) {
+                    const float4 *src =
+                        reinterpret_cast<const float4 *>(J.x + (size_t)(it.pos0 + t) * J.cols + next * 16 + col0);
+                    xr0[d][t] = __ldg(src);
+                    xr1[d][t] = __ldg(src + 1);
                 }
             }
 #pragma unroll
-            for (int r = 0; r < kRowTiles; ++r) {
-                const uint32_t tr = it.row_block * kRowTiles + r;
+            for (int r = 0; r < RT; ++r) {
+                const uint32_t tr = it.row_block * RT + r;
                 if (tr >= TR) break;
-                const uint32_t *tw = J.trellis + (size_t)(tr * TC + tc) * kNeU32PerTile;
-                const uint32_t v = __ldg(tw + lane);
+                const uint32_t v = words[r];
                 const uint32_t v2 = __shfl_sync(0xffffffffu, v, (lane + 1u) & 31u);
                 const uint32_t s0 = v & 0xFFFFu;
                 const uint32_t s1 = __byte_perm(v, 0, 0x4403);
@@ -566,7 +626,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) ne_gemm_kernel(const NeGemmPa
                 const float2 w2 = my_table[ne_table_index(state_product(s2)) * kNeTableCopies];
                 const float2 w3 = my_table[ne_table_index(state_product(s3)) * kNeTableCopies];
 #pragma unroll
-                for (int t = 0; t < kMaxTokens; ++t) {
+                for (int t = 0; t < NT; ++t) {
                     if ((uint32_t)t < n) {
                         float part = w0.x * x0[t].x;
                         part = fmaf(w0.y, x0[t].y, part);
@@ -583,36 +643,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1) ne_gemm_kernel(const NeGemmPa
         }
 
 #pragma unroll
-        for (int r = 0; r < kRowTiles; ++r)
+        for (int r = 0; r < RT; ++r)
 #pragma unroll
-            for (int t = 0; t < kMaxTokens; ++t) acc[r][t] += __shfl_xor_sync(0xffffffffu, acc[r][t], 1);
+            for (int t = 0; t < NT; ++t) acc[r][t] += __shfl_xor_sync(0xffffffffu, acc[r][t], 1);
         if ((lane & 1u) == 0) {
 #pragma unroll
-            for (int r = 0; r < kRowTiles; ++r)
+            for (int r = 0; r < RT; ++r)
 #pragma unroll
-                for (int t = 0; t < kMaxTokens; ++t)
-                    red[((warp * kRowTiles + r) * 16 + (lane >> 1)) * kMaxTokens + t] = acc[r][t];
+                for (int t = 0; t < NT; ++t)
+                    red[((warp * RT + r) * 16 + (lane >> 1)) * kMaxTokens + t] = acc[r][t];
         }
         __syncthreads();
-        const uint32_t rows_here = min((uint32_t)kRowTiles, TR - it.row_block * kRowTiles) * 16;
+        const uint32_t rows_here = min((uint32_t)RT, TR - it.row_block * RT) * 16;
         for (uint32_t idx = threadIdx.x; idx < rows_here * n; idx += blockDim.x) {
             const uint32_t t = idx / rows_here, row = idx % rows_here;
             float sum = 0.0f;
 #pragma unroll
-            for (int w = 0; w < kGemmWarps; ++w) sum += red[((w * kRowTiles) * 16 + row) * kMaxTokens + t];
-            J.acc[(size_t)(it.pos0 + t) * J.rows + it.row_block * kRowTiles * 16 + row] = sum * J.weight_scale;
+            for (int w = 0; w < kGemmWarps; ++w) sum += red[((w * RT) * 16 + row) * kMaxTokens + t];
+            J.acc[(size_t)(it.pos0 + t) * J.rows + it.row_block * RT * 16 + row] = sum * J.weight_scale;
         }
         __syncthreads();
     }
 }
 
-void launch_ne_gemm(const NeGemmParams &p, int grid, cudaStream_t s) {
+template <int RT, int NT>
+void launch_ne_instance(const NeGemmParams &p, int grid, cudaStream_t s) {
     static bool configured = false;
     if (!configured) {
-        cudaFuncSetAttribute(ne_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kNeGemmSmem);
+        cudaFuncSetAttribute(ne_gemm_kernel<RT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kNeGemmSmem);
         configured = true;
     }
-    ne_gemm_kernel<<<grid, kGemmThreads, kNeGemmSmem, s>>>(p);
+    ne_gemm_kernel<RT, NT><<<grid, kGemmThreads, kNeGemmSmem, s>>>(p);
+}
+
+void launch_ne_gemm(const NeGemmParams &p, int grid, cudaStream_t s) {
+    // Small batches: one tile row per item and 1, 2, 4 or 8 tokens per item
+    // (the work list's chunk); otherwise four tile rows and eight tokens.
+    if (p.row_tiles != 1) return launch_ne_instance<kRowTiles, kMaxTokens>(p, grid, s);
+    switch (p.work.chunk) {
+        case 1: return launch_ne_instance<1, 1>(p, grid, s);
+        case 2: return launch_ne_instance<1, 2>(p, grid, s);
+        case 4: return launch_ne_instance<1, 4>(p, grid, s);
+        default: return launch_ne_instance<1, kMaxTokens>(p, grid, s);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -665,14 +738,19 @@ __global__ void bf16_gemm_kernel(const uint16_t *w0, uint32_t rows0, const uint1
 // Wide variant for cols % 256 == 0: a lane takes 8 consecutive columns per
 // step -- one 16-byte load of each of its warp's 4 weight rows, two 16-byte
 // shared loads per token -- for 256 FMAs per 20 memory instructions.
+// NT tokens per block, RPW rows per warp (8 warps). Every (row, token) sum
+// runs the same sequence whatever NT and RPW are -- a lane accumulates its
+// columns lane*8 + 256*i in order, then the warp adds its lanes -- so a
+// token's logits do not depend on the batch it came in.
+template <int NT, int RPW>
 __global__ void __launch_bounds__(256) bf16_gemm_wide_kernel(const uint16_t *w0, uint32_t rows0,
                                                              const uint16_t *w1, uint32_t rows1, const float *x,
                                                              uint32_t tokens, uint32_t cols, float *out,
                                                              uint32_t out_stride) {
     extern __shared__ float xs[];
-    const uint32_t t0 = blockIdx.x * 8;
-    const uint32_t nt = min(8u, tokens - t0);
-    for (uint32_t i = threadIdx.x; i < 2 * cols; i += blockDim.x) {
+    const uint32_t t0 = blockIdx.x * NT;
+    const uint32_t nt = min((uint32_t)NT, tokens - t0);
+    for (uint32_t i = threadIdx.x; i < NT * cols / 4; i += blockDim.x) {
         const uint32_t t = i / (cols / 4);
         const uint32_t c4 = i % (cols / 4);
         reinterpret_cast<float4 *>(xs)[i] = t < nt ? reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * cols)[c4]
@@ -680,26 +758,26 @@ __global__ void __launch_bounds__(256) bf16_gemm_wide_kernel(const uint16_t *w0,
     }
     __syncthreads();
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t rbase = blockIdx.y * 32 + warp * 4;
+    const uint32_t rbase = blockIdx.y * (8 * RPW) + warp * RPW;
     const uint32_t R = rows0 + rows1;
-    const uint16_t *row_ptr[4];
+    const uint16_t *row_ptr[RPW];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < RPW; ++i) {
         const uint32_t r = rbase + i;
         row_ptr[i] = r < rows0 ? w0 + (size_t)r * cols : (r < R ? w1 + (size_t)(r - rows0) * cols : nullptr);
     }
-    float acc[4][8] = {};
+    float acc[RPW][NT] = {};
     for (uint32_t c = lane * 8; c < cols; c += 256) {
-        float xv[8][8];
+        float xv[NT][8];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
+        for (int t = 0; t < NT; ++t) {
             const float4 a = reinterpret_cast<const float4 *>(xs + t * cols + c)[0];
             const float4 b = reinterpret_cast<const float4 *>(xs + t * cols + c)[1];
             xv[t][0] = a.x; xv[t][1] = a.y; xv[t][2] = a.z; xv[t][3] = a.w;
             xv[t][4] = b.x; xv[t][5] = b.y; xv[t][6] = b.z; xv[t][7] = b.w;
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < RPW; ++i) {
             if (!row_ptr[i]) continue;
             const uint4 wq = __ldg(reinterpret_cast<const uint4 *>(row_ptr[i] + c));
             const uint32_t wp[4] = {wq.x, wq.y, wq.z, wq.w};
@@ -707,17 +785,30 @@ __global__ void __launch_bounds__(256) bf16_gemm_wide_kernel(const uint16_t *w0,
             for (int k = 0; k < 8; ++k) {
                 const float wv = __uint_as_float((k & 1) ? (wp[k >> 1] & 0xFFFF0000u) : (wp[k >> 1] << 16));
 #pragma unroll
-                for (int t = 0; t < 8; ++t) acc[i][t] = fmaf(wv, xv[t][k], acc[i][t]);
+                for (int t = 0; t < NT; ++t) acc[i][t] = fmaf(wv, xv[t][k], acc[i][t]);
             }
         }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < RPW; ++i)
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
+        for (int t = 0; t < NT; ++t) {
             const float v = warp_sum(acc[i][t]);
             if (lane == 0 && row_ptr[i] && (uint32_t)t < nt) out[(size_t)(t0 + t) * out_stride + rbase + i] = v;
         }
+}
+
+template <int NT, int RPW>
+void launch_bf16_wide(const uint16_t *w0, uint32_t rows0, const uint16_t *w1, uint32_t rows1, const float *x,
+                      uint32_t tokens, uint32_t cols, float *out, uint32_t out_stride, cudaStream_t s) {
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(bf16_gemm_wide_kernel<NT, RPW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        configured = true;
+    }
+    dim3 grid((tokens + NT - 1) / NT, (rows0 + rows1 + 8 * RPW - 1) / (8 * RPW));
+    bf16_gemm_wide_kernel<NT, RPW><<<grid, 256, NT * cols * sizeof(float), s>>>(w0, rows0, w1, rows1, x, tokens,
+                                                                              cols, out, out_stride);
 }
 
 void launch_bf16_gemm(const uint16_t *w0, uint32_t rows0, const uint16_t *w1, uint32_t rows1,
@@ -725,19 +816,16 @@ void launch_bf16_gemm(const uint16_t *w0, uint32_t rows0, const uint16_t *w1, ui
                       cudaStream_t s) {
     if (tokens == 0) return;
     // The wide kernel needs 16-byte aligned rows: cols a multiple of 256 and
-    // both weight bases 16-byte aligned (device allocations are).
+    // both weight bases 16-byte aligned (device allocations are). Small
+    // batches take one row per warp, so that the rows spread over more SMs.
     if (cols % 256 == 0 && (reinterpret_cast<uintptr_t>(w0) & 15u) == 0 &&
         (rows1 == 0 || (reinterpret_cast<uintptr_t>(w1) & 15u) == 0) &&
         (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
-        static bool wide_configured = false;
-        if (!wide_configured) {
-            cudaFuncSetAttribute(bf16_gemm_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-            wide_configured = true;
-        }
-        dim3 grid((tokens + 7) / 8, (rows0 + rows1 + 31) / 32);
-        bf16_gemm_wide_kernel<<<grid, 256, 8 * cols * sizeof(float), s>>>(w0, rows0, w1, rows1, x, tokens, cols,
-                                                                           out, out_stride);
-        return;
+        if (tokens == 1) return launch_bf16_wide<1, 1>(w0, rows0, w1, rows1, x, tokens, cols, out, out_stride, s);
+        if (tokens == 2) return launch_bf16_wide<2, 1>(w0, rows0, w1, rows1, x, tokens, cols, out, out_stride, s);
+        if (tokens <= 4) return launch_bf16_wide<4, 1>(w0, rows0, w1, rows1, x, tokens, cols, out, out_stride, s);
+        if (tokens <= 64) return launch_bf16_wide<8, 1>(w0, rows0, w1, rows1, x, tokens, cols, out, out_stride, s);
+        return launch_bf16_wide<8, 4>(w0, rows0, w1, rows1, x, tokens, cols, out, out_stride, s);
     }
     static bool configured = false;
     if (!configured) {
@@ -818,11 +906,95 @@ __global__ void top_experts_kernel(const float *logits, uint32_t stride, uint32_
     }
 }
 
+// The same selection with the token's logits held in registers (expert
+// lane + 32 i in slot i): one read of the row instead of eight, the rest
+// register compares and shuffles. Equal to top_experts_kernel for every
+// input, NaNs included.
+template <int V>
+__global__ void top_experts_regs_kernel(const float *logits, uint32_t stride, uint32_t tokens, uint32_t experts,
+                                        uint32_t *route_experts, float *route_weights) {
+    const uint32_t token = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const uint32_t lane = threadIdx.x & 31u;
+    if (token >= tokens) return;
+    const float *l = logits + (size_t)token * stride;
+    float v[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const uint32_t e = lane + 32u * i;
+        v[i] = e < experts ? l[e] : 0.0f;
+    }
+    uint32_t taken = 0;  // bit i: expert lane + 32 i already chosen
+    uint32_t chosen[8];
+    float chosen_value[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        float bv = -INFINITY;
+        uint32_t be = 0xFFFFFFFFu;
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            const uint32_t e = lane + 32u * i;
+            if (e < experts && !((taken >> i) & 1u) && (v[i] > bv || (v[i] == bv && e < be))) {
+                bv = v[i];
+                be = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const uint32_t oe = __shfl_xor_sync(0xffffffffu, be, o);
+            if (ov > bv || (ov == bv && oe < be)) {
+                bv = ov;
+                be = oe;
+            }
+        }
+        if (be == 0xFFFFFFFFu) {
+            // Only NaN logits remain: take the lowest unchosen index, so the
+            // route is always a valid expert.
+            be = 0;
+            for (bool again = true; again;) {
+                again = false;
+#pragma unroll
+                for (int j = 0; j < k; ++j)
+                    if (chosen[j] == be) {
+                        ++be;
+                        again = true;
+                    }
+            }
+            bv = l[be];
+        }
+        if ((be & 31u) == lane) taken |= 1u << (be >> 5);
+        chosen[k] = be;
+        chosen_value[k] = bv;
+    }
+    if (lane == 0) {
+        float selected[8], sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            selected[k] = expf(chosen_value[k] - chosen_value[0]);
+            sum += selected[k];
+        }
+        sum = fmaxf(sum, 6.103515625e-5f);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            route_experts[token * 8 + k] = chosen[k];
+            route_weights[token * 8 + k] = selected[k] / sum;
+        }
+    }
+}
+
 void launch_top_experts(const float *logits, uint32_t logit_stride, uint32_t tokens, uint32_t experts,
                         uint32_t *route_experts, float *route_weights, cudaStream_t s) {
     if (tokens == 0) return;
-    top_experts_kernel<<<(tokens + 7) / 8, 256, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
-                                                        route_weights);
+    const uint32_t blocks = (tokens + 7) / 8;
+    if (experts <= 256)
+        top_experts_regs_kernel<8><<<blocks, 256, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
+                                                         route_weights);
+    else if (experts <= 1024)
+        top_experts_regs_kernel<32><<<blocks, 256, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
+                                                          route_weights);
+    else
+        top_experts_kernel<<<blocks, 256, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
+                                                  route_weights);
 }
 
 // ---------------------------------------------------------------------------
@@ -913,13 +1085,88 @@ __global__ void route_place_kernel(RouteParams p) {
     p.route_to_grouped[i] = pos;
 }
 
-void launch_route(const RouteParams &p, cudaStream_t s) {
+// The whole routing of a small batch (at most kSmallRoutes routes) in one
+// block: counts by shared-memory atomics, the same scans and work lists as
+// route_scan_kernel, and each route's rank within its expert as the number
+// of earlier routes to that expert -- the earlier tokens, as the bitmap
+// prefix counts them (a token names an expert at most once). Same outputs as
+// the three-kernel path.
+constexpr uint32_t kSmallRoutes = 256;
+
+__global__ void __launch_bounds__(1024) route_small_kernel(RouteParams p) {
+    __shared__ uint32_t expert_of[kSmallRoutes];
+    __shared__ uint32_t counts[1024], scan[1024], chunk_scan[1024];
+    const uint32_t t = threadIdx.x, n = p.tokens * 8;
+    counts[t] = 0;
+    __syncthreads();
+    if (t < n) {
+        const uint32_t e = p.route_experts[t];
+        expert_of[t] = e;
+        if (e < p.experts) atomicAdd(&counts[e], 1u);
+    }
+    __syncthreads();
+    const uint32_t e = t;
+    const uint32_t count = e < p.experts ? counts[e] : 0u;
+    const uint32_t chunks = (count + p.chunk - 1) / p.chunk;
+    scan[e] = count;
+    chunk_scan[e] = chunks;
+    __syncthreads();
+    for (uint32_t o = 1; o < 1024; o <<= 1) {
+        const uint32_t a = e >= o ? scan[e - o] : 0u;
+        const uint32_t b = e >= o ? chunk_scan[e - o] : 0u;
+        __syncthreads();
+        scan[e] += a;
+        chunk_scan[e] += b;
+        __syncthreads();
+    }
+    const uint32_t offset = scan[e] - count;
+    const uint32_t chunk_offset = chunk_scan[e] - chunks;
+    if (e < p.experts) {
+        p.counts[e] = count;
+        p.offsets[e] = offset;
+        for (uint32_t i = 0; i < count; ++i) p.pos_expert[offset + i] = e;
+        for (uint32_t c = 0; c < chunks; ++c) {
+            const uint32_t pos0 = offset + c * p.chunk;
+            const uint32_t m = min(p.chunk, count - c * p.chunk);
+            for (uint32_t j = 0; j < 2; ++j)
+                for (uint32_t rb = 0; rb < p.row_blocks_gate_up; ++rb)
+                    p.items_gate_up[((chunk_offset + c) * 2 + j) * p.row_blocks_gate_up + rb] =
+                        make_uint4(e, (j << 16) | rb, pos0, m);
+            for (uint32_t rb = 0; rb < p.row_blocks_down; ++rb)
+                p.items_down[(chunk_offset + c) * p.row_blocks_down + rb] = make_uint4(e, rb, pos0, m);
+        }
+    }
+    if (e == p.experts - 1) {
+        p.offsets[p.experts] = offset + count;
+        const uint32_t total_chunks = chunk_offset + chunks;
+        *p.count_gate_up = total_chunks * 2 * p.row_blocks_gate_up;
+        *p.count_down = total_chunks * p.row_blocks_down;
+    }
+    __syncthreads();
+    if (t < n) {
+        const uint32_t me = expert_of[t];
+        if (me < p.experts) {
+            uint32_t rank = 0;
+            for (uint32_t j = 0; j < t; ++j) rank += expert_of[j] == me;
+            const uint32_t pos = scan[me] - counts[me] + rank;
+            p.grouped[pos] = t >> 3;
+            p.route_to_grouped[t] = pos;
+        }
+    }
+}
+
+uint32_t launch_route(const RouteParams &p, cudaStream_t s) {
+    if (p.tokens * 8 <= kSmallRoutes && p.experts <= 1024) {
+        route_small_kernel<<<1, 1024, 0, s>>>(p);
+        return 1;
+    }
     cudaMemsetAsync(p.counts, 0, sizeof(uint32_t) * p.experts, s);
     cudaMemsetAsync(p.bitmap, 0, sizeof(uint32_t) * (size_t)p.experts * p.words, s);
     const uint32_t n = p.tokens * 8;
     route_count_kernel<<<(n + 255) / 256, 256, 0, s>>>(p);
     route_scan_kernel<<<1, 1024, 0, s>>>(p);
     route_place_kernel<<<(n + 255) / 256, 256, 0, s>>>(p);
+    return 3;
 }
 
 // ---------------------------------------------------------------------------

@@ -66,6 +66,7 @@ struct NeGemmParams {
     NeJob job[2];
     WorkList work;
     const float2 *table;  // [1024] signed value pairs
+    uint32_t row_tiles;   // tile rows per work item: kRowTiles, or 1 to spread small batches
 };
 
 // Codec tables and decode checks.
@@ -132,7 +133,8 @@ struct RouteParams {
     uint32_t *count_down;
     uint32_t row_blocks_down;
 };
-void launch_route(const RouteParams &p, cudaStream_t s);
+// Returns the number of kernels it launched.
+uint32_t launch_route(const RouteParams &p, cudaStream_t s);
 
 // SwiGLU between the gate/up and down projections of the routed experts:
 // xd = H(su_d * silu(H(g)*sv_g) * (H(u)*sv_u)).

@@ -420,12 +420,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t wq1 = wq + 1u == kExpertU32PerTile ? 0u : wq + 1u;
             const uint32_t neg_mask = half == 0 ? 0x8000u : 0u;
             const uint32_t a_lane = tmem_base + ((32u * quarter) << 16) + kTmemAColumn0 + 8u * pair;
-            // The f16x2 gamma (x 2^ka) of this lane's two tiles of chunk kc;
-            // fetched a chunk ahead so the load's latency hides behind a
-            // chunk of work.
-            auto fetch_gamma = [&](const Unit &un, const TcJob &J, uint32_t kc, float gscale, uint32_t t) -> uint32_t {
+            // Tile gammas (x 2^ka, as f16x2) are fetched eight chunks at a
+            // time: the 16 lanes of a half-warp share one tile row, so lane
+            // (h, i) holds the gamma of chunk kc0 + i / 2, tile column
+            // 2 * pair + i % 2, and the next eight chunks' load is issued a
+            // block ahead of its use.
+            auto fetch_gammas = [&](const Unit &un, const TcJob &J, uint32_t kc0, uint32_t chunks,
+                                    float gscale) -> uint32_t {
+                const uint32_t i = lane & 15u, kc = kc0 + (i >> 1);
+                if (kc >= chunks) return 0u;
                 const uint32_t TC = J.cols / 16, TR = J.rows / 16;
-                const uint32_t diag = un.m_block * 8 + tr + kc * 8 + 2u * pair + t;
+                const uint32_t diag = un.m_block * 8 + tr + kc * 8 + 2u * pair + (i & 1u);
                 const uint16_t *gam = J.gamma + (size_t)un.expert * J.gamma_stride;
                 const __half2 g2 =
                     __float2half2_rn(__half2float(__ushort_as_half(__ldg(gam + wave_index(TR, TC, diag)))) * gscale);
@@ -436,13 +441,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const TcJob &J = un.job ? p.job[1] : p.job[0];
                 const uint32_t chunks = J.cols / T::chunk_cols;
                 const float gscale = exp2f((float)J.ka[un.expert]);
-                uint32_t gnext0 = fetch_gamma(un, J, 0, gscale, 0), gnext1 = fetch_gamma(un, J, 0, gscale, 1);
+                uint32_t gblock = fetch_gammas(un, J, 0, chunks, gscale);
+                uint32_t gnext = fetch_gammas(un, J, 8, chunks, gscale);
                 for (uint32_t kc = 0; kc < chunks; ++kc) {
-                    const uint32_t gcur[2] = {gnext0, gnext1};
-                    if (kc + 1 < chunks) {
-                        gnext0 = fetch_gamma(un, J, kc + 1, gscale, 0);
-                        gnext1 = fetch_gamma(un, J, kc + 1, gscale, 1);
+                    if (kc > 0 && (kc & 7u) == 0) {
+                        gblock = gnext;
+                        gnext = fetch_gammas(un, J, kc + 8, chunks, gscale);
                     }
+                    const uint32_t src = (lane & 16u) | ((kc & 7u) << 1);
+                    const uint32_t gcur[2] = {__shfl_sync(0xffffffffu, gblock, src),
+                                              __shfl_sync(0xffffffffu, gblock, src | 1u)};
                     if (ok) ok = mbar_wait(&w_full[w.slot], w.phase, p.error);
                     if (ok) ok = mbar_wait(&a_empty[a.slot], a.phase ^ 1u, p.error);
                     ok = __all_sync(0xffffffffu, ok);  // tcgen05.st is warp-wide

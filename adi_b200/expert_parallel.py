@@ -52,12 +52,13 @@ class DevicePhases:
         handle = torch.cuda.current_stream(device).cuda_stream
         self.ctx.set_stream(handle if handle else CUDA_STREAM_LEGACY)
 
-    def dispatch(self, x: torch.Tensor):
+    def dispatch(self, x: torch.Tensor, logits: torch.Tensor | None = None):
         tokens = x.shape[0]
         self._stream(x.device)
         send = torch.empty(8 * tokens, self.hidden, dtype=torch.float32, device=x.device)
         counts = torch.empty(self.experts, dtype=torch.int32, device=x.device)
-        self.ctx.ep_dispatch_device(self.handle, x.data_ptr(), tokens, send.data_ptr(), counts.data_ptr())
+        self.ctx.ep_dispatch_device(self.handle, x.data_ptr(), tokens, send.data_ptr(), counts.data_ptr(),
+                                    logits_ptr=logits.data_ptr() if logits is not None else 0)
         return send, counts
 
     def experts_forward(self, recv: torch.Tensor, recv_counts: torch.Tensor, world: int) -> torch.Tensor:
@@ -95,9 +96,11 @@ class ExpertParallelMoe:
         self.last_splits: tuple[list[int], list[int]] | None = None  # rows sent to / received from each rank
         self.last_received = None  # rows received per local expert (host, int64)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, logits: torch.Tensor | None = None) -> torch.Tensor:
+        """`logits` [T, experts + 1], when given, replace the router's (the
+        last column is the shared-expert gate): a prescribed routing."""
         tokens = x.shape[0]
-        send, counts = self.phases.dispatch(x)
+        send, counts = self.phases.dispatch(x) if logits is None else self.phases.dispatch(x, logits)
         recv_counts = torch.empty_like(counts)
         dist.all_to_all_single(recv_counts, counts, group=self.group)
         host = torch.cat([counts, recv_counts]).cpu()

@@ -131,6 +131,47 @@ def moe_block(seed: int, hidden: int = 2048, expert_hidden: int = 512, experts: 
     return block
 
 
+def ne_matrix(seed: int, rows: int, columns: int, scale_mu: float = -4.0, scale_sigma: float = 0.5,
+              device: str = "cuda") -> NeView:
+    """A non-expert projection in the NE codec: uniform code words, +-1
+    signs, a log-normal weight scale, a uniform(-1, 1) TLUT."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    tiles = (rows // 16) * (columns // 16)
+    trellis = _host(torch.randint(0, 65536, (tiles * 64,), generator=g, device=device, dtype=torch.int32)
+                    .to(torch.int16), np.uint16)
+    su = (torch.randint(0, 2, (columns,), generator=g, device=device, dtype=torch.int8) * 2 - 1).cpu().numpy()
+    sv = (torch.randint(0, 2, (rows,), generator=g, device=device, dtype=torch.int8) * 2 - 1).cpu().numpy()
+    scale = float(torch.exp(scale_mu + scale_sigma * torch.randn(1, generator=g, device=device)).item())
+    tlut = (torch.rand(1024, generator=g, device=device) * 2 - 1).cpu().numpy().astype(np.float32)
+    return NeView(rows, columns, trellis, su, sv, scale, tlut)
+
+
+@dataclass
+class HeadChunk:
+    rows: int
+    columns: int
+    packed: np.ndarray          # [rows][columns / 8 * 5] int5 codes, 8 per 5 bytes
+    scales: np.ndarray          # f16 bits [rows][columns / 64]
+    protected_rows: np.ndarray  # uint32
+    protected_bf16: np.ndarray  # bf16 bits [protected][columns]
+
+    def packed_bytes(self) -> int:
+        return self.packed.nbytes + self.scales.nbytes + self.protected_bf16.nbytes
+
+
+def head_chunk(seed: int, rows: int, columns: int, device: str = "cuda") -> HeadChunk:
+    """The int5_g64 output head: uniform code bytes, f16 log-normal group
+    scales, no protected rows."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    packed = torch.randint(0, 256, (rows, columns // 8 * 5), generator=g, device=device, dtype=torch.int32)
+    scales = torch.exp(-4.0 + 0.5 * torch.randn(rows, columns // 64, generator=g, device=device))
+    return HeadChunk(rows, columns, packed.to(torch.uint8).cpu().numpy(),
+                     _host(scales.to(torch.float16).view(torch.int16), np.uint16),
+                     np.zeros(0, np.uint32), np.zeros((0, columns), np.uint16))
+
+
 def activations(seed: int, tokens: int, hidden: int, device: str = "cuda") -> torch.Tensor:
     g = torch.Generator(device=device)
     g.manual_seed(seed)

@@ -69,6 +69,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--precision", type=int, default=1, choices=[0, 1],
                     help="0: CUDA-core fp32 throughout; 1: tcgen05 f16 operands for the expert products")
+    ap.add_argument("--routing", choices=["zipf", "router"], default="zipf",
+                    help="N > 1: zipf = C4's prescribed logits, log p(rank) + Gumbel(0,1) with Zipf s=1.1 "
+                         "popularity; router = the block's own router on N(0,1) inputs (near-uniform)")
     ap.add_argument("--no-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-extras", action="store_true",
                     help="only the timed region: no e2e, ubatch sweep or CPU baseline (profiling runs)")
@@ -224,6 +227,114 @@ def run_reference(args, world, rank):
     }), flush=True)
 
 
+# C3: the decode stack -- 40 layers, each a MoE block plus the non-expert
+# projections attention q/k/v/o (2048 -> 4096 / 512 / 512, 4096 -> 2048) and
+# the gated-delta input projection (2048 -> 8192), all NE-coded, then the
+# int5 output head 2048 -> 151936.
+C3_LAYERS = 40
+C3_DISTINCT = 8  # distinct weight sets, cycled: 8 x 175 MB, far above L2
+C3_NE = (("q", 4096, 2048), ("k", 512, 2048), ("v", 512, 2048), ("o", 2048, 4096), ("gated_delta", 8192, 2048))
+C3_VOCAB = 151936
+
+
+def decode_c3(ctx, stream, local, tokens_list=(1, 4), steps=20):
+    """Bandwidth-bound decode over the C3 stack: HBM GB/s of algorithmic
+    bytes (router, shared expert, the experts the step touches, every NE
+    projection, the head) per step, eager and replayed from one CUDA graph."""
+    from adi_b200 import synthetic
+    device = f"cuda:{local}"
+    blocks, moe_h, ne_h, ne_bytes = [], [], [], []
+    for d in range(C3_DISTINCT):
+        b = synthetic.moe_block(seed=5000 + d, device=device)
+        moe_h.append(ctx.upload_moe_layer(b))
+        blocks.append((b.shared_bytes(), b.packed_bytes_per_expert()))
+        hs, nb = {}, 0
+        for i, (name, rows, cols) in enumerate(C3_NE):
+            m = synthetic.ne_matrix(6000 + 16 * d + i, rows, cols, device=device)
+            hs[name] = ctx.upload_ne(m)
+            nb += m.trellis.nbytes + m.su.nbytes + m.sv.nbytes + 4
+        ne_h.append(hs)
+        ne_bytes.append(nb)
+        del b
+    head = synthetic.head_chunk(7000, C3_VOCAB, 2048, device=device)
+    head_h = ctx.upload_head(head)
+    head_bytes = head.packed_bytes()
+    del head
+    out = {}
+    for T in tokens_list:
+        x = synthetic.activations(900 + T, T, 2048, device=device)
+        x4 = synthetic.activations(901 + T, T, 4096, device=device)
+        y = torch.empty(T, 2048, device=device)
+        q = torch.empty(T, 8192, device=device)
+        logits = torch.empty(T, C3_VOCAB, device=device)
+        routes = torch.empty(C3_LAYERS, T, 8, dtype=torch.int32, device=device)
+
+        def step(record_routes=False):
+            for layer in range(C3_LAYERS):
+                d = layer % C3_DISTINCT
+                ctx.moe_forward_batch_device(moe_h[d], x.data_ptr(), T, y.data_ptr(),
+                                             routes[layer].data_ptr() if record_routes else 0, 0)
+                for name, rows, cols in C3_NE:
+                    ctx.matmul_device(ne_h[d][name], (x4 if cols == 4096 else x).data_ptr(), T, q.data_ptr())
+            ctx.matmul_device(head_h, x.data_ptr(), T, logits.data_ptr())
+
+        step(record_routes=True)
+        torch.cuda.synchronize()
+        touched = [int(torch.unique(routes[layer]).numel()) for layer in range(C3_LAYERS)]
+        step_bytes = head_bytes + T * 2048 * 4 * 2 * C3_LAYERS
+        for layer in range(C3_LAYERS):
+            d = layer % C3_DISTINCT
+            shared, per_expert = blocks[d]
+            step_bytes += shared + touched[layer] * per_expert + ne_bytes[d]
+        for _ in range(3):
+            step()
+        b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b.record(stream)
+        for _ in range(steps):
+            step()
+        e.record(stream)
+        torch.cuda.synchronize()
+        eager_ms = b.elapsed_time(e) / steps
+        graph = torch.cuda.CUDAGraph()
+        capture = torch.cuda.Stream(device=local)
+        with torch.cuda.graph(graph, stream=capture):
+            ctx.set_stream(capture.cuda_stream)
+            step()
+        ctx.set_stream(stream.cuda_stream)
+        for _ in range(3):
+            graph.replay()
+        b.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e.record(stream)
+        torch.cuda.synchronize()
+        graph_ms = b.elapsed_time(e) / steps
+        del graph
+        out[f"batch_{T}"] = {"bytes_per_step": step_bytes, "experts_touched_per_layer": sum(touched) / len(touched),
+                             "eager_ms_per_step": eager_ms, "eager_gbs": step_bytes / eager_ms / 1e6,
+                             "graph_ms_per_step": graph_ms, "graph_gbs": step_bytes / graph_ms / 1e6,
+                             "graph_tokens_per_s": T / (graph_ms / 1e3)}
+    for h in moe_h + [head_h] + [m for hs in ne_h for m in hs.values()]:
+        h.release()
+    return out
+
+
+def zipf_logits(pool: int, tokens: int, experts: int, seed: int, device: str) -> torch.Tensor:
+    """C4 router logits [pool, tokens, experts + 1]: log p(rank(e)) +
+    Gumbel(0, 1) with p ~ 1 / (rank + 1)^1.1 and the rank permutation drawn
+    from seed 0 (the same on every rank); top-8 of these samples experts
+    without replacement in proportion to p. Last column: the shared-expert
+    gate logit, N(0, 1)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
+    rank_of = torch.randperm(experts, generator=g, device=device)
+    log_p = -1.1 * torch.log(rank_of.to(torch.float32) + 1.0)
+    g.manual_seed(seed)
+    u = torch.rand(pool, tokens, experts, generator=g, device=device).clamp_(1e-12, 1.0 - 1e-7)
+    gate = torch.randn(pool, tokens, 1, generator=g, device=device)
+    return torch.cat([log_p - torch.log(-torch.log(u)), gate], dim=2).contiguous()
+
+
 def run_ep(args, world, rank, local):
     """Expert-parallel MoE block over `world` ranks (one process per GPU)."""
     import adi_b200
@@ -249,9 +360,10 @@ def run_ep(args, world, rank, local):
     local_experts = E // world
     pool = 8
     inputs = torch.stack([synthetic.activations(7 * rank + i, T, H, device=device) for i in range(pool)])
+    logits = zipf_logits(pool, T, E, seed=11 + rank, device=device) if args.routing == "zipf" else None
 
     def step(k):
-        return layers[k % L](inputs[k % pool])
+        return layers[k % L](inputs[k % pool], None if logits is None else logits[k % pool])
 
     # Local experts each (layer, input) pair touches, from the rows this
     # rank receives per expert: the algorithmic bytes of its expert GEMMs.
@@ -300,7 +412,7 @@ def run_ep(args, world, rank, local):
 
     def e2e_step(k):
         x_dev.copy_(x_host[k % pool], non_blocking=True)
-        y_host.copy_(layers[k % L](x_dev), non_blocking=True)
+        y_host.copy_(layers[k % L](x_dev, None if logits is None else logits[k % pool]), non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
     for k in range(min(args.warmup, 5)):
@@ -321,7 +433,9 @@ def run_ep(args, world, rank, local):
             "config": {"workload": f"C4: expert-parallel MoE block, {T} tokens per GPU, {T * world} per step",
                        "tokens_per_step": T * world, "tokens_per_gpu": T, "hidden": H, "experts": E,
                        "experts_per_gpu": local_experts, "expert_hidden": first.expert_hidden, "top_k": 8,
-                       "blocks_rotated": L, "routing": "N(0,1) inputs, near-uniform",
+                       "blocks_rotated": L,
+                       "routing": ("C4 prescribed logits: log p(rank) + Gumbel(0,1), Zipf s=1.1, rank permutation "
+                                   "from seed 0" if logits is not None else "the block's router on N(0,1) inputs"),
                        "l2": f"inputs larger than L2: {L} distinct blocks rotated",
                        "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single, fp32 rows"},
             "roofline": {"bound": "hbm", "kernel": "expert_gemm_kernel",
@@ -467,7 +581,7 @@ def run_ours(args, world, rank, local):
 
     # Smaller ubatches of the same block (decode and the smaller prefill).
     sweep = {}
-    for tokens in (1, 128):
+    for tokens in (1, 16, 128):
         xs = inputs[0, :tokens].contiguous()
         for _ in range(5):
             ctx.moe_forward_batch_device(handles[0], xs.data_ptr(), tokens, out.data_ptr(), 0, 0)
@@ -478,6 +592,27 @@ def run_ours(args, world, rank, local):
             ctx.moe_forward_batch_device(handles[k % L], xs.data_ptr(), tokens, out.data_ptr(), 0, 0)
         e.record(stream)
         torch.cuda.synchronize()
+        # The same steps replayed from CUDA graphs (one per block), which
+        # takes the host's launch overhead out of small ubatches.
+        graphs = []
+        capture = torch.cuda.Stream(device=local)
+        for k in range(L):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=capture):
+                ctx.set_stream(capture.cuda_stream)
+                ctx.moe_forward_batch_device(handles[k], xs.data_ptr(), tokens, out.data_ptr(), 0, 0)
+            graphs.append(g)
+        ctx.set_stream(stream.cuda_stream)
+        for g in graphs:
+            g.replay()
+        gb, ge = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        gb.record(stream)
+        for k in range(steps):
+            graphs[k % L].replay()
+        ge.record(stream)
+        torch.cuda.synchronize()
+        graph_ms = gb.elapsed_time(ge) / steps
+        del graphs
         # The same steps again with stage timing (separately: its events
         # would add to the timed run).
         ctx.set_profiling(True)
@@ -489,7 +624,19 @@ def run_ours(args, world, rank, local):
         ctx.set_profiling(False)
         sweep[f"ubatch_{tokens}"] = {"tokens_per_s": steps * tokens / (b.elapsed_time(e) / 1e3),
                                      "ms_per_step": b.elapsed_time(e) / steps,
+                                     "graph_tokens_per_s": tokens / (graph_ms / 1e3),
+                                     "graph_ms_per_step": graph_ms,
                                      "stages_ms_per_step": sweep_stages}
+
+    # C3 decode over the 40-layer stack; the prefill blocks are released
+    # first to make room.
+    for h in handles:
+        h.release()
+    handles = []
+    c3 = decode_c3(ctx, stream, local)
+    hbm_peak_c3, _ = peaks()
+    for v in c3.values():
+        v["graph_frac_hbm"] = v["graph_gbs"] / hbm_peak_c3
 
     baseline = None
     if rank == 0 and world == 1 and not args.no_baseline:
@@ -520,6 +667,9 @@ def run_ours(args, world, rank, local):
                           "experts_touched_mean": sum(n_touched) / len(n_touched)},
             "stages_ms_per_step": {k: v[0] / max(1, v[1]) for k, v in stages.items()},
             "ubatch_sweep": sweep,
+            "decode_c3": {"layers": C3_LAYERS, "distinct_weight_sets": C3_DISTINCT,
+                          "per_layer": "MoE block + NE q/k/v/o/gated-delta", "head": f"int5_g64 {C3_VOCAB}x2048",
+                          **c3},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
                     "d2h_bytes_per_step": T * H * 4 + T * 8 * 8, "steps": e2e_steps},
             "gpu_launches": launches,

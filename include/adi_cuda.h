@@ -232,11 +232,15 @@ ADI_CUDA_API int adi_cuda_upload_moe_shard(adi_cuda_context *context, const adi_
                                            uint32_t first_expert, uint32_t expert_count,
                                            adi_cuda_handle *handle);
 /* inputs [tokens][hidden]; send_rows [8 * tokens][hidden]; expert_counts
- * [experts]; route_experts / route_weights [tokens][8] or NULL. */
+ * [experts]; route_experts / route_weights [tokens][8] or NULL.
+ * router_logits: NULL to compute the router from the inputs, or caller
+ * logits [tokens][experts + 1] (the last column the shared-expert gate)
+ * that replace the router product -- for load studies with a prescribed
+ * expert popularity; top_experts and everything after are unchanged. */
 ADI_CUDA_API int adi_cuda_ep_dispatch_device(adi_cuda_context *context, adi_cuda_handle shard,
-                                             const float *inputs, uint32_t tokens, float *send_rows,
-                                             uint32_t *expert_counts, uint32_t *route_experts,
-                                             float *route_weights);
+                                             const float *inputs, const float *router_logits,
+                                             uint32_t tokens, float *send_rows, uint32_t *expert_counts,
+                                             uint32_t *route_experts, float *route_weights);
 /* recv_counts [world][expert_count] (device): rows rank s sent for each of
  * this shard's experts, i.e. what rank s's expert_counts held for them;
  * recv_rows [rows][hidden] as the all-to-all delivered them (rank 0's first,

@@ -8,6 +8,8 @@ logits (bf16 weights), top_experts, per-route SwiGLU expert, route-order
 weighted sum plus sigmoid(shared gate) x shared expert. Routes are grouped
 like the device's counting sort: by expert, then token.
 """
+from __future__ import annotations
+
 import numpy as np
 import torch
 
@@ -32,11 +34,15 @@ class CpuPhases:
         u = project(up, rows)
         return project(down, (silu(g) * u).astype(np.float32))
 
-    def dispatch(self, x: torch.Tensor):
+    def dispatch(self, x: torch.Tensor, given_logits: torch.Tensor | None = None):
         xn = x.numpy()
         T = xn.shape[0]
-        logits = self.ora.bf16_matmul(self.layer.router, xn)
-        self.gate_logits = self.ora.bf16_matmul(self.layer.shared_expert_gate.reshape(1, -1), xn)[:, 0]
+        if given_logits is None:
+            logits = self.ora.bf16_matmul(self.layer.router, xn)
+            self.gate_logits = self.ora.bf16_matmul(self.layer.shared_expert_gate.reshape(1, -1), xn)[:, 0]
+        else:
+            logits = given_logits.numpy()[:, :self.experts]
+            self.gate_logits = given_logits.numpy()[:, self.experts].copy()
         self.route_experts = np.zeros((T, 8), np.uint32)
         self.route_weights = np.zeros((T, 8), np.float32)
         for t in range(T):
@@ -77,3 +83,27 @@ class CpuPhases:
             gate = np.float32(1) / (np.float32(1) + np.exp(-self.gate_logits[t].astype(np.float32)))
             out[t] = acc + gate * self.shared[t]
         return torch.from_numpy(out)
+
+
+def block_with_logits(layer, x: np.ndarray, logits: np.ndarray):
+    """The block on prescribed logits [T][E+1] (last column the shared gate),
+    from the oracle's pieces: routes, weights and outputs."""
+    ora = Oracle()
+    T = x.shape[0]
+    E = layer.experts
+    experts = np.zeros((T, 8), np.uint32)
+    weights = np.zeros((T, 8), np.float32)
+    out = np.zeros_like(x)
+    shared = CpuPhases(layer, 0, 1)._swiglu(ora.ne_matmul, layer.shared_gate, layer.shared_up, layer.shared_down, x)
+    for t in range(T):
+        experts[t], weights[t] = ora.top_experts(logits[t, :E])
+        acc = np.zeros(layer.hidden, np.float32)
+        for k in range(8):
+            e = int(experts[t, k])
+            g = ora.expert_matmul(layer.expert(e, 0), x[t:t + 1])
+            u = ora.expert_matmul(layer.expert(e, 1), x[t:t + 1])
+            d = ora.expert_matmul(layer.expert(e, 2), (silu(g) * u).astype(np.float32))[0]
+            acc = (acc + weights[t, k] * d).astype(np.float32)
+        gate = np.float32(1) / (np.float32(1) + np.exp(-np.float32(logits[t, E])))
+        out[t] = acc + gate * shared[t]
+    return out, experts, weights

@@ -53,6 +53,14 @@ def worker(rank: int, world: int, port: int):
         owners = np.concatenate([Oracle().moe_forward(layer, activations(40 + s, tokens_of(s), layer.hidden))[1]
                                  .reshape(-1) for s in range(world)]) // (layer.experts // world)
         assert sum(recv_splits) == int((owners == rank).sum())
+        # Prescribed routing (caller logits, last column the shared gate).
+        from ep_cpu_phases import block_with_logits
+        rng = np.random.default_rng(100 + rank)
+        logits = rng.normal(size=(tokens_of(rank), layer.experts + 1)).astype(np.float32)
+        y = moe(torch.from_numpy(x), torch.from_numpy(logits)).numpy()
+        want, experts, weights = block_with_logits(layer, x, logits)
+        assert np.array_equal(phases.route_experts, experts)
+        assert rel_l2(y, want) <= TOL, (rank, world, rel_l2(y, want))
         dist.barrier()
     finally:
         dist.destroy_process_group()

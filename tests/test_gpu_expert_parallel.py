@@ -17,7 +17,7 @@ TOL = {0: 1e-3, 1: 1e-2}  # fp32 CUDA-core / f16-operand tensor-core bounds
 SAME = 1e-5  # expert-parallel vs single-GPU: the same kernels on the same rows
 
 
-def emulate(layer, xs, world, precision):
+def emulate(layer, xs, world, precision, logits=None):
     import torch
     import adi_b200
     from adi_b200.expert_parallel import DevicePhases
@@ -27,7 +27,9 @@ def emulate(layer, xs, world, precision):
             c.set_precision(precision)
         phases = [DevicePhases(ctxs[r], layer, r, world) for r in range(world)]
         L = phases[0].local
-        sent = [phases[r].dispatch(torch.from_numpy(xs[r]).cuda()) for r in range(world)]
+        sent = [phases[r].dispatch(torch.from_numpy(xs[r]).cuda()) if logits is None else
+                phases[r].dispatch(torch.from_numpy(xs[r]).cuda(), torch.from_numpy(logits[r]).cuda())
+                for r in range(world)]
         counts = [c.cpu().numpy().reshape(world, L).astype(np.int64) for _, c in sent]
         send_off = [np.concatenate([[0], np.cumsum(c.sum(1))]) for c in counts]
         recv_off = [np.concatenate([[0], np.cumsum([counts[s][d].sum() for s in range(world)])])
@@ -108,3 +110,21 @@ def test_receive_count_mismatch_computes_nothing():
         assert torch.isnan(marker).all()
     finally:
         c.close()
+
+
+@pytest.mark.parametrize("precision", [0, 1])
+def test_prescribed_logits(precision):
+    """Dispatch on caller logits (the C4 load study's Zipf-skewed routing):
+    the block on those routes, against the oracle's pieces."""
+    from ep_cpu_phases import block_with_logits
+    layer = moe_layer(seed=5, hidden=256, expert_hidden=64, experts=16, scale_mu=-1.0, shared_mu=-3.0)
+    rng = np.random.default_rng(3)
+    rank_p = -1.1 * np.log(rng.permutation(16) + 1.0)
+    xs, ls = [], []
+    for r, tokens in enumerate([6, 9]):
+        xs.append(activations(80 + r, tokens, layer.hidden))
+        gumbel = -np.log(-np.log(rng.uniform(1e-9, 1.0, (tokens, 16))))
+        ls.append(np.concatenate([rank_p + gumbel, rng.normal(size=(tokens, 1))], axis=1).astype(np.float32))
+    y = np.concatenate(emulate(layer, xs, 2, precision, logits=ls))
+    want, _, _ = block_with_logits(layer, np.concatenate(xs), np.concatenate(ls))
+    assert rel_l2(y, want) <= TOL[precision]

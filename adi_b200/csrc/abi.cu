@@ -658,6 +658,7 @@ void ne_matmul_dev(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batc
     gp.job[1] = gp.job[0];
     gp.table = m.codec->table.as<float2>();
     gp.row_tiles = ne_row_tiles(c, batch, m.rows, 1);
+    gp.error = c->error_word;
     const uint32_t nt = ne_tokens_per_item(gp.row_tiles, batch);
     gp.work = WorkList{nullptr, nullptr, batch, 1, nt};
     const uint64_t items = uint64_t((batch + nt - 1) / nt) * row_blocks(m.rows, gp.row_tiles);
@@ -797,6 +798,7 @@ void shared_expert(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, 
         np.job[1] = NeJob{L.shared[1].trellis->as<uint32_t>(), sxu, sacc_u, I, H, L.shared[1].weight_scale};
         np.table = L.shared[0].codec->table.as<float2>();
         np.row_tiles = ne_row_tiles(c, T, I, 2);
+        np.error = c->error_word;
         const uint32_t gu_nt = ne_tokens_per_item(np.row_tiles, T);
         np.work = WorkList{nullptr, nullptr, T, 2, gu_nt};
         const uint64_t ne_items = uint64_t((T + gu_nt - 1) / gu_nt) * 2 * row_blocks(I, np.row_tiles);
@@ -822,6 +824,7 @@ void shared_expert(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, 
         nd.job[1] = nd.job[0];
         nd.table = np.table;
         nd.row_tiles = ne_row_tiles(c, T, H, 1);
+        nd.error = c->error_word;
         const uint32_t d_nt = ne_tokens_per_item(nd.row_tiles, T);
         nd.work = WorkList{nullptr, nullptr, T, 1, d_nt};
         const uint64_t nd_items = uint64_t((T + d_nt - 1) / d_nt) * row_blocks(H, nd.row_tiles);
@@ -1022,9 +1025,9 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     rp.grouped = c->buffer<uint32_t>("moe_grouped", P);
     rp.pos_expert = c->buffer<uint32_t>("moe_pos_expert", P);
     rp.route_to_grouped = c->buffer<uint32_t>("moe_r2g", P);
-    // Tensor cores once experts see a few positions each on average; below
-    // that the CUDA-core kernel streams the few touched experts faster.
-    const bool tc = c->precision == 1 && tensor_core_shape(I, H) && uint64_t(T) * 8 >= uint64_t(E) * 4;
+    // Tensor cores whenever the precision mode allows them: even one
+    // position per expert decodes faster there than on CUDA cores.
+    const bool tc = c->precision == 1 && tensor_core_shape(I, H);
     const uint32_t nt = tc ? kTcMaxN : tokens_per_item((uint64_t(T) * 8 + E - 1) / E);
     const uint32_t rb_gate_up = expert_rows_per_item(H), rb_down = expert_rows_per_item(I);
     rp.chunk = nt;
@@ -1253,7 +1256,7 @@ void ep_experts_dev(adi_cuda_context *c, MoeDev &L, const float *recv, const uin
     if (rows == 0) return;
     cudaStream_t s = c->stream;
     const size_t P = rows;
-    const bool tc = c->precision == 1 && tensor_core_shape(I, H) && uint64_t(rows) >= uint64_t(local) * 4;
+    const bool tc = c->precision == 1 && tensor_core_shape(I, H);
     const uint32_t nt = tc ? kTcMaxN : tokens_per_item((uint64_t(rows) + local - 1) / local);
     const uint32_t rb_gate_up = expert_rows_per_item(H), rb_down = expert_rows_per_item(I);
     RouteParams rp{};

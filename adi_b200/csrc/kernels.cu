@@ -317,7 +317,7 @@ struct ExpertStreamSmem {
     static constexpr size_t table = kExpertTableRows * sizeof(uint2);
     static constexpr size_t ring = size_t(kStages) * kSlabBytes;
     static constexpr size_t red = size_t(CW) * kRowTiles * 16 * NT * sizeof(float);
-    static constexpr size_t bars = 2 * kStages * sizeof(uint64_t);
+    static constexpr size_t bars = (2 * kStages + 1) * sizeof(uint64_t);
     static constexpr size_t total = table + ring + red + bars;
 };
 
@@ -330,22 +330,23 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) expert_stream_kernel(const E
     float *red = reinterpret_cast<float *>(smem + L::table + L::ring);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::table + L::ring + L::red);
     uint64_t *empty = full + kStages;
+    uint64_t *table_bar = empty + kStages;
     const uint32_t half = blockIdx.x & 1u;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
 
-    {
-        const uint4 *src = reinterpret_cast<const uint4 *>(p.table + half * kExpertTableRows);
-        uint4 *dst = reinterpret_cast<uint4 *>(table);
-        for (uint32_t i = threadIdx.x; i < kExpertTableRows / 2; i += blockDim.x) dst[i] = src[i];
-    }
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], CW);
         }
+        mbar_init(table_bar, 1);
         fence_barrier_init();
+        // The value half-table (128 KiB) by bulk copy.
+        mbar_arrive_expect_tx(table_bar, kExpertTableRows * sizeof(uint2));
+        bulk_load_pieces(table, p.table + half * kExpertTableRows, kExpertTableRows * sizeof(uint2), table_bar);
     }
     __syncthreads();
+    mbar_wait_own(table_bar, 0, p.error);
 
     const uint32_t rb_rows = p.rows_per_item;
     const uint32_t rb0 = (p.job[0].rows / 16 + rb_rows - 1) / rb_rows;
@@ -532,9 +533,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) ne_gemm_kernel(const NeGemmPa
     extern __shared__ __align__(128) uint8_t smem[];
     float2 *table = reinterpret_cast<float2 *>(smem);
     float *red = reinterpret_cast<float *>(smem + kNeTableRows * kNeTableCopies * sizeof(float2));
+    uint64_t *table_bar = reinterpret_cast<uint64_t *>(smem + kNeGemmSmem - sizeof(uint64_t));
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    for (uint32_t i = threadIdx.x; i < kNeTableRows * kNeTableCopies; i += blockDim.x)
-        table[i] = p.table[i / kNeTableCopies];
+    // The pair table (8 KiB) by bulk copy into the reduction buffer, then
+    // replicated once per bank pair.
+    if (threadIdx.x == 0) {
+        mbar_init(table_bar, 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(table_bar, kNeTableRows * sizeof(float2));
+        bulk_load_pieces(red, p.table, kNeTableRows * sizeof(float2), table_bar);
+    }
+    __syncthreads();
+    mbar_wait_own(table_bar, 0, p.error);
+    {
+        const float2 *staged = reinterpret_cast<const float2 *>(red);
+        for (uint32_t i = threadIdx.x; i < kNeTableRows * kNeTableCopies; i += blockDim.x)
+            table[i] = staged[i / kNeTableCopies];
+    }
     __syncthreads();
 
     const uint32_t rb0 = (p.job[0].rows / 16 + RT - 1) / RT;

@@ -12,7 +12,7 @@ constexpr int kGemmWarps = 8;
 constexpr int kRowTiles = 4;   // tile rows per work item (64 output rows)
 constexpr int kMaxTokens = 8;  // token columns per work item
 constexpr size_t kExpertGemmSmem = 16384 * 8 + kGemmWarps * kRowTiles * 16 * kMaxTokens * 4;
-constexpr size_t kNeGemmSmem = 1024 * 16 * 8 + kGemmWarps * kRowTiles * 16 * kMaxTokens * 4;
+constexpr size_t kNeGemmSmem = 1024 * 16 * 8 + kGemmWarps * kRowTiles * 16 * kMaxTokens * 4 + 16;
 
 // One projection of a set of expert matrices with identical geometry, stored
 // expert-major. `x` rows are positions (grouped token slots); `acc` holds two
@@ -67,6 +67,7 @@ struct NeGemmParams {
     WorkList work;
     const float2 *table;  // [1024] signed value pairs
     uint32_t row_tiles;   // tile rows per work item: kRowTiles, or 1 to spread small batches
+    uint32_t *error;      // device word a bounded wait flags on expiry
 };
 
 // Codec tables and decode checks.

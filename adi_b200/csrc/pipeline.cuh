@@ -104,6 +104,16 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
 }
 
 // Named barrier over `threads` threads (a subset of the block).
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// in pieces of at most 32 KiB, all completing on `bar`: a value table into
+// shared memory at copy-engine speed, instead of a loop of dependent loads.
+// One thread issues it after arming `bar` for `bytes`.
+__device__ __forceinline__ void bulk_load_pieces(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    for (uint32_t off = 0; off < bytes; off += 32768u)
+        bulk_load(static_cast<uint8_t *>(dst) + off, static_cast<const uint8_t *>(src) + off,
+                  bytes - off < 32768u ? bytes - off : 32768u, bar);
+}
+
 __device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }

@@ -80,7 +80,7 @@ struct Smem {
     static constexpr size_t b = a + kAStages * kATileBytes;
     static constexpr size_t words = b + kBStages * kBTileBytes;
     static constexpr size_t bars = words + kWordStages * kWordSlotBytes;
-    static constexpr uint32_t kBars = 2 * kWordStages + 2 * kBStages + 2 * kMaxAStages + 4 + 1;
+    static constexpr uint32_t kBars = 2 * kWordStages + 2 * kBStages + 2 * kMaxAStages + 4 + 1 + 1;
     static constexpr size_t total = bars + kBars * 8 + 16;
 };
 static_assert(Smem::total <= 232448, "shared memory budget");
@@ -240,21 +240,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t *d_full = a_empty + kMaxAStages;
     uint64_t *d_empty = d_full + 2;
     uint64_t *mma_done = d_empty + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+    uint64_t *table_bar = mma_done + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(table_bar + 1);
 
     const uint32_t half = T::halves == 2 ? (blockIdx.x & 1u) : 0u;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
 
-    // Value table into shared memory.
-    if (C == TcCodec::kExpert) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const uint2 *>(p.table) + half * kExpertTableRows);
-        uint4 *dst = reinterpret_cast<uint4 *>(smem);
-        for (uint32_t i = threadIdx.x; i < kExpertTableRows / 2; i += blockDim.x) dst[i] = src[i];
-    } else {
-        const uint32_t *src = static_cast<const uint32_t *>(p.table);
-        uint32_t *dst = reinterpret_cast<uint32_t *>(smem);
-        for (uint32_t i = threadIdx.x; i < kNeTableRows * 32; i += blockDim.x) dst[i] = src[i >> 5];
-    }
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < kWordStages; ++s) {
             mbar_init(&w_full[s], 1);
@@ -273,7 +264,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&d_empty[s], 4);
         }
         mbar_init(mma_done, 1);
+        mbar_init(table_bar, 1);
         fence_barrier_init();
+        // Value table by bulk copy: the expert half-table (128 KiB) straight
+        // into place; the NE pair table (4 KiB) into the word ring, to be
+        // replicated below before any word arrives there.
+        const uint32_t bytes = C == TcCodec::kExpert ? kExpertTableRows * 8u : kNeTableRows * 4u;
+        const uint8_t *src = static_cast<const uint8_t *>(p.table) + (C == TcCodec::kExpert ? half * bytes : 0u);
+        mbar_arrive_expect_tx(table_bar, bytes);
+        bulk_load_pieces(C == TcCodec::kExpert ? smem : word_tiles, src, bytes, table_bar);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -284,6 +283,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    mbar_wait_own(table_bar, 0, p.error);
+    if (C == TcCodec::kNe) {
+        // One copy of the pair table per bank: every gather conflict-free.
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(word_tiles);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(smem);
+        for (uint32_t i = threadIdx.x; i < kNeTableRows * 32; i += blockDim.x) dst[i] = src[i >> 5];
+        __syncthreads();
+    }
 
     const uint32_t n_units = unit_count(p);
     const uint32_t first = T::halves == 2 ? blockIdx.x >> 1 : blockIdx.x;

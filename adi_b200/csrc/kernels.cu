@@ -681,6 +681,201 @@ __global__ void __launch_bounds__(kGemmThreads, 1) ne_gemm_kernel(const NeGemmPa
     }
 }
 
+// NE projections of small batches, pipelined like expert_stream_kernel so
+// that tens of KiB per SM are in flight: a producer lane bulk-copies each
+// item's tile row (all its tiles, 128 B each) into a ring of slabs, and
+// eight consumer warps decode from shared memory, warp w taking tile columns
+// w, w + 8, ... with its inputs prefetched 8/NT columns ahead. The split and
+// the sums are ne_gemm_kernel's (per-warp partials over increasing columns,
+// lane pairs, then the eight warps in order), so the results are identical
+// to it and a token's output does not depend on its batch. The pair table is
+// kept in eight copies (lane & 7 picks one).
+constexpr uint32_t kNeSlabBytes = 32768;  // one tile row of up to 256 tiles (4096 columns)
+constexpr uint32_t kNeSlabStages = 3;
+constexpr uint32_t kNeStreamCopies = 8;
+constexpr uint32_t kNeStreamWarps = 8;
+
+struct NeStreamSmem {
+    static constexpr size_t table = size_t(kNeTableRows) * kNeStreamCopies * sizeof(float2);
+    static constexpr size_t ring = size_t(kNeSlabStages) * kNeSlabBytes;
+    static constexpr size_t red = size_t(kNeStreamWarps) * 16 * kMaxTokens * sizeof(float);
+    static constexpr size_t bars = (2 * kNeSlabStages + 1) * sizeof(uint64_t);
+    static constexpr size_t total = table + ring + red + bars;
+};
+
+template <int NT>
+__global__ void __launch_bounds__((kNeStreamWarps + 1) * 32, 1) ne_stream_kernel(const NeGemmParams p) {
+    using L = NeStreamSmem;
+    extern __shared__ __align__(128) uint8_t smem[];
+    float2 *table = reinterpret_cast<float2 *>(smem);
+    uint8_t *ring = smem + L::table;
+    float *red = reinterpret_cast<float *>(smem + L::table + L::ring);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::table + L::ring + L::red);
+    uint64_t *empty = full + kNeSlabStages;
+    uint64_t *table_bar = empty + kNeSlabStages;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t st = 0; st < kNeSlabStages; ++st) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], kNeStreamWarps);
+        }
+        mbar_init(table_bar, 1);
+        fence_barrier_init();
+        // The pair table (8 KiB) by bulk copy into the first slab, then
+        // replicated below before the producer fills any slab.
+        mbar_arrive_expect_tx(table_bar, kNeTableRows * sizeof(float2));
+        bulk_load_pieces(ring, p.table, kNeTableRows * sizeof(float2), table_bar);
+    }
+    __syncthreads();
+    mbar_wait_own(table_bar, 0, p.error);
+    {
+        const float2 *staged = reinterpret_cast<const float2 *>(ring);
+        for (uint32_t i = threadIdx.x; i < kNeTableRows * kNeStreamCopies; i += blockDim.x)
+            table[i] = staged[i / kNeStreamCopies];
+    }
+    __syncthreads();
+
+    const uint32_t TR = p.job[0].rows / 16;
+    const uint32_t n_items = work_count(p.work, TR);
+
+    if (warp == kNeStreamWarps) {
+        if (lane == 0) {
+            uint32_t slot = 0, phase = 0, issued = 0;
+            for (uint32_t i = blockIdx.x; i < n_items; i += gridDim.x) {
+                const Item it = work_item(p.work, i, TR);
+                const NeJob J = it.job ? p.job[1] : p.job[0];
+                const uint32_t TC = J.cols / 16;
+                if (!mbar_wait(&empty[slot], phase ^ 1u, p.error)) break;
+                const uint32_t bytes = TC * kNeU32PerTile * 4;
+                mbar_arrive_expect_tx(&full[slot], bytes);
+                bulk_load_pieces(ring + slot * kNeSlabBytes, J.trellis + (size_t)it.row_block * TC * kNeU32PerTile,
+                                 bytes, &full[slot]);
+                ++issued;
+                if (++slot == kNeSlabStages) {
+                    slot = 0;
+                    phase ^= 1u;
+                }
+            }
+            // Leave no copy in flight into this CTA's shared memory.
+            for (uint32_t k = 0; k < min(issued, kNeSlabStages); ++k) {
+                slot = slot == 0 ? kNeSlabStages - 1 : slot - 1;
+                if (slot == kNeSlabStages - 1) phase ^= 1u;
+                mbar_wait_own(&full[slot], phase, p.error);
+            }
+        }
+        return;
+    }
+
+    const float2 *my_table = table + (lane & (kNeStreamCopies - 1));
+    const uint32_t col0 = (lane & 1u) * 8;
+    uint32_t slot = 0, phase = 0;
+    bool failed = false;
+    for (uint32_t i = blockIdx.x; i < n_items; i += gridDim.x) {
+        const Item it = work_item(p.work, i, TR);
+        const NeJob J = it.job ? p.job[1] : p.job[0];
+        const uint32_t TC = J.cols / 16, n = it.count;
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+        if (!failed) failed = !mbar_wait(&full[slot], phase, p.error);
+        if (!failed) {
+            const uint32_t *words = reinterpret_cast<const uint32_t *>(ring + slot * kNeSlabBytes) + lane;
+            const float *xbase = J.x + (size_t)it.pos0 * J.cols + col0;
+            constexpr int kXAhead = NT >= 8 ? 1 : 8 / NT;
+            float4 xr0[kXAhead][NT], xr1[kXAhead][NT];
+#pragma unroll
+            for (int d = 0; d < kXAhead; ++d)
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    const uint32_t tcd = warp + d * kNeStreamWarps;
+                    if ((uint32_t)t < n && tcd < TC) {
+                        const float4 *src = reinterpret_cast<const float4 *>(xbase + (size_t)t * J.cols + tcd * 16);
+                        xr0[d][t] = __ldg(src);
+                        xr1[d][t] = __ldg(src + 1);
+                    } else {
+                        xr0[d][t] = xr1[d][t] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                }
+            for (uint32_t tc0 = warp; tc0 < TC; tc0 += kXAhead * kNeStreamWarps)
+#pragma unroll
+            for (int d = 0; d < kXAhead; ++d) {
+                const uint32_t tc = tc0 + d * kNeStreamWarps;
+                if (tc >= TC) break;
+                float4 x0[NT], x1[NT];
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    x0[t] = xr0[d][t];
+                    x1[t] = xr1[d][t];
+                }
+                const uint32_t next = tc + kXAhead * kNeStreamWarps;
+#pragma unroll
+                for (int t = 0; t < NT; ++t)
+                    if ((uint32_t)t < n && next < TC) {
+                        const float4 *src = reinterpret_cast<const float4 *>(xbase + (size_t)t * J.cols + next * 16);
+                        xr0[d][t] = __ldg(src);
+                        xr1[d][t] = __ldg(src + 1);
+                    }
+                const uint32_t v = words[tc * kNeU32PerTile];
+                const uint32_t v2 = __shfl_sync(0xffffffffu, v, (lane + 1u) & 31u);
+                const uint32_t s0 = v & 0xFFFFu;
+                const uint32_t s1 = __byte_perm(v, 0, 0x4403);
+                const uint32_t s2 = v >> 16;
+                const uint32_t s3 = __byte_perm(v, v2, 0x0025) & 0xFFFFu;
+                const float2 w0 = my_table[ne_table_index(state_product(s0)) * kNeStreamCopies];
+                const float2 w1 = my_table[ne_table_index(state_product(s1)) * kNeStreamCopies];
+                const float2 w2 = my_table[ne_table_index(state_product(s2)) * kNeStreamCopies];
+                const float2 w3 = my_table[ne_table_index(state_product(s3)) * kNeStreamCopies];
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    if ((uint32_t)t < n) {
+                        float part = w0.x * x0[t].x;
+                        part = fmaf(w0.y, x0[t].y, part);
+                        part = fmaf(w1.x, x0[t].z, part);
+                        part = fmaf(w1.y, x0[t].w, part);
+                        part = fmaf(w2.x, x1[t].x, part);
+                        part = fmaf(w2.y, x1[t].y, part);
+                        part = fmaf(w3.x, x1[t].z, part);
+                        part = fmaf(w3.y, x1[t].w, part);
+                        acc[t] += part;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (++slot == kNeSlabStages) {
+            slot = 0;
+            phase ^= 1u;
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], 1);
+        if ((lane & 1u) == 0) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) red[(warp * 16 + (lane >> 1)) * kMaxTokens + t] = acc[t];
+        }
+        named_sync(1, kNeStreamWarps * 32);
+        for (uint32_t idx = warp * 32 + lane; idx < 16 * n; idx += kNeStreamWarps * 32) {
+            const uint32_t t = idx / 16, row = idx % 16;
+            float sum = 0.0f;
+#pragma unroll
+            for (int w = 0; w < (int)kNeStreamWarps; ++w) sum += red[(w * 16 + row) * kMaxTokens + t];
+            J.acc[(size_t)(it.pos0 + t) * J.rows + it.row_block * 16 + row] = sum * J.weight_scale;
+        }
+        named_sync(1, kNeStreamWarps * 32);
+    }
+}
+
+template <int NT>
+void launch_ne_stream(const NeGemmParams &p, int grid, cudaStream_t s) {
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(ne_stream_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)NeStreamSmem::total);
+        configured = true;
+    }
+    ne_stream_kernel<NT><<<grid, (kNeStreamWarps + 1) * 32, NeStreamSmem::total, s>>>(p);
+}
+
 template <int RT, int NT>
 void launch_ne_instance(const NeGemmParams &p, int grid, cudaStream_t s) {
     static bool configured = false;
@@ -693,8 +888,18 @@ void launch_ne_instance(const NeGemmParams &p, int grid, cudaStream_t s) {
 
 void launch_ne_gemm(const NeGemmParams &p, int grid, cudaStream_t s) {
     // Small batches: one tile row per item and 1, 2, 4 or 8 tokens per item
-    // (the work list's chunk); otherwise four tile rows and eight tokens.
+    // (the work list's chunk), a warp per item when the tile columns allow;
+    // otherwise four tile rows and eight tokens.
     if (p.row_tiles != 1) return launch_ne_instance<kRowTiles, kMaxTokens>(p, grid, s);
+    if (!p.work.items && p.job[0].cols / 16 * kNeU32PerTile * 4 <= kNeSlabBytes &&
+        (p.work.dense_jobs == 1 || p.job[1].cols == p.job[0].cols)) {
+        switch (p.work.chunk) {
+            case 1: return launch_ne_stream<1>(p, grid, s);
+            case 2: return launch_ne_stream<2>(p, grid, s);
+            case 4: return launch_ne_stream<4>(p, grid, s);
+            default: return launch_ne_stream<kMaxTokens>(p, grid, s);
+        }
+    }
     switch (p.work.chunk) {
         case 1: return launch_ne_instance<1, 1>(p, grid, s);
         case 2: return launch_ne_instance<1, 2>(p, grid, s);
@@ -1428,8 +1633,97 @@ __global__ void head_protected_kernel(HeadParams p) {
     }
 }
 
+// The head for small batches when a row is 32 groups (2048 columns): lane g
+// owns group g, so its 64 inputs per token sit in registers for the whole
+// launch and each row's 40 code bytes and scale stream through a four-row
+// prefetch ring. NT tokens per pass, passes over the batch. Every sum is the
+// same as head_kernel's (codes in column order into `part`, fmaf by the
+// group scale, then the warp sum), so the results are identical.
+template <int NT>
+__global__ void __launch_bounds__(256) head_rows_kernel(HeadParams p) {
+    constexpr uint32_t kGroups = 32, kBytes = 2048 / 8 * 5, kAhead = 4;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t first = blockIdx.x * (blockDim.x / 32) + warp, stride = gridDim.x * (blockDim.x / 32);
+    for (uint32_t b0 = 0; b0 < p.batch; b0 += NT) {
+        const uint32_t nb = min((uint32_t)NT, p.batch - b0);
+        float x[NT][64];
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                const float4 v = (uint32_t)t < nb
+                                     ? __ldg(reinterpret_cast<const float4 *>(p.x + (size_t)(b0 + t) * 2048 +
+                                                                              lane * 64) + q)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                x[t][4 * q] = v.x;
+                x[t][4 * q + 1] = v.y;
+                x[t][4 * q + 2] = v.z;
+                x[t][4 * q + 3] = v.w;
+            }
+        uint2 ring[kAhead][5];
+        uint16_t scale_ring[kAhead];
+        auto fetch = [&](uint32_t row, uint2 (&w)[5], uint16_t &sc) {
+            if (row < p.rows) {
+                const uint2 *src = reinterpret_cast<const uint2 *>(p.packed + (size_t)row * kBytes + lane * 40);
+#pragma unroll
+                for (int k = 0; k < 5; ++k) w[k] = __ldg(src + k);
+                sc = __ldg(p.scales + (size_t)row * kGroups + lane);
+            }
+        };
+#pragma unroll
+        for (uint32_t d = 0; d < kAhead; ++d) fetch(first + d * stride, ring[d], scale_ring[d]);
+        for (uint32_t row0 = first; row0 < p.rows; row0 += kAhead * stride)
+#pragma unroll
+        for (uint32_t d = 0; d < kAhead; ++d) {
+            const uint32_t row = row0 + d * stride;
+            if (row >= p.rows) break;
+            uint32_t w[11];
+#pragma unroll
+            for (int k = 0; k < 5; ++k) {
+                w[2 * k] = ring[d][k].x;
+                w[2 * k + 1] = ring[d][k].y;
+            }
+            w[10] = 0;
+            const float scale = f16_bits_to_f32(scale_ring[d]);
+            fetch(row + kAhead * stride, ring[d], scale_ring[d]);
+            float part[NT];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) part[t] = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 64; ++k) {
+                const uint32_t bit = 5 * k;
+                const uint32_t code = __funnelshift_r(w[bit >> 5], w[(bit >> 5) + 1], bit & 31) & 31u;
+                const float c = (float)((int)code - 16);
+#pragma unroll
+                for (int t = 0; t < NT; ++t) part[t] = fmaf(c, x[t][k], part[t]);
+            }
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const float v = warp_sum(fmaf(part[t], scale, 0.0f));
+                if (lane == 0 && (uint32_t)t < nb) p.out[(size_t)(b0 + t) * p.rows + row] = v;
+            }
+        }
+    }
+}
+
 void launch_head(const HeadParams &p, cudaStream_t s) {
     if (p.batch == 0 || p.rows == 0) return;
+    if (p.cols == 2048 && p.batch <= 8) {
+        // Persistent: one block of eight row-streaming warps per SM.
+        static int sms = [] {
+            int device = 0, count = 148;
+            cudaGetDevice(&device);
+            cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device);
+            return count;
+        }();
+        const uint32_t blocks = min((p.rows + 7) / 8, (uint32_t)sms);
+        if (p.batch == 1)
+            head_rows_kernel<1><<<blocks, 256, 0, s>>>(p);
+        else
+            head_rows_kernel<2><<<blocks, 256, 0, s>>>(p);
+        if (p.protected_count) head_protected_kernel<<<p.protected_count, 256, 0, s>>>(p);
+        return;
+    }
     static bool configured = false;
     if (!configured) {
         cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);

@@ -111,7 +111,7 @@ def test_head_known_answer(ctx):
     h.release()
 
 
-@pytest.mark.parametrize("rows,cols,batch", [(64, 128, 1), (500, 2048, 3), (1000, 2048, 9)])
+@pytest.mark.parametrize("rows,cols,batch", [(64, 128, 1), (777, 2048, 1), (500, 2048, 3), (1000, 2048, 9)])
 def test_head_matches_oracle(ctx, oracle, rows, cols, batch):
     rng = SplitMix64(rows + cols + batch)
     head = head_chunk(rows, cols, rng, protected=[0, rows // 2, rows - 1])
@@ -120,6 +120,42 @@ def test_head_matches_oracle(ctx, oracle, rows, cols, batch):
     got = ctx.mach_head_matmul(h, x)
     want = oracle.head_matmul(head, x)
     assert rel_l2(got, want) <= FP32_TOL
+    h.release()
+
+
+def test_ne_batch_invariant():
+    """On CUDA cores the NE projection takes a warp-per-row kernel for 1, 2
+    or 4 inputs and the block kernels for more; a token's output is the
+    same bits in every batch."""
+    import adi_b200
+    c = adi_b200.Context(0)
+    try:
+        c.set_precision(0)
+        for rows, cols in [(512, 2048), (2048, 512), (4096, 2048)]:
+            rng = SplitMix64(0x1E0 + rows + cols)
+            m = ne_matrix(rows, cols, rng)
+            h = c.upload_ne(m)
+            x = rng.floats(17 * cols).reshape(17, cols)
+            full = c.mach_ne_matmul(h, x)
+            for batch in (1, 2, 3, 4, 8):
+                got = c.mach_ne_matmul(h, x[:batch])
+                assert np.array_equal(got.view(np.uint32), full[:batch].view(np.uint32)), (rows, cols, batch)
+            h.release()
+    finally:
+        c.close()
+
+
+def test_head_batch_invariant(ctx):
+    """Small batches take the register-resident head kernel, larger ones the
+    shared-memory one; a token's logits are the same bits either way."""
+    rng = SplitMix64(0x4EAD2)
+    head = head_chunk(300, 2048, rng, protected=[7])
+    h = ctx.upload_head(head)
+    x = rng.floats(9 * 2048).reshape(9, 2048)
+    nine = ctx.mach_head_matmul(h, x)
+    for batch in (1, 2, 3):
+        small = ctx.mach_head_matmul(h, x[:batch])
+        assert np.array_equal(small.view(np.uint32), nine[:batch].view(np.uint32)), batch
     h.release()
 
 

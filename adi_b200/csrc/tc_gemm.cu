@@ -772,40 +772,62 @@ __device__ __forceinline__ void write_f16_regs(const float (&v)[R], int k, bool 
                                                size_t half_stride, uint32_t row) {
     constexpr uint32_t n = 256u * R;
     const float s = exp2f((float)k);
-    if (split) {
-        // element i = t*R + r -> half (i >> 2) & 1, packed column 4(i >> 3) + (i & 3)
+    if constexpr (R % 4 != 0) {
+        // Two consecutive elements t*R + 2q, +1 (same half, adjacent packed
+        // columns) become one 4-byte store.
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-            const uint32_t i = threadIdx.x * R + r;
-            const uint32_t h = (i >> 2) & 1u;
-            out[h * half_stride + (size_t)row * (n / 2) + 4 * (i >> 3) + (i & 3u)] = __float2half_rn(v[r] * s);
+        for (int q = 0; q < R / 2; ++q) {
+            const __half2 pair = __floats2half2_rn(v[2 * q] * s, v[2 * q + 1] * s);
+            const uint32_t i = threadIdx.x * R + 2 * q;
+            __half *dst = split ? out + ((i >> 2) & 1u) * half_stride + (size_t)row * (n / 2) + 4 * (i >> 3) + (i & 3u)
+                                : out + (size_t)row * n + i;
+            *reinterpret_cast<__half2 *>(dst) = pair;
         }
     } else {
+        // Four consecutive elements t*R + 4q .. +3 become one 8-byte store.
 #pragma unroll
-        for (int r = 0; r < R; ++r) out[(size_t)row * n + threadIdx.x * R + r] = __float2half_rn(v[r] * s);
+        for (int q = 0; q < R / 4; ++q) {
+            const __half2 lo = __floats2half2_rn(v[4 * q] * s, v[4 * q + 1] * s);
+            const __half2 hi = __floats2half2_rn(v[4 * q + 2] * s, v[4 * q + 3] * s);
+            uint2 packed;
+            packed.x = *reinterpret_cast<const uint32_t *>(&lo);
+            packed.y = *reinterpret_cast<const uint32_t *>(&hi);
+            const uint32_t i = threadIdx.x * R + 4 * q;
+            if (split) {
+                // element i -> half (i >> 2) & 1, packed column 4 (i >> 3) + (i & 3)
+                const uint32_t h = (i >> 2) & 1u;
+                *reinterpret_cast<uint2 *>(out + h * half_stride + (size_t)row * (n / 2) + 4 * (i >> 3)) = packed;
+            } else {
+                *reinterpret_cast<uint2 *>(out + (size_t)row * n + i) = packed;
+            }
+        }
     }
 }
 
+// One block per row does every job of that row: the input row is read once
+// (16-byte loads) and transformed once per job's su.
 template <int R>
 __global__ void __launch_bounds__(256) prep_f16_regs_kernel(PrepF16Params p) {
     __shared__ float sh[256 * R];
     __shared__ float scratch[32];
     const uint32_t row = blockIdx.x;
-    const int job = blockIdx.y;
     const uint32_t token = p.grouped ? p.grouped[row] : row;
     const uint32_t expert = p.pos_expert ? p.pos_expert[row] : 0u;
-    const float *x = p.input + (size_t)token * p.cols + threadIdx.x * R;
-    const void *su = job ? p.su[1] : p.su[0];
+    float x[R];
+    load_regs<R>(p.input + (size_t)token * p.cols + threadIdx.x * R, x);
     const size_t su0 = (size_t)expert * p.su_stride + threadIdx.x * R;
-    float v[R];
+    for (int job = 0; job < p.jobs; ++job) {
+        const void *su = job ? p.su[1] : p.su[0];
+        float v[R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) v[r] = __fmul_rn(x[r], scale_value(su, p.su_is_f16, su0 + r));
-    fwht_regs<R>(v, sh);
+        for (int r = 0; r < R; ++r) v[r] = __fmul_rn(x[r], scale_value(su, p.su_is_f16, su0 + r));
+        fwht_regs<R>(v, sh);
 #pragma unroll
-    for (int r = 0; r < R; ++r) v[r] = __fmul_rn(v[r], p.scale);
-    const int k = scale_exponent(block_max_abs_regs<R>(v, scratch));
-    if (threadIdx.x == 0) (job ? p.kx[1] : p.kx[0])[row] = (int8_t)k;
-    write_f16_regs<R>(v, k, p.split != 0, job ? p.xh[1] : p.xh[0], (size_t)p.rows * (p.cols / 2), row);
+        for (int r = 0; r < R; ++r) v[r] = __fmul_rn(v[r], p.scale);
+        const int k = scale_exponent(block_max_abs_regs<R>(v, scratch));
+        if (threadIdx.x == 0) (job ? p.kx[1] : p.kx[0])[row] = (int8_t)k;
+        write_f16_regs<R>(v, k, p.split != 0, job ? p.xh[1] : p.xh[0], (size_t)p.rows * (p.cols / 2), row);
+    }
 }
 
 template <int R>
@@ -848,9 +870,9 @@ void launch_prep_f16(const PrepF16Params &p, cudaStream_t s) {
     if (p.rows == 0) return;
     const dim3 grid(p.rows, p.jobs);
     switch (p.cols) {
-        case 512: prep_f16_regs_kernel<2><<<grid, 256, 0, s>>>(p); return;
-        case 1024: prep_f16_regs_kernel<4><<<grid, 256, 0, s>>>(p); return;
-        case 2048: prep_f16_regs_kernel<8><<<grid, 256, 0, s>>>(p); return;
+        case 512: prep_f16_regs_kernel<2><<<p.rows, 256, 0, s>>>(p); return;
+        case 1024: prep_f16_regs_kernel<4><<<p.rows, 256, 0, s>>>(p); return;
+        case 2048: prep_f16_regs_kernel<8><<<p.rows, 256, 0, s>>>(p); return;
         default: prep_f16_kernel<<<grid, 256, p.cols * sizeof(float), s>>>(p);
     }
 }

@@ -458,6 +458,12 @@ constexpr uint32_t kSplitCombineTokens = 64;
 // Below this many inputs an NE projection streams faster on CUDA cores.
 constexpr uint32_t kNeTensorCoreMinBatch = 16;
 
+// launch_tc_gemm, failing loudly when a tensor map cannot be encoded.
+void tc_launch(TcCodec codec, const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid,
+               cudaStream_t s) {
+    if (!launch_tc_gemm(codec, map0, map1, p, grid, s)) throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
+}
+
 CUtensorMap b_map(const __half *x, uint32_t rows, uint32_t cols) {
     CUtensorMap map;
     if (!make_b_map(&map, x, rows, cols)) throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
@@ -491,7 +497,7 @@ void expert_matmul_tc(adi_cuda_context *c, ExpertDev &m, const float *in, uint32
     tp.table = m.codec->half_tables.ptr;
     tp.error = c->error_word;
     const uint64_t units = uint64_t(m.rows / 128) * ((batch + kTcMaxN - 1) / kTcMaxN);
-    launch_tc_gemm(TcCodec::kExpert, map, map, tp, gemm_grid(c, units, 2), c->stream);
+    tc_launch(TcCodec::kExpert, map, map, tp, gemm_grid(c, units, 2), c->stream);
     launch_finalize(acc, acc + size_t(batch) * m.rows, m.sv->ptr, 1, batch, m.rows, transform_scale(m.rows), out,
                     c->stream);
     c->stage_end();
@@ -525,7 +531,7 @@ void ne_matmul_tc(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batch
     tp.table = m.codec->table_f16.ptr;
     tp.error = c->error_word;
     const uint64_t units = uint64_t(m.rows / 128) * ((batch + kTcMaxN - 1) / kTcMaxN);
-    launch_tc_gemm(TcCodec::kNe, map, map, tp, gemm_grid(c, units, 1), c->stream);
+    tc_launch(TcCodec::kNe, map, map, tp, gemm_grid(c, units, 1), c->stream);
     launch_finalize(acc, nullptr, m.sv->ptr, 0, batch, m.rows, transform_scale(m.rows), out, c->stream);
     c->stage_end();
     c->after_launch(3);
@@ -735,7 +741,7 @@ void shared_expert_tc(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t 
     tp.table = L.shared[0].codec->table_f16.ptr;
     tp.error = c->error_word;
     const uint64_t units_gu = uint64_t(I / 128) * 2 * ((T + kTcMaxN - 1) / kTcMaxN);
-    launch_tc_gemm(TcCodec::kNe, map_g, map_u, tp, gemm_grid(c, units_gu, 1), s);
+    tc_launch(TcCodec::kNe, map_g, map_u, tp, gemm_grid(c, units_gu, 1), s);
     __half *xd = c->buffer<__half>("moe_sxh_d", size_t(T) * I);
     int8_t *kd = c->buffer<int8_t>("moe_skx_d", T);
     MidF16Params mp{};
@@ -763,7 +769,7 @@ void shared_expert_tc(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t 
     dp.table = tp.table;
     dp.error = c->error_word;
     const uint64_t units_d = uint64_t(H / 128) * ((T + kTcMaxN - 1) / kTcMaxN);
-    launch_tc_gemm(TcCodec::kNe, map_d, map_d, dp, gemm_grid(c, units_d, 1), s);
+    tc_launch(TcCodec::kNe, map_d, map_d, dp, gemm_grid(c, units_d, 1), s);
     c->stage_end();
     c->after_launch(4);
 }
@@ -880,12 +886,13 @@ float *routed_experts(adi_cuda_context *c, MoeDev &L, const float *in, size_t P,
                           I / 16 + H / 16, L.ka[0]->as<int8_t>(), 1.0f, kx_g, acc_g, P * I, I, H, uint32_t(P)};
         tp.job[1] = TcJob{L.trellis[1]->as<uint16_t>(), size_t(tiles_gu) * 48, L.gamma[1]->as<uint16_t>(),
                           I / 16 + H / 16, L.ka[1]->as<int8_t>(), 1.0f, kx_u, acc_u, P * I, I, H, uint32_t(P)};
+        tp.job[0].matrices = tp.job[1].matrices = L.local_experts;
         tp.units = rp.items_gate_up;
         tp.unit_count = rp.count_gate_up;
         tp.table = L.codec->half_tables.ptr;
         tp.error = c->error_word;
         c->stage(kStageExpertGateUp);
-        launch_tc_gemm(TcCodec::kExpert, map_g, map_u, tp, c->sms, s);
+        tc_launch(TcCodec::kExpert, map_g, map_u, tp, c->sms, s);
         c->stage_end();
 
         __half *xh_d = c->buffer<__half>("moe_xh_d", P * I);
@@ -913,13 +920,14 @@ float *routed_experts(adi_cuda_context *c, MoeDev &L, const float *in, size_t P,
         TcParams dp{};
         dp.job[0] = TcJob{L.trellis[2]->as<uint16_t>(), size_t(tiles_gu) * 48, L.gamma[2]->as<uint16_t>(),
                           I / 16 + H / 16, L.ka[2]->as<int8_t>(), 1.0f, kx_d, acc_d, P * H, H, I, uint32_t(P)};
+        dp.job[0].matrices = L.local_experts;
         dp.job[1] = dp.job[0];
         dp.units = rp.items_down;
         dp.unit_count = rp.count_down;
         dp.table = tp.table;
         dp.error = c->error_word;
         c->stage(kStageExpertDown);
-        launch_tc_gemm(TcCodec::kExpert, map_d, map_d, dp, c->sms, s);
+        tc_launch(TcCodec::kExpert, map_d, map_d, dp, c->sms, s);
         c->stage_end();
     } else {
         float *xg = c->buffer<float>("moe_xg", P * H);

@@ -20,7 +20,8 @@
 // is conflict-free; a CTA contracts the full K.
 //
 // Warp roles (736 threads, one persistent CTA per SM):
-//   warp 0 lane 0   trellis words of each K-chunk -> word ring (bulk copies)
+//   warp 0 lane 0   trellis words of each K-chunk -> word ring (one 2-D TMA
+//                   box of 8 tile rows per chunk)
 //   warp 1          TMEM allocation; lane 0 issues the MMAs
 //   warp 2 lane 0   B chunk (64 f16 x the unit's rows in 16-row boxes,
 //                   128B-swizzled) -> B ring (TMA), in its own warp so that
@@ -94,9 +95,8 @@ struct Traits<TcCodec::kExpert> {
     static constexpr uint32_t tile_bytes = 48;
     static constexpr uint32_t tiles_per_row = 8;         // per chunk
     static constexpr uint32_t words_bytes = 8 * 8 * 48;  // 8 tile rows
-    // Word-slot stride per tile row: 432 bytes puts consecutive tile rows 12
-    // banks apart, so the two tile rows one warp reads never share a bank.
-    static constexpr uint32_t row_stride = 432;
+    static constexpr uint32_t box_u32 = tiles_per_row * tile_bytes / 4;  // a chunk's tile row, in u32
+    static constexpr uint32_t row_stride = 384;          // the TMA box lands rows densely
     static constexpr uint32_t a_stages = kTmemAStages;
 };
 template <>
@@ -106,6 +106,7 @@ struct Traits<TcCodec::kNe> {
     static constexpr uint32_t tile_bytes = 128;
     static constexpr uint32_t tiles_per_row = 4;
     static constexpr uint32_t words_bytes = 8 * 4 * 128;
+    static constexpr uint32_t box_u32 = tiles_per_row * tile_bytes / 4;
     static constexpr uint32_t row_stride = 512;
     static constexpr uint32_t a_stages = kAStages;
 };
@@ -224,6 +225,7 @@ struct Ring {
 template <TcCodec C>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1,
+                   const __grid_constant__ CUtensorMap wmap0, const __grid_constant__ CUtensorMap wmap1,
                    const TcParams p) {
     using T = Traits<C>;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -298,29 +300,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            // ---- trellis words, 6 chunks ahead ----
+            // ---- trellis words: one 2-D TMA box per chunk (8 tile rows of
+            // the chunk's tiles), kWordStages chunks ahead ----
             Ring r;
             uint32_t issued = 0;
             bool ok = true;
             for (uint32_t u = first; u < n_units && ok; u += stride) {
                 const Unit un = unit_at(p, u);
                 const TcJob &J = un.job ? p.job[1] : p.job[0];
-                const uint32_t TC = J.cols / 16;
+                const CUtensorMap *wmap = un.job ? &wmap1 : &wmap0;
                 const uint32_t chunks = J.cols / T::chunk_cols;
-                const uint8_t *trellis =
-                    reinterpret_cast<const uint8_t *>(J.trellis) + (size_t)un.expert * J.expert_stride_bytes;
+                const int32_t y = (int32_t)(un.expert * (J.rows / 16) + un.m_block * 8);
                 for (uint32_t kc = 0; kc < chunks; ++kc) {
                     if (!mbar_wait(&w_empty[r.slot], r.phase ^ 1u, p.error)) {
                         ok = false;
                         break;
                     }
                     mbar_arrive_expect_tx(&w_full[r.slot], T::words_bytes);
-                    uint8_t *dst = word_tiles + r.slot * kWordSlotBytes;
-                    const uint32_t seg = T::tiles_per_row * T::tile_bytes;
-                    for (uint32_t row = 0; row < 8; ++row) {
-                        const size_t tile = (size_t)(un.m_block * 8 + row) * TC + kc * T::tiles_per_row;
-                        bulk_load(dst + row * T::row_stride, trellis + tile * T::tile_bytes, seg, &w_full[r.slot]);
-                    }
+                    tma_load_2d(word_tiles + r.slot * kWordSlotBytes, wmap, (int32_t)(kc * T::box_u32), y,
+                                &w_full[r.slot]);
                     ++issued;
                     r.advance(kWordStages);
                 }
@@ -611,15 +609,36 @@ EncodeTiled encode_fn() {
     return fn;
 }
 
+// The trellis words of a job as a 2-D u32 tensor: one row per tile row of
+// every stacked matrix, boxes of 8 tile rows x one chunk's tiles.
 template <TcCodec C>
-void launch_codec(const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid, cudaStream_t s) {
+bool make_word_map(CUtensorMap *map, const TcJob &J) {
+    using T = Traits<C>;
+    EncodeTiled fn = encode_fn();
+    if (!fn) return false;
+    const uint64_t row_u32 = uint64_t(J.cols / 16) * T::tile_bytes / 4;
+    const uint64_t rows = uint64_t(J.matrices ? J.matrices : 1) * (J.rows / 16);
+    const cuuint64_t dims[2] = {row_u32, rows};
+    const cuuint64_t strides[1] = {row_u32 * 4};
+    const cuuint32_t box[2] = {T::box_u32, 8};
+    const cuuint32_t elem[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint16_t *>(J.trellis), dims, strides, box, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <TcCodec C>
+bool launch_codec(const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid, cudaStream_t s) {
     static bool configured = false;
     if (!configured) {
         cudaFuncSetAttribute(tc_gemm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Smem::total);
         configured = true;
     }
+    CUtensorMap wmap0, wmap1;
+    if (!make_word_map<C>(&wmap0, p.job[0]) || !make_word_map<C>(&wmap1, p.job[1])) return false;
     if (C == TcCodec::kExpert) grid &= ~1;
-    tc_gemm_kernel<C><<<grid, kTcThreads, Smem::total, s>>>(map0, map1, p);
+    tc_gemm_kernel<C><<<grid, kTcThreads, Smem::total, s>>>(map0, map1, wmap0, wmap1, p);
+    return true;
 }
 
 }  // namespace
@@ -636,12 +655,10 @@ bool make_b_map(CUtensorMap *map, const __half *x, uint32_t rows, uint32_t cols)
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-void launch_tc_gemm(TcCodec codec, const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid,
+bool launch_tc_gemm(TcCodec codec, const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid,
                     cudaStream_t s) {
-    if (codec == TcCodec::kExpert)
-        launch_codec<TcCodec::kExpert>(map0, map1, p, grid, s);
-    else
-        launch_codec<TcCodec::kNe>(map0, map1, p, grid, s);
+    if (codec == TcCodec::kExpert) return launch_codec<TcCodec::kExpert>(map0, map1, p, grid, s);
+    return launch_codec<TcCodec::kNe>(map0, map1, p, grid, s);
 }
 
 // ---------------------------------------------------------------------------

@@ -25,6 +25,7 @@ struct TcJob {
     float *acc;                  // expert [2][positions][rows] (value halves); NE [positions][rows]
     size_t half_stride;          // positions * rows
     uint32_t rows, cols, positions;
+    uint32_t matrices;           // matrices stacked at expert_stride_bytes (0 or 1: one)
 };
 
 // Units {matrix, job << 16 | m_block, pos0, count} with a device-resident
@@ -43,7 +44,8 @@ struct TcParams {
 // B operand map over x [rows][cols] f16: boxes of 64 columns x 16 rows,
 // 128-byte swizzle.
 bool make_b_map(CUtensorMap *map, const __half *x, uint32_t rows, uint32_t cols);
-void launch_tc_gemm(TcCodec codec, const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid,
+// Returns false when a tensor map cannot be encoded (nothing launched).
+bool launch_tc_gemm(TcCodec codec, const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid,
                     cudaStream_t s);
 
 // x' = H(x * su) as f16 * 2^kx for the tensor-core path. With `split` the

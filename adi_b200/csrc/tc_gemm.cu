@@ -425,33 +425,50 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t wq1 = wq + 1u == kExpertU32PerTile ? 0u : wq + 1u;
             const uint32_t neg_mask = half == 0 ? 0x8000u : 0u;
             const uint32_t a_lane = tmem_base + ((32u * quarter) << 16) + kTmemAColumn0 + 8u * pair;
-            // Tile gammas (x 2^ka, as f16x2) are fetched eight chunks at a
-            // time: the 16 lanes of a half-warp share one tile row, so lane
-            // (h, i) holds the gamma of chunk kc0 + i / 2, tile column
-            // 2 * pair + i % 2, and the next eight chunks' load is issued a
-            // block ahead of its use.
-            auto fetch_gammas = [&](const Unit &un, const TcJob &J, uint32_t kc0, uint32_t chunks,
-                                    float gscale) -> uint32_t {
+            // Tile gammas are fetched eight chunks at a time: the 16 lanes of
+            // a half-warp share one tile row, so lane (h, i) holds the gamma
+            // bits of chunk kc0 + i / 2, tile column 2 * pair + i % 2. A
+            // block's load is issued eight chunks before its use, and the
+            // next unit's first block (with the unit itself and its ka) at
+            // the start of the current unit; the bits are scaled by 2^ka
+            // into f16x2 only when their block becomes current, so no load
+            // is waited on early.
+            auto fetch_gammas = [&](const Unit &un, const TcJob &J, uint32_t kc0) -> uint32_t {
                 const uint32_t i = lane & 15u, kc = kc0 + (i >> 1);
-                if (kc >= chunks) return 0u;
+                if (kc >= J.cols / T::chunk_cols) return 0u;
                 const uint32_t TC = J.cols / 16, TR = J.rows / 16;
                 const uint32_t diag = un.m_block * 8 + tr + kc * 8 + 2u * pair + (i & 1u);
-                const uint16_t *gam = J.gamma + (size_t)un.expert * J.gamma_stride;
-                const __half2 g2 =
-                    __float2half2_rn(__half2float(__ushort_as_half(__ldg(gam + wave_index(TR, TC, diag)))) * gscale);
+                return __ldg(J.gamma + (size_t)un.expert * J.gamma_stride + wave_index(TR, TC, diag));
+            };
+            auto scaled = [](uint32_t bits, float gscale) -> uint32_t {
+                const __half2 g2 = __float2half2_rn(__half2float(__ushort_as_half((uint16_t)bits)) * gscale);
                 return *reinterpret_cast<const uint32_t *>(&g2);
             };
+            Unit next = first < n_units ? unit_at(p, first) : Unit{};
+            uint32_t next_first = 0;
+            int8_t next_ka = 0;
+            if (first < n_units) {
+                const TcJob &Jn = next.job ? p.job[1] : p.job[0];
+                next_first = fetch_gammas(next, Jn, 0);
+                next_ka = Jn.ka[next.expert];
+            }
             for (uint32_t u = first; u < n_units; u += stride) {
-                const Unit un = unit_at(p, u);
+                const Unit un = next;
                 const TcJob &J = un.job ? p.job[1] : p.job[0];
                 const uint32_t chunks = J.cols / T::chunk_cols;
-                const float gscale = exp2f((float)J.ka[un.expert]);
-                uint32_t gblock = fetch_gammas(un, J, 0, chunks, gscale);
-                uint32_t gnext = fetch_gammas(un, J, 8, chunks, gscale);
+                const float gscale = exp2f((float)next_ka);
+                uint32_t gblock = scaled(next_first, gscale);
+                uint32_t gnext = fetch_gammas(un, J, 8);
+                if (u + stride < n_units) {
+                    next = unit_at(p, u + stride);
+                    const TcJob &Jn = next.job ? p.job[1] : p.job[0];
+                    next_first = fetch_gammas(next, Jn, 0);
+                    next_ka = Jn.ka[next.expert];
+                }
                 for (uint32_t kc = 0; kc < chunks; ++kc) {
                     if (kc > 0 && (kc & 7u) == 0) {
-                        gblock = gnext;
-                        gnext = fetch_gammas(un, J, kc + 8, chunks, gscale);
+                        gblock = scaled(gnext, gscale);
+                        gnext = fetch_gammas(un, J, kc + 8);
                     }
                     const uint32_t src = (lane & 16u) | ((kc & 7u) << 1);
                     const uint32_t gcur[2] = {__shfl_sync(0xffffffffu, gblock, src),

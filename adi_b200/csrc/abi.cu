@@ -449,6 +449,8 @@ uint32_t tokens_per_item(uint64_t expected) {
 // ---- standalone matmuls on device pointers -------------------------------
 
 bool tensor_core_shape(uint32_t rows, uint32_t cols) { return rows % 128 == 0 && cols % 128 == 0; }
+// The expert codec's tensor-core chunks are 256 columns wide.
+bool expert_tensor_core_shape(uint32_t rows, uint32_t cols) { return rows % 128 == 0 && cols % 256 == 0; }
 
 // Up to this many tokens the block's combine runs as one block per route,
 // then one per token, instead of one block per token doing all nine
@@ -539,7 +541,7 @@ void ne_matmul_tc(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batch
 
 void expert_matmul_dev(adi_cuda_context *c, ExpertDev &m, const float *in, uint32_t batch, float *out) {
     if (batch == 0) invalid("Mach expert batch shape mismatch");
-    if (c->precision == 1 && tensor_core_shape(m.rows, m.cols)) {
+    if (c->precision == 1 && expert_tensor_core_shape(m.rows, m.cols)) {
         expert_matmul_tc(c, m, in, batch, out);
         return;
     }
@@ -1035,7 +1037,7 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     rp.route_to_grouped = c->buffer<uint32_t>("moe_r2g", P);
     // Tensor cores whenever the precision mode allows them: even one
     // position per expert decodes faster there than on CUDA cores.
-    const bool tc = c->precision == 1 && tensor_core_shape(I, H);
+    const bool tc = c->precision == 1 && expert_tensor_core_shape(I, H) && expert_tensor_core_shape(H, I);
     const uint32_t nt = tc ? kTcMaxN : tokens_per_item((uint64_t(T) * 8 + E - 1) / E);
     const uint32_t rb_gate_up = expert_rows_per_item(H), rb_down = expert_rows_per_item(I);
     rp.chunk = nt;
@@ -1264,7 +1266,7 @@ void ep_experts_dev(adi_cuda_context *c, MoeDev &L, const float *recv, const uin
     if (rows == 0) return;
     cudaStream_t s = c->stream;
     const size_t P = rows;
-    const bool tc = c->precision == 1 && tensor_core_shape(I, H);
+    const bool tc = c->precision == 1 && expert_tensor_core_shape(I, H) && expert_tensor_core_shape(H, I);
     const uint32_t nt = tc ? kTcMaxN : tokens_per_item((uint64_t(rows) + local - 1) / local);
     const uint32_t rb_gate_up = expert_rows_per_item(H), rb_down = expert_rows_per_item(I);
     RouteParams rp{};

@@ -59,59 +59,76 @@ constexpr uint32_t kWordStages = ADI_TC_WORD_STAGES;
 constexpr uint32_t kBStages = ADI_TC_B_STAGES;
 constexpr uint32_t kAStages = ADI_TC_A_STAGES;
 constexpr uint32_t kBBoxRows = 16;                    // TMA box height: B loads only the unit's rows
-constexpr uint32_t kChunkK = 64;                     // f16 columns of A and B per chunk
-constexpr uint32_t kATileBytes = 128 * kChunkK * 2;  // 16 KiB
-constexpr uint32_t kBTileBytes = kTcMaxN * kChunkK * 2;
-constexpr uint32_t kWordSlotBytes = 4096;            // expert 3 KiB, NE 4 KiB per chunk
+constexpr uint32_t kChunkK = 64;                     // f16 columns of one 128-byte swizzled B sub-tile
+constexpr uint32_t kATileBytes = 128 * kChunkK * 2;  // 16 KiB (NE: A in shared memory)
+constexpr uint32_t kBSubTileBytes = kTcMaxN * kChunkK * 2;
 constexpr uint32_t kDecodeWarps = 16;
 constexpr uint32_t kDecodeWarp0 = 3;
 constexpr uint32_t kEpilogueWarp0 = kDecodeWarp0 + kDecodeWarps;
 constexpr uint32_t kTcThreads = (kEpilogueWarp0 + 4) * 32;
 // Tensor memory: two accumulator slots of kTcMaxN columns, then (expert
-// codec) kTmemAStages A slots of 32 columns (128 lanes x 64 f16).
+// codec) kTmemAStages A slots of one chunk each (128 lanes x 128 f16 = 64
+// columns).
 constexpr uint32_t kTmemAStages = 4;
 constexpr uint32_t kTmemAColumn0 = 2 * kTcMaxN;
-constexpr uint32_t kTmemAColumns = kChunkK / 2;
-constexpr uint32_t kTmemColumns = 256;
-static_assert(kTmemAColumn0 + kTmemAStages * kTmemAColumns <= kTmemColumns, "tensor memory budget");
 constexpr uint32_t kMaxAStages = kTmemAStages > kAStages ? kTmemAStages : kAStages;
-
-struct Smem {
-    static constexpr size_t a = 131072;  // 1024-aligned
-    static constexpr size_t b = a + kAStages * kATileBytes;
-    static constexpr size_t words = b + kBStages * kBTileBytes;
-    static constexpr size_t bars = words + kWordStages * kWordSlotBytes;
-    static constexpr uint32_t kBars = 2 * kWordStages + 2 * kBStages + 2 * kMaxAStages + 4 + 1 + 1;
-    static constexpr size_t total = bars + kBars * 8 + 16;
-};
-static_assert(Smem::total <= 232448, "shared memory budget");
 
 template <TcCodec C>
 struct Traits;
+// Per codec: a chunk is 8 tile rows x `tiles_per_row` tiles; `k_sub`
+// 64-column B sub-tiles per chunk (K elements of the MMA per chunk =
+// 64 * k_sub). Expert chunks are 256 matrix columns (128 packed): twice the
+// decode work per pipeline round trip of the NE codec's 64.
 template <>
 struct Traits<TcCodec::kExpert> {
     static constexpr uint32_t halves = 2;
-    static constexpr uint32_t chunk_cols = 128;          // matrix columns per chunk (64 packed)
+    static constexpr uint32_t chunk_cols = 256;          // matrix columns per chunk (128 packed)
+    static constexpr uint32_t k_sub = 2;
     static constexpr uint32_t tile_bytes = 48;
-    static constexpr uint32_t tiles_per_row = 8;         // per chunk
-    static constexpr uint32_t words_bytes = 8 * 8 * 48;  // 8 tile rows
-    static constexpr uint32_t box_u32 = tiles_per_row * tile_bytes / 4;  // a chunk's tile row, in u32
-    static constexpr uint32_t row_stride = 384;          // the TMA box lands rows densely
+    static constexpr uint32_t tiles_per_row = 16;        // per chunk
+    static constexpr uint32_t words_bytes = 8 * tiles_per_row * tile_bytes;  // 8 tile rows
+    static constexpr uint32_t box_u32 = tiles_per_row * tile_bytes / 4;     // a chunk's tile row, in u32
+    static constexpr uint32_t row_stride = tiles_per_row * tile_bytes;      // the TMA box lands rows densely
+    static constexpr uint32_t word_slot = 8192;
     static constexpr uint32_t a_stages = kTmemAStages;
+    static constexpr uint32_t a_tile_bytes = 0;          // A lives in tensor memory
+    static constexpr uint32_t tmem_a_columns = 64 * k_sub / 2;
+    static constexpr uint32_t tmem_columns = 512;
 };
 template <>
 struct Traits<TcCodec::kNe> {
     static constexpr uint32_t halves = 1;
     static constexpr uint32_t chunk_cols = 64;
+    static constexpr uint32_t k_sub = 1;
     static constexpr uint32_t tile_bytes = 128;
     static constexpr uint32_t tiles_per_row = 4;
-    static constexpr uint32_t words_bytes = 8 * 4 * 128;
+    static constexpr uint32_t words_bytes = 8 * tiles_per_row * tile_bytes;
     static constexpr uint32_t box_u32 = tiles_per_row * tile_bytes / 4;
-    static constexpr uint32_t row_stride = 512;
+    static constexpr uint32_t row_stride = tiles_per_row * tile_bytes;
+    static constexpr uint32_t word_slot = 4096;
     static constexpr uint32_t a_stages = kAStages;
+    static constexpr uint32_t a_tile_bytes = kATileBytes;
+    static constexpr uint32_t tmem_a_columns = 0;
+    static constexpr uint32_t tmem_columns = 256;
 };
-static_assert(8 * Traits<TcCodec::kExpert>::row_stride <= kWordSlotBytes, "expert word slot");
-static_assert(8 * Traits<TcCodec::kNe>::row_stride <= kWordSlotBytes, "NE word slot");
+
+template <TcCodec C>
+struct Smem {
+    using T = Traits<C>;
+    static constexpr size_t a = 131072;  // after the value table; 1024-aligned
+    static constexpr size_t b = a + size_t(T::a_stages) * T::a_tile_bytes;
+    static constexpr size_t b_tile = size_t(T::k_sub) * kBSubTileBytes;
+    static constexpr size_t words = b + kBStages * b_tile;
+    static constexpr size_t bars = words + size_t(kWordStages) * T::word_slot;
+    static constexpr uint32_t kBars = 2 * kWordStages + 2 * kBStages + 2 * kMaxAStages + 4 + 1 + 1;
+    static constexpr size_t total = bars + kBars * 8 + 16;
+};
+static_assert(Smem<TcCodec::kExpert>::total <= 232448, "shared memory budget");
+static_assert(Smem<TcCodec::kNe>::total <= 232448, "shared memory budget");
+static_assert(8 * Traits<TcCodec::kExpert>::row_stride <= Traits<TcCodec::kExpert>::word_slot, "expert word slot");
+static_assert(8 * Traits<TcCodec::kNe>::row_stride <= Traits<TcCodec::kNe>::word_slot, "NE word slot");
+static_assert(kTmemAColumn0 + kTmemAStages * Traits<TcCodec::kExpert>::tmem_a_columns <=
+                  Traits<TcCodec::kExpert>::tmem_columns, "tensor memory budget");
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
     // K-major, 128-byte swizzle: 8-row groups 1024 B apart (SBO), LBO unused
@@ -155,12 +172,14 @@ __device__ __forceinline__ void mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem,
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
-// Eight consecutive 32-bit TMEM columns of this thread's lane, then waits
+// Sixteen consecutive 32-bit TMEM columns of this thread's lane, then waits
 // for the stores to complete.
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(v[0]),
-        "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
         : "memory");
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -228,11 +247,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                    const __grid_constant__ CUtensorMap wmap0, const __grid_constant__ CUtensorMap wmap1,
                    const TcParams p) {
     using T = Traits<C>;
+    using S = Smem<C>;
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t *a_tiles = smem + Smem::a;
-    uint8_t *b_tiles = smem + Smem::b;
-    uint8_t *word_tiles = smem + Smem::words;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Smem::bars);
+    uint8_t *a_tiles = smem + S::a;
+    uint8_t *b_tiles = smem + S::b;
+    uint8_t *word_tiles = smem + S::words;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S::bars);
     uint64_t *w_full = bars;
     uint64_t *w_empty = w_full + kWordStages;
     uint64_t *b_full = w_empty + kWordStages;
@@ -278,7 +298,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(kTmemColumns));
+                     "r"(T::tmem_columns));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -317,7 +337,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(&w_full[r.slot], T::words_bytes);
-                    tma_load_2d(word_tiles + r.slot * kWordSlotBytes, wmap, (int32_t)(kc * T::box_u32), y,
+                    tma_load_2d(word_tiles + r.slot * T::word_slot, wmap, (int32_t)(kc * T::box_u32), y,
                                 &w_full[r.slot]);
                     ++issued;
                     r.advance(kWordStages);
@@ -346,10 +366,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         break;
                     }
                     const uint32_t n_pad = (un.count + kBBoxRows - 1) & ~(kBBoxRows - 1);
-                    mbar_arrive_expect_tx(&b_full[r.slot], n_pad * kChunkK * 2);
-                    for (uint32_t r0 = 0; r0 < n_pad; r0 += kBBoxRows)
-                        tma_load_2d(b_tiles + r.slot * kBTileBytes + r0 * kChunkK * 2, map, (int32_t)(kc * kChunkK),
-                                    (int32_t)(half * J.positions + un.pos0 + r0), &b_full[r.slot]);
+                    mbar_arrive_expect_tx(&b_full[r.slot], n_pad * kChunkK * 2 * T::k_sub);
+                    for (uint32_t j = 0; j < T::k_sub; ++j)
+                        for (uint32_t r0 = 0; r0 < n_pad; r0 += kBBoxRows)
+                            tma_load_2d(b_tiles + r.slot * S::b_tile + j * kBSubTileBytes + r0 * kChunkK * 2, map,
+                                        (int32_t)((kc * T::k_sub + j) * kChunkK),
+                                        (int32_t)(half * J.positions + un.pos0 + r0), &b_full[r.slot]);
                     ++issued;
                     r.advance(kBStages);
                 }
@@ -380,12 +402,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t b_addr = smem_u32(b_tiles + b.slot * kBTileBytes);
+                    const uint32_t b_addr = smem_u32(b_tiles + b.slot * S::b_tile);
                     if (C == TcCodec::kExpert) {
-                        const uint32_t a_tmem = tmem_base + kTmemAColumn0 + a.slot * kTmemAColumns;
+                        // K step k: A columns 8k .. 8k+7, B sub-tile k / 4, 32-byte step k % 4.
+                        const uint32_t a_tmem = tmem_base + kTmemAColumn0 + a.slot * T::tmem_a_columns;
 #pragma unroll
-                        for (uint32_t k = 0; k < kChunkK / 16; ++k)
-                            mma_f16_tmem_a(d_tmem, a_tmem + k * 8, smem_desc_sw128(b_addr + k * 32), idesc,
+                        for (uint32_t k = 0; k < T::k_sub * kChunkK / 16; ++k)
+                            mma_f16_tmem_a(d_tmem, a_tmem + k * 8,
+                                           smem_desc_sw128(b_addr + (k >> 2) * kBSubTileBytes + (k & 3u) * 32), idesc,
                                            (kc | k) != 0);
                     } else {
                         const uint32_t a_addr = smem_u32(a_tiles + a.slot * kATileBytes);
@@ -411,33 +435,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t dw = warp - kDecodeWarp0;
         Ring w, a;
         bool ok = true;
-        if (C == TcCodec::kExpert) {
+        if constexpr (C == TcCodec::kExpert) {
             const uint2 *table = reinterpret_cast<const uint2 *>(smem);
             // Lane = weight row of the chunk = TMEM lane: this warp may only
             // reach lanes 32*(warp % 4) .. +31, i.e. tile rows tr0, tr0 + 1.
-            // The four warps of a lane quarter split the chunk's 8 tile
-            // columns in pairs: warp `pair` decodes tile columns 2*pair and
-            // 2*pair + 1. In a tile, a row is states 2*rl and 2*rl + 1, stream
+            // The four warps of a lane quarter split the chunk's 16 tile
+            // columns in fours: warp `quad` decodes tile columns 4*quad ..
+            // 4*quad + 3. In a tile, a row is states 2*rl and 2*rl + 1, stream
             // bits 24*rl .. 24*rl + 28: one funnel shift yields both.
-            const uint32_t quarter = warp & 3u, pair = dw >> 2;
+            constexpr uint32_t kTilesPerWarp = T::tiles_per_row / 4;
+            const uint32_t quarter = warp & 3u, quad = dw >> 2;
             const uint32_t tr = 2u * quarter + (lane >> 4), rl = lane & 15u;
             const uint32_t bit0 = rl * 24u, wq = bit0 >> 5, woff = bit0 & 31u;
             const uint32_t wq1 = wq + 1u == kExpertU32PerTile ? 0u : wq + 1u;
             const uint32_t neg_mask = half == 0 ? 0x8000u : 0u;
-            const uint32_t a_lane = tmem_base + ((32u * quarter) << 16) + kTmemAColumn0 + 8u * pair;
-            // Tile gammas are fetched eight chunks at a time: the 16 lanes of
+            const uint32_t a_lane = tmem_base + ((32u * quarter) << 16) + kTmemAColumn0 + 4u * kTilesPerWarp * quad;
+            // Tile gammas are fetched four chunks at a time: the 16 lanes of
             // a half-warp share one tile row, so lane (h, i) holds the gamma
-            // bits of chunk kc0 + i / 2, tile column 2 * pair + i % 2. A
-            // block's load is issued eight chunks before its use, and the
+            // bits of chunk kc0 + i / 4, tile column 4 * quad + i % 4. A
+            // block's load is issued four chunks before its use, and the
             // next unit's first block (with the unit itself and its ka) at
             // the start of the current unit; the bits are scaled by 2^ka
             // into f16x2 only when their block becomes current, so no load
             // is waited on early.
             auto fetch_gammas = [&](const Unit &un, const TcJob &J, uint32_t kc0) -> uint32_t {
-                const uint32_t i = lane & 15u, kc = kc0 + (i >> 1);
+                const uint32_t i = lane & 15u, kc = kc0 + (i >> 2);
                 if (kc >= J.cols / T::chunk_cols) return 0u;
                 const uint32_t TC = J.cols / 16, TR = J.rows / 16;
-                const uint32_t diag = un.m_block * 8 + tr + kc * 8 + 2u * pair + (i & 1u);
+                const uint32_t diag = un.m_block * 8 + tr + kc * T::tiles_per_row + kTilesPerWarp * quad + (i & 3u);
                 return __ldg(J.gamma + (size_t)un.expert * J.gamma_stride + wave_index(TR, TC, diag));
             };
             auto scaled = [](uint32_t bits, float gscale) -> uint32_t {
@@ -458,7 +483,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const uint32_t chunks = J.cols / T::chunk_cols;
                 const float gscale = exp2f((float)next_ka);
                 uint32_t gblock = scaled(next_first, gscale);
-                uint32_t gnext = fetch_gammas(un, J, 8);
+                uint32_t gnext = fetch_gammas(un, J, 4);
                 if (u + stride < n_units) {
                     next = unit_at(p, u + stride);
                     const TcJob &Jn = next.job ? p.job[1] : p.job[0];
@@ -466,24 +491,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     next_ka = Jn.ka[next.expert];
                 }
                 for (uint32_t kc = 0; kc < chunks; ++kc) {
-                    if (kc > 0 && (kc & 7u) == 0) {
+                    if (kc > 0 && (kc & 3u) == 0) {
                         gblock = scaled(gnext, gscale);
-                        gnext = fetch_gammas(un, J, kc + 8);
+                        gnext = fetch_gammas(un, J, kc + 4);
                     }
-                    const uint32_t src = (lane & 16u) | ((kc & 7u) << 1);
-                    const uint32_t gcur[2] = {__shfl_sync(0xffffffffu, gblock, src),
-                                              __shfl_sync(0xffffffffu, gblock, src | 1u)};
+                    const uint32_t src = (lane & 16u) | ((kc & 3u) << 2);
+                    uint32_t gcur[kTilesPerWarp];
+#pragma unroll
+                    for (uint32_t t = 0; t < kTilesPerWarp; ++t) gcur[t] = __shfl_sync(0xffffffffu, gblock, src | t);
                     if (ok) ok = mbar_wait(&w_full[w.slot], w.phase, p.error);
                     if (ok) ok = mbar_wait(&a_empty[a.slot], a.phase ^ 1u, p.error);
                     ok = __all_sync(0xffffffffu, ok);  // tcgen05.st is warp-wide
                     if (ok) {
                         tc_fence_after();
-                        const uint32_t *tw = reinterpret_cast<const uint32_t *>(word_tiles + w.slot * kWordSlotBytes +
+                        const uint32_t *tw = reinterpret_cast<const uint32_t *>(word_tiles + w.slot * T::word_slot +
                                                                                 tr * T::row_stride) +
-                                             2u * pair * kExpertU32PerTile;
-                        uint32_t out[8];
+                                             kTilesPerWarp * quad * kExpertU32PerTile;
+                        uint32_t out[4 * kTilesPerWarp];
 #pragma unroll
-                        for (uint32_t t = 0; t < 2; ++t) {
+                        for (uint32_t t = 0; t < kTilesPerWarp; ++t) {
                             const uint32_t *tile = tw + t * kExpertU32PerTile;
                             const uint32_t window =
                                 __funnelshift_l(stream_order(tile[wq1]), stream_order(tile[wq]), woff);
@@ -503,7 +529,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             out[4 * t + 2] = *reinterpret_cast<const uint32_t *>(&vb0);
                             out[4 * t + 3] = *reinterpret_cast<const uint32_t *>(&vb1);
                         }
-                        tmem_st8(a_lane + a.slot * kTmemAColumns, out);
+                        tmem_st16(a_lane + a.slot * T::tmem_a_columns, out);
                         tc_fence_before();
                     }
                     __syncwarp();
@@ -532,7 +558,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         // Warp dw decodes tile row dw & 7: tiles j = 2 (dw >> 3) and the next.
                         const uint32_t trl = dw & 7u;
                         const uint32_t *tw =
-                            reinterpret_cast<const uint32_t *>(word_tiles + w.slot * kWordSlotBytes) + trl * 128;
+                            reinterpret_cast<const uint32_t *>(word_tiles + w.slot * T::word_slot) + trl * 128;
                         uint8_t *a_row = a_tiles + a.slot * kATileBytes + trl * 2048 + r * 128;
 #pragma unroll
                         for (uint32_t j = (dw >> 3) * 2; j < (dw >> 3) * 2 + 2; ++j) {
@@ -600,7 +626,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemColumns));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(T::tmem_columns));
     }
 }
 
@@ -648,13 +674,13 @@ template <TcCodec C>
 bool launch_codec(const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid, cudaStream_t s) {
     static bool configured = false;
     if (!configured) {
-        cudaFuncSetAttribute(tc_gemm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Smem::total);
+        cudaFuncSetAttribute(tc_gemm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Smem<C>::total);
         configured = true;
     }
     CUtensorMap wmap0, wmap1;
     if (!make_word_map<C>(&wmap0, p.job[0]) || !make_word_map<C>(&wmap1, p.job[1])) return false;
     if (C == TcCodec::kExpert) grid &= ~1;
-    tc_gemm_kernel<C><<<grid, kTcThreads, Smem::total, s>>>(map0, map1, wmap0, wmap1, p);
+    tc_gemm_kernel<C><<<grid, kTcThreads, Smem<C>::total, s>>>(map0, map1, wmap0, wmap1, p);
     return true;
 }
 

@@ -25,8 +25,10 @@ def tensor_cores(ctx):
     ctx.set_precision(0)
 
 
-@pytest.mark.parametrize("rows,cols", [(128, 128), (512, 2048), (2048, 512), (256, 1024)])
+@pytest.mark.parametrize("rows,cols", [(128, 256), (512, 2048), (2048, 512), (256, 1024), (128, 128)])
 def test_expert_matmul_tensor_cores(tensor_cores, oracle, rows, cols):
+    """(128, 128) is below the tensor-core path's 256-column chunk and takes
+    the CUDA-core kernel in the same precision mode."""
     ctx = tensor_cores
     rng = SplitMix64(0x7C0 + rows + cols)
     m = expert_matrix(rows, cols, rng)

@@ -56,7 +56,7 @@ GAMMA_BYTES = 160 * 2
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
 # tensor-core expert GEMM, averaged over the gate/up and down launches of one
 # 512-token block, from one ncu capture (profiles/tc_gemm_expert_t512.md).
-EXPERT_GEMM_TRAFFIC_T512 = (134.81216e6 + 20.108288e6 + 54.997248e6 + 21.127424e6) / 2
+EXPERT_GEMM_TRAFFIC_T512 = (134.808064e6 + 19.59936e6 + 55.002112e6 + 23.05024e6) / 2
 
 
 def parse():

@@ -169,6 +169,8 @@ struct MoeDev {
     uint32_t hidden, inner, experts;
     uint32_t first_expert = 0, local_experts = 0;  // routed experts held: [first, first + local)
     std::unique_ptr<DeviceArray> router;  // [(E+1)][H] bf16: router rows then the shared gate
+    std::unique_ptr<DeviceArray> router3; // [rows_pad][3H] bf16: router rows three times along K, zero rows pad
+    uint32_t router_rows_pad = 0;
     std::unique_ptr<DeviceArray> trellis[3], su[3], sv[3], gamma[3], ka[3];
     ExpertCodec *codec;
     NeDev shared[3];
@@ -776,6 +778,29 @@ void shared_expert_tc(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t 
     c->after_launch(4);
 }
 
+// Router and shared-gate logits [T][E+1]: on tensor cores in precision mode
+// 1 (exact three-term bf16 split of the activations, fp32 accumulation),
+// else the CUDA-core fp32 kernel. Returns the kernels launched.
+uint32_t router_logits(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *logits) {
+    const uint32_t H = L.hidden, E = L.experts;
+    if (c->precision == 1 && H % 64 == 0) {
+        RouterParams rp{};
+        rp.rows_pad = L.router_rows_pad;
+        rp.tokens = T;
+        rp.k = 3 * H;
+        rp.parts = router_tc_parts(rp.rows_pad, T, H, c->sms);
+        rp.partials = c->buffer<float>("router_parts", size_t(rp.parts) * T * rp.rows_pad);
+        rp.error = c->error_word;
+        uint16_t *xs = c->buffer<uint16_t>("router_xs", size_t(T) * 3 * H);
+        if (!launch_router_tc(rp, in, xs, L.router3->as<uint16_t>(), logits, E + 1, E + 1, c->stream))
+            throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
+        return 3;
+    }
+    launch_bf16_gemm(L.router->as<uint16_t>(), E, L.router->as<uint16_t>() + size_t(E) * H, 1, in, T, H, logits,
+                     E + 1, c->stream);
+    return 1;
+}
+
 // The shared NE SwiGLU expert over T tokens: sacc_d = the down projection's
 // accumulators [T][H] before its output transform (combine applies it).
 void shared_expert(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *sacc_d) {
@@ -1016,8 +1041,7 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     uint32_t *re = route_experts_out ? route_experts_out : c->buffer<uint32_t>("moe_re", P);
     float *rw = route_weights_out ? route_weights_out : c->buffer<float>("moe_rw", P);
     c->stage(kStageRouter);
-    launch_bf16_gemm(L.router->as<uint16_t>(), E, L.router->as<uint16_t>() + size_t(E) * H, 1, in, T, H, logits,
-                     E + 1, s);
+    const uint32_t router_launches = router_logits(c, L, in, T, logits);
     c->stage_end();
     c->stage(kStageTopk);
     launch_top_experts(logits, E + 1, T, E, re, rw, s);
@@ -1089,7 +1113,7 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
         launch_ep_finalize(fp, s);
         launch_ep_combine(ecp, s);
         c->stage_end();
-        c->after_launch(2 + route_launches + 2);
+        c->after_launch(router_launches + 1 + route_launches + 2);
         return;
     }
     CombineParams cp{};
@@ -1112,7 +1136,7 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     c->stage_end();
     // router, top-k, the routing kernels, combine (the routed and shared
     // experts count their own four each)
-    c->after_launch(2 + route_launches + 1);
+    c->after_launch(router_launches + 1 + route_launches + 1);
 }
 
 // Host-pointer wrapper: stage inputs, run on device, read outputs back.
@@ -1151,6 +1175,15 @@ uint64_t upload_moe(adi_cuda_context *c, const adi_moe_layer &layer, uint32_t fi
     std::memcpy(router.data(), l->router.values, size_t(E) * H * 2);
     std::memcpy(router.data() + size_t(E) * H, l->shared_expert_gate.values, size_t(H) * 2);
     d->router = upload_bytes(router.data(), router.size() * 2, "router");
+    // The tensor-core router's operand: each row repeated three times along
+    // K (against the three bf16 terms of the activations), rows padded to
+    // the MMA's 128.
+    d->router_rows_pad = (E + 1 + 127) / 128 * 128;
+    std::vector<uint16_t> router3(size_t(d->router_rows_pad) * 3 * H, 0);
+    for (uint32_t r = 0; r <= E; ++r)
+        for (uint32_t j = 0; j < 3; ++j)
+            std::memcpy(router3.data() + (size_t(r) * 3 + j) * H, router.data() + size_t(r) * H, size_t(H) * 2);
+    d->router3 = upload_bytes(router3.data(), router3.size() * 2, "router");
     const float *tlut = l->routed[3 * size_t(first)].tlut;
     const uint32_t tiles = (I / 16) * (H / 16);
     for (int p = 0; p < 3; ++p) {
@@ -1216,9 +1249,7 @@ void ep_dispatch_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const floa
         check(cudaMemcpyAsync(logits, given_logits, size_t(T) * (E + 1) * 4, cudaMemcpyDeviceToDevice, s),
               "logits copy");
     } else {
-        launch_bf16_gemm(L.router->as<uint16_t>(), E, L.router->as<uint16_t>() + size_t(E) * H, 1, in, T, H,
-                         logits, E + 1, s);
-        c->after_launch(1);
+        c->after_launch(router_logits(c, L, in, T, logits));
     }
     c->stage_end();
     c->stage(kStageTopk);

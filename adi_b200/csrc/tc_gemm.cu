@@ -40,6 +40,7 @@
 #include "tc_gemm.cuh"
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 namespace adi_cuda {
@@ -631,6 +632,148 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Router logits on tensor cores
+//
+// logits[t][r] = sum_k W[r][k] * x[t][k] with bf16 router rows W (exact in
+// bf16) and fp32 activations split exactly into three bf16 terms, x = x1 +
+// x2 + x3 (x1 the bf16 rounding of x, x2 of what x1 leaves, x3 the rest,
+// which fits bf16 exactly). Every product of bf16 values is exact in fp32,
+// so [W W W] . [x1 x2 x3] is the fp32 dot product up to the order of the
+// fp32 accumulation. K (3H) is split over CTAs; a second kernel sums the
+// parts in order, so the result is deterministic.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kRouterStages = 4;
+constexpr uint32_t kRouterN = 64;                          // tokens per unit
+constexpr uint32_t kRouterATile = 128 * kChunkK * 2;       // 16 KiB
+constexpr uint32_t kRouterBTile = kRouterN * kChunkK * 2;  // 8 KiB
+constexpr size_t kRouterSmem = kRouterStages * (kRouterATile + kRouterBTile) + (2 * kRouterStages + 1) * 8 + 16;
+
+__global__ void router_split_kernel(const float *x, uint32_t count, uint32_t H, uint16_t *xs) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) {
+        const uint32_t t = i / H, k = i - t * H;
+        const float v = x[i];
+        const __nv_bfloat16 x1 = __float2bfloat16_rn(v);
+        const float r1 = __fsub_rn(v, __bfloat162float(x1));
+        const __nv_bfloat16 x2 = __float2bfloat16_rn(r1);
+        const __nv_bfloat16 x3 = __float2bfloat16_rn(__fsub_rn(r1, __bfloat162float(x2)));
+        uint16_t *row = xs + (size_t)t * 3 * H + k;
+        row[0] = __bfloat16_as_ushort(x1);
+        row[H] = __bfloat16_as_ushort(x2);
+        row[2 * H] = __bfloat16_as_ushort(x3);
+    }
+}
+
+__global__ void __launch_bounds__(192, 1)
+    router_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
+                       const RouterParams p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t *a_tiles = smem;
+    uint8_t *b_tiles = smem + kRouterStages * kRouterATile;
+    uint64_t *full = reinterpret_cast<uint64_t *>(b_tiles + kRouterStages * kRouterBTile);
+    uint64_t *empty = full + kRouterStages;
+    uint64_t *done = empty + kRouterStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    // Unit = (k part, token chunk, 128-row block), row block fastest.
+    const uint32_t m_blocks = p.rows_pad / 128, n_chunks = (p.tokens + kRouterN - 1) / kRouterN;
+    const uint32_t mb = blockIdx.x % m_blocks, nc = (blockIdx.x / m_blocks) % n_chunks;
+    const uint32_t part = blockIdx.x / (m_blocks * n_chunks);
+    const uint32_t chunks = p.k / kChunkK, per_part = (chunks + p.parts - 1) / p.parts;
+    const uint32_t kc0 = part * per_part, kc1 = min(chunks, kc0 + per_part);
+    const uint32_t n0 = nc * kRouterN, n = min(kRouterN, p.tokens - n0), n_pad = (n + 15u) & ~15u;
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < kRouterStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kRouterN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        Ring r;
+        for (uint32_t kc = kc0; kc < kc1; ++kc) {
+            if (!mbar_wait(&empty[r.slot], r.phase ^ 1u, p.error)) break;
+            mbar_arrive_expect_tx(&full[r.slot], kRouterATile + n_pad * kChunkK * 2);
+            tma_load_2d(a_tiles + r.slot * kRouterATile, &amap, (int32_t)(kc * kChunkK), (int32_t)(mb * 128),
+                        &full[r.slot]);
+            for (uint32_t r0 = 0; r0 < n_pad; r0 += kBBoxRows)
+                tma_load_2d(b_tiles + r.slot * kRouterBTile + r0 * kChunkK * 2, &bmap, (int32_t)(kc * kChunkK),
+                            (int32_t)(n0 + r0), &full[r.slot]);
+            r.advance(kRouterStages);
+        }
+        // Leave no copy in flight: the last stages issued land on their own.
+        for (uint32_t k = 0; k < min(kc1 - kc0, kRouterStages); ++k) {
+            r.slot = r.slot == 0 ? kRouterStages - 1 : r.slot - 1;
+            if (r.slot == kRouterStages - 1) r.phase ^= 1u;
+            mbar_wait_own(&full[r.slot], r.phase, p.error);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // A and B bf16 (formats at bits 7 and 10), D f32, K-major, N, M = 128.
+        const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((n_pad >> 3) << 17) | ((128u >> 4) << 24);
+        Ring r;
+        for (uint32_t kc = kc0; kc < kc1; ++kc) {
+            if (!mbar_wait(&full[r.slot], r.phase, p.error)) break;
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(a_tiles + r.slot * kRouterATile);
+            const uint32_t b_addr = smem_u32(b_tiles + r.slot * kRouterBTile);
+#pragma unroll
+            for (uint32_t k = 0; k < kChunkK / 16; ++k)
+                mma_f16(tmem_base, smem_desc_sw128(a_addr + k * 32), smem_desc_sw128(b_addr + k * 32), idesc,
+                        (kc > kc0 || k) ? 1u : 0u);
+            mma_commit(&empty[r.slot]);
+            r.advance(kRouterStages);
+        }
+        mma_commit(done);
+    } else if (warp >= 2) {
+        // Epilogue: warp 2 + q reads TMEM lanes 32 q .. +31 (rows of the block).
+        const uint32_t quarter = warp & 3u, row = mb * 128 + quarter * 32 + lane;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait_own(done, 0, p.error));
+        tc_fence_after();
+        if (ok && kc1 > kc0) {
+            float *out = p.partials + ((size_t)part * p.tokens + n0) * p.rows_pad + row;
+            for (uint32_t c0 = 0; c0 < n_pad; c0 += 16) {
+                float v[16];
+                tmem_ld16(tmem_base + ((quarter * 32) << 16) + c0, v);
+#pragma unroll
+                for (uint32_t i = 0; i < 16; ++i)
+                    if (c0 + i < n) out[(size_t)(c0 + i) * p.rows_pad] = v[i];
+            }
+        } else if (kc1 <= kc0) {
+            float *out = p.partials + ((size_t)part * p.tokens + n0) * p.rows_pad + row;
+            for (uint32_t i = 0; i < n; ++i) out[(size_t)i * p.rows_pad] = 0.0f;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kRouterN));
+    }
+}
+
+// logits[t][r] = sum over parts in order, for the rows that exist.
+__global__ void router_reduce_kernel(const float *partials, uint32_t parts, uint32_t tokens, uint32_t rows_pad,
+                                     uint32_t rows, float *logits, uint32_t stride) {
+    const size_t total = (size_t)tokens * rows;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t t = (uint32_t)(i / rows), r = (uint32_t)(i - (size_t)t * rows);
+        float sum = 0.0f;
+        for (uint32_t q = 0; q < parts; ++q) sum += partials[((size_t)q * tokens + t) * rows_pad + r];
+        logits[(size_t)t * stride + r] = sum;
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 
@@ -945,6 +1088,48 @@ void launch_mid_f16(const MidF16Params &p, cudaStream_t s) {
         case 2048: mid_f16_regs_kernel<8><<<p.positions, 256, 0, s>>>(p); return;
         default: mid_f16_kernel<<<p.positions, 256, 2 * p.inner * sizeof(float), s>>>(p);
     }
+}
+
+
+// The router's split activations [tokens][3H] bf16 and the replicated router
+// [rows_pad][3H] bf16 as 2-D tensors in 64-column, 128B-swizzled boxes.
+static bool make_bf16_map(CUtensorMap *map, const uint16_t *base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    EncodeTiled fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {kChunkK, box_rows};
+    const cuuint32_t elem[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(base), dims, strides, box, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+uint32_t router_tc_parts(uint32_t rows_pad, uint32_t tokens, uint32_t hidden, int sms) {
+    const uint32_t units = (rows_pad / 128) * ((tokens + kRouterN - 1) / kRouterN);
+    const uint32_t chunks = 3 * hidden / kChunkK;
+    uint32_t parts = (uint32_t)sms / (units ? units : 1);
+    if (parts < 1) parts = 1;
+    if (parts > chunks) parts = chunks;
+    return parts;
+}
+
+bool launch_router_tc(const RouterParams &p, const float *x, uint16_t *xs, const uint16_t *w3, float *logits,
+                      uint32_t stride, uint32_t rows, cudaStream_t s) {
+    const uint32_t H = p.k / 3;
+    router_split_kernel<<<1184, 256, 0, s>>>(x, p.tokens * H, H, xs);
+    CUtensorMap amap, bmap;
+    if (!make_bf16_map(&amap, w3, p.rows_pad, p.k, 128) || !make_bf16_map(&bmap, xs, p.tokens, p.k, kBBoxRows))
+        return false;
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRouterSmem);
+        configured = true;
+    }
+    const uint32_t units = (p.rows_pad / 128) * ((p.tokens + kRouterN - 1) / kRouterN) * p.parts;
+    router_gemm_kernel<<<units, 192, kRouterSmem, s>>>(amap, bmap, p);
+    router_reduce_kernel<<<592, 256, 0, s>>>(p.partials, p.parts, p.tokens, p.rows_pad, rows, logits, stride);
+    return true;
 }
 
 }  // namespace adi_cuda

@@ -44,6 +44,20 @@ struct TcParams {
 // B operand map over x [rows][cols] f16: boxes of 64 columns x 16 rows,
 // 128-byte swizzle.
 bool make_b_map(CUtensorMap *map, const __half *x, uint32_t rows, uint32_t cols);
+// Router logits on tensor cores (see tc_gemm.cu): W3 = [W W W] bf16
+// [rows_pad][k = 3H], activations split into xs [tokens][3H] bf16, split-K
+// partials [parts][tokens][rows_pad], summed in order into logits rows
+// 0 .. rows-1 (row stride `stride`). Returns false when a tensor map cannot
+// be encoded.
+struct RouterParams {
+    uint32_t rows_pad, tokens, k, parts;
+    float *partials;
+    uint32_t *error;
+};
+uint32_t router_tc_parts(uint32_t rows_pad, uint32_t tokens, uint32_t hidden, int sms);
+bool launch_router_tc(const RouterParams &p, const float *x, uint16_t *xs, const uint16_t *w3, float *logits,
+                      uint32_t stride, uint32_t rows, cudaStream_t s);
+
 // Returns false when a tensor map cannot be encoded (nothing launched).
 bool launch_tc_gemm(TcCodec codec, const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid,
                     cudaStream_t s);

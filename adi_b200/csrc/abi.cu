@@ -462,6 +462,11 @@ constexpr uint32_t kSplitCombineTokens = 64;
 // Below this many inputs an NE projection streams faster on CUDA cores.
 constexpr uint32_t kNeTensorCoreMinBatch = 16;
 
+// K parts for a dense NE tensor-core launch of `units` units: two when that
+// still fits the SMs (so that small launches use twice the SMs, the two
+// partial sums added by the consumer), else one.
+uint32_t ne_ksplit(adi_cuda_context *c, uint64_t units) { return units * 2 <= uint64_t(c->sms) ? 2u : 1u; }
+
 // launch_tc_gemm, failing loudly when a tensor map cannot be encoded.
 void tc_launch(TcCodec codec, const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid,
                cudaStream_t s) {
@@ -511,7 +516,9 @@ void expert_matmul_tc(adi_cuda_context *c, ExpertDev &m, const float *in, uint32
 void ne_matmul_tc(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batch, float *out) {
     __half *xh = c->buffer<__half>("xh_prep", size_t(batch) * m.cols);
     int8_t *kx = c->buffer<int8_t>("kx_prep", batch);
-    float *acc = c->buffer<float>("acc", size_t(batch) * m.rows);
+    const uint64_t units = uint64_t(m.rows / 128) * ((batch + kTcMaxN - 1) / kTcMaxN);
+    const uint32_t ks = ne_ksplit(c, units);
+    float *acc = c->buffer<float>("acc", ks * size_t(batch) * m.rows);
     c->stage(kStageNeMatmul);
     PrepF16Params pp{};
     pp.input = in;
@@ -532,11 +539,12 @@ void ne_matmul_tc(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batch
     tp.job[1] = tp.job[0];
     tp.dense_positions = batch;
     tp.dense_jobs = 1;
+    tp.dense_ksplit = ks;
     tp.table = m.codec->table_f16.ptr;
     tp.error = c->error_word;
-    const uint64_t units = uint64_t(m.rows / 128) * ((batch + kTcMaxN - 1) / kTcMaxN);
-    tc_launch(TcCodec::kNe, map, map, tp, gemm_grid(c, units, 1), c->stream);
-    launch_finalize(acc, nullptr, m.sv->ptr, 0, batch, m.rows, transform_scale(m.rows), out, c->stream);
+    tc_launch(TcCodec::kNe, map, map, tp, gemm_grid(c, units * ks, 1), c->stream);
+    launch_finalize(acc, ks == 2 ? acc + size_t(batch) * m.rows : nullptr, m.sv->ptr, 0, batch, m.rows,
+                    transform_scale(m.rows), out, c->stream);
     c->stage_end();
     c->after_launch(3);
 }
@@ -732,8 +740,10 @@ void shared_expert_tc(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t 
     pp.su_is_f16 = 0;
     pp.split = 0;
     launch_prep_f16(pp, s);
-    float *acc_g = c->buffer<float>("moe_sacc_g", size_t(T) * I);
-    float *acc_u = c->buffer<float>("moe_sacc_u", size_t(T) * I);
+    const uint64_t units_gu = uint64_t(I / 128) * 2 * ((T + kTcMaxN - 1) / kTcMaxN);
+    const uint32_t ks = ne_ksplit(c, units_gu);
+    float *acc_g = c->buffer<float>("moe_sacc_g", ks * size_t(T) * I);
+    float *acc_u = c->buffer<float>("moe_sacc_u", ks * size_t(T) * I);
     const CUtensorMap map_g = b_map(xg, T, H), map_u = b_map(xu, T, H);
     TcParams tp{};
     tp.job[0] = TcJob{L.shared[0].trellis->as<uint16_t>(), 0, nullptr, 0, nullptr, L.shared[0].weight_scale, kg,
@@ -742,10 +752,10 @@ void shared_expert_tc(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t 
                       acc_u, size_t(T) * I, I, H, T};
     tp.dense_positions = T;
     tp.dense_jobs = 2;
+    tp.dense_ksplit = ks;
     tp.table = L.shared[0].codec->table_f16.ptr;
     tp.error = c->error_word;
-    const uint64_t units_gu = uint64_t(I / 128) * 2 * ((T + kTcMaxN - 1) / kTcMaxN);
-    tc_launch(TcCodec::kNe, map_g, map_u, tp, gemm_grid(c, units_gu, 1), s);
+    tc_launch(TcCodec::kNe, map_g, map_u, tp, gemm_grid(c, units_gu * ks, 1), s);
     __half *xd = c->buffer<__half>("moe_sxh_d", size_t(T) * I);
     int8_t *kd = c->buffer<int8_t>("moe_skx_d", T);
     MidF16Params mp{};
@@ -755,7 +765,8 @@ void shared_expert_tc(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t 
     mp.sv_up = L.shared[1].sv->ptr;
     mp.su_down = L.shared[2].su->ptr;
     mp.is_f16 = 0;
-    mp.halves = 1;
+    mp.halves = ks;
+    mp.half_stride = size_t(T) * I;
     mp.split = 0;
     mp.inner = I;
     mp.scale = transform_scale(I);

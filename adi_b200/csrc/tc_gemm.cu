@@ -208,25 +208,35 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// A unit: matrix, job, 128-row block, positions, and (dense NE work split
+// along K) the part `kpart` covering chunks [kc0, kc1); kc1 == 0: all.
 struct Unit {
-    uint32_t expert, job, m_block, pos0, count;
+    uint32_t expert, job, m_block, pos0, count, kpart = 0, kc0 = 0, kc1 = 0;
 };
+
+__device__ __forceinline__ uint32_t dense_ksplit(const TcParams &p) { return p.dense_ksplit > 1 ? p.dense_ksplit : 1; }
 
 __device__ __forceinline__ uint32_t unit_count(const TcParams &p) {
     if (p.units) return *p.unit_count;
-    return (p.job[0].rows / 128) * p.dense_jobs * ((p.dense_positions + kTcMaxN - 1) / kTcMaxN);
+    return (p.job[0].rows / 128) * p.dense_jobs * ((p.dense_positions + kTcMaxN - 1) / kTcMaxN) * dense_ksplit(p);
 }
 
+template <typename T>
 __device__ __forceinline__ Unit unit_at(const TcParams &p, uint32_t i) {
     if (p.units) {
         const uint4 v = p.units[i];
         return Unit{v.x, v.y >> 16, v.y & 0xFFFFu, v.z, v.w};
     }
     const uint32_t mbs = p.job[0].rows / 128;
-    const uint32_t mb = i % mbs;
-    const uint32_t job = (i / mbs) % p.dense_jobs;
-    const uint32_t pos0 = (i / (mbs * p.dense_jobs)) * kTcMaxN;
-    return Unit{0u, job, mb, pos0, min(kTcMaxN, p.dense_positions - pos0)};
+    const uint32_t base = mbs * p.dense_jobs * ((p.dense_positions + kTcMaxN - 1) / kTcMaxN);
+    const uint32_t kpart = i / base, r = i - kpart * base;
+    const uint32_t mb = r % mbs;
+    const uint32_t job = (r / mbs) % p.dense_jobs;
+    const uint32_t pos0 = (r / (mbs * p.dense_jobs)) * kTcMaxN;
+    const uint32_t chunks = p.job[0].cols / T::chunk_cols, ks = dense_ksplit(p);
+    const uint32_t per = (chunks + ks - 1) / ks;
+    const uint32_t kc0 = min(chunks, kpart * per), kc1 = min(chunks, kc0 + per);
+    return Unit{0u, job, mb, pos0, min(kTcMaxN, p.dense_positions - pos0), kpart, kc0, ks > 1 ? kc1 : 0u};
 }
 
 // Mutable ring position: slot index and the parity of its current use.
@@ -327,12 +337,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t issued = 0;
             bool ok = true;
             for (uint32_t u = first; u < n_units && ok; u += stride) {
-                const Unit un = unit_at(p, u);
+                const Unit un = unit_at<T>(p, u);
                 const TcJob &J = un.job ? p.job[1] : p.job[0];
                 const CUtensorMap *wmap = un.job ? &wmap1 : &wmap0;
-                const uint32_t chunks = J.cols / T::chunk_cols;
+                const uint32_t kc_end = un.kc1 ? un.kc1 : J.cols / T::chunk_cols;
                 const int32_t y = (int32_t)(un.expert * (J.rows / 16) + un.m_block * 8);
-                for (uint32_t kc = 0; kc < chunks; ++kc) {
+                for (uint32_t kc = un.kc0; kc < kc_end; ++kc) {
                     if (!mbar_wait(&w_empty[r.slot], r.phase ^ 1u, p.error)) {
                         ok = false;
                         break;
@@ -357,11 +367,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t issued = 0;
             bool ok = true;
             for (uint32_t u = first; u < n_units && ok; u += stride) {
-                const Unit un = unit_at(p, u);
+                const Unit un = unit_at<T>(p, u);
                 const TcJob &J = un.job ? p.job[1] : p.job[0];
                 const CUtensorMap *map = un.job ? &map1 : &map0;
-                const uint32_t chunks = J.cols / T::chunk_cols;
-                for (uint32_t kc = 0; kc < chunks; ++kc) {
+                const uint32_t kc_end = un.kc1 ? un.kc1 : J.cols / T::chunk_cols;
+                for (uint32_t kc = un.kc0; kc < kc_end; ++kc) {
                     if (!mbar_wait(&b_empty[r.slot], r.phase ^ 1u, p.error)) {
                         ok = false;
                         break;
@@ -389,14 +399,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             Ring a, b, d;
             bool ok = true;
             for (uint32_t u = first; u < n_units && ok; u += stride) {
-                const Unit un = unit_at(p, u);
+                const Unit un = unit_at<T>(p, u);
                 const TcJob &J = un.job ? p.job[1] : p.job[0];
-                const uint32_t chunks = J.cols / T::chunk_cols;
+                const uint32_t kc_end = un.kc1 ? un.kc1 : J.cols / T::chunk_cols;
                 const uint32_t idesc = instr_desc_f16((un.count + 15u) & ~15u);
                 if (!mbar_wait(&d_empty[d.slot], d.phase ^ 1u, p.error)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + d.slot * kTcMaxN;
-                for (uint32_t kc = 0; kc < chunks; ++kc) {
+                for (uint32_t kc = un.kc0; kc < kc_end; ++kc) {
                     if (!mbar_wait(&a_ready[a.slot], a.phase, p.error) ||
                         !mbar_wait(&b_full[b.slot], b.phase, p.error)) {
                         ok = false;
@@ -411,13 +421,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         for (uint32_t k = 0; k < T::k_sub * kChunkK / 16; ++k)
                             mma_f16_tmem_a(d_tmem, a_tmem + k * 8,
                                            smem_desc_sw128(b_addr + (k >> 2) * kBSubTileBytes + (k & 3u) * 32), idesc,
-                                           (kc | k) != 0);
+                                           (kc != un.kc0 || k != 0) ? 1u : 0u);
                     } else {
                         const uint32_t a_addr = smem_u32(a_tiles + a.slot * kATileBytes);
 #pragma unroll
                         for (uint32_t k = 0; k < kChunkK / 16; ++k)
                             mma_f16(d_tmem, smem_desc_sw128(a_addr + k * 32), smem_desc_sw128(b_addr + k * 32),
-                                    idesc, (kc | k) != 0);
+                                    idesc, (kc != un.kc0 || k != 0) ? 1u : 0u);
                     }
                     mma_commit(&a_empty[a.slot]);
                     mma_commit(&b_empty[b.slot]);
@@ -470,7 +480,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const __half2 g2 = __float2half2_rn(__half2float(__ushort_as_half((uint16_t)bits)) * gscale);
                 return *reinterpret_cast<const uint32_t *>(&g2);
             };
-            Unit next = first < n_units ? unit_at(p, first) : Unit{};
+            Unit next = first < n_units ? unit_at<T>(p, first) : Unit{};
             uint32_t next_first = 0;
             int8_t next_ka = 0;
             if (first < n_units) {
@@ -486,7 +496,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 uint32_t gblock = scaled(next_first, gscale);
                 uint32_t gnext = fetch_gammas(un, J, 4);
                 if (u + stride < n_units) {
-                    next = unit_at(p, u + stride);
+                    next = unit_at<T>(p, u + stride);
                     const TcJob &Jn = next.job ? p.job[1] : p.job[0];
                     next_first = fetch_gammas(next, Jn, 0);
                     next_ka = Jn.ka[next.expert];
@@ -549,10 +559,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t r = lane & 15u, hf = lane >> 4;
             const uint32_t src = 2 * r + hf, src1 = (src + 1) & 31u;
             for (uint32_t u = first; u < n_units; u += stride) {
-                const Unit un = unit_at(p, u);
+                const Unit un = unit_at<T>(p, u);
                 const TcJob &J = un.job ? p.job[1] : p.job[0];
-                const uint32_t chunks = J.cols / T::chunk_cols;
-                for (uint32_t kc = 0; kc < chunks; ++kc) {
+                const uint32_t kc_end = un.kc1 ? un.kc1 : J.cols / T::chunk_cols;
+                for (uint32_t kc = un.kc0; kc < kc_end; ++kc) {
                     if (ok) ok = mbar_wait(&w_full[w.slot], w.phase, p.error);
                     if (ok) ok = mbar_wait(&a_empty[a.slot], a.phase ^ 1u, p.error);
                     if (ok) {
@@ -593,7 +603,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         Ring d;
         bool ok = true;
         for (uint32_t u = first; u < n_units; u += stride) {
-            const Unit un = unit_at(p, u);
+            const Unit un = unit_at<T>(p, u);
             const TcJob &J = un.job ? p.job[1] : p.job[0];
             if (ok) ok = mbar_wait(&d_full[d.slot], d.phase, p.error);
             ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-wide
@@ -602,7 +612,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const uint32_t n_pad = (un.count + 15u) & ~15u;
                 const float base_scale =
                     C == TcCodec::kExpert ? exp2f((float)-J.ka[un.expert]) : J.out_scale;
-                float *out = J.acc + half * J.half_stride + un.m_block * 128 + row_local;
+                float *out = J.acc + (half + un.kpart) * J.half_stride + un.m_block * 128 + row_local;
                 for (uint32_t c0 = 0; c0 < n_pad; c0 += 16) {
                     // Lane i < 16 computes column c0 + i's unscale once.
                     const uint32_t ni = c0 + (lane & 15u);
@@ -815,6 +825,7 @@ bool make_word_map(CUtensorMap *map, const TcJob &J) {
 
 template <TcCodec C>
 bool launch_codec(const CUtensorMap &map0, const CUtensorMap &map1, const TcParams &p, int grid, cudaStream_t s) {
+    if (C == TcCodec::kExpert && p.dense_ksplit > 1) return false;  // K parts are an NE-only option
     static bool configured = false;
     if (!configured) {
         cudaFuncSetAttribute(tc_gemm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Smem<C>::total);

@@ -37,6 +37,7 @@ struct TcParams {
     const uint32_t *unit_count;
     uint32_t dense_positions;
     uint32_t dense_jobs;
+    uint32_t dense_ksplit;  // NE, dense units: K in this many parts (0 or 1: whole), part p's sums at acc + p * half_stride
     const void *table;   // expert: uint2 [2][16384] value halves; NE: f16x2 [1024]
     uint32_t *error;     // device error word
 };

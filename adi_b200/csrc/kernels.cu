@@ -1375,9 +1375,111 @@ __global__ void __launch_bounds__(1024) route_small_kernel(RouteParams p) {
     }
 }
 
+// Mid-size batches (up to 8192 routes) in one block as well: counts and the
+// per-expert token bitmaps in shared memory (atomics there), the same scans,
+// work lists and bitmap-prefix ranks as the three-kernel path, so the same
+// outputs, without the two memsets, three launches and global atomics.
+constexpr uint32_t kBlockRoutes = 8192;
+constexpr size_t kRouteBlockSmemLimit = 160 * 1024;
+
+__global__ void __launch_bounds__(1024) route_block_kernel(RouteParams p) {
+    extern __shared__ uint32_t route_smem[];
+    uint32_t *bitmap = route_smem;                       // [E][words]
+    uint32_t *prefix = bitmap + p.experts * p.words;     // [E][words]
+    uint32_t *counts = prefix + p.experts * p.words;     // [1024]
+    uint32_t *scan = counts + 1024, *chunk_scan = scan + 1024;
+    const uint32_t t = threadIdx.x, n = p.tokens * 8, bw = p.experts * p.words;
+    for (uint32_t i = t; i < bw; i += 1024) bitmap[i] = 0;
+    counts[t] = 0;
+    __syncthreads();
+    for (uint32_t i = t; i < n; i += 1024) {
+        const uint32_t e = p.route_experts[i];
+        if (e >= p.experts) continue;
+        const uint32_t tok = i >> 3;
+        atomicAdd(&counts[e], 1u);
+        atomicOr(&bitmap[e * p.words + (tok >> 5)], 1u << (tok & 31u));
+    }
+    __syncthreads();
+    const uint32_t e = t;
+    const uint32_t count = e < p.experts ? counts[e] : 0u;
+    const uint32_t chunks = (count + p.chunk - 1) / p.chunk;
+    scan[e] = count;
+    chunk_scan[e] = chunks;
+    __syncthreads();
+    for (uint32_t o = 1; o < 1024; o <<= 1) {
+        const uint32_t a = e >= o ? scan[e - o] : 0u;
+        const uint32_t b = e >= o ? chunk_scan[e - o] : 0u;
+        __syncthreads();
+        scan[e] += a;
+        chunk_scan[e] += b;
+        __syncthreads();
+    }
+    const uint32_t offset = scan[e] - count;
+    const uint32_t chunk_offset = chunk_scan[e] - chunks;
+    if (e < p.experts) {
+        p.counts[e] = count;
+        p.offsets[e] = offset;
+        for (uint32_t i = 0; i < count; ++i) p.pos_expert[offset + i] = e;
+        for (uint32_t c = 0; c < chunks; ++c) {
+            const uint32_t pos0 = offset + c * p.chunk;
+            const uint32_t m = min(p.chunk, count - c * p.chunk);
+            for (uint32_t j = 0; j < 2; ++j)
+                for (uint32_t rb = 0; rb < p.row_blocks_gate_up; ++rb)
+                    p.items_gate_up[((chunk_offset + c) * 2 + j) * p.row_blocks_gate_up + rb] =
+                        make_uint4(e, (j << 16) | rb, pos0, m);
+            for (uint32_t rb = 0; rb < p.row_blocks_down; ++rb)
+                p.items_down[(chunk_offset + c) * p.row_blocks_down + rb] = make_uint4(e, rb, pos0, m);
+        }
+    }
+    if (e == p.experts - 1) {
+        p.offsets[p.experts] = offset + count;
+        const uint32_t total_chunks = chunk_offset + chunks;
+        *p.count_gate_up = total_chunks * 2 * p.row_blocks_gate_up;
+        *p.count_down = total_chunks * p.row_blocks_down;
+    }
+    // Per-expert exclusive prefix of bitmap popcounts, one warp per expert.
+    const uint32_t warp = t >> 5, lane = t & 31u;
+    for (uint32_t ex = warp; ex < p.experts; ex += 32) {
+        uint32_t running = 0;
+        for (uint32_t w0 = 0; w0 < p.words; w0 += 32) {
+            const uint32_t w = w0 + lane;
+            const uint32_t c = w < p.words ? __popc(bitmap[ex * p.words + w]) : 0u;
+            uint32_t incl = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= (uint32_t)o) incl += v;
+            }
+            if (w < p.words) prefix[ex * p.words + w] = running + incl - c;
+            running += __shfl_sync(0xffffffffu, incl, 31);
+        }
+    }
+    __syncthreads();
+    for (uint32_t i = t; i < n; i += 1024) {
+        const uint32_t ex = p.route_experts[i];
+        if (ex >= p.experts) continue;
+        const uint32_t tok = i >> 3;
+        const uint32_t w = ex * p.words + (tok >> 5);
+        const uint32_t pos = scan[ex] - counts[ex] + prefix[w] + __popc(bitmap[w] & ((1u << (tok & 31u)) - 1u));
+        p.grouped[pos] = tok;
+        p.route_to_grouped[i] = pos;
+    }
+}
+
 uint32_t launch_route(const RouteParams &p, cudaStream_t s) {
     if (p.tokens * 8 <= kSmallRoutes && p.experts <= 1024) {
         route_small_kernel<<<1, 1024, 0, s>>>(p);
+        return 1;
+    }
+    const size_t block_smem = (2 * size_t(p.experts) * p.words + 3 * 1024) * sizeof(uint32_t);
+    if (p.tokens * 8 <= kBlockRoutes && p.experts <= 1024 && block_smem <= kRouteBlockSmemLimit) {
+        static bool configured = false;
+        if (!configured) {
+            cudaFuncSetAttribute(route_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kRouteBlockSmemLimit);
+            configured = true;
+        }
+        route_block_kernel<<<1, 1024, block_smem, s>>>(p);
         return 1;
     }
     cudaMemsetAsync(p.counts, 0, sizeof(uint32_t) * p.experts, s);
@@ -1524,15 +1626,24 @@ __global__ void __launch_bounds__(256) combine_regs_kernel(CombineParams p) {
     float out[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) out[r] = 0.0f;
+    // Route k + 1's two half rows load while route k is transformed.
+    float n0[R], n1[R];
+    {
+        const uint32_t pos = p.route_to_grouped[t * 8];
+        load_regs<R>(p.acc_down + (size_t)pos * H + c0, n0);
+        load_regs<R>(p.acc_down + p.half_stride + (size_t)pos * H + c0, n1);
+    }
     for (int k = 0; k < 8; ++k) {
-        const uint32_t pos = p.route_to_grouped[t * 8 + k];
         const uint32_t e = p.route_experts[t * 8 + k];
         const float w = p.route_weights[t * 8 + k];
-        float v[R], v1[R];
-        load_regs<R>(p.acc_down + (size_t)pos * H + c0, v);
-        load_regs<R>(p.acc_down + p.half_stride + (size_t)pos * H + c0, v1);
+        float v[R];
 #pragma unroll
-        for (int r = 0; r < R; ++r) v[r] += v1[r];
+        for (int r = 0; r < R; ++r) v[r] = n0[r] + n1[r];
+        if (k < 7) {
+            const uint32_t pos = p.route_to_grouped[t * 8 + k + 1];
+            load_regs<R>(p.acc_down + (size_t)pos * H + c0, n0);
+            load_regs<R>(p.acc_down + p.half_stride + (size_t)pos * H + c0, n1);
+        }
         fwht_regs<R>(v, sh);
         const uint16_t *sv = p.sv_down + (size_t)e * H + c0;
 #pragma unroll

@@ -207,4 +207,52 @@ __device__ __forceinline__ void fwht_regs(float (&v)[R], float *sh) {
     __syncthreads();
 }
 
+// FWHT of 2048 values by a 256-thread block that ends transposed: the input
+// is thread t's x[t*8 .. t*8+7] (as fwht_regs<8>), the output v[k] is the
+// transform at element k*256 + t. Strides 1-4 run in registers, 8-128 by
+// warp shuffles, then one pass through `sh` (2048 + 64 floats, padded so
+// that neither side has bank conflicts) hands each thread one element of
+// every 256-block, and strides 256-1024 run in registers: the same butterfly
+// network in the same stride order as fwht_regs, so bit-identical to it,
+// with one shared-memory round trip instead of three. Contains
+// __syncthreads().
+__device__ __forceinline__ uint32_t fwht_pad(uint32_t i) { return i + (i >> 5); }
+
+__device__ __forceinline__ void fwht8_transposed(float (&v)[8], float *sh) {
+#pragma unroll
+    for (int s = 1; s < 8; s <<= 1)
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+            if ((r & s) == 0) {
+                const float a = v[r], b = v[r + s];
+                v[r] = __fadd_rn(a, b);
+                v[r + s] = __fsub_rn(a, b);
+            }
+    const uint32_t lane = threadIdx.x & 31u;
+#pragma unroll
+    for (int s = 0; s < 5; ++s) {
+        const bool upper = (lane >> s) & 1u;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[r], 1u << s);
+            v[r] = upper ? __fsub_rn(o, v[r]) : __fadd_rn(v[r], o);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) sh[fwht_pad(threadIdx.x * 8 + r)] = v[r];
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = sh[fwht_pad(k * 256 + threadIdx.x)];
+#pragma unroll
+    for (int s = 1; s < 8; s <<= 1)
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if ((k & s) == 0) {
+                const float a = v[k], b = v[k + s];
+                v[k] = __fadd_rn(a, b);
+                v[k + s] = __fsub_rn(a, b);
+            }
+    __syncthreads();
+}
+
 }  // namespace adi_cuda

@@ -1660,12 +1660,57 @@ __global__ void __launch_bounds__(256) combine_regs_kernel(CombineParams p) {
     store_regs<R>(p.out + (size_t)t * H + c0, out);
 }
 
+// The fused combine at hidden 2048 with the transposed-output FWHT: element
+// k*256 + t of every route's row after the transform, the same products and
+// the same route-order sums per element as combine_regs_kernel<8>, and
+// stores of 128 contiguous bytes per warp.
+__global__ void __launch_bounds__(256) combine_2048_kernel(CombineParams p) {
+    __shared__ float sh[2048 + 64];
+    constexpr uint32_t H = 2048;
+    const uint32_t t = blockIdx.x, c0 = threadIdx.x * 8;
+    float out[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) out[k] = 0.0f;
+    float n0[8], n1[8];
+    {
+        const uint32_t pos = p.route_to_grouped[t * 8];
+        load_regs<8>(p.acc_down + (size_t)pos * H + c0, n0);
+        load_regs<8>(p.acc_down + p.half_stride + (size_t)pos * H + c0, n1);
+    }
+    for (int r = 0; r < 8; ++r) {
+        const uint32_t e = p.route_experts[t * 8 + r];
+        const float w = p.route_weights[t * 8 + r];
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = n0[k] + n1[k];
+        if (r < 7) {
+            const uint32_t pos = p.route_to_grouped[t * 8 + r + 1];
+            load_regs<8>(p.acc_down + (size_t)pos * H + c0, n0);
+            load_regs<8>(p.acc_down + p.half_stride + (size_t)pos * H + c0, n1);
+        }
+        fwht8_transposed(v, sh);
+        const uint16_t *sv = p.sv_down + (size_t)e * H + threadIdx.x;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            out[k] = fmaf(w, __fmul_rn(__fmul_rn(v[k], p.scale), f16_bits_to_f32(sv[k * 256])), out[k]);
+    }
+    float v[8];
+    load_regs<8>(p.shared_acc + (size_t)t * H + c0, v);
+    fwht8_transposed(v, sh);
+    const float gate = sigmoid_f(p.gate_logits[(size_t)t * p.gate_stride]);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+        out[k] = fmaf(gate, __fmul_rn(__fmul_rn(v[k], p.scale), (float)p.shared_sv[k * 256 + threadIdx.x]), out[k]);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) p.out[(size_t)t * H + k * 256 + threadIdx.x] = out[k];
+}
+
 void launch_combine(const CombineParams &p, cudaStream_t s) {
     if (p.tokens == 0) return;
     switch (p.hidden) {
         case 512: combine_regs_kernel<2><<<p.tokens, 256, 0, s>>>(p); return;
         case 1024: combine_regs_kernel<4><<<p.tokens, 256, 0, s>>>(p); return;
-        case 2048: combine_regs_kernel<8><<<p.tokens, 256, 0, s>>>(p); return;
+        case 2048: combine_2048_kernel<<<p.tokens, 256, 0, s>>>(p); return;
         default: {
             const uint32_t threads = (p.hidden + 7) / 8;  // kPer elements per thread
             combine_kernel<<<p.tokens, threads < 32 ? 32 : threads, p.hidden * sizeof(float), s>>>(p);
@@ -1869,11 +1914,23 @@ __global__ void __launch_bounds__(256) hadamard_regs_kernel(float *values, float
     store_regs<R>(row, v);
 }
 
+// 2048 points with the transposed-output FWHT: thread t stores elements
+// k*256 + t, so every store of the warp is one contiguous 128 B.
+__global__ void __launch_bounds__(256) hadamard_2048_kernel(float *values, float scale) {
+    __shared__ float sh[2048 + 64];
+    float *row = values + (size_t)blockIdx.x * 2048u;
+    float v[8];
+    load_regs<8>(row + threadIdx.x * 8, v);
+    fwht8_transposed(v, sh);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) row[k * 256 + threadIdx.x] = __fmul_rn(v[k], scale);
+}
+
 void launch_hadamard(float *values, uint32_t count, uint32_t n, float scale, cudaStream_t s) {
     if (count == 0) return;
     switch (n) {
         case 512: hadamard_regs_kernel<2><<<count, 256, 0, s>>>(values, scale); return;
-        case 2048: hadamard_regs_kernel<8><<<count, 256, 0, s>>>(values, scale); return;
+        case 2048: hadamard_2048_kernel<<<count, 256, 0, s>>>(values, scale); return;
         default: hadamard_kernel<<<count, 256, n * sizeof(float), s>>>(values, n, scale);
     }
 }

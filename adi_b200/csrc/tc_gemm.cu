@@ -1044,6 +1044,43 @@ __global__ void __launch_bounds__(256) prep_f16_regs_kernel(PrepF16Params p) {
     }
 }
 
+// The prep at 2048 columns with the transposed-output FWHT: thread t ends
+// with elements k*256 + t, so the same values as prep_f16_regs_kernel<8>
+// reach the same f16 columns, written one half per element (each warp's
+// 32 elements are two runs of 16 contiguous halves in the split layout).
+__global__ void __launch_bounds__(256) prep_f16_2048_kernel(PrepF16Params p) {
+    __shared__ float sh[2048 + 64];
+    __shared__ float scratch[32];
+    constexpr uint32_t n = 2048;
+    const uint32_t row = blockIdx.x;
+    const uint32_t token = p.grouped ? p.grouped[row] : row;
+    const uint32_t expert = p.pos_expert ? p.pos_expert[row] : 0u;
+    float x[8];
+    load_regs<8>(p.input + (size_t)token * n + threadIdx.x * 8, x);
+    const size_t su0 = (size_t)expert * p.su_stride + threadIdx.x * 8;
+    const size_t half_stride = (size_t)p.rows * (n / 2);
+    for (int job = 0; job < p.jobs; ++job) {
+        const void *su = job ? p.su[1] : p.su[0];
+        float v[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) v[r] = __fmul_rn(x[r], scale_value(su, p.su_is_f16, su0 + r));
+        fwht8_transposed(v, sh);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(v[k], p.scale);
+        const int k = scale_exponent(block_max_abs_regs<8>(v, scratch));
+        if (threadIdx.x == 0) (job ? p.kx[1] : p.kx[0])[row] = (int8_t)k;
+        const float s = exp2f((float)k);
+        __half *out = job ? p.xh[1] : p.xh[0];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t i = j * 256u + threadIdx.x;
+            __half *dst = p.split ? out + ((i >> 2) & 1u) * half_stride + (size_t)row * (n / 2) + 4 * (i >> 3) + (i & 3u)
+                                  : out + (size_t)row * n + i;
+            *dst = __float2half_rn(v[j] * s);
+        }
+    }
+}
+
 template <int R>
 __global__ void __launch_bounds__(256) mid_f16_regs_kernel(MidF16Params p) {
     __shared__ float sh[256 * R];
@@ -1086,7 +1123,7 @@ void launch_prep_f16(const PrepF16Params &p, cudaStream_t s) {
     switch (p.cols) {
         case 512: prep_f16_regs_kernel<2><<<p.rows, 256, 0, s>>>(p); return;
         case 1024: prep_f16_regs_kernel<4><<<p.rows, 256, 0, s>>>(p); return;
-        case 2048: prep_f16_regs_kernel<8><<<p.rows, 256, 0, s>>>(p); return;
+        case 2048: prep_f16_2048_kernel<<<p.rows, 256, 0, s>>>(p); return;
         default: prep_f16_kernel<<<grid, 256, p.cols * sizeof(float), s>>>(p);
     }
 }

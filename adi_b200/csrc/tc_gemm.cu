@@ -1115,6 +1115,110 @@ __global__ void __launch_bounds__(256) mid_f16_regs_kernel(MidF16Params p) {
     write_f16_regs<R>(g, k, p.split != 0, p.xh, (size_t)p.positions * (p.inner / 2), pos);
 }
 
+// FWHT of 512 values held by one warp, lane l holding x[16l .. 16l+15]:
+// strides 1-8 in registers, 16-256 by shuffles. The same butterflies in the
+// same ascending stride order as fwht_regs<2>, so bit-identical to it, with
+// no shared memory and no block barrier.
+__device__ __forceinline__ void fwht_warp16(float (&v)[16]) {
+#pragma unroll
+    for (int s = 1; s < 16; s <<= 1)
+#pragma unroll
+        for (int r = 0; r < 16; ++r)
+            if ((r & s) == 0) {
+                const float a = v[r], b = v[r + s];
+                v[r] = __fadd_rn(a, b);
+                v[r + s] = __fsub_rn(a, b);
+            }
+    const uint32_t lane = threadIdx.x & 31u;
+#pragma unroll
+    for (int s = 0; s < 5; ++s) {
+        const bool upper = (lane >> s) & 1u;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[r], 1u << s);
+            v[r] = upper ? __fsub_rn(o, v[r]) : __fadd_rn(v[r], o);
+        }
+    }
+}
+
+__device__ __forceinline__ uint4 pack_half8(const float *v, float s) {
+    uint4 q;
+    uint32_t *w = reinterpret_cast<uint32_t *>(&q);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const __half2 h = __floats2half2_rn(v[2 * j] * s, v[2 * j + 1] * s);
+        w[j] = *reinterpret_cast<const uint32_t *>(&h);
+    }
+    return q;
+}
+
+// The SwiGLU middle at inner 512, one warp per position (eight per block):
+// the same arithmetic per element as mid_f16_regs_kernel<2>, with the three
+// transforms and the row's max-abs inside the warp. Lane l's elements
+// 16l .. 16l+15 land in the split layout as two runs of eight halves (one
+// 16-byte store each).
+__global__ void __launch_bounds__(256) mid_f16_warp_kernel(MidF16Params p) {
+    constexpr uint32_t n = 512;
+    const uint32_t pos = blockIdx.x * 8u + (threadIdx.x >> 5), lane = threadIdx.x & 31u;
+    if (pos >= p.positions) return;  // whole warps leave together
+    const uint32_t e = p.pos_expert ? p.pos_expert[pos] : 0u;
+    const size_t base = (size_t)pos * n + lane * 16u;
+    float g[16], u[16];
+    load_regs<16>(p.acc_gate + base, g);
+    load_regs<16>(p.acc_up + base, u);
+    if (p.halves == 2) {
+        float g1[16], u1[16];
+        load_regs<16>(p.acc_gate + p.half_stride + base, g1);
+        load_regs<16>(p.acc_up + p.half_stride + base, u1);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            g[r] += g1[r];
+            u[r] += u1[r];
+        }
+    }
+    fwht_warp16(g);
+    fwht_warp16(u);
+    const size_t s0 = (p.is_f16 ? (size_t)e * n : 0) + lane * 16u;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+        const float gv = __fmul_rn(__fmul_rn(g[r], p.scale), scale_value(p.sv_gate, p.is_f16, s0 + r));
+        const float uv = __fmul_rn(__fmul_rn(u[r], p.scale), scale_value(p.sv_up, p.is_f16, s0 + r));
+        g[r] = __fmul_rn(__fmul_rn(silu_f(gv), uv), scale_value(p.su_down, p.is_f16, s0 + r));
+    }
+    fwht_warp16(g);
+    float m = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+        g[r] = __fmul_rn(g[r], p.scale);
+        m = fmaxf(m, fabsf(g[r]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const int k = scale_exponent(m);
+    if (lane == 0) p.kx[pos] = (int8_t)k;
+    const float sc = exp2f((float)k);
+    if (p.split) {
+        // elements 16l + r: r 0-3 and 8-11 -> half 0, r 4-7 and 12-15 -> half 1,
+        // packed columns 8l .. 8l+7 of each half
+        const size_t half_stride = (size_t)p.positions * (n / 2);
+        float h0[8], h1[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            h0[j] = g[j];
+            h0[4 + j] = g[8 + j];
+            h1[j] = g[4 + j];
+            h1[4 + j] = g[12 + j];
+        }
+        __half *row = p.xh + (size_t)pos * (n / 2) + lane * 8u;
+        *reinterpret_cast<uint4 *>(row) = pack_half8(h0, sc);
+        *reinterpret_cast<uint4 *>(row + half_stride) = pack_half8(h1, sc);
+    } else {
+        __half *row = p.xh + (size_t)pos * n + lane * 16u;
+        *reinterpret_cast<uint4 *>(row) = pack_half8(g, sc);
+        *reinterpret_cast<uint4 *>(row + 8) = pack_half8(g + 8, sc);
+    }
+}
+
 }  // namespace
 
 void launch_prep_f16(const PrepF16Params &p, cudaStream_t s) {
@@ -1131,7 +1235,7 @@ void launch_prep_f16(const PrepF16Params &p, cudaStream_t s) {
 void launch_mid_f16(const MidF16Params &p, cudaStream_t s) {
     if (p.positions == 0) return;
     switch (p.inner) {
-        case 512: mid_f16_regs_kernel<2><<<p.positions, 256, 0, s>>>(p); return;
+        case 512: mid_f16_warp_kernel<<<(p.positions + 7) / 8, 256, 0, s>>>(p); return;
         case 1024: mid_f16_regs_kernel<4><<<p.positions, 256, 0, s>>>(p); return;
         case 2048: mid_f16_regs_kernel<8><<<p.positions, 256, 0, s>>>(p); return;
         default: mid_f16_kernel<<<p.positions, 256, 2 * p.inner * sizeof(float), s>>>(p);

@@ -87,9 +87,15 @@ struct Traits<TcCodec::kExpert> {
     static constexpr uint32_t k_sub = 2;
     static constexpr uint32_t tile_bytes = 48;
     static constexpr uint32_t tiles_per_row = 16;        // per chunk
-    static constexpr uint32_t words_bytes = 8 * tiles_per_row * tile_bytes;  // 8 tile rows
-    static constexpr uint32_t box_u32 = tiles_per_row * tile_bytes / 4;     // a chunk's tile row, in u32
-    static constexpr uint32_t row_stride = tiles_per_row * tile_bytes;      // the TMA box lands rows densely
+    static constexpr uint32_t chunk_u32 = tiles_per_row * tile_bytes / 4;   // a chunk's tile row, in u32
+    // The box is 16 u32 wider than a chunk's tile row (the next chunk's first
+    // words, or zero fill past the row's end): the box lands its rows 832 B
+    // apart, so the two tile rows a decode warp reads sit 16 banks apart and
+    // the warp's word loads are conflict-free (768 B would put both rows on
+    // the same banks).
+    static constexpr uint32_t box_u32 = chunk_u32 + 16;
+    static constexpr uint32_t row_stride = box_u32 * 4;
+    static constexpr uint32_t words_bytes = 8 * row_stride;  // 8 tile rows
     static constexpr uint32_t word_slot = 8192;
     static constexpr uint32_t a_stages = kTmemAStages;
     static constexpr uint32_t a_tile_bytes = 0;          // A lives in tensor memory
@@ -103,9 +109,10 @@ struct Traits<TcCodec::kNe> {
     static constexpr uint32_t k_sub = 1;
     static constexpr uint32_t tile_bytes = 128;
     static constexpr uint32_t tiles_per_row = 4;
-    static constexpr uint32_t words_bytes = 8 * tiles_per_row * tile_bytes;
-    static constexpr uint32_t box_u32 = tiles_per_row * tile_bytes / 4;
-    static constexpr uint32_t row_stride = tiles_per_row * tile_bytes;
+    static constexpr uint32_t chunk_u32 = tiles_per_row * tile_bytes / 4;
+    static constexpr uint32_t box_u32 = chunk_u32;
+    static constexpr uint32_t row_stride = box_u32 * 4;
+    static constexpr uint32_t words_bytes = 8 * row_stride;
     static constexpr uint32_t word_slot = 4096;
     static constexpr uint32_t a_stages = kAStages;
     static constexpr uint32_t a_tile_bytes = kATileBytes;
@@ -348,7 +355,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(&w_full[r.slot], T::words_bytes);
-                    tma_load_2d(word_tiles + r.slot * T::word_slot, wmap, (int32_t)(kc * T::box_u32), y,
+                    tma_load_2d(word_tiles + r.slot * T::word_slot, wmap, (int32_t)(kc * T::chunk_u32), y,
                                 &w_full[r.slot]);
                     ++issued;
                     r.advance(kWordStages);

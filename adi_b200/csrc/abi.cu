@@ -266,6 +266,11 @@ struct adi_cuda_context {
     int sms = 148;
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
+    // A second stream for work that runs beside the main chain (the MoE
+    // block's shared expert), forked from and joined back into `stream`
+    // by the two events.
+    cudaStream_t side_stream = nullptr;
+    cudaEvent_t fork_event = nullptr, join_event = nullptr;
     int precision = 0;
     uint64_t launches = 0;
     std::mutex lock;
@@ -789,6 +794,26 @@ void shared_expert_tc(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t 
     c->after_launch(4);
 }
 
+void shared_expert(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *sacc_d);
+
+// The shared expert on the side stream: forked from the main stream at this
+// point (so it sees the input the main stream has produced) and joined by
+// the event the caller waits on before reading sacc_d.
+void shared_expert_beside(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *sacc_d) {
+    cudaStream_t main = c->stream;
+    check(cudaEventRecord(c->fork_event, main), "cudaEventRecord");
+    check(cudaStreamWaitEvent(c->side_stream, c->fork_event, 0), "cudaStreamWaitEvent");
+    c->stream = c->side_stream;
+    try {
+        shared_expert(c, L, in, T, sacc_d);
+    } catch (...) {
+        c->stream = main;
+        throw;
+    }
+    c->stream = main;
+    check(cudaEventRecord(c->join_event, c->side_stream), "cudaEventRecord");
+}
+
 // Router and shared-gate logits [T][E+1]: on tensor cores in precision mode
 // 1 (exact three-term bf16 split of the activations, fp32 accumulation),
 // else the CUDA-core fp32 kernel. Returns the kernels launched.
@@ -1048,6 +1073,13 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     const size_t P = size_t(T) * 8;
     cudaStream_t s = c->stream;
 
+    // The shared expert depends only on the input: it runs on the side stream
+    // beside the router, routing and routed experts (whose first kernels
+    // leave most SMs idle), and the combine waits for it. Its buffers
+    // (moe_s*) are its own, so the two chains touch no common scratch.
+    float *sacc_d = c->buffer<float>("moe_sacc_d", size_t(T) * H);
+    shared_expert_beside(c, L, in, T, sacc_d);
+
     float *logits = c->buffer<float>("moe_logits", size_t(T) * (E + 1));
     uint32_t *re = route_experts_out ? route_experts_out : c->buffer<uint32_t>("moe_re", P);
     float *rw = route_weights_out ? route_weights_out : c->buffer<float>("moe_rw", P);
@@ -1089,10 +1121,7 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     c->stage_end();
 
     float *acc_d = routed_experts(c, L, in, P, rp, nt, tc);
-
-    // Shared NE expert over all T tokens.
-    float *sacc_d = c->buffer<float>("moe_sacc_d", size_t(T) * H);
-    shared_expert(c, L, in, T, sacc_d);
+    check(cudaStreamWaitEvent(s, c->join_event, 0), "cudaStreamWaitEvent");
 
     if (T <= kSplitCombineTokens) {
         // Small batches: one block per route applies the down projection's
@@ -1402,6 +1431,9 @@ int adi_cuda_init(int device, adi_cuda_context **out) {
         check(cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device), "SM count");
         check(cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking), "cudaStreamCreate");
         c->stream = c->own_stream;
+        check(cudaStreamCreateWithFlags(&c->side_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+        check(cudaEventCreateWithFlags(&c->fork_event, cudaEventDisableTiming), "cudaEventCreate");
+        check(cudaEventCreateWithFlags(&c->join_event, cudaEventDisableTiming), "cudaEventCreate");
         check(cudaMalloc(&c->error_word, sizeof(uint32_t)), "cudaMalloc");
         check(cudaMemset(c->error_word, 0, sizeof(uint32_t)), "cudaMemset");
         *out = c.release();
@@ -1413,11 +1445,16 @@ int adi_cuda_shutdown(adi_cuda_context *c) {
         if (!c) return;
         use_device(c);
         cudaStreamSynchronize(c->stream);
-        cudaStream_t own = c->own_stream;
+        if (c->side_stream) cudaStreamSynchronize(c->side_stream);
+        cudaStream_t own = c->own_stream, side = c->side_stream;
+        cudaEvent_t fork = c->fork_event, join = c->join_event;
         uint32_t *error_word = c->error_word;
         delete c;
         if (error_word) cudaFree(error_word);
         if (own) cudaStreamDestroy(own);
+        if (side) cudaStreamDestroy(side);
+        if (fork) cudaEventDestroy(fork);
+        if (join) cudaEventDestroy(join);
     });
 }
 

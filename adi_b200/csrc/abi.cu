@@ -814,11 +814,15 @@ void shared_expert_beside(adi_cuda_context *c, MoeDev &L, const float *in, uint3
     check(cudaEventRecord(c->join_event, c->side_stream), "cudaEventRecord");
 }
 
-// Router and shared-gate logits [T][E+1]: on tensor cores in precision mode
-// 1 (exact three-term bf16 split of the activations, fp32 accumulation),
-// else the CUDA-core fp32 kernel. Returns the kernels launched.
-uint32_t router_logits(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *logits) {
+// Router and shared-gate logits [T][E+1] and the top-8 routes: on tensor
+// cores in precision mode 1 (exact three-term bf16 split of the
+// activations, fp32 accumulation, the split-K partials summed in order by
+// the top-k kernel as it reads them), else the CUDA-core fp32 kernel and the
+// top-k over its logits. Returns the kernels launched.
+uint32_t route_tokens(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *logits, uint32_t *re,
+                      float *rw) {
     const uint32_t H = L.hidden, E = L.experts;
+    c->stage(kStageRouter);
     if (c->precision == 1 && H % 64 == 0) {
         RouterParams rp{};
         rp.rows_pad = L.router_rows_pad;
@@ -828,13 +832,22 @@ uint32_t router_logits(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t
         rp.partials = c->buffer<float>("router_parts", size_t(rp.parts) * T * rp.rows_pad);
         rp.error = c->error_word;
         uint16_t *xs = c->buffer<uint16_t>("router_xs", size_t(T) * 3 * H);
-        if (!launch_router_tc(rp, in, xs, L.router3->as<uint16_t>(), logits, E + 1, E + 1, c->stream))
+        if (!launch_router_tc(rp, in, xs, L.router3->as<uint16_t>(), nullptr, E + 1, E + 1, c->stream))
             throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
+        c->stage_end();
+        c->stage(kStageTopk);
+        if (!launch_top_experts_parts(rp.partials, rp.parts, rp.rows_pad, logits, E + 1, T, E, re, rw, c->stream))
+            invalid("MoE routing requires between 8 and 1024 experts");
+        c->stage_end();
         return 3;
     }
     launch_bf16_gemm(L.router->as<uint16_t>(), E, L.router->as<uint16_t>() + size_t(E) * H, 1, in, T, H, logits,
                      E + 1, c->stream);
-    return 1;
+    c->stage_end();
+    c->stage(kStageTopk);
+    launch_top_experts(logits, E + 1, T, E, re, rw, c->stream);
+    c->stage_end();
+    return 2;
 }
 
 // The shared NE SwiGLU expert over T tokens: sacc_d = the down projection's
@@ -1083,12 +1096,7 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     float *logits = c->buffer<float>("moe_logits", size_t(T) * (E + 1));
     uint32_t *re = route_experts_out ? route_experts_out : c->buffer<uint32_t>("moe_re", P);
     float *rw = route_weights_out ? route_weights_out : c->buffer<float>("moe_rw", P);
-    c->stage(kStageRouter);
-    const uint32_t router_launches = router_logits(c, L, in, T, logits);
-    c->stage_end();
-    c->stage(kStageTopk);
-    launch_top_experts(logits, E + 1, T, E, re, rw, s);
-    c->stage_end();
+    const uint32_t router_launches = route_tokens(c, L, in, T, logits, re, rw);
 
     RouteParams rp{};
     rp.route_experts = re;
@@ -1153,7 +1161,7 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
         launch_ep_finalize(fp, s);
         launch_ep_combine(ecp, s);
         c->stage_end();
-        c->after_launch(router_launches + 1 + route_launches + 2);
+        c->after_launch(router_launches + route_launches + 2);
         return;
     }
     CombineParams cp{};
@@ -1176,7 +1184,7 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     c->stage_end();
     // router, top-k, the routing kernels, combine (the routed and shared
     // experts count their own four each)
-    c->after_launch(router_launches + 1 + route_launches + 1);
+    c->after_launch(router_launches + route_launches + 1);
 }
 
 // Host-pointer wrapper: stage inputs, run on device, read outputs back.
@@ -1281,20 +1289,24 @@ void ep_dispatch_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const floa
     const uint32_t H = L.hidden, E = L.experts;
     const size_t P = size_t(T) * 8;
     cudaStream_t s = c->stream;
+    // The shared expert of these tokens runs on the side stream through the
+    // exchanges and the expert phase; the combine joins it.
+    shared_expert_beside(c, L, in, T, c->buffer<float>("ep_sacc", size_t(T) * H));
     float *logits = c->buffer<float>("ep_logits", size_t(T) * (E + 1));
     uint32_t *re = c->buffer<uint32_t>("ep_re", P);
     float *rw = c->buffer<float>("ep_rw", P);
-    c->stage(kStageRouter);
     if (given_logits) {
+        c->stage(kStageRouter);
         check(cudaMemcpyAsync(logits, given_logits, size_t(T) * (E + 1) * 4, cudaMemcpyDeviceToDevice, s),
               "logits copy");
+        c->stage_end();
+        c->stage(kStageTopk);
+        launch_top_experts(logits, E + 1, T, E, re, rw, s);
+        c->stage_end();
+        c->after_launch(1);
     } else {
-        c->after_launch(router_logits(c, L, in, T, logits));
+        c->after_launch(route_tokens(c, L, in, T, logits, re, rw));
     }
-    c->stage_end();
-    c->stage(kStageTopk);
-    launch_top_experts(logits, E + 1, T, E, re, rw, s);
-    c->stage_end();
 
     // The counting sort only: no work lists (row_blocks 0), large chunks so
     // the scan's per-expert loop is short.
@@ -1318,9 +1330,8 @@ void ep_dispatch_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const floa
     const uint32_t route_launches = launch_route(rp, s);
     launch_ep_gather(in, rp.grouped, uint32_t(P), H, send, s);
     c->stage_end();
-    c->after_launch(1 + route_launches + 1);
+    c->after_launch(route_launches + 1);
 
-    shared_expert(c, L, in, T, c->buffer<float>("ep_sacc", size_t(T) * H));
     if (route_experts_out)
         check(cudaMemcpyAsync(route_experts_out, re, P * 4, cudaMemcpyDeviceToDevice, s), "route copy");
     if (route_weights_out)
@@ -1407,6 +1418,7 @@ void ep_combine_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const float
     cp.tokens = T;
     cp.scale = transform_scale(H);
     cp.out = out;
+    check(cudaStreamWaitEvent(c->stream, c->join_event, 0), "cudaStreamWaitEvent");
     c->stage(kStageCombine);
     launch_ep_combine(cp, c->stream);
     c->stage_end();

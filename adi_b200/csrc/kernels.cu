@@ -1130,18 +1130,50 @@ __global__ void top_experts_kernel(const float *logits, uint32_t stride, uint32_
 // lane + 32 i in slot i): one read of the row instead of eight, the rest
 // register compares and shuffles. Equal to top_experts_kernel for every
 // input, NaNs included.
+//
+// With `parts` > 0 the logits are first summed from the router's split-K
+// partials [parts][tokens][rows_pad] (q ascending from 0.0f, the order of
+// router_reduce_kernel) and the row -- experts plus the shared-expert gate
+// column -- written to `logits`, so one launch does the reduction and the
+// selection.
 template <int V>
-__global__ void top_experts_regs_kernel(const float *logits, uint32_t stride, uint32_t tokens, uint32_t experts,
-                                        uint32_t *route_experts, float *route_weights) {
+__global__ void top_experts_regs_kernel(float *logits, uint32_t stride, uint32_t tokens, uint32_t experts,
+                                        uint32_t *route_experts, float *route_weights, const float *partials,
+                                        uint32_t parts, uint32_t rows_pad) {
     const uint32_t token = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const uint32_t lane = threadIdx.x & 31u;
     if (token >= tokens) return;
-    const float *l = logits + (size_t)token * stride;
+    float *l = logits + (size_t)token * stride;
     float v[V];
+    if (parts) {
+        const float *pt = partials + (size_t)token * rows_pad;
+        const size_t part_stride = (size_t)tokens * rows_pad;
 #pragma unroll
-    for (int i = 0; i < V; ++i) {
-        const uint32_t e = lane + 32u * i;
-        v[i] = e < experts ? l[e] : 0.0f;
+        for (int i = 0; i < V; ++i) v[i] = 0.0f;
+        for (uint32_t q = 0; q < parts; ++q) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                const uint32_t e = lane + 32u * i;
+                if (e < experts) v[i] += pt[q * part_stride + e];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            const uint32_t e = lane + 32u * i;
+            if (e < experts) l[e] = v[i];
+        }
+        if (lane == 0) {
+            float gate = 0.0f;
+            for (uint32_t q = 0; q < parts; ++q) gate += pt[q * part_stride + experts];
+            l[experts] = gate;
+        }
+        __syncwarp();  // the row is readable by every lane (the NaN fallback reads it)
+    } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            const uint32_t e = lane + 32u * i;
+            v[i] = e < experts ? l[e] : 0.0f;
+        }
     }
     uint32_t taken = 0;  // bit i: expert lane + 32 i already chosen
     uint32_t chosen[8];
@@ -1206,15 +1238,33 @@ void launch_top_experts(const float *logits, uint32_t logit_stride, uint32_t tok
                         uint32_t *route_experts, float *route_weights, cudaStream_t s) {
     if (tokens == 0) return;
     const uint32_t blocks = (tokens + 7) / 8;
+    float *l = const_cast<float *>(logits);  // only read when no partials are given
     if (experts <= 256)
-        top_experts_regs_kernel<8><<<blocks, 256, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
-                                                         route_weights);
+        top_experts_regs_kernel<8><<<blocks, 256, 0, s>>>(l, logit_stride, tokens, experts, route_experts,
+                                                         route_weights, nullptr, 0, 0);
     else if (experts <= 1024)
-        top_experts_regs_kernel<32><<<blocks, 256, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
-                                                          route_weights);
+        top_experts_regs_kernel<32><<<blocks, 256, 0, s>>>(l, logit_stride, tokens, experts, route_experts,
+                                                          route_weights, nullptr, 0, 0);
     else
         top_experts_kernel<<<blocks, 256, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
                                                   route_weights);
+}
+
+bool launch_top_experts_parts(const float *partials, uint32_t parts, uint32_t rows_pad, float *logits,
+                              uint32_t logit_stride, uint32_t tokens, uint32_t experts, uint32_t *route_experts,
+                              float *route_weights, cudaStream_t s) {
+    if (tokens == 0) return true;
+    if (parts == 0 || rows_pad <= experts) return false;
+    const uint32_t blocks = (tokens + 7) / 8;
+    if (experts <= 256)
+        top_experts_regs_kernel<8><<<blocks, 256, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
+                                                         route_weights, partials, parts, rows_pad);
+    else if (experts <= 1024)
+        top_experts_regs_kernel<32><<<blocks, 256, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
+                                                          route_weights, partials, parts, rows_pad);
+    else
+        return false;
+    return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -1389,13 +1439,23 @@ __global__ void __launch_bounds__(1024) route_block_kernel(RouteParams p) {
     uint32_t *counts = prefix + p.experts * p.words;     // [1024]
     uint32_t *scan = counts + 1024, *chunk_scan = scan + 1024;
     const uint32_t t = threadIdx.x, n = p.tokens * 8, bw = p.experts * p.words;
+    // This thread's routes i = t + 1024 k, all loaded at once and kept for
+    // the placement at the end.
+    constexpr int kPer = kBlockRoutes / 1024;
+    uint32_t mine[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const uint32_t i = t + 1024u * k;
+        mine[k] = i < n ? p.route_experts[i] : 0xFFFFFFFFu;
+    }
     for (uint32_t i = t; i < bw; i += 1024) bitmap[i] = 0;
     counts[t] = 0;
     __syncthreads();
-    for (uint32_t i = t; i < n; i += 1024) {
-        const uint32_t e = p.route_experts[i];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const uint32_t e = mine[k];
         if (e >= p.experts) continue;
-        const uint32_t tok = i >> 3;
+        const uint32_t tok = (t + 1024u * k) >> 3;
         atomicAdd(&counts[e], 1u);
         atomicOr(&bitmap[e * p.words + (tok >> 5)], 1u << (tok & 31u));
     }
@@ -1419,7 +1479,6 @@ __global__ void __launch_bounds__(1024) route_block_kernel(RouteParams p) {
     if (e < p.experts) {
         p.counts[e] = count;
         p.offsets[e] = offset;
-        for (uint32_t i = 0; i < count; ++i) p.pos_expert[offset + i] = e;
         for (uint32_t c = 0; c < chunks; ++c) {
             const uint32_t pos0 = offset + c * p.chunk;
             const uint32_t m = min(p.chunk, count - c * p.chunk);
@@ -1455,13 +1514,15 @@ __global__ void __launch_bounds__(1024) route_block_kernel(RouteParams p) {
         }
     }
     __syncthreads();
-    for (uint32_t i = t; i < n; i += 1024) {
-        const uint32_t ex = p.route_experts[i];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const uint32_t ex = mine[k], i = t + 1024u * k;
         if (ex >= p.experts) continue;
         const uint32_t tok = i >> 3;
         const uint32_t w = ex * p.words + (tok >> 5);
         const uint32_t pos = scan[ex] - counts[ex] + prefix[w] + __popc(bitmap[w] & ((1u << (tok & 31u)) - 1u));
         p.grouped[pos] = tok;
+        p.pos_expert[pos] = ex;
         p.route_to_grouped[i] = pos;
     }
 }

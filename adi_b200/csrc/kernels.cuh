@@ -113,6 +113,13 @@ void launch_bf16_gemm(const uint16_t *w0, uint32_t rows0, const uint16_t *w1, ui
 void launch_top_experts(const float *logits, uint32_t logit_stride, uint32_t tokens,
                         uint32_t experts, uint32_t *route_experts, float *route_weights,
                         cudaStream_t s);
+// The same selection over logits summed from the tensor-core router's
+// split-K partials [parts][tokens][rows_pad]; writes the summed row (experts
+// and the gate column) to `logits`. False when the shape needs the separate
+// reduction (more than 1024 experts).
+bool launch_top_experts_parts(const float *partials, uint32_t parts, uint32_t rows_pad, float *logits,
+                              uint32_t logit_stride, uint32_t tokens, uint32_t experts, uint32_t *route_experts,
+                              float *route_weights, cudaStream_t s);
 
 // Device routing: counting sort of the (token, route) pairs into
 // expert-contiguous position ranges, and the expert GEMM work lists.

@@ -1287,7 +1287,8 @@ bool launch_router_tc(const RouterParams &p, const float *x, uint16_t *xs, const
     }
     const uint32_t units = (p.rows_pad / 128) * ((p.tokens + kRouterN - 1) / kRouterN) * p.parts;
     router_gemm_kernel<<<units, 192, kRouterSmem, s>>>(amap, bmap, p);
-    router_reduce_kernel<<<592, 256, 0, s>>>(p.partials, p.parts, p.tokens, p.rows_pad, rows, logits, stride);
+    if (logits)
+        router_reduce_kernel<<<592, 256, 0, s>>>(p.partials, p.parts, p.tokens, p.rows_pad, rows, logits, stride);
     return true;
 }
 

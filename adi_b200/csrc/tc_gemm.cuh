@@ -48,8 +48,9 @@ bool make_b_map(CUtensorMap *map, const __half *x, uint32_t rows, uint32_t cols)
 // Router logits on tensor cores (see tc_gemm.cu): W3 = [W W W] bf16
 // [rows_pad][k = 3H], activations split into xs [tokens][3H] bf16, split-K
 // partials [parts][tokens][rows_pad], summed in order into logits rows
-// 0 .. rows-1 (row stride `stride`). Returns false when a tensor map cannot
-// be encoded.
+// 0 .. rows-1 (row stride `stride`); with logits null the partials are left
+// for the caller to sum (the fused top-k does). Returns false when a tensor
+// map cannot be encoded.
 struct RouterParams {
     uint32_t rows_pad, tokens, k, parts;
     float *partials;

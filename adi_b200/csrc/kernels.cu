@@ -1430,15 +1430,27 @@ __global__ void __launch_bounds__(1024) route_small_kernel(RouteParams p) {
 // work lists and bitmap-prefix ranks as the three-kernel path, so the same
 // outputs, without the two memsets, three launches and global atomics.
 constexpr uint32_t kBlockRoutes = 8192;
-constexpr size_t kRouteBlockSmemLimit = 160 * 1024;
+constexpr size_t kRouteBlockSmemLimit = 200 * 1024;
 
+// Bytes of dynamic shared memory route_block_kernel needs.
+size_t route_block_smem(const RouteParams &p) {
+    return (2 * size_t(p.experts) * p.words + 3 * 1024 + 2 * size_t(p.tokens) * 8) * sizeof(uint32_t);
+}
+
+// The whole counting sort in one 1024-thread block. Every scattered write
+// lands in shared memory; global memory sees coalesced runs only: the
+// position -> token and position -> expert maps are staged in shared memory
+// and copied out in order, and a warp writes each expert's work items as
+// one contiguous run.
 __global__ void __launch_bounds__(1024) route_block_kernel(RouteParams p) {
     extern __shared__ uint32_t route_smem[];
-    uint32_t *bitmap = route_smem;                       // [E][words]
-    uint32_t *prefix = bitmap + p.experts * p.words;     // [E][words]
-    uint32_t *counts = prefix + p.experts * p.words;     // [1024]
-    uint32_t *scan = counts + 1024, *chunk_scan = scan + 1024;
     const uint32_t t = threadIdx.x, n = p.tokens * 8, bw = p.experts * p.words;
+    uint32_t *bitmap = route_smem;                       // [E][words]
+    uint32_t *prefix = bitmap + bw;                      // [E][words]
+    uint32_t *counts = prefix + bw;                      // [1024]
+    uint32_t *scan = counts + 1024, *chunk_scan = scan + 1024;
+    uint32_t *stage_token = chunk_scan + 1024;           // [n] position -> token
+    uint32_t *stage_expert = stage_token + n;            // [n] position -> expert
     // This thread's routes i = t + 1024 k, all loaded at once and kept for
     // the placement at the end.
     constexpr int kPer = kBlockRoutes / 1024;
@@ -1479,16 +1491,6 @@ __global__ void __launch_bounds__(1024) route_block_kernel(RouteParams p) {
     if (e < p.experts) {
         p.counts[e] = count;
         p.offsets[e] = offset;
-        for (uint32_t c = 0; c < chunks; ++c) {
-            const uint32_t pos0 = offset + c * p.chunk;
-            const uint32_t m = min(p.chunk, count - c * p.chunk);
-            for (uint32_t j = 0; j < 2; ++j)
-                for (uint32_t rb = 0; rb < p.row_blocks_gate_up; ++rb)
-                    p.items_gate_up[((chunk_offset + c) * 2 + j) * p.row_blocks_gate_up + rb] =
-                        make_uint4(e, (j << 16) | rb, pos0, m);
-            for (uint32_t rb = 0; rb < p.row_blocks_down; ++rb)
-                p.items_down[(chunk_offset + c) * p.row_blocks_down + rb] = make_uint4(e, rb, pos0, m);
-        }
     }
     if (e == p.experts - 1) {
         p.offsets[p.experts] = offset + count;
@@ -1496,8 +1498,12 @@ __global__ void __launch_bounds__(1024) route_block_kernel(RouteParams p) {
         *p.count_gate_up = total_chunks * 2 * p.row_blocks_gate_up;
         *p.count_down = total_chunks * p.row_blocks_down;
     }
-    // Per-expert exclusive prefix of bitmap popcounts, one warp per expert.
+    // One warp per expert: the exclusive prefix of its bitmap popcounts, and
+    // its work items, gate/up item (c, j, rb) at ((c0 + c) * 2 + j) * rbg + rb
+    // and down item (c, rb) at (c0 + c) * rbd + rb, so consecutive lanes
+    // write consecutive items.
     const uint32_t warp = t >> 5, lane = t & 31u;
+    const uint32_t rbg = p.row_blocks_gate_up, rbd = p.row_blocks_down;
     for (uint32_t ex = warp; ex < p.experts; ex += 32) {
         uint32_t running = 0;
         for (uint32_t w0 = 0; w0 < p.words; w0 += 32) {
@@ -1512,6 +1518,17 @@ __global__ void __launch_bounds__(1024) route_block_kernel(RouteParams p) {
             if (w < p.words) prefix[ex * p.words + w] = running + incl - c;
             running += __shfl_sync(0xffffffffu, incl, 31);
         }
+        const uint32_t cnt = counts[ex], off = scan[ex] - cnt;
+        const uint32_t ch = (cnt + p.chunk - 1) / p.chunk, c0 = chunk_scan[ex] - ch;
+        for (uint32_t c = 0; c < ch; ++c) {
+            const uint32_t pos0 = off + c * p.chunk, m = min(p.chunk, cnt - c * p.chunk);
+            for (uint32_t idx = lane; idx < 2 * rbg; idx += 32) {
+                const uint32_t j = idx / rbg, rb = idx - j * rbg;
+                p.items_gate_up[(c0 + c) * 2 * rbg + idx] = make_uint4(ex, (j << 16) | rb, pos0, m);
+            }
+            for (uint32_t rb = lane; rb < rbd; rb += 32)
+                p.items_down[(c0 + c) * rbd + rb] = make_uint4(ex, rb, pos0, m);
+        }
     }
     __syncthreads();
 #pragma unroll
@@ -1521,9 +1538,15 @@ __global__ void __launch_bounds__(1024) route_block_kernel(RouteParams p) {
         const uint32_t tok = i >> 3;
         const uint32_t w = ex * p.words + (tok >> 5);
         const uint32_t pos = scan[ex] - counts[ex] + prefix[w] + __popc(bitmap[w] & ((1u << (tok & 31u)) - 1u));
-        p.grouped[pos] = tok;
-        p.pos_expert[pos] = ex;
+        stage_token[pos] = tok;
+        stage_expert[pos] = ex;
         p.route_to_grouped[i] = pos;
+    }
+    __syncthreads();
+    const uint32_t placed = scan[1023];
+    for (uint32_t i = t; i < placed; i += 1024) {
+        p.grouped[i] = stage_token[i];
+        p.pos_expert[i] = stage_expert[i];
     }
 }
 
@@ -1532,7 +1555,7 @@ uint32_t launch_route(const RouteParams &p, cudaStream_t s) {
         route_small_kernel<<<1, 1024, 0, s>>>(p);
         return 1;
     }
-    const size_t block_smem = (2 * size_t(p.experts) * p.words + 3 * 1024) * sizeof(uint32_t);
+    const size_t block_smem = route_block_smem(p);
     if (p.tokens * 8 <= kBlockRoutes && p.experts <= 1024 && block_smem <= kRouteBlockSmemLimit) {
         static bool configured = false;
         if (!configured) {

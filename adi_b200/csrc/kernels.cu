@@ -1432,25 +1432,65 @@ __global__ void __launch_bounds__(1024) route_small_kernel(RouteParams p) {
 constexpr uint32_t kBlockRoutes = 8192;
 constexpr size_t kRouteBlockSmemLimit = 200 * 1024;
 
-// Bytes of dynamic shared memory route_block_kernel needs.
+// Bytes of dynamic shared memory route_block_kernel needs: two [E][words|1]
+// bitmaps, the scans and the two position maps.
 size_t route_block_smem(const RouteParams &p) {
-    return (2 * size_t(p.experts) * p.words + 3 * 1024 + 2 * size_t(p.tokens) * 8) * sizeof(uint32_t);
+    return (2 * size_t(p.experts) * (p.words | 1u) + 3 * 1024 + 2 * size_t(p.tokens) * 8) * sizeof(uint32_t);
+}
+
+// Inclusive prefix sums of a[0..1023] and b[0..1023] (one per thread of a
+// 1024-thread block): warp scans by shuffles, then the 32 warp totals.
+__device__ __forceinline__ void block_scan2_1024(uint32_t &a, uint32_t &b, uint32_t *tot_a, uint32_t *tot_b) {
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t va = __shfl_up_sync(0xffffffffu, a, o), vb = __shfl_up_sync(0xffffffffu, b, o);
+        if (lane >= (uint32_t)o) {
+            a += va;
+            b += vb;
+        }
+    }
+    if (lane == 31) {
+        tot_a[warp] = a;
+        tot_b[warp] = b;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t ta = tot_a[lane], tb = tot_b[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t va = __shfl_up_sync(0xffffffffu, ta, o), vb = __shfl_up_sync(0xffffffffu, tb, o);
+            if (lane >= (uint32_t)o) {
+                ta += va;
+                tb += vb;
+            }
+        }
+        tot_a[lane] = ta;
+        tot_b[lane] = tb;
+    }
+    __syncthreads();
+    if (warp > 0) {
+        a += tot_a[warp - 1];
+        b += tot_b[warp - 1];
+    }
 }
 
 // The whole counting sort in one 1024-thread block. Every scattered write
 // lands in shared memory; global memory sees coalesced runs only: the
 // position -> token and position -> expert maps are staged in shared memory
 // and copied out in order, and a warp writes each expert's work items as
-// one contiguous run.
+// one contiguous run. The per-expert bitmaps are [E][words | 1] so that a
+// thread per expert walks its own row without bank conflicts.
 __global__ void __launch_bounds__(1024) route_block_kernel(RouteParams p) {
     extern __shared__ uint32_t route_smem[];
-    const uint32_t t = threadIdx.x, n = p.tokens * 8, bw = p.experts * p.words;
-    uint32_t *bitmap = route_smem;                       // [E][words]
-    uint32_t *prefix = bitmap + bw;                      // [E][words]
+    const uint32_t t = threadIdx.x, n = p.tokens * 8, wp = p.words | 1u, bw = p.experts * wp;
+    uint32_t *bitmap = route_smem;                       // [E][wp]
+    uint32_t *prefix = bitmap + bw;                      // [E][wp]
     uint32_t *counts = prefix + bw;                      // [1024]
-    uint32_t *scan = counts + 1024, *chunk_scan = scan + 1024;
+    uint32_t *scan = counts + 1024, *chunk_scan = scan + 1024;  // inclusive
     uint32_t *stage_token = chunk_scan + 1024;           // [n] position -> token
     uint32_t *stage_expert = stage_token + n;            // [n] position -> expert
+    __shared__ uint32_t tot_a[32], tot_b[32];
     // This thread's routes i = t + 1024 k, all loaded at once and kept for
     // the placement at the end.
     constexpr int kPer = kBlockRoutes / 1024;
@@ -1469,28 +1509,27 @@ __global__ void __launch_bounds__(1024) route_block_kernel(RouteParams p) {
         if (e >= p.experts) continue;
         const uint32_t tok = (t + 1024u * k) >> 3;
         atomicAdd(&counts[e], 1u);
-        atomicOr(&bitmap[e * p.words + (tok >> 5)], 1u << (tok & 31u));
+        atomicOr(&bitmap[e * wp + (tok >> 5)], 1u << (tok & 31u));
     }
     __syncthreads();
     const uint32_t e = t;
     const uint32_t count = e < p.experts ? counts[e] : 0u;
     const uint32_t chunks = (count + p.chunk - 1) / p.chunk;
-    scan[e] = count;
-    chunk_scan[e] = chunks;
-    __syncthreads();
-    for (uint32_t o = 1; o < 1024; o <<= 1) {
-        const uint32_t a = e >= o ? scan[e - o] : 0u;
-        const uint32_t b = e >= o ? chunk_scan[e - o] : 0u;
-        __syncthreads();
-        scan[e] += a;
-        chunk_scan[e] += b;
-        __syncthreads();
-    }
-    const uint32_t offset = scan[e] - count;
-    const uint32_t chunk_offset = chunk_scan[e] - chunks;
+    uint32_t inc = count, chunk_inc = chunks;
+    block_scan2_1024(inc, chunk_inc, tot_a, tot_b);
+    scan[e] = inc;
+    chunk_scan[e] = chunk_inc;
+    const uint32_t offset = inc - count;
+    const uint32_t chunk_offset = chunk_inc - chunks;
     if (e < p.experts) {
         p.counts[e] = count;
         p.offsets[e] = offset;
+        // exclusive prefix of this expert's bitmap popcounts
+        uint32_t running = 0;
+        for (uint32_t w = 0; w < p.words; ++w) {
+            prefix[e * wp + w] = running;
+            running += __popc(bitmap[e * wp + w]);
+        }
     }
     if (e == p.experts - 1) {
         p.offsets[p.experts] = offset + count;
@@ -1498,45 +1537,33 @@ __global__ void __launch_bounds__(1024) route_block_kernel(RouteParams p) {
         *p.count_gate_up = total_chunks * 2 * p.row_blocks_gate_up;
         *p.count_down = total_chunks * p.row_blocks_down;
     }
-    // One warp per expert: the exclusive prefix of its bitmap popcounts, and
-    // its work items, gate/up item (c, j, rb) at ((c0 + c) * 2 + j) * rbg + rb
-    // and down item (c, rb) at (c0 + c) * rbd + rb, so consecutive lanes
-    // write consecutive items.
+    __syncthreads();
+    // One warp per expert writes its work items: gate/up item (c, j, rb) at
+    // ((c0 + c) * 2 + j) * rbg + rb, down item (c, rb) at (c0 + c) * rbd + rb.
     const uint32_t warp = t >> 5, lane = t & 31u;
     const uint32_t rbg = p.row_blocks_gate_up, rbd = p.row_blocks_down;
-    for (uint32_t ex = warp; ex < p.experts; ex += 32) {
-        uint32_t running = 0;
-        for (uint32_t w0 = 0; w0 < p.words; w0 += 32) {
-            const uint32_t w = w0 + lane;
-            const uint32_t c = w < p.words ? __popc(bitmap[ex * p.words + w]) : 0u;
-            uint32_t incl = c;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= (uint32_t)o) incl += v;
+    if (rbg | rbd) {
+        for (uint32_t ex = warp; ex < p.experts; ex += 32) {
+            const uint32_t cnt = counts[ex], off = scan[ex] - cnt;
+            const uint32_t ch = (cnt + p.chunk - 1) / p.chunk, c0 = chunk_scan[ex] - ch;
+            for (uint32_t c = 0; c < ch; ++c) {
+                const uint32_t pos0 = off + c * p.chunk, m = min(p.chunk, cnt - c * p.chunk);
+                uint4 *gu = p.items_gate_up + (size_t)(c0 + c) * 2 * rbg;
+                for (uint32_t rb = lane; rb < rbg; rb += 32) {
+                    gu[rb] = make_uint4(ex, rb, pos0, m);
+                    gu[rbg + rb] = make_uint4(ex, (1u << 16) | rb, pos0, m);
+                }
+                for (uint32_t rb = lane; rb < rbd; rb += 32)
+                    p.items_down[(size_t)(c0 + c) * rbd + rb] = make_uint4(ex, rb, pos0, m);
             }
-            if (w < p.words) prefix[ex * p.words + w] = running + incl - c;
-            running += __shfl_sync(0xffffffffu, incl, 31);
-        }
-        const uint32_t cnt = counts[ex], off = scan[ex] - cnt;
-        const uint32_t ch = (cnt + p.chunk - 1) / p.chunk, c0 = chunk_scan[ex] - ch;
-        for (uint32_t c = 0; c < ch; ++c) {
-            const uint32_t pos0 = off + c * p.chunk, m = min(p.chunk, cnt - c * p.chunk);
-            for (uint32_t idx = lane; idx < 2 * rbg; idx += 32) {
-                const uint32_t j = idx / rbg, rb = idx - j * rbg;
-                p.items_gate_up[(c0 + c) * 2 * rbg + idx] = make_uint4(ex, (j << 16) | rb, pos0, m);
-            }
-            for (uint32_t rb = lane; rb < rbd; rb += 32)
-                p.items_down[(c0 + c) * rbd + rb] = make_uint4(ex, rb, pos0, m);
         }
     }
-    __syncthreads();
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
         const uint32_t ex = mine[k], i = t + 1024u * k;
         if (ex >= p.experts) continue;
         const uint32_t tok = i >> 3;
-        const uint32_t w = ex * p.words + (tok >> 5);
+        const uint32_t w = ex * wp + (tok >> 5);
         const uint32_t pos = scan[ex] - counts[ex] + prefix[w] + __popc(bitmap[w] & ((1u << (tok & 31u)) - 1u));
         stage_token[pos] = tok;
         stage_expert[pos] = ex;

@@ -180,11 +180,13 @@ __device__ __forceinline__ void fwht_regs(float (&v)[R], float *sh) {
     const uint32_t lane = threadIdx.x & 31u;
 #pragma unroll
     for (int s = 0; s < 5; ++s) {
-        const bool upper = (lane >> s) & 1u;
+        // lower lane: v + o; upper lane: o - v. Both as one fma with a +-1
+        // multiplier, which rounds exactly like the add or the subtract.
+        const float sign = ((lane >> s) & 1u) ? -1.0f : 1.0f;
 #pragma unroll
         for (int r = 0; r < R; ++r) {
             const float o = __shfl_xor_sync(0xffffffffu, v[r], 1u << s);
-            v[r] = upper ? __fsub_rn(o, v[r]) : __fadd_rn(v[r], o);
+            v[r] = __fmaf_rn(sign, v[r], o);
         }
     }
     const uint32_t n = 256u * R;
@@ -231,11 +233,13 @@ __device__ __forceinline__ void fwht8_transposed(float (&v)[8], float *sh) {
     const uint32_t lane = threadIdx.x & 31u;
 #pragma unroll
     for (int s = 0; s < 5; ++s) {
-        const bool upper = (lane >> s) & 1u;
+        // lower lane: v + o; upper lane: o - v. Both as one fma with a +-1
+        // multiplier, which rounds exactly like the add or the subtract.
+        const float sign = ((lane >> s) & 1u) ? -1.0f : 1.0f;
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
             const float o = __shfl_xor_sync(0xffffffffu, v[r], 1u << s);
-            v[r] = upper ? __fsub_rn(o, v[r]) : __fadd_rn(v[r], o);
+            v[r] = __fmaf_rn(sign, v[r], o);
         }
     }
 #pragma unroll

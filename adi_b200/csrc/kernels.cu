@@ -1150,12 +1150,22 @@ __global__ void top_experts_regs_kernel(float *logits, uint32_t stride, uint32_t
         const size_t part_stride = (size_t)tokens * rows_pad;
 #pragma unroll
         for (int i = 0; i < V; ++i) v[i] = 0.0f;
-        for (uint32_t q = 0; q < parts; ++q) {
+        // QB parts' loads in flight at a time, added in part order.
+        constexpr uint32_t QB = V <= 8 ? 4 : 1;
+        for (uint32_t q0 = 0; q0 < parts; q0 += QB) {
+            float pv[QB][V];
 #pragma unroll
-            for (int i = 0; i < V; ++i) {
-                const uint32_t e = lane + 32u * i;
-                if (e < experts) v[i] += pt[q * part_stride + e];
-            }
+            for (uint32_t j = 0; j < QB; ++j)
+#pragma unroll
+                for (int i = 0; i < V; ++i) {
+                    const uint32_t e = lane + 32u * i;
+                    pv[j][i] = (e < experts && q0 + j < parts) ? pt[(q0 + j) * part_stride + e] : 0.0f;
+                }
+#pragma unroll
+            for (uint32_t j = 0; j < QB; ++j)
+                if (q0 + j < parts)
+#pragma unroll
+                    for (int i = 0; i < V; ++i) v[i] += pv[j][i];
         }
 #pragma unroll
         for (int i = 0; i < V; ++i) {
@@ -1255,13 +1265,15 @@ bool launch_top_experts_parts(const float *partials, uint32_t parts, uint32_t ro
                               float *route_weights, cudaStream_t s) {
     if (tokens == 0) return true;
     if (parts == 0 || rows_pad <= experts) return false;
-    const uint32_t blocks = (tokens + 7) / 8;
+    // Two tokens (warps) per block: the partial reads of a large batch spread
+    // over every SM.
+    const uint32_t blocks = (tokens + 1) / 2;
     if (experts <= 256)
-        top_experts_regs_kernel<8><<<blocks, 256, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
-                                                         route_weights, partials, parts, rows_pad);
+        top_experts_regs_kernel<8><<<blocks, 64, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
+                                                        route_weights, partials, parts, rows_pad);
     else if (experts <= 1024)
-        top_experts_regs_kernel<32><<<blocks, 256, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
-                                                          route_weights, partials, parts, rows_pad);
+        top_experts_regs_kernel<32><<<blocks, 64, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
+                                                         route_weights, partials, parts, rows_pad);
     else
         return false;
     return true;

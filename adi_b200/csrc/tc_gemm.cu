@@ -1068,9 +1068,25 @@ __global__ void __launch_bounds__(256) prep_f16_2048_kernel(PrepF16Params p) {
     const size_t half_stride = (size_t)p.rows * (n / 2);
     for (int job = 0; job < p.jobs; ++job) {
         const void *su = job ? p.su[1] : p.su[0];
+        // The thread's eight input scales in one load: 16 B of f16 or 8 B of
+        // int8 (su0 is a multiple of 8 elements).
+        float sc[8];
+        if (p.su_is_f16) {
+            const uint4 q = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(su) + su0);
+            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                sc[2 * r] = f16_bits_to_f32(w[r] & 0xFFFFu);
+                sc[2 * r + 1] = f16_bits_to_f32(w[r] >> 16);
+            }
+        } else {
+            const uint2 q = *reinterpret_cast<const uint2 *>(static_cast<const int8_t *>(su) + su0);
+#pragma unroll
+            for (int r = 0; r < 8; ++r) sc[r] = (float)(int8_t)((r < 4 ? q.x : q.y) >> (8 * (r & 3)));
+        }
         float v[8];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) v[r] = __fmul_rn(x[r], scale_value(su, p.su_is_f16, su0 + r));
+        for (int r = 0; r < 8; ++r) v[r] = __fmul_rn(x[r], sc[r]);
         fwht8_transposed(v, sh);
 #pragma unroll
         for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(v[k], p.scale);
@@ -1139,11 +1155,13 @@ __device__ __forceinline__ void fwht_warp16(float (&v)[16]) {
     const uint32_t lane = threadIdx.x & 31u;
 #pragma unroll
     for (int s = 0; s < 5; ++s) {
-        const bool upper = (lane >> s) & 1u;
+        // lower lane: v + o; upper lane: o - v. Both as one fma with a +-1
+        // multiplier, which rounds exactly like the add or the subtract.
+        const float sign = ((lane >> s) & 1u) ? -1.0f : 1.0f;
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
             const float o = __shfl_xor_sync(0xffffffffu, v[r], 1u << s);
-            v[r] = upper ? __fsub_rn(o, v[r]) : __fadd_rn(v[r], o);
+            v[r] = __fmaf_rn(sign, v[r], o);
         }
     }
 }

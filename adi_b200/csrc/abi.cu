@@ -720,6 +720,8 @@ void head_matmul_dev(adi_cuda_context *c, HeadDev &h, const float *in, uint32_t 
 
 // ---- the MoE block --------------------------------------------------------
 
+constexpr uint32_t kSharedExpertKParts = 2;
+
 // Shared NE SwiGLU expert on tensor cores: gate and up in one launch, the
 // SwiGLU between, down after; sacc = pre-transform down accumulators.
 void shared_expert_tc(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *sacc) {
@@ -746,7 +748,10 @@ void shared_expert_tc(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t 
     pp.split = 0;
     launch_prep_f16(pp, s);
     const uint64_t units_gu = uint64_t(I / 128) * 2 * ((T + kTcMaxN - 1) / kTcMaxN);
-    const uint32_t ks = ne_ksplit(c, units_gu);
+    // K in two parts at every batch size (H >= 128 for the tensor-core
+    // path): the sums of a token do not depend on how many tokens share the
+    // launch or on the SMs the launch gets.
+    const uint32_t ks = kSharedExpertKParts;
     float *acc_g = c->buffer<float>("moe_sacc_g", ks * size_t(T) * I);
     float *acc_u = c->buffer<float>("moe_sacc_u", ks * size_t(T) * I);
     const CUtensorMap map_g = b_map(xg, T, H), map_u = b_map(xu, T, H);
@@ -803,14 +808,21 @@ void shared_expert_beside(adi_cuda_context *c, MoeDev &L, const float *in, uint3
     cudaStream_t main = c->stream;
     check(cudaEventRecord(c->fork_event, main), "cudaEventRecord");
     check(cudaStreamWaitEvent(c->side_stream, c->fork_event, 0), "cudaStreamWaitEvent");
+    // A tensor-core GEMM CTA takes an SM's whole register file, so the side
+    // chain's GEMMs get half of the SMs (persistent grids and K splits sized
+    // to that), leaving the rest to the main chain's kernels meanwhile.
+    const int sms = c->sms;
     c->stream = c->side_stream;
+    c->sms = sms / 2;
     try {
         shared_expert(c, L, in, T, sacc_d);
     } catch (...) {
         c->stream = main;
+        c->sms = sms;
         throw;
     }
     c->stream = main;
+    c->sms = sms;
     check(cudaEventRecord(c->join_event, c->side_stream), "cudaEventRecord");
 }
 

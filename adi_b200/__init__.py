@@ -199,7 +199,8 @@ class Context:
     def launch_count(self) -> int:
         return int(self.lib.adi_cuda_launch_count(self.ptr))
 
-    def set_profiling(self, enable: bool):
+    def set_profiling(self, enable):
+        """False/0 off, True/1 every stage, 2 the routed expert GEMMs only."""
         _check(self.lib.adi_cuda_set_profiling(self.ptr, int(enable)), "set_profiling")
 
     def reset_profile(self):

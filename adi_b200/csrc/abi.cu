@@ -203,6 +203,7 @@ const char *const kStageNames[kStageCount] = {
 // CUDA-event brackets around stages, resolved lazily.
 struct Profiler {
     bool enabled = false;
+    uint32_t mask = ~0u;  // stages bracketed while enabled (bit per stage)
     struct Pending {
         int stage;
         cudaEvent_t begin, end;
@@ -225,7 +226,7 @@ struct Profiler {
         return e;
     }
     void begin(int stage, cudaStream_t s) {
-        if (!enabled) return;
+        if (!enabled || !((mask >> stage) & 1u)) return;
         open_stage = stage;
         open_event = take();
         check(cudaEventRecord(open_event, s), "cudaEventRecord");
@@ -1519,7 +1520,9 @@ uint64_t adi_cuda_launch_count(const adi_cuda_context *c) { return c ? c->launch
 int adi_cuda_set_profiling(adi_cuda_context *c, int enable) {
     return guarded([&] {
         std::lock_guard<std::mutex> g(require(c)->lock);
+        if (enable < 0 || enable > 2) invalid("profiling mode must be 0, 1 or 2");
         c->profiler.enabled = enable != 0;
+        c->profiler.mask = enable == 2 ? (1u << kStageExpertGateUp) | (1u << kStageExpertDown) : ~0u;
     });
 }
 

@@ -131,7 +131,9 @@ ADI_CUDA_API uint64_t adi_cuda_launch_count(const adi_cuda_context *context);
  * stream it runs on. adi_cuda_profile_stage reads stage `index`'s name,
  * accumulated milliseconds and bracket count (synchronising first); it
  * returns 1 once `index` is past the last stage. adi_cuda_profile_reset
- * clears the totals. */
+ * clears the totals. `enable`: 0 off, 1 every stage, 2 only the routed
+ * expert GEMM stages (the dominant kernel timed with two events per launch,
+ * so the rest of the call runs unbracketed). */
 ADI_CUDA_API int adi_cuda_set_profiling(adi_cuda_context *context, int enable);
 ADI_CUDA_API int adi_cuda_profile_stage(adi_cuda_context *context, uint32_t index, char *name, size_t name_size,
                                         double *milliseconds, uint64_t *count);

@@ -98,6 +98,8 @@ SIGNATURES = {
     "adi_cuda_bf16_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_moe_forward_batch_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p,
                                                     C.c_void_p, C.c_void_p]),
+    "adi_cuda_moe_stack_forward_device": (C.c_int, [_ctx, C.POINTER(_h), C.c_uint32, C.c_void_p, C.c_void_p, _h,
+                                                    C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_expert_states": (C.c_int, [_ctx, u16p, C.c_uint32, u32p]),
     "adi_cuda_ne_states": (C.c_int, [_ctx, u16p, C.c_uint32, u32p]),
     "adi_cuda_expert_state_values": (C.c_int, [_ctx, f32p, f32p]),
@@ -344,6 +346,17 @@ class Context:
         _check(self.lib.adi_cuda_moe_forward_batch_device(self.ptr, layer.value, inputs_ptr, batch, outputs_ptr,
                                                           route_experts_ptr or None, route_weights_ptr or None),
                "moe_forward_batch_device")
+
+    def moe_stack_forward_device(self, layers, norms_ptr: int, final_norm_ptr: int, head, hidden_ptr: int,
+                                 tokens: int, logits_ptr: int = 0):
+        """hidden [tokens][H] (device, updated in place) through the MoE stack
+        `layers` with their bf16 norms [len(layers)][H]; with `head` and
+        `logits_ptr`, the final norm and the head's logits [tokens][rows]."""
+        arr = (_h * max(1, len(layers)))(*[l.value for l in layers])
+        _check(self.lib.adi_cuda_moe_stack_forward_device(
+            self.ptr, arr, len(layers), norms_ptr or None, final_norm_ptr or None,
+            head.value if head is not None else 0, hidden_ptr, tokens, logits_ptr or None),
+            "moe_stack_forward_device")
 
     # -- expert-parallel phases (device pointers, asynchronous) ---------------
     def ep_dispatch_device(self, shard: Handle, inputs_ptr: int, tokens: int, send_ptr: int, counts_ptr: int,

@@ -192,12 +192,13 @@ enum Stage {
     kStageNeMatmul,
     kStageHead,
     kStageBf16,
+    kStageNorm,
     kStageCount
 };
 const char *const kStageNames[kStageCount] = {
     "router",           "top_experts",      "route",        "expert_prep",  "expert_gemm_gate_up",
     "swiglu",           "expert_gemm_down", "shared_expert", "combine",     "expert_matmul",
-    "ne_matmul",        "head_matmul",      "bf16_matmul",
+    "ne_matmul",        "head_matmul",      "bf16_matmul",  "norm_residual",
 };
 
 // CUDA-event brackets around stages, resolved lazily.
@@ -284,6 +285,7 @@ struct adi_cuda_context {
     std::map<uint64_t, std::unique_ptr<Bf16Dev>> bf16s;
     std::map<uint64_t, std::unique_ptr<MoeDev>> moes;
     uint32_t *error_word = nullptr;  // device word kernels flag timeouts in
+    uint32_t *error_host = nullptr;  // pinned copy of it, read after a synchronise
     // The layer and token count of the last expert-parallel dispatch, whose
     // routes and shared-expert sums the matching combine reads.
     uint64_t ep_layer = 0;
@@ -309,9 +311,11 @@ struct adi_cuda_context {
 
     // Synchronises the stream, then reports (and clears) a kernel timeout.
     void finish() {
+        // The word's copy rides on the stream, so one synchronise covers both.
+        check(cudaMemcpyAsync(error_host, error_word, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream),
+              "read error word");
         check(cudaStreamSynchronize(stream), "synchronize");
-        uint32_t flags = 0;
-        check(cudaMemcpy(&flags, error_word, sizeof flags, cudaMemcpyDeviceToHost), "read error word");
+        const uint32_t flags = *error_host;
         if (flags) {
             check(cudaMemset(error_word, 0, sizeof flags), "clear error word");
             throw Status(ADI_CUDA_TIMEOUT, "a bounded device wait timed out; results are invalid");
@@ -1461,6 +1465,7 @@ int adi_cuda_init(int device, adi_cuda_context **out) {
         check(cudaEventCreateWithFlags(&c->join_event, cudaEventDisableTiming), "cudaEventCreate");
         check(cudaMalloc(&c->error_word, sizeof(uint32_t)), "cudaMalloc");
         check(cudaMemset(c->error_word, 0, sizeof(uint32_t)), "cudaMemset");
+        check(cudaHostAlloc(&c->error_host, sizeof(uint32_t), cudaHostAllocDefault), "cudaHostAlloc");
         *out = c.release();
     });
 }
@@ -1473,9 +1478,10 @@ int adi_cuda_shutdown(adi_cuda_context *c) {
         if (c->side_stream) cudaStreamSynchronize(c->side_stream);
         cudaStream_t own = c->own_stream, side = c->side_stream;
         cudaEvent_t fork = c->fork_event, join = c->join_event;
-        uint32_t *error_word = c->error_word;
+        uint32_t *error_word = c->error_word, *error_host = c->error_host;
         delete c;
         if (error_word) cudaFree(error_word);
+        if (error_host) cudaFreeHost(error_host);
         if (own) cudaStreamDestroy(own);
         if (side) cudaStreamDestroy(side);
         if (fork) cudaEventDestroy(fork);
@@ -1723,6 +1729,49 @@ int adi_cuda_moe_forward_batch_device(adi_cuda_context *c, adi_cuda_handle h, co
         use_device(c);
         if (!in || !out) invalid("input or output pointer is null");
         moe_forward_dev(c, lookup(c->moes, h, "MoE layer"), in, batch, out, route_experts, route_weights);
+    });
+}
+
+int adi_cuda_moe_stack_forward_device(adi_cuda_context *c, const adi_cuda_handle *layers, uint32_t layer_count,
+                                      const uint16_t *norms_bf16, const uint16_t *final_norm_bf16,
+                                      adi_cuda_handle head, float *hidden, uint32_t tokens, float *logits) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!hidden || (layer_count && (!layers || !norms_bf16)) || (logits && !final_norm_bf16))
+            invalid("stack pointer is null");
+        if (tokens == 0) invalid("MoE batch shape mismatch");
+        if (reinterpret_cast<uintptr_t>(hidden) % 16) invalid("hidden must be 16-byte aligned");
+        std::vector<MoeDev *> stack;
+        for (uint32_t l = 0; l < layer_count; ++l) stack.push_back(&lookup(c->moes, layers[l], "MoE layer"));
+        HeadDev *h = logits ? &lookup(c->heads, head, "head") : nullptr;
+        uint32_t H = stack.empty() ? (h ? h->cols : 0u) : stack[0]->hidden;
+        for (MoeDev *L : stack)
+            if (L->hidden != H) invalid("MoE stack layers differ in hidden size");
+        if (h && h->cols != H) invalid("Mach output head batch shape mismatch");
+        if (H == 0) return;
+        cudaStream_t s = c->stream;
+        const size_t n = size_t(tokens) * H;
+        float *normed = c->buffer<float>("stack_normed", n);
+        float *ff = c->buffer<float>("stack_ff", n);
+        for (uint32_t l = 0; l < layer_count; ++l) {
+            c->stage(kStageNorm);
+            launch_rms_norm(hidden, norms_bf16 + size_t(l) * H, tokens, H, 1.0f, 1.0e-6f, normed, s);
+            c->stage_end();
+            c->after_launch(1);
+            moe_forward_dev(c, *stack[l], normed, tokens, ff, nullptr, nullptr);
+            c->stage(kStageNorm);
+            launch_residual_add(hidden, ff, n, s);
+            c->stage_end();
+            c->after_launch(1);
+        }
+        if (h) {
+            c->stage(kStageNorm);
+            launch_rms_norm(hidden, final_norm_bf16, tokens, H, 1.0f, 1.0e-6f, normed, s);
+            c->stage_end();
+            c->after_launch(1);
+            head_matmul_dev(c, *h, normed, tokens, logits);
+        }
     });
 }
 

@@ -2084,4 +2084,25 @@ void launch_rms_norm(const float *x, const uint16_t *w, uint32_t count, uint32_t
     rms_norm_kernel<<<count, 256, 0, s>>>(x, w, n, offset, eps, out);
 }
 
+// hidden[i] += add[i]: the residual update after a block
+// (src/executor.cpp:1525-1527), one add per element.
+__global__ void residual_add_kernel(float4 *hidden, const float4 *add, size_t quads) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < quads; i += (size_t)gridDim.x * blockDim.x) {
+        float4 h = hidden[i];
+        const float4 a = add[i];
+        h.x += a.x;
+        h.y += a.y;
+        h.z += a.z;
+        h.w += a.w;
+        hidden[i] = h;
+    }
+}
+
+void launch_residual_add(float *hidden, const float *add, size_t count, cudaStream_t s) {
+    if (count == 0) return;
+    const size_t quads = count / 4, blocks = (quads + 255) / 256;
+    residual_add_kernel<<<(unsigned)(blocks < 148 * 8 ? blocks : 148 * 8), 256, 0, s>>>(
+        reinterpret_cast<float4 *>(hidden), reinterpret_cast<const float4 *>(add), quads);
+}
+
 }  // namespace adi_cuda

@@ -194,5 +194,7 @@ void launch_head(const HeadParams &p, cudaStream_t s);
 void launch_hadamard(float *values, uint32_t count, uint32_t n, float scale, cudaStream_t s);
 void launch_rms_norm(const float *x, const uint16_t *w, uint32_t count, uint32_t n, float offset,
                      float eps, float *out, cudaStream_t s);
+// hidden += add over `count` floats (a multiple of 4, 16-byte aligned).
+void launch_residual_add(float *hidden, const float *add, size_t count, cudaStream_t s);
 
 }  // namespace adi_cuda

@@ -201,6 +201,23 @@ ADI_CUDA_API int adi_cuda_moe_forward_batch_device(adi_cuda_context *context,
                                       float *outputs, uint32_t *route_experts,
                                       float *route_weights);
 
+/* The MoE half of the decoder layer over a stack of layers, device-resident
+ * (src/executor.cpp:1513-1531 per layer, then finalize_hidden :1533-1540 and
+ * the output head): for each layer l,
+ *     hidden += moe_forward_batch_l(rms_norm(hidden, norm_l, 1, 1e-6));
+ * then logits = head(rms_norm(hidden, final_norm, 1, 1e-6)) when `logits` is
+ * not null. `hidden` [tokens][H] is updated in place; `norms_bf16` is
+ * [layer_count][H] bf16 and `final_norm_bf16` [H], all device pointers;
+ * `logits` is [tokens][head rows]. Activations stay on the device between
+ * layers. The reference interleaves attention between these steps; this
+ * entry covers the stack with the attention half left out. */
+ADI_CUDA_API int adi_cuda_moe_stack_forward_device(adi_cuda_context *context,
+                                      const adi_cuda_handle *layers, uint32_t layer_count,
+                                      const uint16_t *norms_bf16,
+                                      const uint16_t *final_norm_bf16,
+                                      adi_cuda_handle head, float *hidden,
+                                      uint32_t tokens, float *logits);
+
 /* ---- expert parallelism ---------------------------------------------------
  * No counterpart in the reference, which runs one process on one host (its
  * only parallelism is CPU tasks, src/executor.cpp:261, :1302-1371). These

@@ -319,6 +319,102 @@ def decode_c3(ctx, stream, local, tokens_list=(1, 4), steps=20):
     return out
 
 
+C5_LAYERS = 40
+C5_DISTINCT = 8
+C5_PREFILL = 2048
+C5_UBATCH = 512
+C5_DECODE_STEPS = 128
+
+
+def stack_c5(ctx, stream, local):
+    """C5 on one GPU: the 40-layer MoE stack (per layer rms_norm, block,
+    residual; then the final norm and the int5 head) through the
+    device-resident adi_cuda_moe_stack_forward_device. A 2048-token prefill
+    in ubatches of 512 with the last token's logits, then 128 batch-1
+    decode steps (a fresh input row each step), eager and replayed from a
+    CUDA graph. Eight distinct blocks cycle over the 40 layers."""
+    from adi_b200 import synthetic
+    device = f"cuda:{local}"
+    moe_h = []
+    for d in range(C5_DISTINCT):
+        b = synthetic.moe_block(seed=8000 + d, device=device)
+        moe_h.append(ctx.upload_moe_layer(b))
+        del b
+    layers = [moe_h[l % C5_DISTINCT] for l in range(C5_LAYERS)]
+    g = torch.Generator(device=device)
+    g.manual_seed(8100)
+    norms = (torch.randn(C5_LAYERS, 2048, generator=g, device=device) * 0.1).to(torch.bfloat16).view(torch.int16)
+    final = (torch.randn(2048, generator=g, device=device) * 0.1).to(torch.bfloat16).view(torch.int16)
+    head = synthetic.head_chunk(8200, C3_VOCAB, 2048, device=device)
+    head_h = ctx.upload_head(head)
+    del head
+    prompt = synthetic.activations(8300, C5_PREFILL, 2048, device=device)
+    rows = synthetic.activations(8301, C5_DECODE_STEPS, 2048, device=device)
+    hidden = torch.empty_like(prompt)
+    token = torch.empty(1, 2048, device=device)
+    logits = torch.empty(1, C3_VOCAB, device=device)
+
+    def prefill():
+        hidden.copy_(prompt)
+        for a in range(0, C5_PREFILL, C5_UBATCH):
+            ctx.moe_stack_forward_device(layers, norms.data_ptr(), final.data_ptr(), None,
+                                         hidden[a:a + C5_UBATCH].data_ptr(), C5_UBATCH, 0)
+        ctx.moe_stack_forward_device([], 0, final.data_ptr(), head_h, hidden[C5_PREFILL - 1:].data_ptr(), 1,
+                                     logits.data_ptr())
+
+    def decode_step(k):
+        token.copy_(rows[k:k + 1])
+        ctx.moe_stack_forward_device(layers, norms.data_ptr(), final.data_ptr(), head_h, token.data_ptr(), 1,
+                                     logits.data_ptr())
+
+    b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    prefill()
+    b.record(stream)
+    for _ in range(3):
+        prefill()
+    e.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = b.elapsed_time(e) / 3
+    for k in range(3):
+        decode_step(k)
+    b.record(stream)
+    for k in range(C5_DECODE_STEPS):
+        decode_step(k)
+    e.record(stream)
+    torch.cuda.synchronize()
+    eager_ms = b.elapsed_time(e) / C5_DECODE_STEPS
+    # One decode step captured once; each replay reads the row copied into
+    # its fixed input buffer just before it.
+    source = torch.empty(1, 2048, device=device)
+    graph = torch.cuda.CUDAGraph()
+    capture = torch.cuda.Stream(device=local)
+    with torch.cuda.graph(graph, stream=capture):
+        ctx.set_stream(capture.cuda_stream)
+        token.copy_(source)
+        ctx.moe_stack_forward_device(layers, norms.data_ptr(), final.data_ptr(), head_h, token.data_ptr(), 1,
+                                     logits.data_ptr())
+    ctx.set_stream(stream.cuda_stream)
+    for k in range(3):
+        source.copy_(rows[k:k + 1])
+        graph.replay()
+    b.record(stream)
+    for k in range(C5_DECODE_STEPS):
+        source.copy_(rows[k:k + 1])
+        graph.replay()
+    e.record(stream)
+    torch.cuda.synchronize()
+    graph_ms = b.elapsed_time(e) / C5_DECODE_STEPS
+    del graph
+    for h in moe_h + [head_h]:
+        h.release()
+    return {"layers": C5_LAYERS, "distinct_weight_sets": C5_DISTINCT, "per_layer": "rms_norm + MoE block + residual",
+            "head": f"int5_g64 {C3_VOCAB}x2048", "gpus": 1,
+            "prefill_tokens": C5_PREFILL, "ubatch": C5_UBATCH, "prefill_ms": prefill_ms,
+            "prefill_tokens_per_s": C5_PREFILL / (prefill_ms / 1e3),
+            "decode_steps": C5_DECODE_STEPS, "decode_eager_ms_per_token": eager_ms,
+            "decode_graph_ms_per_token": graph_ms, "decode_graph_tokens_per_s": 1e3 / graph_ms}
+
+
 def zipf_logits(pool: int, tokens: int, experts: int, seed: int, device: str) -> torch.Tensor:
     """C4 router logits [pool, tokens, experts + 1]: log p(rank(e)) +
     Gumbel(0, 1) with p ~ 1 / (rank + 1)^1.1 and the rank permutation drawn
@@ -639,6 +735,7 @@ def run_ours(args, world, rank, local):
         h.release()
     handles = []
     c3 = decode_c3(ctx, stream, local)
+    c5 = stack_c5(ctx, stream, local)
     hbm_peak_c3, _ = peaks()
     for v in c3.values():
         v["graph_frac_hbm"] = v["graph_gbs"] / hbm_peak_c3
@@ -675,6 +772,7 @@ def run_ours(args, world, rank, local):
             "decode_c3": {"layers": C3_LAYERS, "distinct_weight_sets": C3_DISTINCT,
                           "per_layer": "MoE block + NE q/k/v/o/gated-delta", "head": f"int5_g64 {C3_VOCAB}x2048",
                           **c3},
+            "stack_c5": c5,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
                     "d2h_bytes_per_step": T * H * 4 + T * 8 * 8, "steps": e2e_steps},
             "gpu_launches": launches,

@@ -98,6 +98,9 @@ SIGNATURES = {
     "adi_cuda_bf16_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_moe_forward_batch_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p,
                                                     C.c_void_p, C.c_void_p]),
+    "adi_cuda_rms_norm_device": (C.c_int, [_ctx, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_float,
+                                           C.c_float, C.c_void_p]),
+    "adi_cuda_residual_add_device": (C.c_int, [_ctx, C.c_void_p, C.c_void_p, C.c_size_t]),
     "adi_cuda_moe_stack_forward_device": (C.c_int, [_ctx, C.POINTER(_h), C.c_uint32, C.c_void_p, C.c_void_p, _h,
                                                     C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_expert_states": (C.c_int, [_ctx, u16p, C.c_uint32, u32p]),
@@ -357,6 +360,14 @@ class Context:
             self.ptr, arr, len(layers), norms_ptr or None, final_norm_ptr or None,
             head.value if head is not None else 0, hidden_ptr, tokens, logits_ptr or None),
             "moe_stack_forward_device")
+
+    def rms_norm_device(self, inputs_ptr: int, weight_ptr: int, count: int, n: int, offset: float,
+                        epsilon: float, outputs_ptr: int):
+        _check(self.lib.adi_cuda_rms_norm_device(self.ptr, inputs_ptr, weight_ptr, count, n, offset, epsilon,
+                                                 outputs_ptr), "rms_norm_device")
+
+    def residual_add_device(self, hidden_ptr: int, add_ptr: int, count: int):
+        _check(self.lib.adi_cuda_residual_add_device(self.ptr, hidden_ptr, add_ptr, count), "residual_add_device")
 
     # -- expert-parallel phases (device pointers, asynchronous) ---------------
     def ep_dispatch_device(self, shard: Handle, inputs_ptr: int, tokens: int, send_ptr: int, counts_ptr: int,

@@ -1884,6 +1884,33 @@ int adi_cuda_rms_norm(adi_cuda_context *c, const float *inputs, const uint16_t *
     });
 }
 
+int adi_cuda_rms_norm_device(adi_cuda_context *c, const float *inputs, const uint16_t *weight_bf16, uint32_t count,
+                             uint32_t n, float weight_offset, float epsilon, float *outputs) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!inputs || !weight_bf16 || !outputs || n == 0) invalid("RMS norm shape mismatch");
+        c->stage(kStageNorm);
+        launch_rms_norm(inputs, weight_bf16, count, n, weight_offset, epsilon, outputs, c->stream);
+        c->stage_end();
+        c->after_launch(count ? 1 : 0);
+    });
+}
+
+int adi_cuda_residual_add_device(adi_cuda_context *c, float *hidden, const float *add, size_t count) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!hidden || !add) invalid("residual pointer is null");
+        if (count % 4 || reinterpret_cast<uintptr_t>(hidden) % 16 || reinterpret_cast<uintptr_t>(add) % 16)
+            invalid("residual rows must be 16-byte aligned multiples of 4 floats");
+        c->stage(kStageNorm);
+        launch_residual_add(hidden, add, count, c->stream);
+        c->stage_end();
+        c->after_launch(count ? 1 : 0);
+    });
+}
+
 int adi_cuda_ep_dispatch_device(adi_cuda_context *c, adi_cuda_handle h, const float *in,
                                 const float *router_logits, uint32_t tokens, float *send_rows,
                                 uint32_t *expert_counts, uint32_t *route_experts, float *route_weights) {

@@ -116,3 +116,61 @@ class ExpertParallelMoe:
         return self.phases.combine(returned, tokens)
 
     __call__ = forward
+
+
+class DeviceStackOps:
+    """The per-layer steps of an expert-parallel stack on the GPU, through
+    the C ABI: rms_norm with layer l's bf16 weights, the residual add, and
+    the final norm plus head (the stack entry with no layers). `norms` is a
+    device int16 view of bf16 [layers][H], `final_norm` of [H]."""
+
+    def __init__(self, ctx, norms, final_norm=None, head=None, vocab: int = 0):
+        self.ctx, self.norms, self.final_norm, self.head, self.vocab = ctx, norms, final_norm, head, vocab
+
+    def _stream(self, t: torch.Tensor):
+        handle = torch.cuda.current_stream(t.device).cuda_stream
+        self.ctx.set_stream(handle if handle else CUDA_STREAM_LEGACY)
+
+    def rms_norm(self, hidden: torch.Tensor, layer: int) -> torch.Tensor:
+        self._stream(hidden)
+        out = torch.empty_like(hidden)
+        T, H = hidden.shape
+        self.ctx.rms_norm_device(hidden.data_ptr(), self.norms[layer].data_ptr(), T, H, 1.0, 1e-6, out.data_ptr())
+        return out
+
+    def residual(self, hidden: torch.Tensor, add: torch.Tensor):
+        self._stream(hidden)
+        self.ctx.residual_add_device(hidden.data_ptr(), add.data_ptr(), hidden.numel())
+
+    def logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        self._stream(hidden)
+        out = torch.empty(hidden.shape[0], self.vocab, dtype=torch.float32, device=hidden.device)
+        self.ctx.moe_stack_forward_device([], 0, self.final_norm.data_ptr(), self.head, hidden.data_ptr(),
+                                          hidden.shape[0], out.data_ptr())
+        return out
+
+
+class ExpertParallelStack:
+    """The MoE stack across the ranks of a group (the decoder layer's MoE
+    half, src/executor.cpp:1513-1531, then finalize_hidden and the head):
+    each rank feeds its own tokens; per layer
+
+        hidden += ExpertParallelMoe_l(rms_norm(hidden, norm_l)),
+
+    every block expert-parallel over the group. `moes` holds one
+    ExpertParallelMoe per layer; `ops` the per-layer steps on this rank
+    (DeviceStackOps on GPUs)."""
+
+    def __init__(self, moes, ops):
+        self.moes, self.ops = moes, ops
+
+    def forward(self, hidden: torch.Tensor, logits: bool = True):
+        """Updates `hidden` [T, H] in place; returns the logits [T, vocab]
+        when `logits`, else None."""
+        for layer, moe in enumerate(self.moes):
+            ff = moe(self.ops.rms_norm(hidden, layer))
+            self.ops.residual(hidden, ff)
+        return self.ops.logits(hidden) if logits else None
+
+    __call__ = forward
+

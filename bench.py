@@ -415,6 +415,74 @@ def stack_c5(ctx, stream, local):
             "decode_graph_ms_per_token": graph_ms, "decode_graph_tokens_per_s": 1e3 / graph_ms}
 
 
+C5_EP_DECODE_STEPS = 32
+
+
+def stack_c5_ep(ctx, stream, local, rank, world):
+    """C5 over `world` ranks: the same 40-layer stack as stack_c5, every
+    block expert-parallel (ExpertParallelStack), each rank feeding its own
+    2048-token prefill in ubatches of 512 and then its own batch-1 decode
+    steps. Times are device events, max over ranks."""
+    from adi_b200 import synthetic
+    from adi_b200.expert_parallel import DevicePhases, DeviceStackOps, ExpertParallelMoe, ExpertParallelStack
+    device = f"cuda:{local}"
+    moes = []
+    for d in range(C5_DISTINCT):
+        b = synthetic.moe_block(seed=8000 + d, device=device)
+        moes.append(ExpertParallelMoe(DevicePhases(ctx, b, rank, world)))
+        del b
+    g = torch.Generator(device=device)
+    g.manual_seed(8100)
+    norms = (torch.randn(C5_LAYERS, 2048, generator=g, device=device) * 0.1).to(torch.bfloat16).view(torch.int16)
+    final = (torch.randn(2048, generator=g, device=device) * 0.1).to(torch.bfloat16).view(torch.int16)
+    head = synthetic.head_chunk(8200, C3_VOCAB, 2048, device=device)
+    head_h = ctx.upload_head(head)
+    del head
+    stack = ExpertParallelStack([moes[l % C5_DISTINCT] for l in range(C5_LAYERS)],
+                                DeviceStackOps(ctx, norms, final, head_h, C3_VOCAB))
+    prompt = synthetic.activations(8300 + rank, C5_PREFILL, 2048, device=device)
+    rows = synthetic.activations(8400 + rank, C5_EP_DECODE_STEPS, 2048, device=device)
+
+    def prefill():
+        hidden = prompt.clone()
+        for a in range(0, C5_PREFILL, C5_UBATCH):
+            stack.forward(hidden[a:a + C5_UBATCH], logits=False)
+        return stack.ops.logits(hidden[C5_PREFILL - 1:])
+
+    def decode(k):
+        return stack.forward(rows[k:k + 1].clone())
+
+    b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    prefill()
+    barrier(world)
+    torch.cuda.synchronize()
+    b.record(stream)
+    prefill()
+    e.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = max_over_ranks(b.elapsed_time(e), world)
+    for k in range(2):
+        decode(k)
+    barrier(world)
+    torch.cuda.synchronize()
+    b.record(stream)
+    for k in range(C5_EP_DECODE_STEPS):
+        decode(k)
+    e.record(stream)
+    torch.cuda.synchronize()
+    decode_ms = max_over_ranks(b.elapsed_time(e), world) / C5_EP_DECODE_STEPS
+    barrier(world)
+    for moe in moes:
+        moe.phases.release()
+    head_h.release()
+    return {"layers": C5_LAYERS, "distinct_weight_sets": C5_DISTINCT, "gpus": world,
+            "per_layer": "rms_norm + expert-parallel MoE block + residual", "head": f"int5_g64 {C3_VOCAB}x2048",
+            "prefill_tokens_per_gpu": C5_PREFILL, "ubatch": C5_UBATCH, "prefill_ms": prefill_ms,
+            "prefill_tokens_per_s": C5_PREFILL * world / (prefill_ms / 1e3),
+            "decode_steps": C5_EP_DECODE_STEPS, "decode_ms_per_step": decode_ms,
+            "decode_tokens_per_s": world / (decode_ms / 1e3)}
+
+
 def zipf_logits(pool: int, tokens: int, experts: int, seed: int, device: str) -> torch.Tensor:
     """C4 router logits [pool, tokens, experts + 1]: log p(rank(e)) +
     Gumbel(0, 1) with p ~ 1 / (rank + 1)^1.1 and the rank permutation drawn
@@ -521,6 +589,7 @@ def run_ep(args, world, rank, local):
         e2e_step(k)
     e2e_s = max_over_ranks(time.perf_counter() - t0, world)
     e2e_value = sum_over_ranks(e2e_steps * T, world) / e2e_s
+    c5 = stack_c5_ep(ctx, stream, local, rank, world) if not args.no_extras else None
 
     if rank == 0:
         line = {
@@ -549,6 +618,8 @@ def run_ep(args, world, rank, local):
             "gpu_launches": launches,
             "clocks": clock_info,
         }
+        if c5 is not None:
+            line["stack_c5"] = c5
         print(json.dumps(line), flush=True)
     barrier(world)
     for moe in layers:

@@ -339,6 +339,16 @@ ADI_CUDA_API int adi_cuda_hadamard(adi_cuda_context *context, float *values, uin
 ADI_CUDA_API int adi_cuda_rms_norm(adi_cuda_context *context, const float *inputs,
                       const uint16_t *weight_bf16, uint32_t count, uint32_t n,
                       float weight_offset, float epsilon, float *outputs);
+/* The same on device pointers (weight_bf16 too), asynchronous on the
+ * context stream; with adi_cuda_residual_add_device (hidden[i] += add[i],
+ * src/executor.cpp:1525-1527; count a multiple of 4, 16-byte aligned) the
+ * per-layer steps of a stack whose blocks run elsewhere (expert-parallel
+ * phases). */
+ADI_CUDA_API int adi_cuda_rms_norm_device(adi_cuda_context *context, const float *inputs,
+                             const uint16_t *weight_bf16, uint32_t count, uint32_t n,
+                             float weight_offset, float epsilon, float *outputs);
+ADI_CUDA_API int adi_cuda_residual_add_device(adi_cuda_context *context, float *hidden,
+                                 const float *add, size_t count);
 
 #ifdef __cplusplus
 }

@@ -107,3 +107,38 @@ def block_with_logits(layer, x: np.ndarray, logits: np.ndarray):
         gate = np.float32(1) / (np.float32(1) + np.exp(-np.float32(logits[t, E])))
         out[t] = acc + gate * shared[t]
     return out, experts, weights
+
+
+class CpuStackOps:
+    """The per-layer steps of ExpertParallelStack on CPU tensors, from the
+    oracle: rms_norm per row (src/kernels.cpp:1052-1073), the residual add,
+    and the final norm plus head."""
+
+    def __init__(self, norms, final_norm, head):
+        self.ora = Oracle()
+        self.norms, self.final_norm, self.head = norms, final_norm, head
+
+    def rms_norm(self, hidden: torch.Tensor, layer: int) -> torch.Tensor:
+        rows = [self.ora.rms_norm(r, self.norms[layer], 1.0, 1e-6) for r in hidden.numpy()]
+        return torch.from_numpy(np.stack(rows).astype(np.float32))
+
+    def residual(self, hidden: torch.Tensor, add: torch.Tensor):
+        hidden += add
+
+    def logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        rows = np.stack([self.ora.rms_norm(r, self.final_norm, 1.0, 1e-6) for r in hidden.numpy()])
+        return torch.from_numpy(self.ora.head_matmul(self.head, rows))
+
+
+def oracle_stack(blocks, norms, final_norm, head, x: np.ndarray):
+    """The stack restated over the oracle's moe_forward, rms_norm and
+    head_matmul, one process: (logits, hidden)."""
+    ora = Oracle()
+    h = x.astype(np.float32).copy()
+    for block, w in zip(blocks, norms):
+        normed = np.stack([ora.rms_norm(r, w, 1.0, 1e-6) for r in h])
+        ff, _, _ = ora.moe_forward(block, normed)
+        h = (h + ff).astype(np.float32)
+    normed = np.stack([ora.rms_norm(r, final_norm, 1.0, 1e-6) for r in h])
+    return ora.head_matmul(head, normed), h
+

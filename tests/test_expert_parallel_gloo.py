@@ -69,3 +69,42 @@ def worker(rank: int, world: int, port: int):
 @pytest.mark.parametrize("world", [2, 4])
 def test_expert_parallel_matches_single_process(world):
     mp.spawn(worker, args=(world, free_port()), nprocs=world, join=True)
+
+
+def stack_worker(rank: int, world: int, port: int):
+    import torch
+    import torch.distributed as dist
+
+    from adi_b200.expert_parallel import ExpertParallelMoe, ExpertParallelStack
+    from ep_cpu_phases import CpuPhases, CpuStackOps, oracle_stack
+    from fixtures import SplitMix64, bf16_bits, head_chunk
+    from oracle_ffi import rel_l2
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        blocks = [moe_layer(seed=60 + l, hidden=256, expert_hidden=64, experts=16, scale_mu=-1.0, shared_mu=-3.0)
+                  for l in range(2)]
+        rng = SplitMix64(61)
+        norms = [bf16_bits(rng.normals(256) * np.float32(0.1)) for _ in blocks]
+        final = bf16_bits(rng.normals(256) * np.float32(0.1))
+        head = head_chunk(300, 256, rng)
+        stack = ExpertParallelStack([ExpertParallelMoe(CpuPhases(b, rank, world)) for b in blocks],
+                                    CpuStackOps(norms, final, head))
+        x = activations(70 + rank, tokens_of(rank), 256)
+        hidden = torch.from_numpy(x.copy())
+        logits = stack(hidden).numpy()
+        want_logits, want_hidden = oracle_stack(blocks, norms, final, head, x)
+        assert rel_l2(hidden.numpy(), want_hidden) <= TOL, (rank, rel_l2(hidden.numpy(), want_hidden))
+        assert rel_l2(logits, want_logits) <= TOL, (rank, rel_l2(logits, want_logits))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_stack_matches_single_process():
+    """ExpertParallelStack over 2 gloo ranks: two layers of rms_norm,
+    expert-parallel block and residual, then the final norm and head, equal
+    on every rank to the one-process restatement of its own tokens."""
+    mp.spawn(stack_worker, args=(2, free_port()), nprocs=2, join=True)
+

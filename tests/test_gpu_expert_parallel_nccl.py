@@ -66,3 +66,64 @@ def test_two_ranks_over_nccl(precision):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     mp.spawn(worker, args=(2, free_port(), precision), nprocs=2, join=True)
+
+
+def stack_worker(rank: int, world: int, port: int):
+    import torch.distributed as dist
+
+    import adi_b200
+    from adi_b200.expert_parallel import DevicePhases, DeviceStackOps, ExpertParallelMoe, ExpertParallelStack
+    from fixtures import SplitMix64, bf16_bits, head_chunk
+    from oracle_ffi import rel_l2
+
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    ctx = adi_b200.Context(rank)
+    errors = []
+    try:
+        ctx.set_precision(1)
+        torch.cuda.set_stream(torch.cuda.Stream())
+        blocks = [moe_layer(seed=70 + l) for l in range(2)]
+        rng = SplitMix64(71)
+        norms = np.stack([bf16_bits(rng.normals(2048) * np.float32(0.1)) for _ in blocks])
+        final = bf16_bits(rng.normals(2048) * np.float32(0.1))
+        head = head_chunk(1000, 2048, rng)
+        norms_d = torch.from_numpy(norms.view(np.int16)).cuda()
+        final_d = torch.from_numpy(final.view(np.int16)).cuda()
+        head_h = ctx.upload_head(head)
+        phases = [DevicePhases(ctx, b, rank, world) for b in blocks]
+        stack = ExpertParallelStack([ExpertParallelMoe(p) for p in phases],
+                                    DeviceStackOps(ctx, norms_d, final_d, head_h, head.rows))
+        x = activations(95 + rank, 48 * (rank + 1), 2048)
+        hidden = torch.from_numpy(x).cuda()
+        logits = stack(hidden).cpu().numpy()
+        # The same tokens through the one-GPU stack entry.
+        full = [ctx.upload_moe_layer(b) for b in blocks]
+        ref_hidden = torch.from_numpy(x).cuda()
+        ref_logits = torch.empty(x.shape[0], head.rows, device="cuda")
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        ctx.moe_stack_forward_device(full, norms_d.data_ptr(), final_d.data_ptr(), head_h, ref_hidden.data_ptr(),
+                                     x.shape[0], ref_logits.data_ptr())
+        torch.cuda.synchronize()
+        errors.append(rel_l2(hidden.cpu().numpy(), ref_hidden.cpu().numpy()))
+        errors.append(rel_l2(logits, ref_logits.cpu().numpy()))
+        for h in full + [head_h]:
+            h.release()
+        for p in phases:
+            p.release()
+        dist.barrier()
+    finally:
+        ctx.close()
+        dist.destroy_process_group()
+    assert max(errors) <= 10 * SAME, (rank, errors)
+
+
+def test_stack_two_ranks_over_nccl():
+    """ExpertParallelStack over NCCL: two configured layers, each rank's
+    logits equal to the one-GPU stack entry on its own tokens."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.spawn(stack_worker, args=(2, free_port()), nprocs=2, join=True)
+

@@ -1140,6 +1140,8 @@ template <int V>
 __global__ void top_experts_regs_kernel(float *logits, uint32_t stride, uint32_t tokens, uint32_t experts,
                                         uint32_t *route_experts, float *route_weights, const float *partials,
                                         uint32_t parts, uint32_t rows_pad) {
+    griddep_launch_dependents();
+    griddep_wait();
     const uint32_t token = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const uint32_t lane = threadIdx.x & 31u;
     if (token >= tokens) return;
@@ -1269,11 +1271,11 @@ bool launch_top_experts_parts(const float *partials, uint32_t parts, uint32_t ro
     // over every SM.
     const uint32_t blocks = (tokens + 1) / 2;
     if (experts <= 256)
-        top_experts_regs_kernel<8><<<blocks, 64, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
-                                                        route_weights, partials, parts, rows_pad);
+        launch_pdl(top_experts_regs_kernel<8>, blocks, 64, 0, s, logits, logit_stride, tokens, experts,
+                   route_experts, route_weights, partials, parts, rows_pad);
     else if (experts <= 1024)
-        top_experts_regs_kernel<32><<<blocks, 64, 0, s>>>(logits, logit_stride, tokens, experts, route_experts,
-                                                         route_weights, partials, parts, rows_pad);
+        launch_pdl(top_experts_regs_kernel<32>, blocks, 64, 0, s, logits, logit_stride, tokens, experts,
+                   route_experts, route_weights, partials, parts, rows_pad);
     else
         return false;
     return true;
@@ -1494,6 +1496,8 @@ __device__ __forceinline__ void block_scan2_1024(uint32_t &a, uint32_t &b, uint3
 // one contiguous run. The per-expert bitmaps are [E][words | 1] so that a
 // thread per expert walks its own row without bank conflicts.
 __global__ void __launch_bounds__(1024) route_block_kernel(RouteParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     extern __shared__ uint32_t route_smem[];
     const uint32_t t = threadIdx.x, n = p.tokens * 8, wp = p.words | 1u, bw = p.experts * wp;
     uint32_t *bitmap = route_smem;                       // [E][wp]
@@ -1602,7 +1606,7 @@ uint32_t launch_route(const RouteParams &p, cudaStream_t s) {
                                  (int)kRouteBlockSmemLimit);
             configured = true;
         }
-        route_block_kernel<<<1, 1024, block_smem, s>>>(p);
+        launch_pdl(route_block_kernel, 1, 1024, block_smem, s, p);
         return 1;
     }
     cudaMemsetAsync(p.counts, 0, sizeof(uint32_t) * p.experts, s);
@@ -1788,6 +1792,8 @@ __global__ void __launch_bounds__(256) combine_regs_kernel(CombineParams p) {
 // the same route-order sums per element as combine_regs_kernel<8>, and
 // stores of 128 contiguous bytes per warp.
 __global__ void __launch_bounds__(256) combine_2048_kernel(CombineParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ float sh[2048 + 64];
     constexpr uint32_t H = 2048;
     const uint32_t t = blockIdx.x, c0 = threadIdx.x * 8;

@@ -114,6 +114,32 @@ __device__ __forceinline__ void bulk_load_pieces(void *dst, const void *src, uin
                   bytes - off < 32768u ? bytes - off : 32768u, bar);
 }
 
+// Programmatic dependent launch. A kernel launched with launch_pdl may
+// start while the kernel before it in the stream is still running; it must
+// call griddep_wait() before it reads anything an earlier kernel wrote (the
+// wait returns once the previous grid has completed and its writes are
+// visible, and immediately when the launch was an ordinary one). A kernel
+// calls griddep_launch_dependents() to let the next grid's blocks be
+// scheduled once all of its own blocks have started.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+template <typename... KernelArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+    cudaLaunchConfig_t config = {};
+    config.gridDim = grid;
+    config.blockDim = block;
+    config.dynamicSmemBytes = smem;
+    config.stream = stream;
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[0].val.programmaticStreamSerializationAllowed = 1;
+    config.attrs = attribute;
+    config.numAttrs = 1;
+    return cudaLaunchKernelEx(&config, kernel, static_cast<KernelArgs>(args)...);
+}
+
 __device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }

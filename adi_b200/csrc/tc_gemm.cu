@@ -285,6 +285,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     const uint32_t half = T::halves == 2 ? (blockIdx.x & 1u) : 0u;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    griddep_launch_dependents();
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < kWordStages; ++s) {
@@ -332,6 +333,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncthreads();
     }
 
+    // Everything above reads only this launch's own arguments and the value
+    // table; the work list, positions and B operand come from the kernels
+    // before this one.
+    griddep_wait();
     const uint32_t n_units = unit_count(p);
     const uint32_t first = T::halves == 2 ? blockIdx.x >> 1 : blockIdx.x;
     const uint32_t stride = T::halves == 2 ? gridDim.x >> 1 : gridDim.x;
@@ -666,6 +671,7 @@ constexpr uint32_t kRouterBTile = kRouterN * kChunkK * 2;  // 8 KiB
 constexpr size_t kRouterSmem = kRouterStages * (kRouterATile + kRouterBTile) + (2 * kRouterStages + 1) * 8 + 16;
 
 __global__ void router_split_kernel(const float *x, uint32_t count, uint32_t H, uint16_t *xs) {
+    griddep_launch_dependents();
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) {
         const uint32_t t = i / H, k = i - t * H;
         const float v = x[i];
@@ -698,6 +704,7 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t chunks = p.k / kChunkK, per_part = (chunks + p.parts - 1) / p.parts;
     const uint32_t kc0 = part * per_part, kc1 = min(chunks, kc0 + per_part);
     const uint32_t n0 = nc * kRouterN, n = min(kRouterN, p.tokens - n0), n_pad = (n + 15u) & ~15u;
+    griddep_launch_dependents();
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < kRouterStages; ++s) {
             mbar_init(&full[s], 1);
@@ -715,6 +722,7 @@ __global__ void __launch_bounds__(192, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    griddep_wait();  // the split activations come from the kernel before
 
     if (warp == 0 && lane == 0) {
         Ring r;
@@ -841,7 +849,7 @@ bool launch_codec(const CUtensorMap &map0, const CUtensorMap &map1, const TcPara
     CUtensorMap wmap0, wmap1;
     if (!make_word_map<C>(&wmap0, p.job[0]) || !make_word_map<C>(&wmap1, p.job[1])) return false;
     if (C == TcCodec::kExpert) grid &= ~1;
-    tc_gemm_kernel<C><<<grid, kTcThreads, Smem<C>::total, s>>>(map0, map1, wmap0, wmap1, p);
+    launch_pdl(tc_gemm_kernel<C>, grid, kTcThreads, Smem<C>::total, s, map0, map1, wmap0, wmap1, p);
     return true;
 }
 
@@ -1056,6 +1064,8 @@ __global__ void __launch_bounds__(256) prep_f16_regs_kernel(PrepF16Params p) {
 // reach the same f16 columns, written one half per element (each warp's
 // 32 elements are two runs of 16 contiguous halves in the split layout).
 __global__ void __launch_bounds__(256) prep_f16_2048_kernel(PrepF16Params p) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ float sh[2048 + 64];
     __shared__ float scratch[32];
     constexpr uint32_t n = 2048;
@@ -1183,6 +1193,8 @@ __device__ __forceinline__ uint4 pack_half8(const float *v, float s) {
 // 16l .. 16l+15 land in the split layout as two runs of eight halves (one
 // 16-byte store each).
 __global__ void __launch_bounds__(256) mid_f16_warp_kernel(MidF16Params p) {
+    griddep_launch_dependents();
+    griddep_wait();
     constexpr uint32_t n = 512;
     const uint32_t pos = blockIdx.x * 8u + (threadIdx.x >> 5), lane = threadIdx.x & 31u;
     if (pos >= p.positions) return;  // whole warps leave together
@@ -1252,7 +1264,7 @@ void launch_prep_f16(const PrepF16Params &p, cudaStream_t s) {
     switch (p.cols) {
         case 512: prep_f16_regs_kernel<2><<<p.rows, 256, 0, s>>>(p); return;
         case 1024: prep_f16_regs_kernel<4><<<p.rows, 256, 0, s>>>(p); return;
-        case 2048: prep_f16_2048_kernel<<<p.rows, 256, 0, s>>>(p); return;
+        case 2048: launch_pdl(prep_f16_2048_kernel, p.rows, 256, 0, s, p); return;
         default: prep_f16_kernel<<<grid, 256, p.cols * sizeof(float), s>>>(p);
     }
 }
@@ -1260,7 +1272,7 @@ void launch_prep_f16(const PrepF16Params &p, cudaStream_t s) {
 void launch_mid_f16(const MidF16Params &p, cudaStream_t s) {
     if (p.positions == 0) return;
     switch (p.inner) {
-        case 512: mid_f16_warp_kernel<<<(p.positions + 7) / 8, 256, 0, s>>>(p); return;
+        case 512: launch_pdl(mid_f16_warp_kernel, (p.positions + 7) / 8, 256, 0, s, p); return;
         case 1024: mid_f16_regs_kernel<4><<<p.positions, 256, 0, s>>>(p); return;
         case 2048: mid_f16_regs_kernel<8><<<p.positions, 256, 0, s>>>(p); return;
         default: mid_f16_kernel<<<p.positions, 256, 2 * p.inner * sizeof(float), s>>>(p);
@@ -1304,7 +1316,7 @@ bool launch_router_tc(const RouterParams &p, const float *x, uint16_t *xs, const
         configured = true;
     }
     const uint32_t units = (p.rows_pad / 128) * ((p.tokens + kRouterN - 1) / kRouterN) * p.parts;
-    router_gemm_kernel<<<units, 192, kRouterSmem, s>>>(amap, bmap, p);
+    launch_pdl(router_gemm_kernel, units, 192, kRouterSmem, s, amap, bmap, p);
     if (logits)
         router_reduce_kernel<<<592, 256, 0, s>>>(p.partials, p.parts, p.tokens, p.rows_pad, rows, logits, stride);
     return true;

@@ -536,8 +536,6 @@ def run_ep(args, world, rank, local):
         step(i)
         touched.append(int((layers[i % L].last_received > 0).sum()))
 
-    # Only the expert GEMM launches are bracketed in the timed region.
-    ctx.set_profiling(2)
     for k in range(max(args.warmup, 1)):
         step(k)
     torch.cuda.synchronize()
@@ -554,11 +552,10 @@ def run_ep(args, world, rank, local):
     torch.cuda.synchronize()
     barrier(world)
     clock_info = clocks.stop()
-    ctx.set_profiling(False)
     launches = ctx.launch_count() - launches0
     ms = begin.elapsed_time(end)
     ms_max = max_over_ranks(ms, world)
-    stages = ctx.profile()
+    stages = gemm_pass(ctx, step, args.steps)
     all_stages = stage_breakdown(ctx, step, min(args.steps, 200))
     value = sum_over_ranks(args.steps * T, world) / (ms_max / 1e3)
     n_touched = [touched[k % (pool * L)] for k in range(args.steps)]
@@ -668,10 +665,8 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     touched_per_step = {i: touched[i] for i in range(len(touched))}
 
-    # The timed region brackets only the routed expert GEMM launches with
-    # events (for the roofline's live kernel time); the warm-up runs the same
-    # way so that the timed region reuses pooled events.
-    ctx.set_profiling(2)
+    # The timed region runs with no events between kernels (they would break
+    # the programmatic launch overlap between consecutive kernels).
     for k in range(max(args.warmup, 1)):
         step(k)
     torch.cuda.synchronize()
@@ -688,11 +683,10 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     barrier(world)
     clock_info = clocks.stop()
-    ctx.set_profiling(False)
     launches = ctx.launch_count() - launches0
     ms = begin.elapsed_time(end)
     ms_max = max_over_ranks(ms, world)
-    stages = ctx.profile()
+    stages = gemm_pass(ctx, step, args.steps)
     all_stages = stage_breakdown(ctx, step, min(args.steps, 200))
     n_touched = [touched_per_step[k % (pool * L)] if (k % (pool * L)) in touched_per_step else touched[0]
                  for k in range(args.steps)]
@@ -855,6 +849,19 @@ def run_ours(args, world, rank, local):
     for h in handles:
         h.release()
     ctx.close()
+
+
+def gemm_pass(ctx, step, steps):
+    """The timed steps again with only the routed expert GEMM launches
+    bracketed by events: the live kernel time of the roofline."""
+    ctx.set_profiling(2)
+    ctx.reset_profile()
+    for k in range(steps):
+        step(k)
+    torch.cuda.synchronize()
+    stages = ctx.profile()
+    ctx.set_profiling(False)
+    return stages
 
 
 def stage_breakdown(ctx, step, steps):

@@ -471,6 +471,10 @@ constexpr uint32_t kSplitCombineTokens = 64;
 
 // Below this many inputs an NE projection streams faster on CUDA cores.
 constexpr uint32_t kNeTensorCoreMinBatch = 16;
+// Below this many tokens the router is a matrix-vector product bound by its
+// 1 MiB of weights: the CUDA-core kernel reads them once, while the
+// tensor-core path pays for its split, its K parts and their reduction.
+constexpr uint32_t kRouterTensorCoreMinTokens = 64;
 
 // K parts for a dense NE tensor-core launch of `units` units: two when that
 // still fits the SMs (so that small launches use twice the SMs, the two
@@ -832,15 +836,16 @@ void shared_expert_beside(adi_cuda_context *c, MoeDev &L, const float *in, uint3
 }
 
 // Router and shared-gate logits [T][E+1] and the top-8 routes: on tensor
-// cores in precision mode 1 (exact three-term bf16 split of the
-// activations, fp32 accumulation, the split-K partials summed in order by
-// the top-k kernel as it reads them), else the CUDA-core fp32 kernel and the
-// top-k over its logits. Returns the kernels launched.
+// cores in precision mode 1 from kRouterTensorCoreMinTokens tokens on
+// (exact three-term bf16 split of the activations, fp32 accumulation, the
+// split-K partials summed in order by the top-k kernel as it reads them),
+// else the CUDA-core fp32 kernel and the top-k over its logits. Returns the
+// kernels launched.
 uint32_t route_tokens(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *logits, uint32_t *re,
                       float *rw) {
     const uint32_t H = L.hidden, E = L.experts;
     c->stage(kStageRouter);
-    if (c->precision == 1 && H % 64 == 0) {
+    if (c->precision == 1 && H % 64 == 0 && T >= kRouterTensorCoreMinTokens) {
         RouterParams rp{};
         rp.rows_pad = L.router_rows_pad;
         rp.tokens = T;

@@ -139,20 +139,27 @@ __global__ void ep_finalize_kernel(EpFinalizeParams p) {
 }
 
 template <int R>
-__global__ void __launch_bounds__(256) ep_combine_regs_kernel(EpCombineParams p) {
+__global__ void __launch_bounds__(256, 4) ep_combine_regs_kernel(EpCombineParams p) {
     __shared__ float sh[256 * R];
     constexpr uint32_t H = 256u * R;
     const uint32_t t = blockIdx.x, c0 = threadIdx.x * R;
     float out[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) out[r] = 0.0f;
-    for (int k = 0; k < 8; ++k) {
-        const uint32_t pos = p.route_to_grouped[t * 8 + k];
-        const float w = p.route_weights[t * 8 + k];
-        float v[R];
-        load_regs<R>(p.returned + (size_t)pos * H + c0, v);
+    // The route rows load four at a time, so their latencies overlap; the
+    // sum stays in route order.
 #pragma unroll
-        for (int r = 0; r < R; ++r) out[r] = fmaf(w, v[r], out[r]);
+    for (int k0 = 0; k0 < 8; k0 += 4) {
+        float rows[4][R];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            load_regs<R>(p.returned + (size_t)p.route_to_grouped[t * 8 + k0 + j] * H + c0, rows[j]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float w = p.route_weights[t * 8 + k0 + j];
+#pragma unroll
+            for (int r = 0; r < R; ++r) out[r] = fmaf(w, rows[j][r], out[r]);
+        }
     }
     float v[R];
     load_regs<R>(p.shared_acc + (size_t)t * H + c0, v);

@@ -86,6 +86,19 @@ def test_moe_block_tensor_cores(tensor_cores, oracle, heavy_layer, tokens):
     assert checked >= 8
 
 
+@pytest.mark.parametrize("tokens", [16, 64, 512])
+def test_router_routes_tensor_cores(tensor_cores, oracle, heavy_layer, tokens):
+    """Every token's top-8 in precision mode 1 (the CUDA-core router below 64
+    tokens, the split-bf16 tensor-core router with the partial sums folded
+    into the top-k from 64 on) equals the oracle's, except at the oracle's
+    own near-ties; the weights agree to the logit rounding noise."""
+    from test_gpu_moe import check_routes
+    layer, handle = heavy_layer
+    x = activations(450 + tokens, tokens, layer.hidden)
+    _, experts, weights = tensor_cores.moe_forward_batch(handle, x)
+    assert check_routes(oracle, layer, x, experts, weights) <= max(1, tokens // 128)
+
+
 def test_moe_block_tensor_cores_configured_scales(tensor_cores, oracle):
     """The configured block (scale surfaces log-normal mu=-4) at ubatch 512."""
     ctx = tensor_cores

@@ -19,6 +19,7 @@
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
 
 using namespace adi_cuda;
@@ -92,6 +93,104 @@ std::unique_ptr<DeviceArray> upload_bytes(const void *host, size_t bytes, const 
     if (bytes) check(cudaMemcpy(a->ptr, host, bytes, cudaMemcpyHostToDevice), "upload");
     return a;
 }
+
+// Host arrays streamed into one device array through two pinned staging
+// buffers: host threads gather the next buffer's pieces while the previous
+// buffer's copy runs, so the upload of a block's packed weights costs about
+// the larger of the host gather and the PCIe copy instead of their sum (the
+// weights come from caller memory, e.g. the model file's mapping, which the
+// copy engine cannot read directly).
+class Stager {
+  public:
+    static constexpr size_t kBufferBytes = size_t(16) << 20;
+    static constexpr unsigned kThreads = 4;
+
+    ~Stager() {
+        for (int i = 0; i < 2; ++i) {
+            if (done_[i]) cudaEventDestroy(done_[i]);
+            if (pinned_[i]) cudaFreeHost(pinned_[i]);
+        }
+        if (stream_) cudaStreamDestroy(stream_);
+    }
+
+    struct Piece {
+        const void *src;
+        size_t bytes;
+    };
+
+    // Copies the pieces, in order and back to back, to `dst` (device).
+    void gather(void *dst, const std::vector<Piece> &pieces) {
+        setup();
+        uint8_t *out = static_cast<uint8_t *>(dst);
+        size_t next = 0, offset_in_piece = 0;
+        int b = 0;
+        while (next < pieces.size()) {
+            check(cudaEventSynchronize(done_[b]), "staging buffer");
+            // Fill buffer b with up to kBufferBytes of the remaining pieces.
+            std::vector<Copy> copies;
+            size_t filled = 0;
+            while (next < pieces.size() && filled < kBufferBytes) {
+                const Piece &pc = pieces[next];
+                const size_t n = std::min(pc.bytes - offset_in_piece, kBufferBytes - filled);
+                copies.push_back({pinned_[b] + filled, static_cast<const uint8_t *>(pc.src) + offset_in_piece, n});
+                filled += n;
+                offset_in_piece += n;
+                if (offset_in_piece == pc.bytes) {
+                    ++next;
+                    offset_in_piece = 0;
+                }
+            }
+            host_copy(copies, filled);
+            check(cudaMemcpyAsync(out, pinned_[b], filled, cudaMemcpyHostToDevice, stream_), "upload");
+            check(cudaEventRecord(done_[b], stream_), "cudaEventRecord");
+            out += filled;
+            b ^= 1;
+        }
+        check(cudaStreamSynchronize(stream_), "upload");
+    }
+
+  private:
+    struct Copy {
+        uint8_t *dst;
+        const uint8_t *src;
+        size_t bytes;
+    };
+
+    void setup() {
+        if (stream_) return;
+        check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+        for (int i = 0; i < 2; ++i) {
+            check(cudaHostAlloc(&pinned_[i], kBufferBytes, cudaHostAllocDefault), "cudaHostAlloc");
+            check(cudaEventCreateWithFlags(&done_[i], cudaEventDisableTiming), "cudaEventCreate");
+            check(cudaEventRecord(done_[i], stream_), "cudaEventRecord");
+        }
+    }
+
+    // The copies of one buffer, split into byte ranges over kThreads threads
+    // when there is enough to share.
+    static void host_copy(const std::vector<Copy> &copies, size_t total) {
+        if (total < (size_t(1) << 20)) {
+            for (const Copy &cp : copies) std::memcpy(cp.dst, cp.src, cp.bytes);
+            return;
+        }
+        auto run = [&](size_t lo, size_t hi) {
+            size_t at = 0;
+            for (const Copy &cp : copies) {
+                const size_t a = std::max(lo, at), e = std::min(hi, at + cp.bytes);
+                if (a < e) std::memcpy(cp.dst + (a - at), cp.src + (a - at), e - a);
+                at += cp.bytes;
+            }
+        };
+        std::vector<std::thread> pool;
+        for (unsigned t = 1; t < kThreads; ++t) pool.emplace_back(run, total * t / kThreads, total * (t + 1) / kThreads);
+        run(0, total / kThreads);
+        for (std::thread &th : pool) th.join();
+    }
+
+    uint8_t *pinned_[2] = {};
+    cudaEvent_t done_[2] = {};
+    cudaStream_t stream_ = nullptr;
+};
 
 // Exact f16 -> f32 on the host (same result as the device conversion).
 float host_f16(uint16_t bits) {
@@ -291,6 +390,7 @@ struct adi_cuda_context {
     uint64_t ep_layer = 0;
     uint32_t ep_tokens = 0;
     Profiler profiler;
+    Stager stager;
     void stage(int st) { profiler.begin(st, stream); }
     void stage_end() { profiler.end(stream); }
     // Scratch arena, grown on demand.
@@ -1118,7 +1218,6 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     float *logits = c->buffer<float>("moe_logits", size_t(T) * (E + 1));
     uint32_t *re = route_experts_out ? route_experts_out : c->buffer<uint32_t>("moe_re", P);
     float *rw = route_weights_out ? route_weights_out : c->buffer<float>("moe_rw", P);
-    const uint32_t router_launches = route_tokens(c, L, in, T, logits, re, rw);
 
     RouteParams rp{};
     rp.route_experts = re;
@@ -1146,6 +1245,7 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     uint32_t *counts2 = c->buffer<uint32_t>("moe_item_counts", 2);
     rp.count_gate_up = counts2;
     rp.count_down = counts2 + 1;
+    const uint32_t router_launches = route_tokens(c, L, in, T, logits, re, rw);
     c->stage(kStageRoute);
     const uint32_t route_launches = launch_route(rp, s);
     c->stage_end();
@@ -1259,23 +1359,29 @@ uint64_t upload_moe(adi_cuda_context *c, const adi_moe_layer &layer, uint32_t fi
     for (int p = 0; p < 3; ++p) {
         const uint32_t rows = p == 2 ? H : I, cols = p == 2 ? I : H;
         const size_t tw = size_t(tiles) * 24, gw = rows / 16 + cols / 16;
-        std::vector<uint16_t> trellis(tw * count), su(size_t(cols) * count), sv(size_t(rows) * count),
-            gamma(gw * count);
+        std::vector<Stager::Piece> trellis, su, sv, gamma;
         for (uint32_t i = 0; i < count; ++i) {
             const adi_expert_matrix &m = l->routed[3 * size_t(first + i) + p];
             if (m.rows != rows || m.columns != cols) invalid("MoE routed expert shape mismatch");
             if (!m.trellis || !m.su_f16 || !m.sv_f16 || !m.wave_gamma_f16)
                 invalid("Mach expert codec tensor shape mismatch");
             if (m.tlut != tlut) invalid("MoE routed experts must share one TLUT");
-            std::memcpy(trellis.data() + i * tw, m.trellis, tw * 2);
-            std::memcpy(su.data() + size_t(i) * cols, m.su_f16, size_t(cols) * 2);
-            std::memcpy(sv.data() + size_t(i) * rows, m.sv_f16, size_t(rows) * 2);
-            std::memcpy(gamma.data() + i * gw, m.wave_gamma_f16, gw * 2);
+            trellis.push_back({m.trellis, tw * 2});
+            su.push_back({m.su_f16, size_t(cols) * 2});
+            sv.push_back({m.sv_f16, size_t(rows) * 2});
+            gamma.push_back({m.wave_gamma_f16, gw * 2});
         }
-        d->trellis[p] = upload_bytes(trellis.data(), trellis.size() * 2, "trellis");
-        d->su[p] = upload_bytes(su.data(), su.size() * 2, "su");
-        d->sv[p] = upload_bytes(sv.data(), sv.size() * 2, "sv");
-        d->gamma[p] = upload_bytes(gamma.data(), gamma.size() * 2, "gamma");
+        // Expert-major, byte for byte: one device array per kind, the
+        // experts' arrays back to back.
+        auto upload = [&](std::unique_ptr<DeviceArray> &dst, const std::vector<Stager::Piece> &pieces, size_t bytes) {
+            dst = std::make_unique<DeviceArray>();
+            dst->reserve(bytes);
+            c->stager.gather(dst->ptr, pieces);
+        };
+        upload(d->trellis[p], trellis, tw * 2 * count);
+        upload(d->su[p], su, size_t(cols) * 2 * count);
+        upload(d->sv[p], sv, size_t(rows) * 2 * count);
+        upload(d->gamma[p], gamma, gw * 2 * count);
     }
     d->codec = c->expert_codec(tlut);
     for (int p = 0; p < 3; ++p) {
@@ -1317,18 +1423,6 @@ void ep_dispatch_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const floa
     float *logits = c->buffer<float>("ep_logits", size_t(T) * (E + 1));
     uint32_t *re = c->buffer<uint32_t>("ep_re", P);
     float *rw = c->buffer<float>("ep_rw", P);
-    if (given_logits) {
-        c->stage(kStageRouter);
-        check(cudaMemcpyAsync(logits, given_logits, size_t(T) * (E + 1) * 4, cudaMemcpyDeviceToDevice, s),
-              "logits copy");
-        c->stage_end();
-        c->stage(kStageTopk);
-        launch_top_experts(logits, E + 1, T, E, re, rw, s);
-        c->stage_end();
-        c->after_launch(1);
-    } else {
-        c->after_launch(route_tokens(c, L, in, T, logits, re, rw));
-    }
 
     // The counting sort only: no work lists (row_blocks 0), large chunks so
     // the scan's per-expert loop is short.
@@ -1348,6 +1442,18 @@ void ep_dispatch_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const floa
     uint32_t *counts2 = c->buffer<uint32_t>("ep_item_counts", 2);
     rp.count_gate_up = counts2;
     rp.count_down = counts2 + 1;
+    if (given_logits) {
+        c->stage(kStageRouter);
+        check(cudaMemcpyAsync(logits, given_logits, size_t(T) * (E + 1) * 4, cudaMemcpyDeviceToDevice, s),
+              "logits copy");
+        c->stage_end();
+        c->stage(kStageTopk);
+        launch_top_experts(logits, E + 1, T, E, re, rw, s);
+        c->stage_end();
+        c->after_launch(1);
+    } else {
+        c->after_launch(route_tokens(c, L, in, T, logits, re, rw));
+    }
     c->stage(kStageRoute);
     const uint32_t route_launches = launch_route(rp, s);
     launch_ep_gather(in, rp.grouped, uint32_t(P), H, send, s);

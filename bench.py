@@ -640,10 +640,12 @@ def run_ours(args, world, rank, local):
     ctx.set_precision(args.precision)
     T, L = args.tokens, args.layers
 
-    blocks, handles = [], []
+    blocks, handles, upload_s = [], [], []
     for layer in range(L):
         block = synthetic.moe_block(seed=1000 * rank + layer, device=f"cuda:{local}")
+        t0 = time.perf_counter()
         handles.append(ctx.upload_moe_layer(block))
+        upload_s.append(time.perf_counter() - t0)
         blocks.append(block if layer == 0 else None)
         del block
     H, E = blocks[0].hidden, blocks[0].experts
@@ -717,6 +719,9 @@ def run_ours(args, world, rank, local):
             h.release()
         ctx.close()
         return
+
+    upload_bytes = blocks[0].shared_bytes() + E * blocks[0].packed_bytes_per_expert()
+    upload_ms = 1e3 * (min(upload_s[1:]) if len(upload_s) > 1 else upload_s[0])
 
     # End to end through the host-pointer C ABI, pinned host buffers.
     x_host = torch.empty(pool, T, H, dtype=torch.float32, pin_memory=True)
@@ -840,6 +845,10 @@ def run_ours(args, world, rank, local):
             "stack_c5": c5,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
                     "d2h_bytes_per_step": T * H * 4 + T * 8 * 8, "steps": e2e_steps},
+            # One block's upload through adi_cuda_upload_moe_layer (host arrays
+            # to HBM, byte for byte), after the first, which sets up the
+            # staging buffers.
+            "upload": {"block_bytes": upload_bytes, "ms": upload_ms, "gbs": upload_bytes / upload_ms / 1e6},
             "gpu_launches": launches,
             "clocks": clock_info,
         }

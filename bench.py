@@ -56,7 +56,7 @@ GAMMA_BYTES = 160 * 2
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
 # tensor-core expert GEMM, averaged over the gate/up and down launches of one
 # 512-token block, from one ncu capture (profiles/tc_gemm_expert_t512.md).
-EXPERT_GEMM_TRAFFIC_T512 = (134.808064e6 + 19.59936e6 + 55.002112e6 + 23.05024e6) / 2
+EXPERT_GEMM_TRAFFIC_T512 = (134.818560e6 + 20.356608e6 + 55.004928e6 + 19.981824e6) / 2
 
 
 def parse():

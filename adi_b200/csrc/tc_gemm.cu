@@ -63,10 +63,10 @@ constexpr uint32_t kBBoxRows = 16;                    // TMA box height: B loads
 constexpr uint32_t kChunkK = 64;                     // f16 columns of one 128-byte swizzled B sub-tile
 constexpr uint32_t kATileBytes = 128 * kChunkK * 2;  // 16 KiB (NE: A in shared memory)
 constexpr uint32_t kBSubTileBytes = kTcMaxN * kChunkK * 2;
-constexpr uint32_t kDecodeWarps = 16;
 constexpr uint32_t kDecodeWarp0 = 3;
-constexpr uint32_t kEpilogueWarp0 = kDecodeWarp0 + kDecodeWarps;
-constexpr uint32_t kTcThreads = (kEpilogueWarp0 + 4) * 32;
+#ifndef ADI_TC_EXPERT_DECODE_WARPS
+#define ADI_TC_EXPERT_DECODE_WARPS 16
+#endif
 // Tensor memory: two accumulator slots of kTcMaxN columns, then (expert
 // codec) kTmemAStages A slots of one chunk each (128 lanes x 128 f16 = 64
 // columns).
@@ -83,6 +83,9 @@ struct Traits;
 template <>
 struct Traits<TcCodec::kExpert> {
     static constexpr uint32_t halves = 2;
+    // Decode warps: four lane quarters (TMEM lanes) times the warps that
+    // split a chunk's 16 tile columns between them.
+    static constexpr uint32_t decode_warps = ADI_TC_EXPERT_DECODE_WARPS;
     static constexpr uint32_t chunk_cols = 256;          // matrix columns per chunk (128 packed)
     static constexpr uint32_t k_sub = 2;
     static constexpr uint32_t tile_bytes = 48;
@@ -105,6 +108,7 @@ struct Traits<TcCodec::kExpert> {
 template <>
 struct Traits<TcCodec::kNe> {
     static constexpr uint32_t halves = 1;
+    static constexpr uint32_t decode_warps = 16;
     static constexpr uint32_t chunk_cols = 64;
     static constexpr uint32_t k_sub = 1;
     static constexpr uint32_t tile_bytes = 128;
@@ -119,6 +123,16 @@ struct Traits<TcCodec::kNe> {
     static constexpr uint32_t tmem_a_columns = 0;
     static constexpr uint32_t tmem_columns = 256;
 };
+
+// Warp roles: word producer, MMA, B producer, the decoders, 4 epilogue warps.
+template <TcCodec C>
+constexpr uint32_t tc_threads() {
+    return (kDecodeWarp0 + Traits<C>::decode_warps + 4) * 32;
+}
+static_assert(Traits<TcCodec::kExpert>::decode_warps % 4 == 0 &&
+                  Traits<TcCodec::kExpert>::tiles_per_row % (Traits<TcCodec::kExpert>::decode_warps / 4) == 0 &&
+                  16 % (Traits<TcCodec::kExpert>::tiles_per_row / (Traits<TcCodec::kExpert>::decode_warps / 4)) == 0,
+              "expert decode warps");
 
 template <TcCodec C>
 struct Smem {
@@ -260,7 +274,7 @@ struct Ring {
 }  // namespace
 
 template <TcCodec C>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(tc_threads<C>(), 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1,
                    const __grid_constant__ CUtensorMap wmap0, const __grid_constant__ CUtensorMap wmap1,
                    const TcParams p) {
@@ -290,14 +304,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < kWordStages; ++s) {
             mbar_init(&w_full[s], 1);
-            mbar_init(&w_empty[s], kDecodeWarps);
+            mbar_init(&w_empty[s], T::decode_warps);
         }
         for (uint32_t s = 0; s < kBStages; ++s) {
             mbar_init(&b_full[s], 1);
             mbar_init(&b_empty[s], 1);
         }
         for (uint32_t s = 0; s < T::a_stages; ++s) {
-            mbar_init(&a_ready[s], kDecodeWarps);
+            mbar_init(&a_ready[s], T::decode_warps);
             mbar_init(&a_empty[s], 1);
         }
         for (uint32_t s = 0; s < 2; ++s) {
@@ -453,7 +467,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mma_commit(mma_done);
             mbar_wait_own(mma_done, 0, p.error);
         }
-    } else if (warp < kEpilogueWarp0) {
+    } else if (warp < kDecodeWarp0 + T::decode_warps) {
         // ---- decoders ----
         const uint32_t dw = warp - kDecodeWarp0;
         Ring w, a;
@@ -462,30 +476,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint2 *table = reinterpret_cast<const uint2 *>(smem);
             // Lane = weight row of the chunk = TMEM lane: this warp may only
             // reach lanes 32*(warp % 4) .. +31, i.e. tile rows tr0, tr0 + 1.
-            // The four warps of a lane quarter split the chunk's 16 tile
-            // columns in fours: warp `quad` decodes tile columns 4*quad ..
-            // 4*quad + 3. In a tile, a row is states 2*rl and 2*rl + 1, stream
-            // bits 24*rl .. 24*rl + 28: one funnel shift yields both.
-            constexpr uint32_t kTilesPerWarp = T::tiles_per_row / 4;
+            // The warps of a lane quarter split the chunk's 16 tile columns:
+            // warp `quad` decodes tile columns kTilesPerWarp*quad and the
+            // next kTilesPerWarp - 1. In a tile, a row is states 2*rl and
+            // 2*rl + 1, stream bits 24*rl .. 24*rl + 28: one funnel shift
+            // yields both.
+            constexpr uint32_t kTilesPerWarp = T::tiles_per_row / (T::decode_warps / 4);
+            constexpr uint32_t kGammaChunks = 16 / kTilesPerWarp;  // chunks per gamma block
             const uint32_t quarter = warp & 3u, quad = dw >> 2;
             const uint32_t tr = 2u * quarter + (lane >> 4), rl = lane & 15u;
             const uint32_t bit0 = rl * 24u, wq = bit0 >> 5, woff = bit0 & 31u;
             const uint32_t wq1 = wq + 1u == kExpertU32PerTile ? 0u : wq + 1u;
             const uint32_t neg_mask = half == 0 ? 0x8000u : 0u;
             const uint32_t a_lane = tmem_base + ((32u * quarter) << 16) + kTmemAColumn0 + 4u * kTilesPerWarp * quad;
-            // Tile gammas are fetched four chunks at a time: the 16 lanes of
-            // a half-warp share one tile row, so lane (h, i) holds the gamma
-            // bits of chunk kc0 + i / 4, tile column 4 * quad + i % 4. A
-            // block's load is issued four chunks before its use, and the
+            // Tile gammas are fetched kGammaChunks chunks at a time: the 16
+            // lanes of a half-warp share one tile row, so lane (h, i) holds
+            // the gamma bits of chunk kc0 + i / kTilesPerWarp, tile column
+            // kTilesPerWarp * quad + i % kTilesPerWarp. A block's load is
+            // issued kGammaChunks chunks before its use, and the
             // next unit's first block (with the unit itself and its ka) at
             // the start of the current unit; the bits are scaled by 2^ka
             // into f16x2 only when their block becomes current, so no load
             // is waited on early.
             auto fetch_gammas = [&](const Unit &un, const TcJob &J, uint32_t kc0) -> uint32_t {
-                const uint32_t i = lane & 15u, kc = kc0 + (i >> 2);
+                const uint32_t i = lane & 15u, kc = kc0 + i / kTilesPerWarp;
                 if (kc >= J.cols / T::chunk_cols) return 0u;
                 const uint32_t TC = J.cols / 16, TR = J.rows / 16;
-                const uint32_t diag = un.m_block * 8 + tr + kc * T::tiles_per_row + kTilesPerWarp * quad + (i & 3u);
+                const uint32_t diag =
+                    un.m_block * 8 + tr + kc * T::tiles_per_row + kTilesPerWarp * quad + i % kTilesPerWarp;
                 return __ldg(J.gamma + (size_t)un.expert * J.gamma_stride + wave_index(TR, TC, diag));
             };
             auto scaled = [](uint32_t bits, float gscale) -> uint32_t {
@@ -506,7 +524,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const uint32_t chunks = J.cols / T::chunk_cols;
                 const float gscale = exp2f((float)next_ka);
                 uint32_t gblock = scaled(next_first, gscale);
-                uint32_t gnext = fetch_gammas(un, J, 4);
+                uint32_t gnext = fetch_gammas(un, J, kGammaChunks);
                 if (u + stride < n_units) {
                     next = unit_at<T>(p, u + stride);
                     const TcJob &Jn = next.job ? p.job[1] : p.job[0];
@@ -514,11 +532,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     next_ka = Jn.ka[next.expert];
                 }
                 for (uint32_t kc = 0; kc < chunks; ++kc) {
-                    if (kc > 0 && (kc & 3u) == 0) {
+                    if (kc > 0 && kc % kGammaChunks == 0) {
                         gblock = scaled(gnext, gscale);
-                        gnext = fetch_gammas(un, J, kc + 4);
+                        gnext = fetch_gammas(un, J, kc + kGammaChunks);
                     }
-                    const uint32_t src = (lane & 16u) | ((kc & 3u) << 2);
+                    const uint32_t src = (lane & 16u) | ((kc % kGammaChunks) * kTilesPerWarp);
                     uint32_t gcur[kTilesPerWarp];
 #pragma unroll
                     for (uint32_t t = 0; t < kTilesPerWarp; ++t) gcur[t] = __shfl_sync(0xffffffffu, gblock, src | t);
@@ -552,7 +570,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             out[4 * t + 2] = *reinterpret_cast<const uint32_t *>(&vb0);
                             out[4 * t + 3] = *reinterpret_cast<const uint32_t *>(&vb1);
                         }
-                        tmem_st16(a_lane + a.slot * T::tmem_a_columns, out);
+#pragma unroll
+                        for (uint32_t g = 0; g < kTilesPerWarp / 4; ++g)
+                            tmem_st16(a_lane + a.slot * T::tmem_a_columns + 16u * g,
+                                      *reinterpret_cast<const uint32_t(*)[16]>(out + 16 * g));
                         tc_fence_before();
                     }
                     __syncwarp();
@@ -849,7 +870,7 @@ bool launch_codec(const CUtensorMap &map0, const CUtensorMap &map1, const TcPara
     CUtensorMap wmap0, wmap1;
     if (!make_word_map<C>(&wmap0, p.job[0]) || !make_word_map<C>(&wmap1, p.job[1])) return false;
     if (C == TcCodec::kExpert) grid &= ~1;
-    launch_pdl(tc_gemm_kernel<C>, grid, kTcThreads, Smem<C>::total, s, map0, map1, wmap0, wmap1, p);
+    launch_pdl(tc_gemm_kernel<C>, grid, tc_threads<C>(), Smem<C>::total, s, map0, map1, wmap0, wmap1, p);
     return true;
 }
 

@@ -98,6 +98,12 @@ SIGNATURES = {
     "adi_cuda_bf16_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_moe_forward_batch_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p,
                                                     C.c_void_p, C.c_void_p]),
+    "adi_cuda_ep_peer_alloc": (C.c_int, [_ctx, C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p]),
+    "adi_cuda_ep_peer_connect": (C.c_int, [_ctx, C.c_uint32, C.c_uint32, C.c_void_p]),
+    "adi_cuda_ep_peer_close": (C.c_int, [_ctx]),
+    "adi_cuda_ep_send_peer_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
+    "adi_cuda_ep_experts_peer_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32]),
+    "adi_cuda_ep_combine_peer_device": (C.c_int, [_ctx, _h, C.c_uint32, C.c_void_p]),
     "adi_cuda_rms_norm_device": (C.c_int, [_ctx, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_float,
                                            C.c_float, C.c_void_p]),
     "adi_cuda_residual_add_device": (C.c_int, [_ctx, C.c_void_p, C.c_void_p, C.c_size_t]),
@@ -368,6 +374,37 @@ class Context:
 
     def residual_add_device(self, hidden_ptr: int, add_ptr: int, count: int):
         _check(self.lib.adi_cuda_residual_add_device(self.ptr, hidden_ptr, add_ptr, count), "residual_add_device")
+
+    # -- peer-memory exchange of expert parallelism ---------------------------
+    def ep_peer_alloc(self, recv_rows: int, returned_rows: int, hidden: int) -> bytes:
+        """Allocates this rank's exchange buffers; returns their IPC handles
+        (192 bytes) for the other ranks."""
+        buf = C.create_string_buffer(192)
+        _check(self.lib.adi_cuda_ep_peer_alloc(self.ptr, recv_rows, returned_rows, hidden, buf), "ep_peer_alloc")
+        return buf.raw
+
+    def ep_peer_connect(self, rank: int, world: int, handles: list):
+        blob = b"".join(handles)
+        if len(blob) != 192 * world:
+            raise ValueError("one 192-byte handle set per rank is required")
+        buf = C.create_string_buffer(blob, len(blob))
+        _check(self.lib.adi_cuda_ep_peer_connect(self.ptr, rank, world, buf), "ep_peer_connect")
+
+    def ep_peer_close(self):
+        _check(self.lib.adi_cuda_ep_peer_close(self.ptr), "ep_peer_close")
+
+    def ep_send_peer_device(self, shard: Handle, inputs_ptr: int, tokens: int, all_counts_host):
+        counts = np.ascontiguousarray(all_counts_host, dtype=np.uint32)
+        _check(self.lib.adi_cuda_ep_send_peer_device(self.ptr, shard.value, inputs_ptr, tokens,
+                                                     counts.ctypes.data_as(C.c_void_p)), "ep_send_peer_device")
+
+    def ep_experts_peer_device(self, shard: Handle, all_counts_ptr: int, rows: int):
+        _check(self.lib.adi_cuda_ep_experts_peer_device(self.ptr, shard.value, all_counts_ptr, rows),
+               "ep_experts_peer_device")
+
+    def ep_combine_peer_device(self, shard: Handle, tokens: int, outputs_ptr: int):
+        _check(self.lib.adi_cuda_ep_combine_peer_device(self.ptr, shard.value, tokens, outputs_ptr),
+               "ep_combine_peer_device")
 
     # -- expert-parallel phases (device pointers, asynchronous) ---------------
     def ep_dispatch_device(self, shard: Handle, inputs_ptr: int, tokens: int, send_ptr: int, counts_ptr: int,

@@ -362,6 +362,25 @@ struct Profiler {
 
 }  // namespace
 
+// This rank's side of the peer-memory exchange of expert parallelism: its
+// receive buffer (rows other ranks send to its experts, with each row's way
+// back), its returned buffer (its routes' expert outputs, written by the
+// experts' ranks), and every rank's pointers to all of them (its own, and
+// the others' opened through CUDA IPC).
+struct PeerExchange {
+    uint32_t rank = 0, world = 0, hidden = 0;
+    uint32_t recv_capacity = 0, returned_capacity = 0;
+    std::unique_ptr<DeviceArray> recv_rows, recv_meta, returned_rows;  // own, cudaMalloc'd (IPC-able)
+    std::vector<void *> opened;                                          // peers' mappings, closed on reset
+    std::unique_ptr<DeviceArray> recv_rows_ptrs, recv_meta_ptrs, returned_ptrs;  // [world] device pointer tables
+    void close_peers() {
+        for (void *ptr : opened) cudaIpcCloseMemHandle(ptr);
+        opened.clear();
+        world = 0;
+    }
+    ~PeerExchange() { close_peers(); }
+};
+
 struct adi_cuda_context {
     int device = 0;
     int sms = 148;
@@ -391,6 +410,7 @@ struct adi_cuda_context {
     uint32_t ep_tokens = 0;
     Profiler profiler;
     Stager stager;
+    PeerExchange peers;
     void stage(int st) { profiler.begin(st, stream); }
     void stage_end() { profiler.end(stream); }
     // Scratch arena, grown on demand.
@@ -1456,9 +1476,9 @@ void ep_dispatch_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const floa
     }
     c->stage(kStageRoute);
     const uint32_t route_launches = launch_route(rp, s);
-    launch_ep_gather(in, rp.grouped, uint32_t(P), H, send, s);
+    if (send) launch_ep_gather(in, rp.grouped, uint32_t(P), H, send, s);
     c->stage_end();
-    c->after_launch(route_launches + 1);
+    c->after_launch(route_launches + (send ? 1 : 0));
 
     if (route_experts_out)
         check(cudaMemcpyAsync(route_experts_out, re, P * 4, cudaMemcpyDeviceToDevice, s), "route copy");
@@ -1469,8 +1489,12 @@ void ep_dispatch_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const floa
 }
 
 // The shard's routed experts on received rows; one output row per row.
+// recv_counts[s * counts_stride + counts_offset + e]: rows of sender s for
+// local expert e. With return_rows, each output row goes straight back to
+// its sender (recv_meta), instead of to expert_rows.
 void ep_experts_dev(adi_cuda_context *c, MoeDev &L, const float *recv, const uint32_t *recv_counts, uint32_t world,
-                    uint32_t rows, float *expert_rows) {
+                    uint32_t rows, float *expert_rows, uint32_t counts_stride, uint32_t counts_offset,
+                    float *const *return_rows = nullptr, const uint32_t *recv_meta = nullptr) {
     const uint32_t H = L.hidden, I = L.inner, local = L.local_experts;
     if (world == 0 || uint64_t(world) * local > 1024) invalid("expert-parallel world times shard experts must be 1..1024");
     if (rows == 0) return;
@@ -1493,6 +1517,8 @@ void ep_experts_dev(adi_cuda_context *c, MoeDev &L, const float *recv, const uin
     rp.count_down = counts3 + 1;
     EpPlanParams pp{};
     pp.recv_counts = recv_counts;
+    pp.counts_stride = counts_stride;
+    pp.counts_offset = counts_offset;
     pp.world = world;
     pp.local = local;
     pp.rows = rows;
@@ -1522,6 +1548,8 @@ void ep_experts_dev(adi_cuda_context *c, MoeDev &L, const float *recv, const uin
     fp.positions = rows;
     fp.scale = transform_scale(H);
     fp.expert_rows = expert_rows;
+    fp.return_rows = return_rows;
+    fp.recv_meta = recv_meta;
     c->stage(kStageCombine);
     launch_ep_finalize(fp, s);
     c->stage_end();
@@ -2028,7 +2056,7 @@ int adi_cuda_ep_dispatch_device(adi_cuda_context *c, adi_cuda_handle h, const fl
     return guarded([&] {
         std::lock_guard<std::mutex> g(require(c)->lock);
         use_device(c);
-        if (!in || !send_rows || !expert_counts) invalid("input, send or count pointer is null");
+        if (!in || !expert_counts) invalid("input or count pointer is null");
         ep_dispatch_dev(c, h, lookup(c->moes, h, "MoE layer"), in, router_logits, tokens, send_rows, expert_counts,
                         route_experts, route_weights);
     });
@@ -2040,7 +2068,157 @@ int adi_cuda_ep_experts_device(adi_cuda_context *c, adi_cuda_handle h, const flo
         std::lock_guard<std::mutex> g(require(c)->lock);
         use_device(c);
         if (!recv_counts || (rows && (!recv_rows || !expert_rows))) invalid("receive or output pointer is null");
-        ep_experts_dev(c, lookup(c->moes, h, "MoE layer"), recv_rows, recv_counts, world, rows, expert_rows);
+        auto &L = lookup(c->moes, h, "MoE layer");
+        ep_experts_dev(c, L, recv_rows, recv_counts, world, rows, expert_rows, L.local_experts, 0);
+    });
+}
+
+int adi_cuda_ep_peer_alloc(adi_cuda_context *c, uint32_t recv_rows, uint32_t returned_rows, uint32_t hidden,
+                           uint8_t *handles) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!handles || recv_rows == 0 || returned_rows == 0 || hidden == 0 || hidden % 4)
+            invalid("peer exchange sizes are invalid");
+        if (returned_rows > (1u << 28)) invalid("peer exchange returned rows exceed 2^28");
+        PeerExchange &px = c->peers;
+        px.close_peers();
+        auto alloc = [](std::unique_ptr<DeviceArray> &a, size_t bytes) {
+            a = std::make_unique<DeviceArray>();
+            a->reserve(bytes);
+        };
+        alloc(px.recv_rows, size_t(recv_rows) * hidden * 4);
+        alloc(px.recv_meta, size_t(recv_rows) * 4);
+        alloc(px.returned_rows, size_t(returned_rows) * hidden * 4);
+        px.recv_capacity = recv_rows;
+        px.returned_capacity = returned_rows;
+        px.hidden = hidden;
+        void *bases[3] = {px.recv_rows->ptr, px.recv_meta->ptr, px.returned_rows->ptr};
+        for (int i = 0; i < 3; ++i) {
+            cudaIpcMemHandle_t hd;
+            check(cudaIpcGetMemHandle(&hd, bases[i]), "cudaIpcGetMemHandle");
+            std::memcpy(handles + 64 * i, &hd, 64);
+        }
+    });
+}
+
+int adi_cuda_ep_peer_connect(adi_cuda_context *c, uint32_t rank, uint32_t world, const uint8_t *handles) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        PeerExchange &px = c->peers;
+        if (!handles || !px.recv_rows) invalid("peer exchange not allocated");
+        if (world == 0 || world > kEpMaxPeers || rank >= world) invalid("peer exchange rank or world is invalid");
+        px.close_peers();
+        std::vector<void *> tables[3];
+        void *own[3] = {px.recv_rows->ptr, px.recv_meta->ptr, px.returned_rows->ptr};
+        for (uint32_t r = 0; r < world; ++r)
+            for (int i = 0; i < 3; ++i) {
+                if (r == rank) {
+                    tables[i].push_back(own[i]);
+                    continue;
+                }
+                cudaIpcMemHandle_t hd;
+                std::memcpy(&hd, handles + (size_t(r) * 3 + i) * 64, 64);
+                void *ptr = nullptr;
+                check(cudaIpcOpenMemHandle(&ptr, hd, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+                px.opened.push_back(ptr);
+                tables[i].push_back(ptr);
+            }
+        std::unique_ptr<DeviceArray> *dst[3] = {&px.recv_rows_ptrs, &px.recv_meta_ptrs, &px.returned_ptrs};
+        for (int i = 0; i < 3; ++i)
+            *dst[i] = upload_bytes(tables[i].data(), tables[i].size() * sizeof(void *), "peer pointers");
+        px.rank = rank;
+        px.world = world;
+    });
+}
+
+int adi_cuda_ep_peer_close(adi_cuda_context *c) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        check(cudaStreamSynchronize(c->stream), "synchronize");
+        c->peers.close_peers();
+    });
+}
+
+int adi_cuda_ep_send_peer_device(adi_cuda_context *c, adi_cuda_handle h, const float *in, uint32_t tokens,
+                                 const uint32_t *all_counts) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        PeerExchange &px = c->peers;
+        auto &L = lookup(c->moes, h, "MoE layer");
+        if (!in || !all_counts) invalid("input or count pointer is null");
+        if (px.world == 0) invalid("peer exchange not connected");
+        if (c->ep_layer != h || c->ep_tokens != tokens || tokens == 0)
+            invalid("peer send must follow a dispatch of the same layer and token count");
+        const uint32_t E = L.experts, local = L.local_experts, world = px.world;
+        if (local * world != E) invalid("the shard's experts times the world size must be the layer's experts");
+        if (L.hidden != px.hidden) invalid("peer exchange hidden size mismatch");
+        EpSendParams sp{};
+        sp.x = in;
+        sp.grouped = c->buffer<uint32_t>("ep_send_grouped", size_t(tokens) * 8);
+        sp.pos_expert = c->buffer<uint32_t>("ep_send_pos_expert", size_t(tokens) * 8);
+        sp.positions = tokens * 8;
+        sp.hidden = L.hidden;
+        sp.rank = px.rank;
+        sp.world = world;
+        sp.local = local;
+        // From the exchanged counts (host copy, [world][E]): where this rank's
+        // rows for each destination start in its receive buffer, and where
+        // they start among this rank's positions.
+        uint64_t sent = 0;
+        for (uint32_t d = 0; d < world; ++d) {
+            uint64_t base = 0, mine = 0, total = 0;
+            for (uint32_t s = 0; s < world; ++s)
+                for (uint32_t e = d * local; e < (d + 1) * local; ++e) {
+                    const uint64_t n = all_counts[size_t(s) * E + e];
+                    if (s < px.rank) base += n;
+                    if (s == px.rank) mine += n;
+                    total += n;
+                }
+            if (total > px.recv_capacity) invalid("peer exchange receive buffer too small for this step");
+            sp.base[d] = uint32_t(base);
+            sp.start[d] = uint32_t(sent);
+            sent += mine;
+        }
+        if (sent != uint64_t(tokens) * 8) invalid("exchanged counts do not match this rank's routes");
+        sp.recv_rows = px.recv_rows_ptrs->as<float *>();
+        sp.recv_meta = px.recv_meta_ptrs->as<uint32_t *>();
+        c->stage(kStageRoute);
+        launch_ep_send_peer(sp, c->stream);
+        c->stage_end();
+        c->after_launch(1);
+    });
+}
+
+int adi_cuda_ep_experts_peer_device(adi_cuda_context *c, adi_cuda_handle h, const uint32_t *all_counts,
+                                    uint32_t rows) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        PeerExchange &px = c->peers;
+        auto &L = lookup(c->moes, h, "MoE layer");
+        if (!all_counts) invalid("count pointer is null");
+        if (px.world == 0) invalid("peer exchange not connected");
+        if (rows > px.recv_capacity) invalid("peer exchange receive buffer too small for this step");
+        if (L.local_experts * px.world != L.experts)
+            invalid("the shard's experts times the world size must be the layer's experts");
+        ep_experts_dev(c, L, px.recv_rows->as<float>(), all_counts, px.world, rows, nullptr, L.experts,
+                       L.first_expert, px.returned_ptrs->as<float *>(), px.recv_meta->as<uint32_t>());
+    });
+}
+
+int adi_cuda_ep_combine_peer_device(adi_cuda_context *c, adi_cuda_handle h, uint32_t tokens, float *outputs) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        PeerExchange &px = c->peers;
+        if (!outputs) invalid("output pointer is null");
+        if (px.world == 0) invalid("peer exchange not connected");
+        if (size_t(tokens) * 8 > px.returned_capacity) invalid("peer exchange returned buffer too small");
+        ep_combine_dev(c, h, lookup(c->moes, h, "MoE layer"), px.returned_rows->as<float>(), tokens, outputs);
     });
 }
 

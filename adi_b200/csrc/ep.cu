@@ -25,6 +25,23 @@ __global__ void ep_gather_kernel(const float4 *x, const uint32_t *grouped, uint3
     }
 }
 
+// A warp per position: the token's row (16-byte loads) to the peer's
+// receive buffer (16-byte stores over NVLink).
+__global__ void ep_send_peer_kernel(EpSendParams p) {
+    const uint32_t lane = threadIdx.x & 31u, quads = p.hidden / 4;
+    const uint32_t warps = gridDim.x * (blockDim.x >> 5);
+    for (uint32_t pos = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); pos < p.positions; pos += warps) {
+        const uint32_t d = p.pos_expert[pos] / p.local;
+        if (d >= p.world) continue;  // never for a consistent plan; keeps the index in bounds
+        const uint32_t row = p.base[d] + pos - p.start[d];
+        const float4 *src = reinterpret_cast<const float4 *>(p.x + (size_t)p.grouped[pos] * p.hidden);
+        float4 *dst = reinterpret_cast<float4 *>(p.recv_rows[d] + (size_t)row * p.hidden);
+        for (uint32_t q = lane; q < quads; q += 32) dst[q] = src[q];
+        if (lane == 0) p.recv_meta[d][row] = (p.rank << 28) | pos;
+    }
+    __threadfence_system();
+}
+
 // Inclusive prefix sum of a[0..1023] by a 1024-thread block.
 __device__ void block_scan_1024(uint32_t *a) {
     const uint32_t t = threadIdx.x;
@@ -39,7 +56,7 @@ __device__ void block_scan_1024(uint32_t *a) {
 __global__ void __launch_bounds__(1024) ep_plan_kernel(EpPlanParams p) {
     __shared__ uint32_t cnt[1024], seg[1024], base[1024], scan[1024], chunk_scan[1024];
     const uint32_t t = threadIdx.x, n = p.world * p.local;
-    const uint32_t c_t = t < n ? p.recv_counts[t] : 0u;
+    const uint32_t c_t = t < n ? p.recv_counts[(t / p.local) * p.counts_stride + p.counts_offset + t % p.local] : 0u;
     cnt[t] = c_t;
     scan[t] = c_t;
     __syncthreads();
@@ -121,7 +138,13 @@ __global__ void __launch_bounds__(256) ep_finalize_regs_kernel(EpFinalizeParams 
     const uint16_t *sv = p.sv_down + (size_t)e * H + c0;
 #pragma unroll
     for (int r = 0; r < R; ++r) v[r] = __fmul_rn(__fmul_rn(v[r], p.scale), f16_bits_to_f32(sv[r]));
-    store_regs<R>(p.expert_rows + (size_t)row * H + c0, v);
+    if (p.return_rows) {
+        const uint32_t meta = p.recv_meta[row];
+        store_regs<R>(p.return_rows[meta >> 28] + (size_t)(meta & 0x0FFFFFFFu) * H + c0, v);
+        __threadfence_system();
+    } else {
+        store_regs<R>(p.expert_rows + (size_t)row * H + c0, v);
+    }
 }
 
 __global__ void ep_finalize_kernel(EpFinalizeParams p) {
@@ -134,8 +157,13 @@ __global__ void ep_finalize_kernel(EpFinalizeParams p) {
     __syncthreads();
     block_fwht(v, H, p.scale);
     const uint16_t *sv = p.sv_down + (size_t)e * H;
-    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x)
-        p.expert_rows[(size_t)row * H + i] = __fmul_rn(v[i], f16_bits_to_f32(sv[i]));
+    float *out = p.expert_rows + (size_t)row * H;
+    if (p.return_rows) {
+        const uint32_t meta = p.recv_meta[row];
+        out = p.return_rows[meta >> 28] + (size_t)(meta & 0x0FFFFFFFu) * H;
+    }
+    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) out[i] = __fmul_rn(v[i], f16_bits_to_f32(sv[i]));
+    if (p.return_rows) __threadfence_system();
 }
 
 template <int R>
@@ -215,6 +243,12 @@ void launch_ep_gather(const float *x, const uint32_t *grouped, uint32_t position
 }
 
 void launch_ep_plan(const EpPlanParams &p, cudaStream_t s) { ep_plan_kernel<<<1, 1024, 0, s>>>(p); }
+
+void launch_ep_send_peer(const EpSendParams &p, cudaStream_t s) {
+    if (p.positions == 0) return;
+    const uint32_t blocks = (p.positions + 7) / 8;
+    ep_send_peer_kernel<<<blocks < 148 * 8 ? blocks : 148 * 8, 256, 0, s>>>(p);
+}
 
 void launch_ep_finalize(const EpFinalizeParams &p, cudaStream_t s) {
     if (p.positions == 0) return;

@@ -14,6 +14,26 @@ namespace adi_cuda {
 void launch_ep_gather(const float *x, const uint32_t *grouped, uint32_t positions, uint32_t hidden, float *send,
                       cudaStream_t s);
 
+// The same rows written straight into the receiving ranks' buffers over
+// NVLink (peer pointers from CUDA IPC): position pos, of global expert e on
+// rank d = e / local, lands at row base[d] + pos - start[d] of
+// recv_rows[d], where base[d] is the rows lower ranks send to d and start[d]
+// this rank's first position bound for d (both from the exchanged counts),
+// and recv_meta[d] of that row records (rank << 28) | pos, the row's way
+// back. Ends with a system-scope fence; the caller orders the receivers
+// after it (a collective on the same stream).
+constexpr uint32_t kEpMaxPeers = 8;
+struct EpSendParams {
+    const float *x;               // [T][hidden]
+    const uint32_t *grouped;      // [positions] token of each position
+    const uint32_t *pos_expert;   // [positions] global expert of each position
+    uint32_t positions, hidden, rank, world, local;
+    uint32_t base[kEpMaxPeers], start[kEpMaxPeers];
+    float *const *recv_rows;      // [world] peer pointers, [capacity][hidden]
+    uint32_t *const *recv_meta;   // [world] peer pointers, [capacity]
+};
+void launch_ep_send_peer(const EpSendParams &p, cudaStream_t s);
+
 // The receiving rank's routing. recv_counts[s][e]: rows rank s sent for
 // local expert e; they sit in the receive buffer in (s, e) order. Positions
 // are expert-major (then sender, then arrival), so each local expert's rows
@@ -21,7 +41,8 @@ void launch_ep_gather(const float *x, const uint32_t *grouped, uint32_t position
 // do not add up to `rows` the plan holds no work (empty lists, *placed = 0,
 // every index 0), so no launch after it reads or writes out of bounds.
 struct EpPlanParams {
-    const uint32_t *recv_counts;  // [world][local]
+    const uint32_t *recv_counts;  // sender s, local expert e at [s * counts_stride + counts_offset + e]
+    uint32_t counts_stride, counts_offset;
     uint32_t world, local;        // world * local <= 1024
     uint32_t rows;                // rows in the receive buffer
     uint32_t *grouped;            // [rows] receive-buffer row of each position
@@ -51,6 +72,12 @@ struct EpFinalizeParams {
     uint32_t hidden, positions;
     float scale;
     float *expert_rows;
+    // With return_rows set, receive row j is written instead to
+    // return_rows[meta >> 28] + (meta & 0x0FFFFFFF) * hidden, meta =
+    // recv_meta[j]: straight into the sending rank's buffer over NVLink,
+    // ending with a system-scope fence.
+    float *const *return_rows;    // [world] peer pointers, or null
+    const uint32_t *recv_meta;    // [rows]
 };
 void launch_ep_finalize(const EpFinalizeParams &p, cudaStream_t s);
 

@@ -19,8 +19,14 @@ layer is three device phases with two exchanges between them:
                gated shared expert
 
 The exchanges are torch.distributed collectives (NCCL over NVLink on the
-GPUs). Every row is computed with the single-GPU kernels, so the output is
-the single-GPU block's output for the same tokens.
+GPUs), or, with a PeerExchange, this library's own kernels over NVLink: the
+dispatch writes every route's row straight into the receive buffer of the
+expert's rank (peer pointers through CUDA IPC), and the experts' output
+transform writes every output row straight back into the sender's buffer;
+only the expert counts go through a collective, and a one-element
+all-reduce orders each rank after the others' writes. Every row is computed
+with the single-GPU kernels, so the output is the single-GPU block's output
+for the same tokens either way.
 """
 from __future__ import annotations
 
@@ -61,6 +67,30 @@ class DevicePhases:
                                     logits_ptr=logits.data_ptr() if logits is not None else 0)
         return send, counts
 
+    def dispatch_counts(self, x: torch.Tensor, logits: torch.Tensor | None = None) -> torch.Tensor:
+        """The dispatch without a send buffer (peer exchange): routes, the
+        shared expert, and the count of routes per expert [E] int32."""
+        tokens = x.shape[0]
+        self._stream(x.device)
+        counts = torch.empty(self.experts, dtype=torch.int32, device=x.device)
+        self.ctx.ep_dispatch_device(self.handle, x.data_ptr(), tokens, 0, counts.data_ptr(),
+                                    logits_ptr=logits.data_ptr() if logits is not None else 0)
+        return counts
+
+    def send_peer(self, x: torch.Tensor, all_counts_host):
+        self._stream(x.device)
+        self.ctx.ep_send_peer_device(self.handle, x.data_ptr(), x.shape[0], all_counts_host)
+
+    def experts_peer(self, all_counts: torch.Tensor, rows: int):
+        self._stream(all_counts.device)
+        self.ctx.ep_experts_peer_device(self.handle, all_counts.data_ptr(), rows)
+
+    def combine_peer(self, tokens: int, device) -> torch.Tensor:
+        self._stream(device)
+        out = torch.empty(tokens, self.hidden, dtype=torch.float32, device=device)
+        self.ctx.ep_combine_peer_device(self.handle, tokens, out.data_ptr())
+        return out
+
     def experts_forward(self, recv: torch.Tensor, recv_counts: torch.Tensor, world: int) -> torch.Tensor:
         self._stream(recv_counts.device)
         rows = recv.shape[0]
@@ -79,6 +109,34 @@ class DevicePhases:
         self.handle.release()
 
 
+class PeerExchange:
+    """This rank's buffers of the peer-memory exchange, connected to every
+    rank of `group`: each rank allocates its receive and returned buffers
+    (for up to `max_tokens` tokens per rank per layer) and the CUDA IPC
+    handles are all-gathered, so every rank holds pointers to every rank's
+    buffers. close() unmaps the others' buffers on every rank; call it on
+    all ranks before any context closes."""
+
+    def __init__(self, ctx, group=None, max_tokens: int = 512, hidden: int = 2048):
+        self.ctx, self.group = ctx, group
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.max_tokens = max_tokens
+        handles = ctx.ep_peer_alloc(self.world * 8 * max_tokens, 8 * max_tokens, hidden)
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, handles, group=group)
+        ctx.ep_peer_connect(self.rank, self.world, gathered)
+        self._order = torch.zeros(1, device=torch.cuda.current_device())
+
+    def fence(self):
+        """Orders this rank's later work after every rank's writes so far
+        (their kernels end with system-scope fences)."""
+        dist.all_reduce(self._order, group=self.group)
+
+    def close(self):
+        self.ctx.ep_peer_close()
+        dist.barrier(group=self.group)
+
+
 class ExpertParallelMoe:
     """One MoE layer across the ranks of `group`; forward(x) takes this
     rank's tokens [T, H] and returns their block outputs [T, H].
@@ -86,9 +144,10 @@ class ExpertParallelMoe:
     `phases` does the per-rank compute (DevicePhases on GPUs); the class
     owns the exchanges, whose sizes come from the routed counts."""
 
-    def __init__(self, phases, group=None):
+    def __init__(self, phases, group=None, exchange: PeerExchange | None = None):
         self.phases = phases
         self.group = group
+        self.exchange = exchange
         self.world = dist.get_world_size(group)
         self.experts, self.hidden, self.local = phases.experts, phases.hidden, phases.local
         if self.local * self.world != self.experts:
@@ -99,6 +158,8 @@ class ExpertParallelMoe:
     def forward(self, x: torch.Tensor, logits: torch.Tensor | None = None) -> torch.Tensor:
         """`logits` [T, experts + 1], when given, replace the router's (the
         last column is the shared-expert gate): a prescribed routing."""
+        if self.exchange is not None:
+            return self._forward_peer(x, logits)
         tokens = x.shape[0]
         send, counts = self.phases.dispatch(x) if logits is None else self.phases.dispatch(x, logits)
         recv_counts = torch.empty_like(counts)
@@ -114,6 +175,24 @@ class ExpertParallelMoe:
         returned = torch.empty_like(send)
         dist.all_to_all_single(returned, expert_rows, send_splits, recv_splits, group=self.group)
         return self.phases.combine(returned, tokens)
+
+    def _forward_peer(self, x: torch.Tensor, logits: torch.Tensor | None) -> torch.Tensor:
+        tokens = x.shape[0]
+        if tokens > self.exchange.max_tokens:
+            raise ValueError(f"{tokens} tokens exceed the peer exchange's {self.exchange.max_tokens}")
+        counts = self.phases.dispatch_counts(x, logits)
+        all_counts = torch.empty(self.world, self.experts, dtype=torch.int32, device=x.device)
+        dist.all_gather_into_tensor(all_counts, counts, group=self.group)
+        host = all_counts.cpu()
+        rank, local = self.exchange.rank, self.local
+        mine = host[:, rank * local:(rank + 1) * local]
+        self.last_splits = (host[rank].view(self.world, local).sum(1).tolist(), mine.sum(1).tolist())
+        self.last_received = mine.sum(0).long()
+        self.phases.send_peer(x, host.numpy())
+        self.exchange.fence()
+        self.phases.experts_peer(all_counts, int(mine.sum()))
+        self.exchange.fence()
+        return self.phases.combine_peer(tokens, x.device)
 
     __call__ = forward
 

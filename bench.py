@@ -72,6 +72,9 @@ def parse():
     ap.add_argument("--routing", choices=["zipf", "router"], default="zipf",
                     help="N > 1: zipf = C4's prescribed logits, log p(rank) + Gumbel(0,1) with Zipf s=1.1 "
                          "popularity; router = the block's own router on N(0,1) inputs (near-uniform)")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",
+                    help="N > 1: peer = rows written straight into the other GPUs' buffers by this library's "
+                         "kernels over NVLink; nccl = NCCL all-to-alls")
     ap.add_argument("--no-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-extras", action="store_true",
                     help="only the timed region: no e2e, ubatch sweep or CPU baseline (profiling runs)")
@@ -418,7 +421,7 @@ def stack_c5(ctx, stream, local):
 C5_EP_DECODE_STEPS = 32
 
 
-def stack_c5_ep(ctx, stream, local, rank, world):
+def stack_c5_ep(ctx, stream, local, rank, world, exchange=None):
     """C5 over `world` ranks: the same 40-layer stack as stack_c5, every
     block expert-parallel (ExpertParallelStack), each rank feeding its own
     2048-token prefill in ubatches of 512 and then its own batch-1 decode
@@ -429,7 +432,7 @@ def stack_c5_ep(ctx, stream, local, rank, world):
     moes = []
     for d in range(C5_DISTINCT):
         b = synthetic.moe_block(seed=8000 + d, device=device)
-        moes.append(ExpertParallelMoe(DevicePhases(ctx, b, rank, world)))
+        moes.append(ExpertParallelMoe(DevicePhases(ctx, b, rank, world), exchange=exchange))
         del b
     g = torch.Generator(device=device)
     g.manual_seed(8100)
@@ -503,7 +506,7 @@ def run_ep(args, world, rank, local):
     """Expert-parallel MoE block over `world` ranks (one process per GPU)."""
     import adi_b200
     from adi_b200 import synthetic
-    from adi_b200.expert_parallel import DevicePhases, ExpertParallelMoe
+    from adi_b200.expert_parallel import DevicePhases, ExpertParallelMoe, PeerExchange
     torch.cuda.set_device(local)
     device = f"cuda:{local}"
     ctx = adi_b200.Context(local)
@@ -512,11 +515,12 @@ def run_ep(args, world, rank, local):
     ctx.set_stream(stream.cuda_stream)
     ctx.set_precision(args.precision)
     T, L = args.tokens, args.layers
+    exchange = PeerExchange(ctx, max_tokens=max(T, C5_UBATCH), hidden=2048) if args.exchange == "peer" else None
 
     layers, first = [], None
     for layer in range(L):
         block = synthetic.moe_block(seed=layer, device=device)  # the same blocks on every rank
-        layers.append(ExpertParallelMoe(DevicePhases(ctx, block, rank, world)))
+        layers.append(ExpertParallelMoe(DevicePhases(ctx, block, rank, world), exchange=exchange))
         if first is None:
             first = block
         del block
@@ -586,7 +590,7 @@ def run_ep(args, world, rank, local):
         e2e_step(k)
     e2e_s = max_over_ranks(time.perf_counter() - t0, world)
     e2e_value = sum_over_ranks(e2e_steps * T, world) / e2e_s
-    c5 = stack_c5_ep(ctx, stream, local, rank, world) if not args.no_extras else None
+    c5 = stack_c5_ep(ctx, stream, local, rank, world, exchange) if not args.no_extras else None
 
     if rank == 0:
         line = {
@@ -601,7 +605,10 @@ def run_ep(args, world, rank, local):
                        "routing": ("C4 prescribed logits: log p(rank) + Gumbel(0,1), Zipf s=1.1, rank permutation "
                                    "from seed 0" if logits is not None else "the block's router on N(0,1) inputs"),
                        "l2": f"inputs larger than L2: {L} distinct blocks rotated",
-                       "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single, fp32 rows"},
+                       "parallelism": f"ep{world}",
+                       "exchange": ("rows written over NVLink by the dispatch and output-transform kernels "
+                                    "(CUDA IPC peer pointers); counts by NCCL all_gather" if exchange is not None
+                                    else "NCCL all_to_all_single, fp32 rows")},
             "roofline": {"bound": "hbm", "kernel": "expert_gemm_kernel",
                          "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": (achieved / hbm_peak) if achieved else None, "peak_kind": peak_kind,
@@ -621,6 +628,8 @@ def run_ep(args, world, rank, local):
     barrier(world)
     for moe in layers:
         moe.phases.release()
+    if exchange is not None:
+        exchange.close()
     ctx.close()
 
 

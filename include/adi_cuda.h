@@ -242,6 +242,49 @@ ADI_CUDA_API int adi_cuda_moe_stack_forward_device(adi_cuda_context *context,
  * partial sums in the context for 5. All are asynchronous on the context
  * stream. */
 
+/* Peer-memory exchange (one node; no counterpart in the reference). The
+ * same split as above with the two row exchanges done by this library's
+ * kernels over NVLink instead of by the caller: the dispatch writes each
+ * route's row straight into the receive buffer of the rank that owns its
+ * expert, and the experts' output transform writes each output row straight
+ * back into the sender's returned buffer. Per block and rank:
+ *
+ *   1. adi_cuda_ep_dispatch_device with send_rows null (routes, counts,
+ *      shared expert);
+ *   2. the caller all-gathers the expert counts ([world][E] int32) and
+ *      copies them to the host;
+ *   3. adi_cuda_ep_send_peer_device (host counts) writes the rows;
+ *   4. the caller orders every rank after every rank's step 3 (e.g. a
+ *      one-element all-reduce on the same stream);
+ *   5. adi_cuda_ep_experts_peer_device (device counts, received row count)
+ *      runs this rank's experts and writes the rows back;
+ *   6. the same ordering as 4;
+ *   7. adi_cuda_ep_combine_peer_device.
+ *
+ * Set-up: adi_cuda_ep_peer_alloc allocates this rank's buffers (receive
+ * rows of `recv_rows`, returned rows of `returned_rows`, `hidden` floats
+ * each) and writes their three 64-byte CUDA IPC handles to handles[0..191];
+ * after the caller gathers every rank's handles ([world][192] bytes),
+ * adi_cuda_ep_peer_connect opens the others' buffers. adi_cuda_ep_peer_close
+ * closes those mappings; every rank closes before any rank shuts its context
+ * down, since shutting down frees the buffers others map. world <= 8. */
+ADI_CUDA_API int adi_cuda_ep_peer_alloc(adi_cuda_context *context, uint32_t recv_rows,
+                                        uint32_t returned_rows, uint32_t hidden,
+                                        uint8_t *handles);
+ADI_CUDA_API int adi_cuda_ep_peer_connect(adi_cuda_context *context, uint32_t rank,
+                                          uint32_t world, const uint8_t *handles);
+ADI_CUDA_API int adi_cuda_ep_peer_close(adi_cuda_context *context);
+ADI_CUDA_API int adi_cuda_ep_send_peer_device(adi_cuda_context *context, adi_cuda_handle shard,
+                                              const float *inputs, uint32_t tokens,
+                                              const uint32_t *all_counts_host);
+ADI_CUDA_API int adi_cuda_ep_experts_peer_device(adi_cuda_context *context,
+                                                 adi_cuda_handle shard,
+                                                 const uint32_t *all_counts_device,
+                                                 uint32_t rows);
+ADI_CUDA_API int adi_cuda_ep_combine_peer_device(adi_cuda_context *context,
+                                                 adi_cuda_handle shard, uint32_t tokens,
+                                                 float *outputs);
+
 /* Uploads routed experts [first_expert, first_expert + expert_count) of
  * `layer` plus its router and shared expert (replicated). `layer->routed`
  * is the full [experts * 3] array; only the shard's entries are read. The
@@ -250,7 +293,8 @@ ADI_CUDA_API int adi_cuda_moe_stack_forward_device(adi_cuda_context *context,
 ADI_CUDA_API int adi_cuda_upload_moe_shard(adi_cuda_context *context, const adi_moe_layer *layer,
                                            uint32_t first_expert, uint32_t expert_count,
                                            adi_cuda_handle *handle);
-/* inputs [tokens][hidden]; send_rows [8 * tokens][hidden]; expert_counts
+/* inputs [tokens][hidden]; send_rows [8 * tokens][hidden] (NULL with the
+ * peer exchange: no rows are gathered); expert_counts
  * [experts]; route_experts / route_weights [tokens][8] or NULL.
  * router_logits: NULL to compute the router from the inputs, or caller
  * logits [tokens][experts + 1] (the last column the shared-expert gate)

@@ -72,7 +72,7 @@ def parse():
     ap.add_argument("--routing", choices=["zipf", "router"], default="zipf",
                     help="N > 1: zipf = C4's prescribed logits, log p(rank) + Gumbel(0,1) with Zipf s=1.1 "
                          "popularity; router = the block's own router on N(0,1) inputs (near-uniform)")
-    ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="N > 1: peer = rows written straight into the other GPUs' buffers by this library's "
                          "kernels over NVLink; nccl = NCCL all-to-alls")
     ap.add_argument("--no-baseline", action="store_true", help="skip the CPU baseline leg")

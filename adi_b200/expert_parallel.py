@@ -30,6 +30,7 @@ for the same tokens either way.
 """
 from __future__ import annotations
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -181,18 +182,21 @@ class ExpertParallelMoe:
         if tokens > self.exchange.max_tokens:
             raise ValueError(f"{tokens} tokens exceed the peer exchange's {self.exchange.max_tokens}")
         counts = self.phases.dispatch_counts(x, logits)
-        all_counts = torch.empty(self.world, self.experts, dtype=torch.int32, device=x.device)
+        all_counts = torch.empty(self.world * self.experts, dtype=torch.int32, device=x.device)
         dist.all_gather_into_tensor(all_counts, counts, group=self.group)
-        host = all_counts.cpu()
+        host = all_counts.cpu().numpy().reshape(self.world, self.experts)
         rank, local = self.exchange.rank, self.local
         mine = host[:, rank * local:(rank + 1) * local]
-        self.last_splits = (host[rank].view(self.world, local).sum(1).tolist(), mine.sum(1).tolist())
-        self.last_received = mine.sum(0).long()
-        self.phases.send_peer(x, host.numpy())
+        # The device waits on this host step: issue its work first, then the
+        # bookkeeping.
+        self.phases.send_peer(x, host)
         self.exchange.fence()
         self.phases.experts_peer(all_counts, int(mine.sum()))
         self.exchange.fence()
-        return self.phases.combine_peer(tokens, x.device)
+        out = self.phases.combine_peer(tokens, x.device)
+        self.last_splits = (host[rank].reshape(self.world, local).sum(1).tolist(), mine.sum(1).tolist())
+        self.last_received = torch.from_numpy(mine.sum(0).astype(np.int64))
+        return out
 
     __call__ = forward
 

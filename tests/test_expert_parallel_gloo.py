@@ -108,3 +108,76 @@ def test_expert_parallel_stack_matches_single_process():
     on every rank to the one-process restatement of its own tokens."""
     mp.spawn(stack_worker, args=(2, free_port()), nprocs=2, join=True)
 
+
+
+class _PeerStandIn:
+    """Phases of the peer-memory path that only record what the exchange
+    logic hands them (the data movement itself needs GPUs): rank r routes
+    all of its tokens' routes to expert 3 * r."""
+    experts, hidden, local = 16, 8, 8
+
+    def __init__(self, rank):
+        self.rank = rank
+
+    def dispatch_counts(self, x, logits=None):
+        import torch
+        counts = torch.zeros(self.experts, dtype=torch.int32)
+        counts[3 * self.rank] = 8 * x.shape[0]
+        return counts
+
+    def send_peer(self, x, host):
+        self.host = host.copy()
+
+    def experts_peer(self, all_counts, rows):
+        self.rows = rows
+
+    def combine_peer(self, tokens, device):
+        import torch
+        return torch.zeros(tokens, self.hidden)
+
+
+class _OrderStandIn:
+    def __init__(self, rank):
+        self.rank, self.max_tokens = rank, 64
+
+    def fence(self):
+        import torch
+        import torch.distributed as dist
+        dist.all_reduce(torch.zeros(1))
+
+
+def peer_logic_worker(rank: int, world: int, port: int):
+    import torch
+    import torch.distributed as dist
+
+    from adi_b200.expert_parallel import ExpertParallelMoe
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        phases = _PeerStandIn(rank)
+        moe = ExpertParallelMoe(phases, exchange=_OrderStandIn(rank))
+        tokens = 3 + rank
+        y = moe(torch.zeros(tokens, 8))
+        assert y.shape == (tokens, 8)
+        # every rank's counts reach every rank, in rank order
+        want = np.zeros((world, 16), np.int32)
+        for s in range(world):
+            want[s, 3 * s] = 8 * (3 + s)
+        assert np.array_equal(phases.host, want)
+        # rank 0 owns experts 0-7: the routes of ranks 0 (expert 0) and 1 (expert 3)
+        received = 8 * 3 + 8 * 4 if rank == 0 else 0
+        assert phases.rows == received
+        send_splits, recv_splits = moe.last_splits
+        assert send_splits == [8 * tokens, 0]
+        assert recv_splits == ([24, 32] if rank == 0 else [0, 0])
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_host_logic():
+    """The host side of the peer-memory exchange (ExpertParallelMoe with a
+    PeerExchange) on 2 gloo ranks: the all-gathered counts, the rows each
+    rank receives and the per-rank splits."""
+    mp.spawn(peer_logic_worker, args=(2, free_port()), nprocs=2, join=True)

@@ -87,6 +87,8 @@ SIGNATURES = {
     "adi_cuda_moe_forward_batch": (C.c_int, [_ctx, _h, f32p, C.c_uint32, f32p, u32p, f32p]),
     "adi_cuda_expert_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_ne_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
+    "adi_cuda_ne_matmul_group_device": (C.c_int, [_ctx, C.c_uint32, C.POINTER(_h), C.POINTER(C.c_void_p),
+                                                  C.POINTER(C.c_void_p), C.c_uint32]),
     "adi_cuda_expert_matmul_device_noalloc": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_upload_moe_shard": (C.c_int, [_ctx, C.POINTER(MoeLayerDesc), C.c_uint32, C.c_uint32, C.POINTER(_h)]),
     "adi_cuda_ep_dispatch_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p,
@@ -426,6 +428,16 @@ class Context:
         fn = {"expert": self.lib.adi_cuda_expert_matmul_device, "ne": self.lib.adi_cuda_ne_matmul_device,
               "head": self.lib.adi_cuda_head_matmul_device, "bf16": self.lib.adi_cuda_bf16_matmul_device}[handle.kind]
         _check(fn(self.ptr, handle.value, inputs_ptr, batch, outputs_ptr), fn.__name__)
+
+    def ne_matmul_group_device(self, handles, inputs_ptrs, outputs_ptrs, batch: int):
+        """Several NE projections of one small batch (device pointers): the
+        small-batch group path, two launches for up to eight projections."""
+        n = len(handles)
+        hs = (C.c_uint64 * n)(*[h.value for h in handles])
+        ins = (C.c_void_p * n)(*inputs_ptrs)
+        outs = (C.c_void_p * n)(*outputs_ptrs)
+        _check(self.lib.adi_cuda_ne_matmul_group_device(self.ptr, n, hs, ins, outs, batch),
+               "adi_cuda_ne_matmul_group_device")
 
     # -- codec pieces ----------------------------------------------------------
     def expert_states(self, words) -> np.ndarray:

@@ -9,9 +9,11 @@
 #include "tc_gemm.cuh"
 #include "kernels.cuh"
 #include "ep.cuh"
+#include "decode.cuh"
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -403,6 +405,9 @@ struct adi_cuda_context {
     std::map<uint64_t, std::unique_ptr<Bf16Dev>> bf16s;
     std::map<uint64_t, std::unique_ptr<MoeDev>> moes;
     uint32_t *error_word = nullptr;  // device word kernels flag timeouts in
+    // Arrival counters of the small-batch NE launches (decode.cu), one set
+    // per stream the context launches on (main, side); zero between launches.
+    uint32_t *decode_done = nullptr;
     uint32_t *error_host = nullptr;  // pinned copy of it, read after a synchronise
     // The layer and token count of the last expert-parallel dispatch, whose
     // routes and shared-expert sums the matching combine reads.
@@ -786,8 +791,83 @@ void expert_matmul_noalloc(adi_cuda_context *c, ExpertDev &m, const float *in, u
     c->after_launch(3);
 }
 
+// One NE projection of a small-batch group: matrix, input [batch][cols],
+// output [batch][rows], all device pointers.
+struct NeDecodeCall {
+    NeDev *m;
+    const float *in;
+    float *out;
+};
+
+// Small-batch NE projections through the decode kernels (decode.cu): the
+// projections that share a value table go up to kNeDecodeMaxJobs per launch
+// pair, largest first, so that the job finishing last has the shortest
+// output transform. Every call must satisfy ne_decode_shape.
+void ne_decode_dev(adi_cuda_context *c, std::vector<NeDecodeCall> calls, uint32_t batch) {
+    std::stable_sort(calls.begin(), calls.end(), [](const NeDecodeCall &a, const NeDecodeCall &b) {
+        if (a.m->codec != b.m->codec) return a.m->codec < b.m->codec;
+        return a.m->rows > b.m->rows;
+    });
+    uint32_t *done = c->decode_done + (c->stream == c->side_stream ? kNeDecodeDoneWords : 0);
+    c->stage(kStageNeMatmul);
+    for (size_t first = 0; first < calls.size();) {
+        size_t n = 1;
+        while (first + n < calls.size() && n < kNeDecodeMaxJobs && calls[first + n].m->codec == calls[first].m->codec)
+            ++n;
+        size_t xp_total = 0, acc_total = 0;
+        for (size_t i = 0; i < n; ++i) {
+            xp_total += size_t(batch) * calls[first + i].m->cols;
+            acc_total += size_t(batch) * calls[first + i].m->rows;
+        }
+        // A later launch pair writes these only after the earlier pair has
+        // completed (each kernel waits for its predecessor before its first
+        // write), so consecutive pairs share them; the side stream has its own.
+        const bool side = c->stream == c->side_stream;
+        float *xp = c->buffer<float>(side ? "ne_dec_xp_side" : "ne_dec_xp", xp_total);
+        float *acc = c->buffer<float>(side ? "ne_dec_acc_side" : "ne_dec_acc", acc_total);
+        NeDecodeParams p{};
+        p.jobs = uint32_t(n);
+        p.tokens = batch;
+        p.table = calls[first].m->codec->table.as<float2>();
+        p.done = done;
+        size_t xo = 0, ao = 0;
+        for (size_t i = 0; i < n; ++i) {
+            NeDev &m = *calls[first + i].m;
+            NeDecodeJob &J = p.job[i];
+            J.trellis = m.trellis->as<uint32_t>();
+            J.input = calls[first + i].in;
+            J.su = m.su->as<int8_t>();
+            J.sv = m.sv->as<int8_t>();
+            J.xp = xp + xo;
+            J.acc = acc + ao;
+            J.out = calls[first + i].out;
+            J.rows = m.rows;
+            J.cols = m.cols;
+            J.weight_scale = m.weight_scale;
+            J.in_scale = transform_scale(m.cols);
+            J.out_scale = transform_scale(m.rows);
+            J.chunk_tokens = ne_decode_chunk_tokens(m.cols, batch);
+            J.chunks = (batch + J.chunk_tokens - 1) / J.chunk_tokens;
+            J.tile_row_shift = 0;
+            while ((16u << J.tile_row_shift) < m.rows) ++J.tile_row_shift;
+            J.first_item = p.items;
+            p.items += m.rows / 16 * J.chunks;
+            xo += size_t(batch) * m.cols;
+            ao += size_t(batch) * m.rows;
+        }
+        launch_ne_decode(p, c->sms, c->stream);
+        c->after_launch(2);
+        first += n;
+    }
+    c->stage_end();
+}
+
 void ne_matmul_dev(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batch, float *out) {
     if (batch == 0) invalid("Mach NE batch shape mismatch");
+    if (ne_decode_shape(m.rows, m.cols, batch)) {
+        ne_decode_dev(c, {NeDecodeCall{&m, in, out}}, batch);
+        return;
+    }
     if (c->precision == 1 && tensor_core_shape(m.rows, m.cols) && batch >= kNeTensorCoreMinBatch) {
         ne_matmul_tc(c, m, in, batch, out);
         return;
@@ -1604,6 +1684,8 @@ int adi_cuda_init(int device, adi_cuda_context **out) {
         check(cudaEventCreateWithFlags(&c->join_event, cudaEventDisableTiming), "cudaEventCreate");
         check(cudaMalloc(&c->error_word, sizeof(uint32_t)), "cudaMalloc");
         check(cudaMemset(c->error_word, 0, sizeof(uint32_t)), "cudaMemset");
+        check(cudaMalloc(&c->decode_done, 2 * kNeDecodeDoneWords * sizeof(uint32_t)), "cudaMalloc");
+        check(cudaMemset(c->decode_done, 0, 2 * kNeDecodeDoneWords * sizeof(uint32_t)), "cudaMemset");
         check(cudaHostAlloc(&c->error_host, sizeof(uint32_t), cudaHostAllocDefault), "cudaHostAlloc");
         *out = c.release();
     });
@@ -1617,9 +1699,10 @@ int adi_cuda_shutdown(adi_cuda_context *c) {
         if (c->side_stream) cudaStreamSynchronize(c->side_stream);
         cudaStream_t own = c->own_stream, side = c->side_stream;
         cudaEvent_t fork = c->fork_event, join = c->join_event;
-        uint32_t *error_word = c->error_word, *error_host = c->error_host;
+        uint32_t *error_word = c->error_word, *error_host = c->error_host, *decode_done = c->decode_done;
         delete c;
         if (error_word) cudaFree(error_word);
+        if (decode_done) cudaFree(decode_done);
         if (error_host) cudaFreeHost(error_host);
         if (own) cudaStreamDestroy(own);
         if (side) cudaStreamDestroy(side);
@@ -1828,6 +1911,25 @@ ADI_HOST_MATMUL(adi_cuda_expert_matmul, experts, "expert", expert_matmul_dev)
 ADI_HOST_MATMUL(adi_cuda_ne_matmul, nes, "NE", ne_matmul_dev)
 ADI_HOST_MATMUL(adi_cuda_head_matmul, heads, "head", head_matmul_dev)
 ADI_HOST_MATMUL(adi_cuda_bf16_matmul, bf16s, "bf16", bf16_matmul_dev)
+
+int adi_cuda_ne_matmul_group_device(adi_cuda_context *c, uint32_t count, const adi_cuda_handle *matrices,
+                                    const float *const *inputs, float *const *outputs, uint32_t batch) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (count && (!matrices || !inputs || !outputs)) invalid("matrix, input or output array is null");
+        if (batch == 0) invalid("Mach NE batch shape mismatch");
+        std::vector<NeDecodeCall> decode;
+        std::vector<NeDecodeCall> other;
+        for (uint32_t i = 0; i < count; ++i) {
+            if (!inputs[i] || !outputs[i]) invalid("input or output pointer is null");
+            NeDev &m = lookup(c->nes, matrices[i], "NE");
+            (ne_decode_shape(m.rows, m.cols, batch) ? decode : other).push_back(NeDecodeCall{&m, inputs[i], outputs[i]});
+        }
+        if (!decode.empty()) ne_decode_dev(c, decode, batch);
+        for (const NeDecodeCall &call : other) ne_matmul_dev(c, *call.m, call.in, batch, call.out);
+    });
+}
 
 int adi_cuda_expert_matmul_device_noalloc(adi_cuda_context *c, adi_cuda_handle h, const float *in, uint32_t batch,
                                           float *out) {

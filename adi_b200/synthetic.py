@@ -88,8 +88,22 @@ def _host(t: torch.Tensor, dtype) -> np.ndarray:
     return t.cpu().numpy().view(dtype)
 
 
+def model_tluts(seed: int, device: str = "cuda"):
+    """The model-wide value tables: one expert TLUT [32768 x 8] and one NE
+    TLUT [512 x 2], uniform(-1, 1). A checkpoint has exactly one of each,
+    shared by every matrix of its codec (src/model.cpp:281-301, 495-551 of
+    the reference)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    expert = (torch.rand(32768 * 8, generator=g, device=device) * 2 - 1).cpu().numpy().astype(np.float32)
+    ne = (torch.rand(512 * 2, generator=g, device=device) * 2 - 1).cpu().numpy().astype(np.float32)
+    return expert, ne
+
+
 def moe_block(seed: int, hidden: int = 2048, expert_hidden: int = 512, experts: int = 256,
-              scale_mu: float = -4.0, scale_sigma: float = 0.5, device: str = "cuda") -> MoeBlock:
+              scale_mu: float = -4.0, scale_sigma: float = 0.5, device: str = "cuda", tluts=None) -> MoeBlock:
+    """`tluts` = model_tluts(...) to share the model's value tables; without
+    it the block draws its own."""
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     H, I, E = hidden, expert_hidden, experts
@@ -114,6 +128,8 @@ def moe_block(seed: int, hidden: int = 2048, expert_hidden: int = 512, experts: 
                             .view(torch.int16), np.uint16)
     expert_tlut = uniform(32768 * 8)
     ne_tlut = uniform(512 * 2)
+    if tluts is not None:
+        expert_tlut, ne_tlut = tluts
     block = MoeBlock(H, I, E, router, shared_gate_row, None, None, None, expert_tlut, ne_tlut)
     for projection in range(3):
         rows, columns = block.shape(projection)
@@ -132,9 +148,10 @@ def moe_block(seed: int, hidden: int = 2048, expert_hidden: int = 512, experts: 
 
 
 def ne_matrix(seed: int, rows: int, columns: int, scale_mu: float = -4.0, scale_sigma: float = 0.5,
-              device: str = "cuda") -> NeView:
+              device: str = "cuda", tlut=None) -> NeView:
     """A non-expert projection in the NE codec: uniform code words, +-1
-    signs, a log-normal weight scale, a uniform(-1, 1) TLUT."""
+    signs, a log-normal weight scale, a uniform(-1, 1) TLUT (or the model's,
+    `tlut`)."""
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     tiles = (rows // 16) * (columns // 16)
@@ -143,8 +160,8 @@ def ne_matrix(seed: int, rows: int, columns: int, scale_mu: float = -4.0, scale_
     su = (torch.randint(0, 2, (columns,), generator=g, device=device, dtype=torch.int8) * 2 - 1).cpu().numpy()
     sv = (torch.randint(0, 2, (rows,), generator=g, device=device, dtype=torch.int8) * 2 - 1).cpu().numpy()
     scale = float(torch.exp(scale_mu + scale_sigma * torch.randn(1, generator=g, device=device)).item())
-    tlut = (torch.rand(1024, generator=g, device=device) * 2 - 1).cpu().numpy().astype(np.float32)
-    return NeView(rows, columns, trellis, su, sv, scale, tlut)
+    own = (torch.rand(1024, generator=g, device=device) * 2 - 1).cpu().numpy().astype(np.float32)
+    return NeView(rows, columns, trellis, su, sv, scale, own if tlut is None else tlut)
 
 
 @dataclass

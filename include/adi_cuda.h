@@ -218,6 +218,22 @@ ADI_CUDA_API int adi_cuda_moe_stack_forward_device(adi_cuda_context *context,
                                       adi_cuda_handle head, float *hidden,
                                       uint32_t tokens, float *logits);
 
+/* Several NE projections of one small batch in one call, device pointers:
+ * outputs[i] [batch][rows_i] = mach_ne_matmul(matrices[i], inputs[i]
+ * [batch][cols_i]), the same results as one adi_cuda_ne_matmul_device per
+ * projection. The reference's decode step calls ne_matvec once per
+ * projection on the same input -- query, key, value of full attention
+ * (src/executor.cpp:358-372), qkv and gate of linear attention (:449-458);
+ * this entry takes such a group at once: up to eight projections that share
+ * the model's NE value table and have 1-8 inputs run as two launches in
+ * all (the input transforms, then the products and output transforms), any
+ * others as separate calls. `matrices`, `inputs` and `outputs` are host
+ * arrays of `count` entries. */
+ADI_CUDA_API int adi_cuda_ne_matmul_group_device(adi_cuda_context *context, uint32_t count,
+                                                const adi_cuda_handle *matrices,
+                                                const float *const *inputs, float *const *outputs,
+                                                uint32_t batch);
+
 /* ---- expert parallelism ---------------------------------------------------
  * No counterpart in the reference, which runs one process on one host (its
  * only parallelism is CPU tasks, src/executor.cpp:261, :1302-1371). These

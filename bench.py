@@ -55,7 +55,8 @@ TRELLIS_BYTES = 4096 * 48  # one expert projection's trellis
 GAMMA_BYTES = 160 * 2
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
 # tensor-core expert GEMM, averaged over the gate/up and down launches of one
-# 512-token block, from one ncu capture (profiles/tc_gemm_expert_t512.md).
+# 512-token block, from one ncu capture of the current kernel; a change to
+# the kernel needs a new capture and a new value here.
 EXPERT_GEMM_TRAFFIC_T512 = (134.818560e6 + 20.356608e6 + 55.004928e6 + 19.981824e6) / 2
 
 
@@ -246,14 +247,17 @@ def decode_c3(ctx, stream, local, tokens_list=(1, 4), steps=20):
     projection, the head) per step, eager and replayed from one CUDA graph."""
     from adi_b200 import synthetic
     device = f"cuda:{local}"
+    # One expert and one NE value table for the whole model, as a checkpoint
+    # has them (src/model.cpp:281-301, 495-551).
+    tluts = synthetic.model_tluts(4999, device=device)
     blocks, moe_h, ne_h, ne_bytes = [], [], [], []
     for d in range(C3_DISTINCT):
-        b = synthetic.moe_block(seed=5000 + d, device=device)
+        b = synthetic.moe_block(seed=5000 + d, device=device, tluts=tluts)
         moe_h.append(ctx.upload_moe_layer(b))
         blocks.append((b.shared_bytes(), b.packed_bytes_per_expert()))
         hs, nb = {}, 0
         for i, (name, rows, cols) in enumerate(C3_NE):
-            m = synthetic.ne_matrix(6000 + 16 * d + i, rows, cols, device=device)
+            m = synthetic.ne_matrix(6000 + 16 * d + i, rows, cols, device=device, tlut=tluts[1])
             hs[name] = ctx.upload_ne(m)
             nb += m.trellis.nbytes + m.su.nbytes + m.sv.nbytes + 4
         ne_h.append(hs)
@@ -268,17 +272,23 @@ def decode_c3(ctx, stream, local, tokens_list=(1, 4), steps=20):
         x = synthetic.activations(900 + T, T, 2048, device=device)
         x4 = synthetic.activations(901 + T, T, 4096, device=device)
         y = torch.empty(T, 2048, device=device)
-        q = torch.empty(T, 8192, device=device)
         logits = torch.empty(T, C3_VOCAB, device=device)
         routes = torch.empty(C3_LAYERS, T, 8, dtype=torch.int32, device=device)
+
+        # The projections that read the layer input go as one group (the
+        # attention q/k/v and the gated-delta input projection), the output
+        # projection alone: its input is the attention's output.
+        group = [name for name, _, cols in C3_NE if cols == 2048]
+        outs = {name: torch.empty(T, rows, device=device) for name, rows, _ in C3_NE}
 
         def step(record_routes=False):
             for layer in range(C3_LAYERS):
                 d = layer % C3_DISTINCT
                 ctx.moe_forward_batch_device(moe_h[d], x.data_ptr(), T, y.data_ptr(),
                                              routes[layer].data_ptr() if record_routes else 0, 0)
-                for name, rows, cols in C3_NE:
-                    ctx.matmul_device(ne_h[d][name], (x4 if cols == 4096 else x).data_ptr(), T, q.data_ptr())
+                ctx.ne_matmul_group_device([ne_h[d][n] for n in group], [x.data_ptr()] * len(group),
+                                           [outs[n].data_ptr() for n in group], T)
+                ctx.matmul_device(ne_h[d]["o"], x4.data_ptr(), T, outs["o"].data_ptr())
             ctx.matmul_device(head_h, x.data_ptr(), T, logits.data_ptr())
 
         step(record_routes=True)

@@ -116,7 +116,8 @@ def main():
     x = rng.floats(3 * 128).reshape(3, 128)
     out["head_96x128_b3"] = ref.head_matmul(head, x)
 
-    # The configured block: 16 tokens, and a block
+    # The configured block (hidden 2048, 256 experts of 512, top-8, a
+    # shared expert) at 16 tokens, and a block
     # whose routed experts carry the output.
     meta = {}
     for name, kwargs in (("c1", {}), ("routed", {"seed": 11, "scale_mu": -1.0, "shared_mu": -6.0})):

@@ -1,6 +1,9 @@
 """The allocation-free expert projection (adi_cuda_expert_matmul_device_noalloc)
 against the allocating one (adi_cuda_expert_matmul_device on the CUDA-core
-path), through the C ABI, on two calls in a row; and its size limit.
+path), through the C ABI, on two calls in a row: the same kernels with the
+same parameters, so the outputs must be the same bits; against the oracle's
+mach_expert_matmul within the fp32 bound; with the device's free memory
+unchanged across the calls; and its size limit.
 
 Collected last on purpose: it must hold whether or not other contexts have
 already run on the device. It makes its own context so the precision it
@@ -41,25 +44,38 @@ def noalloc(ctx, h, x, batch, y):
 
 
 @pytest.mark.parametrize("rows,cols,batch", [(512, 2048, 33), (2048, 512, 1), (64, 32, 17)])
-def test_matches_the_allocating_entry(context, rows, cols, batch):
+def test_matches_the_allocating_entry(context, oracle, rows, cols, batch):
     import torch
     import adi_b200
     rng = SplitMix64(0x0A110C + rows + cols + batch)
     m = expert_matrix(rows, cols, rng)
     h = context.upload_expert(m)
     assert needed_bytes(batch, rows, cols) <= SCRATCH_BYTES
+    xs = [rng.floats(batch * cols).reshape(batch, cols) for _ in range(2)]
+    dx = [torch.from_numpy(x).cuda() for x in xs]
+    want = [torch.empty(batch, rows, device="cuda") for _ in range(2)]
+    got = [torch.full((batch, rows), float("nan"), device="cuda") for _ in range(2)]
+    # The allocating entry first (it may grow its arena), and one call of the
+    # allocation-free entry (its first call on a device may load the library's
+    # module there, which places the fixed array): after that, nothing the
+    # entry does may change the device's free memory.
     for call in range(2):
-        x = torch.from_numpy(rng.floats(batch * cols).reshape(batch, cols)).cuda()
-        want = torch.empty(batch, rows, device="cuda")
-        got = torch.full((batch, rows), float("nan"), device="cuda")
+        context.matmul_device(h, dx[call].data_ptr(), batch, want[call].data_ptr())
+    assert noalloc(context, h, dx[0], batch, got[0]) == 0, adi_b200.last_error()
+    context.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    for call in range(2):
+        got[call].fill_(float("nan"))
         torch.cuda.synchronize()
-        context.matmul_device(h, x.data_ptr(), batch, want.data_ptr())
         before = context.launch_count()
-        status = noalloc(context, h, x, batch, got)
+        status = noalloc(context, h, dx[call], batch, got[call])
         assert status == 0, adi_b200.last_error()
         assert context.launch_count() == before + 3
         context.synchronize()
-        err = rel_l2(got.cpu().numpy(), want.cpu().numpy())
+        assert torch.cuda.mem_get_info()[0] == free_before, "the allocation-free entry changed free device memory"
+        g, w = got[call].cpu().numpy(), want[call].cpu().numpy()
+        assert np.array_equal(g.view(np.uint32), w.view(np.uint32)), (rows, cols, batch, call, rel_l2(g, w))
+        err = rel_l2(g, oracle.expert_matmul(m, xs[call]))
         assert err <= FP32_TOL, (rows, cols, batch, call, err)
     h.release()
 

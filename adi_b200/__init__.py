@@ -100,11 +100,14 @@ SIGNATURES = {
     "adi_cuda_bf16_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_moe_forward_batch_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p,
                                                     C.c_void_p, C.c_void_p]),
+    "adi_cuda_moe_forward_batch_logits_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_void_p, C.c_uint32,
+                                                           C.c_void_p, C.c_void_p, C.c_void_p]),
     "adi_cuda_ep_peer_alloc": (C.c_int, [_ctx, C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p]),
     "adi_cuda_ep_peer_connect": (C.c_int, [_ctx, C.c_uint32, C.c_uint32, C.c_void_p]),
     "adi_cuda_ep_peer_close": (C.c_int, [_ctx]),
     "adi_cuda_ep_send_peer_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
-    "adi_cuda_ep_experts_peer_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32]),
+    "adi_cuda_ep_experts_peer_device": (C.c_int, [_ctx, _h]),
+    "adi_cuda_ep_peer_counts_device": (C.c_int, [_ctx, C.c_uint32, C.c_void_p]),
     "adi_cuda_ep_combine_peer_device": (C.c_int, [_ctx, _h, C.c_uint32, C.c_void_p]),
     "adi_cuda_rms_norm_device": (C.c_int, [_ctx, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_float,
                                            C.c_float, C.c_void_p]),
@@ -121,6 +124,7 @@ SIGNATURES = {
 }
 
 INVALID_ARGUMENT = 1
+EP_PEER_HANDLE_BYTES = 272  # ADI_CUDA_EP_PEER_HANDLE_BYTES
 
 _lib: Optional[C.CDLL] = None
 
@@ -358,6 +362,13 @@ class Context:
                                                           route_experts_ptr or None, route_weights_ptr or None),
                "moe_forward_batch_device")
 
+    def moe_forward_batch_logits_device(self, layer: Handle, inputs_ptr: int, logits_ptr: int, batch: int,
+                                        outputs_ptr: int, experts_ptr: int = 0, weights_ptr: int = 0):
+        """The block with prescribed router logits [batch][experts + 1]."""
+        _check(self.lib.adi_cuda_moe_forward_batch_logits_device(self.ptr, layer.value, inputs_ptr, logits_ptr,
+                                                                  batch, outputs_ptr, experts_ptr, weights_ptr),
+               "adi_cuda_moe_forward_batch_logits_device")
+
     def moe_stack_forward_device(self, layers, norms_ptr: int, final_norm_ptr: int, head, hidden_ptr: int,
                                  tokens: int, logits_ptr: int = 0):
         """hidden [tokens][H] (device, updated in place) through the MoE stack
@@ -380,29 +391,32 @@ class Context:
     # -- peer-memory exchange of expert parallelism ---------------------------
     def ep_peer_alloc(self, recv_rows: int, returned_rows: int, hidden: int) -> bytes:
         """Allocates this rank's exchange buffers; returns their IPC handles
-        (192 bytes) for the other ranks."""
-        buf = C.create_string_buffer(192)
+        and sizes (EP_PEER_HANDLE_BYTES) for the other ranks."""
+        buf = C.create_string_buffer(EP_PEER_HANDLE_BYTES)
         _check(self.lib.adi_cuda_ep_peer_alloc(self.ptr, recv_rows, returned_rows, hidden, buf), "ep_peer_alloc")
         return buf.raw
 
     def ep_peer_connect(self, rank: int, world: int, handles: list):
         blob = b"".join(handles)
-        if len(blob) != 192 * world:
-            raise ValueError("one 192-byte handle set per rank is required")
+        if len(blob) != EP_PEER_HANDLE_BYTES * world:
+            raise ValueError(f"one {EP_PEER_HANDLE_BYTES}-byte handle blob per rank is required")
         buf = C.create_string_buffer(blob, len(blob))
         _check(self.lib.adi_cuda_ep_peer_connect(self.ptr, rank, world, buf), "ep_peer_connect")
 
     def ep_peer_close(self):
         _check(self.lib.adi_cuda_ep_peer_close(self.ptr), "ep_peer_close")
 
-    def ep_send_peer_device(self, shard: Handle, inputs_ptr: int, tokens: int, all_counts_host):
-        counts = np.ascontiguousarray(all_counts_host, dtype=np.uint32)
-        _check(self.lib.adi_cuda_ep_send_peer_device(self.ptr, shard.value, inputs_ptr, tokens,
-                                                     counts.ctypes.data_as(C.c_void_p)), "ep_send_peer_device")
+    def ep_send_peer_device(self, shard: Handle, inputs_ptr: int, tokens: int, counts_ptr: int):
+        """Counts to every rank, barrier, rows to the experts' ranks, barrier
+        (all on the device)."""
+        _check(self.lib.adi_cuda_ep_send_peer_device(self.ptr, shard.value, inputs_ptr, tokens, counts_ptr),
+               "ep_send_peer_device")
 
-    def ep_experts_peer_device(self, shard: Handle, all_counts_ptr: int, rows: int):
-        _check(self.lib.adi_cuda_ep_experts_peer_device(self.ptr, shard.value, all_counts_ptr, rows),
-               "ep_experts_peer_device")
+    def ep_experts_peer_device(self, shard: Handle):
+        _check(self.lib.adi_cuda_ep_experts_peer_device(self.ptr, shard.value), "ep_experts_peer_device")
+
+    def ep_peer_counts_device(self, experts: int, counts_ptr: int):
+        _check(self.lib.adi_cuda_ep_peer_counts_device(self.ptr, experts, counts_ptr), "ep_peer_counts_device")
 
     def ep_combine_peer_device(self, shard: Handle, tokens: int, outputs_ptr: int):
         _check(self.lib.adi_cuda_ep_combine_peer_device(self.ptr, shard.value, tokens, outputs_ptr),

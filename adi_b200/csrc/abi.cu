@@ -10,6 +10,7 @@
 #include "kernels.cuh"
 #include "ep.cuh"
 #include "decode.cuh"
+#include "pipeline.cuh"
 
 #include <cuda_runtime.h>
 
@@ -367,14 +368,24 @@ struct Profiler {
 // This rank's side of the peer-memory exchange of expert parallelism: its
 // receive buffer (rows other ranks send to its experts, with each row's way
 // back), its returned buffer (its routes' expert outputs, written by the
-// experts' ranks), and every rank's pointers to all of them (its own, and
-// the others' opened through CUDA IPC).
+// experts' ranks), its synchronisation buffer (barrier flags and every
+// rank's expert counts, written by every rank), and every rank's pointers to
+// all of them (its own, and the others' opened through CUDA IPC), with every
+// rank's capacities.
 struct PeerExchange {
+    static constexpr size_t kFlagsWords = kEpMaxPeers;
+    static constexpr size_t kSyncWords = kFlagsWords + size_t(kEpMaxPeers) * kEpMaxExperts;
     uint32_t rank = 0, world = 0, hidden = 0;
     uint32_t recv_capacity = 0, returned_capacity = 0;
-    std::unique_ptr<DeviceArray> recv_rows, recv_meta, returned_rows;  // own, cudaMalloc'd (IPC-able)
-    std::vector<void *> opened;                                          // peers' mappings, closed on reset
-    std::unique_ptr<DeviceArray> recv_rows_ptrs, recv_meta_ptrs, returned_ptrs;  // [world] device pointer tables
+    uint32_t recv_caps[kEpMaxPeers] = {}, returned_caps[kEpMaxPeers] = {};  // every rank's
+    std::unique_ptr<DeviceArray> recv_rows, recv_meta, returned_rows, sync;  // own, cudaMalloc'd (IPC-able)
+    std::unique_ptr<DeviceArray> local;  // own, not shared: [0] barriers passed, [1] last send's verdict
+    std::vector<void *> opened;                                              // peers' mappings, closed on reset
+    // [world] device pointer tables: receive rows, receive records, returned
+    // rows, flags, counts
+    std::unique_ptr<DeviceArray> recv_rows_ptrs, recv_meta_ptrs, returned_ptrs, flags_ptrs, counts_ptrs;
+    uint32_t *own_flags() const { return sync->as<uint32_t>(); }
+    uint32_t *own_counts() const { return sync->as<uint32_t>() + kFlagsWords; }
     void close_peers() {
         for (void *ptr : opened) cudaIpcCloseMemHandle(ptr);
         opened.clear();
@@ -443,7 +454,11 @@ struct adi_cuda_context {
         const uint32_t flags = *error_host;
         if (flags) {
             check(cudaMemset(error_word, 0, sizeof flags), "clear error word");
-            throw Status(ADI_CUDA_TIMEOUT, "a bounded device wait timed out; results are invalid");
+            if (flags & kErrorTimeout)
+                throw Status(ADI_CUDA_TIMEOUT, "a bounded device wait timed out; results are invalid");
+            throw Status(ADI_CUDA_INVALID_ARGUMENT,
+                         "an expert-parallel exchange did not fit a rank's buffers, or its counts did not match "
+                         "its rows; nothing was exchanged and results are invalid");
         }
     }
 
@@ -1144,8 +1159,11 @@ void shared_expert(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, 
 // input row, position -> expert, 0-based in L's experts) and the work lists
 // in chunks of `nt` positions. Returns the down projection's two partial
 // accumulators, [2][P][H], before its output transform.
+// `limit`, when not null, is a device count of the positions actually
+// planned (P is then an upper bound): the per-position kernels loop over the
+// positions below it.
 float *routed_experts(adi_cuda_context *c, MoeDev &L, const float *in, size_t P, const RouteParams &rp, uint32_t nt,
-                      bool tc) {
+                      bool tc, const uint32_t *limit = nullptr) {
     const uint32_t H = L.hidden, I = L.inner;
     const uint32_t rb_gate_up = expert_rows_per_item(H), rb_down = expert_rows_per_item(I);
     cudaStream_t s = c->stream;
@@ -1171,6 +1189,7 @@ float *routed_experts(adi_cuda_context *c, MoeDev &L, const float *in, size_t P,
         pp.su_stride = H;
         pp.cols = H;
         pp.rows = uint32_t(P);
+        pp.limit = limit;
         pp.scale = transform_scale(H);
         pp.jobs = 2;
         pp.su_is_f16 = 1;
@@ -1211,6 +1230,7 @@ float *routed_experts(adi_cuda_context *c, MoeDev &L, const float *in, size_t P,
         mp.xh = xh_d;
         mp.kx = kx_d;
         mp.positions = uint32_t(P);
+        mp.limit = limit;
         c->stage(kStageSwiglu);
         launch_mid_f16(mp, s);
         c->stage_end();
@@ -1242,6 +1262,7 @@ float *routed_experts(adi_cuda_context *c, MoeDev &L, const float *in, size_t P,
         pp.cols = H;
         pp.scale = transform_scale(H);
         pp.rows = uint32_t(P);
+        pp.limit = limit;
         pp.jobs = 2;
         pp.su_is_f16 = 1;
         c->stage(kStagePrep);
@@ -1277,6 +1298,7 @@ float *routed_experts(adi_cuda_context *c, MoeDev &L, const float *in, size_t P,
         mp.scale = transform_scale(I);
         mp.xd = xd;
         mp.positions = uint32_t(P);
+        mp.limit = limit;
         c->stage(kStageSwiglu);
         launch_mid(mp, s);
         c->stage_end();
@@ -1299,8 +1321,10 @@ float *routed_experts(adi_cuda_context *c, MoeDev &L, const float *in, size_t P,
     return acc_d;
 }
 
+// `given_logits`, when not null, [T][E + 1] replace the router and shared
+// gate products (prescribed routing); top_experts and all after unchanged.
 void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T, float *out,
-                     uint32_t *route_experts_out, float *route_weights_out) {
+                     uint32_t *route_experts_out, float *route_weights_out, const float *given_logits = nullptr) {
     if (T == 0) invalid("MoE batch shape mismatch");
     if (L.local_experts != L.experts)
         invalid("MoE layer handle holds a shard of the routed experts; use the expert-parallel entries");
@@ -1345,7 +1369,18 @@ void moe_forward_dev(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t T
     uint32_t *counts2 = c->buffer<uint32_t>("moe_item_counts", 2);
     rp.count_gate_up = counts2;
     rp.count_down = counts2 + 1;
-    const uint32_t router_launches = route_tokens(c, L, in, T, logits, re, rw);
+    uint32_t router_launches = 1;
+    if (given_logits) {
+        c->stage(kStageRouter);
+        check(cudaMemcpyAsync(logits, given_logits, size_t(T) * (E + 1) * 4, cudaMemcpyDeviceToDevice, s),
+              "logits copy");
+        c->stage_end();
+        c->stage(kStageTopk);
+        launch_top_experts(logits, E + 1, T, E, re, rw, s);
+        c->stage_end();
+    } else {
+        router_launches = route_tokens(c, L, in, T, logits, re, rw);
+    }
     c->stage(kStageRoute);
     const uint32_t route_launches = launch_route(rp, s);
     c->stage_end();
@@ -1568,20 +1603,36 @@ void ep_dispatch_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const floa
     c->ep_tokens = T;
 }
 
+// Where the peer exchange's expert output rows go: straight back into each
+// sender's returned buffer, bounded by that buffer's capacity.
+struct EpReturn {
+    float *const *rows;       // [world] device table of every rank's returned buffer
+    const uint32_t *meta;     // this rank's receive records
+    uint32_t world;
+    const uint32_t *capacity; // [world] returned rows each rank holds (host)
+};
+
 // The shard's routed experts on received rows; one output row per row.
 // recv_counts[s * counts_stride + counts_offset + e]: rows of sender s for
-// local expert e. With return_rows, each output row goes straight back to
-// its sender (recv_meta), instead of to expert_rows.
+// local expert e. rows = kEpRowsFromCounts takes the row count from the
+// counts on the device (at most `capacity`): every launch is then sized for
+// the capacity and loops over the rows planned. With `ret`, each output row
+// goes straight back to its sender instead of to expert_rows.
 void ep_experts_dev(adi_cuda_context *c, MoeDev &L, const float *recv, const uint32_t *recv_counts, uint32_t world,
                     uint32_t rows, float *expert_rows, uint32_t counts_stride, uint32_t counts_offset,
-                    float *const *return_rows = nullptr, const uint32_t *recv_meta = nullptr) {
+                    const EpReturn *ret = nullptr, uint32_t capacity = 0, const uint32_t *verdict = nullptr) {
     const uint32_t H = L.hidden, I = L.inner, local = L.local_experts;
     if (world == 0 || uint64_t(world) * local > 1024) invalid("expert-parallel world times shard experts must be 1..1024");
+    const bool from_counts = rows == kEpRowsFromCounts;
+    if (from_counts && capacity == 0) invalid("expert-parallel receive capacity is zero");
     if (rows == 0) return;
     cudaStream_t s = c->stream;
-    const size_t P = rows;
+    const size_t P = from_counts ? capacity : rows;
     const bool tc = c->precision == 1 && expert_tensor_core_shape(I, H) && expert_tensor_core_shape(H, I);
-    const uint32_t nt = tc ? kTcMaxN : tokens_per_item((uint64_t(rows) + local - 1) / local);
+    // Positions per CUDA-core work item from the expected rows per expert
+    // (with device-side counts: the capacity's average share per rank).
+    const uint64_t expected_rows = from_counts ? (uint64_t(capacity) + world - 1) / world : rows;
+    const uint32_t nt = tc ? kTcMaxN : tokens_per_item((expected_rows + local - 1) / local);
     const uint32_t rb_gate_up = expert_rows_per_item(H), rb_down = expert_rows_per_item(I);
     RouteParams rp{};
     rp.grouped = c->buffer<uint32_t>("ep_grouped", P);
@@ -1602,6 +1653,9 @@ void ep_experts_dev(adi_cuda_context *c, MoeDev &L, const float *recv, const uin
     pp.world = world;
     pp.local = local;
     pp.rows = rows;
+    pp.capacity = uint32_t(P);
+    pp.verdict = verdict;
+    pp.error = c->error_word;
     pp.grouped = rp.grouped;
     pp.pos_expert = rp.pos_expert;
     pp.placed = counts3 + 2;
@@ -1616,7 +1670,7 @@ void ep_experts_dev(adi_cuda_context *c, MoeDev &L, const float *recv, const uin
     launch_ep_plan(pp, s);
     c->stage_end();
     c->after_launch(1);
-    float *acc_d = routed_experts(c, L, recv, P, rp, nt, tc);
+    float *acc_d = routed_experts(c, L, recv, P, rp, nt, tc, from_counts ? pp.placed : nullptr);
     EpFinalizeParams fp{};
     fp.acc_down = acc_d;
     fp.half_stride = P * H;
@@ -1625,11 +1679,16 @@ void ep_experts_dev(adi_cuda_context *c, MoeDev &L, const float *recv, const uin
     fp.placed = pp.placed;
     fp.sv_down = L.sv[2]->as<uint16_t>();
     fp.hidden = H;
-    fp.positions = rows;
+    fp.positions = uint32_t(P);
     fp.scale = transform_scale(H);
     fp.expert_rows = expert_rows;
-    fp.return_rows = return_rows;
-    fp.recv_meta = recv_meta;
+    fp.error = c->error_word;
+    if (ret) {
+        fp.return_rows = ret->rows;
+        fp.recv_meta = ret->meta;
+        fp.return_world = ret->world;
+        for (uint32_t r = 0; r < ret->world && r < kEpMaxPeers; ++r) fp.returned_capacity[r] = ret->capacity[r];
+    }
     c->stage(kStageCombine);
     launch_ep_finalize(fp, s);
     c->stage_end();
@@ -1661,6 +1720,34 @@ void ep_combine_dev(adi_cuda_context *c, uint64_t handle, MoeDev &L, const float
     c->after_launch(1);
     c->ep_layer = 0;
     c->ep_tokens = 0;
+}
+
+}  // namespace
+
+namespace {
+
+// Every rank's copy of the flag barrier (EpBarrierParams), on the stream.
+void peer_barrier(adi_cuda_context *c) {
+    PeerExchange &px = c->peers;
+    EpBarrierParams bp{};
+    bp.peer_flags = px.flags_ptrs->as<uint32_t *>();
+    bp.own_flags = px.own_flags();
+    bp.epoch = px.local->as<uint32_t>();
+    bp.rank = px.rank;
+    bp.world = px.world;
+    bp.error = c->error_word;
+    launch_ep_barrier(bp, c->stream);
+    c->after_launch(1);
+}
+
+PeerExchange &connected_peers(adi_cuda_context *c, MoeDev &L) {
+    PeerExchange &px = c->peers;
+    if (px.world == 0) invalid("peer exchange not connected");
+    if (L.local_experts * px.world != L.experts)
+        invalid("the shard's experts times the world size must be the layer's experts");
+    if (L.experts > kEpMaxExperts) invalid("peer exchange supports at most 1024 experts");
+    if (L.hidden != px.hidden) invalid("peer exchange hidden size mismatch");
+    return px;
 }
 
 }  // namespace
@@ -1973,6 +2060,18 @@ int adi_cuda_moe_forward_batch_device(adi_cuda_context *c, adi_cuda_handle h, co
     });
 }
 
+int adi_cuda_moe_forward_batch_logits_device(adi_cuda_context *c, adi_cuda_handle h, const float *in,
+                                             const float *router_logits, uint32_t batch, float *out,
+                                             uint32_t *route_experts, float *route_weights) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!in || !out || !router_logits) invalid("input, logits or output pointer is null");
+        moe_forward_dev(c, lookup(c->moes, h, "MoE layer"), in, batch, out, route_experts, route_weights,
+                        router_logits);
+    });
+}
+
 int adi_cuda_moe_stack_forward_device(adi_cuda_context *c, const adi_cuda_handle *layers, uint32_t layer_count,
                                       const uint16_t *norms_bf16, const uint16_t *final_norm_bf16,
                                       adi_cuda_handle head, float *hidden, uint32_t tokens, float *logits) {
@@ -2175,6 +2274,13 @@ int adi_cuda_ep_experts_device(adi_cuda_context *c, adi_cuda_handle h, const flo
     });
 }
 
+// The record each rank publishes beside its IPC handles.
+struct PeerRecord {
+    uint32_t recv_rows, returned_rows, hidden, magic;
+};
+constexpr uint32_t kPeerRecordMagic = 0xAD1B2000u;
+static_assert(ADI_CUDA_EP_PEER_HANDLE_BYTES == 4 * 64 + sizeof(PeerRecord), "handle blob layout");
+
 int adi_cuda_ep_peer_alloc(adi_cuda_context *c, uint32_t recv_rows, uint32_t returned_rows, uint32_t hidden,
                            uint8_t *handles) {
     return guarded([&] {
@@ -2192,15 +2298,24 @@ int adi_cuda_ep_peer_alloc(adi_cuda_context *c, uint32_t recv_rows, uint32_t ret
         alloc(px.recv_rows, size_t(recv_rows) * hidden * 4);
         alloc(px.recv_meta, size_t(recv_rows) * 4);
         alloc(px.returned_rows, size_t(returned_rows) * hidden * 4);
+        alloc(px.sync, PeerExchange::kSyncWords * 4);
+        alloc(px.local, 8);
+        // Flags and counts start at zero before any rank can signal: the
+        // handles reach the other ranks only after this returns.
+        check(cudaMemset(px.sync->ptr, 0, PeerExchange::kSyncWords * 4), "cudaMemset");
+        check(cudaMemset(px.local->ptr, 0, 8), "cudaMemset");
+        check(cudaDeviceSynchronize(), "synchronize");
         px.recv_capacity = recv_rows;
         px.returned_capacity = returned_rows;
         px.hidden = hidden;
-        void *bases[3] = {px.recv_rows->ptr, px.recv_meta->ptr, px.returned_rows->ptr};
-        for (int i = 0; i < 3; ++i) {
+        void *bases[4] = {px.recv_rows->ptr, px.recv_meta->ptr, px.returned_rows->ptr, px.sync->ptr};
+        for (int i = 0; i < 4; ++i) {
             cudaIpcMemHandle_t hd;
             check(cudaIpcGetMemHandle(&hd, bases[i]), "cudaIpcGetMemHandle");
             std::memcpy(handles + 64 * i, &hd, 64);
         }
+        const PeerRecord record{recv_rows, returned_rows, hidden, kPeerRecordMagic};
+        std::memcpy(handles + 4 * 64, &record, sizeof record);
     });
 }
 
@@ -2211,25 +2326,42 @@ int adi_cuda_ep_peer_connect(adi_cuda_context *c, uint32_t rank, uint32_t world,
         PeerExchange &px = c->peers;
         if (!handles || !px.recv_rows) invalid("peer exchange not allocated");
         if (world == 0 || world > kEpMaxPeers || rank >= world) invalid("peer exchange rank or world is invalid");
+        // Every rank's buffers must take what this rank's kernels write
+        // into them: the same row width everywhere; capacities per rank.
+        for (uint32_t r = 0; r < world; ++r) {
+            PeerRecord record;
+            std::memcpy(&record, handles + size_t(r) * ADI_CUDA_EP_PEER_HANDLE_BYTES + 4 * 64, sizeof record);
+            if (record.magic != kPeerRecordMagic) invalid("peer exchange handles are not this library's");
+            if (record.hidden != px.hidden) invalid("peer exchange ranks differ in hidden size");
+            px.recv_caps[r] = record.recv_rows;
+            px.returned_caps[r] = record.returned_rows;
+        }
         px.close_peers();
-        std::vector<void *> tables[3];
-        void *own[3] = {px.recv_rows->ptr, px.recv_meta->ptr, px.returned_rows->ptr};
+        std::vector<void *> tables[4];
+        void *own[4] = {px.recv_rows->ptr, px.recv_meta->ptr, px.returned_rows->ptr, px.sync->ptr};
         for (uint32_t r = 0; r < world; ++r)
-            for (int i = 0; i < 3; ++i) {
+            for (int i = 0; i < 4; ++i) {
                 if (r == rank) {
                     tables[i].push_back(own[i]);
                     continue;
                 }
                 cudaIpcMemHandle_t hd;
-                std::memcpy(&hd, handles + (size_t(r) * 3 + i) * 64, 64);
+                std::memcpy(&hd, handles + size_t(r) * ADI_CUDA_EP_PEER_HANDLE_BYTES + 64 * i, 64);
                 void *ptr = nullptr;
                 check(cudaIpcOpenMemHandle(&ptr, hd, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
                 px.opened.push_back(ptr);
                 tables[i].push_back(ptr);
             }
-        std::unique_ptr<DeviceArray> *dst[3] = {&px.recv_rows_ptrs, &px.recv_meta_ptrs, &px.returned_ptrs};
-        for (int i = 0; i < 3; ++i)
-            *dst[i] = upload_bytes(tables[i].data(), tables[i].size() * sizeof(void *), "peer pointers");
+        std::vector<void *> flags(world), counts(world);
+        for (uint32_t r = 0; r < world; ++r) {
+            flags[r] = tables[3][r];
+            counts[r] = static_cast<uint32_t *>(tables[3][r]) + PeerExchange::kFlagsWords;
+        }
+        px.recv_rows_ptrs = upload_bytes(tables[0].data(), world * sizeof(void *), "peer pointers");
+        px.recv_meta_ptrs = upload_bytes(tables[1].data(), world * sizeof(void *), "peer pointers");
+        px.returned_ptrs = upload_bytes(tables[2].data(), world * sizeof(void *), "peer pointers");
+        px.flags_ptrs = upload_bytes(flags.data(), world * sizeof(void *), "peer pointers");
+        px.counts_ptrs = upload_bytes(counts.data(), world * sizeof(void *), "peer pointers");
         px.rank = rank;
         px.world = world;
     });
@@ -2245,70 +2377,65 @@ int adi_cuda_ep_peer_close(adi_cuda_context *c) {
 }
 
 int adi_cuda_ep_send_peer_device(adi_cuda_context *c, adi_cuda_handle h, const float *in, uint32_t tokens,
-                                 const uint32_t *all_counts) {
+                                 const uint32_t *counts) {
     return guarded([&] {
         std::lock_guard<std::mutex> g(require(c)->lock);
         use_device(c);
-        PeerExchange &px = c->peers;
         auto &L = lookup(c->moes, h, "MoE layer");
-        if (!in || !all_counts) invalid("input or count pointer is null");
-        if (px.world == 0) invalid("peer exchange not connected");
+        PeerExchange &px = connected_peers(c, L);
+        if (!in || !counts) invalid("input or count pointer is null");
         if (c->ep_layer != h || c->ep_tokens != tokens || tokens == 0)
             invalid("peer send must follow a dispatch of the same layer and token count");
-        const uint32_t E = L.experts, local = L.local_experts, world = px.world;
-        if (local * world != E) invalid("the shard's experts times the world size must be the layer's experts");
-        if (L.hidden != px.hidden) invalid("peer exchange hidden size mismatch");
+        // 1. This rank's counts into row `rank` of every rank's all_counts.
+        EpCountsParams cp{};
+        cp.counts = counts;
+        cp.experts = L.experts;
+        cp.rank = px.rank;
+        cp.world = px.world;
+        cp.peer_counts = px.counts_ptrs->as<uint32_t *>();
+        c->stage(kStageRoute);
+        launch_ep_counts_peer(cp, c->stream);
+        c->after_launch(1);
+        peer_barrier(c);
+        // 2. The rows, placed from this rank's copy of every rank's counts.
         EpSendParams sp{};
         sp.x = in;
         sp.grouped = c->buffer<uint32_t>("ep_send_grouped", size_t(tokens) * 8);
         sp.pos_expert = c->buffer<uint32_t>("ep_send_pos_expert", size_t(tokens) * 8);
+        sp.all_counts = px.own_counts();
         sp.positions = tokens * 8;
         sp.hidden = L.hidden;
         sp.rank = px.rank;
-        sp.world = world;
-        sp.local = local;
-        // From the exchanged counts (host copy, [world][E]): where this rank's
-        // rows for each destination start in its receive buffer, and where
-        // they start among this rank's positions.
-        uint64_t sent = 0;
-        for (uint32_t d = 0; d < world; ++d) {
-            uint64_t base = 0, mine = 0, total = 0;
-            for (uint32_t s = 0; s < world; ++s)
-                for (uint32_t e = d * local; e < (d + 1) * local; ++e) {
-                    const uint64_t n = all_counts[size_t(s) * E + e];
-                    if (s < px.rank) base += n;
-                    if (s == px.rank) mine += n;
-                    total += n;
-                }
-            if (total > px.recv_capacity) invalid("peer exchange receive buffer too small for this step");
-            sp.base[d] = uint32_t(base);
-            sp.start[d] = uint32_t(sent);
-            sent += mine;
+        sp.world = px.world;
+        sp.local = L.local_experts;
+        sp.experts = L.experts;
+        for (uint32_t r = 0; r < px.world; ++r) {
+            sp.recv_capacity[r] = px.recv_caps[r];
+            sp.returned_capacity[r] = px.returned_caps[r];
         }
-        if (sent != uint64_t(tokens) * 8) invalid("exchanged counts do not match this rank's routes");
         sp.recv_rows = px.recv_rows_ptrs->as<float *>();
         sp.recv_meta = px.recv_meta_ptrs->as<uint32_t *>();
-        c->stage(kStageRoute);
+        sp.error = c->error_word;
+        sp.verdict = px.local->as<uint32_t>() + 1;
         launch_ep_send_peer(sp, c->stream);
-        c->stage_end();
         c->after_launch(1);
+        // 3. No rank reads its receive buffer before every rank has written.
+        peer_barrier(c);
+        c->stage_end();
     });
 }
 
-int adi_cuda_ep_experts_peer_device(adi_cuda_context *c, adi_cuda_handle h, const uint32_t *all_counts,
-                                    uint32_t rows) {
+int adi_cuda_ep_experts_peer_device(adi_cuda_context *c, adi_cuda_handle h) {
     return guarded([&] {
         std::lock_guard<std::mutex> g(require(c)->lock);
         use_device(c);
-        PeerExchange &px = c->peers;
         auto &L = lookup(c->moes, h, "MoE layer");
-        if (!all_counts) invalid("count pointer is null");
-        if (px.world == 0) invalid("peer exchange not connected");
-        if (rows > px.recv_capacity) invalid("peer exchange receive buffer too small for this step");
-        if (L.local_experts * px.world != L.experts)
-            invalid("the shard's experts times the world size must be the layer's experts");
-        ep_experts_dev(c, L, px.recv_rows->as<float>(), all_counts, px.world, rows, nullptr, L.experts,
-                       L.first_expert, px.returned_ptrs->as<float *>(), px.recv_meta->as<uint32_t>());
+        PeerExchange &px = connected_peers(c, L);
+        const EpReturn ret{px.returned_ptrs->as<float *>(), px.recv_meta->as<uint32_t>(), px.world, px.returned_caps};
+        ep_experts_dev(c, L, px.recv_rows->as<float>(), px.own_counts(), px.world, kEpRowsFromCounts, nullptr,
+                       kEpMaxExperts, L.first_expert, &ret, px.recv_capacity, px.local->as<uint32_t>() + 1);
+        // No rank reads its returned buffer before every rank has written.
+        peer_barrier(c);
     });
 }
 
@@ -2321,6 +2448,20 @@ int adi_cuda_ep_combine_peer_device(adi_cuda_context *c, adi_cuda_handle h, uint
         if (px.world == 0) invalid("peer exchange not connected");
         if (size_t(tokens) * 8 > px.returned_capacity) invalid("peer exchange returned buffer too small");
         ep_combine_dev(c, h, lookup(c->moes, h, "MoE layer"), px.returned_rows->as<float>(), tokens, outputs);
+    });
+}
+
+int adi_cuda_ep_peer_counts_device(adi_cuda_context *c, uint32_t experts, uint32_t *counts) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        PeerExchange &px = c->peers;
+        if (!counts) invalid("count pointer is null");
+        if (px.world == 0) invalid("peer exchange not connected");
+        if (experts == 0 || experts > kEpMaxExperts) invalid("expert count out of range");
+        check(cudaMemcpy2DAsync(counts, experts * 4, px.own_counts(), kEpMaxExperts * 4, experts * 4, px.world,
+                                cudaMemcpyDeviceToDevice, c->stream),
+              "counts copy");
     });
 }
 

@@ -226,15 +226,29 @@ __device__ __forceinline__ ItemPos locate(const NeDecodeParams &p, uint32_t item
     return ItemPos{j, local & ((1u << shift) - 1u), local >> shift};
 }
 
-__device__ __forceinline__ void load_batch(const NeDecodeParams &p, uint32_t item, uint32_t k0, uint32_t w,
-                                           uint32_t lane, uint32_t (&dst)[kWordBatch]) {
+// Where warp w's lane finds the words of an item's class: tile (row,
+// w + 8 k) at wp + k * 8 * 32, k < K.
+struct ClassWords {
+    const uint32_t *wp;
+    uint32_t K;
+};
+
+__device__ __forceinline__ ClassWords class_words(const NeDecodeParams &p, uint32_t item, uint32_t w, uint32_t lane) {
     const ItemPos at = locate(p, item);
     const NeDecodeJob &J = p.job[at.job];
-    const uint32_t TC = J.cols >> 4, K = TC >> 3;
-    const uint32_t *wp = J.trellis + ((size_t)at.tile_row * TC + w) * kNeU32PerTile + lane;
+    const uint32_t TC = J.cols >> 4;
+    return ClassWords{J.trellis + ((size_t)at.tile_row * TC + w) * kNeU32PerTile + lane, TC >> 3};
+}
+
+__device__ __forceinline__ void load_batch(const ClassWords &c, uint32_t k0, uint32_t (&dst)[kWordBatch]) {
+    const uint32_t *src = c.wp + size_t(k0) * 8 * kNeU32PerTile;
+    if (k0 + kWordBatch <= c.K) {
 #pragma unroll
-    for (uint32_t i = 0; i < kWordBatch; ++i)
-        dst[i] = k0 + i < K ? load_stream(wp + size_t(k0 + i) * 8 * kNeU32PerTile) : 0u;
+        for (uint32_t i = 0; i < kWordBatch; ++i) dst[i] = load_stream(src + i * 8 * kNeU32PerTile);
+    } else {
+#pragma unroll
+        for (uint32_t i = 0; i < kWordBatch; ++i) dst[i] = k0 + i < c.K ? load_stream(src + i * 8 * kNeU32PerTile) : 0u;
+    }
 }
 
 template <int NT>
@@ -257,7 +271,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) ne_decode_kernel(const __gr
     // and the wait for the prep overlap the words' flight.
     static_assert(kNeTableRows == 2 * kDecodeThreads, "two table entries per thread");
     const float2 e0 = __ldg(p.table + threadIdx.x), e1 = __ldg(p.table + threadIdx.x + kDecodeThreads);
-    if (item < p.items) load_batch(p, item, 0, w, lane, words);
+    ClassWords next_words{nullptr, 0};
+    if (item < p.items) load_batch(class_words(p, item, w, lane), 0, words);
     // Replicated: entry i of copy c at i * 16 + c, so lane c and lane c + 16
     // read banks 2c, 2c + 1 whatever i. Each store instruction of a warp
     // writes the sixteen copies of two of its entries (256 contiguous bytes,
@@ -280,6 +295,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) ne_decode_kernel(const __gr
     // (2p & 0x1FF80) | 8c.
     const char *table_bytes = reinterpret_cast<const char *>(table);
     const uint32_t copy8 = (lane & (kCopies - 1u)) * 8u;
+    // Only bits 0..15 of a state reach bits 7..16 of 2p, so a state may
+    // carry garbage above bit 15.
     auto gather = [&](uint32_t state) -> float2 {
         const uint32_t p2 = state * (2u * state + 2u);
         return *reinterpret_cast<const float2 *>(table_bytes + ((p2 & 0x1FF80u) | copy8));
@@ -318,21 +335,27 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) ne_decode_kernel(const __gr
 #pragma unroll
         for (int q = 0; q < NT; ++q) acc[q] = 0.0f;
 
+        const ClassWords cur_words{J.trellis + ((size_t)at.tile_row * TC + w) * kNeU32PerTile + lane, K};
+        const bool has_next = item + stride < p.items;
+        if (has_next) next_words = class_words(p, item + stride, w, lane);
         for (uint32_t k0 = 0; k0 < K; k0 += kWordBatch) {
             // The batch after this one: this item's next, or the next item's first.
-            const bool more = k0 + kWordBatch < K;
-            const uint32_t n_item = more ? item : item + stride;
-            if (n_item < p.items) load_batch(p, n_item, more ? k0 + kWordBatch : 0u, w, lane, next);
+            if (k0 + kWordBatch < K)
+                load_batch(cur_words, k0 + kWordBatch, next);
+            else if (has_next)
+                load_batch(next_words, 0, next);
 #pragma unroll
             for (uint32_t i = 0; i < kWordBatch; ++i) {
                 if (k0 + i >= K) break;
                 const uint32_t tc = w + 8u * (k0 + i);
                 const uint32_t v = words[i];
                 const uint32_t v2 = __shfl_sync(0xffffffffu, v, (lane + 1u) & 31u);
-                const uint32_t s0 = v & 0xFFFFu;
+                // States 4L .. 4L+3: stream bytes (1,0), (0,3), (3,2) of this
+                // lane's word and (2, next word's 1); bits above 15 are ignored.
+                const uint32_t s0 = v;
                 const uint32_t s1 = __byte_perm(v, 0, 0x4403);
                 const uint32_t s2 = v >> 16;
-                const uint32_t s3 = __byte_perm(v, v2, 0x0025) & 0xFFFFu;
+                const uint32_t s3 = __byte_perm(v, v2, 0x0025);
                 const float2 w0 = gather(s0), w1 = gather(s1), w2 = gather(s2), w3 = gather(s3);
                 const float *xk = stage + tc * 16u + col0;
 #pragma unroll

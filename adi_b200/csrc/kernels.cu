@@ -159,7 +159,8 @@ void launch_ne_state_values(const float2 *table, float *values, cudaStream_t s) 
 // one rounded multiply per element, then the butterfly network.
 __global__ void prep_kernel(PrepParams p) {
     extern __shared__ float v[];
-    const uint32_t row = blockIdx.x;
+    const uint32_t row_end = p.limit ? min(p.rows, *p.limit) : p.rows;
+    for (uint32_t row = blockIdx.x; row < row_end; row += gridDim.x) {
     const int job = blockIdx.y;
     const uint32_t token = p.grouped ? p.grouped[row] : row;
     const uint32_t expert = p.pos_expert ? p.pos_expert[row] : 0u;
@@ -178,13 +179,16 @@ __global__ void prep_kernel(PrepParams p) {
     __syncthreads();
     block_fwht(v, p.cols, p.scale);
     for (uint32_t c = threadIdx.x; c < p.cols; c += blockDim.x) out[c] = v[c];
+    __syncthreads();
+    }
 }
 
 // Register-resident variant for cols = 256 * R (thread t owns t*R .. +R-1).
 template <int R>
 __global__ void __launch_bounds__(256) prep_regs_kernel(PrepParams p) {
     __shared__ float sh[256 * R];
-    const uint32_t row = blockIdx.x;
+    const uint32_t row_end = p.limit ? min(p.rows, *p.limit) : p.rows;
+    for (uint32_t row = blockIdx.x; row < row_end; row += gridDim.x) {
     const int job = blockIdx.y;
     const uint32_t token = p.grouped ? p.grouped[row] : row;
     const uint32_t expert = p.pos_expert ? p.pos_expert[row] : 0u;
@@ -198,11 +202,13 @@ __global__ void __launch_bounds__(256) prep_regs_kernel(PrepParams p) {
 #pragma unroll
     for (int r = 0; r < R; ++r) v[r] = __fmul_rn(v[r], p.scale);
     store_regs<R>((job ? p.out[1] : p.out[0]) + (size_t)row * p.cols + threadIdx.x * R, v);
+    __syncthreads();
+    }
 }
 
 void launch_prep(const PrepParams &p, cudaStream_t s) {
     if (p.rows == 0) return;
-    dim3 grid(p.rows, p.jobs);
+    dim3 grid(loop_grid(p.rows, p.limit), p.jobs);
     switch (p.cols) {
         case 512: prep_regs_kernel<2><<<grid, 256, 0, s>>>(p); return;
         case 1024: prep_regs_kernel<4><<<grid, 256, 0, s>>>(p); return;
@@ -1624,7 +1630,8 @@ uint32_t launch_route(const RouteParams &p, cudaStream_t s) {
 __global__ void mid_kernel(MidParams p) {
     extern __shared__ float sm[];
     float *g = sm, *u = sm + p.inner;
-    const uint32_t pos = blockIdx.x;
+    const uint32_t pos_end = p.limit ? min(p.positions, *p.limit) : p.positions;
+    for (uint32_t pos = blockIdx.x; pos < pos_end; pos += gridDim.x) {
     const uint32_t e = p.pos_expert ? p.pos_expert[pos] : 0u;
     const size_t base = (size_t)pos * p.inner;
     for (uint32_t i = threadIdx.x; i < p.inner; i += blockDim.x) {
@@ -1657,12 +1664,15 @@ __global__ void mid_kernel(MidParams p) {
     __syncthreads();
     block_fwht(g, p.inner, p.scale);
     for (uint32_t i = threadIdx.x; i < p.inner; i += blockDim.x) p.xd[base + i] = g[i];
+    __syncthreads();
+    }
 }
 
 template <int R>
 __global__ void __launch_bounds__(256) mid_regs_kernel(MidParams p) {
     __shared__ float sh[256 * R];
-    const uint32_t pos = blockIdx.x;
+    const uint32_t pos_end = p.limit ? min(p.positions, *p.limit) : p.positions;
+    for (uint32_t pos = blockIdx.x; pos < pos_end; pos += gridDim.x) {
     const uint32_t e = p.pos_expert ? p.pos_expert[pos] : 0u;
     const size_t base = (size_t)pos * p.inner + threadIdx.x * R;
     float g[R], u[R];
@@ -1691,15 +1701,18 @@ __global__ void __launch_bounds__(256) mid_regs_kernel(MidParams p) {
 #pragma unroll
     for (int r = 0; r < R; ++r) g[r] = __fmul_rn(g[r], p.scale);
     store_regs<R>(p.xd + base, g);
+    __syncthreads();
+    }
 }
 
 void launch_mid(const MidParams &p, cudaStream_t s) {
     if (p.positions == 0) return;
+    const uint32_t blocks = loop_grid(p.positions, p.limit);
     switch (p.inner) {
-        case 512: mid_regs_kernel<2><<<p.positions, 256, 0, s>>>(p); return;
-        case 1024: mid_regs_kernel<4><<<p.positions, 256, 0, s>>>(p); return;
-        case 2048: mid_regs_kernel<8><<<p.positions, 256, 0, s>>>(p); return;
-        default: mid_kernel<<<p.positions, 256, 2 * p.inner * sizeof(float), s>>>(p);
+        case 512: mid_regs_kernel<2><<<blocks, 256, 0, s>>>(p); return;
+        case 1024: mid_regs_kernel<4><<<blocks, 256, 0, s>>>(p); return;
+        case 2048: mid_regs_kernel<8><<<blocks, 256, 0, s>>>(p); return;
+        default: mid_kernel<<<blocks, 256, 2 * p.inner * sizeof(float), s>>>(p);
     }
 }
 

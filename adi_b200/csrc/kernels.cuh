@@ -94,6 +94,7 @@ struct PrepParams {
     uint32_t rows;  // positions
     int jobs;
     int su_is_f16;
+    const uint32_t *limit;  // nullable: device count; rows at or past it are skipped
 };
 void launch_prep(const PrepParams &p, cudaStream_t s);
 
@@ -158,6 +159,7 @@ struct MidParams {
     float scale;
     float *xd;        // [P][I]
     uint32_t positions;
+    const uint32_t *limit;  // nullable: device count; positions at or past it are skipped
 };
 void launch_mid(const MidParams &p, cudaStream_t s);
 

@@ -140,6 +140,15 @@ cudaError_t launch_pdl(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, siz
     return cudaLaunchKernelEx(&config, kernel, static_cast<KernelArgs>(args)...);
 }
 
+// Blocks of a launch over `rows` rows (or positions): one per row, or, when a
+// device-side limit is given (rows is then only an upper bound, e.g. a
+// buffer's capacity), at most kLoopBlocks blocks that loop over the rows
+// below the limit.
+constexpr uint32_t kLoopBlocks = 148 * 8;
+inline uint32_t loop_grid(uint32_t rows, const uint32_t *limit) {
+    return limit && rows > kLoopBlocks ? kLoopBlocks : rows;
+}
+
 __device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }

@@ -951,7 +951,8 @@ __device__ __forceinline__ float scale_value(const void *base, int is_f16, size_
 __global__ void prep_f16_kernel(PrepF16Params p) {
     extern __shared__ float v[];
     __shared__ float scratch[32];
-    const uint32_t row = blockIdx.x;
+    const uint32_t row_end = p.limit ? min(p.rows, *p.limit) : p.rows;
+    for (uint32_t row = blockIdx.x; row < row_end; row += gridDim.x) {
     const int job = blockIdx.y;
     const uint32_t token = p.grouped ? p.grouped[row] : row;
     const uint32_t expert = p.pos_expert ? p.pos_expert[row] : 0u;
@@ -965,13 +966,16 @@ __global__ void prep_f16_kernel(PrepF16Params p) {
     const int k = scale_exponent(block_max_abs(v, p.cols, scratch));
     if (threadIdx.x == 0) (job ? p.kx[1] : p.kx[0])[row] = (int8_t)k;
     write_f16(v, p.cols, k, p.split != 0, job ? p.xh[1] : p.xh[0], (size_t)p.rows * (p.cols / 2), row);
+    __syncthreads();
+    }
 }
 
 __global__ void mid_f16_kernel(MidF16Params p) {
     extern __shared__ float sm[];
     __shared__ float scratch[32];
     float *g = sm, *u = sm + p.inner;
-    const uint32_t pos = blockIdx.x;
+    const uint32_t pos_end = p.limit ? min(p.positions, *p.limit) : p.positions;
+    for (uint32_t pos = blockIdx.x; pos < pos_end; pos += gridDim.x) {
     const uint32_t e = p.pos_expert ? p.pos_expert[pos] : 0u;
     const size_t base = (size_t)pos * p.inner;
     for (uint32_t i = threadIdx.x; i < p.inner; i += blockDim.x) {
@@ -997,6 +1001,8 @@ __global__ void mid_f16_kernel(MidF16Params p) {
     const int k = scale_exponent(block_max_abs(g, p.inner, scratch));
     if (threadIdx.x == 0) p.kx[pos] = (int8_t)k;
     write_f16(g, p.inner, k, p.split != 0, p.xh, (size_t)p.positions * (p.inner / 2), pos);
+    __syncthreads();
+    }
 }
 
 // Register-resident versions for lengths 256 * R: thread t owns elements
@@ -1060,7 +1066,8 @@ template <int R>
 __global__ void __launch_bounds__(256) prep_f16_regs_kernel(PrepF16Params p) {
     __shared__ float sh[256 * R];
     __shared__ float scratch[32];
-    const uint32_t row = blockIdx.x;
+    const uint32_t row_end = p.limit ? min(p.rows, *p.limit) : p.rows;
+    for (uint32_t row = blockIdx.x; row < row_end; row += gridDim.x) {
     const uint32_t token = p.grouped ? p.grouped[row] : row;
     const uint32_t expert = p.pos_expert ? p.pos_expert[row] : 0u;
     float x[R];
@@ -1078,6 +1085,8 @@ __global__ void __launch_bounds__(256) prep_f16_regs_kernel(PrepF16Params p) {
         if (threadIdx.x == 0) (job ? p.kx[1] : p.kx[0])[row] = (int8_t)k;
         write_f16_regs<R>(v, k, p.split != 0, job ? p.xh[1] : p.xh[0], (size_t)p.rows * (p.cols / 2), row);
     }
+    __syncthreads();
+    }
 }
 
 // The prep at 2048 columns with the transposed-output FWHT: thread t ends
@@ -1090,7 +1099,8 @@ __global__ void __launch_bounds__(256) prep_f16_2048_kernel(PrepF16Params p) {
     __shared__ float sh[2048 + 64];
     __shared__ float scratch[32];
     constexpr uint32_t n = 2048;
-    const uint32_t row = blockIdx.x;
+    const uint32_t row_end = p.limit ? min(p.rows, *p.limit) : p.rows;
+    for (uint32_t row = blockIdx.x; row < row_end; row += gridDim.x) {
     const uint32_t token = p.grouped ? p.grouped[row] : row;
     const uint32_t expert = p.pos_expert ? p.pos_expert[row] : 0u;
     float x[8];
@@ -1133,13 +1143,16 @@ __global__ void __launch_bounds__(256) prep_f16_2048_kernel(PrepF16Params p) {
             *dst = __float2half_rn(v[j] * s);
         }
     }
+    __syncthreads();
+    }
 }
 
 template <int R>
 __global__ void __launch_bounds__(256) mid_f16_regs_kernel(MidF16Params p) {
     __shared__ float sh[256 * R];
     __shared__ float scratch[32];
-    const uint32_t pos = blockIdx.x;
+    const uint32_t pos_end = p.limit ? min(p.positions, *p.limit) : p.positions;
+    for (uint32_t pos = blockIdx.x; pos < pos_end; pos += gridDim.x) {
     const uint32_t e = p.pos_expert ? p.pos_expert[pos] : 0u;
     const size_t base = (size_t)pos * p.inner + threadIdx.x * R;
     float g[R], u[R];
@@ -1167,6 +1180,8 @@ __global__ void __launch_bounds__(256) mid_f16_regs_kernel(MidF16Params p) {
     const int k = scale_exponent(block_max_abs_regs<R>(g, scratch));
     if (threadIdx.x == 0) p.kx[pos] = (int8_t)k;
     write_f16_regs<R>(g, k, p.split != 0, p.xh, (size_t)p.positions * (p.inner / 2), pos);
+    __syncthreads();
+    }
 }
 
 // FWHT of 512 values held by one warp, lane l holding x[16l .. 16l+15]:
@@ -1217,8 +1232,10 @@ __global__ void __launch_bounds__(256) mid_f16_warp_kernel(MidF16Params p) {
     griddep_launch_dependents();
     griddep_wait();
     constexpr uint32_t n = 512;
-    const uint32_t pos = blockIdx.x * 8u + (threadIdx.x >> 5), lane = threadIdx.x & 31u;
-    if (pos >= p.positions) return;  // whole warps leave together
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t pos_end = p.limit ? min(p.positions, *p.limit) : p.positions;
+    // Whole warps take whole positions, so a warp leaves or loops together.
+    for (uint32_t pos = blockIdx.x * 8u + (threadIdx.x >> 5); pos < pos_end; pos += gridDim.x * 8u) {
     const uint32_t e = p.pos_expert ? p.pos_expert[pos] : 0u;
     const size_t base = (size_t)pos * n + lane * 16u;
     float g[16], u[16];
@@ -1275,28 +1292,31 @@ __global__ void __launch_bounds__(256) mid_f16_warp_kernel(MidF16Params p) {
         *reinterpret_cast<uint4 *>(row) = pack_half8(g, sc);
         *reinterpret_cast<uint4 *>(row + 8) = pack_half8(g + 8, sc);
     }
+    }
 }
 
 }  // namespace
 
 void launch_prep_f16(const PrepF16Params &p, cudaStream_t s) {
     if (p.rows == 0) return;
-    const dim3 grid(p.rows, p.jobs);
+    const uint32_t blocks = loop_grid(p.rows, p.limit);
+    const dim3 grid(blocks, p.jobs);
     switch (p.cols) {
-        case 512: prep_f16_regs_kernel<2><<<p.rows, 256, 0, s>>>(p); return;
-        case 1024: prep_f16_regs_kernel<4><<<p.rows, 256, 0, s>>>(p); return;
-        case 2048: launch_pdl(prep_f16_2048_kernel, p.rows, 256, 0, s, p); return;
+        case 512: prep_f16_regs_kernel<2><<<blocks, 256, 0, s>>>(p); return;
+        case 1024: prep_f16_regs_kernel<4><<<blocks, 256, 0, s>>>(p); return;
+        case 2048: launch_pdl(prep_f16_2048_kernel, blocks, 256, 0, s, p); return;
         default: prep_f16_kernel<<<grid, 256, p.cols * sizeof(float), s>>>(p);
     }
 }
 
 void launch_mid_f16(const MidF16Params &p, cudaStream_t s) {
     if (p.positions == 0) return;
+    const uint32_t blocks = loop_grid(p.positions, p.limit);
     switch (p.inner) {
-        case 512: launch_pdl(mid_f16_warp_kernel, (p.positions + 7) / 8, 256, 0, s, p); return;
-        case 1024: mid_f16_regs_kernel<4><<<p.positions, 256, 0, s>>>(p); return;
-        case 2048: mid_f16_regs_kernel<8><<<p.positions, 256, 0, s>>>(p); return;
-        default: mid_f16_kernel<<<p.positions, 256, 2 * p.inner * sizeof(float), s>>>(p);
+        case 512: launch_pdl(mid_f16_warp_kernel, loop_grid((p.positions + 7) / 8, p.limit), 256, 0, s, p); return;
+        case 1024: mid_f16_regs_kernel<4><<<blocks, 256, 0, s>>>(p); return;
+        case 2048: mid_f16_regs_kernel<8><<<blocks, 256, 0, s>>>(p); return;
+        default: mid_f16_kernel<<<blocks, 256, 2 * p.inner * sizeof(float), s>>>(p);
     }
 }
 

@@ -77,6 +77,7 @@ struct PrepF16Params {
     uint32_t su_stride, cols, rows;
     float scale;
     int jobs, su_is_f16, split;
+    const uint32_t *limit;       // nullable: device count; rows at or past it are skipped
 };
 void launch_prep_f16(const PrepF16Params &p, cudaStream_t s);
 
@@ -93,6 +94,7 @@ struct MidF16Params {
     __half *xh;
     int8_t *kx;
     uint32_t positions;
+    const uint32_t *limit;           // nullable: device count; positions at or past it are skipped
 };
 void launch_mid_f16(const MidF16Params &p, cudaStream_t s);
 

@@ -19,14 +19,15 @@ layer is three device phases with two exchanges between them:
                gated shared expert
 
 The exchanges are torch.distributed collectives (NCCL over NVLink on the
-GPUs), or, with a PeerExchange, this library's own kernels over NVLink: the
-dispatch writes every route's row straight into the receive buffer of the
-expert's rank (peer pointers through CUDA IPC), and the experts' output
-transform writes every output row straight back into the sender's buffer;
-only the expert counts go through a collective, and a one-element
-all-reduce orders each rank after the others' writes. Every row is computed
-with the single-GPU kernels, so the output is the single-GPU block's output
-for the same tokens either way.
+GPUs), or, with a PeerExchange, this library's own kernels over NVLink with
+nothing passing through the host: every rank writes its expert counts into
+every rank's memory, derives every offset from them on the device, writes
+every route's row straight into the receive buffer of the expert's rank
+(peer pointers through CUDA IPC), and the experts' output transform writes
+every output row straight back into the sender's buffer; device barriers
+(flags in each other's memory, bounded waits) order the ranks. Every row is
+computed with the single-GPU kernels, so the output is the single-GPU
+block's output for the same tokens either way.
 """
 from __future__ import annotations
 
@@ -78,13 +79,22 @@ class DevicePhases:
                                     logits_ptr=logits.data_ptr() if logits is not None else 0)
         return counts
 
-    def send_peer(self, x: torch.Tensor, all_counts_host):
+    def send_peer(self, x: torch.Tensor, counts: torch.Tensor):
+        """This rank's counts to every rank, then its rows to the experts'
+        ranks, each step closed by a device barrier."""
         self._stream(x.device)
-        self.ctx.ep_send_peer_device(self.handle, x.data_ptr(), x.shape[0], all_counts_host)
+        self.ctx.ep_send_peer_device(self.handle, x.data_ptr(), x.shape[0], counts.data_ptr())
 
-    def experts_peer(self, all_counts: torch.Tensor, rows: int):
-        self._stream(all_counts.device)
-        self.ctx.ep_experts_peer_device(self.handle, all_counts.data_ptr(), rows)
+    def experts_peer(self, device):
+        self._stream(device)
+        self.ctx.ep_experts_peer_device(self.handle)
+
+    def peer_counts(self, world: int, device) -> torch.Tensor:
+        """The last block's exchanged counts [world][experts] (device)."""
+        self._stream(device)
+        out = torch.empty(world, self.experts, dtype=torch.int32, device=device)
+        self.ctx.ep_peer_counts_device(self.experts, out.data_ptr())
+        return out
 
     def combine_peer(self, tokens: int, device) -> torch.Tensor:
         self._stream(device)
@@ -115,8 +125,9 @@ class PeerExchange:
     rank of `group`: each rank allocates its receive and returned buffers
     (for up to `max_tokens` tokens per rank per layer) and the CUDA IPC
     handles are all-gathered, so every rank holds pointers to every rank's
-    buffers. close() unmaps the others' buffers on every rank; call it on
-    all ranks before any context closes."""
+    buffers. After set-up no collective is involved: the blocks synchronise
+    through device barriers. close() unmaps the others' buffers on every
+    rank; call it on all ranks before any context closes."""
 
     def __init__(self, ctx, group=None, max_tokens: int = 512, hidden: int = 2048):
         self.ctx, self.group = ctx, group
@@ -126,12 +137,6 @@ class PeerExchange:
         gathered = [None] * self.world
         dist.all_gather_object(gathered, handles, group=group)
         ctx.ep_peer_connect(self.rank, self.world, gathered)
-        self._order = torch.zeros(1, device=torch.cuda.current_device())
-
-    def fence(self):
-        """Orders this rank's later work after every rank's writes so far
-        (their kernels end with system-scope fences)."""
-        dist.all_reduce(self._order, group=self.group)
 
     def close(self):
         self.ctx.ep_peer_close()
@@ -178,25 +183,32 @@ class ExpertParallelMoe:
         return self.phases.combine(returned, tokens)
 
     def _forward_peer(self, x: torch.Tensor, logits: torch.Tensor | None) -> torch.Tensor:
-        tokens = x.shape[0]
-        if tokens > self.exchange.max_tokens:
-            raise ValueError(f"{tokens} tokens exceed the peer exchange's {self.exchange.max_tokens}")
+        # Nothing here waits for the device: counts, offsets and sizes stay on
+        # the GPUs, and every rank checks every rank's capacities on the same
+        # exchanged counts (an overflow is reported by the next synchronising
+        # call on every rank). Token counts above the exchange's max_tokens are
+        # refused the same way, so no rank leaves the block's barriers early.
         counts = self.phases.dispatch_counts(x, logits)
-        all_counts = torch.empty(self.world * self.experts, dtype=torch.int32, device=x.device)
-        dist.all_gather_into_tensor(all_counts, counts, group=self.group)
-        host = all_counts.cpu().numpy().reshape(self.world, self.experts)
-        rank, local = self.exchange.rank, self.local
-        mine = host[:, rank * local:(rank + 1) * local]
-        # The device waits on this host step: issue its work first, then the
-        # bookkeeping.
-        self.phases.send_peer(x, host)
-        self.exchange.fence()
-        self.phases.experts_peer(all_counts, int(mine.sum()))
-        self.exchange.fence()
-        out = self.phases.combine_peer(tokens, x.device)
-        self.last_splits = (host[rank].reshape(self.world, local).sum(1).tolist(), mine.sum(1).tolist())
-        self.last_received = torch.from_numpy(mine.sum(0).astype(np.int64))
+        self.phases.send_peer(x, counts)
+        self.phases.experts_peer(x.device)
+        out = self.phases.combine_peer(x.shape[0], x.device)
+        self._peer_stats_device = x.device
         return out
+
+    def exchange_stats(self):
+        """(rows sent to each rank, rows received from each rank, rows
+        received per local expert) of the last block. With a PeerExchange this
+        reads the exchanged counts back from the device, so call it outside a
+        timed region."""
+        device = getattr(self, "_peer_stats_device", None)
+        if self.exchange is not None and device is not None:
+            counts = self.phases.peer_counts(self.world, device).cpu().numpy()
+            rank, local = self.exchange.rank, self.local
+            mine = counts[:, rank * local:(rank + 1) * local]
+            self.last_splits = (counts[rank].reshape(self.world, local).sum(1).tolist(), mine.sum(1).tolist())
+            self.last_received = torch.from_numpy(mine.sum(0).astype(np.int64))
+            self._peer_stats_device = None
+        return self.last_splits, self.last_received
 
     __call__ = forward
 

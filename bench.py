@@ -3,27 +3,34 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (one GPU): one Qwen3.5-MoE sparse block -- hidden 2048, 256 routed
-experts of intermediate 512 in the K=1.5 trellis codec, one shared NE expert,
-top-8 -- at prefill ubatch 512 with N(0,1) activations (near-uniform
-routing). A step is one pass of the block over one ubatch. Four distinct
+Workload (every N, C4): one Qwen3.5-MoE sparse block -- hidden 2048, 256
+routed experts of intermediate 512 in the K=1.5 trellis codec, one shared NE
+expert, top-8 -- over 4096 tokens per step, N(0, 1) activations, router
+logits prescribed with Zipf-skewed expert popularity (log p(rank) +
+Gumbel(0, 1), s = 1.1). On one GPU a step is the block over the 4096 tokens;
+on N GPUs (torchrun) each rank feeds 4096 / N tokens and holds 256 / N of
+the routed experts (plus the router and shared expert), and the block is
+expert-parallel: this library's kernels exchange counts and rows over
+NVLink through peer memory, synchronised by device barriers, with nothing
+passing through the host (`--exchange nccl`: NCCL all-to-alls instead).
+Total work per step is fixed, so the scaling is strong. Four distinct
 synthetic blocks (157 MB of packed weights each, more than the 126 MB L2)
 are used in turn, so no step finds its weights in L2.
 
 `value` is device time: K steps bracketed by a barrier and a synchronize,
 CUDA events on the stream the kernels run on, max over ranks, inputs already
-in HBM. `e2e` runs the same steps through the C ABI's host-pointer entry
-(adi_cuda_moe_forward_batch): pinned host inputs copied in, outputs and
-routes copied back, every step. `roofline` is the expert GEMM kernel (the
-dominant one): packed expert bytes it must stream per launch over its
-event-timed duration. `cpu_baseline` is the reference CPU implementation
-(built from its own sources into oracle/_ref) on this host's cores.
+in HBM. `e2e` runs the same steps with every step's tokens (and logits)
+copied in from pinned host memory and its outputs copied back. `roofline` is
+the tensor-core expert GEMM (the dominant kernel): packed expert bytes it
+must stream per launch over its event-timed duration. `cpu_baseline` is the
+reference CPU implementation (built from its own sources into oracle/_ref)
+on this host's cores, on the same 4096-token step.
 
-With N > 1 under torchrun the block is expert-parallel (C4): every rank
-holds 256/N of each block's routed experts plus the router and shared
-expert, feeds its own 512 tokens (weak scaling: 512 x N tokens per step, so
-4096 at N = 8), and each layer exchanges route counts, token rows and
-expert output rows with NCCL all-to-alls (adi_b200.expert_parallel).
+One GPU also reports C2 (the block at prefill ubatch 512 with its own
+router, near-uniform routing), a ubatch sweep (1/16/128/512), the C3 decode
+stack and the C5 stack; N GPUs also report the expert-parallel output
+checked against the one-GPU block (`ep_parity`) and the C5 stack with every
+block expert-parallel.
 
 `--impl reference` times the reference CPU implementation on the same
 workload (rank 0 only).
@@ -51,6 +58,7 @@ import torch.distributed as dist  # noqa: E402
 METRIC = "MoE-block tokens/s (ubatch 1/128/512) at 1/2/4/8 B200; % HBM/tensor roofline"
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 TRELLIS_BYTES = 4096 * 48  # one expert projection's trellis
 GAMMA_BYTES = 160 * 2
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
@@ -66,7 +74,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--tokens", type=int, default=512)
+    ap.add_argument("--ubatch", type=int, default=512, help="the C2 extra's prefill ubatch (one GPU)")
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--precision", type=int, default=1, choices=[0, 1],
                     help="0: CUDA-core fp32 throughout; 1: tcgen05 f16 operands for the expert products")
@@ -89,6 +97,15 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def tensor_peak():
+    """Dense bf16 TFLOP/s: the burst figure, for a kernel timed on its own
+    launches."""
+    if PEAKS_FILE.exists():
+        data = json.loads(PEAKS_FILE.read_text())
+        return float(data["bf16_tflops"]), "measured"
+    return FALLBACK_BF16_TFLOPS, "fallback"
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -97,6 +114,10 @@ class ClockSampler:
 
     def __init__(self, index: int):
         self.proc = None
+        self.index = index
+        # One read-only query right before the timed region, the periodic ones
+        # during it, one right after: a short region still gets samples.
+        self.first = self._once()
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
@@ -104,11 +125,19 @@ class ClockSampler:
         except OSError:
             self.proc = None
 
+    def _once(self) -> str:
+        try:
+            return subprocess.run(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                   "-i", str(self.index)], capture_output=True, text=True, timeout=10).stdout
+        except (OSError, subprocess.SubprocessError):
+            return ""
+
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
         out, _ = self.proc.communicate(timeout=10)
+        out = self.first + out + self._once()
         sm, smax, power, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in out.strip().splitlines():
@@ -159,32 +188,60 @@ def barrier(world: int):
         dist.barrier()
 
 
-def reference_forward_seconds(ref, block, x: np.ndarray, budget_s: float, max_calls: int):
+# The headline workload at every N (C4): 4096 tokens per step, the tokens
+# split evenly over the GPUs (4096 / N per GPU, strong scaling), experts
+# sharded over them, router logits prescribed with Zipf-skewed expert
+# popularity; four distinct blocks rotated. The reference arm runs the same
+# workload on the host's cores.
+C4_TOKENS = 4096
+C4_POOL = 4  # input / logit sets cycled
+C4_ROUTING = ("prescribed logits log p(rank(e)) + Gumbel(0, 1), Zipf s = 1.1 popularity, rank permutation "
+              "from seed 0")
+
+
+def c4_config(hidden: int, experts: int, expert_hidden: int, blocks: int) -> dict:
+    """The headline workload; the same dict in both arms."""
+    return {"workload": f"C4: MoE block, {C4_TOKENS} tokens per step split evenly over the GPUs, experts "
+                        "sharded over them, Zipf-skewed routing",
+            "tokens_per_step": C4_TOKENS, "hidden": hidden, "experts": experts, "expert_hidden": expert_hidden,
+            "top_k": 8, "blocks_rotated": blocks, "routing": C4_ROUTING,
+            "l2": f"inputs larger than L2: {blocks} distinct blocks rotated"}
+
+
+def reference_forward_seconds(ref, block, x: np.ndarray, logits, budget_s: float, max_calls: int):
     """Times the reference's MoE block (restated moe_forward_batch glue over
     its public kernels) on `x`; one untimed call first."""
-    ref.moe_forward(block, x)
+    ref.moe_forward(block, x, logits=logits)
     times = []
     start = time.perf_counter()
     while len(times) < max_calls and (time.perf_counter() - start < budget_s or len(times) < 2):
         t0 = time.perf_counter()
-        ref.moe_forward(block, x)
+        ref.moe_forward(block, x, logits=logits)
         times.append(time.perf_counter() - t0)
     return times
 
 
-def cpu_baseline(block, tokens: int, seed_input) -> dict:
+def reference_c4_inputs(block):
+    """The C4 step's inputs on the host: tokens N(0, 1), prescribed logits."""
+    from adi_b200 import synthetic
+    x = synthetic.activations(1000, C4_TOKENS, block.hidden, device="cpu").numpy()
+    logits = zipf_logits(1, C4_TOKENS, block.experts, seed=11, device="cpu")[0].numpy()
+    return x, logits
+
+
+def cpu_baseline(block) -> dict:
     sys.path.insert(0, str(ROOT / "oracle"))
     from ffi import Reference, reference_available  # noqa: E402
     if not reference_available():
         return {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "reference",
                 "sample": "oracle/_ref not built"}
     ref = Reference()
-    x = seed_input.cpu().numpy()
-    times = reference_forward_seconds(ref, block, x, budget_s=15.0, max_calls=30)
+    x, logits = reference_c4_inputs(block)
+    times = reference_forward_seconds(ref, block, x, logits, budget_s=15.0, max_calls=10)
     per = statistics.median(times)
-    return {"value": tokens / per, "unit": "tokens/s", "cores": int(ref.lib.ref_worker_threads()),
+    return {"value": C4_TOKENS / per, "unit": "tokens/s", "cores": int(ref.lib.ref_worker_threads()),
             "kind": "reference", "isa": ref.isa(),
-            "sample": f"{len(times)} calls of the full {tokens}-token block after one warm call; median "
+            "sample": f"{len(times)} calls of the full {C4_TOKENS}-token step after one warm call; median "
                       f"{per * 1e3:.1f} ms/call"}
 
 
@@ -200,32 +257,34 @@ def run_reference(args, world, rank):
         print(json.dumps({**base, "unavailable": "oracle/_ref/libadi_ref.so was not built"}), flush=True)
         return
     ref = Reference()
-    block = synthetic.moe_block(seed=0, device="cpu")
-    x = synthetic.activations(1000, args.tokens, block.hidden, device="cpu").numpy()
-    for _ in range(max(0, min(args.warmup, 3))):
-        ref.moe_forward(block, x)
-    # Each step is one full forward of the ubatch; the run stops early once
-    # it has used its time budget, and `steps` says how many were timed.
+    tluts = synthetic.model_tluts(4999, device="cpu")
+    block = synthetic.moe_block(seed=0, device="cpu", tluts=tluts)
+    x, logits = reference_c4_inputs(block)
+    for _ in range(args.warmup):
+        ref.moe_forward(block, x, logits=logits)
+    # Each step is one full forward of the 4096-token step; the run stops
+    # early once it has used its time budget, and `steps` says how many
+    # were timed.
     times = []
     budget = 150.0
     start = time.perf_counter()
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        ref.moe_forward(block, x)
+        ref.moe_forward(block, x, logits=logits)
         times.append(time.perf_counter() - t0)
         if time.perf_counter() - start > budget:
             break
     total = sum(times)
-    value = len(times) * args.tokens / total
+    value = len(times) * C4_TOKENS / total
     cores = int(ref.lib.ref_worker_threads())
     print(json.dumps({
-        **base, "value": value, "steps": len(times), "warmup": min(args.warmup, 3),
-        "ms_per_step": 1e3 * total / len(times), "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        **base, "value": value, "steps": len(times), "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / len(times), "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": f"MoE block, ubatch {args.tokens}, reference CPU path", "tokens_per_step": args.tokens,
-                   "hidden": block.hidden, "experts": block.experts, "top_k": 8},
+        "config": c4_config(block.hidden, block.experts, block.expert_hidden, args.layers),
+        "parallelism": "the reference's CPU threads",
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "reference",
-                         "sample": f"{len(times)} full {args.tokens}-token forwards, ADI_THREADS={cores}, "
+                         "sample": f"{len(times)} full {C4_TOKENS}-token steps, ADI_THREADS={cores}, "
                                    f"ISA {ref.isa()}"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -428,7 +487,7 @@ def stack_c5(ctx, stream, local):
             "decode_graph_ms_per_token": graph_ms, "decode_graph_tokens_per_s": 1e3 / graph_ms}
 
 
-C5_EP_DECODE_STEPS = 32
+C5_EP_DECODE_STEPS = 128
 
 
 def stack_c5_ep(ctx, stream, local, rank, world, exchange=None):
@@ -512,8 +571,60 @@ def zipf_logits(pool: int, tokens: int, experts: int, seed: int, device: str) ->
     return torch.cat([log_p - torch.log(-torch.log(u)), gate], dim=2).contiguous()
 
 
+def expert_gemm_roofline(stages, n_touched, positions_per_step, hidden=2048, inner=512):
+    """The dominant kernel's roofline, over its launches' event-timed
+    duration. Below ~280 flop per packed byte (the ridge of measured HBM and
+    bf16 peaks) it is HBM-bound: achieved = packed expert bytes its launches
+    must stream (trellis + wave gamma of every touched expert and
+    projection); above, tensor-bound: achieved = the products' flops
+    (2 * positions * hidden * inner per projection, three projections)."""
+    gemm_ms = stages.get("expert_gemm_gate_up", (0, 0))[0] + stages.get("expert_gemm_down", (0, 0))[0]
+    gemm_launches = stages.get("expert_gemm_gate_up", (0, 0))[1] + stages.get("expert_gemm_down", (0, 0))[1]
+    steps = len(n_touched)
+    gemm_bytes = sum(n * 3 * (TRELLIS_BYTES + GAMMA_BYTES) for n in n_touched)
+    gemm_flops = steps * positions_per_step * 3 * 2 * hidden * inner
+    hbm_peak, peak_kind = peaks()
+    tflops_peak, _ = tensor_peak()
+    launches = max(1, gemm_launches)
+    out = {"kernel": "tc_gemm_kernel<kExpert> (routed expert gate/up and down)", "peak_kind": peak_kind,
+           "traffic": None, "bytes_per_launch": gemm_bytes / launches, "flops_per_launch": gemm_flops / launches,
+           "ms_per_launch": gemm_ms / launches,
+           "intensity_flop_per_byte": gemm_flops / gemm_bytes if gemm_bytes else None}
+    if gemm_ms <= 0:
+        return {**out, "bound": None, "achieved": None, "peak": None, "unit": None, "frac": None}
+    if gemm_bytes and gemm_flops / gemm_bytes > 1e3 * tflops_peak / hbm_peak:
+        achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
+        return {**out, "bound": "tensor", "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s",
+                "frac": achieved / tflops_peak}
+    achieved = gemm_bytes / (gemm_ms / 1e3) / 1e9
+    return {**out, "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+            "frac": achieved / hbm_peak}
+
+
+def timed_steps(step, steps, warmup, world, stream, local):
+    """W untimed steps, then K steps between a barrier and a synchronize on
+    each side, CUDA events on the launching stream; max over ranks."""
+    for k in range(max(warmup, 1)):
+        step(k)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    begin.record(stream)
+    for k in range(steps):
+        step(k)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clock_info = clocks.stop()
+    return max_over_ranks(begin.elapsed_time(end), world), clock_info
+
+
 def run_ep(args, world, rank, local):
-    """Expert-parallel MoE block over `world` ranks (one process per GPU)."""
+    """The C4 step over `world` ranks (one process per GPU): each rank feeds
+    4096 / world tokens, the experts are sharded, the exchanges are this
+    library's peer-memory kernels (or NCCL all-to-alls)."""
     import adi_b200
     from adi_b200 import synthetic
     from adi_b200.expert_parallel import DevicePhases, ExpertParallelMoe, PeerExchange
@@ -524,19 +635,24 @@ def run_ep(args, world, rank, local):
     torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
     ctx.set_precision(args.precision)
-    T, L = args.tokens, args.layers
+    T, L = C4_TOKENS // world, args.layers
     exchange = PeerExchange(ctx, max_tokens=max(T, C5_UBATCH), hidden=2048) if args.exchange == "peer" else None
 
-    layers, first = [], None
+    tluts = synthetic.model_tluts(4999, device=device)
+    layers, first, full0 = [], None, None
     for layer in range(L):
-        block = synthetic.moe_block(seed=layer, device=device)  # the same blocks on every rank
+        block = synthetic.moe_block(seed=layer, device=device, tluts=tluts)  # the same blocks on every rank
         layers.append(ExpertParallelMoe(DevicePhases(ctx, block, rank, world), exchange=exchange))
         if first is None:
             first = block
+            # Rank 0 also holds block 0 whole: the expert-parallel output of a
+            # sample of its tokens is checked against the one-GPU block.
+            if rank == 0:
+                full0 = ctx.upload_moe_layer(block)
         del block
     H, E = first.hidden, first.experts
     local_experts = E // world
-    pool = 8
+    pool = C4_POOL
     inputs = torch.stack([synthetic.activations(7 * rank + i, T, H, device=device) for i in range(pool)])
     logits = zipf_logits(pool, T, E, seed=11 + rank, device=device) if args.routing == "zipf" else None
 
@@ -544,52 +660,65 @@ def run_ep(args, world, rank, local):
         return layers[k % L](inputs[k % pool], None if logits is None else logits[k % pool])
 
     # Local experts each (layer, input) pair touches, from the rows this
-    # rank receives per expert: the algorithmic bytes of its expert GEMMs.
-    touched = []
+    # rank receives per expert (read back outside the timed region): the
+    # algorithmic bytes of its expert GEMMs; and the rows per rank.
+    touched, received_rows = [], []
     for i in range(pool * L):
         step(i)
-        touched.append(int((layers[i % L].last_received > 0).sum()))
+        _, received = layers[i % L].exchange_stats()
+        touched.append(int((received > 0).sum()))
+        received_rows.append(int(received.sum()))
+    own_rows_mean = sum(received_rows) / len(received_rows)
+    rows_max = max_over_ranks(float(max(received_rows)), world)
+    rows_mean = sum_over_ranks(float(sum(received_rows) / len(received_rows)), world) / world
 
-    for k in range(max(args.warmup, 1)):
-        step(k)
+    # Parity of the timed path: rank 0's first input through block 0, the
+    # expert-parallel output against the one-GPU block on the same logits.
+    y_ep = step(0).clone()
     torch.cuda.synchronize()
+    parity = None
+    if rank == 0:
+        y_one = torch.empty_like(y_ep)
+        sample = min(T, 64)
+        if logits is None:
+            ctx.moe_forward_batch_device(full0, inputs[0, :sample].contiguous().data_ptr(), sample,
+                                         y_one.data_ptr(), 0, 0)
+        else:
+            ctx.moe_forward_batch_logits_device(full0, inputs[0, :sample].contiguous().data_ptr(),
+                                                logits[0, :sample].contiguous().data_ptr(), sample,
+                                                y_one.data_ptr())
+        torch.cuda.synchronize()
+        diff = (y_ep[:sample] - y_one[:sample]).double()
+        parity = {"tokens": sample, "rel_l2_vs_one_gpu_block": float(diff.norm() / y_one[:sample].double().norm()),
+                  "bit_identical": bool(torch.equal(y_ep[:sample], y_one[:sample]))}
+        full0.release()
+
     ctx.reset_profile()
     launches0 = ctx.launch_count()
-    barrier(world)
-    torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    begin.record(stream)
-    for k in range(args.steps):
-        step(k)
-    end.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    clock_info = clocks.stop()
+    ms_max, clock_info = timed_steps(step, args.steps, args.warmup, world, stream, local)
     launches = ctx.launch_count() - launches0
-    ms = begin.elapsed_time(end)
-    ms_max = max_over_ranks(ms, world)
     stages = gemm_pass(ctx, step, args.steps)
     all_stages = stage_breakdown(ctx, step, min(args.steps, 200))
-    value = sum_over_ranks(args.steps * T, world) / (ms_max / 1e3)
+    value = C4_TOKENS * args.steps / (ms_max / 1e3)
     n_touched = [touched[k % (pool * L)] for k in range(args.steps)]
 
-    gemm_ms = stages.get("expert_gemm_gate_up", (0, 0))[0] + stages.get("expert_gemm_down", (0, 0))[0]
-    gemm_launches = stages.get("expert_gemm_gate_up", (0, 0))[1] + stages.get("expert_gemm_down", (0, 0))[1]
-    hbm_peak, peak_kind = peaks()
-    gemm_bytes = sum(n * 3 * (TRELLIS_BYTES + GAMMA_BYTES) for n in n_touched)
-    achieved = (gemm_bytes / (gemm_ms / 1e3)) / 1e9 if gemm_ms > 0 else None
-
-    # End to end through the public API: pinned host tokens in, outputs back.
+    # End to end: pinned host tokens (and logits) in, outputs back, every step.
     x_host = torch.empty(pool, T, H, dtype=torch.float32, pin_memory=True)
     x_host.copy_(inputs.cpu())
+    lg_host = None
+    if logits is not None:
+        lg_host = torch.empty(pool, T, E + 1, dtype=torch.float32, pin_memory=True)
+        lg_host.copy_(logits.cpu())
+    lg_dev = torch.empty(T, E + 1, device=device)
     y_host = torch.empty(T, H, dtype=torch.float32, pin_memory=True)
     x_dev = torch.empty(T, H, device=device)
     e2e_steps = max(1, min(args.steps, 200))
 
     def e2e_step(k):
         x_dev.copy_(x_host[k % pool], non_blocking=True)
-        y_host.copy_(layers[k % L](x_dev, None if logits is None else logits[k % pool]), non_blocking=True)
+        if lg_host is not None:
+            lg_dev.copy_(lg_host[k % pool], non_blocking=True)
+        y_host.copy_(layers[k % L](x_dev, None if lg_host is None else lg_dev), non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
     for k in range(min(args.warmup, 5)):
@@ -599,36 +728,28 @@ def run_ep(args, world, rank, local):
     for k in range(e2e_steps):
         e2e_step(k)
     e2e_s = max_over_ranks(time.perf_counter() - t0, world)
-    e2e_value = sum_over_ranks(e2e_steps * T, world) / e2e_s
+    e2e_value = C4_TOKENS * e2e_steps / e2e_s
     c5 = stack_c5_ep(ctx, stream, local, rank, world, exchange) if not args.no_extras else None
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "scaling": "strong", "vs_baseline": None,
             "dtype": "f16 operands, f32 accumulate" if args.precision else "f32", "data": "synthetic",
-            "config": {"workload": f"C4: expert-parallel MoE block, {T} tokens per GPU, {T * world} per step",
-                       "tokens_per_step": T * world, "tokens_per_gpu": T, "hidden": H, "experts": E,
-                       "experts_per_gpu": local_experts, "expert_hidden": first.expert_hidden, "top_k": 8,
-                       "blocks_rotated": L,
-                       "routing": ("C4 prescribed logits: log p(rank) + Gumbel(0,1), Zipf s=1.1, rank permutation "
-                                   "from seed 0" if logits is not None else "the block's router on N(0,1) inputs"),
-                       "l2": f"inputs larger than L2: {L} distinct blocks rotated",
-                       "parallelism": f"ep{world}",
-                       "exchange": ("rows written over NVLink by the dispatch and output-transform kernels "
-                                    "(CUDA IPC peer pointers); counts by NCCL all_gather" if exchange is not None
-                                    else "NCCL all_to_all_single, fp32 rows")},
-            "roofline": {"bound": "hbm", "kernel": "expert_gemm_kernel",
-                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": (achieved / hbm_peak) if achieved else None, "peak_kind": peak_kind,
-                         "traffic": None,
-                         "bytes_per_launch": gemm_bytes / max(1, gemm_launches),
-                         "ms_per_launch": gemm_ms / max(1, gemm_launches)},
+            "config": c4_config(H, E, first.expert_hidden, L),
+            "parallelism": f"ep{world}: {local_experts} experts and {T} tokens per GPU",
+            "exchange": ("this library's kernels over NVLink (CUDA IPC peer pointers): counts written into every "
+                         "rank's memory, rows into the experts' ranks and back, device flag barriers; nothing "
+                         "through the host" if exchange is not None else "NCCL all_to_all_single, fp32 rows"),
+            "roofline": expert_gemm_roofline(stages, n_touched, own_rows_mean),
             "local_experts_touched_mean": sum(n_touched) / len(n_touched),
+            "received_rows_per_rank": {"max": rows_max, "mean": rows_mean},
+            "ep_parity": parity,
             "stages_ms_per_step": {k: v[0] / max(1, v[1]) for k, v in all_stages.items()},
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4 * world,
-                    "d2h_bytes_per_step": T * H * 4 * world, "steps": e2e_steps},
+            "e2e": {"value": e2e_value, "unit": "tokens/s",
+                    "h2d_bytes_per_step": C4_TOKENS * H * 4 + (C4_TOKENS * (E + 1) * 4 if lg_host is not None else 0),
+                    "d2h_bytes_per_step": C4_TOKENS * H * 4, "steps": e2e_steps},
             "gpu_launches": launches,
             "clocks": clock_info,
         }
@@ -643,135 +764,13 @@ def run_ep(args, world, rank, local):
     ctx.close()
 
 
-def run_ours(args, world, rank, local):
-    import adi_b200
-    from adi_b200 import synthetic
-    if world > 1:
-        run_ep(args, world, rank, local)
-        return
-    torch.cuda.set_device(local)
-    ctx = adi_b200.Context(local)
-    # One explicit stream for everything: the context launches on it and the
-    # timing events are recorded on it.
-    stream = torch.cuda.Stream(device=local)
-    torch.cuda.set_stream(stream)
-    ctx.set_stream(stream.cuda_stream)
-    ctx.set_precision(args.precision)
-    T, L = args.tokens, args.layers
-
-    blocks, handles, upload_s = [], [], []
-    for layer in range(L):
-        block = synthetic.moe_block(seed=1000 * rank + layer, device=f"cuda:{local}")
-        t0 = time.perf_counter()
-        handles.append(ctx.upload_moe_layer(block))
-        upload_s.append(time.perf_counter() - t0)
-        blocks.append(block if layer == 0 else None)
-        del block
-    H, E = blocks[0].hidden, blocks[0].experts
-    pool = 8
-    inputs = torch.stack([synthetic.activations(7 * rank + i, T, H, device=f"cuda:{local}") for i in range(pool)])
-    out = torch.empty(T, H, device=f"cuda:{local}")
-    re = torch.empty(T, 8, dtype=torch.int32, device=f"cuda:{local}")
-    rw = torch.empty(T, 8, device=f"cuda:{local}")
-
-    def step(k):
-        ctx.moe_forward_batch_device(handles[k % L], inputs[k % pool].data_ptr(), T, out.data_ptr(),
-                                     re.data_ptr(), rw.data_ptr())
-
-    # Experts each input batch touches (for the algorithmic byte count).
-    touched = []
-    for i in range(pool * L):
-        step(i)
-        touched.append(int(torch.unique(re).numel()))
-    torch.cuda.synchronize()
-    touched_per_step = {i: touched[i] for i in range(len(touched))}
-
-    # The timed region runs with no events between kernels (they would break
-    # the programmatic launch overlap between consecutive kernels).
-    for k in range(max(args.warmup, 1)):
-        step(k)
-    torch.cuda.synchronize()
-    ctx.reset_profile()
-    launches0 = ctx.launch_count()
-    barrier(world)
-    torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    begin.record(stream)
-    for k in range(args.steps):
-        step(k)
-    end.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    clock_info = clocks.stop()
-    launches = ctx.launch_count() - launches0
-    ms = begin.elapsed_time(end)
-    ms_max = max_over_ranks(ms, world)
-    stages = gemm_pass(ctx, step, args.steps)
-    all_stages = stage_breakdown(ctx, step, min(args.steps, 200))
-    n_touched = [touched_per_step[k % (pool * L)] if (k % (pool * L)) in touched_per_step else touched[0]
-                 for k in range(args.steps)]
-    # touched[] was measured with step(i) for i in range(pool*L): step k uses
-    # layer k % L and input k % pool, the same pair as step k % (pool * L).
-
-    value = sum_over_ranks(args.steps * T, world) / (ms_max / 1e3)
-
-    # Roofline of the expert GEMM kernel (both of its launches per step).
-    gemm_ms = stages.get("expert_gemm_gate_up", (0, 0))[0] + stages.get("expert_gemm_down", (0, 0))[0]
-    gemm_launches = stages.get("expert_gemm_gate_up", (0, 0))[1] + stages.get("expert_gemm_down", (0, 0))[1]
-    gemm_bytes = sum(n * 3 * (TRELLIS_BYTES + GAMMA_BYTES) for n in n_touched)
-    hbm_peak, peak_kind = peaks()
-    achieved = (gemm_bytes / (gemm_ms / 1e3)) / 1e9 if gemm_ms > 0 else None
-    # Whole-block algorithmic bytes (router + shared + touched experts +
-    # activations in and out), for the block-level fraction.
-    block_bytes = [blocks[0].shared_bytes() + n * blocks[0].packed_bytes_per_expert() + T * H * 4 * 2
-                   for n in n_touched]
-    block_gbs = sum(block_bytes) / (ms / 1e3) / 1e9
-
-    if args.no_extras:
-        if rank == 0:
-            print(json.dumps({"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-                              "steps": args.steps, "ms_per_step": ms_max / args.steps, "profiling_run": True,
-                              "stages_ms_per_step": {k: v[0] / max(1, v[1]) for k, v in all_stages.items()}}),
-                  flush=True)
-        for h in handles:
-            h.release()
-        ctx.close()
-        return
-
-    upload_bytes = blocks[0].shared_bytes() + E * blocks[0].packed_bytes_per_expert()
-    upload_ms = 1e3 * (min(upload_s[1:]) if len(upload_s) > 1 else upload_s[0])
-
-    # End to end through the host-pointer C ABI, pinned host buffers.
-    x_host = torch.empty(pool, T, H, dtype=torch.float32, pin_memory=True)
-    x_host.copy_(inputs.cpu())
-    y_host = torch.empty(T, H, dtype=torch.float32, pin_memory=True)
-    re_host = torch.empty(T, 8, dtype=torch.int32, pin_memory=True)
-    rw_host = torch.empty(T, 8, dtype=torch.float32, pin_memory=True)
-    f32p = C.POINTER(C.c_float)
-    u32p = C.POINTER(C.c_uint32)
-
-    def e2e_step(k):
-        status = ctx.lib.adi_cuda_moe_forward_batch(
-            ctx.ptr, handles[k % L].value, C.cast(x_host[k % pool].data_ptr(), f32p), T,
-            C.cast(y_host.data_ptr(), f32p), C.cast(re_host.data_ptr(), u32p), C.cast(rw_host.data_ptr(), f32p))
-        if status:
-            raise RuntimeError(adi_b200.last_error())
-
-    e2e_steps = max(1, min(args.steps, 200))
-    for k in range(min(args.warmup, 5)):
-        e2e_step(k)
-    barrier(world)
-    t0 = time.perf_counter()
-    for k in range(e2e_steps):
-        e2e_step(k)
-    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
-    e2e_value = sum_over_ranks(e2e_steps * T, world) / e2e_s
-
-    # Smaller ubatches of the same block (decode and the smaller prefill),
-    # and the headline ubatch again for its CUDA-graph figure.
+def ubatch_sweep(ctx, stream, local, handles, inputs, out):
+    """The block at ubatch 1, 16 (C1's size), 128 and 512 (C2) with its own
+    router on N(0, 1) tokens: eager, replayed from CUDA graphs (one per
+    block, the host's launch overhead removed), and a stage breakdown."""
+    L = len(handles)
     sweep = {}
-    for tokens in sorted({1, 16, 128, T}):
+    for tokens in (1, 16, 128, 512):
         xs = inputs[0, :tokens].contiguous()
         for _ in range(5):
             ctx.moe_forward_batch_device(handles[0], xs.data_ptr(), tokens, out.data_ptr(), 0, 0)
@@ -782,8 +781,6 @@ def run_ours(args, world, rank, local):
             ctx.moe_forward_batch_device(handles[k % L], xs.data_ptr(), tokens, out.data_ptr(), 0, 0)
         e.record(stream)
         torch.cuda.synchronize()
-        # The same steps replayed from CUDA graphs (one per block), which
-        # takes the host's launch overhead out of small ubatches.
         graphs = []
         capture = torch.cuda.Stream(device=local)
         for k in range(L):
@@ -803,8 +800,6 @@ def run_ours(args, world, rank, local):
         torch.cuda.synchronize()
         graph_ms = gb.elapsed_time(ge) / steps
         del graphs
-        # The same steps again with stage timing (separately: its events
-        # would add to the timed run).
         ctx.set_profiling(True)
         ctx.reset_profile()
         for k in range(50):
@@ -817,65 +812,191 @@ def run_ours(args, world, rank, local):
                                      "graph_tokens_per_s": tokens / (graph_ms / 1e3),
                                      "graph_ms_per_step": graph_ms,
                                      "stages_ms_per_step": sweep_stages}
+    return sweep
 
-    # C3 decode over the 40-layer stack; the prefill blocks are released
-    # first to make room.
+
+def run_ours(args, world, rank, local):
+    import adi_b200
+    from adi_b200 import synthetic
+    if world > 1:
+        run_ep(args, world, rank, local)
+        return
+    torch.cuda.set_device(local)
+    device = f"cuda:{local}"
+    ctx = adi_b200.Context(local)
+    # One explicit stream for everything: the context launches on it and the
+    # timing events are recorded on it.
+    stream = torch.cuda.Stream(device=local)
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    ctx.set_precision(args.precision)
+    T, L = C4_TOKENS, args.layers
+
+    tluts = synthetic.model_tluts(4999, device=device)
+    blocks, handles, upload_s = [], [], []
+    for layer in range(L):
+        block = synthetic.moe_block(seed=layer, device=device, tluts=tluts)
+        t0 = time.perf_counter()
+        handles.append(ctx.upload_moe_layer(block))
+        upload_s.append(time.perf_counter() - t0)
+        blocks.append(block if layer == 0 else None)
+        del block
+    H, E = blocks[0].hidden, blocks[0].experts
+    pool = C4_POOL
+    inputs = torch.stack([synthetic.activations(7 * rank + i, T, H, device=device) for i in range(pool)])
+    logits = zipf_logits(pool, T, E, seed=11 + rank, device=device)
+    out = torch.empty(T, H, device=device)
+    re = torch.empty(T, 8, dtype=torch.int32, device=device)
+    rw = torch.empty(T, 8, device=device)
+
+    def step(k):
+        ctx.moe_forward_batch_logits_device(handles[k % L], inputs[k % pool].data_ptr(), logits[k % pool].data_ptr(),
+                                            T, out.data_ptr(), re.data_ptr(), rw.data_ptr())
+
+    # Experts each (block, input) pair touches (for the algorithmic bytes).
+    touched = []
+    for i in range(pool * L):
+        step(i)
+        touched.append(int(torch.unique(re).numel()))
+    torch.cuda.synchronize()
+
+    # The timed region runs with no events between kernels (they would break
+    # the programmatic launch overlap between consecutive kernels).
+    ctx.reset_profile()
+    launches0 = ctx.launch_count()
+    ms_max, clock_info = timed_steps(step, args.steps, args.warmup, world, stream, local)
+    launches = ctx.launch_count() - launches0
+    stages = gemm_pass(ctx, step, args.steps)
+    all_stages = stage_breakdown(ctx, step, min(args.steps, 200))
+    n_touched = [touched[k % (pool * L)] for k in range(args.steps)]
+    value = T * args.steps / (ms_max / 1e3)
+    hbm_peak, _ = peaks()
+    block_bytes = [blocks[0].shared_bytes() + n * blocks[0].packed_bytes_per_expert() + T * H * 4 * 2
+                   for n in n_touched]
+    block_gbs = sum(block_bytes) / (ms_max / 1e3) / 1e9
+
+    if args.no_extras:
+        print(json.dumps({"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+                          "steps": args.steps, "ms_per_step": ms_max / args.steps, "profiling_run": True,
+                          "stages_ms_per_step": {k: v[0] / max(1, v[1]) for k, v in all_stages.items()}}),
+              flush=True)
+        for h in handles:
+            h.release()
+        ctx.close()
+        return
+
+    # End to end: the step's tokens and logits from pinned host memory, the
+    # outputs back, every step; the copies of step k+1's inputs overlap step
+    # k's kernels on a second stream (two device buffers in turn).
+    x_host = torch.empty(pool, T, H, dtype=torch.float32, pin_memory=True)
+    x_host.copy_(inputs.cpu())
+    lg_host = torch.empty(pool, T, E + 1, dtype=torch.float32, pin_memory=True)
+    lg_host.copy_(logits.cpu())
+    y_host = torch.empty(2, T, H, dtype=torch.float32, pin_memory=True)
+    x_dev = torch.empty(2, T, H, device=device)
+    lg_dev = torch.empty(2, T, E + 1, device=device)
+    y_dev = torch.empty(2, T, H, device=device)
+    copies = torch.cuda.Stream(device=local)
+    e2e_steps = max(1, min(args.steps, 200))
+
+    def e2e_run(n):
+        loaded = [torch.cuda.Event() for _ in range(2)]
+        done = [torch.cuda.Event() for _ in range(2)]
+        with torch.cuda.stream(copies):
+            x_dev[0].copy_(x_host[0], non_blocking=True)
+            lg_dev[0].copy_(lg_host[0], non_blocking=True)
+            loaded[0].record(copies)
+        for k in range(n):
+            b = k % 2
+            if k + 1 < n:
+                with torch.cuda.stream(copies):
+                    if k >= 1:
+                        copies.wait_event(done[1 - b])  # buffer 1-b's step k-1 has finished reading it
+                    x_dev[1 - b].copy_(x_host[(k + 1) % pool], non_blocking=True)
+                    lg_dev[1 - b].copy_(lg_host[(k + 1) % pool], non_blocking=True)
+                    loaded[1 - b].record(copies)
+            stream.wait_event(loaded[b])
+            ctx.moe_forward_batch_logits_device(handles[k % L], x_dev[b].data_ptr(), lg_dev[b].data_ptr(), T,
+                                                y_dev[b].data_ptr())
+            done[b].record(stream)
+            with torch.cuda.stream(copies):
+                copies.wait_event(done[b])
+                y_host[b].copy_(y_dev[b], non_blocking=True)
+        torch.cuda.synchronize()
+
+    e2e_run(min(args.warmup, 5) + 1)
+    t0 = time.perf_counter()
+    e2e_run(e2e_steps)
+    e2e_value = T * e2e_steps / (time.perf_counter() - t0)
+
+    # C2: the block at prefill ubatch 512 with its own router on N(0, 1)
+    # tokens (near-uniform routing), device-timed like the headline.
+    U = args.ubatch
+    c2_inputs = torch.stack([synthetic.activations(70 + i, U, H, device=device) for i in range(pool)])
+    c2_re = torch.empty(U, 8, dtype=torch.int32, device=device)
+
+    def c2_step(k):
+        ctx.moe_forward_batch_device(handles[k % L], c2_inputs[k % pool].data_ptr(), U, out.data_ptr(),
+                                     c2_re.data_ptr(), 0)
+
+    c2_touched = []
+    for i in range(pool * L):
+        c2_step(i)
+        c2_touched.append(int(torch.unique(c2_re).numel()))
+    c2_steps = max(args.steps, 20)
+    c2_ms, _ = timed_steps(c2_step, c2_steps, args.warmup, world, stream, local)
+    c2_stages = gemm_pass(ctx, c2_step, c2_steps)
+    c2 = {"workload": f"C2: one MoE block, prefill ubatch {U}, its own router on N(0, 1) tokens (near-uniform "
+                      "routing)", "tokens_per_s": U * c2_steps / (c2_ms / 1e3), "ms_per_step": c2_ms / c2_steps,
+          "roofline": expert_gemm_roofline(c2_stages, [c2_touched[k % (pool * L)] for k in range(c2_steps)], 8 * U)}
+    if U == 512 and args.precision == 1:
+        c2["roofline"]["traffic"] = EXPERT_GEMM_TRAFFIC_T512
+    sweep = ubatch_sweep(ctx, stream, local, handles, c2_inputs, out)
+
+    upload_bytes = blocks[0].shared_bytes() + E * blocks[0].packed_bytes_per_expert()
+    upload_ms = 1e3 * (min(upload_s[1:]) if len(upload_s) > 1 else upload_s[0])
+
+    # C3 decode over the 40-layer stack and C5; the prefill blocks are
+    # released first to make room.
     for h in handles:
         h.release()
     handles = []
     c3 = decode_c3(ctx, stream, local)
     c5 = stack_c5(ctx, stream, local)
-    hbm_peak_c3, _ = peaks()
     for v in c3.values():
-        v["graph_frac_hbm"] = v["graph_gbs"] / hbm_peak_c3
+        v["graph_frac_hbm"] = v["graph_gbs"] / hbm_peak
 
-    baseline = None
-    if rank == 0 and world == 1 and not args.no_baseline:
-        baseline = cpu_baseline(blocks[0], T, inputs[0])
-
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16 operands, f32 accumulate" if args.precision else "f32", "data": "synthetic",
-            "config": {"workload": f"C2: one MoE block, prefill ubatch {T}, "
-                                   + ("1 GPU" if world == 1 else f"{world} GPU replicas"),
-                       "tokens_per_step": T, "hidden": H, "experts": E, "expert_hidden": blocks[0].expert_hidden,
-                       "top_k": 8, "blocks_rotated": L,
-                       "l2": f"inputs larger than L2: {L} distinct blocks of "
-                             f"{(blocks[0].shared_bytes() + E * blocks[0].packed_bytes_per_expert()) / 1e6:.0f} MB rotated",
-                       "parallelism": "dp1" if world == 1 else f"replicas{world}"},
-            "roofline": {"bound": "hbm", "kernel": "expert_gemm_kernel",
-                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": (achieved / hbm_peak) if achieved else None, "peak_kind": peak_kind,
-                         "traffic": EXPERT_GEMM_TRAFFIC_T512 if (T == 512 and args.precision == 1) else None,
-                         "traffic_source": "ncu capture of this workload, bytes per launch",
-                         "bytes_per_launch": gemm_bytes / max(1, gemm_launches),
-                         "ms_per_launch": gemm_ms / max(1, gemm_launches)},
-            "block_hbm": {"achieved_gbs": block_gbs, "frac": block_gbs / hbm_peak,
-                          "bytes_per_step": sum(block_bytes) / len(block_bytes),
-                          "experts_touched_mean": sum(n_touched) / len(n_touched)},
-            "stages_ms_per_step": {k: v[0] / max(1, v[1]) for k, v in all_stages.items()},
-            "ubatch_sweep": sweep,
-            "decode_c3": {"layers": C3_LAYERS, "distinct_weight_sets": C3_DISTINCT,
-                          "per_layer": "MoE block + NE q/k/v/o/gated-delta", "head": f"int5_g64 {C3_VOCAB}x2048",
-                          **c3},
-            "stack_c5": c5,
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
-                    "d2h_bytes_per_step": T * H * 4 + T * 8 * 8, "steps": e2e_steps},
-            # One block's upload through adi_cuda_upload_moe_layer (host arrays
-            # to HBM, byte for byte), after the first, which sets up the
-            # staging buffers.
-            "upload": {"block_bytes": upload_bytes, "ms": upload_ms, "gbs": upload_bytes / upload_ms / 1e6},
-            "gpu_launches": launches,
-            "clocks": clock_info,
-        }
-        if baseline is not None:
-            line["cpu_baseline"] = baseline
-        print(json.dumps(line), flush=True)
-    for h in handles:
-        h.release()
+    baseline = None if args.no_baseline else cpu_baseline(blocks[0])
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "f16 operands, f32 accumulate" if args.precision else "f32", "data": "synthetic",
+        "config": c4_config(H, E, blocks[0].expert_hidden, L),
+        "parallelism": "one GPU: all experts, all tokens",
+        "roofline": expert_gemm_roofline(stages, n_touched, 8 * T),
+        "block_hbm": {"achieved_gbs": block_gbs, "frac": block_gbs / hbm_peak,
+                      "bytes_per_step": sum(block_bytes) / len(block_bytes),
+                      "experts_touched_mean": sum(n_touched) / len(n_touched)},
+        "stages_ms_per_step": {k: v[0] / max(1, v[1]) for k, v in all_stages.items()},
+        "c2": c2,
+        "ubatch_sweep": sweep,
+        "decode_c3": {"layers": C3_LAYERS, "distinct_weight_sets": C3_DISTINCT,
+                      "per_layer": "MoE block + NE q/k/v/gated-delta (one group call) + NE o",
+                      "head": f"int5_g64 {C3_VOCAB}x2048", **c3},
+        "stack_c5": c5,
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4 + T * (E + 1) * 4,
+                "d2h_bytes_per_step": T * H * 4, "steps": e2e_steps},
+        # One block's upload through adi_cuda_upload_moe_layer (host arrays
+        # to HBM, byte for byte), after the first, which sets up the
+        # staging buffers.
+        "upload": {"block_bytes": upload_bytes, "ms": upload_ms, "gbs": upload_bytes / upload_ms / 1e6},
+        "gpu_launches": launches,
+        "clocks": clock_info,
+    }
+    if baseline is not None:
+        line["cpu_baseline"] = baseline
+    print(json.dumps(line), flush=True)
     ctx.close()
 
 

@@ -201,6 +201,17 @@ ADI_CUDA_API int adi_cuda_moe_forward_batch_device(adi_cuda_context *context,
                                       float *outputs, uint32_t *route_experts,
                                       float *route_weights);
 
+/* moe_forward_batch with a prescribed routing (no counterpart in the
+ * reference's API; its harness does the same for load studies): the caller's
+ * router_logits [batch][experts + 1] (the last column the shared-expert gate
+ * logit) replace the router and shared-gate products; top_experts and every
+ * step after are the block's own. Device pointers, asynchronous. */
+ADI_CUDA_API int adi_cuda_moe_forward_batch_logits_device(adi_cuda_context *context,
+                                      adi_cuda_handle layer, const float *inputs,
+                                      const float *router_logits, uint32_t batch,
+                                      float *outputs, uint32_t *route_experts,
+                                      float *route_weights);
+
 /* The MoE half of the decoder layer over a stack of layers, device-resident
  * (src/executor.cpp:1513-1531 per layer, then finalize_hidden :1533-1540 and
  * the output head): for each layer l,
@@ -259,31 +270,41 @@ ADI_CUDA_API int adi_cuda_ne_matmul_group_device(adi_cuda_context *context, uint
  * stream. */
 
 /* Peer-memory exchange (one node; no counterpart in the reference). The
- * same split as above with the two row exchanges done by this library's
- * kernels over NVLink instead of by the caller: the dispatch writes each
- * route's row straight into the receive buffer of the rank that owns its
- * expert, and the experts' output transform writes each output row straight
- * back into the sender's returned buffer. Per block and rank:
+ * same split as above with every exchange done by this library's kernels
+ * over NVLink, and no count, offset or size passing through the host: the
+ * ranks exchange their expert counts through each other's memory, derive
+ * every offset from them on the device, write each route's row straight into
+ * the receive buffer of the rank that owns its expert, and write each expert
+ * output row straight back into the sender's returned buffer. Per block and
+ * rank, all asynchronous on the context stream:
  *
  *   1. adi_cuda_ep_dispatch_device with send_rows null (routes, counts,
  *      shared expert);
- *   2. the caller all-gathers the expert counts ([world][E] int32) and
- *      copies them to the host;
- *   3. adi_cuda_ep_send_peer_device (host counts) writes the rows;
- *   4. the caller orders every rank after every rank's step 3 (e.g. a
- *      one-element all-reduce on the same stream);
- *   5. adi_cuda_ep_experts_peer_device (device counts, received row count)
- *      runs this rank's experts and writes the rows back;
- *   6. the same ordering as 4;
- *   7. adi_cuda_ep_combine_peer_device.
+ *   2. adi_cuda_ep_send_peer_device (this rank's counts from step 1): the
+ *      counts to every rank, a barrier, the rows, a barrier;
+ *   3. adi_cuda_ep_experts_peer_device: this rank's experts on what it
+ *      received, the output rows back to their senders, a barrier;
+ *   4. adi_cuda_ep_combine_peer_device.
+ *
+ * The barriers are kernels that signal every rank through its memory and
+ * wait for every rank's signal, each wait bounded (2 s; then the next
+ * synchronising call returns ADI_CUDA_TIMEOUT). Every rank must make the
+ * same calls in the same order. Every rank checks every rank's buffer
+ * capacities on the same exchanged counts, so they agree: a block whose
+ * rows would not fit writes nothing, and the next synchronising call of
+ * every rank returns ADI_CUDA_INVALID_ARGUMENT.
  *
  * Set-up: adi_cuda_ep_peer_alloc allocates this rank's buffers (receive
  * rows of `recv_rows`, returned rows of `returned_rows`, `hidden` floats
- * each) and writes their three 64-byte CUDA IPC handles to handles[0..191];
- * after the caller gathers every rank's handles ([world][192] bytes),
- * adi_cuda_ep_peer_connect opens the others' buffers. adi_cuda_ep_peer_close
- * closes those mappings; every rank closes before any rank shuts its context
- * down, since shutting down frees the buffers others map. world <= 8. */
+ * each, and the barrier and count buffer) and writes their CUDA IPC handles
+ * and sizes to handles[0 .. ADI_CUDA_EP_PEER_HANDLE_BYTES); after the caller
+ * gathers every rank's blob ([world][ADI_CUDA_EP_PEER_HANDLE_BYTES] bytes,
+ * rank order), adi_cuda_ep_peer_connect checks that every rank has the same
+ * hidden size, records every rank's capacities and opens the others'
+ * buffers. adi_cuda_ep_peer_close closes those mappings; every rank closes
+ * before any rank shuts its context down, since shutting down frees the
+ * buffers others map. world <= 8, experts <= 1024. */
+#define ADI_CUDA_EP_PEER_HANDLE_BYTES 272
 ADI_CUDA_API int adi_cuda_ep_peer_alloc(adi_cuda_context *context, uint32_t recv_rows,
                                         uint32_t returned_rows, uint32_t hidden,
                                         uint8_t *handles);
@@ -292,14 +313,16 @@ ADI_CUDA_API int adi_cuda_ep_peer_connect(adi_cuda_context *context, uint32_t ra
 ADI_CUDA_API int adi_cuda_ep_peer_close(adi_cuda_context *context);
 ADI_CUDA_API int adi_cuda_ep_send_peer_device(adi_cuda_context *context, adi_cuda_handle shard,
                                               const float *inputs, uint32_t tokens,
-                                              const uint32_t *all_counts_host);
+                                              const uint32_t *expert_counts);
 ADI_CUDA_API int adi_cuda_ep_experts_peer_device(adi_cuda_context *context,
-                                                 adi_cuda_handle shard,
-                                                 const uint32_t *all_counts_device,
-                                                 uint32_t rows);
+                                                 adi_cuda_handle shard);
 ADI_CUDA_API int adi_cuda_ep_combine_peer_device(adi_cuda_context *context,
                                                  adi_cuda_handle shard, uint32_t tokens,
                                                  float *outputs);
+/* The exchanged counts of the last block, [world][experts] into a device
+ * buffer (asynchronous): row s holds rank s's routes per global expert. */
+ADI_CUDA_API int adi_cuda_ep_peer_counts_device(adi_cuda_context *context, uint32_t experts,
+                                                uint32_t *counts);
 
 /* Uploads routed experts [first_expert, first_expert + expert_count) of
  * `layer` plus its router and shared expert (replicated). `layer->routed`

@@ -243,14 +243,23 @@ class Reference(_Checker):
         self.lib.ref_ne_row_states(ptr(np.ascontiguousarray(words, np.uint16), u16p), ptr(out, u32p))
         return out
 
-    def moe_forward(self, layer, inputs: np.ndarray, batched: bool = True):
+    def moe_forward(self, layer, inputs: np.ndarray, batched: bool = True, logits: np.ndarray | None = None):
+        """The reference's batched (or per-token) MoE glue. `logits`
+        [T][experts + 1], when given, replace the router and shared-gate
+        products (a prescribed routing; batched only)."""
         x = np.ascontiguousarray(inputs, np.float32).reshape(-1, layer.hidden)
         T = x.shape[0]
         out = np.zeros_like(x)
         experts = np.zeros((T, 8), np.uint32)
         weights = np.zeros((T, 8), np.float32)
         desc = self.moe_desc(layer)
-        if batched:
+        if logits is not None:
+            lg = np.ascontiguousarray(logits, np.float32).reshape(T, layer.experts + 1)
+            status = self.lib.ref_moe_forward_batch_logits(C.byref(desc), ptr(x, f32p), ptr(lg, f32p), T,
+                                                           ptr(out, f32p), ptr(experts, u32p), ptr(weights, f32p))
+            if status:
+                raise ValueError(self.last_error())
+        elif batched:
             status = self.lib.ref_moe_forward_batch(C.byref(desc), ptr(x, f32p), T, ptr(out, f32p),
                                                     ptr(experts, u32p), ptr(weights, f32p))
             if status:

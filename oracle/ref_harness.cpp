@@ -383,10 +383,47 @@ int ref_moe_forward(const ref_moe_layer *layer, const float *input,
 // sort that gives every active expert one contiguous row range, a gather,
 // expert tasks of at most 32 rows pulled dynamically, the route-order
 // combine, and the shared expert over the whole batch.
+namespace {
+// moe_forward_batch's glue (src/executor.cpp:1181-1453); given_logits, when
+// not null, [batch][experts + 1], replace the router product and the shared
+// expert's gate product (the last column): a prescribed routing for load
+// studies, everything after the router unchanged.
+void moe_forward_batch_impl(const ref_moe_layer *layer, const float *inputs,
+                            std::uint32_t batch, const float *given_logits,
+                            float *outputs, std::uint32_t *route_experts,
+                            float *route_weights);
+}  // namespace
+
 int ref_moe_forward_batch(const ref_moe_layer *layer, const float *inputs,
                           std::uint32_t batch, float *outputs,
                           std::uint32_t *route_experts, float *route_weights) {
     return guarded([&] {
+        moe_forward_batch_impl(layer, inputs, batch, nullptr, outputs,
+                               route_experts, route_weights);
+    });
+}
+
+int ref_moe_forward_batch_logits(const ref_moe_layer *layer, const float *inputs,
+                                 const float *logits, std::uint32_t batch,
+                                 float *outputs, std::uint32_t *route_experts,
+                                 float *route_weights) {
+    return guarded([&] {
+        if (!logits) {
+            throw std::invalid_argument("router logits pointer is null");
+        }
+        moe_forward_batch_impl(layer, inputs, batch, logits, outputs,
+                               route_experts, route_weights);
+    });
+}
+
+} // extern "C"
+
+namespace {
+void moe_forward_batch_impl(const ref_moe_layer *layer, const float *inputs,
+                            std::uint32_t batch, const float *given_logits,
+                            float *outputs, std::uint32_t *route_experts,
+                            float *route_weights) {
+    {
         constexpr std::uint32_t top = 8;
         constexpr std::uint32_t rows_per_task = 32;
         const auto &backend = adi::cpu_backend();
@@ -401,9 +438,16 @@ int ref_moe_forward_batch(const ref_moe_layer *layer, const float *inputs,
         const std::uint32_t positions = batch * top;
 
         std::vector<float> logits(static_cast<std::size_t>(batch) * experts);
-        backend.dense_bf16_matmul(
-            bf16_view(layer->router_bf16, experts, layer->hidden), x, batch,
-            logits);
+        if (given_logits) {
+            for (std::uint32_t t = 0; t < batch; ++t) {
+                std::copy_n(given_logits + static_cast<std::size_t>(t) * (experts + 1),
+                            experts, logits.begin() + static_cast<std::size_t>(t) * experts);
+            }
+        } else {
+            backend.dense_bf16_matmul(
+                bf16_view(layer->router_bf16, experts, layer->hidden), x, batch,
+                logits);
+        }
 
         std::vector<std::array<adi::ExpertRoute, 8>> routes(batch);
         std::vector<std::uint32_t> counts(experts, 0), offsets(experts + 1),
@@ -503,9 +547,15 @@ int ref_moe_forward_batch(const ref_moe_layer *layer, const float *inputs,
             p0[i] = adi::silu(p0[i]) * p1[i];
         }
         backend.ne_matmul(ne_view(layer->shared_down), p0, batch, p2, codec);
-        backend.dense_bf16_matmul(
-            bf16_view(layer->shared_expert_gate_bf16, 1, layer->hidden), x,
-            batch, p3);
+        if (given_logits) {
+            for (std::uint32_t t = 0; t < batch; ++t) {
+                p3[t] = given_logits[static_cast<std::size_t>(t) * (experts + 1) + experts];
+            }
+        } else {
+            backend.dense_bf16_matmul(
+                bf16_view(layer->shared_expert_gate_bf16, 1, layer->hidden), x,
+                batch, p3);
+        }
         for (std::uint32_t t = 0; t < batch; ++t) {
             const float shared_weight = adi::sigmoid(p3[t]);
             for (std::size_t i = 0; i < hidden; ++i) {
@@ -518,7 +568,10 @@ int ref_moe_forward_batch(const ref_moe_layer *layer, const float *inputs,
                 route_weights[t * top + r] = routes[t][r].weight;
             }
         }
-    });
+    }
 }
+}  // namespace
+
+extern "C" {
 
 } // extern "C"

@@ -111,39 +111,46 @@ def test_expert_parallel_stack_matches_single_process():
 
 
 class _PeerStandIn:
-    """Phases of the peer-memory path that only record what the exchange
-    logic hands them (the data movement itself needs GPUs): rank r routes
-    all of its tokens' routes to expert 3 * r."""
+    """Phases of the peer-memory path that record what the exchange logic
+    hands them (the data movement itself needs GPUs); the count exchange the
+    device does is emulated by a gloo all-gather. Rank r routes all of its
+    tokens' routes to expert 3 * r."""
     experts, hidden, local = 16, 8, 8
 
     def __init__(self, rank):
-        self.rank = rank
+        self.rank, self.calls = rank, []
 
     def dispatch_counts(self, x, logits=None):
         import torch
+        self.calls.append("dispatch")
         counts = torch.zeros(self.experts, dtype=torch.int32)
         counts[3 * self.rank] = 8 * x.shape[0]
+        self.counts = counts
         return counts
 
-    def send_peer(self, x, host):
-        self.host = host.copy()
+    def send_peer(self, x, counts):
+        self.calls.append("send")
+        assert counts is self.counts  # the dispatch's device counts, not a host copy
 
-    def experts_peer(self, all_counts, rows):
-        self.rows = rows
+    def experts_peer(self, device):
+        self.calls.append("experts")
 
     def combine_peer(self, tokens, device):
         import torch
+        self.calls.append("combine")
         return torch.zeros(tokens, self.hidden)
+
+    def peer_counts(self, world, device):
+        import torch
+        import torch.distributed as dist
+        rows = [torch.zeros(self.experts, dtype=torch.int32) for _ in range(world)]
+        dist.all_gather(rows, self.counts)
+        return torch.stack(rows)
 
 
 class _OrderStandIn:
     def __init__(self, rank):
         self.rank, self.max_tokens = rank, 64
-
-    def fence(self):
-        import torch
-        import torch.distributed as dist
-        dist.all_reduce(torch.zeros(1))
 
 
 def peer_logic_worker(rank: int, world: int, port: int):
@@ -160,17 +167,15 @@ def peer_logic_worker(rank: int, world: int, port: int):
         tokens = 3 + rank
         y = moe(torch.zeros(tokens, 8))
         assert y.shape == (tokens, 8)
-        # every rank's counts reach every rank, in rank order
-        want = np.zeros((world, 16), np.int32)
-        for s in range(world):
-            want[s, 3 * s] = 8 * (3 + s)
-        assert np.array_equal(phases.host, want)
+        # the block issues its four device phases and nothing else: no
+        # collective and no read of the counts on the host
+        assert phases.calls == ["dispatch", "send", "experts", "combine"]
+        # the statistics, read afterwards from the exchanged counts
+        (send_splits, recv_splits), received = moe.exchange_stats()
         # rank 0 owns experts 0-7: the routes of ranks 0 (expert 0) and 1 (expert 3)
-        received = 8 * 3 + 8 * 4 if rank == 0 else 0
-        assert phases.rows == received
-        send_splits, recv_splits = moe.last_splits
         assert send_splits == [8 * tokens, 0]
         assert recv_splits == ([24, 32] if rank == 0 else [0, 0])
+        assert int(received.sum()) == (8 * 3 + 8 * 4 if rank == 0 else 0)
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -178,6 +183,6 @@ def peer_logic_worker(rank: int, world: int, port: int):
 
 def test_peer_exchange_host_logic():
     """The host side of the peer-memory exchange (ExpertParallelMoe with a
-    PeerExchange) on 2 gloo ranks: the all-gathered counts, the rows each
-    rank receives and the per-rank splits."""
+    PeerExchange) on 2 gloo ranks: the four device phases in order with no
+    host read in between, and the per-rank splits read back afterwards."""
     mp.spawn(peer_logic_worker, args=(2, free_port()), nprocs=2, join=True)

@@ -90,8 +90,9 @@ def test_configured_block_eight_ranks(oracle):
 
 
 def test_receive_count_mismatch_computes_nothing():
-    """Rows that do not match the counts: no work and the outputs untouched
-    (the plan keeps every index in bounds)."""
+    """Rows that do not match the counts: no work, the outputs untouched (the
+    plan keeps every index in bounds), and the next synchronising call
+    reports the failure; the call after it is clean again."""
     import torch
     import adi_b200
     from adi_b200.expert_parallel import DevicePhases
@@ -101,13 +102,12 @@ def test_receive_count_mismatch_computes_nothing():
         ph = DevicePhases(c, layer, 0, 2)
         recv = torch.randn(10, 256, device="cuda")
         counts = torch.tensor([1] * 8 + [0] * 8, dtype=torch.int32, device="cuda")  # sums to 8, not 10
-        out = ph.experts_forward(recv, counts, 2)
-        torch.cuda.synchronize()
-        assert out.shape == (10, 256)
         marker = torch.full((10, 256), float("nan"), device="cuda")
         c.ep_experts_device(ph.handle, recv.data_ptr(), counts.data_ptr(), 2, 10, marker.data_ptr())
-        c.synchronize()
+        with pytest.raises(ValueError, match="did not match its rows"):
+            c.synchronize()
         assert torch.isnan(marker).all()
+        c.synchronize()
     finally:
         c.close()
 

@@ -87,6 +87,7 @@ SIGNATURES = {
     "adi_cuda_moe_forward_batch": (C.c_int, [_ctx, _h, f32p, C.c_uint32, f32p, u32p, f32p]),
     "adi_cuda_expert_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
     "adi_cuda_ne_matmul_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
+    "adi_cuda_ne_matmul_cropped_device": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p, C.c_uint32]),
     "adi_cuda_ne_matmul_group_device": (C.c_int, [_ctx, C.c_uint32, C.POINTER(_h), C.POINTER(C.c_void_p),
                                                   C.POINTER(C.c_void_p), C.c_uint32]),
     "adi_cuda_expert_matmul_device_noalloc": (C.c_int, [_ctx, _h, C.c_void_p, C.c_uint32, C.c_void_p]),
@@ -124,6 +125,9 @@ SIGNATURES = {
 }
 
 INVALID_ARGUMENT = 1
+# cudaStreamLegacy: the default stream with its implicit ordering against
+# every blocking stream (what torch launches on unless told otherwise).
+CUDA_STREAM_LEGACY = 0x1
 EP_PEER_HANDLE_BYTES = 272  # ADI_CUDA_EP_PEER_HANDLE_BYTES
 
 _lib: Optional[C.CDLL] = None
@@ -442,6 +446,11 @@ class Context:
         fn = {"expert": self.lib.adi_cuda_expert_matmul_device, "ne": self.lib.adi_cuda_ne_matmul_device,
               "head": self.lib.adi_cuda_head_matmul_device, "bf16": self.lib.adi_cuda_bf16_matmul_device}[handle.kind]
         _check(fn(self.ptr, handle.value, inputs_ptr, batch, outputs_ptr), fn.__name__)
+
+    def ne_matmul_cropped_device(self, handle: Handle, inputs_ptr: int, batch: int, outputs_ptr: int, kept: int):
+        """mach_ne_matmul keeping the first `kept` rows (a padded NE head)."""
+        _check(self.lib.adi_cuda_ne_matmul_cropped_device(self.ptr, handle.value, inputs_ptr, batch, outputs_ptr,
+                                                           kept), "adi_cuda_ne_matmul_cropped_device")
 
     def ne_matmul_group_device(self, handles, inputs_ptrs, outputs_ptrs, batch: int):
         """Several NE projections of one small batch (device pointers): the

@@ -812,6 +812,7 @@ struct NeDecodeCall {
     NeDev *m;
     const float *in;
     float *out;
+    float *sums = nullptr;  // set: leave the weighted sums [batch][rows] here, no output transform
 };
 
 // Small-batch NE projections through the decode kernels (decode.cu): the
@@ -856,6 +857,10 @@ void ne_decode_dev(adi_cuda_context *c, std::vector<NeDecodeCall> calls, uint32_
             J.xp = xp + xo;
             J.acc = acc + ao;
             J.out = calls[first + i].out;
+            if (calls[first + i].sums) {
+                J.acc = calls[first + i].sums;
+                J.sums_only = 1;
+            }
             J.rows = m.rows;
             J.cols = m.cols;
             J.weight_scale = m.weight_scale;
@@ -877,8 +882,57 @@ void ne_decode_dev(adi_cuda_context *c, std::vector<NeDecodeCall> calls, uint32_
     c->stage_end();
 }
 
+void ne_matmul_dev(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batch, float *out);
+
+// Projections with more rows than one block's transform takes (the NE-coded
+// output head, padded to a power of two): the weighted sums, then the
+// multi-pass output transform, which writes rows [0, kept) of each token to
+// out [batch][kept].
+void ne_big_matmul_dev(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batch, float *out, uint32_t kept) {
+    float *acc = c->buffer<float>("ne_big_acc", size_t(batch) * m.rows);
+    if (ne_decode_sums_shape(m.rows, m.cols, batch)) {
+        NeDecodeCall call{&m, in, nullptr, acc};
+        ne_decode_dev(c, {call}, batch);
+    } else {
+        float *xp = c->buffer<float>("x_prep", size_t(batch) * m.cols);
+        c->stage(kStageNeMatmul);
+        PrepParams pp{};
+        pp.input = in;
+        pp.su[0] = m.su->ptr;
+        pp.out[0] = xp;
+        pp.cols = m.cols;
+        pp.scale = transform_scale(m.cols);
+        pp.rows = batch;
+        pp.jobs = 1;
+        pp.su_is_f16 = 0;
+        launch_prep(pp, c->stream);
+        NeGemmParams gp{};
+        gp.job[0] = NeJob{m.trellis->as<uint32_t>(), xp, acc, m.rows, m.cols, m.weight_scale};
+        gp.job[1] = gp.job[0];
+        gp.table = m.codec->table.as<float2>();
+        gp.row_tiles = ne_row_tiles(c, batch, m.rows, 1);
+        gp.error = c->error_word;
+        const uint32_t nt = ne_tokens_per_item(gp.row_tiles, batch);
+        gp.work = WorkList{nullptr, nullptr, batch, 1, nt};
+        const uint64_t items = uint64_t((batch + nt - 1) / nt) * row_blocks(m.rows, gp.row_tiles);
+        launch_ne_gemm(gp, gemm_grid(c, items, 1), c->stream);
+        c->stage_end();
+        c->after_launch(2);
+    }
+    uint32_t log2_rows = 0;
+    while ((1u << log2_rows) < m.rows) ++log2_rows;
+    const uint32_t passes = 1 + (log2_rows - 8 + 4) / 5;  // strides 1-128, then five doublings a pass
+    launch_ne_big_transform(acc, batch, m.rows, m.sv->as<int8_t>(), transform_scale(m.rows), out, kept,
+                            c->stream);
+    c->after_launch(passes);
+}
+
 void ne_matmul_dev(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batch, float *out) {
     if (batch == 0) invalid("Mach NE batch shape mismatch");
+    if (m.rows > kNeDecodeMaxRows) {
+        ne_big_matmul_dev(c, m, in, batch, out, m.rows);
+        return;
+    }
     if (ne_decode_shape(m.rows, m.cols, batch)) {
         ne_decode_dev(c, {NeDecodeCall{&m, in, out}}, batch);
         return;
@@ -1998,6 +2052,31 @@ ADI_HOST_MATMUL(adi_cuda_expert_matmul, experts, "expert", expert_matmul_dev)
 ADI_HOST_MATMUL(adi_cuda_ne_matmul, nes, "NE", ne_matmul_dev)
 ADI_HOST_MATMUL(adi_cuda_head_matmul, heads, "head", head_matmul_dev)
 ADI_HOST_MATMUL(adi_cuda_bf16_matmul, bf16s, "bf16", bf16_matmul_dev)
+
+int adi_cuda_ne_matmul_cropped_device(adi_cuda_context *c, adi_cuda_handle h, const float *in, uint32_t batch,
+                                      float *out, uint32_t kept_rows) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!in || !out) invalid("input or output pointer is null");
+        NeDev &m = lookup(c->nes, h, "NE");
+        if (batch == 0) invalid("Mach NE batch shape mismatch");
+        if (kept_rows == 0 || kept_rows > m.rows) invalid("Mach NE kept rows out of range");
+        if (m.rows > kNeDecodeMaxRows) {
+            ne_big_matmul_dev(c, m, in, batch, out, kept_rows);
+            return;
+        }
+        if (kept_rows == m.rows) {
+            ne_matmul_dev(c, m, in, batch, out);
+            return;
+        }
+        float *full = c->buffer<float>("ne_crop_full", size_t(batch) * m.rows);
+        ne_matmul_dev(c, m, in, batch, full);
+        check(cudaMemcpy2DAsync(out, size_t(kept_rows) * 4, full, size_t(m.rows) * 4, size_t(kept_rows) * 4, batch,
+                                cudaMemcpyDeviceToDevice, c->stream),
+              "crop copy");
+    });
+}
 
 int adi_cuda_ne_matmul_group_device(adi_cuda_context *c, uint32_t count, const adi_cuda_handle *matrices,
                                     const float *const *inputs, float *const *outputs, uint32_t batch) {

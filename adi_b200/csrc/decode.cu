@@ -394,6 +394,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) ne_decode_kernel(const __gr
             for (int c = 0; c < 8; ++c) sum += my_red[(c * 16 + row) * NT + q];
             J.acc[(size_t)(t0 + q) * J.rows + at.tile_row * 16 + row] = sum * J.weight_scale;
         }
+        if (J.sums_only) {
+            named_sync(bar, kGroupThreads);  // the sums are read out of my_red before its next use
+            continue;
+        }
         // Arrival: the group's stores are ordered before one thread's fence
         // and count by the barrier (the pattern of a cooperative grid sync);
         // the last arrival fences again before its group reads the other
@@ -435,6 +439,61 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) ne_decode_kernel(const __gr
     griddep_launch_dependents();
 }
 
+// ---- the output transform of large projections ------------------------------
+
+// Strides 1 .. 128 inside each 256-row block of every token's row.
+__global__ void __launch_bounds__(256) fwht_blocks_kernel(float *data, uint32_t n) {
+    __shared__ float sh[padded(256)];
+    float *row = data + (size_t)blockIdx.y * n + (size_t)blockIdx.x * 256u;
+    float v[1] = {row[threadIdx.x]};
+    fwht_strided<1>(v, sh, threadIdx.x, 0);
+    row[threadIdx.x] = v[0];
+}
+
+// Strides 2^lo .. 2^(lo + LB - 1): thread k of a token holds the 2^LB
+// elements base + j 2^lo (base = k with LB zero bits inserted at bit lo),
+// consecutive threads consecutive bases (coalesced for lo >= 5). With
+// `out`, this is the last pass: scale, signs, and only rows below `kept`.
+template <int LB>
+__global__ void __launch_bounds__(256) fwht_columns_kernel(float *data, uint32_t n, uint32_t lo, const int8_t *sv,
+                                                           float scale, float *out, uint32_t kept) {
+    constexpr uint32_t B = 1u << LB;
+    const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= n / B) return;
+    const uint32_t t = blockIdx.y;
+    const size_t base = ((size_t)(k >> lo) << (lo + LB)) | (k & ((1u << lo) - 1u));
+    float *row = data + (size_t)t * n;
+    float v[B];
+#pragma unroll
+    for (uint32_t j = 0; j < B; ++j) v[j] = row[base + ((size_t)j << lo)];
+#pragma unroll
+    for (uint32_t s = 1; s < B; s <<= 1)
+#pragma unroll
+        for (uint32_t r = 0; r < B; ++r)
+            if ((r & s) == 0) {
+                const float a = v[r], b = v[r + s];
+                v[r] = __fadd_rn(a, b);
+                v[r + s] = __fsub_rn(a, b);
+            }
+    if (!out) {
+#pragma unroll
+        for (uint32_t j = 0; j < B; ++j) row[base + ((size_t)j << lo)] = v[j];
+        return;
+    }
+    // The signs first: int8 loads may alias the outputs.
+    float sign[B];
+#pragma unroll
+    for (uint32_t j = 0; j < B; ++j) {
+        const size_t i = base + ((size_t)j << lo);
+        sign[j] = i < kept ? (float)sv[i] : 0.0f;
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < B; ++j) {
+        const size_t i = base + ((size_t)j << lo);
+        if (i < kept) out[(size_t)t * kept + i] = __fmul_rn(__fmul_rn(v[j], scale), sign[j]);
+    }
+}
+
 template <int NT>
 void launch_decode_instance(const NeDecodeParams &p, int grid, cudaStream_t s) {
     static bool configured = false;
@@ -448,10 +507,38 @@ void launch_decode_instance(const NeDecodeParams &p, int grid, cudaStream_t s) {
 
 }  // namespace
 
+bool ne_decode_sums_shape(uint32_t rows, uint32_t cols, uint32_t tokens) {
+    auto pow2 = [](uint32_t v) { return v != 0 && (v & (v - 1)) == 0; };
+    return tokens >= 1 && tokens <= kNeDecodeMaxTokens && pow2(rows) && rows >= 256 && rows <= (1u << 24) &&
+           pow2(cols) && cols >= 256 && cols <= kNeDecodeMaxCols;
+}
+
 bool ne_decode_shape(uint32_t rows, uint32_t cols, uint32_t tokens) {
     auto pow2 = [](uint32_t v) { return v != 0 && (v & (v - 1)) == 0; };
     return tokens >= 1 && tokens <= kNeDecodeMaxTokens && pow2(rows) && rows >= 256 && rows <= kNeDecodeMaxRows &&
            pow2(cols) && cols >= 256 && cols <= kNeDecodeMaxCols;
+}
+
+void launch_ne_big_transform(float *acc, uint32_t tokens, uint32_t n, const int8_t *sv, float scale, float *out,
+                             uint32_t kept, cudaStream_t s) {
+    fwht_blocks_kernel<<<dim3(n / 256, tokens), 256, 0, s>>>(acc, n);
+    uint32_t lo = 8, k = 0;
+    while ((1u << (lo + k)) < n) ++k;  // bits left above the first eight
+    while (k > 0) {
+        const uint32_t lb = k < 5 ? k : 5;
+        const bool last = lb == k;
+        const dim3 grid(((n >> lb) + 255) / 256, tokens);
+        float *o = last ? out : nullptr;
+        switch (lb) {
+            case 1: fwht_columns_kernel<1><<<grid, 256, 0, s>>>(acc, n, lo, sv, scale, o, kept); break;
+            case 2: fwht_columns_kernel<2><<<grid, 256, 0, s>>>(acc, n, lo, sv, scale, o, kept); break;
+            case 3: fwht_columns_kernel<3><<<grid, 256, 0, s>>>(acc, n, lo, sv, scale, o, kept); break;
+            case 4: fwht_columns_kernel<4><<<grid, 256, 0, s>>>(acc, n, lo, sv, scale, o, kept); break;
+            default: fwht_columns_kernel<5><<<grid, 256, 0, s>>>(acc, n, lo, sv, scale, o, kept); break;
+        }
+        lo += lb;
+        k -= lb;
+    }
 }
 
 void launch_ne_decode(const NeDecodeParams &p, int sms, cudaStream_t s) {

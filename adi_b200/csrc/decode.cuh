@@ -50,6 +50,8 @@ struct NeDecodeJob {
     // chunk so that a chunk's x' fits a group's staging buffer.
     uint32_t chunk_tokens, chunks;
     uint32_t tile_row_shift;    // log2(rows / 16)
+    uint32_t sums_only;         // 1: leave the weighted sums in `acc` (no output transform; rows may
+                                // exceed kNeDecodeMaxRows) for launch_ne_big_transform
     uint32_t first_item;        // the job's first item in the launch's item list; items are
                                 // chunk-major: first_item + chunk * rows / 16 + tile row
 };
@@ -63,6 +65,20 @@ struct NeDecodeParams {
 
 // True when a projection of this shape and batch can take the decode path.
 bool ne_decode_shape(uint32_t rows, uint32_t cols, uint32_t tokens);
+
+// The same with the output transform left to launch_ne_big_transform:
+// any power-of-two row count from 256 up.
+bool ne_decode_sums_shape(uint32_t rows, uint32_t cols, uint32_t tokens);
+
+// y = H(acc) / sqrt(n) * sv for power-of-two n > kNeDecodeMaxRows (the
+// output transform of a large projection such as the NE-coded head, whose
+// rows are padded to a power of two): `acc` [tokens][n] is transformed in
+// place by passes of strides 1-128, then up to five doublings at a time;
+// the last pass writes rows [0, kept) of each token to out [tokens][kept]
+// (the crop from the padding). The same butterflies in the same stride
+// order as every other transform here.
+void launch_ne_big_transform(float *acc, uint32_t tokens, uint32_t n, const int8_t *sv, float scale, float *out,
+                             uint32_t kept, cudaStream_t s);
 
 // Tokens per work item of a job with `cols` columns: as many as fit one
 // group's x' staging buffer (kNeDecodeMaxCols floats).

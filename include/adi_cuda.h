@@ -229,6 +229,16 @@ ADI_CUDA_API int adi_cuda_moe_stack_forward_device(adi_cuda_context *context,
                                       adi_cuda_handle head, float *hidden,
                                       uint32_t tokens, float *logits);
 
+/* mach_ne_matmul keeping rows [0, kept_rows) of each output row: out
+ * [batch][kept_rows]. For a projection stored padded to a power of two, as
+ * the NE-coded output head is (its rows padded and the result cropped,
+ * docs/gguf.md:84-93 of the reference: "crop from power-of-two padding").
+ * Projections of more than 8192 rows take a multi-pass output transform
+ * here and in the other NE entries. Device pointers, asynchronous. */
+ADI_CUDA_API int adi_cuda_ne_matmul_cropped_device(adi_cuda_context *context, adi_cuda_handle matrix,
+                                                  const float *inputs, uint32_t batch, float *outputs,
+                                                  uint32_t kept_rows);
+
 /* Several NE projections of one small batch in one call, device pointers:
  * outputs[i] [batch][rows_i] = mach_ne_matmul(matrices[i], inputs[i]
  * [batch][cols_i]), the same results as one adi_cuda_ne_matmul_device per

@@ -24,5 +24,8 @@ def oracle():
 def ctx():
     import adi_b200
     context = adi_b200.Context(0)
+    # The tests stage inputs and outputs with torch on the default stream:
+    # the context launches there too, so the two stay ordered.
+    context.set_stream(adi_b200.CUDA_STREAM_LEGACY)
     yield context
     context.close()

@@ -82,6 +82,7 @@ def gpu_stack(blocks, norms, final, head, prompt, rows):
     import adi_b200
     ctx = adi_b200.Context(0)
     try:
+        ctx.set_stream(adi_b200.CUDA_STREAM_LEGACY)  # ordered with torch's copies of the decode rows
         ctx.set_precision(1)
         moe_h = [ctx.upload_moe_layer(b) for b in blocks]
         head_h = ctx.upload_head(head)

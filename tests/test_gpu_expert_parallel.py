@@ -99,6 +99,7 @@ def test_receive_count_mismatch_computes_nothing():
     layer = moe_layer(seed=5, hidden=256, expert_hidden=64, experts=16, scale_mu=-1.0, shared_mu=-3.0)
     c = adi_b200.Context(0)
     try:
+        c.set_stream(adi_b200.CUDA_STREAM_LEGACY)  # ordered with torch's fills
         ph = DevicePhases(c, layer, 0, 2)
         recv = torch.randn(10, 256, device="cuda")
         counts = torch.tensor([1] * 8 + [0] * 8, dtype=torch.int32, device="cuda")  # sums to 8, not 10

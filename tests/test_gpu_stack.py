@@ -115,6 +115,7 @@ def test_stack_configured_tensor_cores(oracle):
     x = activations(902, 8, 2048)
     c = adi_b200.Context(0)
     try:
+        c.set_stream(adi_b200.CUDA_STREAM_LEGACY)  # ordered with torch's copies
         c.set_precision(1)
         stack = GpuStack(c, blocks, norms, final, head)
         try:

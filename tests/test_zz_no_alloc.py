@@ -33,6 +33,7 @@ def needed_bytes(batch, rows, cols):
 def context():
     import adi_b200
     c = adi_b200.Context(0)
+    c.set_stream(adi_b200.CUDA_STREAM_LEGACY)  # ordered with torch's fills and copies
     c.set_precision(0)
     yield c
     c.close()

@@ -1293,13 +1293,24 @@ bool launch_top_experts_parts(const float *partials, uint32_t parts, uint32_t ro
 // rank within its expert is the number of earlier tokens routed there,
 // read off a per-expert token bitmap.
 // ---------------------------------------------------------------------------
+// Counts per expert in shared memory first (one global add per block and
+// expert: a skewed routing would otherwise queue thousands of adds on one
+// address), and each route's bit in its expert's token bitmap.
 __global__ void route_count_kernel(RouteParams p) {
+    extern __shared__ uint32_t block_counts[];
+    for (uint32_t e = threadIdx.x; e < p.experts; e += blockDim.x) block_counts[e] = 0;
+    __syncthreads();
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= p.tokens * 8) return;
-    const uint32_t t = i >> 3, e = p.route_experts[i];
-    if (e >= p.experts) return;  // top-k never emits one; never index with it
-    atomicAdd(p.counts + e, 1u);
-    atomicOr(p.bitmap + (size_t)e * p.words + (t >> 5), 1u << (t & 31u));
+    if (i < p.tokens * 8) {
+        const uint32_t t = i >> 3, e = p.route_experts[i];
+        if (e < p.experts) {  // top-k never emits another; never index with it
+            atomicAdd(block_counts + e, 1u);
+            atomicOr(p.bitmap + (size_t)e * p.words + (t >> 5), 1u << (t & 31u));
+        }
+    }
+    __syncthreads();
+    for (uint32_t e = threadIdx.x; e < p.experts; e += blockDim.x)
+        if (block_counts[e]) atomicAdd(p.counts + e, block_counts[e]);
 }
 
 // One block of 1024 threads: offsets, per-expert word prefixes, the position
@@ -1324,28 +1335,37 @@ __global__ void route_scan_kernel(RouteParams p) {
     }
     const uint32_t offset = scan[e] - count;
     const uint32_t chunk_offset = chunk_scan[e] - chunks;
-    if (e < p.experts) {
-        p.offsets[e] = offset;
-        for (uint32_t i = 0; i < count; ++i) p.pos_expert[offset + i] = e;
-        for (uint32_t c = 0; c < chunks; ++c) {
-            const uint32_t pos0 = offset + c * p.chunk;
-            const uint32_t n = min(p.chunk, count - c * p.chunk);
-            for (uint32_t j = 0; j < 2; ++j)
-                for (uint32_t rb = 0; rb < p.row_blocks_gate_up; ++rb)
-                    p.items_gate_up[((chunk_offset + c) * 2 + j) * p.row_blocks_gate_up + rb] =
-                        make_uint4(e, (j << 16) | rb, pos0, n);
-            for (uint32_t rb = 0; rb < p.row_blocks_down; ++rb)
-                p.items_down[(chunk_offset + c) * p.row_blocks_down + rb] = make_uint4(e, rb, pos0, n);
-        }
-    }
+    if (e < p.experts) p.offsets[e] = offset;
     if (e == p.experts - 1) {
         p.offsets[p.experts] = offset + count;
         const uint32_t total_chunks = chunk_offset + chunks;
         *p.count_gate_up = total_chunks * 2 * p.row_blocks_gate_up;
         *p.count_down = total_chunks * p.row_blocks_down;
     }
-    // Per-expert exclusive prefix of bitmap popcounts, one warp per expert.
+    // The position -> expert map and the work items, a warp per expert (a
+    // popular expert's thousands of positions would serialise one thread).
+    __syncthreads();
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    for (uint32_t ex = warp; ex < p.experts; ex += 32) {
+        const uint32_t ex_count = scan[ex] - (ex ? scan[ex - 1] : 0u);
+        const uint32_t ex_offset = scan[ex] - ex_count;
+        const uint32_t ex_chunks = (ex_count + p.chunk - 1) / p.chunk;
+        const uint32_t ex_chunk_offset = chunk_scan[ex] - ex_chunks;
+        for (uint32_t i = lane; i < ex_count; i += 32) p.pos_expert[ex_offset + i] = ex;
+        const uint32_t per_chunk = 2 * p.row_blocks_gate_up;
+        for (uint32_t k = lane; k < ex_chunks * per_chunk; k += 32) {
+            const uint32_t c = k / per_chunk, j = (k % per_chunk) / p.row_blocks_gate_up, rb = k % p.row_blocks_gate_up;
+            const uint32_t pos0 = ex_offset + c * p.chunk, n = min(p.chunk, ex_count - c * p.chunk);
+            p.items_gate_up[((ex_chunk_offset + c) * 2 + j) * p.row_blocks_gate_up + rb] =
+                make_uint4(ex, (j << 16) | rb, pos0, n);
+        }
+        for (uint32_t k = lane; k < ex_chunks * p.row_blocks_down; k += 32) {
+            const uint32_t c = k / p.row_blocks_down, rb = k % p.row_blocks_down;
+            const uint32_t pos0 = ex_offset + c * p.chunk, n = min(p.chunk, ex_count - c * p.chunk);
+            p.items_down[(ex_chunk_offset + c) * p.row_blocks_down + rb] = make_uint4(ex, rb, pos0, n);
+        }
+    }
+    // Per-expert exclusive prefix of bitmap popcounts, one warp per expert.
     for (uint32_t ex = warp; ex < p.experts; ex += 32) {
         uint32_t running = 0;
         for (uint32_t w0 = 0; w0 < p.words; w0 += 32) {
@@ -1618,7 +1638,7 @@ uint32_t launch_route(const RouteParams &p, cudaStream_t s) {
     cudaMemsetAsync(p.counts, 0, sizeof(uint32_t) * p.experts, s);
     cudaMemsetAsync(p.bitmap, 0, sizeof(uint32_t) * (size_t)p.experts * p.words, s);
     const uint32_t n = p.tokens * 8;
-    route_count_kernel<<<(n + 255) / 256, 256, 0, s>>>(p);
+    route_count_kernel<<<(n + 255) / 256, 256, p.experts * sizeof(uint32_t), s>>>(p);
     route_scan_kernel<<<1, 1024, 0, s>>>(p);
     route_place_kernel<<<(n + 255) / 256, 256, 0, s>>>(p);
     return 3;

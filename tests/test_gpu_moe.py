@@ -131,3 +131,50 @@ def test_top_experts_bit_exact(ctx, oracle):
     e, w = ctx.top_experts(np.arange(16, dtype=np.float32)[None, :])
     assert list(e[0]) == list(range(15, 7, -1))
     assert abs(w[0].sum() - 1.0) < 1e-6
+
+
+@pytest.mark.parametrize("precision,tol", [(0, FP32_TOL), (1, 1e-2)])
+def test_large_ubatch_prescribed_zipf_logits(precision, tol):
+    """2048 tokens (16384 routes: the multi-kernel counting sort) with router
+    logits prescribed as C4 prescribes them (Zipf-skewed expert popularity,
+    so some experts get thousands of routes), through
+    adi_cuda_moe_forward_batch_logits_device, against the reference build's
+    batched glue on the same logits: routes bit-exact, outputs within the
+    precision mode's bound."""
+    import sys
+    from pathlib import Path
+
+    import torch
+    import adi_b200
+    from adi_b200 import synthetic
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "oracle"))
+    from ffi import Reference, reference_available
+    if not reference_available():
+        pytest.skip("oracle/_ref is not built")
+    block = synthetic.moe_block(seed=31, scale_mu=-1.0, device="cuda")
+    T, E = 2048, block.experts
+    rng = np.random.default_rng(32)
+    log_p = -1.1 * np.log(rng.permutation(E) + 1.0)
+    u = rng.random((T, E)).clip(1e-12, 1 - 1e-7)
+    logits = np.concatenate([log_p - np.log(-np.log(u)), rng.standard_normal((T, 1))], axis=1).astype(np.float32)
+    x = synthetic.activations(33, T, block.hidden, device="cpu").numpy()
+    c = adi_b200.Context(0)
+    try:
+        c.set_stream(adi_b200.CUDA_STREAM_LEGACY)
+        c.set_precision(precision)
+        h = c.upload_moe_layer(block)
+        dx, dl = torch.from_numpy(x).cuda(), torch.from_numpy(logits).cuda()
+        y = torch.empty(T, block.hidden, device="cuda")
+        re = torch.empty(T, 8, dtype=torch.int32, device="cuda")
+        rw = torch.empty(T, 8, device="cuda")
+        c.moe_forward_batch_logits_device(h, dx.data_ptr(), dl.data_ptr(), T, y.data_ptr(), re.data_ptr(),
+                                          rw.data_ptr())
+        c.synchronize()
+        got, got_e = y.cpu().numpy(), re.cpu().numpy().astype(np.uint32)
+        h.release()
+    finally:
+        c.close()
+    want, want_e, _ = Reference().moe_forward(block, x, logits=logits)
+    assert np.array_equal(got_e, want_e)
+    assert np.bincount(want_e.reshape(-1), minlength=E).max() > 1000  # the skew reaches the sort
+    assert rel_l2(got, want) <= tol

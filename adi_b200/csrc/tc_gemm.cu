@@ -48,10 +48,10 @@ namespace {
 
 // Ring depths (overridable at build time for tuning sweeps).
 #ifndef ADI_TC_WORD_STAGES
-#define ADI_TC_WORD_STAGES 5
+#define ADI_TC_WORD_STAGES 4
 #endif
 #ifndef ADI_TC_B_STAGES
-#define ADI_TC_B_STAGES 3
+#define ADI_TC_B_STAGES 2
 #endif
 #ifndef ADI_TC_A_STAGES
 #define ADI_TC_A_STAGES 3

@@ -9,7 +9,14 @@
 
 namespace adi_cuda {
 
-constexpr uint32_t kTcMaxN = 64;  // positions per work unit (MMA N)
+// Positions per work unit (MMA N). 128: at 128 positions per expert (a
+// 4096-token step) each 128-row block of an expert is decoded once instead
+// of twice; measured 0.82 -> 0.71 ms of expert GEMM per 4096-token block.
+// It takes the shallower rings below to fit shared memory.
+#ifndef ADI_TC_MAX_N
+#define ADI_TC_MAX_N 128
+#endif
+constexpr uint32_t kTcMaxN = ADI_TC_MAX_N;
 
 enum class TcCodec { kExpert, kNe };
 

@@ -271,7 +271,6 @@ struct MoeDev {
     uint32_t hidden, inner, experts;
     uint32_t first_expert = 0, local_experts = 0;  // routed experts held: [first, first + local)
     std::unique_ptr<DeviceArray> router;  // [(E+1)][H] bf16: router rows then the shared gate
-    std::unique_ptr<DeviceArray> router3; // [rows_pad][3H] bf16: router rows three times along K, zero rows pad
     uint32_t router_rows_pad = 0;
     std::unique_ptr<DeviceArray> trellis[3], su[3], sv[3], gamma[3], ka[3];
     ExpertCodec *codec;
@@ -1123,7 +1122,8 @@ uint32_t route_tokens(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t 
         rp.partials = c->buffer<float>("router_parts", size_t(rp.parts) * T * rp.rows_pad);
         rp.error = c->error_word;
         uint16_t *xs = c->buffer<uint16_t>("router_xs", size_t(T) * 3 * H);
-        if (!launch_router_tc(rp, in, xs, L.router3->as<uint16_t>(), nullptr, E + 1, E + 1, c->stream))
+        rp.w_rows = E + 1;
+        if (!launch_router_tc(rp, in, xs, L.router->as<uint16_t>(), nullptr, E + 1, E + 1, c->stream))
             throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
         c->stage_end();
         c->stage(kStageTopk);
@@ -1534,15 +1534,9 @@ uint64_t upload_moe(adi_cuda_context *c, const adi_moe_layer &layer, uint32_t fi
     std::memcpy(router.data(), l->router.values, size_t(E) * H * 2);
     std::memcpy(router.data() + size_t(E) * H, l->shared_expert_gate.values, size_t(H) * 2);
     d->router = upload_bytes(router.data(), router.size() * 2, "router");
-    // The tensor-core router's operand: each row repeated three times along
-    // K (against the three bf16 terms of the activations), rows padded to
-    // the MMA's 128.
+    // The tensor-core router reads these rows too (in 128-row blocks, the
+    // rows past E + 1 zero-filled by its tensor map).
     d->router_rows_pad = (E + 1 + 127) / 128 * 128;
-    std::vector<uint16_t> router3(size_t(d->router_rows_pad) * 3 * H, 0);
-    for (uint32_t r = 0; r <= E; ++r)
-        for (uint32_t j = 0; j < 3; ++j)
-            std::memcpy(router3.data() + (size_t(r) * 3 + j) * H, router.data() + size_t(r) * H, size_t(H) * 2);
-    d->router3 = upload_bytes(router3.data(), router3.size() * 2, "router");
     const float *tlut = l->routed[3 * size_t(first)].tlut;
     const uint32_t tiles = (I / 16) * (H / 16);
     for (int p = 0; p < 3; ++p) {

@@ -682,8 +682,11 @@ __global__ void __launch_bounds__(tc_threads<C>(), 1)
 // x2 + x3 (x1 the bf16 rounding of x, x2 of what x1 leaves, x3 the rest,
 // which fits bf16 exactly). Every product of bf16 values is exact in fp32,
 // so [W W W] . [x1 x2 x3] is the fp32 dot product up to the order of the
-// fp32 accumulation. K (3H) is split over CTAs; a second kernel sums the
-// parts in order, so the result is deterministic.
+// fp32 accumulation. W is stored once: the A tile of K chunk kc is W's
+// columns (kc * 64) mod H, so the three K segments read the same rows (the
+// rows past W's last are the tensor map's zero fill). K (3H) is split over
+// CTAs; a second kernel sums the parts in order, so the result is
+// deterministic.
 // ---------------------------------------------------------------------------
 constexpr uint32_t kRouterStages = 4;
 constexpr uint32_t kRouterN = 64;                          // tokens per unit
@@ -750,8 +753,8 @@ __global__ void __launch_bounds__(192, 1)
         for (uint32_t kc = kc0; kc < kc1; ++kc) {
             if (!mbar_wait(&empty[r.slot], r.phase ^ 1u, p.error)) break;
             mbar_arrive_expect_tx(&full[r.slot], kRouterATile + n_pad * kChunkK * 2);
-            tma_load_2d(a_tiles + r.slot * kRouterATile, &amap, (int32_t)(kc * kChunkK), (int32_t)(mb * 128),
-                        &full[r.slot]);
+            tma_load_2d(a_tiles + r.slot * kRouterATile, &amap, (int32_t)((kc * kChunkK) % (p.k / 3)),
+                        (int32_t)(mb * 128), &full[r.slot]);
             for (uint32_t r0 = 0; r0 < n_pad; r0 += kBBoxRows)
                 tma_load_2d(b_tiles + r.slot * kRouterBTile + r0 * kChunkK * 2, &bmap, (int32_t)(kc * kChunkK),
                             (int32_t)(n0 + r0), &full[r.slot]);
@@ -1344,12 +1347,13 @@ uint32_t router_tc_parts(uint32_t rows_pad, uint32_t tokens, uint32_t hidden, in
     return parts;
 }
 
-bool launch_router_tc(const RouterParams &p, const float *x, uint16_t *xs, const uint16_t *w3, float *logits,
+bool launch_router_tc(const RouterParams &p, const float *x, uint16_t *xs, const uint16_t *w, float *logits,
                       uint32_t stride, uint32_t rows, cudaStream_t s) {
     const uint32_t H = p.k / 3;
+    if (H % kChunkK) return false;
     router_split_kernel<<<1184, 256, 0, s>>>(x, p.tokens * H, H, xs);
     CUtensorMap amap, bmap;
-    if (!make_bf16_map(&amap, w3, p.rows_pad, p.k, 128) || !make_bf16_map(&bmap, xs, p.tokens, p.k, kBBoxRows))
+    if (!make_bf16_map(&amap, w, p.w_rows, H, 128) || !make_bf16_map(&bmap, xs, p.tokens, p.k, kBBoxRows))
         return false;
     static bool configured = false;
     if (!configured) {

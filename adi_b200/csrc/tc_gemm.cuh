@@ -60,11 +60,12 @@ bool make_b_map(CUtensorMap *map, const __half *x, uint32_t rows, uint32_t cols)
 // map cannot be encoded.
 struct RouterParams {
     uint32_t rows_pad, tokens, k, parts;
+    uint32_t w_rows;             // rows of the router matrix W [w_rows][k / 3] (rows_pad: w_rows rounded up to 128)
     float *partials;
     uint32_t *error;
 };
 uint32_t router_tc_parts(uint32_t rows_pad, uint32_t tokens, uint32_t hidden, int sms);
-bool launch_router_tc(const RouterParams &p, const float *x, uint16_t *xs, const uint16_t *w3, float *logits,
+bool launch_router_tc(const RouterParams &p, const float *x, uint16_t *xs, const uint16_t *w, float *logits,
                       uint32_t stride, uint32_t rows, cudaStream_t s);
 
 // Returns false when a tensor map cannot be encoded (nothing launched).

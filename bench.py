@@ -326,8 +326,15 @@ def decode_c3(ctx, stream, local, tokens_list=(1, 4), steps=20):
     head_h = ctx.upload_head(head)
     head_bytes = head.packed_bytes()
     del head
+    # The head in the NE codec instead: the vocabulary padded to 2^18 rows
+    # (docs/gguf.md:84-93, crop from power-of-two padding); it streams every
+    # padded row's words.
+    ne_head = synthetic.ne_matrix(7001, 1 << 18, 2048, device=device, tlut=tluts[1])
+    ne_head_h = ctx.upload_ne(ne_head)
+    ne_head_bytes = ne_head.trellis.nbytes + ne_head.su.nbytes + ne_head.sv.nbytes + 4
+    del ne_head
     out = {}
-    for T in tokens_list:
+    for T, head_kind in [(T, kind) for T in tokens_list for kind in ("int5", "ne")]:
         x = synthetic.activations(900 + T, T, 2048, device=device)
         x4 = synthetic.activations(901 + T, T, 4096, device=device)
         y = torch.empty(T, 2048, device=device)
@@ -348,12 +355,15 @@ def decode_c3(ctx, stream, local, tokens_list=(1, 4), steps=20):
                 ctx.ne_matmul_group_device([ne_h[d][n] for n in group], [x.data_ptr()] * len(group),
                                            [outs[n].data_ptr() for n in group], T)
                 ctx.matmul_device(ne_h[d]["o"], x4.data_ptr(), T, outs["o"].data_ptr())
-            ctx.matmul_device(head_h, x.data_ptr(), T, logits.data_ptr())
+            if head_kind == "int5":
+                ctx.matmul_device(head_h, x.data_ptr(), T, logits.data_ptr())
+            else:
+                ctx.ne_matmul_cropped_device(ne_head_h, x.data_ptr(), T, logits.data_ptr(), C3_VOCAB)
 
         step(record_routes=True)
         torch.cuda.synchronize()
         touched = [int(torch.unique(routes[layer]).numel()) for layer in range(C3_LAYERS)]
-        step_bytes = head_bytes + T * 2048 * 4 * 2 * C3_LAYERS
+        step_bytes = (head_bytes if head_kind == "int5" else ne_head_bytes) + T * 2048 * 4 * 2 * C3_LAYERS
         for layer in range(C3_LAYERS):
             d = layer % C3_DISTINCT
             shared, per_expert = blocks[d]
@@ -382,11 +392,11 @@ def decode_c3(ctx, stream, local, tokens_list=(1, 4), steps=20):
         torch.cuda.synchronize()
         graph_ms = b.elapsed_time(e) / steps
         del graph
-        out[f"batch_{T}"] = {"bytes_per_step": step_bytes, "experts_touched_per_layer": sum(touched) / len(touched),
+        out[f"batch_{T}" + ("" if head_kind == "int5" else "_ne_head")] = {"bytes_per_step": step_bytes, "experts_touched_per_layer": sum(touched) / len(touched),
                              "eager_ms_per_step": eager_ms, "eager_gbs": step_bytes / eager_ms / 1e6,
                              "graph_ms_per_step": graph_ms, "graph_gbs": step_bytes / graph_ms / 1e6,
                              "graph_tokens_per_s": T / (graph_ms / 1e3)}
-    for h in moe_h + [head_h] + [m for hs in ne_h for m in hs.values()]:
+    for h in moe_h + [head_h, ne_head_h] + [m for hs in ne_h for m in hs.values()]:
         h.release()
     return out
 
@@ -983,7 +993,8 @@ def run_ours(args, world, rank, local):
         "ubatch_sweep": sweep,
         "decode_c3": {"layers": C3_LAYERS, "distinct_weight_sets": C3_DISTINCT,
                       "per_layer": "MoE block + NE q/k/v/gated-delta (one group call) + NE o",
-                      "head": f"int5_g64 {C3_VOCAB}x2048", **c3},
+                      "head": f"int5_g64 {C3_VOCAB}x2048; *_ne_head: NE codec padded to 2^18 rows, cropped",
+                      **c3},
         "stack_c5": c5,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4 + T * (E + 1) * 4,
                 "d2h_bytes_per_step": T * H * 4, "steps": e2e_steps},

@@ -74,6 +74,8 @@ SIGNATURES = {
     "adi_cuda_profile_stage": (C.c_int, [_ctx, C.c_uint32, C.c_char_p, C.c_size_t, C.POINTER(C.c_double),
                                          C.POINTER(C.c_uint64)]),
     "adi_cuda_profile_reset": (C.c_int, [_ctx]),
+    "adi_cuda_host_register": (C.c_int, [_ctx, C.c_void_p, C.c_size_t]),
+    "adi_cuda_host_unregister": (C.c_int, [_ctx, C.c_void_p]),
     "adi_cuda_upload_expert": (C.c_int, [_ctx, C.POINTER(ExpertMatrixDesc), C.POINTER(_h)]),
     "adi_cuda_upload_ne": (C.c_int, [_ctx, C.POINTER(NeMatrixDesc), C.POINTER(_h)]),
     "adi_cuda_upload_head": (C.c_int, [_ctx, C.POINTER(HeadChunkDesc), C.POINTER(_h)]),
@@ -245,6 +247,15 @@ class Context:
         return out
 
     # -- uploads -------------------------------------------------------------
+    def host_register(self, array: np.ndarray):
+        """Page-locks `array`'s memory (read-only) so uploads from it go
+        straight to the device: the model file's mapping, registered once."""
+        _check(self.lib.adi_cuda_host_register(self.ptr, C.c_void_p(array.ctypes.data), array.nbytes),
+               "host_register")
+
+    def host_unregister(self, array: np.ndarray):
+        _check(self.lib.adi_cuda_host_unregister(self.ptr, C.c_void_p(array.ctypes.data)), "host_unregister")
+
     @staticmethod
     def expert_desc(m, keep: list) -> ExpertMatrixDesc:
         arrays = [_arr(m.trellis, np.uint16), _arr(m.su, np.uint16), _arr(m.sv, np.uint16),

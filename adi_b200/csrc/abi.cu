@@ -97,12 +97,14 @@ std::unique_ptr<DeviceArray> upload_bytes(const void *host, size_t bytes, const 
     return a;
 }
 
-// Host arrays streamed into one device array through two pinned staging
-// buffers: host threads gather the next buffer's pieces while the previous
-// buffer's copy runs, so the upload of a block's packed weights costs about
-// the larger of the host gather and the PCIe copy instead of their sum (the
-// weights come from caller memory, e.g. the model file's mapping, which the
-// copy engine cannot read directly).
+// Host arrays streamed into one device array. Pieces that are adjacent in
+// host memory (the experts of one 32-expert chunk of the model file, which
+// stores them back to back) go as one copy. A run in page-locked memory --
+// the model file's mapping once registered (adi_cuda_host_register) -- is
+// copied straight to the device by the copy engine. Other runs go through
+// two pinned staging buffers: host threads gather the next buffer's pieces
+// while the previous buffer's copy runs, so they cost about the larger of
+// the host gather and the PCIe copy instead of their sum.
 class Stager {
   public:
     static constexpr size_t kBufferBytes = size_t(16) << 20;
@@ -121,10 +123,56 @@ class Stager {
         size_t bytes;
     };
 
-    // Copies the pieces, in order and back to back, to `dst` (device).
-    void gather(void *dst, const std::vector<Piece> &pieces) {
+    // Copies the pieces, in order and back to back, to `dst` (device), on
+    // the staging stream; finish() waits for every gather so far. The pieces
+    // must stay valid until then.
+    void gather(void *dst, const std::vector<Piece> &input) {
         setup();
         uint8_t *out = static_cast<uint8_t *>(dst);
+        // Adjacent pieces merged into runs.
+        std::vector<Piece> runs;
+        for (const Piece &pc : input) {
+            if (!runs.empty() && static_cast<const uint8_t *>(runs.back().src) + runs.back().bytes == pc.src)
+                runs.back().bytes += pc.bytes;
+            else
+                runs.push_back(pc);
+        }
+        // Runs in page-locked host memory straight to the device; the rest
+        // staged, in order.
+        std::vector<Piece> pieces;
+        auto flush_staged = [&] {
+            if (pieces.empty()) return;
+            out = staged(out, pieces);
+            pieces.clear();
+        };
+        for (const Piece &run : runs) {
+            if (page_locked(run.src)) {
+                flush_staged();
+                check(cudaMemcpyAsync(out, run.src, run.bytes, cudaMemcpyHostToDevice, stream_), "upload");
+                out += run.bytes;
+            } else {
+                pieces.push_back(run);
+            }
+        }
+        flush_staged();
+    }
+
+    void finish() {
+        if (stream_) check(cudaStreamSynchronize(stream_), "upload");
+    }
+
+  private:
+    static bool page_locked(const void *p) {
+        cudaPointerAttributes a{};
+        if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+            cudaGetLastError();  // clear: pageable memory may report an error on some drivers
+            return false;
+        }
+        return a.type == cudaMemoryTypeHost;
+    }
+
+    // The staged path for `pieces`, from `out` on; returns the end.
+    uint8_t *staged(uint8_t *out, const std::vector<Piece> &pieces) {
         size_t next = 0, offset_in_piece = 0;
         int b = 0;
         while (next < pieces.size()) {
@@ -149,10 +197,9 @@ class Stager {
             out += filled;
             b ^= 1;
         }
-        check(cudaStreamSynchronize(stream_), "upload");
+        return out;
     }
 
-  private:
     struct Copy {
         uint8_t *dst;
         const uint8_t *src;
@@ -1539,6 +1586,17 @@ uint64_t upload_moe(adi_cuda_context *c, const adi_moe_layer &layer, uint32_t fi
     d->router_rows_pad = (E + 1 + 127) / 128 * 128;
     const float *tlut = l->routed[3 * size_t(first)].tlut;
     const uint32_t tiles = (I / 16) * (H / 16);
+    // Copies in flight read the caller's arrays: wait for them on every way
+    // out of this function.
+    struct Drain {
+        Stager &stager;
+        ~Drain() {
+            try {
+                stager.finish();
+            } catch (...) {
+            }
+        }
+    } drain{c->stager};
     for (int p = 0; p < 3; ++p) {
         const uint32_t rows = p == 2 ? H : I, cols = p == 2 ? I : H;
         const size_t tw = size_t(tiles) * 24, gw = rows / 16 + cols / 16;
@@ -1566,6 +1624,7 @@ uint64_t upload_moe(adi_cuda_context *c, const adi_moe_layer &layer, uint32_t fi
         upload(d->sv[p], sv, size_t(rows) * 2 * count);
         upload(d->gamma[p], gamma, gw * 2 * count);
     }
+    c->stager.finish();
     d->codec = c->expert_codec(tlut);
     for (int p = 0; p < 3; ++p) {
         const uint32_t rows = p == 2 ? H : I, cols = p == 2 ? I : H;
@@ -1919,6 +1978,27 @@ int adi_cuda_profile_reset(adi_cuda_context *c) {
             c->profiler.ms[i] = 0;
             c->profiler.count[i] = 0;
         }
+    });
+}
+
+int adi_cuda_host_register(adi_cuda_context *c, const void *ptr, size_t bytes) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!ptr || bytes == 0) invalid("host range is empty");
+        // Read-only: the model file is mapped read-only, and nothing here
+        // writes to host memory through the registration.
+        check(cudaHostRegister(const_cast<void *>(ptr), bytes, cudaHostRegisterReadOnly | cudaHostRegisterPortable),
+              "cudaHostRegister");
+    });
+}
+
+int adi_cuda_host_unregister(adi_cuda_context *c, const void *ptr) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!ptr) invalid("host pointer is null");
+        check(cudaHostUnregister(const_cast<void *>(ptr)), "cudaHostUnregister");
     });
 }
 

@@ -193,3 +193,55 @@ def activations(seed: int, tokens: int, hidden: int, device: str = "cuda") -> to
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     return torch.randn(tokens, hidden, generator=g, device=device, dtype=torch.float32)
+
+
+class GgufLayout:
+    """A block's routed experts laid out as the model file stores them: per
+    32-expert chunk and projection, the tensors `trellis` [24, tiles, 32],
+    `su` [columns, 32], `sv` [rows, 32] and `wave_gamma` [tiles_r + tiles_c,
+    32] (GGUF order, first dimension contiguous: expert e's arrays back to
+    back), each 32-byte aligned in one host buffer -- the stand-in for the
+    file's mapping. `expert(e, projection)` returns views into that buffer
+    exactly as MachModel::expert slices them (src/model.cpp:483-531 of the
+    reference); everything else is the block's own."""
+
+    def __init__(self, block: MoeBlock):
+        self.block = block
+        E = block.experts
+        if E % 32:
+            raise ValueError("experts must come in chunks of 32")
+        sizes = []
+        for _ in range(E // 32):
+            for p in range(3):
+                rows, columns = block.shape(p)
+                tiles = (rows // 16) * (columns // 16)
+                for count in (24 * tiles, columns, rows, rows // 16 + columns // 16):
+                    sizes.append(32 * count * 2)
+        offsets, at = [], 0
+        for n in sizes:
+            offsets.append(at)
+            at += (n + 31) // 32 * 32
+        self.buffer = np.zeros(at, np.uint8)
+        self._views = {}
+        k = 0
+        for chunk in range(E // 32):
+            for p in range(3):
+                rows, columns = block.shape(p)
+                tiles = (rows // 16) * (columns // 16)
+                tensors = []
+                for src, count in ((block.trellis[p], 24 * tiles), (block.su[p], columns), (block.sv[p], rows),
+                                   (block.gamma[p], rows // 16 + columns // 16)):
+                    view = self.buffer[offsets[k]:offsets[k] + 32 * count * 2].view(np.uint16).reshape(32, count)
+                    view[:] = src[32 * chunk:32 * chunk + 32]
+                    tensors.append(view)
+                    k += 1
+                self._views[(chunk, p)] = tensors
+
+    def __getattr__(self, name):
+        return getattr(self.block, name)
+
+    def expert(self, e: int, projection: int) -> ExpertView:
+        rows, columns = self.block.shape(projection)
+        trellis, su, sv, gamma = self._views[(e // 32, projection)]
+        i = e % 32
+        return ExpertView(rows, columns, trellis[i], su[i], sv[i], gamma[i], self.block.expert_tlut)

@@ -139,6 +139,16 @@ ADI_CUDA_API int adi_cuda_profile_stage(adi_cuda_context *context, uint32_t inde
                                         double *milliseconds, uint64_t *count);
 ADI_CUDA_API int adi_cuda_profile_reset(adi_cuda_context *context);
 
+/* Page-locks a host range read-only for the uploads (no counterpart in the
+ * reference, which reads its weights in place from the model file's
+ * read-only mapping, src/model.cpp:52-63). Register that mapping once and
+ * every upload whose arrays lie in it is copied straight from it by the copy
+ * engine; the arrays of one 32-expert chunk, which the file stores back to
+ * back (src/model.cpp:483-531), go as one copy. Unregistered arrays are
+ * staged through pinned buffers. Unregister before unmapping. */
+ADI_CUDA_API int adi_cuda_host_register(adi_cuda_context *context, const void *ptr, size_t bytes);
+ADI_CUDA_API int adi_cuda_host_unregister(adi_cuda_context *context, const void *ptr);
+
 /* ---- weight upload (once per matrix, byte for byte) ------------------
  * Replace the mmap'd views of MachModel::expert / non_expert / head_chunk
  * (src/model.cpp:267-314, :367-438, :472-533) with device copies. */

@@ -124,9 +124,26 @@ SIGNATURES = {
     "adi_cuda_top_experts": (C.c_int, [_ctx, f32p, C.c_uint32, C.c_uint32, u32p, f32p]),
     "adi_cuda_hadamard": (C.c_int, [_ctx, f32p, C.c_uint32, C.c_uint32]),
     "adi_cuda_rms_norm": (C.c_int, [_ctx, f32p, u16p, C.c_uint32, C.c_uint32, C.c_float, C.c_float, f32p]),
+    "adi_cuda_full_attention_device": (C.c_int, [_ctx, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                 C.c_uint32, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p,
+                                                 C.c_uint32, C.c_uint32, C.c_void_p]),
+    "adi_cuda_gated_delta_device": (C.c_int, [_ctx, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                              C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p,
+                                              C.c_uint32, C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p]),
 }
 
 INVALID_ARGUMENT = 1
+
+
+class Sequence(C.Structure):
+    """adi_cuda_sequence: one sequence's rows and cache slot in a call."""
+    _fields_ = [("slot", C.c_uint32), ("first_token", C.c_uint32), ("count", C.c_uint32),
+                ("position", C.c_uint32)]
+
+
+def sequence_table(sequences):
+    rows = [tuple(q) + (0,) * (4 - len(tuple(q))) for q in sequences]
+    return (Sequence * len(rows))(*[Sequence(*r) for r in rows])
 # cudaStreamLegacy: the default stream with its implicit ordering against
 # every blocking stream (what torch launches on unless told otherwise).
 CUDA_STREAM_LEGACY = 0x1
@@ -402,6 +419,29 @@ class Context:
 
     def residual_add_device(self, hidden_ptr: int, add_ptr: int, count: int):
         _check(self.lib.adi_cuda_residual_add_device(self.ptr, hidden_ptr, add_ptr, count), "residual_add_device")
+
+    # -- attention halves of a decoder layer ---------------------------------
+    def full_attention_device(self, query_norm_ptr: int, key_norm_ptr: int, query_gate_ptr: int, key_ptr: int,
+                              value_ptr: int, tokens: int, sequences, key_cache_ptr: int, value_cache_ptr: int,
+                              slots: int, capacity: int, attended_ptr: int):
+        """Full attention after the q/k/v projections (device pointers;
+        `sequences` a list of (slot, first_token, count, position))."""
+        table = sequence_table(sequences)
+        _check(self.lib.adi_cuda_full_attention_device(
+            self.ptr, query_norm_ptr, key_norm_ptr, query_gate_ptr, key_ptr, value_ptr, tokens,
+            C.cast(table, C.c_void_p), len(table), key_cache_ptr, value_cache_ptr, slots, capacity, attended_ptr),
+            "full_attention_device")
+
+    def gated_delta_device(self, convolution_ptr: int, alpha_bias_ptr: int, a_log_ptr: int, norm_ptr: int,
+                           qkv_ptr: int, gate_ptr: int, alpha_ptr: int, beta_ptr: int, tokens: int, sequences,
+                           convolution_state_ptr: int, recurrent_ptr: int, slots: int, normalized_ptr: int):
+        """Gated DeltaNet after the qkv/z/a/b projections (device pointers;
+        `sequences` a list of (slot, first_token, count[, position]))."""
+        table = sequence_table(sequences)
+        _check(self.lib.adi_cuda_gated_delta_device(
+            self.ptr, convolution_ptr, alpha_bias_ptr, a_log_ptr, norm_ptr, qkv_ptr, gate_ptr, alpha_ptr, beta_ptr,
+            tokens, C.cast(table, C.c_void_p), len(table), convolution_state_ptr, recurrent_ptr, slots,
+            normalized_ptr), "gated_delta_device")
 
     # -- peer-memory exchange of expert parallelism ---------------------------
     def ep_peer_alloc(self, recv_rows: int, returned_rows: int, hidden: int) -> bytes:

@@ -18,7 +18,7 @@ PACKAGE = Path(__file__).resolve().parent
 ROOT = PACKAGE.parent
 CSRC = PACKAGE / "csrc"
 LIBRARY = PACKAGE / "libadi_cuda.so"
-SOURCES = ["kernels.cu", "tc_gemm.cu", "ep.cu", "decode.cu", "abi.cu"]
+SOURCES = ["kernels.cu", "tc_gemm.cu", "ep.cu", "decode.cu", "attention.cu", "abi.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -9,6 +9,7 @@
 #include "tc_gemm.cuh"
 #include "kernels.cuh"
 #include "ep.cuh"
+#include "attention.cuh"
 #include "decode.cuh"
 #include "pipeline.cuh"
 
@@ -341,12 +342,15 @@ enum Stage {
     kStageHead,
     kStageBf16,
     kStageNorm,
+    kStageAttention,
+    kStageGatedDelta,
     kStageCount
 };
 const char *const kStageNames[kStageCount] = {
     "router",           "top_experts",      "route",        "expert_prep",  "expert_gemm_gate_up",
     "swiglu",           "expert_gemm_down", "shared_expert", "combine",     "expert_matmul",
-    "ne_matmul",        "head_matmul",      "bf16_matmul",  "norm_residual",
+    "ne_matmul",        "head_matmul",      "bf16_matmul",  "norm_residual", "full_attention",
+    "gated_delta",
 };
 
 // CUDA-event brackets around stages, resolved lazily.
@@ -466,6 +470,10 @@ struct adi_cuda_context {
     // per stream the context launches on (main, side); zero between launches.
     uint32_t *decode_done = nullptr;
     uint32_t *error_host = nullptr;  // pinned copy of it, read after a synchronise
+    // Pinned ring the sequence tables of the attention entries pass through
+    // on their way to the device ring "seq_ring" (same offsets).
+    adi_cuda_sequence *seq_host = nullptr;
+    uint32_t seq_head = 0;
     // The layer and token count of the last expert-parallel dispatch, whose
     // routes and shared-expert sums the matching combine reads.
     uint64_t ep_layer = 0;
@@ -1857,6 +1865,58 @@ PeerExchange &connected_peers(adi_cuda_context *c, MoeDev &L) {
     return px;
 }
 
+// The sequence tables of the attention entries: checked on the host, then
+// copied through a pinned ring into the device ring at the same offset (so a
+// table stays put while the launches that read it are queued). Wrapping the
+// ring waits for the stream once, so the host never rewrites a slot whose
+// copy is still queued.
+constexpr uint32_t kSeqRing = 1u << 16;
+static_assert(sizeof(SeqDesc) == sizeof(adi_cuda_sequence), "sequence table layouts differ");
+
+struct SeqBounds {
+    uint32_t max_count = 0, max_end = 0;
+};
+
+const SeqDesc *stage_sequences(adi_cuda_context *c, const adi_cuda_sequence *seqs, uint32_t n, uint32_t tokens,
+                               uint32_t slots, uint32_t capacity, SeqBounds *bounds) {
+    if (!seqs || n == 0) invalid("sequence table is empty");
+    if (n > 65535) invalid("a call carries at most 65535 sequences");
+    std::vector<uint8_t> used(slots, 0);
+    std::vector<std::pair<uint32_t, uint32_t>> rows(n);
+    for (uint32_t i = 0; i < n; ++i) {
+        const adi_cuda_sequence &q = seqs[i];
+        if (q.slot >= slots) invalid("sequence slot out of range");
+        if (used[q.slot]) invalid("two sequences of one call share a slot");
+        used[q.slot] = 1;
+        if (q.count == 0 || q.first_token >= tokens || q.count > tokens - q.first_token)
+            invalid("sequence rows outside the token buffers");
+        if (capacity && (q.position >= capacity || q.count > capacity - q.position))
+            invalid("sequence exceeds the cache capacity");
+        rows[i] = {q.first_token, q.count};
+        bounds->max_count = std::max(bounds->max_count, q.count);
+        if (capacity) bounds->max_end = std::max(bounds->max_end, q.position + q.count);
+    }
+    std::sort(rows.begin(), rows.end());
+    for (uint32_t i = 1; i < n; ++i)
+        if (rows[i].first < rows[i - 1].first + rows[i - 1].second) invalid("sequences overlap in the token buffers");
+    SeqDesc *ring = c->buffer<SeqDesc>("seq_ring", kSeqRing);
+    if (!c->seq_host)
+        check(cudaHostAlloc(&c->seq_host, kSeqRing * sizeof(adi_cuda_sequence), cudaHostAllocDefault),
+              "cudaHostAlloc");
+    if (c->seq_head + n > kSeqRing) {
+        check(cudaStreamSynchronize(c->stream), "synchronize");
+        c->seq_head = 0;
+    }
+    adi_cuda_sequence *host = c->seq_host + c->seq_head;
+    std::memcpy(host, seqs, n * sizeof(adi_cuda_sequence));
+    SeqDesc *dev = ring + c->seq_head;
+    check(cudaMemcpyAsync(dev, host, n * sizeof(SeqDesc), cudaMemcpyHostToDevice, c->stream), "sequence table");
+    c->seq_head += n;
+    return dev;
+}
+
+bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
 }  // namespace
 
 extern "C" {
@@ -1894,7 +1954,9 @@ int adi_cuda_shutdown(adi_cuda_context *c) {
         cudaStream_t own = c->own_stream, side = c->side_stream;
         cudaEvent_t fork = c->fork_event, join = c->join_event;
         uint32_t *error_word = c->error_word, *error_host = c->error_host, *decode_done = c->decode_done;
+        adi_cuda_sequence *seq_host = c->seq_host;
         delete c;
+        if (seq_host) cudaFreeHost(seq_host);
         if (error_word) cudaFree(error_word);
         if (decode_done) cudaFree(decode_done);
         if (error_host) cudaFreeHost(error_host);
@@ -2401,6 +2463,101 @@ int adi_cuda_residual_add_device(adi_cuda_context *c, float *hidden, const float
         launch_residual_add(hidden, add, count, c->stream);
         c->stage_end();
         c->after_launch(count ? 1 : 0);
+    });
+}
+
+int adi_cuda_full_attention_device(adi_cuda_context *c, const uint16_t *query_norm_bf16,
+                                   const uint16_t *key_norm_bf16, float *query_gate, const float *key,
+                                   const float *value, uint32_t tokens, const adi_cuda_sequence *sequences,
+                                   uint32_t sequence_count, float *key_cache, float *value_cache, uint32_t slots,
+                                   uint32_t capacity, float *attended) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!query_norm_bf16 || !key_norm_bf16 || !query_gate || !key || !value || !key_cache || !value_cache ||
+            !attended)
+            invalid("full attention pointer is null");
+        if (tokens == 0 || slots == 0 || capacity == 0) invalid("full attention shape mismatch");
+        if (!aligned16(query_gate) || !aligned16(attended) || !aligned16(key_cache) || !aligned16(value_cache))
+            invalid("full attention buffers must be 16-byte aligned");
+        SeqBounds b;
+        const SeqDesc *seqs = stage_sequences(c, sequences, sequence_count, tokens, slots, capacity, &b);
+        cudaStream_t s = c->stream;
+        c->stage(kStageAttention);
+        AttnPrepParams pp{};
+        pp.query_gate = query_gate;
+        pp.key = key;
+        pp.value = value;
+        pp.query_norm = query_norm_bf16;
+        pp.key_norm = key_norm_bf16;
+        pp.seqs = seqs;
+        pp.key_cache = key_cache;
+        pp.value_cache = value_cache;
+        pp.capacity = capacity;
+        // model.cpp:604-611: theta_base^(2i / rotary dimensions), in float.
+        for (uint32_t i = 0; i < kAttnRopeHalf; ++i)
+            pp.divisors[i] = std::pow(10000000.0f, 2.0f * static_cast<float>(i) / 64.0f);
+        launch_attention_prep(pp, sequence_count, b.max_count, s);
+        uint32_t splits = 1, split_keys = 0, tpb = 1;
+        attention_splits(sequence_count, b.max_count, b.max_end, static_cast<uint32_t>(c->sms), &splits, &split_keys,
+                         &tpb);
+        AttnParams ap{};
+        ap.query_gate = query_gate;
+        ap.key_cache = key_cache;
+        ap.value_cache = value_cache;
+        ap.capacity = capacity;
+        ap.seqs = seqs;
+        ap.attended = attended;
+        ap.splits = splits;
+        ap.split_keys = split_keys;
+        ap.error = c->error_word;
+        if (splits > 1) {
+            const size_t rows = size_t(tokens) * kAttnQueryHeads * splits;
+            ap.partial = c->buffer<float>("attn_partial", rows * kAttnHeadSize);
+            ap.partial_ml = c->buffer<float>("attn_partial_ml", rows * 2);
+        }
+        launch_attention(ap, sequence_count, b.max_count, tpb, s);
+        c->stage_end();
+        c->after_launch(splits > 1 ? 3 : 2);
+    });
+}
+
+int adi_cuda_gated_delta_device(adi_cuda_context *c, const uint16_t *convolution_bf16, const uint16_t *alpha_bias_bf16,
+                                const uint16_t *a_log_bf16, const uint16_t *norm_bf16, const float *qkv,
+                                const float *gate, const float *alpha, const float *beta, uint32_t tokens,
+                                const adi_cuda_sequence *sequences, uint32_t sequence_count,
+                                float *convolution_state, float *recurrent_state, uint32_t slots,
+                                float *normalized) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!convolution_bf16 || !alpha_bias_bf16 || !a_log_bf16 || !norm_bf16 || !qkv || !gate || !alpha || !beta ||
+            !convolution_state || !recurrent_state || !normalized)
+            invalid("linear attention pointer is null");
+        if (tokens == 0 || slots == 0) invalid("linear attention shape mismatch");
+        if (!aligned16(qkv) || !aligned16(recurrent_state) || reinterpret_cast<uintptr_t>(convolution_bf16) % 8)
+            invalid("linear attention buffers must be 16-byte aligned (the convolution weights 8-byte)");
+        SeqBounds b;
+        const SeqDesc *seqs = stage_sequences(c, sequences, sequence_count, tokens, slots, 0, &b);
+        GdParams gp{};
+        gp.qkv = qkv;
+        gp.gate = gate;
+        gp.alpha = alpha;
+        gp.beta = beta;
+        gp.convolution = convolution_bf16;
+        gp.alpha_bias = alpha_bias_bf16;
+        gp.a_log = a_log_bf16;
+        gp.norm = norm_bf16;
+        gp.seqs = seqs;
+        gp.conv_state = convolution_state;
+        gp.recurrent = recurrent_state;
+        gp.convolved = c->buffer<float>("gd_convolved", size_t(tokens) * kGdChannels);
+        gp.raw = c->buffer<float>("gd_raw", size_t(tokens) * kGdValueSize);
+        gp.out = normalized;
+        c->stage(kStageGatedDelta);
+        launch_gated_delta(gp, sequence_count, b.max_count, c->stream);
+        c->stage_end();
+        c->after_launch(3);
     });
 }
 

@@ -1,0 +1,562 @@
+// Full attention and Gated DeltaNet linear attention of a decoder layer, after
+// their input projections. See attention.cuh for the layouts.
+//
+// Full attention runs as one pass per query tile over the cached keys: the
+// keys and values of one KV head stream through shared memory in tiles of 32
+// positions (two bulk copies per tile, double buffered), and each warp keeps
+// its own online-softmax state (running maximum, denominator, and an 8-head x
+// 256-dim accumulator in registers) for one query token. A decode token
+// spreads each tile over the block's 8 warps (4 keys each) and the warps'
+// states are merged at the end; a prefill tile gives each of 8 tokens its
+// own warp. Long histories with few query tiles are split over blocks and
+// merged by a second kernel. The arithmetic is fp32 throughout; the softmax
+// is evaluated in the online form of src/attention.cpp (rescaling by
+// exp(old max - new max)), with the order of the sums over keys and
+// dimensions differing from the reference's.
+//
+// Gated DeltaNet: the convolution is not recursive in its output, so every
+// (token, channel) is computed in parallel from the last three inputs of its
+// sequence (the convolution state before the first); the recurrence is
+// sequential over a sequence's tokens but independent over the 128 rows of
+// each value head's state, so a warp owns four rows (4 columns per lane,
+// state in registers for the whole run of tokens) and the block's 8 warps a
+// 32-row slice of one head.
+#include "attention.cuh"
+#include "codec.cuh"
+#include "pipeline.cuh"
+
+#include <algorithm>
+
+namespace adi_cuda {
+namespace {
+
+__device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
+
+__device__ __forceinline__ float warp_total(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Sum over a block of THREADS threads; every thread returns the same value
+// (the warps' partials are added in one fixed order by all of them).
+template <int THREADS>
+__device__ __forceinline__ float block_total(float v, float *red) {
+    v = warp_total(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < THREADS / 32; ++w) t += red[w];
+    return t;
+}
+
+__device__ __forceinline__ float sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+
+// ---------------------------------------------------------------------------
+// Full attention.
+
+// Per (token, head): RMS-normalise with (1 + w), rotate the first 64
+// dimensions, and write the query back or the key and value into the cache
+// (src/executor.cpp:25-73, 640-672).
+__global__ void __launch_bounds__(256) attention_prep_kernel(const __grid_constant__ AttnPrepParams p) {
+    __shared__ float red[8];
+    __shared__ float y[kAttnHeadSize];
+    const SeqDesc sq = p.seqs[blockIdx.y];
+    const uint32_t li = blockIdx.x;
+    if (li >= sq.count) return;
+    const size_t t = sq.first + li;
+    const uint32_t pos = sq.position + li, head = blockIdx.z, d = threadIdx.x;
+    const bool query = head < kAttnQueryHeads;
+    const uint32_t kh = head - kAttnQueryHeads;
+    float *qrow = p.query_gate + (t * kAttnQueryHeads + head) * kAttnQueryStride;
+    const float x = query ? qrow[d] : p.key[(t * kAttnKvHeads + kh) * kAttnHeadSize + d];
+    const float squares = block_total<256>(x * x, red);
+    const float scale = 1.0f / sqrtf(squares / static_cast<float>(kAttnHeadSize) + 1.0e-6f);
+    float v = x * (scale * (1.0f + bf16_bits_to_f32(query ? p.query_norm[d] : p.key_norm[d])));
+    y[d] = v;
+    __syncthreads();
+    if (d < 2 * kAttnRopeHalf) {
+        const uint32_t i = d & (kAttnRopeHalf - 1);
+        const float theta = static_cast<float>(pos) / p.divisors[i];
+        float sine, cosine;
+        sincosf(theta, &sine, &cosine);
+        const float first = y[i], second = y[i + kAttnRopeHalf];
+        v = d < kAttnRopeHalf ? __fsub_rn(__fmul_rn(first, cosine), __fmul_rn(second, sine))
+                              : __fadd_rn(__fmul_rn(second, cosine), __fmul_rn(first, sine));
+    }
+    if (query) {
+        qrow[d] = v;
+    } else {
+        const size_t row = ((size_t)(sq.slot * kAttnKvHeads + kh) * p.capacity + pos) * kAttnHeadSize;
+        p.key_cache[row + d] = v;
+        p.value_cache[row + d] = p.value[(t * kAttnKvHeads + kh) * kAttnHeadSize + d];
+    }
+}
+
+constexpr uint32_t kTileFloats = kAttnKeyTile * kAttnHeadSize;
+
+template <int QT>
+__host__ __device__ constexpr uint32_t keys_per_warp() {
+    return kAttnKeyTile / (8 / QT);
+}
+
+// Reduces 32 values v[0..31] over the warp's 32 lanes and leaves the total of
+// value `lane` in v[0] (each step keeps half of the values and adds the
+// partner's copies of them).
+__device__ __forceinline__ void transpose_reduce32(float (&v)[32], uint32_t lane) {
+#pragma unroll
+    for (int s = 16, n = 32; s >= 1; s >>= 1, n >>= 1) {
+        const bool upper = (lane & s) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float send = upper ? v[i] : v[i + n / 2];
+            const float keep = upper ? v[i + n / 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+        }
+    }
+}
+
+template <int QT>
+__global__ void __launch_bounds__(256, 1) attention_kernel(const __grid_constant__ AttnParams p) {
+    constexpr int KW = 8 / QT;                  // warps per query token
+    constexpr int KPW = keys_per_warp<QT>();    // keys of a tile per warp
+    constexpr int G = KPW / 4;                  // groups of four keys
+    extern __shared__ __align__(128) uint8_t smem[];
+    float *kbuf = reinterpret_cast<float *>(smem);  // [2][32][256]
+    float *vbuf = kbuf + 2 * kTileFloats;           // [2][32][256]
+    float *pbuf = vbuf + 2 * kTileFloats;           // [8 warps][KPW][8]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(pbuf + 8 * KPW * 8);
+
+    const SeqDesc sq = p.seqs[blockIdx.z];
+    const uint32_t tile0 = blockIdx.y * QT;
+    if (tile0 >= sq.count) return;
+    const uint32_t g = blockIdx.x / p.splits, sp = blockIdx.x % p.splits;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t tq = warp / KW, ks = warp % KW;
+    const uint32_t li = tile0 + tq;
+    const bool active = li < sq.count;
+    const uint32_t qpos = sq.position + li;
+    const uint32_t last = sq.position + min(sq.count, tile0 + QT) - 1;
+    const uint32_t kbegin = sp * p.split_keys;
+    const uint32_t kend = min(kbegin + p.split_keys, last + 1);
+    const uint32_t ntiles = kend > kbegin ? (kend - kbegin + kAttnKeyTile - 1) / kAttnKeyTile : 0;
+    const size_t head_base = (size_t)(sq.slot * kAttnKvHeads + g) * p.capacity * kAttnHeadSize;
+    const float *kc = p.key_cache + head_base;
+    const float *vc = p.value_cache + head_base;
+
+    // The token's 8 query heads of this group, dimensions 4*lane..+3 and
+    // 128+4*lane..+3 (an inactive warp loads a valid row and ignores it).
+    float q[8][8];
+    {
+        const size_t t = sq.first + (active ? li : tile0);
+        const float *qrow = p.query_gate + (t * kAttnQueryHeads + g * kAttnGroup) * kAttnQueryStride;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const float4 a = *reinterpret_cast<const float4 *>(qrow + r * kAttnQueryStride + 4 * lane);
+            const float4 b = *reinterpret_cast<const float4 *>(qrow + r * kAttnQueryStride + 128 + 4 * lane);
+            q[r][0] = a.x, q[r][1] = a.y, q[r][2] = a.z, q[r][3] = a.w;
+            q[r][4] = b.x, q[r][5] = b.y, q[r][6] = b.z, q[r][7] = b.w;
+        }
+    }
+    float acc[8][8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[r][j] = 0.0f;
+    // Lane-distributed softmax state: lane holds row (lane & 7).
+    float m_lane = neg_inf(), l_lane = 0.0f;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    uint32_t issued = 0;  // thread 0's count of tiles requested
+    auto issue = [&](uint32_t it) {
+        const uint32_t start = kbegin + it * kAttnKeyTile;
+        const uint32_t bytes = min(kAttnKeyTile, kend - start) * kAttnHeadSize * 4;
+        uint64_t *bar = &bars[it & 1];
+        mbar_arrive_expect_tx(bar, 2 * bytes);
+        bulk_load(kbuf + (it & 1) * kTileFloats, kc + (size_t)start * kAttnHeadSize, bytes, bar);
+        bulk_load(vbuf + (it & 1) * kTileFloats, vc + (size_t)start * kAttnHeadSize, bytes, bar);
+        issued = it + 1;
+    };
+    if (threadIdx.x == 0) {
+        if (ntiles > 0) issue(0);
+        if (ntiles > 1) issue(1);
+    }
+    bool ok = true;
+    uint32_t it = 0;
+    for (; it < ntiles; ++it) {
+        const uint32_t b = it & 1;
+        const bool waited = mbar_wait(&bars[b], (it >> 1) & 1, p.error);
+        if (__syncthreads_or(!waited)) {
+            ok = false;
+            break;
+        }
+        if (active) {
+            const float *K = kbuf + b * kTileFloats;
+            const float *V = vbuf + b * kTileFloats;
+            const uint32_t start = kbegin + it * kAttnKeyTile;
+            const uint32_t nk = min(kAttnKeyTile, kend - start);
+            float *pw = pbuf + warp * (KPW * 8);
+            float sc[G];
+#pragma unroll
+            for (int gi = 0; gi < G; ++gi) {
+                float part[32];
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const float *krow = K + (ks * KPW + gi * 4 + kk) * kAttnHeadSize;
+                    const float4 a = *reinterpret_cast<const float4 *>(krow + 4 * lane);
+                    const float4 c = *reinterpret_cast<const float4 *>(krow + 128 + 4 * lane);
+#pragma unroll
+                    for (int r = 0; r < 8; ++r) {
+                        float s = q[r][0] * a.x;
+                        s = fmaf(q[r][1], a.y, s);
+                        s = fmaf(q[r][2], a.z, s);
+                        s = fmaf(q[r][3], a.w, s);
+                        s = fmaf(q[r][4], c.x, s);
+                        s = fmaf(q[r][5], c.y, s);
+                        s = fmaf(q[r][6], c.z, s);
+                        s = fmaf(q[r][7], c.w, s);
+                        part[kk * 8 + r] = s;
+                    }
+                }
+                transpose_reduce32(part, lane);
+                // Lane holds key (gi*4 + lane/8) of this warp, row lane%8.
+                const uint32_t key = ks * KPW + gi * 4 + (lane >> 3);
+                const bool valid = key < nk && start + key <= qpos;
+                sc[gi] = valid ? part[0] * 0.0625f : neg_inf();  // 1/sqrt(256)
+            }
+            float tm = sc[0];
+#pragma unroll
+            for (int gi = 1; gi < G; ++gi) tm = fmaxf(tm, sc[gi]);
+            tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 8));
+            tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 16));
+            const float m_new = fmaxf(m_lane, tm);
+            float rowsum = 0.0f;
+#pragma unroll
+            for (int gi = 0; gi < G; ++gi) {
+                sc[gi] = sc[gi] == neg_inf() ? 0.0f : expf(sc[gi] - m_new);
+                rowsum += sc[gi];
+            }
+            rowsum += __shfl_xor_sync(0xffffffffu, rowsum, 8);
+            rowsum += __shfl_xor_sync(0xffffffffu, rowsum, 16);
+            const float alpha = m_new == neg_inf() ? 1.0f : expf(m_lane - m_new);
+            l_lane = l_lane * alpha + rowsum;
+            m_lane = m_new;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                const float ar = __shfl_sync(0xffffffffu, alpha, r);
+                if (ar != 1.0f) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[r][j] *= ar;
+                }
+            }
+#pragma unroll
+            for (int gi = 0; gi < G; ++gi) pw[(gi * 4 + (lane >> 3)) * 8 + (lane & 7)] = sc[gi];
+            __syncwarp();
+            const int kw_end = min(max((int)nk - (int)(ks * KPW), 0), KPW);
+            for (int kw = 0; kw < kw_end; ++kw) {
+                const float4 p0 = *reinterpret_cast<const float4 *>(pw + kw * 8);
+                const float4 p1 = *reinterpret_cast<const float4 *>(pw + kw * 8 + 4);
+                const float *vrow = V + (ks * KPW + kw) * kAttnHeadSize + lane;
+                float vv[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) vv[j] = vrow[32 * j];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    acc[0][j] = fmaf(p0.x, vv[j], acc[0][j]);
+                    acc[1][j] = fmaf(p0.y, vv[j], acc[1][j]);
+                    acc[2][j] = fmaf(p0.z, vv[j], acc[2][j]);
+                    acc[3][j] = fmaf(p0.w, vv[j], acc[3][j]);
+                    acc[4][j] = fmaf(p1.x, vv[j], acc[4][j]);
+                    acc[5][j] = fmaf(p1.y, vv[j], acc[5][j]);
+                    acc[6][j] = fmaf(p1.z, vv[j], acc[6][j]);
+                    acc[7][j] = fmaf(p1.w, vv[j], acc[7][j]);
+                }
+            }
+            __syncwarp();
+        }
+        __syncthreads();
+        if (threadIdx.x == 0 && it + 2 < ntiles) issue(it + 2);
+    }
+    if (!ok) {
+        // A copy did not land in time: let this block's own copies finish
+        // (bounded) before the block's shared memory goes away.
+        if (threadIdx.x == 0)
+            for (uint32_t j = it; j < issued; ++j) mbar_wait_own(&bars[j & 1], (j >> 1) & 1, p.error);
+        return;
+    }
+
+    // Merge the warps of each token (the tile buffers are free: the loop
+    // ended on a block barrier or never ran).
+    float *abuf = kbuf;  // [8 warps][8 rows][256]
+    float *mlbuf = vbuf;  // [8 warps][8 rows][2]
+    if (active) {
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) abuf[(warp * 8 + r) * kAttnHeadSize + lane + 32 * j] = acc[r][j];
+        if (lane < 8) {
+            mlbuf[(warp * 8 + lane) * 2] = m_lane;
+            mlbuf[(warp * 8 + lane) * 2 + 1] = l_lane;
+        }
+    }
+    __syncthreads();
+    if (!active) return;
+    const size_t t = sq.first + li;
+    for (uint32_t e = ks * 32 + lane; e < 8 * kAttnHeadSize; e += KW * 32) {
+        const uint32_t r = e / kAttnHeadSize, d = e % kAttnHeadSize;
+        float M = neg_inf();
+#pragma unroll
+        for (int w = 0; w < KW; ++w) M = fmaxf(M, mlbuf[((tq * KW + w) * 8 + r) * 2]);
+        float L = 0.0f, o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < KW; ++w) {
+            const float mw = mlbuf[((tq * KW + w) * 8 + r) * 2];
+            if (mw != neg_inf()) {
+                const float f = expf(mw - M);
+                L += mlbuf[((tq * KW + w) * 8 + r) * 2 + 1] * f;
+                o += abuf[((tq * KW + w) * 8 + r) * kAttnHeadSize + d] * f;
+            }
+        }
+        const size_t h = t * kAttnQueryHeads + g * kAttnGroup + r;
+        if (p.splits == 1) {
+            const float gate = p.query_gate[h * kAttnQueryStride + kAttnHeadSize + d];
+            p.attended[h * kAttnHeadSize + d] = o * (1.0f / L) * sigmoid(gate);
+        } else {
+            const size_t pi = h * p.splits + sp;
+            p.partial[pi * kAttnHeadSize + d] = o;
+            if (d == 0) {
+                p.partial_ml[pi * 2] = M;
+                p.partial_ml[pi * 2 + 1] = L;
+            }
+        }
+    }
+}
+
+// Merges the splits of each (token, query head) and applies the gate.
+__global__ void __launch_bounds__(256) attention_combine_kernel(const __grid_constant__ AttnParams p) {
+    const SeqDesc sq = p.seqs[blockIdx.y];
+    const uint32_t li = blockIdx.x;
+    if (li >= sq.count) return;
+    const size_t h = (size_t)(sq.first + li) * kAttnQueryHeads + blockIdx.z;
+    const uint32_t d = threadIdx.x;
+    const size_t base = h * p.splits;
+    float M = neg_inf();
+    for (uint32_t s = 0; s < p.splits; ++s) M = fmaxf(M, p.partial_ml[(base + s) * 2]);
+    float L = 0.0f, o = 0.0f;
+    for (uint32_t s = 0; s < p.splits; ++s) {
+        const float mw = p.partial_ml[(base + s) * 2];
+        if (mw != neg_inf()) {
+            const float f = expf(mw - M);
+            L += p.partial_ml[(base + s) * 2 + 1] * f;
+            o += p.partial[(base + s) * kAttnHeadSize + d] * f;
+        }
+    }
+    const float gate = p.query_gate[h * kAttnQueryStride + kAttnHeadSize + d];
+    p.attended[h * kAttnHeadSize + d] = o * (1.0f / L) * sigmoid(gate);
+}
+
+// ---------------------------------------------------------------------------
+// Gated DeltaNet.
+
+// Per (token, channel): the width-4 causal convolution over the sequence's
+// last three inputs and this one, silu, and for the query and key heads the
+// l2 normalisation (src/executor.cpp:1071-1113).
+__global__ void __launch_bounds__(128) gd_conv_kernel(const __grid_constant__ GdParams p) {
+    __shared__ float red[4];
+    const SeqDesc sq = p.seqs[blockIdx.y];
+    const uint32_t li = blockIdx.x;
+    if (li >= sq.count) return;
+    const uint32_t c = blockIdx.z * kGdHeadSize + threadIdx.x;
+    const size_t t = sq.first + li;
+    float h[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+        const int back = static_cast<int>(li) - 3 + j;
+        h[j] = back >= 0 ? p.qkv[(size_t)(sq.first + back) * kGdChannels + c]
+                         : p.conv_state[((size_t)sq.slot * kGdChannels + c) * 3 + (3 + back)];
+    }
+    const uint2 wb = *reinterpret_cast<const uint2 *>(p.convolution + (size_t)c * kGdConvWidth);
+    const float x = p.qkv[t * kGdChannels + c];
+    // Each product and sum rounded on its own, in the reference's order.
+    float v = 0.0f;
+    v = __fadd_rn(v, __fmul_rn(h[0], bf16_bits_to_f32(wb.x & 0xffffu)));
+    v = __fadd_rn(v, __fmul_rn(h[1], bf16_bits_to_f32(wb.x >> 16)));
+    v = __fadd_rn(v, __fmul_rn(h[2], bf16_bits_to_f32(wb.y & 0xffffu)));
+    v = __fadd_rn(v, __fmul_rn(x, bf16_bits_to_f32(wb.y >> 16)));
+    float y = silu(v);
+    if (blockIdx.z < 2 * kGdKeyHeads) {
+        const float squares = block_total<128>(y * y, red);
+        y *= 1.0f / sqrtf(squares + 1.0e-6f);
+    }
+    p.convolved[t * kGdChannels + c] = y;
+}
+
+// Reduces four values over the warp; lane ends with the total of value
+// lane/8.
+__device__ __forceinline__ float transpose_reduce4(float v0, float v1, float v2, float v3, uint32_t lane) {
+    const bool hi16 = (lane & 16) != 0;
+    float a = (hi16 ? v2 : v0) + __shfl_xor_sync(0xffffffffu, hi16 ? v0 : v2, 16);
+    float b = (hi16 ? v3 : v1) + __shfl_xor_sync(0xffffffffu, hi16 ? v1 : v3, 16);
+    const bool hi8 = (lane & 8) != 0;
+    float s = (hi8 ? b : a) + __shfl_xor_sync(0xffffffffu, hi8 ? a : b, 8);
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    return s;
+}
+
+// Per (32-row slice, value head, sequence): the recurrence over the
+// sequence's tokens (src/executor.cpp:123-144, src/simd.cpp:108-127). Block
+// x = 0 of each head also advances the convolution state of 256 channels.
+__global__ void __launch_bounds__(256) gd_recurrence_kernel(const __grid_constant__ GdParams p) {
+    const SeqDesc sq = p.seqs[blockIdx.z];
+    const uint32_t head = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t row0 = blockIdx.x * 32 + warp * 4;
+    const uint32_t kh = head / (kGdValueHeads / kGdKeyHeads);
+
+    if (blockIdx.x == 0) {
+        // The convolution kernel (the previous launch) has read the old state.
+        const uint32_t c = head * (kGdChannels / kGdValueHeads) + threadIdx.x;
+        float *st = p.conv_state + ((size_t)sq.slot * kGdChannels + c) * 3;
+        const float old[3] = {st[0], st[1], st[2]};
+        float next[3];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            const uint32_t n = sq.count + j;  // index in (old state ++ this call's inputs)
+            next[j] = n >= 3 ? p.qkv[(size_t)(sq.first + n - 3) * kGdChannels + c] : old[n < 3 ? n : 0];
+        }
+        st[0] = next[0], st[1] = next[1], st[2] = next[2];
+    }
+
+    float *S = p.recurrent + (((size_t)sq.slot * kGdValueHeads + head) * kGdHeadSize + row0) * kGdHeadSize + 4 * lane;
+    float4 s[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) s[i] = *reinterpret_cast<const float4 *>(S + i * kGdHeadSize);
+    const float alpha_bias = bf16_bits_to_f32(p.alpha_bias[head]);
+    const float A = expf(bf16_bits_to_f32(p.a_log[head]));
+    const float out_scale = 1.0f / sqrtf(static_cast<float>(kGdHeadSize));
+    const uint32_t my_row = lane >> 3;
+
+    struct Tok {
+        float4 q, k, v;
+        float a, b;
+    };
+    auto load = [&](uint32_t i) {
+        const size_t t = sq.first + i;
+        const float *cv = p.convolved + t * kGdChannels;
+        Tok x;
+        x.q = *reinterpret_cast<const float4 *>(cv + kh * kGdHeadSize + 4 * lane);
+        x.k = *reinterpret_cast<const float4 *>(cv + kGdQkSize + kh * kGdHeadSize + 4 * lane);
+        x.v = *reinterpret_cast<const float4 *>(cv + 2 * kGdQkSize + head * kGdHeadSize + row0);
+        x.a = p.alpha[t * kGdValueHeads + head];
+        x.b = p.beta[t * kGdValueHeads + head];
+        return x;
+    };
+    Tok cur = load(0);
+    for (uint32_t i = 0; i < sq.count; ++i) {
+        const Tok nxt = load(i + 1 < sq.count ? i + 1 : i);
+        const float beta = sigmoid(cur.b);
+        const float biased = cur.a + alpha_bias;
+        const float softplus = biased > 20.0f ? biased : log1pf(expf(biased));
+        const float decay = expf(-A * softplus);
+        float part[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            s[r].x *= decay, s[r].y *= decay, s[r].z *= decay, s[r].w *= decay;
+            part[r] = s[r].x * cur.k.x + s[r].y * cur.k.y + s[r].z * cur.k.z + s[r].w * cur.k.w;
+        }
+        const float prediction = transpose_reduce4(part[0], part[1], part[2], part[3], lane);
+        const float value = my_row == 0 ? cur.v.x : my_row == 1 ? cur.v.y : my_row == 2 ? cur.v.z : cur.v.w;
+        const float delta = (value - prediction) * beta;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const float dr = __shfl_sync(0xffffffffu, delta, 8 * r);
+            s[r].x = fmaf(cur.k.x, dr, s[r].x);
+            s[r].y = fmaf(cur.k.y, dr, s[r].y);
+            s[r].z = fmaf(cur.k.z, dr, s[r].z);
+            s[r].w = fmaf(cur.k.w, dr, s[r].w);
+            part[r] = s[r].x * cur.q.x + s[r].y * cur.q.y + s[r].z * cur.q.z + s[r].w * cur.q.w;
+        }
+        const float attended = transpose_reduce4(part[0], part[1], part[2], part[3], lane);
+        if ((lane & 7) == 0)
+            p.raw[(size_t)(sq.first + i) * kGdValueSize + head * kGdHeadSize + row0 + my_row] = attended * out_scale;
+        cur = nxt;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) *reinterpret_cast<float4 *>(S + i * kGdHeadSize) = s[i];
+}
+
+// Per (token, value head): RMS norm with weight offset 0, times silu of the
+// gate (src/executor.cpp:1158-1176).
+__global__ void __launch_bounds__(128) gd_norm_gate_kernel(const __grid_constant__ GdParams p) {
+    __shared__ float red[4];
+    const SeqDesc sq = p.seqs[blockIdx.y];
+    const uint32_t li = blockIdx.x;
+    if (li >= sq.count) return;
+    const size_t i = ((size_t)(sq.first + li) * kGdValueHeads + blockIdx.z) * kGdHeadSize + threadIdx.x;
+    const float x = p.raw[i];
+    const float squares = block_total<128>(x * x, red);
+    const float scale = 1.0f / sqrtf(squares / static_cast<float>(kGdHeadSize) + 1.0e-6f);
+    p.out[i] = x * scale * bf16_bits_to_f32(p.norm[threadIdx.x]) * silu(p.gate[i]);
+}
+
+}  // namespace
+
+size_t attention_smem_bytes(uint32_t tokens_per_block) {
+    const uint32_t kpw = kAttnKeyTile / (8 / tokens_per_block);
+    return 4ull * kTileFloats * 4 + 8ull * kpw * 8 * 4 + 2 * sizeof(uint64_t);
+}
+
+void attention_splits(uint32_t sequences, uint32_t max_count, uint32_t max_end, uint32_t sms, uint32_t *splits,
+                      uint32_t *split_keys, uint32_t *tokens_per_block) {
+    const uint32_t tpb = max_count <= 1 ? 1 : 8;
+    const uint64_t base = (uint64_t)sequences * kAttnKvHeads * ((max_count + tpb - 1) / tpb);
+    const uint32_t key_tiles = (max_end + kAttnKeyTile - 1) / kAttnKeyTile;
+    const uint64_t target = 2ull * sms;
+    uint32_t n = static_cast<uint32_t>(std::min<uint64_t>(key_tiles, std::max<uint64_t>(1, (target + base - 1) / base)));
+    const uint32_t tiles_per_split = (key_tiles + n - 1) / n;
+    *split_keys = tiles_per_split * kAttnKeyTile;
+    *splits = (max_end + *split_keys - 1) / *split_keys;
+    *tokens_per_block = tpb;
+}
+
+void launch_attention_prep(const AttnPrepParams &p, uint32_t sequences, uint32_t max_count, cudaStream_t s) {
+    attention_prep_kernel<<<dim3(max_count, sequences, kAttnQueryHeads + kAttnKvHeads), 256, 0, s>>>(p);
+}
+
+void launch_attention(const AttnParams &p, uint32_t sequences, uint32_t max_count, uint32_t tokens_per_block,
+                      cudaStream_t s) {
+    const dim3 grid(kAttnKvHeads * p.splits, (max_count + tokens_per_block - 1) / tokens_per_block, sequences);
+    const size_t smem = attention_smem_bytes(tokens_per_block);
+    if (tokens_per_block == 1) {
+        static bool configured = false;
+        if (!configured) {
+            cudaFuncSetAttribute(attention_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            configured = true;
+        }
+        attention_kernel<1><<<grid, 256, smem, s>>>(p);
+    } else {
+        static bool configured = false;
+        if (!configured) {
+            cudaFuncSetAttribute(attention_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            configured = true;
+        }
+        attention_kernel<8><<<grid, 256, smem, s>>>(p);
+    }
+    if (p.splits > 1) attention_combine_kernel<<<dim3(max_count, sequences, kAttnQueryHeads), 256, 0, s>>>(p);
+}
+
+void launch_gated_delta(const GdParams &p, uint32_t sequences, uint32_t max_count, cudaStream_t s) {
+    gd_conv_kernel<<<dim3(max_count, sequences, kGdChannels / kGdHeadSize), 128, 0, s>>>(p);
+    gd_recurrence_kernel<<<dim3(kGdHeadSize / 32, kGdValueHeads, sequences), 256, 0, s>>>(p);
+    gd_norm_gate_kernel<<<dim3(max_count, sequences, kGdValueHeads), 128, 0, s>>>(p);
+}
+
+}  // namespace adi_cuda

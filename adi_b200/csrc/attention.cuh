@@ -1,0 +1,87 @@
+// The attention halves of a decoder layer on the device, after their input
+// projections (which are NE matmuls and bf16 GEMVs, launched elsewhere):
+//
+// * full attention (src/executor.cpp:618-724 of the reference): per token
+//   the 16 query heads and 2 key heads are RMS-normalised with their bf16
+//   weights and rotated (RoPE over the first 64 of 256 dimensions), the keys
+//   and values are appended to the sequence's cache, and every token attends
+//   over its causal prefix (16 query heads over 2 KV heads), gated by
+//   sigmoid of the projection's gate half;
+// * Gated DeltaNet linear attention (src/executor.cpp:1038-1179): the causal
+//   width-4 convolution with silu over 8192 channels, l2 normalisation of the
+//   query and key heads, the gated delta recurrence over 32 value heads of
+//   128x128 state, then a per-head RMS norm times silu of the gate.
+//
+// Sequences: a call carries several sequences, each a run of consecutive
+// token rows in the token-major buffers (first, count), its state slot, and
+// (full attention) the position of its first token. A decode batch is many
+// sequences of one token; a prefill chunk is one sequence of many.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace adi_cuda {
+
+constexpr uint32_t kAttnQueryHeads = 16, kAttnKvHeads = 2, kAttnHeadSize = 256;
+constexpr uint32_t kAttnQueryStride = 2 * kAttnHeadSize;  // [query | gate] per head
+constexpr uint32_t kAttnGroup = kAttnQueryHeads / kAttnKvHeads;
+constexpr uint32_t kAttnRopeHalf = 32;  // rotary dimensions 64
+constexpr uint32_t kAttnKeyTile = 32;   // keys per shared-memory tile
+
+constexpr uint32_t kGdKeyHeads = 16, kGdValueHeads = 32, kGdHeadSize = 128;
+constexpr uint32_t kGdQkSize = kGdKeyHeads * kGdHeadSize;
+constexpr uint32_t kGdValueSize = kGdValueHeads * kGdHeadSize;
+constexpr uint32_t kGdChannels = 2 * kGdQkSize + kGdValueSize;
+constexpr uint32_t kGdConvWidth = 4;
+
+struct SeqDesc {
+    uint32_t slot, first, count, position;
+};
+
+struct AttnPrepParams {
+    float *query_gate;                  // [tokens][16][512]; queries rewritten in place
+    const float *key, *value;           // [tokens][2][256]
+    const uint16_t *query_norm, *key_norm;  // bf16 [256]
+    const SeqDesc *seqs;
+    float *key_cache, *value_cache;     // [slots][2][capacity][256]
+    uint32_t capacity;
+    float divisors[kAttnRopeHalf];      // theta_base^(2i/64)
+};
+
+struct AttnParams {
+    const float *query_gate;
+    const float *key_cache, *value_cache;
+    uint32_t capacity;
+    const SeqDesc *seqs;
+    float *attended;    // [tokens][16][256], written when splits == 1
+    float *partial;     // [tokens][16][splits][256] unnormalised sums, splits > 1
+    float *partial_ml;  // [tokens][16][splits][2] running maximum and denominator
+    uint32_t splits, split_keys;
+    uint32_t *error;
+};
+
+struct GdParams {
+    const float *qkv, *gate, *alpha, *beta;  // [tokens][8192], [tokens][4096], [tokens][32] x2
+    const uint16_t *convolution, *alpha_bias, *a_log, *norm;  // bf16
+    const SeqDesc *seqs;
+    float *conv_state;  // [slots][8192][3]
+    float *recurrent;   // [slots][32][128][128]
+    float *convolved;   // scratch [tokens][8192]
+    float *raw;         // scratch [tokens][4096]
+    float *out;         // [tokens][4096]
+};
+
+// Shared memory of the attention kernel.
+size_t attention_smem_bytes(uint32_t tokens_per_block);
+
+// Splits of the key range that keep about two waves of blocks in flight.
+void attention_splits(uint32_t sequences, uint32_t max_count, uint32_t max_end, uint32_t sms,
+                      uint32_t *splits, uint32_t *split_keys, uint32_t *tokens_per_block);
+
+void launch_attention_prep(const AttnPrepParams &p, uint32_t sequences, uint32_t max_count, cudaStream_t s);
+void launch_attention(const AttnParams &p, uint32_t sequences, uint32_t max_count, uint32_t tokens_per_block,
+                      cudaStream_t s);
+void launch_gated_delta(const GdParams &p, uint32_t sequences, uint32_t max_count, cudaStream_t s);
+
+}  // namespace adi_cuda

@@ -245,3 +245,61 @@ class GgufLayout:
         trellis, su, sv, gamma = self._views[(e // 32, projection)]
         i = e % 32
         return ExpertView(rows, columns, trellis[i], su[i], sv[i], gamma[i], self.block.expert_tlut)
+
+
+def _bf16_bits(values: np.ndarray) -> np.ndarray:
+    """float32 -> bf16 bits, round to nearest even."""
+    u = np.ascontiguousarray(values, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+@dataclass
+class FullAttentionWeights:
+    """The bf16 per-head norms of a full-attention layer (q_norm, k_norm;
+    applied as x * scale * (1 + w), src/executor.cpp:25-42)."""
+    query_norm: np.ndarray
+    key_norm: np.ndarray
+
+
+@dataclass
+class LinearAttentionWeights:
+    """The bf16 small weights of a Gated DeltaNet layer: the causal
+    convolution [8192][4], the per-value-head alpha bias and A_log, and the
+    per-head output norm [128] (src/executor.cpp:428-556)."""
+    convolution: np.ndarray
+    alpha_bias: np.ndarray
+    a_log: np.ndarray
+    norm: np.ndarray
+
+
+def full_attention_weights(seed: int) -> FullAttentionWeights:
+    rng = np.random.default_rng(seed)
+    return FullAttentionWeights(_bf16_bits(rng.normal(0, 0.1, 256)), _bf16_bits(rng.normal(0, 0.1, 256)))
+
+
+def linear_attention_weights(seed: int) -> LinearAttentionWeights:
+    """Convolution N(0, 0.3); alpha bias N(0, 1); A_log = log U(1, 16) (so the
+    per-token decay exp(-A softplus(alpha)) spans fast and slow heads); norm
+    1 + N(0, 0.1)."""
+    rng = np.random.default_rng(seed)
+    return LinearAttentionWeights(
+        _bf16_bits(rng.normal(0, 0.3, 8192 * 4)),
+        _bf16_bits(rng.normal(0, 1.0, 32)),
+        _bf16_bits(np.log(rng.uniform(1.0, 16.0, 32))),
+        _bf16_bits(1.0 + rng.normal(0, 0.1, 128)))
+
+
+def full_attention_projections(seed: int, tokens: int):
+    """query_gate [T][16*512], key and value [T][2*256], N(0, 1): the outputs
+    of the q, k and v projections."""
+    rng = np.random.default_rng(seed)
+    f = lambda n: rng.standard_normal((tokens, n)).astype(np.float32)  # noqa: E731
+    return f(16 * 512), f(512), f(512)
+
+
+def linear_attention_projections(seed: int, tokens: int):
+    """qkv [T][8192], gate [T][4096], alpha and beta [T][32], N(0, 1): the
+    outputs of the qkv, z, a and b projections."""
+    rng = np.random.default_rng(seed)
+    f = lambda n: rng.standard_normal((tokens, n)).astype(np.float32)  # noqa: E731
+    return f(8192), f(4096), f(32), f(32)

@@ -453,6 +453,72 @@ ADI_CUDA_API int adi_cuda_rms_norm_device(adi_cuda_context *context, const float
 ADI_CUDA_API int adi_cuda_residual_add_device(adi_cuda_context *context, float *hidden,
                                  const float *add, size_t count);
 
+/* ---- Attention halves of a decoder layer --------------------------------
+ *
+ * The steps of a decoder layer between its attention input projections (NE
+ * matmuls and bf16 GEMVs: adi_cuda_ne_matmul_group_device and friends) and
+ * its output projection, for the configured geometry: full attention with 16
+ * query heads over 2 KV heads of 256 (queries interleaved with their gate:
+ * [16][512] per token), and Gated DeltaNet with 16 key heads, 32 value heads
+ * of 128 and 8192 convolution channels.
+ *
+ * A call carries one or more sequences. Each is a run of `count` consecutive
+ * token rows starting at `first_token` in the token-major buffers, owns the
+ * cache / state `slot`, and (full attention) its first token sits at
+ * `position` (the number of tokens already in the slot's cache). A decode
+ * batch is many sequences of one token; a prefill chunk one sequence of many.
+ * The table is a HOST array; it is validated (slots distinct and in range,
+ * rows within `tokens`, positions within the cache) and copied to the device
+ * with the call. */
+typedef struct adi_cuda_sequence {
+    uint32_t slot;
+    uint32_t first_token;
+    uint32_t count;
+    uint32_t position;
+} adi_cuda_sequence;
+
+/* Full attention after the q/k/v projections, executor.cpp:618-724
+ * (full_attention_forward_batch): per token each query head and key head is
+ * RMS-normalised with its bf16 weight as x*scale*(1+w) (executor.cpp:25-42)
+ * and RoPE-rotated over its first 64 dimensions with theta = position /
+ * 1e7^(2i/64) (model.cpp:604-611, executor.cpp:44-73); keys and values are
+ * appended to the slot's cache at their positions; each token attends over
+ * positions 0..its own (grouped_query_online_attention, attention.cpp), and
+ * the result is multiplied by sigmoid of the gate half.
+ *   query_gate  [tokens][16][512] (device; the queries are rewritten in place
+ *               normalised and rotated, as the reference does)
+ *   key, value  [tokens][2][256] (device)
+ *   query_norm_bf16, key_norm_bf16  [256] (device)
+ *   key_cache, value_cache  [slots][2][capacity][256] fp32 (device)
+ *   attended    [tokens][16][256] (device): the input of the o projection.
+ * Asynchronous on the context stream. */
+ADI_CUDA_API int adi_cuda_full_attention_device(
+    adi_cuda_context *context, const uint16_t *query_norm_bf16, const uint16_t *key_norm_bf16,
+    float *query_gate, const float *key, const float *value, uint32_t tokens,
+    const adi_cuda_sequence *sequences, uint32_t sequence_count, float *key_cache,
+    float *value_cache, uint32_t slots, uint32_t capacity, float *attended);
+
+/* Gated DeltaNet after the qkv, z, a and b projections, executor.cpp:1038-1179
+ * (linear_attention_prefill_chunk) and :808-948 (the decode batch): the causal
+ * width-4 convolution with silu over 8192 channels, l2 normalisation of the
+ * 16 query and 16 key heads, the gated delta recurrence of the 32 value heads
+ * (decay exp(-exp(A_log) softplus(alpha + alpha_bias)), beta sigmoid(b),
+ * executor.cpp:123-144 and simd.cpp:108-127), then per value head an RMS norm
+ * (weight offset 0) times silu of the gate.
+ *   qkv [tokens][8192], gate [tokens][4096], alpha, beta [tokens][32] (device)
+ *   convolution_bf16 [8192][4], alpha_bias_bf16, a_log_bf16 [32], norm_bf16
+ *               [128] (device)
+ *   convolution_state [slots][8192][3], recurrent_state [slots][32][128][128]
+ *               fp32 (device), advanced in place
+ *   normalized  [tokens][4096] (device): the input of the output projection.
+ * Asynchronous on the context stream. */
+ADI_CUDA_API int adi_cuda_gated_delta_device(
+    adi_cuda_context *context, const uint16_t *convolution_bf16, const uint16_t *alpha_bias_bf16,
+    const uint16_t *a_log_bf16, const uint16_t *norm_bf16, const float *qkv, const float *gate,
+    const float *alpha, const float *beta, uint32_t tokens, const adi_cuda_sequence *sequences,
+    uint32_t sequence_count, float *convolution_state, float *recurrent_state, uint32_t slots,
+    float *normalized);
+
 #ifdef __cplusplus
 }
 #endif

@@ -273,6 +273,52 @@ class Reference(_Checker):
                     raise ValueError(self.last_error())
         return out, experts, weights
 
+    def full_attention(self, query_gate, key, value, position, query_norm, key_norm, keys, values):
+        """One sequence's full-attention step (src/executor.cpp:618-724) over
+        T new tokens at positions position..position+T-1. query_gate
+        [T][8192], key/value [T][512]; keys/values [>= position][512] hold
+        the history. Returns (attended [T][4096], the normalised and rotated
+        query_gate, keys and values [position+T][512])."""
+        qg = np.array(query_gate, np.float32, copy=True).reshape(-1, 16 * 512)
+        T = qg.shape[0]
+        k = np.ascontiguousarray(key, np.float32).reshape(T, 512)
+        v = np.ascontiguousarray(value, np.float32).reshape(T, 512)
+        hk = np.zeros((position + T, 512), np.float32)
+        hv = np.zeros((position + T, 512), np.float32)
+        hk[:position] = np.asarray(keys, np.float32).reshape(-1, 512)[:position]
+        hv[:position] = np.asarray(values, np.float32).reshape(-1, 512)[:position]
+        out = np.zeros((T, 16 * 256), np.float32)
+        status = self.lib.ref_full_attention(
+            ptr(qg, f32p), ptr(k, f32p), ptr(v, f32p), C.c_uint32(T), C.c_uint32(position),
+            ptr(_c(query_norm, np.uint16), u16p), ptr(_c(key_norm, np.uint16), u16p),
+            ptr(hk, f32p), ptr(hv, f32p), ptr(out, f32p))
+        if status:
+            raise ValueError(self.last_error())
+        return out, qg, hk, hv
+
+    def linear_attention(self, qkv, gate, alpha, beta, convolution, alpha_bias, a_log, norm,
+                         convolution_state, recurrent):
+        """One sequence's Gated DeltaNet step over T tokens after its
+        projections (src/executor.cpp:1038-1179). Returns (normalized
+        [T][4096], convolution_state [8192*3], recurrent [32*128*128]) with
+        the states advanced (the inputs are not modified)."""
+        q = np.ascontiguousarray(qkv, np.float32).reshape(-1, 8192)
+        T = q.shape[0]
+        g = np.ascontiguousarray(gate, np.float32).reshape(T, 4096)
+        a = np.ascontiguousarray(alpha, np.float32).reshape(T, 32)
+        b = np.ascontiguousarray(beta, np.float32).reshape(T, 32)
+        conv_state = np.array(convolution_state, np.float32, copy=True).reshape(-1)
+        rec = np.array(recurrent, np.float32, copy=True).reshape(-1)
+        out = np.zeros((T, 4096), np.float32)
+        status = self.lib.ref_linear_attention(
+            ptr(q, f32p), ptr(g, f32p), ptr(a, f32p), ptr(b, f32p), C.c_uint32(T),
+            ptr(_c(convolution, np.uint16), u16p), ptr(_c(alpha_bias, np.uint16), u16p),
+            ptr(_c(a_log, np.uint16), u16p), ptr(_c(norm, np.uint16), u16p),
+            ptr(conv_state, f32p), ptr(rec, f32p), ptr(out, f32p))
+        if status:
+            raise ValueError(self.last_error())
+        return out, conv_state, rec
+
 
 def reference_available() -> bool:
     return REF_SO.exists()

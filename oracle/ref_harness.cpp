@@ -14,6 +14,7 @@
 #include "adi/backend.hpp"
 #include "adi/executor.hpp"
 #include "adi/kernels.hpp"
+#include "attention.hpp"
 #include "codec_cache.hpp"
 #include "expert_trellis.hpp"
 #include "ne_trellis.hpp"
@@ -21,6 +22,7 @@
 #include "simd.hpp"
 
 #include <algorithm>
+#include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <exception>
@@ -572,6 +574,177 @@ void moe_forward_batch_impl(const ref_moe_layer *layer, const float *inputs,
 }
 }  // namespace
 
+// The attention halves of a decoder layer, after their input projections.
+// The reference's own functions (full_attention_forward_batch,
+// linear_attention_prefill_chunk) need a MachModel; these restate their glue
+// over the reference's callable kernels: grouped_query_online_attention
+// (src/attention.cpp), gated_delta_update (src/simd.cpp), rms_norm,
+// l2_normalize, silu and sigmoid (src/kernels.cpp).
+namespace {
+
+constexpr std::uint32_t query_heads = 16, kv_heads = 2, attn_head = 256;
+constexpr std::uint32_t query_stride = 2 * attn_head;
+constexpr std::uint32_t key_heads = 16, value_heads = 32, gd_head = 128;
+constexpr std::uint32_t qk_size = key_heads * gd_head;
+constexpr std::uint32_t value_size = value_heads * gd_head;
+constexpr std::uint32_t channels = 2 * qk_size + value_size;
+constexpr float epsilon = 1.0e-6F;
+
+// src/executor.cpp:25-42 (normalize_head).
+void normalize_head(float *values, const std::uint16_t *weights, std::uint32_t n) {
+    float squares = 0.0F;
+    for (std::uint32_t i = 0; i < n; ++i) {
+        squares += values[i] * values[i];
+    }
+    const float scale = 1.0F / std::sqrt(squares / static_cast<float>(n) + epsilon);
+    for (std::uint32_t i = 0; i < n; ++i) {
+        values[i] *= scale * (1.0F + adi::bf16_to_f32(weights[i]));
+    }
+}
+
+// src/model.cpp:604-611 (divisors) with src/executor.cpp:44-58
+// (prepare_rope) and :60-73 (apply_rope).
+void apply_rope(float *values, std::uint32_t position) {
+    constexpr float theta_base = 10000000.0F;
+    constexpr float rotary_dimensions = 64.0F;
+    for (std::uint32_t i = 0; i < 32; ++i) {
+        const float divisor = std::pow(theta_base, 2.0F * static_cast<float>(i) / rotary_dimensions);
+        const float theta = static_cast<float>(position) / divisor;
+        const float cosine = std::cos(theta);
+        const float sine = std::sin(theta);
+        const float first = values[i];
+        const float second = values[i + 32];
+        values[i] = first * cosine - second * sine;
+        values[i + 32] = second * cosine + first * sine;
+    }
+}
+
+}  // namespace
+
 extern "C" {
+
+// One sequence's full-attention step over `tokens` new tokens at positions
+// position .. position+tokens-1 (src/executor.cpp:618-724): per token the
+// query and key heads are normalised and rotated, the keys and values are
+// appended to the history, and each token attends over its causal prefix,
+// gated by sigmoid of the gate half. query_gate [tokens][16][512] is updated
+// in place; keys/values [position+tokens][2][256] hold the history on entry
+// (first `position` rows) and gain the new rows; attended is
+// [tokens][16][256].
+int ref_full_attention(float *query_gate, const float *key, const float *value,
+                       std::uint32_t tokens, std::uint32_t position,
+                       const std::uint16_t *query_norm, const std::uint16_t *key_norm,
+                       float *keys, float *values, float *attended) {
+    return guarded([&] {
+        if (!query_gate || !key || !value || !keys || !values || !attended || tokens == 0) {
+            throw std::invalid_argument("full attention shape mismatch");
+        }
+        const std::size_t row = static_cast<std::size_t>(kv_heads) * attn_head;
+        for (std::uint32_t t = 0; t < tokens; ++t) {
+            float *q = query_gate + static_cast<std::size_t>(t) * query_heads * query_stride;
+            for (std::uint32_t h = 0; h < query_heads; ++h) {
+                normalize_head(q + h * query_stride, query_norm, attn_head);
+                apply_rope(q + h * query_stride, position + t);
+            }
+            float *k = keys + (static_cast<std::size_t>(position) + t) * row;
+            std::memcpy(k, key + t * row, row * sizeof(float));
+            std::memcpy(values + (static_cast<std::size_t>(position) + t) * row, value + t * row,
+                        row * sizeof(float));
+            for (std::uint32_t h = 0; h < kv_heads; ++h) {
+                normalize_head(k + h * attn_head, key_norm, attn_head);
+                apply_rope(k + h * attn_head, position + t);
+            }
+        }
+        for (std::uint32_t t = 0; t < tokens; ++t) {
+            const std::size_t history = (static_cast<std::size_t>(position) + t + 1) * row;
+            const float *q = query_gate + static_cast<std::size_t>(t) * query_heads * query_stride;
+            float *out = attended + static_cast<std::size_t>(t) * query_heads * attn_head;
+            adi::detail::grouped_query_online_attention(
+                std::span<const float>(q, query_heads * query_stride),
+                std::span<const float>(keys, history), std::span<const float>(values, history),
+                query_heads, kv_heads, attn_head, query_stride, tokens == 1,
+                std::span<float>(out, query_heads * attn_head));
+            for (std::uint32_t h = 0; h < query_heads; ++h) {
+                for (std::uint32_t i = 0; i < attn_head; ++i) {
+                    out[h * attn_head + i] *= adi::sigmoid(q[h * query_stride + attn_head + i]);
+                }
+            }
+        }
+    });
+}
+
+// One sequence's linear-attention (Gated DeltaNet) step over `tokens` tokens
+// after the qkv, gate, alpha and beta projections: phases B-D of
+// linear_attention_prefill_chunk (src/executor.cpp:1038-1179). The
+// convolution state [8192][3] and recurrent state [32][128][128] are updated
+// in place; normalized [tokens][4096] is the input of the output projection.
+int ref_linear_attention(const float *qkv, const float *gate, const float *alpha,
+                         const float *beta, std::uint32_t tokens,
+                         const std::uint16_t *convolution, const std::uint16_t *alpha_bias,
+                         const std::uint16_t *a_log, const std::uint16_t *norm,
+                         float *convolution_state, float *recurrent, float *normalized) {
+    return guarded([&] {
+        if (!qkv || !gate || !alpha || !beta || !convolution || !alpha_bias || !a_log || !norm ||
+            !convolution_state || !recurrent || !normalized || tokens == 0) {
+            throw std::invalid_argument("linear attention shape mismatch");
+        }
+        std::vector<float> convolved(static_cast<std::size_t>(tokens) * channels);
+        for (std::uint32_t t = 0; t < tokens; ++t) {
+            for (std::uint32_t c = 0; c < channels; ++c) {
+                float *history = convolution_state + static_cast<std::size_t>(c) * 3;
+                const std::uint16_t *w = convolution + static_cast<std::size_t>(c) * 4;
+                const float x = qkv[static_cast<std::size_t>(t) * channels + c];
+                float v = 0.0F;
+                for (std::uint32_t i = 0; i < 3; ++i) {
+                    v += history[i] * adi::bf16_to_f32(w[i]);
+                }
+                v += x * adi::bf16_to_f32(w[3]);
+                convolved[static_cast<std::size_t>(t) * channels + c] = adi::silu(v);
+                history[0] = history[1];
+                history[1] = history[2];
+                history[2] = x;
+            }
+            for (std::uint32_t h = 0; h < 2 * key_heads; ++h) {
+                adi::l2_normalize(
+                    std::span<float>(convolved.data() + static_cast<std::size_t>(t) * channels + h * gd_head,
+                                     gd_head),
+                    epsilon);
+            }
+        }
+        std::vector<float> raw(static_cast<std::size_t>(tokens) * value_size);
+        const float output_scale = 1.0F / std::sqrt(static_cast<float>(gd_head));
+        for (std::uint32_t head = 0; head < value_heads; ++head) {
+            const std::uint32_t key_head = adi::gated_delta_key_head(head, value_heads, key_heads);
+            for (std::uint32_t t = 0; t < tokens; ++t) {
+                const float *cv = convolved.data() + static_cast<std::size_t>(t) * channels;
+                const std::span<const float> q(cv + key_head * gd_head, gd_head);
+                const std::span<const float> k(cv + qk_size + key_head * gd_head, gd_head);
+                const float *v = cv + 2 * qk_size + head * gd_head;
+                const float beta_value = adi::sigmoid(beta[t * value_heads + head]);
+                const float biased = alpha[t * value_heads + head] + adi::bf16_to_f32(alpha_bias[head]);
+                const float softplus = biased > 20.0F ? biased : std::log1p(std::exp(biased));
+                const float decay = std::exp(-std::exp(adi::bf16_to_f32(a_log[head])) * softplus);
+                for (std::uint32_t r = 0; r < gd_head; ++r) {
+                    std::span<float> state(
+                        recurrent + (static_cast<std::size_t>(head) * gd_head + r) * gd_head, gd_head);
+                    raw[static_cast<std::size_t>(t) * value_size + head * gd_head + r] =
+                        adi::detail::gated_delta_update(state, q, k, v[r], beta_value, decay) *
+                        output_scale;
+                }
+            }
+        }
+        for (std::uint32_t t = 0; t < tokens; ++t) {
+            for (std::uint32_t head = 0; head < value_heads; ++head) {
+                const std::size_t offset = static_cast<std::size_t>(t) * value_size + head * gd_head;
+                adi::rms_norm(std::span<const float>(raw.data() + offset, gd_head),
+                              std::span<const std::uint16_t>(norm, gd_head), 0.0F, epsilon,
+                              std::span<float>(normalized + offset, gd_head));
+                for (std::uint32_t i = 0; i < gd_head; ++i) {
+                    normalized[offset + i] *= adi::silu(gate[offset + i]);
+                }
+            }
+        }
+    });
+}
 
 } // extern "C"

@@ -127,6 +127,23 @@ SIGNATURES = {
     "adi_cuda_full_attention_device": (C.c_int, [_ctx, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                                  C.c_uint32, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p,
                                                  C.c_uint32, C.c_uint32, C.c_void_p]),
+    "adi_cuda_decoder_forward_device": (C.c_int, [_ctx, C.c_void_p, C.c_uint32, C.c_void_p, C.c_uint32, C.c_void_p,
+                                                  C.c_uint32, C.c_void_p, _h, C.c_uint32, C.c_void_p]),
+    "adi_cuda_decoder_step_device": (C.c_int, [_ctx, C.c_void_p, C.c_uint32, C.c_void_p, C.c_uint32, C.c_uint32,
+                                               C.c_void_p, C.c_uint32, C.c_void_p, _h, C.c_uint32, C.c_void_p]),
+    "adi_cuda_upload_embedding": (C.c_int, [_ctx, C.c_void_p, C.POINTER(_h)]),
+    "adi_cuda_get_stream": (C.c_int, [_ctx, C.POINTER(C.c_void_p)]),
+    "adi_cuda_sample_tokens": (C.c_int, [f32p, C.c_uint32, C.c_float, C.c_float, C.c_uint64, C.c_uint32, u32p]),
+    "adi_cuda_batcher_create": (C.c_int, [_ctx, C.c_void_p, C.POINTER(C.c_void_p)]),
+    "adi_cuda_batcher_destroy": (C.c_int, [C.c_void_p]),
+    "adi_cuda_batcher_submit": (C.c_int, [C.c_void_p, u32p, C.c_uint32, C.c_void_p, C.POINTER(C.c_uint64)]),
+    "adi_cuda_batcher_cancel": (C.c_int, [C.c_void_p, C.c_uint64]),
+    "adi_cuda_batcher_step": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint32)]),
+    "adi_cuda_batcher_pending": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
+    "adi_cuda_batcher_result": (C.c_int, [C.c_void_p, C.c_uint64, u32p, C.c_uint32, C.POINTER(C.c_uint32),
+                                          C.POINTER(C.c_int32), C.c_char_p, C.c_size_t]),
+    "adi_cuda_batcher_last_error": (C.c_size_t, [C.c_char_p, C.c_size_t]),
+    "adi_cuda_embedding_rows_device": (C.c_int, [_ctx, _h, u32p, C.c_uint32, C.c_void_p]),
     "adi_cuda_gated_delta_device": (C.c_int, [_ctx, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                               C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p,
                                               C.c_uint32, C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p]),
@@ -139,6 +156,24 @@ class Sequence(C.Structure):
     """adi_cuda_sequence: one sequence's rows and cache slot in a call."""
     _fields_ = [("slot", C.c_uint32), ("first_token", C.c_uint32), ("count", C.c_uint32),
                 ("position", C.c_uint32)]
+
+
+class EmbeddingDesc(C.Structure):
+    _fields_ = [("rows", C.c_uint32), ("columns", C.c_uint32), ("packed", C.c_void_p), ("minimum_f16", C.c_void_p),
+                ("maximum_f16", C.c_void_p), ("exception_indexes", C.c_void_p), ("exception_bf16", C.c_void_p),
+                ("exception_count", C.c_uint32)]
+
+
+class DecoderLayer(C.Structure):
+    """adi_cuda_decoder_layer: one layer of the device decoder stack."""
+    _fields_ = [("full_attention", C.c_uint32), ("input_norm_bf16", C.c_void_p),
+                ("post_attention_norm_bf16", C.c_void_p), ("moe", C.c_uint64), ("output", C.c_uint64),
+                ("slots", C.c_uint32), ("query", C.c_uint64), ("key", C.c_uint64), ("value", C.c_uint64),
+                ("query_norm_bf16", C.c_void_p), ("key_norm_bf16", C.c_void_p), ("key_cache", C.c_void_p),
+                ("value_cache", C.c_void_p), ("capacity", C.c_uint32), ("qkv", C.c_uint64), ("gate", C.c_uint64),
+                ("alpha", C.c_uint64), ("beta", C.c_uint64), ("convolution_bf16", C.c_void_p),
+                ("alpha_bias_bf16", C.c_void_p), ("a_log_bf16", C.c_void_p), ("norm_bf16", C.c_void_p),
+                ("convolution_state", C.c_void_p), ("recurrent_state", C.c_void_p)]
 
 
 def sequence_table(sequences):
@@ -420,6 +455,21 @@ class Context:
     def residual_add_device(self, hidden_ptr: int, add_ptr: int, count: int):
         _check(self.lib.adi_cuda_residual_add_device(self.ptr, hidden_ptr, add_ptr, count), "residual_add_device")
 
+    def upload_embedding(self, e) -> Handle:
+        """`e` provides rows, columns, packed, minimum_f16, maximum_f16,
+        exception_indexes, exception_bf16 (the reference's layouts)."""
+        arrays = [_arr(e.packed, np.uint8), _arr(e.minimum_f16, np.uint16), _arr(e.maximum_f16, np.uint16),
+                  _arr(e.exception_indexes, np.uint32), _arr(e.exception_bf16, np.uint16)]
+        desc = EmbeddingDesc(e.rows, e.columns, *[a.ctypes.data for a in arrays], len(arrays[3]))
+        h = C.c_uint64()
+        _check(self.lib.adi_cuda_upload_embedding(self.ptr, C.byref(desc), C.byref(h)), "upload_embedding")
+        return Handle(self, h.value, "embedding", e.rows, e.columns)
+
+    def embedding_rows_device(self, embedding: Handle, tokens, out_ptr: int):
+        ids = np.ascontiguousarray(tokens, np.uint32)
+        _check(self.lib.adi_cuda_embedding_rows_device(self.ptr, embedding.value, _p(ids, u32p), len(ids), out_ptr),
+               "embedding_rows_device")
+
     # -- attention halves of a decoder layer ---------------------------------
     def full_attention_device(self, query_norm_ptr: int, key_norm_ptr: int, query_gate_ptr: int, key_ptr: int,
                               value_ptr: int, tokens: int, sequences, key_cache_ptr: int, value_cache_ptr: int,
@@ -442,6 +492,28 @@ class Context:
             self.ptr, convolution_ptr, alpha_bias_ptr, a_log_ptr, norm_ptr, qkv_ptr, gate_ptr, alpha_ptr, beta_ptr,
             tokens, C.cast(table, C.c_void_p), len(table), convolution_state_ptr, recurrent_ptr, slots,
             normalized_ptr), "gated_delta_device")
+
+    def decoder_forward_device(self, layers, sequences, hidden_ptr: int, tokens: int, final_norm_ptr: int = 0,
+                               head: Handle | None = None, vocabulary: int = 0, logits_ptr: int = 0):
+        """The decoder stack over device hidden rows; `layers` a list of
+        DecoderLayer, `sequences` (slot, first_token, count, position)."""
+        arr = (DecoderLayer * len(layers))(*layers)
+        table = sequence_table(sequences)
+        _check(self.lib.adi_cuda_decoder_forward_device(
+            self.ptr, C.cast(arr, C.c_void_p), len(layers), C.cast(table, C.c_void_p), len(table), hidden_ptr,
+            tokens, final_norm_ptr, head.value if head else 0, vocabulary, logits_ptr), "decoder_forward_device")
+
+    def decoder_step_device(self, layers, table_ptr: int, sequence_count: int, max_count: int, hidden_ptr: int,
+                            tokens: int, final_norm_ptr: int = 0, head: Handle | None = None, vocabulary: int = 0,
+                            logits_ptr: int = 0):
+        """One replayable decoder step over a device-resident sequence table
+        (int32 [sequences][4]: slot, first_token, count, position); the
+        positions advance on the device. Capturable into a CUDA graph."""
+        arr = (DecoderLayer * len(layers))(*layers)
+        self._step_layers = arr  # kept alive for the graph that may capture this call
+        _check(self.lib.adi_cuda_decoder_step_device(
+            self.ptr, C.cast(arr, C.c_void_p), len(layers), table_ptr, sequence_count, max_count, hidden_ptr, tokens,
+            final_norm_ptr, head.value if head else 0, vocabulary, logits_ptr), "decoder_step_device")
 
     # -- peer-memory exchange of expert parallelism ---------------------------
     def ep_peer_alloc(self, recv_rows: int, returned_rows: int, hidden: int) -> bytes:

@@ -18,7 +18,7 @@ PACKAGE = Path(__file__).resolve().parent
 ROOT = PACKAGE.parent
 CSRC = PACKAGE / "csrc"
 LIBRARY = PACKAGE / "libadi_cuda.so"
-SOURCES = ["kernels.cu", "tc_gemm.cu", "ep.cu", "decode.cu", "attention.cu", "abi.cu"]
+SOURCES = ["kernels.cu", "tc_gemm.cu", "ep.cu", "decode.cu", "attention.cu", "embedding.cu", "abi.cu", "batcher.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -33,7 +33,7 @@ def stale() -> bool:
     if not LIBRARY.exists():
         return True
     built = LIBRARY.stat().st_mtime
-    inputs = list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + [ROOT / "include" / "adi_cuda.h", Path(__file__)]
+    inputs = list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.cpp")) + [ROOT / "include" / "adi_cuda.h", Path(__file__)]
     return any(p.stat().st_mtime > built for p in inputs)
 
 

@@ -11,6 +11,7 @@
 #include "ep.cuh"
 #include "attention.cuh"
 #include "decode.cuh"
+#include "embedding.cuh"
 #include "pipeline.cuh"
 
 #include <cuda_runtime.h>
@@ -311,6 +312,10 @@ struct HeadDev {
     uint32_t rows, cols, protected_count;
     std::unique_ptr<DeviceArray> packed, scales, protected_rows, protected_bf16;
 };
+struct EmbeddingDev {
+    uint32_t rows, cols, exception_count;
+    std::unique_ptr<DeviceArray> packed, minimum, maximum, exception_indexes, exception_bf16;
+};
 struct Bf16Dev {
     uint32_t rows, cols;
     std::unique_ptr<DeviceArray> values;
@@ -325,7 +330,7 @@ struct MoeDev {
     NeDev shared[3];
 };
 
-enum Kind { kExpert = 1, kNe, kHead, kBf16, kMoe };
+enum Kind { kExpert = 1, kNe, kHead, kBf16, kMoe, kEmbedding };
 
 enum Stage {
     kStageRouter,
@@ -465,6 +470,7 @@ struct adi_cuda_context {
     std::map<uint64_t, std::unique_ptr<HeadDev>> heads;
     std::map<uint64_t, std::unique_ptr<Bf16Dev>> bf16s;
     std::map<uint64_t, std::unique_ptr<MoeDev>> moes;
+    std::map<uint64_t, std::unique_ptr<EmbeddingDev>> embeddings;
     uint32_t *error_word = nullptr;  // device word kernels flag timeouts in
     // Arrival counters of the small-batch NE launches (decode.cu), one set
     // per stream the context launches on (main, side); zero between launches.
@@ -474,6 +480,8 @@ struct adi_cuda_context {
     // on their way to the device ring "seq_ring" (same offsets).
     adi_cuda_sequence *seq_host = nullptr;
     uint32_t seq_head = 0;
+    uint32_t *token_host = nullptr;
+    uint32_t token_head = 0;
     // The layer and token count of the last expert-parallel dispatch, whose
     // routes and shared-expert sums the matching combine reads.
     uint64_t ep_layer = 0;
@@ -510,6 +518,12 @@ struct adi_cuda_context {
             check(cudaMemset(error_word, 0, sizeof flags), "clear error word");
             if (flags & kErrorTimeout)
                 throw Status(ADI_CUDA_TIMEOUT, "a bounded device wait timed out; results are invalid");
+            if (flags & kErrorToken)
+                throw Status(ADI_CUDA_INVALID_ARGUMENT, "a token id was outside the embedding's rows");
+            if (flags & kErrorSequence)
+                throw Status(ADI_CUDA_INVALID_ARGUMENT,
+                             "a device sequence table named a slot, rows or positions outside the call's buffers; "
+                             "that sequence's work was skipped and results are invalid");
             throw Status(ADI_CUDA_INVALID_ARGUMENT,
                          "an expert-parallel exchange did not fit a rank's buffers, or its counts did not match "
                          "its rows; nothing was exchanged and results are invalid");
@@ -1917,6 +1931,288 @@ const SeqDesc *stage_sequences(adi_cuda_context *c, const adi_cuda_sequence *seq
 
 bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
+// Token ids on their way to the device, through a pinned ring into the
+// device ring "token_ring" as stage_sequences does with its tables.
+constexpr uint32_t kTokenRing = 1u << 16;
+
+const uint32_t *stage_tokens(adi_cuda_context *c, const uint32_t *tokens, uint32_t n) {
+    if (n > kTokenRing) invalid("too many tokens in one call");
+    uint32_t *ring = c->buffer<uint32_t>("token_ring", kTokenRing);
+    if (!c->token_host)
+        check(cudaHostAlloc(&c->token_host, kTokenRing * sizeof(uint32_t), cudaHostAllocDefault), "cudaHostAlloc");
+    if (c->token_head + n > kTokenRing) {
+        check(cudaStreamSynchronize(c->stream), "synchronize");
+        c->token_head = 0;
+    }
+    std::memcpy(c->token_host + c->token_head, tokens, n * sizeof(uint32_t));
+    check(cudaMemcpyAsync(ring + c->token_head, c->token_host + c->token_head, n * sizeof(uint32_t),
+                          cudaMemcpyHostToDevice, c->stream),
+          "token ids");
+    const uint32_t *dev = ring + c->token_head;
+    c->token_head += n;
+    return dev;
+}
+
+// The first kept_rows rows of an NE product (a head padded to a power of
+// two, cropped to the vocabulary).
+void ne_cropped_dev(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batch, float *out, uint32_t kept_rows) {
+    if (m.rows > kNeDecodeMaxRows) {
+        ne_big_matmul_dev(c, m, in, batch, out, kept_rows);
+        return;
+    }
+    if (kept_rows == m.rows) {
+        ne_matmul_dev(c, m, in, batch, out);
+        return;
+    }
+    float *full = c->buffer<float>("ne_crop_full", size_t(batch) * m.rows);
+    ne_matmul_dev(c, m, in, batch, full);
+    check(cudaMemcpy2DAsync(out, size_t(kept_rows) * 4, full, size_t(m.rows) * 4, size_t(kept_rows) * 4, batch,
+                            cudaMemcpyDeviceToDevice, c->stream),
+          "crop copy");
+}
+
+// NE products of one batch size, the small-batch shapes in one grouped
+// launch and the rest one by one.
+void ne_group_dev(adi_cuda_context *c, const std::vector<NeDecodeCall> &calls, uint32_t batch) {
+    std::vector<NeDecodeCall> decode, other;
+    for (const NeDecodeCall &call : calls)
+        (ne_decode_shape(call.m->rows, call.m->cols, batch) ? decode : other).push_back(call);
+    if (!decode.empty()) ne_decode_dev(c, decode, batch);
+    for (const NeDecodeCall &call : other) ne_matmul_dev(c, *call.m, call.in, batch, call.out);
+}
+
+void full_attention_run(adi_cuda_context *c, const uint16_t *query_norm, const uint16_t *key_norm, float *query_gate,
+                        const float *key, const float *value, uint32_t tokens, const SeqDesc *seqs, uint32_t n,
+                        const SeqBounds &b, float *key_cache, float *value_cache, uint32_t slots, uint32_t capacity,
+                        float *attended) {
+    cudaStream_t s = c->stream;
+    c->stage(kStageAttention);
+    AttnPrepParams pp{};
+    pp.query_gate = query_gate;
+    pp.key = key;
+    pp.value = value;
+    pp.query_norm = query_norm;
+    pp.key_norm = key_norm;
+    pp.seqs = seqs;
+    pp.key_cache = key_cache;
+    pp.value_cache = value_cache;
+    pp.capacity = capacity;
+    pp.tokens = tokens;
+    pp.slots = slots;
+    pp.error = c->error_word;
+    // model.cpp:604-611: theta_base^(2i / rotary dimensions), in float.
+    for (uint32_t i = 0; i < kAttnRopeHalf; ++i)
+        pp.divisors[i] = std::pow(10000000.0f, 2.0f * static_cast<float>(i) / 64.0f);
+    launch_attention_prep(pp, n, b.max_count, s);
+    uint32_t splits = 1, split_keys = 0, tpb = 1;
+    attention_splits(n, b.max_count, b.max_end, static_cast<uint32_t>(c->sms), &splits, &split_keys, &tpb);
+    AttnParams ap{};
+    ap.query_gate = query_gate;
+    ap.key_cache = key_cache;
+    ap.value_cache = value_cache;
+    ap.capacity = capacity;
+    ap.tokens = tokens;
+    ap.slots = slots;
+    ap.seqs = seqs;
+    ap.attended = attended;
+    ap.splits = splits;
+    ap.split_keys = split_keys;
+    ap.error = c->error_word;
+    if (splits > 1) {
+        const size_t rows = size_t(tokens) * kAttnQueryHeads * splits;
+        ap.partial = c->buffer<float>("attn_partial", rows * kAttnHeadSize);
+        ap.partial_ml = c->buffer<float>("attn_partial_ml", rows * 2);
+    }
+    launch_attention(ap, n, b.max_count, tpb, s);
+    c->stage_end();
+    c->after_launch(splits > 1 ? 3 : 2);
+}
+
+void gated_delta_run(adi_cuda_context *c, const uint16_t *convolution, const uint16_t *alpha_bias,
+                     const uint16_t *a_log, const uint16_t *norm, const float *qkv, const float *gate,
+                     const float *alpha, const float *beta, uint32_t tokens, const SeqDesc *seqs, uint32_t n,
+                     const SeqBounds &b, float *convolution_state, float *recurrent_state, uint32_t slots,
+                     float *normalized) {
+    GdParams gp{};
+    gp.qkv = qkv;
+    gp.gate = gate;
+    gp.alpha = alpha;
+    gp.beta = beta;
+    gp.convolution = convolution;
+    gp.alpha_bias = alpha_bias;
+    gp.a_log = a_log;
+    gp.norm = norm;
+    gp.seqs = seqs;
+    gp.conv_state = convolution_state;
+    gp.recurrent = recurrent_state;
+    gp.convolved = c->buffer<float>("gd_convolved", size_t(tokens) * kGdChannels);
+    gp.raw = c->buffer<float>("gd_raw", size_t(tokens) * kGdValueSize);
+    gp.out = normalized;
+    gp.tokens = tokens;
+    gp.slots = slots;
+    gp.error = c->error_word;
+    c->stage(kStageGatedDelta);
+    launch_gated_delta(gp, n, b.max_count, c->stream);
+    c->stage_end();
+    c->after_launch(3);
+}
+
+// The layers of a decoder call, resolved and checked before anything is
+// launched (executor.cpp:1473-1528 decode_layer per layer).
+struct DecoderLayerDev {
+    const adi_cuda_decoder_layer *desc;
+    MoeDev *moe;
+    NeDev *proj[3];
+    NeDev *output;
+    Bf16Dev *alpha, *beta;
+};
+
+struct DecoderPlan {
+    std::vector<DecoderLayerDev> layers;
+    uint32_t hidden = 0;
+    uint32_t slots = 0;     // the fewest slots of any layer
+    uint32_t capacity = 0;  // the smallest cache of any full-attention layer (0: none)
+    HeadDev *head = nullptr;
+    NeDev *ne_head = nullptr;
+};
+
+DecoderPlan plan_decoder(adi_cuda_context *c, const adi_cuda_decoder_layer *layers, uint32_t layer_count,
+                         adi_cuda_handle head, uint32_t vocabulary, bool want_logits) {
+    DecoderPlan plan;
+    plan.layers.resize(layer_count);
+    uint32_t &H = plan.hidden;
+    plan.slots = layer_count ? UINT32_MAX : (1u << 20);
+    plan.capacity = UINT32_MAX;
+    for (uint32_t l = 0; l < layer_count; ++l) {
+        const adi_cuda_decoder_layer &L = layers[l];
+        DecoderLayerDev &r = plan.layers[l];
+        r.desc = &L;
+        r.moe = &lookup(c->moes, L.moe, "MoE layer");
+        if (l == 0) H = r.moe->hidden;
+        if (r.moe->hidden != H) invalid("decoder layers differ in hidden size");
+        if (!L.input_norm_bf16 || !L.post_attention_norm_bf16) invalid("decoder layer norm pointer is null");
+        if (L.slots == 0) invalid("decoder layer has no state slots");
+        plan.slots = std::min(plan.slots, L.slots);
+        r.output = &lookup(c->nes, L.output, "NE");
+        if (L.full_attention) {
+            r.proj[0] = &lookup(c->nes, L.query, "NE");
+            r.proj[1] = &lookup(c->nes, L.key, "NE");
+            r.proj[2] = &lookup(c->nes, L.value, "NE");
+            if (r.proj[0]->rows != kAttnQueryHeads * kAttnQueryStride || r.proj[1]->rows != kAttnKvHeads * kAttnHeadSize ||
+                r.proj[2]->rows != kAttnKvHeads * kAttnHeadSize || r.output->cols != kAttnQueryHeads * kAttnHeadSize)
+                invalid("full attention projection shape mismatch");
+            if (!L.query_norm_bf16 || !L.key_norm_bf16 || !L.key_cache || !L.value_cache || L.capacity == 0)
+                invalid("full attention pointer is null");
+            if (!aligned16(L.key_cache) || !aligned16(L.value_cache)) invalid("caches must be 16-byte aligned");
+            plan.capacity = std::min(plan.capacity, L.capacity);
+        } else {
+            r.proj[0] = &lookup(c->nes, L.qkv, "NE");
+            r.proj[1] = &lookup(c->nes, L.gate, "NE");
+            r.proj[2] = nullptr;
+            r.alpha = &lookup(c->bf16s, L.alpha, "bf16 matrix");
+            r.beta = &lookup(c->bf16s, L.beta, "bf16 matrix");
+            if (r.proj[0]->rows != kGdChannels || r.proj[1]->rows != kGdValueSize || r.alpha->rows != kGdValueHeads ||
+                r.beta->rows != kGdValueHeads || r.output->cols != kGdValueSize)
+                invalid("linear attention projection shape mismatch");
+            if (!L.convolution_bf16 || !L.alpha_bias_bf16 || !L.a_log_bf16 || !L.norm_bf16 || !L.convolution_state ||
+                !L.recurrent_state)
+                invalid("linear attention pointer is null");
+            if (!aligned16(L.recurrent_state) || reinterpret_cast<uintptr_t>(L.convolution_bf16) % 8)
+                invalid("linear attention state must be 16-byte aligned");
+            if (r.alpha->cols != H || r.beta->cols != H) invalid("attention projection columns must be the hidden size");
+        }
+        for (NeDev *m : r.proj)
+            if (m && m->cols != H) invalid("attention projection columns must be the hidden size");
+        if (r.output->rows != H) invalid("attention output rows must be the hidden size");
+    }
+    if (plan.capacity == UINT32_MAX) plan.capacity = 0;
+    if (want_logits) {
+        if (c->heads.count(head)) {
+            plan.head = &lookup(c->heads, head, "head");
+            if (vocabulary != plan.head->rows) invalid("vocabulary must be the head's rows");
+            if (layer_count == 0) H = plan.head->cols;
+            if (plan.head->cols != H) invalid("Mach output head batch shape mismatch");
+        } else {
+            plan.ne_head = &lookup(c->nes, head, "head");
+            if (vocabulary == 0 || vocabulary > plan.ne_head->rows) invalid("vocabulary exceeds the head's rows");
+            if (layer_count == 0) H = plan.ne_head->cols;
+            if (plan.ne_head->cols != H) invalid("Mach output head batch shape mismatch");
+        }
+    }
+    if (H % 4) invalid("hidden size must be a multiple of 4");
+    return plan;
+}
+
+// Every layer over `hidden`, then (logits) the head on each sequence's last
+// token; with `advance` the table's positions move on by the counts at the
+// end (a device-resident table that a replayed step reuses).
+void decoder_run(adi_cuda_context *c, const DecoderPlan &plan, SeqDesc *seqs, uint32_t n, const SeqBounds &b,
+                 float *hidden, uint32_t tokens, const uint16_t *final_norm, uint32_t vocabulary, float *logits,
+                 bool advance) {
+    const uint32_t H = plan.hidden;
+    if (H == 0) return;
+    cudaStream_t s = c->stream;
+    const size_t nh = size_t(tokens) * H;
+    float *normed = c->buffer<float>("dec_normed", nh);
+    float *attn = c->buffer<float>("dec_attn", nh);
+    float *ff = c->buffer<float>("dec_ff", nh);
+    float *p0 = c->buffer<float>("dec_p0", size_t(tokens) * kGdChannels);   // q|gate, or qkv
+    float *p1 = c->buffer<float>("dec_p1", size_t(tokens) * kGdValueSize);  // k and v, or gate
+    float *p2 = c->buffer<float>("dec_p2", size_t(tokens) * kGdValueSize);  // attended, or normalized
+    float *ab = c->buffer<float>("dec_ab", size_t(tokens) * 2 * kGdValueHeads);
+    for (const DecoderLayerDev &r : plan.layers) {
+        const adi_cuda_decoder_layer &L = *r.desc;
+        c->stage(kStageNorm);
+        launch_rms_norm(hidden, L.input_norm_bf16, tokens, H, 1.0f, 1.0e-6f, normed, s);
+        c->stage_end();
+        c->after_launch(1);
+        if (L.full_attention) {
+            float *kb = p1, *vb = p1 + size_t(tokens) * kAttnKvHeads * kAttnHeadSize;
+            ne_group_dev(c, {NeDecodeCall{r.proj[0], normed, p0}, NeDecodeCall{r.proj[1], normed, kb},
+                             NeDecodeCall{r.proj[2], normed, vb}},
+                         tokens);
+            full_attention_run(c, L.query_norm_bf16, L.key_norm_bf16, p0, kb, vb, tokens, seqs, n, b, L.key_cache,
+                               L.value_cache, plan.slots, L.capacity, p2);
+        } else {
+            ne_group_dev(c, {NeDecodeCall{r.proj[0], normed, p0}, NeDecodeCall{r.proj[1], normed, p1}}, tokens);
+            float *al = ab, *be = ab + size_t(tokens) * kGdValueHeads;
+            bf16_matmul_dev(c, *r.alpha, normed, tokens, al);
+            bf16_matmul_dev(c, *r.beta, normed, tokens, be);
+            gated_delta_run(c, L.convolution_bf16, L.alpha_bias_bf16, L.a_log_bf16, L.norm_bf16, p0, p1, al, be, tokens,
+                            seqs, n, b, L.convolution_state, L.recurrent_state, plan.slots, p2);
+        }
+        ne_matmul_dev(c, *r.output, p2, tokens, attn);
+        c->stage(kStageNorm);
+        launch_residual_add(hidden, attn, nh, s);
+        launch_rms_norm(hidden, L.post_attention_norm_bf16, tokens, H, 1.0f, 1.0e-6f, normed, s);
+        c->stage_end();
+        c->after_launch(2);
+        moe_forward_dev(c, *r.moe, normed, tokens, ff, nullptr, nullptr);
+        c->stage(kStageNorm);
+        launch_residual_add(hidden, ff, nh, s);
+        c->stage_end();
+        c->after_launch(1);
+    }
+    if (logits) {
+        // The last token of each sequence: gathered, normalised, projected.
+        float *last = c->buffer<float>("dec_last", size_t(n) * H);
+        float *last_normed = c->buffer<float>("dec_last_normed", size_t(n) * H);
+        c->stage(kStageNorm);
+        launch_last_rows(hidden, seqs, n, H, tokens, c->error_word, last, s);
+        launch_rms_norm(last, final_norm, n, H, 1.0f, 1.0e-6f, last_normed, s);
+        c->stage_end();
+        c->after_launch(2);
+        if (plan.head)
+            head_matmul_dev(c, *plan.head, last_normed, n, logits);
+        else
+            ne_cropped_dev(c, *plan.ne_head, last_normed, n, logits, vocabulary);
+    }
+    if (advance) {
+        launch_advance_positions(seqs, n, s);
+        c->after_launch(1);
+    }
+}
+
 }  // namespace
 
 extern "C" {
@@ -1955,8 +2251,10 @@ int adi_cuda_shutdown(adi_cuda_context *c) {
         cudaEvent_t fork = c->fork_event, join = c->join_event;
         uint32_t *error_word = c->error_word, *error_host = c->error_host, *decode_done = c->decode_done;
         adi_cuda_sequence *seq_host = c->seq_host;
+        uint32_t *token_host = c->token_host;
         delete c;
         if (seq_host) cudaFreeHost(seq_host);
+        if (token_host) cudaFreeHost(token_host);
         if (error_word) cudaFree(error_word);
         if (decode_done) cudaFree(decode_done);
         if (error_host) cudaFreeHost(error_host);
@@ -1980,6 +2278,14 @@ int adi_cuda_set_stream(adi_cuda_context *c, void *stream) {
     return guarded([&] {
         std::lock_guard<std::mutex> g(require(c)->lock);
         c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own_stream;
+    });
+}
+
+int adi_cuda_get_stream(adi_cuda_context *c, void **stream) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        if (!stream) invalid("stream pointer is null");
+        *stream = c->stream;
     });
 }
 
@@ -2159,7 +2465,7 @@ int adi_cuda_release(adi_cuda_context *c, adi_cuda_handle h) {
         use_device(c);
         check(cudaStreamSynchronize(c->stream), "synchronize");
         const size_t erased = c->experts.erase(h) + c->nes.erase(h) + c->heads.erase(h) + c->bf16s.erase(h) +
-                              c->moes.erase(h);
+                              c->moes.erase(h) + c->embeddings.erase(h);
         if (!erased) invalid("unknown handle");
     });
 }
@@ -2198,19 +2504,7 @@ int adi_cuda_ne_matmul_cropped_device(adi_cuda_context *c, adi_cuda_handle h, co
         NeDev &m = lookup(c->nes, h, "NE");
         if (batch == 0) invalid("Mach NE batch shape mismatch");
         if (kept_rows == 0 || kept_rows > m.rows) invalid("Mach NE kept rows out of range");
-        if (m.rows > kNeDecodeMaxRows) {
-            ne_big_matmul_dev(c, m, in, batch, out, kept_rows);
-            return;
-        }
-        if (kept_rows == m.rows) {
-            ne_matmul_dev(c, m, in, batch, out);
-            return;
-        }
-        float *full = c->buffer<float>("ne_crop_full", size_t(batch) * m.rows);
-        ne_matmul_dev(c, m, in, batch, full);
-        check(cudaMemcpy2DAsync(out, size_t(kept_rows) * 4, full, size_t(m.rows) * 4, size_t(kept_rows) * 4, batch,
-                                cudaMemcpyDeviceToDevice, c->stream),
-              "crop copy");
+        ne_cropped_dev(c, m, in, batch, out, kept_rows);
     });
 }
 
@@ -2221,15 +2515,12 @@ int adi_cuda_ne_matmul_group_device(adi_cuda_context *c, uint32_t count, const a
         use_device(c);
         if (count && (!matrices || !inputs || !outputs)) invalid("matrix, input or output array is null");
         if (batch == 0) invalid("Mach NE batch shape mismatch");
-        std::vector<NeDecodeCall> decode;
-        std::vector<NeDecodeCall> other;
+        std::vector<NeDecodeCall> calls;
         for (uint32_t i = 0; i < count; ++i) {
             if (!inputs[i] || !outputs[i]) invalid("input or output pointer is null");
-            NeDev &m = lookup(c->nes, matrices[i], "NE");
-            (ne_decode_shape(m.rows, m.cols, batch) ? decode : other).push_back(NeDecodeCall{&m, inputs[i], outputs[i]});
+            calls.push_back(NeDecodeCall{&lookup(c->nes, matrices[i], "NE"), inputs[i], outputs[i]});
         }
-        if (!decode.empty()) ne_decode_dev(c, decode, batch);
-        for (const NeDecodeCall &call : other) ne_matmul_dev(c, *call.m, call.in, batch, call.out);
+        ne_group_dev(c, calls, batch);
     });
 }
 
@@ -2466,6 +2757,62 @@ int adi_cuda_residual_add_device(adi_cuda_context *c, float *hidden, const float
     });
 }
 
+int adi_cuda_upload_embedding(adi_cuda_context *c, const adi_embedding *m, adi_cuda_handle *h) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        if (!m || !h) invalid("embedding or handle pointer is null");
+        use_device(c);
+        if (m->rows == 0 || m->columns == 0 || m->columns % 64 || !m->packed || !m->minimum_f16 || !m->maximum_f16 ||
+            (m->exception_count && (!m->exception_indexes || !m->exception_bf16)))
+            invalid("Mach embedding shape mismatch");
+        if (uint64_t(m->rows) * m->columns > UINT32_MAX) invalid("Mach embedding has more than 2^32 values");
+        for (uint32_t i = 0; i < m->exception_count; ++i)
+            if (m->exception_indexes[i] >= m->rows * m->columns || (i && m->exception_indexes[i] <= m->exception_indexes[i - 1]))
+                invalid("Mach embedding exceptions must be ascending and in range");
+        auto d = std::make_unique<EmbeddingDev>();
+        d->rows = m->rows;
+        d->cols = m->columns;
+        d->exception_count = m->exception_count;
+        const size_t groups = size_t(m->rows) * (m->columns / 64);
+        d->packed = upload_bytes(m->packed, size_t(m->rows) * m->columns / 2, "packed");
+        d->minimum = upload_bytes(m->minimum_f16, groups * 2, "minimum");
+        d->maximum = upload_bytes(m->maximum_f16, groups * 2, "maximum");
+        d->exception_indexes = upload_bytes(m->exception_indexes, size_t(m->exception_count) * 4, "exception indexes");
+        d->exception_bf16 = upload_bytes(m->exception_bf16, size_t(m->exception_count) * 2, "exception values");
+        const uint64_t id = c->new_handle(kEmbedding);
+        c->embeddings[id] = std::move(d);
+        *h = id;
+    });
+}
+
+int adi_cuda_embedding_rows_device(adi_cuda_context *c, adi_cuda_handle h, const uint32_t *tokens, uint32_t count,
+                                   float *out) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!tokens || !out) invalid("token or output pointer is null");
+        EmbeddingDev &e = lookup(c->embeddings, h, "embedding");
+        if (count == 0) return;
+        for (uint32_t i = 0; i < count; ++i)
+            if (tokens[i] >= e.rows) invalid("decoder token is out of range");
+        const uint32_t *dev = stage_tokens(c, tokens, count);
+        EmbeddingParams p{};
+        p.packed = e.packed->as<uint8_t>();
+        p.minimum = e.minimum->as<uint16_t>();
+        p.maximum = e.maximum->as<uint16_t>();
+        p.exception_indexes = e.exception_indexes->as<uint32_t>();
+        p.exception_bf16 = e.exception_bf16->as<uint16_t>();
+        p.exception_count = e.exception_count;
+        p.rows = e.rows;
+        p.columns = e.cols;
+        p.tokens = dev;
+        p.out = out;
+        p.error = c->error_word;
+        launch_embedding_rows(p, count, c->stream);
+        c->after_launch(1);
+    });
+}
+
 int adi_cuda_full_attention_device(adi_cuda_context *c, const uint16_t *query_norm_bf16,
                                    const uint16_t *key_norm_bf16, float *query_gate, const float *key,
                                    const float *value, uint32_t tokens, const adi_cuda_sequence *sequences,
@@ -2482,43 +2829,8 @@ int adi_cuda_full_attention_device(adi_cuda_context *c, const uint16_t *query_no
             invalid("full attention buffers must be 16-byte aligned");
         SeqBounds b;
         const SeqDesc *seqs = stage_sequences(c, sequences, sequence_count, tokens, slots, capacity, &b);
-        cudaStream_t s = c->stream;
-        c->stage(kStageAttention);
-        AttnPrepParams pp{};
-        pp.query_gate = query_gate;
-        pp.key = key;
-        pp.value = value;
-        pp.query_norm = query_norm_bf16;
-        pp.key_norm = key_norm_bf16;
-        pp.seqs = seqs;
-        pp.key_cache = key_cache;
-        pp.value_cache = value_cache;
-        pp.capacity = capacity;
-        // model.cpp:604-611: theta_base^(2i / rotary dimensions), in float.
-        for (uint32_t i = 0; i < kAttnRopeHalf; ++i)
-            pp.divisors[i] = std::pow(10000000.0f, 2.0f * static_cast<float>(i) / 64.0f);
-        launch_attention_prep(pp, sequence_count, b.max_count, s);
-        uint32_t splits = 1, split_keys = 0, tpb = 1;
-        attention_splits(sequence_count, b.max_count, b.max_end, static_cast<uint32_t>(c->sms), &splits, &split_keys,
-                         &tpb);
-        AttnParams ap{};
-        ap.query_gate = query_gate;
-        ap.key_cache = key_cache;
-        ap.value_cache = value_cache;
-        ap.capacity = capacity;
-        ap.seqs = seqs;
-        ap.attended = attended;
-        ap.splits = splits;
-        ap.split_keys = split_keys;
-        ap.error = c->error_word;
-        if (splits > 1) {
-            const size_t rows = size_t(tokens) * kAttnQueryHeads * splits;
-            ap.partial = c->buffer<float>("attn_partial", rows * kAttnHeadSize);
-            ap.partial_ml = c->buffer<float>("attn_partial_ml", rows * 2);
-        }
-        launch_attention(ap, sequence_count, b.max_count, tpb, s);
-        c->stage_end();
-        c->after_launch(splits > 1 ? 3 : 2);
+        full_attention_run(c, query_norm_bf16, key_norm_bf16, query_gate, key, value, tokens, seqs, sequence_count, b,
+                           key_cache, value_cache, slots, capacity, attended);
     });
 }
 
@@ -2539,25 +2851,50 @@ int adi_cuda_gated_delta_device(adi_cuda_context *c, const uint16_t *convolution
             invalid("linear attention buffers must be 16-byte aligned (the convolution weights 8-byte)");
         SeqBounds b;
         const SeqDesc *seqs = stage_sequences(c, sequences, sequence_count, tokens, slots, 0, &b);
-        GdParams gp{};
-        gp.qkv = qkv;
-        gp.gate = gate;
-        gp.alpha = alpha;
-        gp.beta = beta;
-        gp.convolution = convolution_bf16;
-        gp.alpha_bias = alpha_bias_bf16;
-        gp.a_log = a_log_bf16;
-        gp.norm = norm_bf16;
-        gp.seqs = seqs;
-        gp.conv_state = convolution_state;
-        gp.recurrent = recurrent_state;
-        gp.convolved = c->buffer<float>("gd_convolved", size_t(tokens) * kGdChannels);
-        gp.raw = c->buffer<float>("gd_raw", size_t(tokens) * kGdValueSize);
-        gp.out = normalized;
-        c->stage(kStageGatedDelta);
-        launch_gated_delta(gp, sequence_count, b.max_count, c->stream);
-        c->stage_end();
-        c->after_launch(3);
+        gated_delta_run(c, convolution_bf16, alpha_bias_bf16, a_log_bf16, norm_bf16, qkv, gate, alpha, beta, tokens,
+                        seqs, sequence_count, b, convolution_state, recurrent_state, slots, normalized);
+    });
+}
+
+int adi_cuda_decoder_forward_device(adi_cuda_context *c, const adi_cuda_decoder_layer *layers, uint32_t layer_count,
+                                    const adi_cuda_sequence *sequences, uint32_t sequence_count, float *hidden,
+                                    uint32_t tokens, const uint16_t *final_norm_bf16, adi_cuda_handle head,
+                                    uint32_t vocabulary, float *logits) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!hidden || (layer_count && !layers) || (logits && !final_norm_bf16)) invalid("decoder pointer is null");
+        if (tokens == 0) invalid("decoder batch shape mismatch");
+        if (!aligned16(hidden) || (logits && !aligned16(logits))) invalid("hidden and logits must be 16-byte aligned");
+        const DecoderPlan plan = plan_decoder(c, layers, layer_count, head, vocabulary, logits != nullptr);
+        SeqBounds b;
+        SeqDesc *seqs = const_cast<SeqDesc *>(
+            stage_sequences(c, sequences, sequence_count, tokens, plan.slots, plan.capacity, &b));
+        decoder_run(c, plan, seqs, sequence_count, b, hidden, tokens, final_norm_bf16, vocabulary, logits, false);
+    });
+}
+
+int adi_cuda_decoder_step_device(adi_cuda_context *c, const adi_cuda_decoder_layer *layers, uint32_t layer_count,
+                                 adi_cuda_sequence *device_sequences, uint32_t sequence_count, uint32_t max_count,
+                                 float *hidden, uint32_t tokens, const uint16_t *final_norm_bf16, adi_cuda_handle head,
+                                 uint32_t vocabulary, float *logits) {
+    return guarded([&] {
+        std::lock_guard<std::mutex> g(require(c)->lock);
+        use_device(c);
+        if (!hidden || !device_sequences || (layer_count && !layers) || (logits && !final_norm_bf16))
+            invalid("decoder pointer is null");
+        if (tokens == 0 || sequence_count == 0 || sequence_count > 65535 || max_count == 0 || max_count > tokens)
+            invalid("decoder batch shape mismatch");
+        if (!aligned16(hidden) || (logits && !aligned16(logits)) || !aligned16(device_sequences))
+            invalid("hidden, logits and the sequence table must be 16-byte aligned");
+        const DecoderPlan plan = plan_decoder(c, layers, layer_count, head, vocabulary, logits != nullptr);
+        // Positions are only known on the device: the key range is planned
+        // for the whole cache, and the kernels check every entry.
+        SeqBounds b;
+        b.max_count = max_count;
+        b.max_end = plan.capacity;
+        decoder_run(c, plan, reinterpret_cast<SeqDesc *>(device_sequences), sequence_count, b, hidden, tokens,
+                    final_norm_bf16, vocabulary, logits, true);
     });
 }
 

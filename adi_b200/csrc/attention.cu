@@ -51,6 +51,17 @@ __device__ __forceinline__ float block_total(float v, float *red) {
     return t;
 }
 
+// A table entry lies inside the call's buffers (capacity 0: no cache). The
+// check is uniform over a block, which returns before any barrier when it
+// fails.
+__device__ __forceinline__ bool sequence_in_range(const SeqDesc &sq, uint32_t tokens, uint32_t slots,
+                                                  uint32_t capacity, uint32_t *error) {
+    const bool ok = sq.slot < slots && sq.count <= tokens && sq.first <= tokens - sq.count &&
+                    (capacity == 0 || (sq.position <= capacity && sq.count <= capacity - sq.position));
+    if (!ok && threadIdx.x == 0) atomicOr(error, kErrorSequence);
+    return ok;
+}
+
 __device__ __forceinline__ float sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 
@@ -66,6 +77,7 @@ __global__ void __launch_bounds__(256) attention_prep_kernel(const __grid_consta
     const SeqDesc sq = p.seqs[blockIdx.y];
     const uint32_t li = blockIdx.x;
     if (li >= sq.count) return;
+    if (!sequence_in_range(sq, p.tokens, p.slots, p.capacity, p.error)) return;
     const size_t t = sq.first + li;
     const uint32_t pos = sq.position + li, head = blockIdx.z, d = threadIdx.x;
     const bool query = head < kAttnQueryHeads;
@@ -132,6 +144,7 @@ __global__ void __launch_bounds__(256, 1) attention_kernel(const __grid_constant
     const SeqDesc sq = p.seqs[blockIdx.z];
     const uint32_t tile0 = blockIdx.y * QT;
     if (tile0 >= sq.count) return;
+    if (!sequence_in_range(sq, p.tokens, p.slots, p.capacity, p.error)) return;
     const uint32_t g = blockIdx.x / p.splits, sp = blockIdx.x % p.splits;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t tq = warp / KW, ks = warp % KW;
@@ -344,6 +357,7 @@ __global__ void __launch_bounds__(256) attention_combine_kernel(const __grid_con
     const SeqDesc sq = p.seqs[blockIdx.y];
     const uint32_t li = blockIdx.x;
     if (li >= sq.count) return;
+    if (!sequence_in_range(sq, p.tokens, p.slots, p.capacity, p.error)) return;
     const size_t h = (size_t)(sq.first + li) * kAttnQueryHeads + blockIdx.z;
     const uint32_t d = threadIdx.x;
     const size_t base = h * p.splits;
@@ -373,6 +387,7 @@ __global__ void __launch_bounds__(128) gd_conv_kernel(const __grid_constant__ Gd
     const SeqDesc sq = p.seqs[blockIdx.y];
     const uint32_t li = blockIdx.x;
     if (li >= sq.count) return;
+    if (!sequence_in_range(sq, p.tokens, p.slots, 0, p.error)) return;
     const uint32_t c = blockIdx.z * kGdHeadSize + threadIdx.x;
     const size_t t = sq.first + li;
     float h[3];
@@ -417,6 +432,7 @@ __device__ __forceinline__ float transpose_reduce4(float v0, float v1, float v2,
 // x = 0 of each head also advances the convolution state of 256 channels.
 __global__ void __launch_bounds__(256) gd_recurrence_kernel(const __grid_constant__ GdParams p) {
     const SeqDesc sq = p.seqs[blockIdx.z];
+    if (!sequence_in_range(sq, p.tokens, p.slots, 0, p.error) || sq.count == 0) return;
     const uint32_t head = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t row0 = blockIdx.x * 32 + warp * 4;
     const uint32_t kh = head / (kGdValueHeads / kGdKeyHeads);
@@ -500,6 +516,7 @@ __global__ void __launch_bounds__(128) gd_norm_gate_kernel(const __grid_constant
     const SeqDesc sq = p.seqs[blockIdx.y];
     const uint32_t li = blockIdx.x;
     if (li >= sq.count) return;
+    if (!sequence_in_range(sq, p.tokens, p.slots, 0, p.error)) return;
     const size_t i = ((size_t)(sq.first + li) * kGdValueHeads + blockIdx.z) * kGdHeadSize + threadIdx.x;
     const float x = p.raw[i];
     const float squares = block_total<128>(x * x, red);
@@ -507,7 +524,31 @@ __global__ void __launch_bounds__(128) gd_norm_gate_kernel(const __grid_constant
     p.out[i] = x * scale * bf16_bits_to_f32(p.norm[threadIdx.x]) * silu(p.gate[i]);
 }
 
+// out[i] = hidden[last token of sequence i].
+__global__ void last_rows_kernel(const float4 *hidden, const SeqDesc *seqs, uint32_t quads, uint32_t tokens,
+                                 uint32_t *error, float4 *out) {
+    const SeqDesc sq = seqs[blockIdx.x];
+    if (!sequence_in_range(sq, tokens, ~0u, 0, error) || sq.count == 0) return;
+    const float4 *row = hidden + (size_t)(sq.first + sq.count - 1) * quads;
+    for (uint32_t i = threadIdx.x; i < quads; i += blockDim.x) out[(size_t)blockIdx.x * quads + i] = row[i];
+}
+
+__global__ void advance_positions_kernel(SeqDesc *seqs, uint32_t n) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) seqs[i].position += seqs[i].count;
+}
+
 }  // namespace
+
+void launch_last_rows(const float *hidden, const SeqDesc *seqs, uint32_t sequences, uint32_t hidden_size,
+                      uint32_t tokens, uint32_t *error, float *out, cudaStream_t s) {
+    last_rows_kernel<<<sequences, 256, 0, s>>>(reinterpret_cast<const float4 *>(hidden), seqs, hidden_size / 4, tokens,
+                                                error, reinterpret_cast<float4 *>(out));
+}
+
+void launch_advance_positions(SeqDesc *seqs, uint32_t sequences, cudaStream_t s) {
+    advance_positions_kernel<<<(sequences + 255) / 256, 256, 0, s>>>(seqs, sequences);
+}
 
 size_t attention_smem_bytes(uint32_t tokens_per_block) {
     const uint32_t kpw = kAttnKeyTile / (8 / tokens_per_block);

@@ -39,20 +39,25 @@ struct SeqDesc {
     uint32_t slot, first, count, position;
 };
 
+// Device error word bit: a sequence of a device-resident table named a slot,
+// rows or positions outside the call's buffers; its work was skipped.
+constexpr uint32_t kErrorSequence = 4u;
+
 struct AttnPrepParams {
     float *query_gate;                  // [tokens][16][512]; queries rewritten in place
     const float *key, *value;           // [tokens][2][256]
     const uint16_t *query_norm, *key_norm;  // bf16 [256]
     const SeqDesc *seqs;
     float *key_cache, *value_cache;     // [slots][2][capacity][256]
-    uint32_t capacity;
+    uint32_t capacity, tokens, slots;
+    uint32_t *error;
     float divisors[kAttnRopeHalf];      // theta_base^(2i/64)
 };
 
 struct AttnParams {
     const float *query_gate;
     const float *key_cache, *value_cache;
-    uint32_t capacity;
+    uint32_t capacity, tokens, slots;
     const SeqDesc *seqs;
     float *attended;    // [tokens][16][256], written when splits == 1
     float *partial;     // [tokens][16][splits][256] unnormalised sums, splits > 1
@@ -70,6 +75,8 @@ struct GdParams {
     float *convolved;   // scratch [tokens][8192]
     float *raw;         // scratch [tokens][4096]
     float *out;         // [tokens][4096]
+    uint32_t tokens, slots;
+    uint32_t *error;
 };
 
 // Shared memory of the attention kernel.
@@ -83,5 +90,12 @@ void launch_attention_prep(const AttnPrepParams &p, uint32_t sequences, uint32_t
 void launch_attention(const AttnParams &p, uint32_t sequences, uint32_t max_count, uint32_t tokens_per_block,
                       cudaStream_t s);
 void launch_gated_delta(const GdParams &p, uint32_t sequences, uint32_t max_count, cudaStream_t s);
+// Adds each sequence's count to its position (a device-resident table after
+// a step, so a replayed step continues where the last one ended).
+void launch_advance_positions(SeqDesc *seqs, uint32_t sequences, cudaStream_t s);
+// Gathers the hidden row of each sequence's last token (hidden_size a
+// multiple of 4, rows 16-byte aligned).
+void launch_last_rows(const float *hidden, const SeqDesc *seqs, uint32_t sequences, uint32_t hidden_size,
+                      uint32_t tokens, uint32_t *error, float *out, cudaStream_t s);
 
 }  // namespace adi_cuda

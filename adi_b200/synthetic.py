@@ -303,3 +303,30 @@ def linear_attention_projections(seed: int, tokens: int):
     rng = np.random.default_rng(seed)
     f = lambda n: rng.standard_normal((tokens, n)).astype(np.float32)  # noqa: E731
     return f(8192), f(4096), f(32), f(32)
+
+
+@dataclass
+class Embedding:
+    """The 4-bit token embedding in the reference's layout (MachEmbedding)."""
+    rows: int
+    columns: int
+    packed: np.ndarray
+    minimum_f16: np.ndarray
+    maximum_f16: np.ndarray
+    exception_indexes: np.ndarray
+    exception_bf16: np.ndarray
+
+
+def embedding(seed: int, rows: int, columns: int, exceptions: int = 64) -> Embedding:
+    """Uniform codes; per 64-column group a minimum N(-0.05, 0.01) and a
+    maximum 0.1 above it (f16), a few groups with maximum == minimum (the
+    1e-8 floor); `exceptions` bf16 values N(0, 1) at random flat indexes."""
+    rng = np.random.default_rng(seed)
+    groups = rows * columns // 64
+    lo = rng.normal(-0.05, 0.01, groups).astype(np.float16)
+    hi = (lo.astype(np.float32) + 0.1).astype(np.float16)
+    flat = rng.choice(groups, size=min(groups, 8), replace=False)
+    hi[flat] = lo[flat]
+    idx = np.sort(rng.choice(rows * columns, size=exceptions, replace=False)).astype(np.uint32)
+    return Embedding(rows, columns, rng.integers(0, 256, rows * columns // 2, dtype=np.uint8),
+                     lo.view(np.uint16), hi.view(np.uint16), idx, _bf16_bits(rng.normal(0, 1, exceptions)))

@@ -119,6 +119,8 @@ ADI_CUDA_API size_t adi_cuda_last_error(char *buffer, size_t size);
 /* Runs the context on a caller's cudaStream_t (NULL: back to its own). */
 ADI_CUDA_API int adi_cuda_set_stream(adi_cuda_context *context, void *stream);
 ADI_CUDA_API int adi_cuda_synchronize(adi_cuda_context *context);
+/* The stream the context launches on (its own, or the one last set). */
+ADI_CUDA_API int adi_cuda_get_stream(adi_cuda_context *context, void **stream);
 /* Matmul arithmetic: 0 = CUDA-core fp32 throughout (parity 1e-3 rel L2);
  * 1 = tensor-core operands where a path has them (parity 1e-2 rel L2). */
 ADI_CUDA_API int adi_cuda_set_precision(adi_cuda_context *context, int mode);
@@ -453,6 +455,29 @@ ADI_CUDA_API int adi_cuda_rms_norm_device(adi_cuda_context *context, const float
 ADI_CUDA_API int adi_cuda_residual_add_device(adi_cuda_context *context, float *hidden,
                                  const float *add, size_t count);
 
+/* MachEmbedding (include/adi/kernels.hpp:54-62): the 4-bit token embedding,
+ * [rows][columns/2] packed codes (high nibble first), f16 minimum and
+ * maximum per 64-column group, and bf16 exceptions at ascending flat
+ * indexes. */
+typedef struct adi_embedding {
+    uint32_t rows;
+    uint32_t columns;
+    const uint8_t *packed;
+    const uint16_t *minimum_f16;
+    const uint16_t *maximum_f16;
+    const uint32_t *exception_indexes;
+    const uint16_t *exception_bf16;
+    uint32_t exception_count;
+} adi_embedding;
+
+ADI_CUDA_API int adi_cuda_upload_embedding(adi_cuda_context *context, const adi_embedding *embedding,
+                                           adi_cuda_handle *handle);
+/* mach_embedding_row (src/kernels.cpp:802-845) for `count` token ids (a HOST
+ * array, checked against the rows) into out [count][columns] (device),
+ * bit-exact; asynchronous on the context stream. */
+ADI_CUDA_API int adi_cuda_embedding_rows_device(adi_cuda_context *context, adi_cuda_handle embedding,
+                                                const uint32_t *tokens, uint32_t count, float *out);
+
 /* ---- Attention halves of a decoder layer --------------------------------
  *
  * The steps of a decoder layer between its attention input projections (NE
@@ -518,6 +543,127 @@ ADI_CUDA_API int adi_cuda_gated_delta_device(
     const float *alpha, const float *beta, uint32_t tokens, const adi_cuda_sequence *sequences,
     uint32_t sequence_count, float *convolution_state, float *recurrent_state, uint32_t slots,
     float *normalized);
+
+/* One decoder layer of the stack entry below: the attention half (full
+ * attention or Gated DeltaNet, with its projections and state), the MoE
+ * block, and the two RMS norms (executor.cpp:1473-1528 decode_layer,
+ * :1592-1825 decode_batch, :1827-2101 prefill). Handles come from
+ * adi_cuda_upload_ne / adi_cuda_upload_bf16 / adi_cuda_upload_moe_layer;
+ * pointers are device pointers. */
+typedef struct adi_cuda_decoder_layer {
+    uint32_t full_attention;                 /* 1: full attention, 0: Gated DeltaNet */
+    const uint16_t *input_norm_bf16;         /* [hidden], applied as x*scale*(1+w) */
+    const uint16_t *post_attention_norm_bf16;
+    adi_cuda_handle moe;
+    adi_cuda_handle output;                  /* NE [hidden x 4096] */
+    uint32_t slots;                          /* state slots of this layer */
+    /* full attention */
+    adi_cuda_handle query, key, value;       /* NE [8192 x hidden], [512 x hidden] x2 */
+    const uint16_t *query_norm_bf16, *key_norm_bf16;  /* [256] */
+    float *key_cache, *value_cache;          /* [slots][2][capacity][256] */
+    uint32_t capacity;
+    /* Gated DeltaNet */
+    adi_cuda_handle qkv, gate;               /* NE [8192 x hidden], [4096 x hidden] */
+    adi_cuda_handle alpha, beta;             /* bf16 [32 x hidden] */
+    const uint16_t *convolution_bf16, *alpha_bias_bf16, *a_log_bf16, *norm_bf16;
+    float *convolution_state, *recurrent_state;  /* [slots][8192][3], [slots][32][128][128] */
+} adi_cuda_decoder_layer;
+
+/* The decoder stack on the device: hidden [tokens][H] (the embedded tokens
+ * of the sequences in `sequences`, their rows as the table says) goes
+ * through every layer in turn -- RMS norm, the attention half and its output
+ * projection, the residual, RMS norm, the MoE block, the residual -- with no
+ * host round trip; the layers' caches and states advance. With `logits`,
+ * the last token of each sequence is normalised by final_norm_bf16 and
+ * projected by `head` (an int5_g64 head whose rows are `vocabulary`, or an
+ * NE head cropped to `vocabulary` rows) into logits [sequence_count]
+ * [vocabulary]. Asynchronous on the context stream. */
+ADI_CUDA_API int adi_cuda_decoder_forward_device(
+    adi_cuda_context *context, const adi_cuda_decoder_layer *layers, uint32_t layer_count,
+    const adi_cuda_sequence *sequences, uint32_t sequence_count, float *hidden, uint32_t tokens,
+    const uint16_t *final_norm_bf16, adi_cuda_handle head, uint32_t vocabulary, float *logits);
+
+/* The same stack as one replayable decode step: the sequence table lives in
+ * device memory (16-byte aligned, owned by the caller) and each sequence's
+ * position advances by its count at the end of the step, so the call can be
+ * captured into a CUDA graph once and replayed for consecutive steps.
+ * max_count bounds every entry's count. Positions are not known on the host:
+ * the kernels check each entry against the layers' slots, caches and the
+ * token rows, skip an entry that falls outside them and flag it, and the
+ * next synchronising call reports ADI_CUDA_INVALID_ARGUMENT. */
+ADI_CUDA_API int adi_cuda_decoder_step_device(
+    adi_cuda_context *context, const adi_cuda_decoder_layer *layers, uint32_t layer_count,
+    adi_cuda_sequence *device_sequences, uint32_t sequence_count, uint32_t max_count, float *hidden,
+    uint32_t tokens, const uint16_t *final_norm_bf16, adi_cuda_handle head, uint32_t vocabulary,
+    float *logits);
+
+/* ---- Continuous batching -------------------------------------------------
+ *
+ * The scheduling loop of the reference's ContinuousBatcher
+ * (src/generation.cpp:315-672) over adi_cuda_decoder_forward_device: tokens
+ * in, tokens out (the tokenizer is the caller's). Each adi_cuda_batcher_step
+ * admits at most one queued request (a free state slot, its Gated DeltaNet
+ * states zeroed, its prompt prefilled in prefill_ubatch chunks with logits
+ * for the last), samples the next token of every active request
+ * (sample_token, src/generation.cpp:208-276, on the request's own
+ * std::mt19937_64 seeded with its seed), finishes requests on a stop token or
+ * at their output limit, and decodes the rest as one batch. */
+typedef struct adi_cuda_generation_options {
+    uint32_t max_output_tokens; /* 0: the rest of the context */
+    float temperature;          /* 0 (argmax) or [1e-4, 2] */
+    float top_p;                /* (0, 1] */
+    uint64_t seed;
+} adi_cuda_generation_options;
+
+typedef struct adi_cuda_batcher_config {
+    const adi_cuda_decoder_layer *layers; /* copied */
+    uint32_t layer_count;
+    adi_cuda_handle embedding;            /* adi_cuda_upload_embedding */
+    adi_cuda_handle head;                 /* int5 head, or NE head cropped to vocabulary */
+    const uint16_t *final_norm_bf16;      /* device [hidden] */
+    uint32_t hidden;
+    uint32_t vocabulary;
+    uint32_t slots;                       /* sequences at once; every layer has at least these */
+    uint32_t context;                     /* positions per sequence; every cache at least these */
+    uint32_t prefill_ubatch;
+    uint32_t stop_tokens[2];              /* eos and <|im_end|> */
+    uint32_t stop_count;
+    const uint32_t *masked_tokens;        /* set to the lowest float before sampling; copied */
+    uint32_t masked_count;
+} adi_cuda_batcher_config;
+
+enum {
+    ADI_CUDA_REQUEST_QUEUED = 0,
+    ADI_CUDA_REQUEST_RUNNING = 1,
+    ADI_CUDA_REQUEST_STOP_TOKEN = 2,
+    ADI_CUDA_REQUEST_LENGTH = 3,
+    ADI_CUDA_REQUEST_FAILED = 4
+};
+
+typedef struct adi_cuda_batcher adi_cuda_batcher;
+
+ADI_CUDA_API int adi_cuda_batcher_create(adi_cuda_context *context, const adi_cuda_batcher_config *config,
+                                         adi_cuda_batcher **batcher);
+ADI_CUDA_API int adi_cuda_batcher_destroy(adi_cuda_batcher *batcher);
+/* Queues a request; its options are checked now (validate_generation_options),
+ * its prompt against the context when it is admitted. */
+ADI_CUDA_API int adi_cuda_batcher_submit(adi_cuda_batcher *batcher, const uint32_t *prompt, uint32_t count,
+                                         const adi_cuda_generation_options *options, uint64_t *request);
+/* The request fails ("generation cancelled") at its next admission or sampling. */
+ADI_CUDA_API int adi_cuda_batcher_cancel(adi_cuda_batcher *batcher, uint64_t request);
+/* One iteration of the loop; *active: requests still decoding after it. */
+ADI_CUDA_API int adi_cuda_batcher_step(adi_cuda_batcher *batcher, uint32_t *active);
+ADI_CUDA_API int adi_cuda_batcher_pending(adi_cuda_batcher *batcher, uint32_t *queued, uint32_t *active);
+/* The request's output tokens so far (up to `capacity`), their count, its
+ * ADI_CUDA_REQUEST_* status and, when it failed, the reason. */
+ADI_CUDA_API int adi_cuda_batcher_result(adi_cuda_batcher *batcher, uint64_t request, uint32_t *tokens,
+                                         uint32_t capacity, uint32_t *count, int32_t *status, char *message,
+                                         size_t message_size);
+ADI_CUDA_API size_t adi_cuda_batcher_last_error(char *buffer, size_t size);
+/* sample_token (src/generation.cpp:208-276) `draws` times on one generator
+ * seeded with `seed`: the batcher's sampler, on the host. */
+ADI_CUDA_API int adi_cuda_sample_tokens(const float *logits, uint32_t count, float temperature, float top_p,
+                                        uint64_t seed, uint32_t draws, uint32_t *out);
 
 #ifdef __cplusplus
 }

@@ -211,6 +211,12 @@ class Oracle(_Checker):
         return out, experts, weights
 
 
+class _EmbeddingDesc(C.Structure):
+    _fields_ = [("rows", C.c_uint32), ("columns", C.c_uint32), ("packed", C.c_void_p), ("minimum_f16", C.c_void_p),
+                ("maximum_f16", C.c_void_p), ("exception_indexes", C.c_void_p), ("exception_bf16", C.c_void_p),
+                ("exception_count", C.c_uint32)]
+
+
 class Reference(_Checker):
     """The reference implementation built from its own sources."""
     prefix = "ref_"
@@ -318,6 +324,27 @@ class Reference(_Checker):
         if status:
             raise ValueError(self.last_error())
         return out, conv_state, rec
+
+    def embedding_row(self, e, token: int) -> np.ndarray:
+        """mach_embedding_row (src/kernels.cpp:802-845)."""
+        arrays = [_c(e.packed, np.uint8), _c(e.minimum_f16, np.uint16), _c(e.maximum_f16, np.uint16),
+                  _c(e.exception_indexes, np.uint32), _c(e.exception_bf16, np.uint16)]
+        desc = _EmbeddingDesc(e.rows, e.columns, *[a.ctypes.data for a in arrays], len(arrays[3]))
+        out = np.zeros(e.columns, np.float32)
+        if self.lib.ref_embedding_row(C.byref(desc), C.c_uint32(token), ptr(out, f32p)):
+            raise ValueError(self.last_error())
+        return out
+
+
+    def sample_tokens(self, logits, temperature: float, top_p: float, seed: int, draws: int = 1) -> np.ndarray:
+        """`draws` consecutive sample_token calls (src/generation.cpp:208-276) on
+        one std::mt19937_64 seeded with `seed`."""
+        lg = _c(logits, np.float32)
+        out = np.zeros(draws, np.uint32)
+        if self.lib.ref_sample_tokens(ptr(lg, f32p), C.c_uint32(len(lg)), C.c_float(temperature), C.c_float(top_p),
+                                      C.c_uint64(seed), C.c_uint32(draws), ptr(out, u32p)):
+            raise ValueError(self.last_error())
+        return out
 
 
 def reference_available() -> bool:

@@ -748,3 +748,47 @@ int ref_linear_attention(const float *qkv, const float *gate, const float *alpha
 }
 
 } // extern "C"
+
+// The sampler and the embedding row of the decode loop: the reference's own
+// sample_token (src/generation.cpp:208-276) and mach_embedding_row
+// (src/kernels.cpp:802-845), called as they are.
+#include "adi/generation.hpp"
+
+#include <random>
+
+extern "C" {
+
+struct ref_embedding {
+    std::uint32_t rows, columns;
+    const std::uint8_t *packed;
+    const std::uint16_t *minimum_f16, *maximum_f16;
+    const std::uint32_t *exception_indexes;
+    const std::uint16_t *exception_bf16;
+    std::uint32_t exception_count;
+};
+
+int ref_embedding_row(const ref_embedding *e, std::uint32_t token, float *out) {
+    return guarded([&] {
+        const std::size_t groups = static_cast<std::size_t>(e->rows) * e->columns / 64;
+        adi::MachEmbedding view{
+            e->rows, e->columns,
+            {e->packed, static_cast<std::size_t>(e->rows) * e->columns / 2},
+            {e->minimum_f16, groups}, {e->maximum_f16, groups},
+            {e->exception_indexes, e->exception_count}, {e->exception_bf16, e->exception_count}};
+        adi::mach_embedding_row(view, token, std::span<float>(out, e->columns));
+    });
+}
+
+// Draws `draws` tokens from the same logits with one generator seeded by
+// `seed` (as one request's consecutive steps would).
+int ref_sample_tokens(const float *logits, std::uint32_t count, float temperature, float top_p,
+                      std::uint64_t seed, std::uint32_t draws, std::uint32_t *out) {
+    return guarded([&] {
+        std::mt19937_64 random(seed);
+        for (std::uint32_t i = 0; i < draws; ++i) {
+            out[i] = adi::sample_token(std::span<const float>(logits, count), temperature, top_p, random);
+        }
+    });
+}
+
+} // extern "C"

@@ -413,28 +413,45 @@ __global__ void __launch_bounds__(128) gd_conv_kernel(const __grid_constant__ Gd
     p.convolved[t * kGdChannels + c] = y;
 }
 
-// Reduces four values over the warp; lane ends with the total of value
-// lane/8.
-__device__ __forceinline__ float transpose_reduce4(float v0, float v1, float v2, float v3, uint32_t lane) {
-    const bool hi16 = (lane & 16) != 0;
-    float a = (hi16 ? v2 : v0) + __shfl_xor_sync(0xffffffffu, hi16 ? v0 : v2, 16);
-    float b = (hi16 ? v3 : v1) + __shfl_xor_sync(0xffffffffu, hi16 ? v1 : v3, 16);
-    const bool hi8 = (lane & 8) != 0;
-    float s = (hi8 ? b : a) + __shfl_xor_sync(0xffffffffu, hi8 ? a : b, 8);
-    s += __shfl_xor_sync(0xffffffffu, s, 4);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    return s;
+constexpr uint32_t kGdChunk = 32;      // tokens staged per shared-memory buffer
+constexpr uint32_t kGdBlockRows = 32;  // state rows per block: 8 warps x 4 rows
+
+struct GdStage {
+    float qk[kGdChunk][2][kGdHeadSize];  // the key head's query and key rows
+    float v[kGdChunk][kGdBlockRows];     // this block's rows of the value head
+    float alpha[kGdChunk], beta[kGdChunk];
+    float decay[kGdChunk], gain[kGdChunk];  // exp(-A softplus(alpha + bias)), sigmoid(beta)
+};
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *smem, const void *gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // Per (32-row slice, value head, sequence): the recurrence over the
-// sequence's tokens (src/executor.cpp:123-144, src/simd.cpp:108-127). Block
-// x = 0 of each head also advances the convolution state of 256 channels.
+// sequence's tokens (src/executor.cpp:123-144, src/simd.cpp:108-127).
+// Eight lanes share a state row, 16 columns each, so each of the token's two
+// row sums takes three shuffles; the tokens' query, key and value rows are
+// staged 32 at a time into shared memory by cp.async, one chunk ahead of
+// the chunk being computed, and the per-token decay and gain are computed
+// once per chunk. Block x = 0 of each head also advances the convolution
+// state of 256 channels.
 __global__ void __launch_bounds__(256) gd_recurrence_kernel(const __grid_constant__ GdParams p) {
+    extern __shared__ __align__(16) uint8_t gd_smem[];
+    GdStage *stage = reinterpret_cast<GdStage *>(gd_smem);  // [2]
     const SeqDesc sq = p.seqs[blockIdx.z];
     if (!sequence_in_range(sq, p.tokens, p.slots, 0, p.error) || sq.count == 0) return;
     const uint32_t head = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t row0 = blockIdx.x * 32 + warp * 4;
+    const uint32_t block_row0 = blockIdx.x * kGdBlockRows;
+    const uint32_t my_row = warp * 4 + (lane >> 3);  // within the block
+    const uint32_t col0 = (lane & 7) * 16;
     const uint32_t kh = head / (kGdValueHeads / kGdKeyHeads);
 
     if (blockIdx.x == 0) {
@@ -451,62 +468,117 @@ __global__ void __launch_bounds__(256) gd_recurrence_kernel(const __grid_constan
         st[0] = next[0], st[1] = next[1], st[2] = next[2];
     }
 
-    float *S = p.recurrent + (((size_t)sq.slot * kGdValueHeads + head) * kGdHeadSize + row0) * kGdHeadSize + 4 * lane;
-    float4 s[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) s[i] = *reinterpret_cast<const float4 *>(S + i * kGdHeadSize);
     const float alpha_bias = bf16_bits_to_f32(p.alpha_bias[head]);
     const float A = expf(bf16_bits_to_f32(p.a_log[head]));
     const float out_scale = 1.0f / sqrtf(static_cast<float>(kGdHeadSize));
-    const uint32_t my_row = lane >> 3;
 
-    struct Tok {
-        float4 q, k, v;
-        float a, b;
-    };
-    auto load = [&](uint32_t i) {
-        const size_t t = sq.first + i;
-        const float *cv = p.convolved + t * kGdChannels;
-        Tok x;
-        x.q = *reinterpret_cast<const float4 *>(cv + kh * kGdHeadSize + 4 * lane);
-        x.k = *reinterpret_cast<const float4 *>(cv + kGdQkSize + kh * kGdHeadSize + 4 * lane);
-        x.v = *reinterpret_cast<const float4 *>(cv + 2 * kGdQkSize + head * kGdHeadSize + row0);
-        x.a = p.alpha[t * kGdValueHeads + head];
-        x.b = p.beta[t * kGdValueHeads + head];
-        return x;
-    };
-    Tok cur = load(0);
-    for (uint32_t i = 0; i < sq.count; ++i) {
-        const Tok nxt = load(i + 1 < sq.count ? i + 1 : i);
-        const float beta = sigmoid(cur.b);
-        const float biased = cur.a + alpha_bias;
-        const float softplus = biased > 20.0f ? biased : log1pf(expf(biased));
-        const float decay = expf(-A * softplus);
-        float part[4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            s[r].x *= decay, s[r].y *= decay, s[r].z *= decay, s[r].w *= decay;
-            part[r] = s[r].x * cur.k.x + s[r].y * cur.k.y + s[r].z * cur.k.z + s[r].w * cur.k.w;
+    // Chunk c's rows into stage[c & 1] (cp.async, one group per chunk).
+    auto issue = [&](uint32_t chunk) {
+        GdStage &st = stage[chunk & 1];
+        const uint32_t t0 = chunk * kGdChunk;
+        const uint32_t n = min(kGdChunk, sq.count - t0);
+        // query and key rows: n tokens x 2 x 32 float4
+        for (uint32_t i = threadIdx.x; i < n * 64; i += blockDim.x) {
+            const uint32_t t = i / 64, w = i % 64, which = w / 32, q4 = w % 32;
+            const float *src = p.convolved + (size_t)(sq.first + t0 + t) * kGdChannels + which * kGdQkSize +
+                               kh * kGdHeadSize + 4 * q4;
+            // Columns 4*q4.. go to slot (q4 % 4) * 8 + q4 / 4: the 8 lanes of
+            // a row group then read 8 consecutive 16-byte slots (no bank
+            // conflict) for each of their four float4s.
+            cp_async16(&st.qk[t][which][4 * ((q4 % 4) * 8 + q4 / 4)], src);
         }
-        const float prediction = transpose_reduce4(part[0], part[1], part[2], part[3], lane);
-        const float value = my_row == 0 ? cur.v.x : my_row == 1 ? cur.v.y : my_row == 2 ? cur.v.z : cur.v.w;
-        const float delta = (value - prediction) * beta;
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const float dr = __shfl_sync(0xffffffffu, delta, 8 * r);
-            s[r].x = fmaf(cur.k.x, dr, s[r].x);
-            s[r].y = fmaf(cur.k.y, dr, s[r].y);
-            s[r].z = fmaf(cur.k.z, dr, s[r].z);
-            s[r].w = fmaf(cur.k.w, dr, s[r].w);
-            part[r] = s[r].x * cur.q.x + s[r].y * cur.q.y + s[r].z * cur.q.z + s[r].w * cur.q.w;
+        // value rows: n tokens x 8 float4
+        for (uint32_t i = threadIdx.x; i < n * (kGdBlockRows / 4); i += blockDim.x) {
+            const uint32_t t = i / (kGdBlockRows / 4), q4 = i % (kGdBlockRows / 4);
+            const float *src = p.convolved + (size_t)(sq.first + t0 + t) * kGdChannels + 2 * kGdQkSize +
+                               head * kGdHeadSize + block_row0 + 4 * q4;
+            cp_async16(&st.v[t][4 * q4], src);
         }
-        const float attended = transpose_reduce4(part[0], part[1], part[2], part[3], lane);
-        if ((lane & 7) == 0)
-            p.raw[(size_t)(sq.first + i) * kGdValueSize + head * kGdHeadSize + row0 + my_row] = attended * out_scale;
-        cur = nxt;
+        if (threadIdx.x < n) {
+            cp_async4(&st.alpha[threadIdx.x], p.alpha + (size_t)(sq.first + t0 + threadIdx.x) * kGdValueHeads + head);
+            cp_async4(&st.beta[threadIdx.x], p.beta + (size_t)(sq.first + t0 + threadIdx.x) * kGdValueHeads + head);
+        }
+        cp_async_commit();
+    };
+
+    float *S = p.recurrent + (((size_t)sq.slot * kGdValueHeads + head) * kGdHeadSize + block_row0 + my_row) *
+                                 kGdHeadSize + col0;
+    float s[16];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float4 v = *reinterpret_cast<const float4 *>(S + 4 * j);
+        s[4 * j] = v.x, s[4 * j + 1] = v.y, s[4 * j + 2] = v.z, s[4 * j + 3] = v.w;
+    }
+
+    const uint32_t chunks = (sq.count + kGdChunk - 1) / kGdChunk;
+    issue(0);
+    for (uint32_t chunk = 0; chunk < chunks; ++chunk) {
+        if (chunk + 1 < chunks) {
+            issue(chunk + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        GdStage &st = stage[chunk & 1];
+        const uint32_t n = min(kGdChunk, sq.count - chunk * kGdChunk);
+        if (threadIdx.x < n) {
+            const float biased = st.alpha[threadIdx.x] + alpha_bias;
+            const float softplus = biased > 20.0f ? biased : log1pf(expf(biased));
+            st.decay[threadIdx.x] = expf(-A * softplus);
+            st.gain[threadIdx.x] = sigmoid(st.beta[threadIdx.x]);
+        }
+        __syncthreads();
+        for (uint32_t t = 0; t < n; ++t) {
+            const float decay = st.decay[t], gain = st.gain[t];
+            float k[16], q[16];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t slot = 4 * (j * 8 + (lane & 7));  // columns col0 + 4j .. +3
+                const float4 kv = *reinterpret_cast<const float4 *>(&st.qk[t][1][slot]);
+                const float4 qv = *reinterpret_cast<const float4 *>(&st.qk[t][0][slot]);
+                k[4 * j] = kv.x, k[4 * j + 1] = kv.y, k[4 * j + 2] = kv.z, k[4 * j + 3] = kv.w;
+                q[4 * j] = qv.x, q[4 * j + 1] = qv.y, q[4 * j + 2] = qv.z, q[4 * j + 3] = qv.w;
+            }
+            float pa = 0.0f, pb = 0.0f, pc = 0.0f, pd = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+                s[j] *= decay, s[j + 1] *= decay, s[j + 2] *= decay, s[j + 3] *= decay;
+                pa = fmaf(s[j], k[j], pa);
+                pb = fmaf(s[j + 1], k[j + 1], pb);
+                pc = fmaf(s[j + 2], k[j + 2], pc);
+                pd = fmaf(s[j + 3], k[j + 3], pd);
+            }
+            float prediction = (pa + pb) + (pc + pd);
+            prediction += __shfl_xor_sync(0xffffffffu, prediction, 4);
+            prediction += __shfl_xor_sync(0xffffffffu, prediction, 2);
+            prediction += __shfl_xor_sync(0xffffffffu, prediction, 1);
+            const float delta = (st.v[t][my_row] - prediction) * gain;
+            float oa = 0.0f, ob = 0.0f, oc = 0.0f, od = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+                s[j] = fmaf(k[j], delta, s[j]);
+                s[j + 1] = fmaf(k[j + 1], delta, s[j + 1]);
+                s[j + 2] = fmaf(k[j + 2], delta, s[j + 2]);
+                s[j + 3] = fmaf(k[j + 3], delta, s[j + 3]);
+                oa = fmaf(s[j], q[j], oa);
+                ob = fmaf(s[j + 1], q[j + 1], ob);
+                oc = fmaf(s[j + 2], q[j + 2], oc);
+                od = fmaf(s[j + 3], q[j + 3], od);
+            }
+            float attended = (oa + ob) + (oc + od);
+            attended += __shfl_xor_sync(0xffffffffu, attended, 4);
+            attended += __shfl_xor_sync(0xffffffffu, attended, 2);
+            attended += __shfl_xor_sync(0xffffffffu, attended, 1);
+            if ((lane & 7) == 0)
+                p.raw[(size_t)(sq.first + chunk * kGdChunk + t) * kGdValueSize + head * kGdHeadSize + block_row0 +
+                      my_row] = attended * out_scale;
+        }
+        __syncthreads();  // stage[chunk & 1] is refilled by the issue two chunks on
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) *reinterpret_cast<float4 *>(S + i * kGdHeadSize) = s[i];
+    for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<float4 *>(S + 4 * j) = make_float4(s[4 * j], s[4 * j + 1], s[4 * j + 2], s[4 * j + 3]);
 }
 
 // Per (token, value head): RMS norm with weight offset 0, times silu of the
@@ -596,7 +668,14 @@ void launch_attention(const AttnParams &p, uint32_t sequences, uint32_t max_coun
 
 void launch_gated_delta(const GdParams &p, uint32_t sequences, uint32_t max_count, cudaStream_t s) {
     gd_conv_kernel<<<dim3(max_count, sequences, kGdChannels / kGdHeadSize), 128, 0, s>>>(p);
-    gd_recurrence_kernel<<<dim3(kGdHeadSize / 32, kGdValueHeads, sequences), 256, 0, s>>>(p);
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(gd_recurrence_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(2 * sizeof(GdStage)));
+        configured = true;
+    }
+    gd_recurrence_kernel<<<dim3(kGdHeadSize / kGdBlockRows, kGdValueHeads, sequences), 256, 2 * sizeof(GdStage), s>>>(
+        p);
     gd_norm_gate_kernel<<<dim3(max_count, sequences, kGdValueHeads), 128, 0, s>>>(p);
 }
 

@@ -28,7 +28,8 @@ on this host's cores, on the same 4096-token step.
 
 One GPU also reports C2 (the block at prefill ubatch 512 with its own
 router, near-uniform routing), a ubatch sweep (1/16/128/512), the C3 decode
-stack and the C5 stack; N GPUs also report the expert-parallel output
+stack, the C5 stack and the whole decode step of the 40-layer model through
+the device decoder (`decode_decoder`: attention, Gated DeltaNet, MoE, head); N GPUs also report the expert-parallel output
 checked against the one-GPU block (`ep_parity`) and the C5 stack with every
 block expert-parallel.
 
@@ -397,6 +398,100 @@ def decode_c3(ctx, stream, local, tokens_list=(1, 4), steps=20):
                              "graph_ms_per_step": graph_ms, "graph_gbs": step_bytes / graph_ms / 1e6,
                              "graph_tokens_per_s": T / (graph_ms / 1e3)}
     for h in moe_h + [head_h, ne_head_h] + [m for hs in ne_h for m in hs.values()]:
+        h.release()
+    return out
+
+
+DEC_HISTORY = 2048  # positions already in every sequence's cache at the decode steps
+
+
+def decode_decoder(ctx, stream, local, batches=(1, 4), steps=20):
+    """The whole decode step of the 40-layer model through the device
+    decoder stack (adi_cuda_decoder_step_device, replayed from one CUDA
+    graph): per layer the input norm, the attention half -- full attention
+    every fourth layer (NE q/k/v/o, head norms, RoPE, the cache), Gated
+    DeltaNet otherwise (NE qkv/z/o, bf16 a/b, convolution, recurrence, norm
+    and gate) -- the residual, the post-attention norm, the MoE block and its
+    residual; then the final norm and the int5 head. Every sequence first
+    holds DEC_HISTORY positions (one 2048-token prefill each, timed too).
+
+    Algorithmic bytes per step: every weight the step reads once (NE
+    projections, bf16 a/b, router, shared expert, the routed experts the
+    step touches -- 8 per token at batch 1; at batch B the expected number of
+    distinct experts under uniform routing, 256 (1 - (1 - 8/256)^B) -- and
+    the head) plus the per-sequence state: the caches' keys and values read
+    (DEC_HISTORY positions x 2 KV heads x 256 x 2 x 4 bytes per full layer)
+    and the Gated DeltaNet states read and written (32 x 128 x 128 x 4 bytes
+    x 2 per layer)."""
+    from adi_b200 import decoder, synthetic
+    device = f"cuda:{local}"
+    tluts = synthetic.model_tluts(4999, device=device)
+    blocks = [synthetic.moe_block(seed=9000 + d, device=device, tluts=tluts) for d in range(C3_DISTINCT)]
+    moe_h = [ctx.upload_moe_layer(b) for b in blocks]
+    layers = [decoder.synthetic_layer(9100 + i, i, blocks[i % C3_DISTINCT], device=device) for i in range(C3_LAYERS)]
+    weight_bytes = 0
+    for w in layers:
+        weight_bytes += sum(m.trellis.nbytes + m.su.nbytes + m.sv.nbytes + 4 for m in w.projections.values())
+        if not w.full_attention:
+            weight_bytes += w.alpha.nbytes + w.beta.nbytes
+    moe_shared = blocks[0].shared_bytes()
+    per_expert = blocks[0].packed_bytes_per_expert()
+    max_b = max(batches)
+    dec = decoder.DeviceDecoder(ctx, layers, slots=max_b, capacity=DEC_HISTORY + 64,
+                                moe_handles=[moe_h[i % C3_DISTINCT] for i in range(C3_LAYERS)])
+    head = synthetic.head_chunk(9200, C3_VOCAB, 2048, device=device)
+    head_h = ctx.upload_head(head)
+    head_bytes = head.packed_bytes()
+    del head, blocks
+    final = torch.zeros(2048, dtype=torch.int16, device=device)
+    out = {"layers": C3_LAYERS, "history": DEC_HISTORY,
+           "per_layer": "input norm; full attention (every 4th) or Gated DeltaNet with their NE projections; "
+                        "residual; norm; MoE block; residual", "head": f"int5_g64 {C3_VOCAB}x2048"}
+    with torch.cuda.stream(stream):
+        prompt = synthetic.activations(9300, DEC_HISTORY, 2048, device=device)
+        prefill_ms = []
+        for s in range(max_b):
+            h = prompt.clone()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            dec.forward([(s, DEC_HISTORY)], h)
+            b.record(stream)
+            stream.synchronize()
+            prefill_ms.append(a.elapsed_time(b))
+        out["prefill_2048"] = {"ms": min(prefill_ms), "tokens_per_s": DEC_HISTORY / (min(prefill_ms) / 1e3)}
+        for B in batches:
+            counts = [(s, 1) for s in range(B)]
+            x = synthetic.activations(9400 + B, B, 2048, device=device)
+            logits = torch.empty(B, C3_VOCAB, device=device)
+            table = dec.device_table(counts)
+            dec.step(table, counts, x, final, head_h, C3_VOCAB, logits)  # sizes the scratch before capture
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                dec.step(table, counts, x, final, head_h, C3_VOCAB, logits)
+            for _ in range(3):
+                graph.replay()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            b.record(stream)
+            stream.synchronize()
+            ctx.synchronize()  # the device checks of the table's entries
+            ms = a.elapsed_time(b) / steps
+            del graph
+            touched = 8.0 if B == 1 else 256 * (1 - (1 - 8 / 256) ** B)
+            state = B * (10 * DEC_HISTORY * 2 * 256 * 2 * 4 + 30 * 32 * 128 * 128 * 4 * 2)
+            step_bytes = weight_bytes + C3_LAYERS * (moe_shared + touched * per_expert) + head_bytes + state
+            out[f"batch_{B}"] = {"graph_ms_per_step": ms, "tokens_per_s": B / (ms / 1e3),
+                                 "bytes_per_step": step_bytes, "state_bytes_per_step": state,
+                                 "experts_touched_per_layer": touched, "graph_gbs": step_bytes / ms / 1e6}
+            # The replays advanced every sequence; move them back.
+            dec.positions = [DEC_HISTORY + 1] * max_b
+            table.copy_(dec.device_table(counts))
+    dec.release()
+    head_h.release()
+    for h in moe_h:
         h.release()
     return out
 
@@ -988,6 +1083,10 @@ def run_ours(args, world, rank, local):
     c5 = stack_c5(ctx, stream, local)
     for v in c3.values():
         v["graph_frac_hbm"] = v["graph_gbs"] / hbm_peak
+    dd = decode_decoder(ctx, stream, local)
+    for k, v in dd.items():
+        if k.startswith("batch_"):
+            v["graph_frac_hbm"] = v["graph_gbs"] / hbm_peak
 
     baseline = None if args.no_baseline else cpu_baseline(blocks[0])
     line = {
@@ -1009,6 +1108,7 @@ def run_ours(args, world, rank, local):
                       "head": f"int5_g64 {C3_VOCAB}x2048; *_ne_head: NE codec padded to 2^18 rows, cropped",
                       **c3},
         "stack_c5": c5,
+        "decode_decoder": dd,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4 + T * (E + 1) * 4,
                 "d2h_bytes_per_step": T * H * 4, "steps": e2e_steps},
         # One block's upload through adi_cuda_upload_moe_layer (host arrays

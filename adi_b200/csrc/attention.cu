@@ -72,6 +72,8 @@ __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 // dimensions, and write the query back or the key and value into the cache
 // (src/executor.cpp:25-73, 640-672).
 __global__ void __launch_bounds__(256) attention_prep_kernel(const __grid_constant__ AttnPrepParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ float red[8];
     __shared__ float y[kAttnHeadSize];
     const SeqDesc sq = p.seqs[blockIdx.y];
@@ -132,6 +134,8 @@ __device__ __forceinline__ void transpose_reduce32(float (&v)[32], uint32_t lane
 
 template <int QT>
 __global__ void __launch_bounds__(256, 1) attention_kernel(const __grid_constant__ AttnParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     constexpr int KW = 8 / QT;                  // warps per query token
     constexpr int KPW = keys_per_warp<QT>();    // keys of a tile per warp
     constexpr int G = KPW / 4;                  // groups of four keys
@@ -354,6 +358,8 @@ __global__ void __launch_bounds__(256, 1) attention_kernel(const __grid_constant
 
 // Merges the splits of each (token, query head) and applies the gate.
 __global__ void __launch_bounds__(256) attention_combine_kernel(const __grid_constant__ AttnParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     const SeqDesc sq = p.seqs[blockIdx.y];
     const uint32_t li = blockIdx.x;
     if (li >= sq.count) return;
@@ -383,6 +389,8 @@ __global__ void __launch_bounds__(256) attention_combine_kernel(const __grid_con
 // last three inputs and this one, silu, and for the query and key heads the
 // l2 normalisation (src/executor.cpp:1071-1113).
 __global__ void __launch_bounds__(128) gd_conv_kernel(const __grid_constant__ GdParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ float red[4];
     const SeqDesc sq = p.seqs[blockIdx.y];
     const uint32_t li = blockIdx.x;
@@ -444,6 +452,8 @@ __device__ __forceinline__ void cp_async_wait() {
 // once per chunk. Block x = 0 of each head also advances the convolution
 // state of 256 channels.
 __global__ void __launch_bounds__(256) gd_recurrence_kernel(const __grid_constant__ GdParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     extern __shared__ __align__(16) uint8_t gd_smem[];
     GdStage *stage = reinterpret_cast<GdStage *>(gd_smem);  // [2]
     const SeqDesc sq = p.seqs[blockIdx.z];
@@ -584,6 +594,8 @@ __global__ void __launch_bounds__(256) gd_recurrence_kernel(const __grid_constan
 // Per (token, value head): RMS norm with weight offset 0, times silu of the
 // gate (src/executor.cpp:1158-1176).
 __global__ void __launch_bounds__(128) gd_norm_gate_kernel(const __grid_constant__ GdParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ float red[4];
     const SeqDesc sq = p.seqs[blockIdx.y];
     const uint32_t li = blockIdx.x;
@@ -599,6 +611,8 @@ __global__ void __launch_bounds__(128) gd_norm_gate_kernel(const __grid_constant
 // out[i] = hidden[last token of sequence i].
 __global__ void last_rows_kernel(const float4 *hidden, const SeqDesc *seqs, uint32_t quads, uint32_t tokens,
                                  uint32_t *error, float4 *out) {
+    griddep_launch_dependents();
+    griddep_wait();
     const SeqDesc sq = seqs[blockIdx.x];
     if (!sequence_in_range(sq, tokens, ~0u, 0, error) || sq.count == 0) return;
     const float4 *row = hidden + (size_t)(sq.first + sq.count - 1) * quads;
@@ -606,6 +620,8 @@ __global__ void last_rows_kernel(const float4 *hidden, const SeqDesc *seqs, uint
 }
 
 __global__ void advance_positions_kernel(SeqDesc *seqs, uint32_t n) {
+    griddep_launch_dependents();
+    griddep_wait();
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) seqs[i].position += seqs[i].count;
 }
@@ -614,12 +630,12 @@ __global__ void advance_positions_kernel(SeqDesc *seqs, uint32_t n) {
 
 void launch_last_rows(const float *hidden, const SeqDesc *seqs, uint32_t sequences, uint32_t hidden_size,
                       uint32_t tokens, uint32_t *error, float *out, cudaStream_t s) {
-    last_rows_kernel<<<sequences, 256, 0, s>>>(reinterpret_cast<const float4 *>(hidden), seqs, hidden_size / 4, tokens,
+    launch_pdl(last_rows_kernel, sequences, 256, 0, s, reinterpret_cast<const float4 *>(hidden), seqs, hidden_size / 4, tokens,
                                                 error, reinterpret_cast<float4 *>(out));
 }
 
 void launch_advance_positions(SeqDesc *seqs, uint32_t sequences, cudaStream_t s) {
-    advance_positions_kernel<<<(sequences + 255) / 256, 256, 0, s>>>(seqs, sequences);
+    launch_pdl(advance_positions_kernel, (sequences + 255) / 256, 256, 0, s, seqs, sequences);
 }
 
 size_t attention_smem_bytes(uint32_t tokens_per_block) {
@@ -641,7 +657,7 @@ void attention_splits(uint32_t sequences, uint32_t max_count, uint32_t max_end, 
 }
 
 void launch_attention_prep(const AttnPrepParams &p, uint32_t sequences, uint32_t max_count, cudaStream_t s) {
-    attention_prep_kernel<<<dim3(max_count, sequences, kAttnQueryHeads + kAttnKvHeads), 256, 0, s>>>(p);
+    launch_pdl(attention_prep_kernel, dim3(max_count, sequences, kAttnQueryHeads + kAttnKvHeads), 256, 0, s, p);
 }
 
 void launch_attention(const AttnParams &p, uint32_t sequences, uint32_t max_count, uint32_t tokens_per_block,
@@ -654,29 +670,29 @@ void launch_attention(const AttnParams &p, uint32_t sequences, uint32_t max_coun
             cudaFuncSetAttribute(attention_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             configured = true;
         }
-        attention_kernel<1><<<grid, 256, smem, s>>>(p);
+        launch_pdl(attention_kernel<1>, grid, 256, smem, s, p);
     } else {
         static bool configured = false;
         if (!configured) {
             cudaFuncSetAttribute(attention_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             configured = true;
         }
-        attention_kernel<8><<<grid, 256, smem, s>>>(p);
+        launch_pdl(attention_kernel<8>, grid, 256, smem, s, p);
     }
-    if (p.splits > 1) attention_combine_kernel<<<dim3(max_count, sequences, kAttnQueryHeads), 256, 0, s>>>(p);
+    if (p.splits > 1) launch_pdl(attention_combine_kernel, dim3(max_count, sequences, kAttnQueryHeads), 256, 0, s, p);
 }
 
 void launch_gated_delta(const GdParams &p, uint32_t sequences, uint32_t max_count, cudaStream_t s) {
-    gd_conv_kernel<<<dim3(max_count, sequences, kGdChannels / kGdHeadSize), 128, 0, s>>>(p);
+    launch_pdl(gd_conv_kernel, dim3(max_count, sequences, kGdChannels / kGdHeadSize), 128, 0, s, p);
     static bool configured = false;
     if (!configured) {
         cudaFuncSetAttribute(gd_recurrence_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)(2 * sizeof(GdStage)));
         configured = true;
     }
-    gd_recurrence_kernel<<<dim3(kGdHeadSize / kGdBlockRows, kGdValueHeads, sequences), 256, 2 * sizeof(GdStage), s>>>(
+    launch_pdl(gd_recurrence_kernel, dim3(kGdHeadSize / kGdBlockRows, kGdValueHeads, sequences), 256, 2 * sizeof(GdStage), s, 
         p);
-    gd_norm_gate_kernel<<<dim3(max_count, sequences, kGdValueHeads), 128, 0, s>>>(p);
+    launch_pdl(gd_norm_gate_kernel, dim3(max_count, sequences, kGdValueHeads), 128, 0, s, p);
 }
 
 }  // namespace adi_cuda

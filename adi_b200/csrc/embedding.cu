@@ -1,4 +1,5 @@
 #include "embedding.cuh"
+#include "pipeline.cuh"
 
 #include <cuda_fp16.h>
 
@@ -6,6 +7,8 @@ namespace adi_cuda {
 namespace {
 
 __global__ void __launch_bounds__(256) embedding_rows_kernel(const __grid_constant__ EmbeddingParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ uint32_t range[2];
     const uint32_t token = p.tokens[blockIdx.x];
     if (token >= p.rows) {
@@ -44,7 +47,7 @@ __global__ void __launch_bounds__(256) embedding_rows_kernel(const __grid_consta
 }  // namespace
 
 void launch_embedding_rows(const EmbeddingParams &p, uint32_t count, cudaStream_t s) {
-    if (count) embedding_rows_kernel<<<count, 256, 0, s>>>(p);
+    if (count) launch_pdl(embedding_rows_kernel, count, 256, 0, s, p);
 }
 
 }  // namespace adi_cuda

@@ -227,6 +227,8 @@ __device__ __forceinline__ float *return_row(const EpFinalizeParams &p, uint32_t
 
 template <int R>
 __global__ void __launch_bounds__(256) ep_finalize_regs_kernel(EpFinalizeParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ float sh[256 * R];
     constexpr uint32_t H = 256u * R;
     const uint32_t c0 = threadIdx.x * R;
@@ -273,6 +275,8 @@ __global__ void ep_finalize_kernel(EpFinalizeParams p) {
 
 template <int R>
 __global__ void __launch_bounds__(256, 4) ep_combine_regs_kernel(EpCombineParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ float sh[256 * R];
     constexpr uint32_t H = 256u * R;
     const uint32_t t = blockIdx.x, c0 = threadIdx.x * R;
@@ -370,9 +374,9 @@ void launch_ep_finalize(const EpFinalizeParams &p, cudaStream_t s) {
     if (p.positions == 0) return;
     const uint32_t grid = p.placed && p.positions > kEpLoopBlocks ? kEpLoopBlocks : p.positions;
     switch (p.hidden) {
-        case 512: ep_finalize_regs_kernel<2><<<grid, 256, 0, s>>>(p); return;
-        case 1024: ep_finalize_regs_kernel<4><<<grid, 256, 0, s>>>(p); return;
-        case 2048: ep_finalize_regs_kernel<8><<<grid, 256, 0, s>>>(p); return;
+        case 512: launch_pdl(ep_finalize_regs_kernel<2>, grid, 256, 0, s, p); return;
+        case 1024: launch_pdl(ep_finalize_regs_kernel<4>, grid, 256, 0, s, p); return;
+        case 2048: launch_pdl(ep_finalize_regs_kernel<8>, grid, 256, 0, s, p); return;
         default: ep_finalize_kernel<<<grid, 256, p.hidden * sizeof(float), s>>>(p);
     }
 }
@@ -380,9 +384,9 @@ void launch_ep_finalize(const EpFinalizeParams &p, cudaStream_t s) {
 void launch_ep_combine(const EpCombineParams &p, cudaStream_t s) {
     if (p.tokens == 0) return;
     switch (p.hidden) {
-        case 512: ep_combine_regs_kernel<2><<<p.tokens, 256, 0, s>>>(p); return;
-        case 1024: ep_combine_regs_kernel<4><<<p.tokens, 256, 0, s>>>(p); return;
-        case 2048: ep_combine_regs_kernel<8><<<p.tokens, 256, 0, s>>>(p); return;
+        case 512: launch_pdl(ep_combine_regs_kernel<2>, p.tokens, 256, 0, s, p); return;
+        case 1024: launch_pdl(ep_combine_regs_kernel<4>, p.tokens, 256, 0, s, p); return;
+        case 2048: launch_pdl(ep_combine_regs_kernel<8>, p.tokens, 256, 0, s, p); return;
         default: {
             const uint32_t threads = (p.hidden + 7) / 8;
             ep_combine_kernel<<<p.tokens, threads < 32 ? 32 : threads, p.hidden * sizeof(float), s>>>(p);

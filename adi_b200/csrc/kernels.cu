@@ -186,6 +186,8 @@ __global__ void prep_kernel(PrepParams p) {
 // Register-resident variant for cols = 256 * R (thread t owns t*R .. +R-1).
 template <int R>
 __global__ void __launch_bounds__(256) prep_regs_kernel(PrepParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ float sh[256 * R];
     const uint32_t row_end = p.limit ? min(p.rows, *p.limit) : p.rows;
     for (uint32_t row = blockIdx.x; row < row_end; row += gridDim.x) {
@@ -210,11 +212,11 @@ void launch_prep(const PrepParams &p, cudaStream_t s) {
     if (p.rows == 0) return;
     dim3 grid(loop_grid(p.rows, p.limit), p.jobs);
     switch (p.cols) {
-        case 512: prep_regs_kernel<2><<<grid, 256, 0, s>>>(p); return;
-        case 1024: prep_regs_kernel<4><<<grid, 256, 0, s>>>(p); return;
-        case 2048: prep_regs_kernel<8><<<grid, 256, 0, s>>>(p); return;
-        case 4096: prep_regs_kernel<16><<<grid, 256, 0, s>>>(p); return;
-        case 8192: prep_regs_kernel<32><<<grid, 256, 0, s>>>(p); return;
+        case 512: launch_pdl(prep_regs_kernel<2>, grid, 256, 0, s, p); return;
+        case 1024: launch_pdl(prep_regs_kernel<4>, grid, 256, 0, s, p); return;
+        case 2048: launch_pdl(prep_regs_kernel<8>, grid, 256, 0, s, p); return;
+        case 4096: launch_pdl(prep_regs_kernel<16>, grid, 256, 0, s, p); return;
+        case 8192: launch_pdl(prep_regs_kernel<32>, grid, 256, 0, s, p); return;
         default: prep_kernel<<<grid, 256, p.cols * sizeof(float), s>>>(p);
     }
 }
@@ -711,6 +713,8 @@ struct NeStreamSmem {
 
 template <int NT>
 __global__ void __launch_bounds__((kNeStreamWarps + 1) * 32, 1) ne_stream_kernel(const NeGemmParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     using L = NeStreamSmem;
     extern __shared__ __align__(128) uint8_t smem[];
     float2 *table = reinterpret_cast<float2 *>(smem);
@@ -879,7 +883,7 @@ void launch_ne_stream(const NeGemmParams &p, int grid, cudaStream_t s) {
         cudaFuncSetAttribute(ne_stream_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)NeStreamSmem::total);
         configured = true;
     }
-    ne_stream_kernel<NT><<<grid, (kNeStreamWarps + 1) * 32, NeStreamSmem::total, s>>>(p);
+    launch_pdl(ne_stream_kernel<NT>, grid, (kNeStreamWarps + 1) * 32, NeStreamSmem::total, s, p);
 }
 
 template <int RT, int NT>
@@ -973,6 +977,8 @@ __global__ void __launch_bounds__(256) bf16_gemm_wide_kernel(const uint16_t *w0,
                                                              const uint16_t *w1, uint32_t rows1, const float *x,
                                                              uint32_t tokens, uint32_t cols, float *out,
                                                              uint32_t out_stride) {
+    griddep_launch_dependents();
+    griddep_wait();
     extern __shared__ float xs[];
     const uint32_t t0 = blockIdx.x * NT;
     const uint32_t nt = min((uint32_t)NT, tokens - t0);
@@ -1033,7 +1039,7 @@ void launch_bf16_wide(const uint16_t *w0, uint32_t rows0, const uint16_t *w1, ui
         configured = true;
     }
     dim3 grid((tokens + NT - 1) / NT, (rows0 + rows1 + 8 * RPW - 1) / (8 * RPW));
-    bf16_gemm_wide_kernel<NT, RPW><<<grid, 256, NT * cols * sizeof(float), s>>>(w0, rows0, w1, rows1, x, tokens,
+    launch_pdl(bf16_gemm_wide_kernel<NT, RPW>, grid, 256, NT * cols * sizeof(float), s, w0, rows0, w1, rows1, x, tokens,
                                                                               cols, out, out_stride);
 }
 
@@ -1404,6 +1410,8 @@ __global__ void route_place_kernel(RouteParams p) {
 constexpr uint32_t kSmallRoutes = 256;
 
 __global__ void __launch_bounds__(1024) route_small_kernel(RouteParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ uint32_t expert_of[kSmallRoutes];
     __shared__ uint32_t counts[1024], scan[1024], chunk_scan[1024];
     const uint32_t t = threadIdx.x, n = p.tokens * 8;
@@ -1621,7 +1629,7 @@ __global__ void __launch_bounds__(1024) route_block_kernel(RouteParams p) {
 
 uint32_t launch_route(const RouteParams &p, cudaStream_t s) {
     if (p.tokens * 8 <= kSmallRoutes && p.experts <= 1024) {
-        route_small_kernel<<<1, 1024, 0, s>>>(p);
+        launch_pdl(route_small_kernel, 1, 1024, 0, s, p);
         return 1;
     }
     const size_t block_smem = route_block_smem(p);
@@ -1690,6 +1698,8 @@ __global__ void mid_kernel(MidParams p) {
 
 template <int R>
 __global__ void __launch_bounds__(256) mid_regs_kernel(MidParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ float sh[256 * R];
     const uint32_t pos_end = p.limit ? min(p.positions, *p.limit) : p.positions;
     for (uint32_t pos = blockIdx.x; pos < pos_end; pos += gridDim.x) {
@@ -1729,9 +1739,9 @@ void launch_mid(const MidParams &p, cudaStream_t s) {
     if (p.positions == 0) return;
     const uint32_t blocks = loop_grid(p.positions, p.limit);
     switch (p.inner) {
-        case 512: mid_regs_kernel<2><<<blocks, 256, 0, s>>>(p); return;
-        case 1024: mid_regs_kernel<4><<<blocks, 256, 0, s>>>(p); return;
-        case 2048: mid_regs_kernel<8><<<blocks, 256, 0, s>>>(p); return;
+        case 512: launch_pdl(mid_regs_kernel<2>, blocks, 256, 0, s, p); return;
+        case 1024: launch_pdl(mid_regs_kernel<4>, blocks, 256, 0, s, p); return;
+        case 2048: launch_pdl(mid_regs_kernel<8>, blocks, 256, 0, s, p); return;
         default: mid_kernel<<<blocks, 256, 2 * p.inner * sizeof(float), s>>>(p);
     }
 }
@@ -1959,6 +1969,8 @@ __global__ void head_protected_kernel(HeadParams p) {
 // group scale, then the warp sum), so the results are identical.
 template <int NT>
 __global__ void __launch_bounds__(256) head_rows_kernel(HeadParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     constexpr uint32_t kGroups = 32, kBytes = 2048 / 8 * 5, kAhead = 4;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t first = blockIdx.x * (blockDim.x / 32) + warp, stride = gridDim.x * (blockDim.x / 32);
@@ -2036,9 +2048,9 @@ void launch_head(const HeadParams &p, cudaStream_t s) {
         }();
         const uint32_t blocks = min((p.rows + 7) / 8, (uint32_t)sms);
         if (p.batch == 1)
-            head_rows_kernel<1><<<blocks, 256, 0, s>>>(p);
+            launch_pdl(head_rows_kernel<1>, blocks, 256, 0, s, p);
         else
-            head_rows_kernel<2><<<blocks, 256, 0, s>>>(p);
+            launch_pdl(head_rows_kernel<2>, blocks, 256, 0, s, p);
         if (p.protected_count) head_protected_kernel<<<p.protected_count, 256, 0, s>>>(p);
         return;
     }
@@ -2099,6 +2111,8 @@ void launch_hadamard(float *values, uint32_t count, uint32_t n, float scale, cud
 
 __global__ void rms_norm_kernel(const float *x, const uint16_t *w, uint32_t n, float offset, float eps,
                                 float *out) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ float partial[32];
     const float *row = x + (size_t)blockIdx.x * n;
     float sq = 0.0f;
@@ -2120,12 +2134,14 @@ __global__ void rms_norm_kernel(const float *x, const uint16_t *w, uint32_t n, f
 void launch_rms_norm(const float *x, const uint16_t *w, uint32_t count, uint32_t n, float offset, float eps,
                      float *out, cudaStream_t s) {
     if (count == 0) return;
-    rms_norm_kernel<<<count, 256, 0, s>>>(x, w, n, offset, eps, out);
+    launch_pdl(rms_norm_kernel, count, 256, 0, s, x, w, n, offset, eps, out);
 }
 
 // hidden[i] += add[i]: the residual update after a block
 // (src/executor.cpp:1525-1527), one add per element.
 __global__ void residual_add_kernel(float4 *hidden, const float4 *add, size_t quads) {
+    griddep_launch_dependents();
+    griddep_wait();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < quads; i += (size_t)gridDim.x * blockDim.x) {
         float4 h = hidden[i];
         const float4 a = add[i];
@@ -2140,7 +2156,7 @@ __global__ void residual_add_kernel(float4 *hidden, const float4 *add, size_t qu
 void launch_residual_add(float *hidden, const float *add, size_t count, cudaStream_t s) {
     if (count == 0) return;
     const size_t quads = count / 4, blocks = (quads + 255) / 256;
-    residual_add_kernel<<<(unsigned)(blocks < 148 * 8 ? blocks : 148 * 8), 256, 0, s>>>(
+    launch_pdl(residual_add_kernel, (unsigned)(blocks < 148 * 8 ? blocks : 148 * 8), 256, 0, s, 
         reinterpret_cast<float4 *>(hidden), reinterpret_cast<const float4 *>(add), quads);
 }
 

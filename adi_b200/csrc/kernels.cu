@@ -1303,6 +1303,8 @@ bool launch_top_experts_parts(const float *partials, uint32_t parts, uint32_t ro
 // expert: a skewed routing would otherwise queue thousands of adds on one
 // address), and each route's bit in its expert's token bitmap.
 __global__ void route_count_kernel(RouteParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     extern __shared__ uint32_t block_counts[];
     for (uint32_t e = threadIdx.x; e < p.experts; e += blockDim.x) block_counts[e] = 0;
     __syncthreads();
@@ -1322,9 +1324,14 @@ __global__ void route_count_kernel(RouteParams p) {
 // One block of 1024 threads: offsets, per-expert word prefixes, the position
 // -> expert map and the GEMM work lists (ordered expert-major so that the
 // CTAs working on one expert run together and share its inputs in L2).
+constexpr uint32_t kScanStage = 32768;  // bitmap words whose popcounts route_scan stages
+
 __global__ void route_scan_kernel(RouteParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ uint32_t scan[1024];
     __shared__ uint32_t chunk_scan[1024];
+    __shared__ uint8_t stage[kScanStage];
     const uint32_t e = threadIdx.x;
     const uint32_t count = e < p.experts ? p.counts[e] : 0u;
     const uint32_t chunks = (count + p.chunk - 1) / p.chunk;
@@ -1372,11 +1379,22 @@ __global__ void route_scan_kernel(RouteParams p) {
         }
     }
     // Per-expert exclusive prefix of bitmap popcounts, one warp per expert.
+    // When they fit, every word's popcount is staged in shared memory first:
+    // all the block's bitmap loads are then in flight together instead of
+    // one dependent load per warp and step.
+    const bool staged = (size_t)p.experts * p.words <= kScanStage;
+    if (staged) {
+#pragma unroll 8
+        for (uint32_t i = threadIdx.x; i < p.experts * p.words; i += blockDim.x) stage[i] = (uint8_t)__popc(p.bitmap[i]);
+        __syncthreads();
+    }
     for (uint32_t ex = warp; ex < p.experts; ex += 32) {
         uint32_t running = 0;
         for (uint32_t w0 = 0; w0 < p.words; w0 += 32) {
             const uint32_t w = w0 + lane;
-            const uint32_t c = w < p.words ? __popc(p.bitmap[(size_t)ex * p.words + w]) : 0u;
+            const uint32_t c = w >= p.words ? 0u
+                               : staged   ? (uint32_t)stage[(size_t)ex * p.words + w]
+                                          : __popc(p.bitmap[(size_t)ex * p.words + w]);
             uint32_t incl = c;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -1390,6 +1408,8 @@ __global__ void route_scan_kernel(RouteParams p) {
 }
 
 __global__ void route_place_kernel(RouteParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= p.tokens * 8) return;
     const uint32_t t = i >> 3, e = p.route_experts[i];
@@ -1646,9 +1666,9 @@ uint32_t launch_route(const RouteParams &p, cudaStream_t s) {
     cudaMemsetAsync(p.counts, 0, sizeof(uint32_t) * p.experts, s);
     cudaMemsetAsync(p.bitmap, 0, sizeof(uint32_t) * (size_t)p.experts * p.words, s);
     const uint32_t n = p.tokens * 8;
-    route_count_kernel<<<(n + 255) / 256, 256, p.experts * sizeof(uint32_t), s>>>(p);
-    route_scan_kernel<<<1, 1024, 0, s>>>(p);
-    route_place_kernel<<<(n + 255) / 256, 256, 0, s>>>(p);
+    launch_pdl(route_count_kernel, (n + 255) / 256, 256, p.experts * sizeof(uint32_t), s, p);
+    launch_pdl(route_scan_kernel, 1, 1024, 0, s, p);
+    launch_pdl(route_place_kernel, (n + 255) / 256, 256, 0, s, p);
     return 3;
 }
 

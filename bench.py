@@ -88,6 +88,10 @@ def parse():
     ap.add_argument("--no-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-extras", action="store_true",
                     help="only the timed region: no e2e, ubatch sweep or CPU baseline (profiling runs)")
+    ap.add_argument("--profile", choices=["decode", "attention"],
+                    help="one warm step between cudaProfilerStart/Stop (for ncu --profile-from-start off), then "
+                         "exit: decode = the 40-layer batch-1 decode step through the device decoder; attention = "
+                         "a 2048-token Gated DeltaNet and full-attention prefill")
     return ap.parse_args()
 
 
@@ -1153,8 +1157,55 @@ def stage_breakdown(ctx, step, steps):
     return stages
 
 
+def profile_step(kind: str):
+    """One warm step of `kind` between cudaProfilerStart and Stop, for an ncu
+    launch list or capture of just that step."""
+    import adi_b200
+    from adi_b200 import attention, decoder, synthetic
+    ctx = adi_b200.Context(0)
+    ctx.set_precision(1)
+    ctx.set_stream(adi_b200.CUDA_STREAM_LEGACY)
+    if kind == "decode":
+        tluts = synthetic.model_tluts(4999, device="cuda")
+        blocks = [synthetic.moe_block(seed=9000 + d, device="cuda", tluts=tluts) for d in range(C3_DISTINCT)]
+        layers = [decoder.synthetic_layer(9100 + i, i, blocks[i % C3_DISTINCT]) for i in range(C3_LAYERS)]
+        dec = decoder.DeviceDecoder(ctx, layers, slots=1, capacity=DEC_HISTORY + 64)
+        head = ctx.upload_head(synthetic.head_chunk(9200, C3_VOCAB, 2048, device="cuda"))
+        final = torch.zeros(2048, dtype=torch.int16, device="cuda")
+        dec.forward([(0, DEC_HISTORY)], synthetic.activations(9300, DEC_HISTORY, 2048, device="cuda"))
+        x = synthetic.activations(9301, 1, 2048, device="cuda")
+        logits = torch.empty(1, C3_VOCAB, device="cuda")
+        run = lambda: dec.forward([(0, 1)], x, final, head, C3_VOCAB, logits)  # noqa: E731
+    else:
+        T = 2048
+        lw = attention.LinearAttentionDevice.upload(synthetic.linear_attention_weights(2))
+        fw = attention.FullAttentionDevice.upload(synthetic.full_attention_weights(1))
+        states = attention.LinearAttentionStates(1)
+        cache = attention.FullAttentionCache(1, T)
+        qkv, gate, alpha, beta = (torch.from_numpy(a).cuda() for a in synthetic.linear_attention_projections(3, T))
+        qg, k, v = (torch.from_numpy(a).cuda() for a in synthetic.full_attention_projections(4, T))
+        out = torch.empty(T, 4096, device="cuda")
+
+        def run():
+            cache.reset(0)  # host-side length only: both runs fill positions 0..T-1
+            attention.gated_delta(ctx, lw, states, [(0, T)], qkv, gate, alpha, beta, out)
+            attention.full_attention(ctx, fw, cache, [(0, T)], qg, k, v, out)
+    run()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    run()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    ctx.synchronize()
+    print(json.dumps({"profiled": kind, "launches": ctx.launch_count()}))
+    ctx.close()
+
+
 def main():
     args = parse()
+    if args.profile:
+        profile_step(args.profile)
+        return
     world, rank, local = setup_distributed()
     try:
         if args.impl == "reference":

@@ -2030,14 +2030,15 @@ void full_attention_run(adi_cuda_context *c, const uint16_t *query_norm, const u
 
 void gated_delta_run(adi_cuda_context *c, const uint16_t *convolution, const uint16_t *alpha_bias,
                      const uint16_t *a_log, const uint16_t *norm, const float *qkv, const float *gate,
-                     const float *alpha, const float *beta, uint32_t tokens, const SeqDesc *seqs, uint32_t n,
-                     const SeqBounds &b, float *convolution_state, float *recurrent_state, uint32_t slots,
-                     float *normalized) {
+                     const float *alpha, const float *beta, uint32_t ab_stride, uint32_t tokens,
+                     const SeqDesc *seqs, uint32_t n, const SeqBounds &b, float *convolution_state,
+                     float *recurrent_state, uint32_t slots, float *normalized) {
     GdParams gp{};
     gp.qkv = qkv;
     gp.gate = gate;
     gp.alpha = alpha;
     gp.beta = beta;
+    gp.ab_stride = ab_stride;
     gp.convolution = convolution;
     gp.alpha_bias = alpha_bias;
     gp.a_log = a_log;
@@ -2160,12 +2161,19 @@ void decoder_run(adi_cuda_context *c, const DecoderPlan &plan, SeqDesc *seqs, ui
     float *p1 = c->buffer<float>("dec_p1", size_t(tokens) * kGdValueSize);  // k and v, or gate
     float *p2 = c->buffer<float>("dec_p2", size_t(tokens) * kGdValueSize);  // attended, or normalized
     float *ab = c->buffer<float>("dec_ab", size_t(tokens) * 2 * kGdValueHeads);
-    for (const DecoderLayerDev &r : plan.layers) {
+    // Residual adds fuse with the norm that follows them (the same bits as
+    // the two kernels): after the attention half with the post-attention
+    // norm, after the MoE block with the next layer's input norm.
+    const bool fuse = H <= 8192;
+    for (size_t li = 0; li < plan.layers.size(); ++li) {
+        const DecoderLayerDev &r = plan.layers[li];
         const adi_cuda_decoder_layer &L = *r.desc;
-        c->stage(kStageNorm);
-        launch_rms_norm(hidden, L.input_norm_bf16, tokens, H, 1.0f, 1.0e-6f, normed, s);
-        c->stage_end();
-        c->after_launch(1);
+        if (li == 0 || !fuse) {
+            c->stage(kStageNorm);
+            launch_rms_norm(hidden, L.input_norm_bf16, tokens, H, 1.0f, 1.0e-6f, normed, s);
+            c->stage_end();
+            c->after_launch(1);
+        }
         if (L.full_attention) {
             float *kb = p1, *vb = p1 + size_t(tokens) * kAttnKvHeads * kAttnHeadSize;
             ne_group_dev(c, {NeDecodeCall{r.proj[0], normed, p0}, NeDecodeCall{r.proj[1], normed, kb},
@@ -2175,21 +2183,34 @@ void decoder_run(adi_cuda_context *c, const DecoderPlan &plan, SeqDesc *seqs, ui
                                L.value_cache, plan.slots, L.capacity, p2);
         } else {
             ne_group_dev(c, {NeDecodeCall{r.proj[0], normed, p0}, NeDecodeCall{r.proj[1], normed, p1}}, tokens);
-            float *al = ab, *be = ab + size_t(tokens) * kGdValueHeads;
-            bf16_matmul_dev(c, *r.alpha, normed, tokens, al);
-            bf16_matmul_dev(c, *r.beta, normed, tokens, be);
-            gated_delta_run(c, L.convolution_bf16, L.alpha_bias_bf16, L.a_log_bf16, L.norm_bf16, p0, p1, al, be, tokens,
-                            seqs, n, b, L.convolution_state, L.recurrent_state, plan.slots, p2);
+            // a and b in one launch: rows [a | b] per token, 64 floats apart.
+            c->stage(kStageBf16);
+            launch_bf16_gemm(r.alpha->values->as<uint16_t>(), kGdValueHeads, r.beta->values->as<uint16_t>(),
+                             kGdValueHeads, normed, tokens, H, ab, 2 * kGdValueHeads, s);
+            c->stage_end();
+            c->after_launch(1);
+            gated_delta_run(c, L.convolution_bf16, L.alpha_bias_bf16, L.a_log_bf16, L.norm_bf16, p0, p1, ab,
+                            ab + kGdValueHeads, 2 * kGdValueHeads, tokens, seqs, n, b, L.convolution_state,
+                            L.recurrent_state, plan.slots, p2);
         }
         ne_matmul_dev(c, *r.output, p2, tokens, attn);
         c->stage(kStageNorm);
-        launch_residual_add(hidden, attn, nh, s);
-        launch_rms_norm(hidden, L.post_attention_norm_bf16, tokens, H, 1.0f, 1.0e-6f, normed, s);
+        if (fuse) {
+            launch_add_rms_norm(hidden, attn, L.post_attention_norm_bf16, tokens, H, 1.0f, 1.0e-6f, normed, s);
+            c->after_launch(1);
+        } else {
+            launch_residual_add(hidden, attn, nh, s);
+            launch_rms_norm(hidden, L.post_attention_norm_bf16, tokens, H, 1.0f, 1.0e-6f, normed, s);
+            c->after_launch(2);
+        }
         c->stage_end();
-        c->after_launch(2);
         moe_forward_dev(c, *r.moe, normed, tokens, ff, nullptr, nullptr);
         c->stage(kStageNorm);
-        launch_residual_add(hidden, ff, nh, s);
+        if (fuse && li + 1 < plan.layers.size())
+            launch_add_rms_norm(hidden, ff, plan.layers[li + 1].desc->input_norm_bf16, tokens, H, 1.0f, 1.0e-6f,
+                                normed, s);
+        else
+            launch_residual_add(hidden, ff, nh, s);
         c->stage_end();
         c->after_launch(1);
     }
@@ -2851,8 +2872,9 @@ int adi_cuda_gated_delta_device(adi_cuda_context *c, const uint16_t *convolution
             invalid("linear attention buffers must be 16-byte aligned (the convolution weights 8-byte)");
         SeqBounds b;
         const SeqDesc *seqs = stage_sequences(c, sequences, sequence_count, tokens, slots, 0, &b);
-        gated_delta_run(c, convolution_bf16, alpha_bias_bf16, a_log_bf16, norm_bf16, qkv, gate, alpha, beta, tokens,
-                        seqs, sequence_count, b, convolution_state, recurrent_state, slots, normalized);
+        gated_delta_run(c, convolution_bf16, alpha_bias_bf16, a_log_bf16, norm_bf16, qkv, gate, alpha, beta,
+                        kGdValueHeads, tokens, seqs, sequence_count, b, convolution_state, recurrent_state, slots,
+                        normalized);
     });
 }
 

@@ -505,8 +505,8 @@ __global__ void __launch_bounds__(256) gd_recurrence_kernel(const __grid_constan
             cp_async16(&st.v[t][4 * q4], src);
         }
         if (threadIdx.x < n) {
-            cp_async4(&st.alpha[threadIdx.x], p.alpha + (size_t)(sq.first + t0 + threadIdx.x) * kGdValueHeads + head);
-            cp_async4(&st.beta[threadIdx.x], p.beta + (size_t)(sq.first + t0 + threadIdx.x) * kGdValueHeads + head);
+            cp_async4(&st.alpha[threadIdx.x], p.alpha + (size_t)(sq.first + t0 + threadIdx.x) * p.ab_stride + head);
+            cp_async4(&st.beta[threadIdx.x], p.beta + (size_t)(sq.first + t0 + threadIdx.x) * p.ab_stride + head);
         }
         cp_async_commit();
     };

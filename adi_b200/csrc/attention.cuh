@@ -67,7 +67,8 @@ struct AttnParams {
 };
 
 struct GdParams {
-    const float *qkv, *gate, *alpha, *beta;  // [tokens][8192], [tokens][4096], [tokens][32] x2
+    const float *qkv, *gate, *alpha, *beta;  // [tokens][8192], [tokens][4096], alpha/beta rows of ab_stride
+    uint32_t ab_stride;                      // floats between consecutive tokens' alpha (and beta) rows
     const uint16_t *convolution, *alpha_bias, *a_log, *norm;  // bf16
     const SeqDesc *seqs;
     float *conv_state;  // [slots][8192][3]

@@ -2157,6 +2157,55 @@ void launch_rms_norm(const float *x, const uint16_t *w, uint32_t count, uint32_t
     launch_pdl(rms_norm_kernel, count, 256, 0, s, x, w, n, offset, eps, out);
 }
 
+// hidden[row] += add[row], then out[row] = rms_norm(hidden[row]): the
+// residual update followed by the next norm (src/executor.cpp:1507-1520),
+// in one pass. The sum of squares runs in rms_norm_kernel's order (thread
+// t adds elements t, t + 256, ... with fmaf, then the same reductions), so
+// the output is the two kernels' bit for bit. n <= 256 * kAddNormMax.
+constexpr uint32_t kAddNormMax = 32;
+
+__global__ void add_rms_norm_kernel(float *hidden, const float *add, const uint16_t *w, uint32_t n, float offset,
+                                    float eps, float *out) {
+    griddep_launch_dependents();
+    griddep_wait();
+    __shared__ float partial[32];
+    float *row = hidden + (size_t)blockIdx.x * n;
+    const float *a = add + (size_t)blockIdx.x * n;
+    float v[kAddNormMax];
+    float sq = 0.0f;
+#pragma unroll
+    for (uint32_t k = 0; k < kAddNormMax; ++k) {
+        const uint32_t i = threadIdx.x + k * blockDim.x;
+        if (i < n) {
+            v[k] = row[i] + a[i];
+            row[i] = v[k];
+            sq = fmaf(v[k], v[k], sq);
+        }
+    }
+    sq = warp_sum(sq);
+    if ((threadIdx.x & 31u) == 0) partial[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float t = threadIdx.x < blockDim.x / 32 ? partial[threadIdx.x] : 0.0f;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) partial[0] = t;
+    }
+    __syncthreads();
+    const float scale = 1.0f / sqrtf(partial[0] / (float)n + eps);
+#pragma unroll
+    for (uint32_t k = 0; k < kAddNormMax; ++k) {
+        const uint32_t i = threadIdx.x + k * blockDim.x;
+        if (i < n) out[(size_t)blockIdx.x * n + i] = v[k] * scale * (offset + bf16_bits_to_f32(w[i]));
+    }
+}
+
+bool launch_add_rms_norm(float *hidden, const float *add, const uint16_t *w, uint32_t count, uint32_t n,
+                         float offset, float eps, float *out, cudaStream_t s) {
+    if (n > 256 * kAddNormMax) return false;
+    if (count) launch_pdl(add_rms_norm_kernel, count, 256, 0, s, hidden, add, w, n, offset, eps, out);
+    return true;
+}
+
 // hidden[i] += add[i]: the residual update after a block
 // (src/executor.cpp:1525-1527), one add per element.
 __global__ void residual_add_kernel(float4 *hidden, const float4 *add, size_t quads) {

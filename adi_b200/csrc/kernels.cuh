@@ -198,5 +198,10 @@ void launch_rms_norm(const float *x, const uint16_t *w, uint32_t count, uint32_t
                      float eps, float *out, cudaStream_t s);
 // hidden += add over `count` floats (a multiple of 4, 16-byte aligned).
 void launch_residual_add(float *hidden, const float *add, size_t count, cudaStream_t s);
+// hidden += add, then out = rms_norm(hidden) per row, in one launch; the same
+// bits as launch_residual_add followed by launch_rms_norm. Returns false
+// (launching nothing) when n is beyond its register tile (8192).
+bool launch_add_rms_norm(float *hidden, const float *add, const uint16_t *w, uint32_t count, uint32_t n,
+                         float offset, float eps, float *out, cudaStream_t s);
 
 }  // namespace adi_cuda

@@ -811,31 +811,53 @@ def run_ep(args, world, rank, local):
     value = C4_TOKENS * args.steps / (ms_max / 1e3)
     n_touched = [touched[k % (pool * L)] for k in range(args.steps)]
 
-    # End to end: pinned host tokens (and logits) in, outputs back, every step.
+    # End to end: pinned host tokens (and logits) in, outputs back, every
+    # step; inputs up on one copy stream, outputs down on another, both
+    # beside the block's kernels (two device input buffers in turn).
     x_host = torch.empty(pool, T, H, dtype=torch.float32, pin_memory=True)
     x_host.copy_(inputs.cpu())
     lg_host = None
     if logits is not None:
         lg_host = torch.empty(pool, T, E + 1, dtype=torch.float32, pin_memory=True)
         lg_host.copy_(logits.cpu())
-    lg_dev = torch.empty(T, E + 1, device=device)
-    y_host = torch.empty(T, H, dtype=torch.float32, pin_memory=True)
-    x_dev = torch.empty(T, H, device=device)
+    lg_dev = torch.empty(2, T, E + 1, device=device)
+    y_host = torch.empty(2, T, H, dtype=torch.float32, pin_memory=True)
+    x_dev = torch.empty(2, T, H, device=device)
+    up = torch.cuda.Stream(device=local)
+    down = torch.cuda.Stream(device=local)
     e2e_steps = max(1, min(args.steps, 200))
 
-    def e2e_step(k):
-        x_dev.copy_(x_host[k % pool], non_blocking=True)
-        if lg_host is not None:
-            lg_dev.copy_(lg_host[k % pool], non_blocking=True)
-        y_host.copy_(layers[k % L](x_dev, None if lg_host is None else lg_dev), non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+    def e2e_run(n):
+        loaded = [torch.cuda.Event() for _ in range(2)]
+        done = [torch.cuda.Event() for _ in range(2)]
 
-    for k in range(min(args.warmup, 5)):
-        e2e_step(k)
+        def load(k, b):
+            with torch.cuda.stream(up):
+                x_dev[b].copy_(x_host[k % pool], non_blocking=True)
+                if lg_host is not None:
+                    lg_dev[b].copy_(lg_host[k % pool], non_blocking=True)
+                loaded[b].record(up)
+
+        load(0, 0)
+        for k in range(n):
+            b = k % 2
+            if k + 1 < n:
+                if k >= 1:
+                    up.wait_event(done[1 - b])  # step k-1 has finished reading buffer 1-b
+                load(k + 1, 1 - b)
+            stream.wait_event(loaded[b])
+            y = layers[k % L](x_dev[b], None if lg_host is None else lg_dev[b])
+            done[b].record(stream)
+            with torch.cuda.stream(down):
+                down.wait_event(done[b])
+                y_host[b].copy_(y, non_blocking=True)
+                y.record_stream(down)
+        torch.cuda.synchronize()
+
+    e2e_run(min(args.warmup, 5) + 1)
     barrier(world)
     t0 = time.perf_counter()
-    for k in range(e2e_steps):
-        e2e_step(k)
+    e2e_run(e2e_steps)
     e2e_s = max_over_ranks(time.perf_counter() - t0, world)
     e2e_value = C4_TOKENS * e2e_steps / e2e_s
     c5 = stack_c5_ep(ctx, stream, local, rank, world, exchange) if not args.no_extras else None
@@ -995,8 +1017,10 @@ def run_ours(args, world, rank, local):
         return
 
     # End to end: the step's tokens and logits from pinned host memory, the
-    # outputs back, every step; the copies of step k+1's inputs overlap step
-    # k's kernels on a second stream (two device buffers in turn).
+    # outputs back, every step. Inputs go up on one copy stream and outputs
+    # come down on another (the two directions of the link run at once), both
+    # beside the kernels: step k+1's inputs load while step k computes and
+    # step k-1's outputs drain (two device buffers in turn).
     x_host = torch.empty(pool, T, H, dtype=torch.float32, pin_memory=True)
     x_host.copy_(inputs.cpu())
     lg_host = torch.empty(pool, T, E + 1, dtype=torch.float32, pin_memory=True)
@@ -1005,32 +1029,37 @@ def run_ours(args, world, rank, local):
     x_dev = torch.empty(2, T, H, device=device)
     lg_dev = torch.empty(2, T, E + 1, device=device)
     y_dev = torch.empty(2, T, H, device=device)
-    copies = torch.cuda.Stream(device=local)
+    up = torch.cuda.Stream(device=local)
+    down = torch.cuda.Stream(device=local)
     e2e_steps = max(1, min(args.steps, 200))
 
     def e2e_run(n):
         loaded = [torch.cuda.Event() for _ in range(2)]
         done = [torch.cuda.Event() for _ in range(2)]
-        with torch.cuda.stream(copies):
+        drained = [torch.cuda.Event() for _ in range(2)]
+        with torch.cuda.stream(up):
             x_dev[0].copy_(x_host[0], non_blocking=True)
             lg_dev[0].copy_(lg_host[0], non_blocking=True)
-            loaded[0].record(copies)
+            loaded[0].record(up)
         for k in range(n):
             b = k % 2
             if k + 1 < n:
-                with torch.cuda.stream(copies):
+                with torch.cuda.stream(up):
                     if k >= 1:
-                        copies.wait_event(done[1 - b])  # buffer 1-b's step k-1 has finished reading it
+                        up.wait_event(done[1 - b])  # step k-1 has finished reading buffer 1-b
                     x_dev[1 - b].copy_(x_host[(k + 1) % pool], non_blocking=True)
                     lg_dev[1 - b].copy_(lg_host[(k + 1) % pool], non_blocking=True)
-                    loaded[1 - b].record(copies)
+                    loaded[1 - b].record(up)
             stream.wait_event(loaded[b])
+            if k >= 2:
+                stream.wait_event(drained[b])  # step k-2's outputs have left buffer b
             ctx.moe_forward_batch_logits_device(handles[k % L], x_dev[b].data_ptr(), lg_dev[b].data_ptr(), T,
                                                 y_dev[b].data_ptr())
             done[b].record(stream)
-            with torch.cuda.stream(copies):
-                copies.wait_event(done[b])
+            with torch.cuda.stream(down):
+                down.wait_event(done[b])
                 y_host[b].copy_(y_dev[b], non_blocking=True)
+                drained[b].record(down)
         torch.cuda.synchronize()
 
     e2e_run(min(args.warmup, 5) + 1)

@@ -67,6 +67,11 @@ GAMMA_BYTES = 160 * 2
 # 512-token block, from one ncu capture of the current kernel; a change to
 # the kernel needs a new capture and a new value here.
 EXPERT_GEMM_TRAFFIC_T512 = (134.818560e6 + 20.356608e6 + 55.004928e6 + 19.981824e6) / 2
+# The same at C4 (4096 tokens, Zipf routing, one GPU): gate/up reads
+# 370.07 MB and writes 236.08 MB, down reads 84.45 MB and writes 473.76 MB
+# (profiles/tc_gemm_expert_c4_traffic.md). Most of it is the f16 inputs and
+# the two fp32 partial-sum halves, not the packed weights.
+EXPERT_GEMM_TRAFFIC_C4 = (370.070016e6 + 236.075776e6 + 84.445696e6 + 473.762304e6) / 2
 
 
 def parse():
@@ -1129,7 +1134,8 @@ def run_ours(args, world, rank, local):
         "dtype": "f16 operands, f32 accumulate" if args.precision else "f32", "data": "synthetic",
         "config": c4_config(H, E, blocks[0].expert_hidden, L),
         "parallelism": "one GPU: all experts, all tokens",
-        "roofline": expert_gemm_roofline(stages, n_touched, 8 * T),
+        "roofline": {**expert_gemm_roofline(stages, n_touched, 8 * T),
+                     "traffic": EXPERT_GEMM_TRAFFIC_C4 if args.precision == 1 else None},
         "block_hbm": {"achieved_gbs": block_gbs, "frac": block_gbs / hbm_peak,
                       "bytes_per_step": sum(block_bytes) / len(block_bytes),
                       "experts_touched_mean": sum(n_touched) / len(n_touched)},

@@ -4,7 +4,7 @@
 // the device (src/kernels.cpp:385-1050 of the reference), then calls the ABI;
 // ABI status 1 becomes std::invalid_argument, any other failure
 // std::runtime_error (the reference's "exceptions during setup, status at
-// request boundaries" policy, AGENTS.md:26).
+// request boundaries" policy, the reference's AGENTS.md:26).
 #include "cuda_backend.hpp"
 
 #include "adi/kernels.hpp"

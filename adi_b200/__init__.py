@@ -16,6 +16,7 @@ fails.
 from __future__ import annotations
 
 import ctypes as C
+import time
 from pathlib import Path
 from typing import Optional
 
@@ -357,18 +358,20 @@ class Context:
         _check(self.lib.adi_cuda_upload_bf16(self.ptr, C.byref(desc), C.byref(h)), "upload_bf16")
         return Handle(self, h.value, "bf16", v.shape[0], v.shape[1])
 
-    def upload_moe_layer(self, layer) -> Handle:
+    def upload_moe_layer(self, layer, timing: dict | None = None) -> Handle:
         """`layer` provides hidden, expert_hidden, experts, router [E][H] and
         shared_expert_gate [H] (bf16 bits), shared_gate/up/down (NE views) and
-        expert(e, projection) -> expert view, projection 0/1/2 = gate/up/down."""
-        return self._upload_moe(layer, 0, layer.experts)
+        expert(e, projection) -> expert view, projection 0/1/2 = gate/up/down.
+        `timing`, when given, receives the seconds of the C call alone
+        (`abi_s`), apart from building its descriptors here."""
+        return self._upload_moe(layer, 0, layer.experts, timing)
 
     def upload_moe_shard(self, layer, first_expert: int, expert_count: int) -> Handle:
         """Routed experts [first_expert, first_expert + expert_count) of
         `layer` plus its router and shared expert, for the ep_* phases."""
         return self._upload_moe(layer, first_expert, expert_count)
 
-    def _upload_moe(self, layer, first: int, count: int) -> Handle:
+    def _upload_moe(self, layer, first: int, count: int, timing: dict | None = None) -> Handle:
         keep: list = []
         E = layer.experts
         routed = (ExpertMatrixDesc * (3 * E))()
@@ -385,11 +388,14 @@ class Context:
                             self.ne_desc(layer.shared_down, keep),
                             C.cast(routed, C.POINTER(ExpertMatrixDesc)))
         h = C.c_uint64()
+        start = time.perf_counter()
         if first == 0 and count == E:
             _check(self.lib.adi_cuda_upload_moe_layer(self.ptr, C.byref(desc), C.byref(h)), "upload_moe_layer")
         else:
             _check(self.lib.adi_cuda_upload_moe_shard(self.ptr, C.byref(desc), first, count, C.byref(h)),
                    "upload_moe_shard")
+        if timing is not None:
+            timing["abi_s"] = time.perf_counter() - start
         return Handle(self, h.value, "moe", layer.hidden, layer.hidden)
 
     # -- the Backend table operations, host arrays ---------------------------

@@ -498,6 +498,17 @@ def decode_decoder(ctx, stream, local, batches=(1, 4), steps=20):
             # The replays advanced every sequence; move them back.
             dec.positions = [DEC_HISTORY + 1] * max_b
             table.copy_(dec.device_table(counts))
+            # Where a step's time goes: one more step with every stage
+            # bracketed by events (the brackets serialise the kernels, so the
+            # stages add up to more than the graph's step).
+            ctx.set_profiling(True)
+            ctx.reset_profile()
+            dec.step(table, counts, x, final, head_h, C3_VOCAB, logits)
+            stream.synchronize()
+            out[f"batch_{B}"]["stages_ms_per_step"] = {k: v[0] for k, v in ctx.profile().items()}
+            ctx.set_profiling(False)
+            dec.positions = [DEC_HISTORY + 1] * max_b
+            table.copy_(dec.device_table(counts))
     dec.release()
     head_h.release()
     for h in moe_h:

@@ -186,3 +186,45 @@ def test_decoder_step_graph_replays_match_eager():
         graphed.release()
     finally:
         ctx.close()
+
+
+def test_decoder_ne_head_cropped_and_full_cache(reference):
+    """The stack with the NE-coded head (8192 rows cropped to a 6000-token
+    vocabulary, as the model file pads the head to a power of two) against
+    the reference's mach_ne_matmul on the padded head; the caches filled to
+    their last position (a 24-token prefill and 8 decode steps into a
+    32-position cache), and one step past them refused on the host."""
+    import torch
+    import adi_b200
+    from adi_b200 import decoder, synthetic
+
+    block = synthetic.moe_block(seed=0xE00, scale_mu=-2.0, device="cuda")
+    layers = [decoder.synthetic_layer(0xE010 + i, i, block) for i in range(LAYERS)]
+    head = synthetic.ne_matrix(0xE020, 8192, H, device="cuda")
+    final = synthetic._bf16_bits(np.random.default_rng(0xE021).normal(0, 0.1, H))
+    rs = RefStack(reference, layers, final, synthetic.head_chunk(0xE022, 64, H, device="cuda"))
+    kept = 6000
+    ctx = adi_b200.Context(0)
+    try:
+        ctx.set_stream(adi_b200.CUDA_STREAM_LEGACY)
+        dec = decoder.DeviceDecoder(ctx, layers, slots=1, capacity=32)
+        head_h = ctx.upload_ne(head)
+        dfinal = torch.from_numpy(final.view(np.int16)).cuda()
+        for k, count in enumerate([24] + [1] * 8):
+            x = synthetic.activations(0xE030 + k, count, H, device="cpu").numpy()
+            hidden = torch.from_numpy(x).cuda()
+            logits = torch.full((1, kept), float("nan"), device="cuda")
+            dec.forward([(0, count)], hidden, dfinal, head_h, kept, logits)
+            ctx.synchronize()
+            want_h, _ = rs.forward([(0, count)], x)
+            normed = rs.norm(want_h[-1:], final)
+            want = reference.ne_matmul(head, normed)[:, :kept]
+            assert rel_l2(hidden.cpu().numpy() - x, want_h - x) <= TOL, k
+            assert rel_l2(logits.cpu().numpy(), want) <= TOL, k
+        assert dec.positions[0] == 32
+        with pytest.raises(ValueError):
+            dec.forward([(0, 1)], torch.zeros(1, H, device="cuda"))
+        head_h.release()
+        dec.release()
+    finally:
+        ctx.close()

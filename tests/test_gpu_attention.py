@@ -205,3 +205,19 @@ def test_gated_delta_long_prefill(ctx, reference):
     got, want = rig.step([(0, 1024)], seed=90)
     assert rel_l2(got, want) <= TOL
     rig.check_states(0)
+
+
+def test_full_attention_chunk_over_long_history(ctx, reference):
+    """A 20-token chunk on a 2000-token history, and then a mixed batch of
+    that sequence and two short ones: few query tiles of eight tokens over a
+    long key range, so the key range splits over blocks and blocks whose
+    split lies past a token's position merge as empty."""
+    rig = FullRig(ctx, reference, slots=3, capacity=4096, seed=12)
+    rig.step([(0, 2000)], seed=120)
+    got, want = rig.step([(0, 20)], seed=121)
+    assert rel_l2(got, want) <= TOL
+    rig.step([(1, 3)], seed=122)
+    got, want = rig.step([(2, 9), (0, 2), (1, 1)], seed=123)
+    assert rel_l2(got, want) <= TOL
+    for s in range(3):
+        rig.check_cache(s)

@@ -1321,50 +1321,72 @@ __global__ void route_count_kernel(RouteParams p) {
         if (block_counts[e]) atomicAdd(p.counts + e, block_counts[e]);
 }
 
-// One block of 1024 threads: offsets, per-expert word prefixes, the position
-// -> expert map and the GEMM work lists (ordered expert-major so that the
-// CTAs working on one expert run together and share its inputs in L2).
-constexpr uint32_t kScanStage = 32768;  // bitmap words whose popcounts route_scan stages
+// Offsets, per-expert bitmap-word prefixes, the position -> expert map and
+// the GEMM work lists (ordered expert-major so that the CTAs working on one
+// expert run together and share its inputs in L2), over many blocks: every
+// block scans the expert counts itself (at most 1024, four per thread), then
+// warp w of block b takes expert 8b + w (its work items and its bitmap
+// prefix) and the block's threads fill a grid-stride share of the position
+// -> expert map. The outputs are the same whichever block writes them.
+constexpr uint32_t kListsThreads = 256;
+constexpr uint32_t kListsWarps = kListsThreads / 32;
 
-__global__ void route_scan_kernel(RouteParams p) {
+__global__ void __launch_bounds__(kListsThreads) route_lists_kernel(RouteParams p) {
     griddep_launch_dependents();
     griddep_wait();
-    __shared__ uint32_t scan[1024];
-    __shared__ uint32_t chunk_scan[1024];
-    __shared__ uint8_t stage[kScanStage];
-    const uint32_t e = threadIdx.x;
-    const uint32_t count = e < p.experts ? p.counts[e] : 0u;
-    const uint32_t chunks = (count + p.chunk - 1) / p.chunk;
-    scan[e] = count;
-    chunk_scan[e] = chunks;
-    __syncthreads();
-    for (uint32_t o = 1; o < 1024; o <<= 1) {
-        const uint32_t a = e >= o ? scan[e - o] : 0u;
-        const uint32_t b = e >= o ? chunk_scan[e - o] : 0u;
-        __syncthreads();
-        scan[e] += a;
-        chunk_scan[e] += b;
-        __syncthreads();
+    __shared__ uint32_t scan[1024], chunk_scan[1024];  // inclusive, over experts
+    __shared__ uint32_t tot_a[kListsWarps], tot_b[kListsWarps];
+    const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+    uint32_t cnt[4], chk[4], sa = 0, sb = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t e = 4 * t + j;
+        cnt[j] = e < p.experts ? p.counts[e] : 0u;
+        chk[j] = (cnt[j] + p.chunk - 1) / p.chunk;
+        sa += cnt[j];
+        sb += chk[j];
     }
-    const uint32_t offset = scan[e] - count;
-    const uint32_t chunk_offset = chunk_scan[e] - chunks;
-    if (e < p.experts) p.offsets[e] = offset;
-    if (e == p.experts - 1) {
-        p.offsets[p.experts] = offset + count;
-        const uint32_t total_chunks = chunk_offset + chunks;
-        *p.count_gate_up = total_chunks * 2 * p.row_blocks_gate_up;
-        *p.count_down = total_chunks * p.row_blocks_down;
+    uint32_t a = sa, b = sb;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t va = __shfl_up_sync(0xffffffffu, a, o), vb = __shfl_up_sync(0xffffffffu, b, o);
+        if (lane >= (uint32_t)o) {
+            a += va;
+            b += vb;
+        }
     }
-    // The position -> expert map and the work items, a warp per expert (a
-    // popular expert's thousands of positions would serialise one thread).
+    if (lane == 31) {
+        tot_a[warp] = a;
+        tot_b[warp] = b;
+    }
     __syncthreads();
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    for (uint32_t ex = warp; ex < p.experts; ex += 32) {
-        const uint32_t ex_count = scan[ex] - (ex ? scan[ex - 1] : 0u);
-        const uint32_t ex_offset = scan[ex] - ex_count;
-        const uint32_t ex_chunks = (ex_count + p.chunk - 1) / p.chunk;
-        const uint32_t ex_chunk_offset = chunk_scan[ex] - ex_chunks;
-        for (uint32_t i = lane; i < ex_count; i += 32) p.pos_expert[ex_offset + i] = ex;
+    for (uint32_t w = 0; w < warp; ++w) {
+        a += tot_a[w];
+        b += tot_b[w];
+    }
+    a -= sa;  // exclusive: the experts before 4t
+    b -= sb;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        a += cnt[j];
+        b += chk[j];
+        scan[4 * t + j] = a;
+        chunk_scan[4 * t + j] = b;
+    }
+    __syncthreads();
+    const uint32_t E = p.experts, total = scan[E - 1];
+    if (blockIdx.x == 0) {
+        for (uint32_t e = t; e < E; e += kListsThreads) p.offsets[e] = e ? scan[e - 1] : 0u;
+        if (t == 0) {
+            p.offsets[E] = total;
+            *p.count_gate_up = chunk_scan[E - 1] * 2 * p.row_blocks_gate_up;
+            *p.count_down = chunk_scan[E - 1] * p.row_blocks_down;
+        }
+    }
+    const uint32_t ex = blockIdx.x * kListsWarps + warp;
+    if (ex < E) {
+        const uint32_t ex_offset = ex ? scan[ex - 1] : 0u, ex_count = scan[ex] - ex_offset;
+        const uint32_t ex_chunk_offset = ex ? chunk_scan[ex - 1] : 0u, ex_chunks = chunk_scan[ex] - ex_chunk_offset;
         const uint32_t per_chunk = 2 * p.row_blocks_gate_up;
         for (uint32_t k = lane; k < ex_chunks * per_chunk; k += 32) {
             const uint32_t c = k / per_chunk, j = (k % per_chunk) / p.row_blocks_gate_up, rb = k % p.row_blocks_gate_up;
@@ -1377,33 +1399,34 @@ __global__ void route_scan_kernel(RouteParams p) {
             const uint32_t pos0 = ex_offset + c * p.chunk, n = min(p.chunk, ex_count - c * p.chunk);
             p.items_down[(ex_chunk_offset + c) * p.row_blocks_down + rb] = make_uint4(ex, rb, pos0, n);
         }
-    }
-    // Per-expert exclusive prefix of bitmap popcounts, one warp per expert.
-    // When they fit, every word's popcount is staged in shared memory first:
-    // all the block's bitmap loads are then in flight together instead of
-    // one dependent load per warp and step.
-    const bool staged = (size_t)p.experts * p.words <= kScanStage;
-    if (staged) {
-#pragma unroll 8
-        for (uint32_t i = threadIdx.x; i < p.experts * p.words; i += blockDim.x) stage[i] = (uint8_t)__popc(p.bitmap[i]);
-        __syncthreads();
-    }
-    for (uint32_t ex = warp; ex < p.experts; ex += 32) {
+        // Exclusive prefix of the expert's bitmap-word popcounts.
+        const uint32_t *bits = p.bitmap + (size_t)ex * p.words;
+        uint32_t *prefix = p.prefix + (size_t)ex * p.words;
         uint32_t running = 0;
         for (uint32_t w0 = 0; w0 < p.words; w0 += 32) {
             const uint32_t w = w0 + lane;
-            const uint32_t c = w >= p.words ? 0u
-                               : staged   ? (uint32_t)stage[(size_t)ex * p.words + w]
-                                          : __popc(p.bitmap[(size_t)ex * p.words + w]);
+            const uint32_t c = w < p.words ? __popc(bits[w]) : 0u;
             uint32_t incl = c;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
                 if (lane >= (uint32_t)o) incl += v;
             }
-            if (w < p.words) p.prefix[(size_t)ex * p.words + w] = running + incl - c;
+            if (w < p.words) prefix[w] = running + incl - c;
             running += __shfl_sync(0xffffffffu, incl, 31);
         }
+    }
+    // Position -> expert: the first expert whose inclusive count passes it.
+    for (uint32_t pos = blockIdx.x * kListsThreads + t; pos < total; pos += gridDim.x * kListsThreads) {
+        uint32_t lo = 0, hi = E - 1;
+        while (lo < hi) {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (scan[mid] > pos)
+                hi = mid;
+            else
+                lo = mid + 1;
+        }
+        p.pos_expert[pos] = lo;
     }
 }
 
@@ -1423,7 +1446,7 @@ __global__ void route_place_kernel(RouteParams p) {
 
 // The whole routing of a small batch (at most kSmallRoutes routes) in one
 // block: counts by shared-memory atomics, the same scans and work lists as
-// route_scan_kernel, and each route's rank within its expert as the number
+// route_lists_kernel, and each route's rank within its expert as the number
 // of earlier routes to that expert -- the earlier tokens, as the bitmap
 // prefix counts them (a token names an expert at most once). Same outputs as
 // the three-kernel path.
@@ -1667,7 +1690,7 @@ uint32_t launch_route(const RouteParams &p, cudaStream_t s) {
     cudaMemsetAsync(p.bitmap, 0, sizeof(uint32_t) * (size_t)p.experts * p.words, s);
     const uint32_t n = p.tokens * 8;
     launch_pdl(route_count_kernel, (n + 255) / 256, 256, p.experts * sizeof(uint32_t), s, p);
-    launch_pdl(route_scan_kernel, 1, 1024, 0, s, p);
+    launch_pdl(route_lists_kernel, (p.experts + kListsWarps - 1) / kListsWarps, kListsThreads, 0, s, p);
     launch_pdl(route_place_kernel, (n + 255) / 256, 256, 0, s, p);
     return 3;
 }

@@ -431,6 +431,10 @@ struct GdStage {
     float decay[kGdChunk], gain[kGdChunk];  // exp(-A softplus(alpha + bias)), sigmoid(beta)
 };
 
+// Two stages and the output partials of one chunk.
+constexpr size_t kGdSmemBytes = 2 * sizeof(GdStage) + sizeof(float) * kGdChunk * kGdBlockRows * 8;
+static_assert(sizeof(GdStage) % 16 == 0, "the output partials are read as float4");
+
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
 }
@@ -445,8 +449,9 @@ __device__ __forceinline__ void cp_async_wait() {
 
 // Per (32-row slice, value head, sequence): the recurrence over the
 // sequence's tokens (src/executor.cpp:123-144, src/simd.cpp:108-127).
-// Eight lanes share a state row, 16 columns each, so each of the token's two
-// row sums takes three shuffles; the tokens' query, key and value rows are
+// Eight lanes share a state row, 16 columns each, so the prediction's row
+// sum takes three shuffles (the output's row sums are taken after each chunk
+// from lane partials in shared memory); the tokens' query, key and value rows are
 // staged 32 at a time into shared memory by cp.async, one chunk ahead of
 // the chunk being computed, and the per-token decay and gain are computed
 // once per chunk. Block x = 0 of each head also advances the convolution
@@ -456,6 +461,7 @@ __global__ void __launch_bounds__(256) gd_recurrence_kernel(const __grid_constan
     griddep_wait();
     extern __shared__ __align__(16) uint8_t gd_smem[];
     GdStage *stage = reinterpret_cast<GdStage *>(gd_smem);  // [2]
+    float *opart = reinterpret_cast<float *>(stage + 2);     // [kGdChunk][kGdBlockRows][8] output lane partials
     const SeqDesc sq = p.seqs[blockIdx.z];
     if (!sequence_in_range(sq, p.tokens, p.slots, 0, p.error) || sq.count == 0) return;
     const uint32_t head = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -576,15 +582,24 @@ __global__ void __launch_bounds__(256) gd_recurrence_kernel(const __grid_constan
                 oc = fmaf(s[j + 2], q[j + 2], oc);
                 od = fmaf(s[j + 3], q[j + 3], od);
             }
-            float attended = (oa + ob) + (oc + od);
-            attended += __shfl_xor_sync(0xffffffffu, attended, 4);
-            attended += __shfl_xor_sync(0xffffffffu, attended, 2);
-            attended += __shfl_xor_sync(0xffffffffu, attended, 1);
-            if ((lane & 7) == 0)
-                p.raw[(size_t)(sq.first + chunk * kGdChunk + t) * kGdValueSize + head * kGdHeadSize + block_row0 +
-                      my_row] = attended * out_scale;
+            // The output's row sum is no input of the next token: its lane
+            // partials wait in shared memory and are summed after the chunk,
+            // so that no shuffle of it holds up the recurrence.
+            opart[(t * kGdBlockRows + my_row) * 8 + (lane & 7)] = (oa + ob) + (oc + od);
         }
-        __syncthreads();  // stage[chunk & 1] is refilled by the issue two chunks on
+        __syncthreads();
+        // Row sums of the chunk's outputs: the tree of a three-step xor
+        // butterfly over the eight lanes, ((p0 + p4) + (p2 + p6)) + ((p1 + p5)
+        // + (p3 + p7)), a token's 32 rows per warp (coalesced stores).
+        for (uint32_t i = threadIdx.x; i < n * kGdBlockRows; i += blockDim.x) {
+            const float4 a = *reinterpret_cast<const float4 *>(&opart[i * 8]);
+            const float4 b = *reinterpret_cast<const float4 *>(&opart[i * 8 + 4]);
+            const float attended = ((a.x + b.x) + (a.z + b.z)) + ((a.y + b.y) + (a.w + b.w));
+            const uint32_t t = i / kGdBlockRows, row = i % kGdBlockRows;
+            p.raw[(size_t)(sq.first + chunk * kGdChunk + t) * kGdValueSize + head * kGdHeadSize + block_row0 + row] =
+                attended * out_scale;
+        }
+        __syncthreads();  // stage[chunk & 1] is refilled by the issue two chunks on, opart by the next chunk
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j)
@@ -686,12 +701,11 @@ void launch_gated_delta(const GdParams &p, uint32_t sequences, uint32_t max_coun
     launch_pdl(gd_conv_kernel, dim3(max_count, sequences, kGdChannels / kGdHeadSize), 128, 0, s, p);
     static bool configured = false;
     if (!configured) {
-        cudaFuncSetAttribute(gd_recurrence_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(2 * sizeof(GdStage)));
+        cudaFuncSetAttribute(gd_recurrence_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGdSmemBytes);
         configured = true;
     }
-    launch_pdl(gd_recurrence_kernel, dim3(kGdHeadSize / kGdBlockRows, kGdValueHeads, sequences), 256, 2 * sizeof(GdStage), s, 
-        p);
+    launch_pdl(gd_recurrence_kernel, dim3(kGdHeadSize / kGdBlockRows, kGdValueHeads, sequences), 256, kGdSmemBytes, s,
+               p);
     launch_pdl(gd_norm_gate_kernel, dim3(max_count, sequences, kGdValueHeads), 128, 0, s, p);
 }
 

@@ -18,7 +18,7 @@ PACKAGE = Path(__file__).resolve().parent
 ROOT = PACKAGE.parent
 CSRC = PACKAGE / "csrc"
 LIBRARY = PACKAGE / "libadi_cuda.so"
-SOURCES = ["kernels.cu", "tc_gemm.cu", "ep.cu", "decode.cu", "attention.cu", "embedding.cu", "abi.cu", "batcher.cpp"]
+SOURCES = ["kernels.cu", "tc_gemm.cu", "ep.cu", "decode.cu", "attention.cu", "attention_tc.cu", "embedding.cu", "abi.cu", "batcher.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -2004,6 +2004,24 @@ void full_attention_run(adi_cuda_context *c, const uint16_t *query_norm, const u
     for (uint32_t i = 0; i < kAttnRopeHalf; ++i)
         pp.divisors[i] = std::pow(10000000.0f, 2.0f * static_cast<float>(i) / 64.0f);
     launch_attention_prep(pp, n, b.max_count, s);
+    if (c->precision == 1 && b.max_count >= kAttnTcMinTokens) {
+        // Prefill chunks on the tensor cores.
+        AttnParams ap{};
+        ap.query_gate = query_gate;
+        ap.key_cache = key_cache;
+        ap.value_cache = value_cache;
+        ap.capacity = capacity;
+        ap.tokens = tokens;
+        ap.slots = slots;
+        ap.seqs = seqs;
+        ap.attended = attended;
+        ap.splits = 1;
+        ap.error = c->error_word;
+        launch_attention_tc(ap, n, b.max_count, s);
+        c->stage_end();
+        c->after_launch(2);
+        return;
+    }
     uint32_t splits = 1, split_keys = 0, tpb = 1;
     attention_splits(n, b.max_count, b.max_end, static_cast<uint32_t>(c->sms), &splits, &split_keys, &tpb);
     AttnParams ap{};

@@ -51,17 +51,6 @@ __device__ __forceinline__ float block_total(float v, float *red) {
     return t;
 }
 
-// A table entry lies inside the call's buffers (capacity 0: no cache). The
-// check is uniform over a block, which returns before any barrier when it
-// fails.
-__device__ __forceinline__ bool sequence_in_range(const SeqDesc &sq, uint32_t tokens, uint32_t slots,
-                                                  uint32_t capacity, uint32_t *error) {
-    const bool ok = sq.slot < slots && sq.count <= tokens && sq.first <= tokens - sq.count &&
-                    (capacity == 0 || (sq.position <= capacity && sq.count <= capacity - sq.position));
-    if (!ok && threadIdx.x == 0) atomicOr(error, kErrorSequence);
-    return ok;
-}
-
 __device__ __forceinline__ float sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 

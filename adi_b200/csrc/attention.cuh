@@ -43,6 +43,17 @@ struct SeqDesc {
 // rows or positions outside the call's buffers; its work was skipped.
 constexpr uint32_t kErrorSequence = 4u;
 
+// A table entry lies inside the call's buffers (capacity 0: no cache). The
+// check is uniform over a block, which returns before any barrier when it
+// fails.
+__device__ __forceinline__ bool sequence_in_range(const SeqDesc &sq, uint32_t tokens, uint32_t slots,
+                                                  uint32_t capacity, uint32_t *error) {
+    const bool ok = sq.slot < slots && sq.count <= tokens && sq.first <= tokens - sq.count &&
+                    (capacity == 0 || (sq.position <= capacity && sq.count <= capacity - sq.position));
+    if (!ok && threadIdx.x == 0) atomicOr(error, kErrorSequence);
+    return ok;
+}
+
 struct AttnPrepParams {
     float *query_gate;                  // [tokens][16][512]; queries rewritten in place
     const float *key, *value;           // [tokens][2][256]
@@ -90,6 +101,13 @@ void attention_splits(uint32_t sequences, uint32_t max_count, uint32_t max_end, 
 void launch_attention_prep(const AttnPrepParams &p, uint32_t sequences, uint32_t max_count, cudaStream_t s);
 void launch_attention(const AttnParams &p, uint32_t sequences, uint32_t max_count, uint32_t tokens_per_block,
                       cudaStream_t s);
+// The same attention on tcgen05 tensor cores (attention_tc.cu): f16 Q, K,
+// V and P with fp32 accumulation and an fp32 online softmax; one CTA per
+// (KV head, 16 query tokens, sequence) walks the whole causal key range (no
+// split: p.splits must be 1). For the tensor-core precision mode's prefill
+// chunks, from kAttnTcMinTokens tokens in a sequence.
+constexpr uint32_t kAttnTcMinTokens = 64;
+void launch_attention_tc(const AttnParams &p, uint32_t sequences, uint32_t max_count, cudaStream_t s);
 void launch_gated_delta(const GdParams &p, uint32_t sequences, uint32_t max_count, cudaStream_t s);
 // Adds each sequence's count to its position (a device-resident table after
 // a step, so a replayed step continues where the last one ended).

@@ -221,3 +221,32 @@ def test_full_attention_chunk_over_long_history(ctx, reference):
     assert rel_l2(got, want) <= TOL
     for s in range(3):
         rig.check_cache(s)
+
+
+TC_TOL = 1e-2  # f16 Q, K, V and P with fp32 accumulation (observed about 1e-3)
+
+
+def test_full_attention_tensor_core_prefill(reference):
+    """Precision mode 1 sends calls whose longest sequence has at least 64
+    tokens to the tcgen05 kernel (attention_tc.cu): a 300-token prefill
+    (ragged query and key tiles), a 77-token chunk over that history, a
+    short chunk on the fp32 kernel, then a mixed batch whose longest
+    sequence takes the tensor-core kernel with a decode token and a short
+    chunk riding along. Outputs within 1e-2 relative L2 of the reference,
+    per token as well; the caches as the fp32 path leaves them."""
+    import adi_b200
+    c = adi_b200.Context(0)
+    try:
+        c.set_stream(adi_b200.CUDA_STREAM_LEGACY)
+        c.set_precision(1)
+        rig = FullRig(c, reference, slots=3, capacity=1024, seed=13)
+        for counts, seed in (([(0, 300)], 130), ([(0, 77)], 131), ([(1, 5)], 132),
+                             ([(2, 100), (1, 1), (0, 3)], 133)):
+            got, want = rig.step(counts, seed=seed)
+            assert rel_l2(got, want) <= TC_TOL, counts
+            for t in range(len(got)):
+                assert rel_l2(got[t], want[t]) <= TC_TOL, (counts, t)
+        for s in range(3):
+            rig.check_cache(s)
+    finally:
+        c.close()

@@ -12,9 +12,12 @@
 // layout of tcgen05.cuh: the queries and cached keys and values are
 // converted from fp32 as they are staged (V transposed, so that its K
 // dimension -- the key positions -- is contiguous). S and O are fp32 in
-// tensor memory (columns 0-63 and 64-319). A thread of warps 0-3 owns one
-// row (its TMEM lane): it reads the row's scores, keeps the row's running
-// maximum m and denominator l, and writes the row of P. O is rescaled (a
+// tensor memory (columns 0-63 and 64-319). Keys and values are double
+// buffered: while the tensor cores and warps 0-3 work on one tile, the
+// producer warps (4 on) load and convert the next into the other buffers
+// (the commit after a tile's PV MMAs frees them). A thread of warps 0-3
+// owns one row (its TMEM lane): it reads the row's scores, keeps the row's
+// running maximum m and denominator l, and writes the row of P. O is rescaled (a
 // read-modify-write of tensor memory) only when a row's maximum grows by
 // more than kRescaleMargin (in log2 units): until then p = 2^(x - m) stays
 // below 2^8, well inside f16, and the final O / l is the same quotient an
@@ -43,19 +46,27 @@ namespace {
 constexpr uint32_t kTcQTokens = 16;                   // query tokens per CTA
 constexpr uint32_t kTcRows = kTcQTokens * kAttnGroup;  // 128 MMA rows
 constexpr uint32_t kTcKeys = 64;                      // key positions per tile
-constexpr uint32_t kTcThreads = 256;
+// Warps 0-3 own the 128 rows; the producer warps stage the next tile.
+#ifndef ADI_ATTN_PRODUCER_WARPS
+#define ADI_ATTN_PRODUCER_WARPS 8
+#endif
+constexpr uint32_t kProducerThreads = 32 * ADI_ATTN_PRODUCER_WARPS;
+constexpr uint32_t kTcThreads = 128 + kProducerThreads;
 constexpr uint32_t kTcChunk = 64;                     // f16 columns of one 128-byte swizzled tile
 constexpr uint32_t kTcChunks = kAttnHeadSize / kTcChunk;
 
 // Shared memory (offsets from a 1024-byte aligned base).
 constexpr uint32_t kQChunkBytes = kTcRows * 128;  // 16 KiB: 128 rows x 64 dims
 constexpr uint32_t kKChunkBytes = kTcKeys * 128;  // 8 KiB: 64 keys x 64 dims
+constexpr uint32_t kKBytes = kTcChunks * kKChunkBytes;  // 32 KiB: one tile of keys
+constexpr uint32_t kVBytes = kAttnHeadSize * 128;        // 32 KiB: V^T, 256 dims x 64 keys
 constexpr uint32_t kQOff = 0;
-constexpr uint32_t kKOff = kQOff + kTcChunks * kQChunkBytes;        // 64 KiB of Q
-constexpr uint32_t kVOff = kKOff + kTcChunks * kKChunkBytes;        // 32 KiB of K
-constexpr uint32_t kPOff = kVOff + kAttnHeadSize * 128;             // 32 KiB of V^T: 256 dims x 64 keys
-constexpr uint32_t kBarOff = kPOff + kTcRows * 128;                 // 16 KiB of P: 128 rows x 64 keys
+constexpr uint32_t kKOff = kQOff + kTcChunks * kQChunkBytes;  // 64 KiB of Q
+constexpr uint32_t kVOff = kKOff + 2 * kKBytes;               // two tiles of K
+constexpr uint32_t kPOff = kVOff + 2 * kVBytes;               // two tiles of V^T
+constexpr uint32_t kBarOff = kPOff + kTcRows * 128;           // 16 KiB of P: 128 rows x 64 keys
 constexpr uint32_t kTcSmemBytes = kBarOff + 32;
+static_assert(kTcSmemBytes <= 227 * 1024, "shared memory of one CTA");
 
 // Tensor memory: S in columns [0, 64), O in [64, 320); allocations are
 // powers of two.
@@ -105,9 +116,10 @@ __device__ __forceinline__ void stage_queries(uint8_t *qs, const AttnParams &p, 
 
 // Key rows kb .. kb + 63 of the head's cache; positions at or past `kend`
 // are zeros.
-__device__ __forceinline__ void stage_keys(uint8_t *ks, const float *kc, uint32_t kb, uint32_t kend) {
-#pragma unroll
-    for (uint32_t i = threadIdx.x; i < kTcKeys * 32; i += kTcThreads) {
+__device__ __forceinline__ void stage_keys(uint8_t *ks, const float *kc, uint32_t kb, uint32_t kend, uint32_t t,
+                                           uint32_t threads) {
+#pragma unroll 4
+    for (uint32_t i = t; i < kTcKeys * 32; i += threads) {
         const uint32_t n = i >> 5, unit = i & 31u;
         uint4 packed = make_uint4(0u, 0u, 0u, 0u);
         if (kb + n < kend) {
@@ -119,12 +131,14 @@ __device__ __forceinline__ void stage_keys(uint8_t *ks, const float *kc, uint32_
 }
 
 // The same positions of the value cache, transposed: row d of V^T holds
-// dimension d of the 64 positions (thread d, eight units of eight keys; a
-// warp reads 128 contiguous bytes of each key row).
-__device__ __forceinline__ void stage_values(uint8_t *vs, const float *vc, uint32_t kb, uint32_t kend) {
-    const uint32_t d = threadIdx.x;
+// dimension d of the 64 positions. A unit is eight keys of one dimension;
+// consecutive threads take consecutive dimensions, so a warp reads 128
+// contiguous bytes of each key row.
+__device__ __forceinline__ void stage_values(uint8_t *vs, const float *vc, uint32_t kb, uint32_t kend, uint32_t t,
+                                             uint32_t threads) {
 #pragma unroll 2
-    for (uint32_t ng = 0; ng < kTcKeys / 8; ++ng) {
+    for (uint32_t i = t; i < kAttnHeadSize * (kTcKeys / 8); i += threads) {
+        const uint32_t d = i % kAttnHeadSize, ng = i / kAttnHeadSize;
         float v[8];
 #pragma unroll
         for (uint32_t j = 0; j < 8; ++j) {
@@ -135,7 +149,6 @@ __device__ __forceinline__ void stage_values(uint8_t *vs, const float *vc, uint3
             make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]), pack_half2(v[4], v[5]), pack_half2(v[6], v[7]));
     }
 }
-static_assert(kTcThreads == kAttnHeadSize, "stage_values gives each thread one dimension");
 
 __device__ __forceinline__ float gate_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
 
@@ -175,13 +188,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const __gri
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     stage_queries(qs, p, sq, tile0, g);
+    stage_keys(ks, kc, 0, kend, threadIdx.x, kTcThreads);
+    stage_values(vs, vc, 0, kend, threadIdx.x, kTcThreads);
     fence_async_shared();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    // Warps 0-3: thread r owns row r = 8 tq + h (TMEM lane r).
+    // Warps 0-3: thread r owns row r = 8 tq + h (TMEM lane r). The producer
+    // warps (4 on) stage the next tile's keys and values into the other
+    // buffers while the rows take the softmax of the current one.
     const uint32_t r = threadIdx.x;
     const uint32_t qpos = sq.position + tile0 + (r >> 3);
     const uint32_t lane_addr = tmem_base + ((warp * 32u) << 16);
@@ -190,24 +207,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const __gri
     uint32_t last_parity = 0;
     bool ok = true;
     for (uint32_t it = 0; it < ntiles; ++it) {
-        const uint32_t kb = it * kTcKeys;
-        if (it > 0) {
-            // V^T and P of the previous tile are operands of its PV MMAs.
-            const bool done = mbar_wait(bar_pv, (it - 1) & 1u, p.error);
-            if (__syncthreads_or(!done)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-        }
-        stage_keys(ks, kc, kb, kend);
-        stage_values(vs, vc, kb, kend);
-        fence_async_shared();
-        __syncthreads();
+        const uint32_t kb = it * kTcKeys, buf = it & 1u;
         if (threadIdx.x == 0) {
+            // S = Q K^T of this tile (its keys were staged and fenced before
+            // the block barrier that ended the previous iteration).
             tc_fence_after();
             const uint32_t idesc = instr_desc_f16(kTcKeys);
-            const uint32_t qa = smem_u32(qs), ka = smem_u32(ks);
+            const uint32_t qa = smem_u32(qs), ka = smem_u32(ks + buf * kKBytes);
 #pragma unroll
             for (uint32_t c = 0; c < kTcChunks; ++c)
 #pragma unroll
@@ -219,7 +225,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const __gri
             last_parity = it & 1u;
         }
         bool fail = false;
-        if (warp < 4) {
+        if (warp >= 4) {
+            if (it + 1 < ntiles) {
+                // The other buffers were read by the previous tile's MMAs,
+                // whose commit (after its PV MMAs) must have landed.
+                const bool free = it == 0 || mbar_wait(bar_pv, (it - 1) & 1u, p.error);
+                if (free) {
+                    const uint32_t nb = buf ^ 1u, t = threadIdx.x - 128u;
+                    stage_keys(ks + nb * kKBytes, kc, kb + kTcKeys, kend, t, kProducerThreads);
+                    stage_values(vs + nb * kVBytes, vc, kb + kTcKeys, kend, t, kProducerThreads);
+                    fence_async_shared();
+                } else {
+                    fail = true;
+                }
+            }
+        } else {
+            // The commit after S covers every earlier MMA, so the previous
+            // tile's PV MMAs are done too: P and O are free.
             const bool landed = __all_sync(0xffffffffu, mbar_wait(bar_s, it & 1u, p.error));
             if (landed) {
                 tc_fence_after();
@@ -279,7 +301,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const __gri
         if (threadIdx.x == 0) {
             tc_fence_after();
             const uint32_t idesc = instr_desc_f16(kAttnHeadSize);
-            const uint32_t pa = smem_u32(ps), va = smem_u32(vs);
+            const uint32_t pa = smem_u32(ps), va = smem_u32(vs + buf * kVBytes);
 #pragma unroll
             for (uint32_t k = 0; k < kTcKeys / 16; ++k)
                 mma_f16(tmem_base + kOCol, smem_desc_sw128(pa + k * 32), smem_desc_sw128(va + k * 32), idesc,

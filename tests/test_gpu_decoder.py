@@ -180,6 +180,12 @@ def test_decoder_step_graph_replays_match_eager():
             graphed.step(bad, [(0, 1)], x[:1])
             with pytest.raises(ValueError):
                 ctx.synchronize()
+            # The same on the tensor-core attention path (a 64-token chunk
+            # whose end lies past the caches).
+            bad = torch.tensor([[0, 0, 64, 100]], dtype=torch.int32, device="cuda")
+            graphed.step(bad, [(0, 64)], torch.zeros(64, H, device="cuda"))
+            with pytest.raises(ValueError):
+                ctx.synchronize()
         del graph
         head_h.release()
         eager.release()

@@ -75,9 +75,13 @@ __global__ void __launch_bounds__(256) attention_prep_kernel(const __grid_consta
     const uint32_t kh = head - kAttnQueryHeads;
     float *qrow = p.query_gate + (t * kAttnQueryHeads + head) * kAttnQueryStride;
     const float x = query ? qrow[d] : p.key[(t * kAttnKvHeads + kh) * kAttnHeadSize + d];
+    // The norm weight (and a key's value row) load beside x, not after the
+    // reduction's barriers.
+    const float w = 1.0f + bf16_bits_to_f32(query ? p.query_norm[d] : p.key_norm[d]);
+    const float value = query ? 0.0f : p.value[(t * kAttnKvHeads + kh) * kAttnHeadSize + d];
     const float squares = block_total<256>(x * x, red);
     const float scale = 1.0f / sqrtf(squares / static_cast<float>(kAttnHeadSize) + 1.0e-6f);
-    float v = x * (scale * (1.0f + bf16_bits_to_f32(query ? p.query_norm[d] : p.key_norm[d])));
+    float v = x * (scale * w);
     y[d] = v;
     __syncthreads();
     if (d < 2 * kAttnRopeHalf) {
@@ -94,7 +98,7 @@ __global__ void __launch_bounds__(256) attention_prep_kernel(const __grid_consta
     } else {
         const size_t row = ((size_t)(sq.slot * kAttnKvHeads + kh) * p.capacity + pos) * kAttnHeadSize;
         p.key_cache[row + d] = v;
-        p.value_cache[row + d] = p.value[(t * kAttnKvHeads + kh) * kAttnHeadSize + d];
+        p.value_cache[row + d] = value;
     }
 }
 
@@ -607,9 +611,12 @@ __global__ void __launch_bounds__(128) gd_norm_gate_kernel(const __grid_constant
     if (!sequence_in_range(sq, p.tokens, p.slots, 0, p.error)) return;
     const size_t i = ((size_t)(sq.first + li) * kGdValueHeads + blockIdx.z) * kGdHeadSize + threadIdx.x;
     const float x = p.raw[i];
+    // The weight and gate load beside x, not after the reduction's barriers.
+    const float w = bf16_bits_to_f32(p.norm[threadIdx.x]);
+    const float g = silu(p.gate[i]);
     const float squares = block_total<128>(x * x, red);
     const float scale = 1.0f / sqrtf(squares / static_cast<float>(kGdHeadSize) + 1.0e-6f);
-    p.out[i] = x * scale * bf16_bits_to_f32(p.norm[threadIdx.x]) * silu(p.gate[i]);
+    p.out[i] = x * scale * w * g;
 }
 
 // out[i] = hidden[last token of sequence i].

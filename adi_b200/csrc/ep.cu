@@ -238,12 +238,16 @@ __global__ void __launch_bounds__(256) ep_finalize_regs_kernel(EpFinalizeParams 
     float v[R], v1[R];
     load_regs<R>(p.acc_down + (size_t)pos * H + c0, v);
     load_regs<R>(p.acc_down + p.half_stride + (size_t)pos * H + c0, v1);
+    // The output scales load beside the sums, not after the transform.
+    const uint16_t *sv = p.sv_down + (size_t)e * H + c0;
+    float svf[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) svf[r] = f16_bits_to_f32(sv[r]);
 #pragma unroll
     for (int r = 0; r < R; ++r) v[r] += v1[r];
     fwht_regs<R>(v, sh);
-    const uint16_t *sv = p.sv_down + (size_t)e * H + c0;
 #pragma unroll
-    for (int r = 0; r < R; ++r) v[r] = __fmul_rn(__fmul_rn(v[r], p.scale), f16_bits_to_f32(sv[r]));
+    for (int r = 0; r < R; ++r) v[r] = __fmul_rn(__fmul_rn(v[r], p.scale), svf[r]);
     if (p.return_rows) {
         float *dst = return_row(p, row, H);
         if (dst) store_regs<R>(dst + c0, v);
@@ -283,6 +287,14 @@ __global__ void __launch_bounds__(256, 4) ep_combine_regs_kernel(EpCombineParams
     float out[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) out[r] = 0.0f;
+    // The shared expert's sums, its gate and output signs are independent
+    // of the route rows: their loads go out first, beside the rows'.
+    float v[R];
+    load_regs<R>(p.shared_acc + (size_t)t * H + c0, v);
+    const float gate_logit = p.gate_logits[(size_t)t * p.gate_stride];
+    int8_t sv[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) sv[r] = p.shared_sv[c0 + r];
     // The route rows load four at a time, so their latencies overlap; the
     // sum stays in route order.
 #pragma unroll
@@ -298,13 +310,10 @@ __global__ void __launch_bounds__(256, 4) ep_combine_regs_kernel(EpCombineParams
             for (int r = 0; r < R; ++r) out[r] = fmaf(w, rows[j][r], out[r]);
         }
     }
-    float v[R];
-    load_regs<R>(p.shared_acc + (size_t)t * H + c0, v);
     fwht_regs<R>(v, sh);
-    const float gate = sigmoid_f(p.gate_logits[(size_t)t * p.gate_stride]);
+    const float gate = sigmoid_f(gate_logit);
 #pragma unroll
-    for (int r = 0; r < R; ++r)
-        out[r] = fmaf(gate, __fmul_rn(__fmul_rn(v[r], p.scale), (float)p.shared_sv[c0 + r]), out[r]);
+    for (int r = 0; r < R; ++r) out[r] = fmaf(gate, __fmul_rn(__fmul_rn(v[r], p.scale), (float)sv[r]), out[r]);
     store_regs<R>(p.out + (size_t)t * H + c0, out);
 }
 

@@ -1761,14 +1761,23 @@ __global__ void __launch_bounds__(256) mid_regs_kernel(MidParams p) {
             u[r] += u1[r];
         }
     }
-    fwht_regs<R>(g, sh);
-    fwht_regs<R>(u, sh);
+    // The scales load beside the sums (not after the transforms), so their
+    // latency overlaps.
     const size_t s0 = (p.is_f16 ? (size_t)e * p.inner : 0) + threadIdx.x * R;
+    float sg[R], su[R], sd[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-        const float gv = __fmul_rn(__fmul_rn(g[r], p.scale), scale_of(p.sv_gate, p.is_f16, s0 + r));
-        const float uv = __fmul_rn(__fmul_rn(u[r], p.scale), scale_of(p.sv_up, p.is_f16, s0 + r));
-        g[r] = __fmul_rn(__fmul_rn(silu_f(gv), uv), scale_of(p.su_down, p.is_f16, s0 + r));
+        sg[r] = scale_of(p.sv_gate, p.is_f16, s0 + r);
+        su[r] = scale_of(p.sv_up, p.is_f16, s0 + r);
+        sd[r] = scale_of(p.su_down, p.is_f16, s0 + r);
+    }
+    fwht_regs<R>(g, sh);
+    fwht_regs<R>(u, sh);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const float gv = __fmul_rn(__fmul_rn(g[r], p.scale), sg[r]);
+        const float uv = __fmul_rn(__fmul_rn(u[r], p.scale), su[r]);
+        g[r] = __fmul_rn(__fmul_rn(silu_f(gv), uv), sd[r]);
     }
     fwht_regs<R>(g, sh);
 #pragma unroll
@@ -2152,12 +2161,48 @@ void launch_hadamard(float *values, uint32_t count, uint32_t n, float scale, cud
     }
 }
 
+constexpr uint32_t kNormRegs = 32;  // elements per thread of the register path (n <= 256 * kNormRegs)
+
 __global__ void rms_norm_kernel(const float *x, const uint16_t *w, uint32_t n, float offset, float eps,
                                 float *out) {
     griddep_launch_dependents();
     griddep_wait();
     __shared__ float partial[32];
     const float *row = x + (size_t)blockIdx.x * n;
+    if (n <= kNormRegs * blockDim.x) {
+        // The row and weights in registers, every load in flight at once
+        // (the loop below reloads the row after the reduction and stores
+        // between loads); the same sums in the same order.
+        float v[kNormRegs], wv[kNormRegs];
+#pragma unroll
+        for (uint32_t k = 0; k < kNormRegs; ++k) {
+            const uint32_t i = threadIdx.x + k * blockDim.x;
+            if (i < n) {
+                v[k] = row[i];
+                wv[k] = offset + bf16_bits_to_f32(w[i]);
+            }
+        }
+        float sq = 0.0f;
+#pragma unroll
+        for (uint32_t k = 0; k < kNormRegs; ++k)
+            if (threadIdx.x + k * blockDim.x < n) sq = fmaf(v[k], v[k], sq);
+        sq = warp_sum(sq);
+        if ((threadIdx.x & 31u) == 0) partial[threadIdx.x >> 5] = sq;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            float t = threadIdx.x < blockDim.x / 32 ? partial[threadIdx.x] : 0.0f;
+            t = warp_sum(t);
+            if (threadIdx.x == 0) partial[0] = t;
+        }
+        __syncthreads();
+        const float scale = 1.0f / sqrtf(partial[0] / (float)n + eps);
+#pragma unroll
+        for (uint32_t k = 0; k < kNormRegs; ++k) {
+            const uint32_t i = threadIdx.x + k * blockDim.x;
+            if (i < n) out[(size_t)blockIdx.x * n + i] = v[k] * scale * wv[k];
+        }
+        return;
+    }
     float sq = 0.0f;
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) sq = fmaf(row[i], row[i], sq);
     sq = warp_sum(sq);
@@ -2194,13 +2239,22 @@ __global__ void add_rms_norm_kernel(float *hidden, const float *add, const uint1
     __shared__ float partial[32];
     float *row = hidden + (size_t)blockIdx.x * n;
     const float *a = add + (size_t)blockIdx.x * n;
-    float v[kAddNormMax];
-    float sq = 0.0f;
+    // Every load first (no store between them, so they are all in flight at
+    // once: a store to `row` could alias a later load), then the stores.
+    float v[kAddNormMax], wv[kAddNormMax];
 #pragma unroll
     for (uint32_t k = 0; k < kAddNormMax; ++k) {
         const uint32_t i = threadIdx.x + k * blockDim.x;
         if (i < n) {
             v[k] = row[i] + a[i];
+            wv[k] = offset + bf16_bits_to_f32(w[i]);
+        }
+    }
+    float sq = 0.0f;
+#pragma unroll
+    for (uint32_t k = 0; k < kAddNormMax; ++k) {
+        const uint32_t i = threadIdx.x + k * blockDim.x;
+        if (i < n) {
             row[i] = v[k];
             sq = fmaf(v[k], v[k], sq);
         }
@@ -2218,7 +2272,7 @@ __global__ void add_rms_norm_kernel(float *hidden, const float *add, const uint1
 #pragma unroll
     for (uint32_t k = 0; k < kAddNormMax; ++k) {
         const uint32_t i = threadIdx.x + k * blockDim.x;
-        if (i < n) out[(size_t)blockIdx.x * n + i] = v[k] * scale * (offset + bf16_bits_to_f32(w[i]));
+        if (i < n) out[(size_t)blockIdx.x * n + i] = v[k] * scale * wv[k];
     }
 }
 

@@ -1164,6 +1164,10 @@ __device__ __forceinline__ uint4 pack_half8(const float *v, float s) {
 // transforms and the row's max-abs inside the warp. Lane l's elements
 // 16l .. 16l+15 land in the split layout as two runs of eight halves (one
 // 16-byte store each).
+// kPrefetch: the scales load beside the sums (decode-sized calls, where the
+// latency counts); without, after the transforms, in fewer registers (large
+// calls, where occupancy counts).
+template <bool kPrefetch>
 __global__ void __launch_bounds__(256) mid_f16_warp_kernel(MidF16Params p) {
     griddep_launch_dependents();
     griddep_wait();
@@ -1187,14 +1191,32 @@ __global__ void __launch_bounds__(256) mid_f16_warp_kernel(MidF16Params p) {
             u[r] += u1[r];
         }
     }
-    fwht_warp16(g);
-    fwht_warp16(u);
     const size_t s0 = (p.is_f16 ? (size_t)e * n : 0) + lane * 16u;
+    if constexpr (kPrefetch) {
+        float sg[16], su[16], sd[16];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-        const float gv = __fmul_rn(__fmul_rn(g[r], p.scale), scale_value(p.sv_gate, p.is_f16, s0 + r));
-        const float uv = __fmul_rn(__fmul_rn(u[r], p.scale), scale_value(p.sv_up, p.is_f16, s0 + r));
-        g[r] = __fmul_rn(__fmul_rn(silu_f(gv), uv), scale_value(p.su_down, p.is_f16, s0 + r));
+        for (int r = 0; r < 16; ++r) {
+            sg[r] = scale_value(p.sv_gate, p.is_f16, s0 + r);
+            su[r] = scale_value(p.sv_up, p.is_f16, s0 + r);
+            sd[r] = scale_value(p.su_down, p.is_f16, s0 + r);
+        }
+        fwht_warp16(g);
+        fwht_warp16(u);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const float gv = __fmul_rn(__fmul_rn(g[r], p.scale), sg[r]);
+            const float uv = __fmul_rn(__fmul_rn(u[r], p.scale), su[r]);
+            g[r] = __fmul_rn(__fmul_rn(silu_f(gv), uv), sd[r]);
+        }
+    } else {
+        fwht_warp16(g);
+        fwht_warp16(u);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const float gv = __fmul_rn(__fmul_rn(g[r], p.scale), scale_value(p.sv_gate, p.is_f16, s0 + r));
+            const float uv = __fmul_rn(__fmul_rn(u[r], p.scale), scale_value(p.sv_up, p.is_f16, s0 + r));
+            g[r] = __fmul_rn(__fmul_rn(silu_f(gv), uv), scale_value(p.su_down, p.is_f16, s0 + r));
+        }
     }
     fwht_warp16(g);
     float m = 0.0f;
@@ -1249,7 +1271,12 @@ void launch_mid_f16(const MidF16Params &p, cudaStream_t s) {
     if (p.positions == 0) return;
     const uint32_t blocks = loop_grid(p.positions, p.limit);
     switch (p.inner) {
-        case 512: launch_pdl(mid_f16_warp_kernel, loop_grid((p.positions + 7) / 8, p.limit), 256, 0, s, p); return;
+        case 512:
+            if (p.positions <= 64)
+                launch_pdl(mid_f16_warp_kernel<true>, loop_grid((p.positions + 7) / 8, p.limit), 256, 0, s, p);
+            else
+                launch_pdl(mid_f16_warp_kernel<false>, loop_grid((p.positions + 7) / 8, p.limit), 256, 0, s, p);
+            return;
         case 1024: mid_f16_regs_kernel<4><<<blocks, 256, 0, s>>>(p); return;
         case 2048: mid_f16_regs_kernel<8><<<blocks, 256, 0, s>>>(p); return;
         default: mid_f16_kernel<<<blocks, 256, 2 * p.inner * sizeof(float), s>>>(p);

@@ -978,17 +978,7 @@ __global__ void __launch_bounds__(256) bf16_gemm_wide_kernel(const uint16_t *w0,
                                                              uint32_t tokens, uint32_t cols, float *out,
                                                              uint32_t out_stride) {
     griddep_launch_dependents();
-    griddep_wait();
     extern __shared__ float xs[];
-    const uint32_t t0 = blockIdx.x * NT;
-    const uint32_t nt = min((uint32_t)NT, tokens - t0);
-    for (uint32_t i = threadIdx.x; i < NT * cols / 4; i += blockDim.x) {
-        const uint32_t t = i / (cols / 4);
-        const uint32_t c4 = i % (cols / 4);
-        reinterpret_cast<float4 *>(xs)[i] = t < nt ? reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * cols)[c4]
-                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    __syncthreads();
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t rbase = blockIdx.y * (8 * RPW) + warp * RPW;
     const uint32_t R = rows0 + rows1;
@@ -998,8 +988,34 @@ __global__ void __launch_bounds__(256) bf16_gemm_wide_kernel(const uint16_t *w0,
         const uint32_t r = rbase + i;
         row_ptr[i] = r < rows0 ? w0 + (size_t)r * cols : (r < R ? w1 + (size_t)(r - rows0) * cols : nullptr);
     }
+    // One row per warp and at most 2048 columns (the decode-sized calls):
+    // the row's weights are constants, so their loads go out before the
+    // wait for the kernel that produces x, and overlap its tail.
+    constexpr uint32_t kPreChunks = 8;
+    const bool pre = RPW == 1 && cols <= 256 * kPreChunks;
+    uint4 wpre[kPreChunks];
+    if (pre) {
+#pragma unroll
+        for (uint32_t j = 0; j < kPreChunks; ++j) {
+            const uint32_t c = lane * 8 + 256 * j;
+            wpre[j] = row_ptr[0] && c < cols ? __ldg(reinterpret_cast<const uint4 *>(row_ptr[0] + c))
+                                             : make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+    griddep_wait();
+    const uint32_t t0 = blockIdx.x * NT;
+    const uint32_t nt = min((uint32_t)NT, tokens - t0);
+    for (uint32_t i = threadIdx.x; i < NT * cols / 4; i += blockDim.x) {
+        const uint32_t t = i / (cols / 4);
+        const uint32_t c4 = i % (cols / 4);
+        reinterpret_cast<float4 *>(xs)[i] = t < nt ? reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * cols)[c4]
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __syncthreads();
     float acc[RPW][NT] = {};
-    for (uint32_t c = lane * 8; c < cols; c += 256) {
+    // Columns c = lane * 8 + 256 j in ascending j, the eight of a chunk in
+    // order: the same sums with or without the early loads.
+    auto chunk = [&](uint32_t c, int i, const uint4 &wq) {
         float xv[NT][8];
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
@@ -1008,16 +1024,28 @@ __global__ void __launch_bounds__(256) bf16_gemm_wide_kernel(const uint16_t *w0,
             xv[t][0] = a.x; xv[t][1] = a.y; xv[t][2] = a.z; xv[t][3] = a.w;
             xv[t][4] = b.x; xv[t][5] = b.y; xv[t][6] = b.z; xv[t][7] = b.w;
         }
+        const uint32_t wp[4] = {wq.x, wq.y, wq.z, wq.w};
 #pragma unroll
-        for (int i = 0; i < RPW; ++i) {
-            if (!row_ptr[i]) continue;
-            const uint4 wq = __ldg(reinterpret_cast<const uint4 *>(row_ptr[i] + c));
-            const uint32_t wp[4] = {wq.x, wq.y, wq.z, wq.w};
+        for (int k = 0; k < 8; ++k) {
+            const float wv = __uint_as_float((k & 1) ? (wp[k >> 1] & 0xFFFF0000u) : (wp[k >> 1] << 16));
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const float wv = __uint_as_float((k & 1) ? (wp[k >> 1] & 0xFFFF0000u) : (wp[k >> 1] << 16));
+            for (int t = 0; t < NT; ++t) acc[i][t] = fmaf(wv, xv[t][k], acc[i][t]);
+        }
+    };
+    if (pre) {
+        if (row_ptr[0]) {
 #pragma unroll
-                for (int t = 0; t < NT; ++t) acc[i][t] = fmaf(wv, xv[t][k], acc[i][t]);
+            for (uint32_t j = 0; j < kPreChunks; ++j) {
+                const uint32_t c = lane * 8 + 256 * j;
+                if (c < cols) chunk(c, 0, wpre[j]);
+            }
+        }
+    } else {
+        for (uint32_t c = lane * 8; c < cols; c += 256) {
+#pragma unroll
+            for (int i = 0; i < RPW; ++i) {
+                if (!row_ptr[i]) continue;
+                chunk(c, i, __ldg(reinterpret_cast<const uint4 *>(row_ptr[i] + c)));
             }
         }
     }

@@ -943,8 +943,7 @@ void ne_decode_dev(adi_cuda_context *c, std::vector<NeDecodeCall> calls, uint32_
             xo += size_t(batch) * m.cols;
             ao += size_t(batch) * m.rows;
         }
-        launch_ne_decode(p, c->sms, c->stream);
-        c->after_launch(2);
+        c->after_launch(launch_ne_decode(p, c->sms, c->stream));
         first += n;
     }
     c->stage_end();

@@ -129,10 +129,36 @@ __global__ void __launch_bounds__(256) ne_decode_prep_kernel(const __grid_consta
     }
 }
 
+// x' of a call's one token computed by a decode group (the prep kernel's
+// arithmetic and fwht_strided's order, so the same bits): x' in stage[0,
+// cols), the transform's workspace after it (cols + padded(cols) floats,
+// which the staging buffer holds for cols <= 4096).
+template <int R>
+__device__ __forceinline__ void stage_prep(const NeDecodeJob &J, float *stage, uint32_t t, uint32_t bar) {
+    float v[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = __fmul_rn(J.input[t + 256u * r], (float)J.su[t + 256u * r]);
+    fwht_strided<R>(v, stage + 256u * R, t, bar);
+#pragma unroll
+    for (int r = 0; r < R; ++r) stage[t + 256u * r] = __fmul_rn(v[r], J.in_scale);
+}
+
+__device__ __forceinline__ void stage_prep_any(const NeDecodeJob &J, float *stage, uint32_t t, uint32_t bar) {
+    switch (J.cols) {
+        case 256: stage_prep<1>(J, stage, t, bar); break;
+        case 512: stage_prep<2>(J, stage, t, bar); break;
+        case 1024: stage_prep<4>(J, stage, t, bar); break;
+        case 2048: stage_prep<8>(J, stage, t, bar); break;
+        case 4096: stage_prep<16>(J, stage, t, bar); break;
+        default: break;  // the host launches the prep kernel instead
+    }
+}
+
 // ---- y = H(acc) / sqrt(rows) * sv, in two phases -------------------------
 //
-// The transform's strides 1 .. 128 act inside aligned 256-row blocks, the
-// strides 256 .. rows/2 across them. Phase 1 runs per block, by the group
+// Jobs above kSingleLevelRows rows times tokens (below, whole_transform
+// does it all in one group). The transform's strides 1 .. 128 act inside aligned 256-row
+// blocks, the strides 256 .. rows/2 across them. Phase 1 runs per block, by the group
 // that completes the block's last tile row, in place on the sums; phase 2
 // by the group that completes the job's last block, one thread per column
 // t of the rows viewed as [rows / 256][256], all in registers. The stride
@@ -184,6 +210,47 @@ __device__ __forceinline__ void job_transform(const NeDecodeJob &J, uint32_t tok
                 }
 #pragma unroll
         for (int r = 0; r < R; ++r) out[(size_t)q * J.rows + t + 256u * r] = __fmul_rn(__fmul_rn(v[r], J.out_scale), sv[r]);
+    }
+}
+
+// Jobs of at most this many rows times tokens take the whole output
+// transform in the group that completes their last item (one arrival
+// counter, one load of the sums); larger ones run its first eight strides
+// per 256-row block in parallel first (block counters, then the job
+// counter).
+constexpr uint32_t kSingleLevelRows = 4096;
+
+// The whole transform of a job of 256 R rows by one group: element t + 256 r
+// of every token, all strides in fwht_strided's ascending order (the same
+// butterflies as block_transform followed by job_transform), then the
+// scales.
+template <int R>
+__device__ __forceinline__ void whole_transform(const NeDecodeJob &J, uint32_t tokens, float *sh, uint32_t t,
+                                                uint32_t bar) {
+    // The signs first: a load through an int8 pointer may alias the outputs.
+    float sv[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) sv[r] = (float)J.sv[t + 256u * r];
+    for (uint32_t q = 0; q < tokens; ++q) {
+        float v[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) v[r] = __ldcg(J.acc + (size_t)q * J.rows + t + 256u * r);
+        fwht_strided<R>(v, sh, t, bar);
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            J.out[(size_t)q * J.rows + t + 256u * r] = __fmul_rn(__fmul_rn(v[r], J.out_scale), sv[r]);
+    }
+}
+
+__device__ __forceinline__ void finalize_whole(const NeDecodeJob &J, uint32_t tokens, float *sh, uint32_t t,
+                                               uint32_t bar) {
+    switch (J.rows) {
+        case 256: whole_transform<1>(J, tokens, sh, t, bar); break;
+        case 512: whole_transform<2>(J, tokens, sh, t, bar); break;
+        case 1024: whole_transform<4>(J, tokens, sh, t, bar); break;
+        case 2048: whole_transform<8>(J, tokens, sh, t, bar); break;
+        case 4096: whole_transform<16>(J, tokens, sh, t, bar); break;
+        default: break;  // larger jobs take the two-level path
     }
 }
 
@@ -313,6 +380,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) ne_decode_kernel(const __gr
         const uint32_t t0 = at.chunk * J.chunk_tokens;
         const uint32_t nt = min(J.chunk_tokens, p.tokens - t0);
         const uint32_t key = (at.job << 16) | at.chunk;
+        if (staged != key && p.fused_prep) {
+            named_sync(bar, kGroupThreads);  // nobody still reads the old rows
+            stage_prep_any(J, stage, t, bar);
+            named_sync(bar, kGroupThreads);
+            staged = key;
+        }
         if (staged != key) {
             named_sync(bar, kGroupThreads);  // nobody still reads the old rows
             const float4 *src = reinterpret_cast<const float4 *>(J.xp + (size_t)t0 * J.cols);
@@ -402,13 +475,34 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) ne_decode_kernel(const __gr
         // and count by the barrier (the pattern of a cooperative grid sync);
         // the last arrival fences again before its group reads the other
         // groups' rows.
-        // Counters: p.done[job] counts the job's completed blocks,
-        // p.done[kNeDecodeMaxJobs + 32 job + block] a block's completed items
-        // (16 tile rows times the token chunks). A counter's last arrival
-        // resets it, so the next launch finds it at zero.
+        // Counters: for a job of up to kSingleLevelRows rows times tokens
+        // p.done[job] counts its completed items; for a larger one the job's
+        // completed blocks, and p.done[kNeDecodeMaxJobs + 32 job + block] a
+        // block's completed items (16 tile rows times the token chunks). A
+        // counter's last arrival resets it, so the next launch finds it at
+        // zero.
+        named_sync(bar, kGroupThreads);
+        if (J.rows * p.tokens <= kSingleLevelRows) {
+            // p.done[job] counts the job's completed items; the last one
+            // transforms the whole job.
+            if (t == 0) {
+                __threadfence();
+                const bool last = atomicAdd(p.done + at.job, 1u) + 1 == (J.rows >> 4) * J.chunks;
+                if (last) {
+                    __threadfence();
+                    p.done[at.job] = 0;
+                }
+                last_flag[g] = last ? 1u : 0u;
+            }
+            named_sync(bar, kGroupThreads);
+            if (last_flag[g]) {
+                finalize_whole(J, p.tokens, stage, t, bar);
+                staged = ~0u;
+            }
+            continue;
+        }
         const uint32_t block = at.tile_row >> 4;
         uint32_t *block_count = p.done + kNeDecodeMaxJobs + at.job * (kNeDecodeMaxRows / 256) + block;
-        named_sync(bar, kGroupThreads);
         if (t == 0) {
             __threadfence();
             const bool last = atomicAdd(block_count, 1u) + 1 == 16u * J.chunks;
@@ -541,15 +635,23 @@ void launch_ne_big_transform(float *acc, uint32_t tokens, uint32_t n, const int8
     }
 }
 
-void launch_ne_decode(const NeDecodeParams &p, int sms, cudaStream_t s) {
-    if (p.jobs == 0 || p.items == 0) return;
-    launch_pdl(ne_decode_prep_kernel, dim3(p.tokens, p.jobs), 256, 0, s, p);
+uint32_t launch_ne_decode(const NeDecodeParams &params, int sms, cudaStream_t s) {
+    if (params.jobs == 0 || params.items == 0) return 0;
+    NeDecodeParams p = params;
+    p.fused_prep = p.tokens == 1;
+    for (uint32_t j = 0; j < p.jobs; ++j) p.fused_prep &= p.job[j].cols <= 4096u;
+    if (!p.fused_prep) launch_pdl(ne_decode_prep_kernel, dim3(p.tokens, p.jobs), 256, 0, s, p);
     const uint32_t want = (p.items + kGroups - 1) / kGroups;
     const int grid = int(want < uint32_t(sms) ? want : uint32_t(sms));
-    if (p.tokens <= 1) return launch_decode_instance<1>(p, grid, s);
-    if (p.tokens <= 2) return launch_decode_instance<2>(p, grid, s);
-    if (p.tokens <= 4) return launch_decode_instance<4>(p, grid, s);
-    return launch_decode_instance<8>(p, grid, s);
+    if (p.tokens <= 1)
+        launch_decode_instance<1>(p, grid, s);
+    else if (p.tokens <= 2)
+        launch_decode_instance<2>(p, grid, s);
+    else if (p.tokens <= 4)
+        launch_decode_instance<4>(p, grid, s);
+    else
+        launch_decode_instance<8>(p, grid, s);
+    return p.fused_prep ? 1u : 2u;
 }
 
 }  // namespace adi_cuda

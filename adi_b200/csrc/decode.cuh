@@ -14,7 +14,10 @@
 //
 // The second is launched as a programmatic dependent of the first: its
 // blocks set up the value table and start streaming code words while the
-// prep runs, and wait for the prep only before they read x'.
+// prep runs, and wait for the prep only before they read x'. At one token
+// (every job at most 4096 columns wide) there is no prep launch: each group
+// computes its job's x' itself, the same arithmetic in the same order, and
+// the kernel waits only for the producer of x.
 //
 // Arithmetic: the same sums in the same order as the CUDA-core NE kernels
 // (per-warp partials over the tile columns w, w+8, ... of class w, lane
@@ -61,6 +64,7 @@ struct NeDecodeParams {
     uint32_t jobs, tokens, items;  // items = total (tile row, token chunk) pairs
     const float2 *table;           // [1024] signed value pairs
     uint32_t *done;                // [kNeDecodeDoneWords] arrival counters; zero between launches
+    uint32_t fused_prep;           // set by launch_ne_decode: x' computed by the decode kernel's groups
 };
 
 // True when a projection of this shape and batch can take the decode path.
@@ -87,7 +91,9 @@ inline uint32_t ne_decode_chunk_tokens(uint32_t cols, uint32_t tokens) {
     return tokens < fit ? tokens : fit;
 }
 
-// Both launches. `sms` sizes the persistent grid.
-void launch_ne_decode(const NeDecodeParams &p, int sms, cudaStream_t s);
+// Both launches, or at one token with every job at most 4096 columns wide
+// the decode kernel alone, its groups computing x' themselves. `sms` sizes
+// the persistent grid. Returns the kernels launched.
+uint32_t launch_ne_decode(const NeDecodeParams &p, int sms, cudaStream_t s);
 
 }  // namespace adi_cuda

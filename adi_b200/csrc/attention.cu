@@ -349,6 +349,8 @@ __global__ void __launch_bounds__(256, 1) attention_kernel(const __grid_constant
     }
 }
 
+constexpr uint32_t kCombineSplits = 256;  // splits whose maxima and denominators go through shared memory
+
 // Merges the splits of each (token, query head) and applies the gate.
 __global__ void __launch_bounds__(256) attention_combine_kernel(const __grid_constant__ AttnParams p) {
     griddep_launch_dependents();
@@ -360,18 +362,36 @@ __global__ void __launch_bounds__(256) attention_combine_kernel(const __grid_con
     const size_t h = (size_t)(sq.first + li) * kAttnQueryHeads + blockIdx.z;
     const uint32_t d = threadIdx.x;
     const size_t base = h * p.splits;
+    const float gate = p.query_gate[h * kAttnQueryStride + kAttnHeadSize + d];
+    // The splits' maxima and denominators through shared memory (one load
+    // each, all in flight), then the dimension's partial sums kUnroll at a
+    // time; the sums run over the splits in order, as before.
+    __shared__ float ml[2 * kCombineSplits];
+    const uint32_t staged = min(p.splits, kCombineSplits);
+    for (uint32_t i = d; i < 2 * staged; i += blockDim.x) ml[i] = p.partial_ml[base * 2 + i];
+    __syncthreads();
+    auto m_of = [&](uint32_t s) { return s < staged ? ml[2 * s] : p.partial_ml[(base + s) * 2]; };
+    auto l_of = [&](uint32_t s) { return s < staged ? ml[2 * s + 1] : p.partial_ml[(base + s) * 2 + 1]; };
     float M = neg_inf();
-    for (uint32_t s = 0; s < p.splits; ++s) M = fmaxf(M, p.partial_ml[(base + s) * 2]);
+    for (uint32_t s = 0; s < p.splits; ++s) M = fmaxf(M, m_of(s));
     float L = 0.0f, o = 0.0f;
-    for (uint32_t s = 0; s < p.splits; ++s) {
-        const float mw = p.partial_ml[(base + s) * 2];
-        if (mw != neg_inf()) {
-            const float f = expf(mw - M);
-            L += p.partial_ml[(base + s) * 2 + 1] * f;
-            o += p.partial[(base + s) * kAttnHeadSize + d] * f;
+    constexpr uint32_t kUnroll = 8;
+    for (uint32_t s0 = 0; s0 < p.splits; s0 += kUnroll) {
+        float part[kUnroll];
+#pragma unroll
+        for (uint32_t j = 0; j < kUnroll; ++j)
+            part[j] = s0 + j < p.splits ? p.partial[(base + s0 + j) * kAttnHeadSize + d] : 0.0f;
+#pragma unroll
+        for (uint32_t j = 0; j < kUnroll; ++j) {
+            if (s0 + j >= p.splits) break;
+            const float mw = m_of(s0 + j);
+            if (mw != neg_inf()) {
+                const float f = expf(mw - M);
+                L += l_of(s0 + j) * f;
+                o += part[j] * f;
+            }
         }
     }
-    const float gate = p.query_gate[h * kAttnQueryStride + kAttnHeadSize + d];
     p.attended[h * kAttnHeadSize + d] = o * (1.0f / L) * sigmoid(gate);
 }
 

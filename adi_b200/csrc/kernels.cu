@@ -1472,6 +1472,43 @@ __global__ void route_place_kernel(RouteParams p) {
     p.route_to_grouped[i] = pos;
 }
 
+// Inclusive prefix sums of a[0..1023] and b[0..1023] (one per thread of a
+// 1024-thread block): warp scans by shuffles, then the 32 warp totals.
+__device__ __forceinline__ void block_scan2_1024(uint32_t &a, uint32_t &b, uint32_t *tot_a, uint32_t *tot_b) {
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t va = __shfl_up_sync(0xffffffffu, a, o), vb = __shfl_up_sync(0xffffffffu, b, o);
+        if (lane >= (uint32_t)o) {
+            a += va;
+            b += vb;
+        }
+    }
+    if (lane == 31) {
+        tot_a[warp] = a;
+        tot_b[warp] = b;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t ta = tot_a[lane], tb = tot_b[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t va = __shfl_up_sync(0xffffffffu, ta, o), vb = __shfl_up_sync(0xffffffffu, tb, o);
+            if (lane >= (uint32_t)o) {
+                ta += va;
+                tb += vb;
+            }
+        }
+        tot_a[lane] = ta;
+        tot_b[lane] = tb;
+    }
+    __syncthreads();
+    if (warp > 0) {
+        a += tot_a[warp - 1];
+        b += tot_b[warp - 1];
+    }
+}
+
 // The whole routing of a small batch (at most kSmallRoutes routes) in one
 // block: counts by shared-memory atomics, the same scans and work lists as
 // route_lists_kernel, and each route's rank within its expert as the number
@@ -1484,7 +1521,8 @@ __global__ void __launch_bounds__(1024) route_small_kernel(RouteParams p) {
     griddep_launch_dependents();
     griddep_wait();
     __shared__ uint32_t expert_of[kSmallRoutes];
-    __shared__ uint32_t counts[1024], scan[1024], chunk_scan[1024];
+    __shared__ uint32_t counts[1024], scan[1024];
+    __shared__ uint32_t tot_a[32], tot_b[32];
     const uint32_t t = threadIdx.x, n = p.tokens * 8;
     counts[t] = 0;
     __syncthreads();
@@ -1497,19 +1535,11 @@ __global__ void __launch_bounds__(1024) route_small_kernel(RouteParams p) {
     const uint32_t e = t;
     const uint32_t count = e < p.experts ? counts[e] : 0u;
     const uint32_t chunks = (count + p.chunk - 1) / p.chunk;
-    scan[e] = count;
-    chunk_scan[e] = chunks;
-    __syncthreads();
-    for (uint32_t o = 1; o < 1024; o <<= 1) {
-        const uint32_t a = e >= o ? scan[e - o] : 0u;
-        const uint32_t b = e >= o ? chunk_scan[e - o] : 0u;
-        __syncthreads();
-        scan[e] += a;
-        chunk_scan[e] += b;
-        __syncthreads();
-    }
-    const uint32_t offset = scan[e] - count;
-    const uint32_t chunk_offset = chunk_scan[e] - chunks;
+    uint32_t inc = count, chunk_inc = chunks;  // inclusive scans by warp shuffles
+    block_scan2_1024(inc, chunk_inc, tot_a, tot_b);
+    scan[e] = inc;
+    const uint32_t offset = inc - count;
+    const uint32_t chunk_offset = chunk_inc - chunks;
     if (e < p.experts) {
         p.counts[e] = count;
         p.offsets[e] = offset;
@@ -1557,42 +1587,6 @@ size_t route_block_smem(const RouteParams &p) {
     return (2 * size_t(p.experts) * (p.words | 1u) + 3 * 1024 + 2 * size_t(p.tokens) * 8) * sizeof(uint32_t);
 }
 
-// Inclusive prefix sums of a[0..1023] and b[0..1023] (one per thread of a
-// 1024-thread block): warp scans by shuffles, then the 32 warp totals.
-__device__ __forceinline__ void block_scan2_1024(uint32_t &a, uint32_t &b, uint32_t *tot_a, uint32_t *tot_b) {
-    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t va = __shfl_up_sync(0xffffffffu, a, o), vb = __shfl_up_sync(0xffffffffu, b, o);
-        if (lane >= (uint32_t)o) {
-            a += va;
-            b += vb;
-        }
-    }
-    if (lane == 31) {
-        tot_a[warp] = a;
-        tot_b[warp] = b;
-    }
-    __syncthreads();
-    if (warp == 0) {
-        uint32_t ta = tot_a[lane], tb = tot_b[lane];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t va = __shfl_up_sync(0xffffffffu, ta, o), vb = __shfl_up_sync(0xffffffffu, tb, o);
-            if (lane >= (uint32_t)o) {
-                ta += va;
-                tb += vb;
-            }
-        }
-        tot_a[lane] = ta;
-        tot_b[lane] = tb;
-    }
-    __syncthreads();
-    if (warp > 0) {
-        a += tot_a[warp - 1];
-        b += tot_b[warp - 1];
-    }
-}
 
 // The whole counting sort in one 1024-thread block. Every scattered write
 // lands in shared memory; global memory sees coalesced runs only: the
@@ -1976,6 +1970,7 @@ void launch_combine(const CombineParams &p, cudaStream_t s) {
 // integer whose k-th 5-bit field is column k. Warp per row, lane per group;
 // up to 8 input rows per pass from shared memory.
 // ---------------------------------------------------------------------------
+
 __global__ void head_kernel(HeadParams p) {
     extern __shared__ float xs[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;

@@ -122,7 +122,8 @@ ADI_CUDA_API int adi_cuda_synchronize(adi_cuda_context *context);
 /* The stream the context launches on (its own, or the one last set). */
 ADI_CUDA_API int adi_cuda_get_stream(adi_cuda_context *context, void **stream);
 /* Matmul arithmetic: 0 = CUDA-core fp32 throughout (parity 1e-3 rel L2);
- * 1 = tensor-core operands where a path has them (parity 1e-2 rel L2). */
+ * 1 = tensor-core operands where a path has them (parity 1e-2 rel L2),
+ * full attention's prefill chunks (64 tokens or more) included. */
 ADI_CUDA_API int adi_cuda_set_precision(adi_cuda_context *context, int mode);
 /* Device kernels this context has launched so far (for launch accounting). */
 ADI_CUDA_API uint64_t adi_cuda_launch_count(const adi_cuda_context *context);

@@ -695,9 +695,9 @@ void tc_launch(TcCodec codec, const CUtensorMap &map0, const CUtensorMap &map1, 
     if (!launch_tc_gemm(codec, map0, map1, p, grid, s)) throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
 }
 
-CUtensorMap b_map(const __half *x, uint32_t rows, uint32_t cols) {
+CUtensorMap b_map(const __half *x, uint32_t rows, uint32_t cols, uint32_t box_rows = 16) {
     CUtensorMap map;
-    if (!make_b_map(&map, x, rows, cols)) throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
+    if (!make_b_map(&map, x, rows, cols, box_rows)) throw Status(ADI_CUDA_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
     return map;
 }
 
@@ -754,7 +754,7 @@ void ne_matmul_tc(adi_cuda_context *c, NeDev &m, const float *in, uint32_t batch
     pp.su_is_f16 = 0;
     pp.split = 0;
     launch_prep_f16(pp, c->stream);
-    const CUtensorMap map = b_map(xh, batch, m.cols);
+    const CUtensorMap map = b_map(xh, batch, m.cols, kTcNeBoxRows);
     TcParams tp{};
     tp.job[0] = TcJob{m.trellis->as<uint16_t>(), 0, nullptr, 0, nullptr, m.weight_scale, kx, acc,
                       size_t(batch) * m.rows, m.rows, m.cols, batch};
@@ -1099,7 +1099,7 @@ void shared_expert_tc(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t 
     const uint32_t ks = kSharedExpertKParts;
     float *acc_g = c->buffer<float>("moe_sacc_g", ks * size_t(T) * I);
     float *acc_u = c->buffer<float>("moe_sacc_u", ks * size_t(T) * I);
-    const CUtensorMap map_g = b_map(xg, T, H), map_u = b_map(xu, T, H);
+    const CUtensorMap map_g = b_map(xg, T, H, kTcNeBoxRows), map_u = b_map(xu, T, H, kTcNeBoxRows);
     TcParams tp{};
     tp.job[0] = TcJob{L.shared[0].trellis->as<uint16_t>(), 0, nullptr, 0, nullptr, L.shared[0].weight_scale, kg,
                       acc_g, size_t(T) * I, I, H, T};
@@ -1129,7 +1129,7 @@ void shared_expert_tc(adi_cuda_context *c, MoeDev &L, const float *in, uint32_t 
     mp.kx = kd;
     mp.positions = T;
     launch_mid_f16(mp, s);
-    const CUtensorMap map_d = b_map(xd, T, I);
+    const CUtensorMap map_d = b_map(xd, T, I, kTcNeBoxRows);
     TcParams dp{};
     dp.job[0] = TcJob{L.shared[2].trellis->as<uint16_t>(), 0, nullptr, 0, nullptr, L.shared[2].weight_scale, kd,
                       sacc, size_t(T) * H, H, I, T};

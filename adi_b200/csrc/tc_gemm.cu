@@ -73,7 +73,23 @@ constexpr uint32_t kDecodeWarp0 = 3;
 // columns).
 constexpr uint32_t kTmemAStages = 4;
 constexpr uint32_t kTmemAColumn0 = 2 * kTcMaxN;
-constexpr uint32_t kMaxAStages = kTmemAStages > kAStages ? kTmemAStages : kAStages;
+// The NE codec's rings (its A tiles live in shared memory, so its B ring
+// and A ring share what the value table leaves).
+#ifndef ADI_TC_NE_A_STAGES
+#define ADI_TC_NE_A_STAGES kAStages
+#endif
+#ifndef ADI_TC_NE_B_STAGES
+#define ADI_TC_NE_B_STAGES kBStages
+#endif
+constexpr uint32_t kNeAStages = ADI_TC_NE_A_STAGES;
+constexpr uint32_t kNeBStages = ADI_TC_NE_B_STAGES;
+constexpr uint32_t kMaxAStages = kTmemAStages > kNeAStages ? kTmemAStages : kNeAStages;
+constexpr uint32_t kMaxBStages = kBStages > kNeBStages ? kBStages : kNeBStages;
+#ifndef ADI_TC_NE_WORD_STAGES
+#define ADI_TC_NE_WORD_STAGES kWordStages
+#endif
+constexpr uint32_t kNeWordStages = ADI_TC_NE_WORD_STAGES;
+constexpr uint32_t kMaxWordStages = kWordStages > kNeWordStages ? kWordStages : kNeWordStages;
 
 template <TcCodec C>
 struct Traits;
@@ -102,6 +118,9 @@ struct Traits<TcCodec::kExpert> {
     static constexpr uint32_t words_bytes = 8 * row_stride;  // 8 tile rows
     static constexpr uint32_t word_slot = 8192;
     static constexpr uint32_t a_stages = kTmemAStages;
+    static constexpr uint32_t b_stages = kBStages;
+    static constexpr uint32_t w_stages = kWordStages;
+    static constexpr uint32_t b_box_rows = kBBoxRows;
     static constexpr uint32_t a_tile_bytes = 0;          // A lives in tensor memory
     static constexpr uint32_t tmem_a_columns = 64 * k_sub / 2;
     static constexpr uint32_t tmem_columns = 512;
@@ -119,7 +138,10 @@ struct Traits<TcCodec::kNe> {
     static constexpr uint32_t row_stride = box_u32 * 4;
     static constexpr uint32_t words_bytes = 8 * row_stride;
     static constexpr uint32_t word_slot = 4096;
-    static constexpr uint32_t a_stages = kAStages;
+    static constexpr uint32_t a_stages = kNeAStages;
+    static constexpr uint32_t b_stages = kNeBStages;
+    static constexpr uint32_t w_stages = kNeWordStages;
+    static constexpr uint32_t b_box_rows = kTcNeBoxRows;
     static constexpr uint32_t a_tile_bytes = kATileBytes;
     static constexpr uint32_t tmem_a_columns = 0;
     static constexpr uint32_t tmem_columns = 256;
@@ -141,9 +163,9 @@ struct Smem {
     static constexpr size_t a = 131072;  // after the value table; 1024-aligned
     static constexpr size_t b = a + size_t(T::a_stages) * T::a_tile_bytes;
     static constexpr size_t b_tile = size_t(T::k_sub) * kBSubTileBytes;
-    static constexpr size_t words = b + kBStages * b_tile;
-    static constexpr size_t bars = words + size_t(kWordStages) * T::word_slot;
-    static constexpr uint32_t kBars = 2 * kWordStages + 2 * kBStages + 2 * kMaxAStages + 4 + 1 + 1;
+    static constexpr size_t words = b + T::b_stages * b_tile;
+    static constexpr size_t bars = words + size_t(T::w_stages) * T::word_slot;
+    static constexpr uint32_t kBars = 2 * kMaxWordStages + 2 * kMaxBStages + 2 * kMaxAStages + 4 + 1 + 1;
     static constexpr size_t total = bars + kBars * 8 + 16;
 };
 static_assert(Smem<TcCodec::kExpert>::total <= 232448, "shared memory budget");
@@ -219,10 +241,10 @@ __global__ void __launch_bounds__(tc_threads<C>(), 1)
     uint8_t *word_tiles = smem + S::words;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S::bars);
     uint64_t *w_full = bars;
-    uint64_t *w_empty = w_full + kWordStages;
-    uint64_t *b_full = w_empty + kWordStages;
-    uint64_t *b_empty = b_full + kBStages;
-    uint64_t *a_ready = b_empty + kBStages;
+    uint64_t *w_empty = w_full + kMaxWordStages;
+    uint64_t *b_full = w_empty + kMaxWordStages;
+    uint64_t *b_empty = b_full + kMaxBStages;
+    uint64_t *a_ready = b_empty + kMaxBStages;
     uint64_t *a_empty = a_ready + kMaxAStages;
     uint64_t *d_full = a_empty + kMaxAStages;
     uint64_t *d_empty = d_full + 2;
@@ -235,11 +257,11 @@ __global__ void __launch_bounds__(tc_threads<C>(), 1)
     griddep_launch_dependents();
 
     if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < kWordStages; ++s) {
+        for (uint32_t s = 0; s < T::w_stages; ++s) {
             mbar_init(&w_full[s], 1);
             mbar_init(&w_empty[s], T::decode_warps);
         }
-        for (uint32_t s = 0; s < kBStages; ++s) {
+        for (uint32_t s = 0; s < T::b_stages; ++s) {
             mbar_init(&b_full[s], 1);
             mbar_init(&b_empty[s], 1);
         }
@@ -291,7 +313,7 @@ __global__ void __launch_bounds__(tc_threads<C>(), 1)
     if (warp == 0) {
         if (lane == 0) {
             // ---- trellis words: one 2-D TMA box per chunk (8 tile rows of
-            // the chunk's tiles), kWordStages chunks ahead ----
+            // the chunk's tiles), T::w_stages chunks ahead ----
             Ring r;
             uint32_t issued = 0;
             bool ok = true;
@@ -310,12 +332,12 @@ __global__ void __launch_bounds__(tc_threads<C>(), 1)
                     tma_load_2d(word_tiles + r.slot * T::word_slot, wmap, (int32_t)(kc * T::chunk_u32), y,
                                 &w_full[r.slot]);
                     ++issued;
-                    r.advance(kWordStages);
+                    r.advance(T::w_stages);
                 }
             }
-            for (uint32_t k = 0; k < min(issued, kWordStages); ++k) {
-                r.slot = r.slot == 0 ? kWordStages - 1 : r.slot - 1;
-                if (r.slot == kWordStages - 1) r.phase ^= 1u;
+            for (uint32_t k = 0; k < min(issued, T::w_stages); ++k) {
+                r.slot = r.slot == 0 ? T::w_stages - 1 : r.slot - 1;
+                if (r.slot == T::w_stages - 1) r.phase ^= 1u;
                 mbar_wait_own(&w_full[r.slot], r.phase, p.error);
             }
         }
@@ -335,20 +357,20 @@ __global__ void __launch_bounds__(tc_threads<C>(), 1)
                         ok = false;
                         break;
                     }
-                    const uint32_t n_pad = (un.count + kBBoxRows - 1) & ~(kBBoxRows - 1);
+                    const uint32_t n_pad = (un.count + T::b_box_rows - 1) & ~(T::b_box_rows - 1);
                     mbar_arrive_expect_tx(&b_full[r.slot], n_pad * kChunkK * 2 * T::k_sub);
                     for (uint32_t j = 0; j < T::k_sub; ++j)
-                        for (uint32_t r0 = 0; r0 < n_pad; r0 += kBBoxRows)
+                        for (uint32_t r0 = 0; r0 < n_pad; r0 += T::b_box_rows)
                             tma_load_2d(b_tiles + r.slot * S::b_tile + j * kBSubTileBytes + r0 * kChunkK * 2, map,
                                         (int32_t)((kc * T::k_sub + j) * kChunkK),
                                         (int32_t)(half * J.positions + un.pos0 + r0), &b_full[r.slot]);
                     ++issued;
-                    r.advance(kBStages);
+                    r.advance(T::b_stages);
                 }
             }
-            for (uint32_t k = 0; k < min(issued, kBStages); ++k) {
-                r.slot = r.slot == 0 ? kBStages - 1 : r.slot - 1;
-                if (r.slot == kBStages - 1) r.phase ^= 1u;
+            for (uint32_t k = 0; k < min(issued, T::b_stages); ++k) {
+                r.slot = r.slot == 0 ? T::b_stages - 1 : r.slot - 1;
+                if (r.slot == T::b_stages - 1) r.phase ^= 1u;
                 mbar_wait_own(&b_full[r.slot], r.phase, p.error);
             }
         }
@@ -391,7 +413,7 @@ __global__ void __launch_bounds__(tc_threads<C>(), 1)
                     mma_commit(&a_empty[a.slot]);
                     mma_commit(&b_empty[b.slot]);
                     a.advance(T::a_stages);
-                    b.advance(kBStages);
+                    b.advance(T::b_stages);
                 }
                 if (!ok) break;
                 mma_commit(&d_full[d.slot]);
@@ -514,7 +536,7 @@ __global__ void __launch_bounds__(tc_threads<C>(), 1)
                         mbar_arrive(&a_ready[a.slot]);
                         mbar_arrive(&w_empty[w.slot]);
                     }
-                    w.advance(kWordStages);
+                    w.advance(T::w_stages);
                     a.advance(T::a_stages);
                 }
             }
@@ -557,7 +579,7 @@ __global__ void __launch_bounds__(tc_threads<C>(), 1)
                         mbar_arrive(&a_ready[a.slot]);
                         mbar_arrive(&w_empty[w.slot]);
                     }
-                    w.advance(kWordStages);
+                    w.advance(T::w_stages);
                     a.advance(T::a_stages);
                 }
             }
@@ -812,12 +834,12 @@ bool launch_codec(const CUtensorMap &map0, const CUtensorMap &map1, const TcPara
 
 }  // namespace
 
-bool make_b_map(CUtensorMap *map, const __half *x, uint32_t rows, uint32_t cols) {
+bool make_b_map(CUtensorMap *map, const __half *x, uint32_t rows, uint32_t cols, uint32_t box_rows) {
     EncodeTiled fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[2] = {cols, rows};
     const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {kChunkK, kBBoxRows};
+    const cuuint32_t box[2] = {kChunkK, box_rows};
     const cuuint32_t elem[2] = {1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(x), dims, strides, box, elem,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

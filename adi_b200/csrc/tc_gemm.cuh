@@ -49,9 +49,19 @@ struct TcParams {
     uint32_t *error;     // device error word
 };
 
-// B operand map over x [rows][cols] f16: boxes of 64 columns x 16 rows,
-// 128-byte swizzle.
-bool make_b_map(CUtensorMap *map, const __half *x, uint32_t rows, uint32_t cols);
+// Rows of one B box of the NE codec: its units cover kTcMaxN positions
+// (fewer only at the end of a batch, where the box's rows past the input
+// are zero fill), so whole-tile boxes mean one copy per chunk.
+#ifndef ADI_TC_NE_BOX_ROWS
+#define ADI_TC_NE_BOX_ROWS 64
+#endif
+constexpr uint32_t kTcNeBoxRows = ADI_TC_NE_BOX_ROWS;
+static_assert(kTcMaxN % kTcNeBoxRows == 0 && kTcNeBoxRows % 16 == 0, "NE box rows");
+
+// B operand map over x [rows][cols] f16: boxes of 64 columns x box_rows
+// rows (16 for the expert codec, kTcNeBoxRows for the NE codec), 128-byte
+// swizzle.
+bool make_b_map(CUtensorMap *map, const __half *x, uint32_t rows, uint32_t cols, uint32_t box_rows = 16);
 // Router logits on tensor cores (see tc_gemm.cu): W3 = [W W W] bf16
 // [rows_pad][k = 3H], activations split into xs [tokens][3H] bf16, split-K
 // partials [parts][tokens][rows_pad], summed in order into logits rows

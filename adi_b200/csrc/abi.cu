@@ -718,7 +718,7 @@ void expert_matmul_tc(adi_cuda_context *c, ExpertDev &m, const float *in, uint32
     pp.su_is_f16 = 1;
     pp.split = 1;
     launch_prep_f16(pp, c->stream);
-    const CUtensorMap map = b_map(xh, 2 * batch, m.cols / 2);
+    const CUtensorMap map = b_map(xh, 2 * batch, m.cols / 2, kTcExpertBoxRows);
     TcParams tp{};
     tp.job[0] = TcJob{m.trellis->as<uint16_t>(), 0, m.gamma->as<uint16_t>(), 0, m.ka->as<int8_t>(), 1.0f, kx, acc,
                       size_t(batch) * m.rows, m.rows, m.cols, batch};
@@ -1319,7 +1319,8 @@ float *routed_experts(adi_cuda_context *c, MoeDev &L, const float *in, size_t P,
         c->stage(kStagePrep);
         launch_prep_f16(pp, s);
         c->stage_end();
-        const CUtensorMap map_g = b_map(xh_g, uint32_t(2 * P), H / 2), map_u = b_map(xh_u, uint32_t(2 * P), H / 2);
+        const CUtensorMap map_g = b_map(xh_g, uint32_t(2 * P), H / 2, kTcExpertBoxRows),
+                          map_u = b_map(xh_u, uint32_t(2 * P), H / 2, kTcExpertBoxRows);
         TcParams tp{};
         tp.job[0] = TcJob{L.trellis[0]->as<uint16_t>(), size_t(tiles_gu) * 48, L.gamma[0]->as<uint16_t>(),
                           I / 16 + H / 16, L.ka[0]->as<int8_t>(), 1.0f, kx_g, acc_g, P * I, I, H, uint32_t(P)};
@@ -1356,7 +1357,7 @@ float *routed_experts(adi_cuda_context *c, MoeDev &L, const float *in, size_t P,
         c->stage(kStageSwiglu);
         launch_mid_f16(mp, s);
         c->stage_end();
-        const CUtensorMap map_d = b_map(xh_d, uint32_t(2 * P), I / 2);
+        const CUtensorMap map_d = b_map(xh_d, uint32_t(2 * P), I / 2, kTcExpertBoxRows);
         TcParams dp{};
         dp.job[0] = TcJob{L.trellis[2]->as<uint16_t>(), size_t(tiles_gu) * 48, L.gamma[2]->as<uint16_t>(),
                           I / 16 + H / 16, L.ka[2]->as<int8_t>(), 1.0f, kx_d, acc_d, P * H, H, I, uint32_t(P)};

@@ -120,7 +120,7 @@ struct Traits<TcCodec::kExpert> {
     static constexpr uint32_t a_stages = kTmemAStages;
     static constexpr uint32_t b_stages = kBStages;
     static constexpr uint32_t w_stages = kWordStages;
-    static constexpr uint32_t b_box_rows = kBBoxRows;
+    static constexpr uint32_t b_box_rows = kTcExpertBoxRows;
     static constexpr uint32_t a_tile_bytes = 0;          // A lives in tensor memory
     static constexpr uint32_t tmem_a_columns = 64 * k_sub / 2;
     static constexpr uint32_t tmem_columns = 512;

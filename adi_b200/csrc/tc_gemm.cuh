@@ -56,6 +56,13 @@ struct TcParams {
 #define ADI_TC_NE_BOX_ROWS 64
 #endif
 constexpr uint32_t kTcNeBoxRows = ADI_TC_NE_BOX_ROWS;
+// The expert codec's: its units hold the positions routed to one expert,
+// often few, and a box's rows past them are other experts' positions.
+#ifndef ADI_TC_EXPERT_BOX_ROWS
+#define ADI_TC_EXPERT_BOX_ROWS 64
+#endif
+constexpr uint32_t kTcExpertBoxRows = ADI_TC_EXPERT_BOX_ROWS;
+static_assert(kTcMaxN % kTcExpertBoxRows == 0 && kTcExpertBoxRows % 16 == 0, "expert box rows");
 static_assert(kTcMaxN % kTcNeBoxRows == 0 && kTcNeBoxRows % 16 == 0, "NE box rows");
 
 // B operand map over x [rows][cols] f16: boxes of 64 columns x box_rows

@@ -71,7 +71,7 @@ EXPERT_GEMM_TRAFFIC_T512 = (134.818560e6 + 20.356608e6 + 55.004928e6 + 19.981824
 # 370.07 MB and writes 236.08 MB, down reads 84.45 MB and writes 473.76 MB
 # (one capture of this workload, 4 launches). Most of it is the f16 inputs and
 # the two fp32 partial-sum halves, not the packed weights.
-EXPERT_GEMM_TRAFFIC_C4 = (370.070016e6 + 236.075776e6 + 84.445696e6 + 473.762304e6) / 2
+EXPERT_GEMM_TRAFFIC_C4 = (370.175232e6 + 237.533440e6 + 84.516864e6 + 474.408192e6) / 2
 
 
 def parse():

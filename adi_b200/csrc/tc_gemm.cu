@@ -593,23 +593,33 @@ __global__ void __launch_bounds__(tc_threads<C>(), 1)
         for (uint32_t u = first; u < n_units; u += stride) {
             const Unit un = unit_at<T>(p, u);
             const TcJob &J = un.job ? p.job[1] : p.job[0];
+            // The unit's column unscales load before its accumulator is
+            // waited for, all at once: lane L holds those of positions L,
+            // L + 32, ... (one round trip per unit, not one per 16 columns).
+            static_assert(kTcMaxN <= 128, "four unscales per lane");
+            auto unscale_of = [&](uint32_t m) {
+                const uint32_t ni = lane + 32u * m;
+                return ni < un.count ? exp2f((float)-J.kx[un.pos0 + ni]) : 0.0f;
+            };
+            const float e0 = unscale_of(0), e1 = unscale_of(1), e2 = unscale_of(2), e3 = unscale_of(3);
+            const float base_scale = C == TcCodec::kExpert ? exp2f((float)-J.ka[un.expert]) : J.out_scale;
+            const float u0 = base_scale * e0, u1 = base_scale * e1, u2 = base_scale * e2, u3 = base_scale * e3;
             if (ok) ok = mbar_wait(&d_full[d.slot], d.phase, p.error);
             ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-wide
             tc_fence_after();
             if (ok) {
                 const uint32_t n_pad = (un.count + 15u) & ~15u;
-                const float base_scale =
-                    C == TcCodec::kExpert ? exp2f((float)-J.ka[un.expert]) : J.out_scale;
                 float *out = J.acc + (half + un.kpart) * J.half_stride + un.m_block * 128 + row_local;
                 for (uint32_t c0 = 0; c0 < n_pad; c0 += 16) {
-                    // Lane i < 16 computes column c0 + i's unscale once.
-                    const uint32_t ni = c0 + (lane & 15u);
-                    const float mine = ni < un.count ? base_scale * exp2f((float)-J.kx[un.pos0 + ni]) : 0.0f;
+                    // Column c0 + i's unscale is held by lane (c0 + i) % 32 in
+                    // register (c0 + i) / 32, the same for the 16 columns.
+                    const uint32_t m = c0 >> 5;
+                    const float held = m == 0 ? u0 : (m == 1 ? u1 : (m == 2 ? u2 : u3));
                     float v[16];
                     tmem_ld16(tmem_base + ((quarter * 32) << 16) + d.slot * kTcMaxN + c0, v);
 #pragma unroll
                     for (uint32_t i = 0; i < 16; ++i) {
-                        const float sc = __shfl_sync(0xffffffffu, mine, i);
+                        const float sc = __shfl_sync(0xffffffffu, held, (c0 & 31u) + i);
                         if (c0 + i < un.count) out[(size_t)(un.pos0 + c0 + i) * J.rows] = v[i] * sc;
                     }
                 }
